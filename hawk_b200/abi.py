@@ -1,0 +1,189 @@
+"""ctypes binding of libhawk_b200 (include/hawk_b200.h).
+
+The in-tree library ``hawk_b200/lib/libhawk_b200.so`` is the only native code
+this module loads; when it is missing the import of the runtime fails loudly
+(build it with ``python -m hawk_b200.csrc.build``).  There is no fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+from .errors import HawkError
+
+LIBRARY_PATH = Path(__file__).resolve().parent / "lib" / "libhawk_b200.so"
+
+OK = 0
+OP = {"sum": 0, "mean": 0, "max": 1, "min": 2}
+DTYPE = {"float64": 0, "float32": 1}
+LEAF_ROWS = 4096
+
+#: Every symbol include/hawk_b200.h declares, with (restype, argtypes).
+_c = ctypes
+_P = _c.c_void_p
+SIGNATURES = {
+    "hkb_last_error": (_c.c_char_p, []),
+    "hkb_build_digest": (_c.c_char_p, []),
+    "hkb_layout_sizes": (_c.c_int, [_c.POINTER(_c.c_uint64)]),
+    "hkb_device_count": (_c.c_int, [_c.POINTER(_c.c_int)]),
+    "hkb_library_load": (_c.c_int, [_P, _c.c_size_t, _c.c_int, _c.POINTER(_P)]),
+    "hkb_library_load_file": (_c.c_int, [_c.c_char_p, _c.c_int, _c.POINTER(_P)]),
+    "hkb_library_free": (None, [_P]),
+    "hkb_library_entry": (_c.c_int, [_P, _c.c_char_p, _c.POINTER(_P)]),
+    "hkb_entry_info": (_c.c_int, [_P, _c.POINTER(_c.c_int), _c.POINTER(_c.c_int), _c.POINTER(_c.c_int),
+                                  _c.c_int64, _c.POINTER(_c.c_int64)]),
+    "hkb_argblock_create": (_c.c_int, [_c.POINTER(_c.c_char_p), _c.c_size_t, _c.POINTER(_P)]),
+    "hkb_argblock_free": (None, [_P]),
+    "hkb_argblock_bind": (_c.c_int, [_P, _c.c_size_t, _c.c_size_t, _c.c_uint64, _c.c_uint64,
+                                     _c.c_int32, _c.c_int32]),
+    "hkb_argblock_rebind": (_c.c_int, [_P, _c.POINTER(_c.c_int64), _c.POINTER(_c.c_int64), _c.c_size_t]),
+    "hkb_entry_launch": (_c.c_int, [_P, _P, _c.c_int64, _c.c_int64, _c.c_int64, _P]),
+    "hkb_cells_leaves": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _c.POINTER(_P), _c.POINTER(_P),
+                                    _c.c_int64, _P, _P, _P]),
+    "hkb_cells_tree": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _P, _P, _c.c_int64, _P, _P]),
+    "hkb_cells_scratch_bytes": (_c.c_size_t, [_c.c_int, _c.c_int, _c.c_int64]),
+    "hkb_cells_finish": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _c.POINTER(_P), _c.POINTER(_P),
+                                    _c.c_int64, _P, _P, _P]),
+}
+
+_LOCK = threading.Lock()
+_LIB = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (loaded once; raises when it is not built)."""
+    global _LIB
+    with _LOCK:
+        if _LIB is None:
+            if not LIBRARY_PATH.exists():
+                raise HawkError(f"{LIBRARY_PATH.name} is not built (expected at {LIBRARY_PATH}); "
+                                "build it with `python -m hawk_b200.csrc.build`")
+            handle = ctypes.CDLL(str(LIBRARY_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+            _LIB = handle
+        return _LIB
+
+
+def check(status: int, what: str) -> None:
+    if status != OK:
+        msg = lib().hkb_last_error().decode(errors="replace")
+        raise HawkError(f"{what}: {msg} (status {status})")
+
+
+def layout_sizes() -> list:
+    out = (ctypes.c_uint64 * 5)()
+    check(lib().hkb_layout_sizes(out), "hkb_layout_sizes")
+    return [int(v) for v in out]
+
+
+def build_digest() -> str:
+    return lib().hkb_build_digest().decode()
+
+
+def device_count() -> int:
+    n = ctypes.c_int(0)
+    check(lib().hkb_device_count(ctypes.byref(n)), "hkb_device_count")
+    return int(n.value)
+
+
+class Library:
+    """A loaded sm_100a artifact (``hawk._core.HostLibrary``'s device twin)."""
+
+    def __init__(self, path, device: int) -> None:
+        self._h = ctypes.c_void_p()
+        self.path = Path(path)
+        self.device = int(device)
+        check(lib().hkb_library_load_file(str(self.path).encode(), self.device, ctypes.byref(self._h)),
+              f"loading {self.path.name} on device {self.device}")
+
+    def entry(self, name: str) -> "Entry":
+        return Entry(self, name)
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h and h.value and _LIB is not None:
+            _LIB.hkb_library_free(h)
+            self._h = None
+
+
+class Entry:
+    def __init__(self, library: Library, name: str) -> None:
+        self.library = library       # keeps the image loaded
+        self.name = name
+        self._h = ctypes.c_void_p()
+        check(lib().hkb_library_entry(library._h, name.encode(), ctypes.byref(self._h)),
+              f"entry {name!r} of {library.path.name}")
+
+    def info(self, count: int = 0) -> dict:
+        regs, bps, block = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        grid = ctypes.c_int64()
+        check(lib().hkb_entry_info(self._h, ctypes.byref(regs), ctypes.byref(bps), ctypes.byref(block),
+                                   int(count), ctypes.byref(grid)), "hkb_entry_info")
+        return {"regs": regs.value, "blocks_per_sm": bps.value, "block": block.value, "grid": grid.value}
+
+    def launch(self, block: "ArgBlock", base: int, count: int, n_samples: int, stream: int = 0) -> None:
+        check(lib().hkb_entry_launch(self._h, block._h, int(base), int(count), int(n_samples),
+                                     ctypes.c_void_p(int(stream) or None)),
+              f"launching {self.name!r}")
+
+
+class ArgBlock:
+    """``hawk._core.ArgBlock``'s device twin: one by-value cell per slot."""
+
+    def __init__(self, kinds) -> None:
+        self.kinds = list(kinds)
+        arr = (ctypes.c_char_p * len(self.kinds))(*[k.encode() for k in self.kinds])
+        self._h = ctypes.c_void_p()
+        check(lib().hkb_argblock_create(arr, len(self.kinds), ctypes.byref(self._h)), "hkb_argblock_create")
+
+    def bind(self, slot: int, ptr: int, samples: int, stride: int = 1, device_type: int = 2,
+             device_id: int = 0) -> None:
+        check(lib().hkb_argblock_bind(self._h, int(slot), int(ptr), int(samples), int(stride),
+                                      int(device_type), int(device_id)), f"binding slot {slot}")
+
+    def rebind(self, slots, ptrs) -> None:
+        n = len(slots)
+        s = (ctypes.c_int64 * n)(*[int(x) for x in slots])
+        p = (ctypes.c_int64 * n)(*[int(x) for x in ptrs])
+        check(lib().hkb_argblock_rebind(self._h, s, p, n), "hkb_argblock_rebind")
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h and h.value and _LIB is not None:
+            _LIB.hkb_argblock_free(h)
+            self._h = None
+
+
+def _ptr_array(ptrs):
+    return (ctypes.c_void_p * len(ptrs))(*[ctypes.c_void_p(int(p) or None) for p in ptrs])
+
+
+def cells_scratch_bytes(dtype: str, ncols: int, rows: int) -> int:
+    return int(lib().hkb_cells_scratch_bytes(DTYPE[dtype], int(ncols), int(rows)))
+
+
+def cells_finish(op: str, dtype: str, hi, comp, rows: int, scratch: int, out: int, stream: int = 0) -> None:
+    """Rows of ``len(hi)`` columns finished into ``out`` (device pointers)."""
+    check(lib().hkb_cells_finish(OP[op], DTYPE[dtype], len(hi), _ptr_array(hi),
+                                 _ptr_array(comp) if comp is not None else None, int(rows),
+                                 ctypes.c_void_p(int(scratch)), ctypes.c_void_p(int(out)),
+                                 ctypes.c_void_p(int(stream) or None)), "hkb_cells_finish")
+
+
+def cells_leaves(op: str, dtype: str, hi, comp, rows: int, leaf_hi: int, leaf_comp: int, stream: int = 0) -> None:
+    check(lib().hkb_cells_leaves(OP[op], DTYPE[dtype], len(hi), _ptr_array(hi),
+                                 _ptr_array(comp) if comp is not None else None, int(rows),
+                                 ctypes.c_void_p(int(leaf_hi)), ctypes.c_void_p(int(leaf_comp)),
+                                 ctypes.c_void_p(int(stream) or None)), "hkb_cells_leaves")
+
+
+def cells_tree(op: str, dtype: str, ncols: int, leaf_hi: int, leaf_comp: int, leaves: int, out: int,
+               stream: int = 0) -> None:
+    check(lib().hkb_cells_tree(OP[op], DTYPE[dtype], int(ncols), ctypes.c_void_p(int(leaf_hi)),
+                               ctypes.c_void_p(int(leaf_comp)), int(leaves), ctypes.c_void_p(int(out)),
+                               ctypes.c_void_p(int(stream) or None)), "hkb_cells_tree")

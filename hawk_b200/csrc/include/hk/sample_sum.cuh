@@ -1,0 +1,124 @@
+// hawk_b200 device library: reductions over samples.
+//
+// A kernel with SampleSum sinks (Param gradients of a VJP, hawk.sum/max/min
+// cells) writes one row per 32 consecutive samples and column: the row is a
+// fixed binary tree over the 32 lanes of a warp -- lanes paired across bit 4,
+// then bit 3, ..., bit 0 -- whose nodes combine (sum, compensation) pairs
+// (hawk/emit/wrapper.py:561-592, the host twin sampleSumRow_ and the device
+// butterfly sampleSumWarp_ pair the same lanes).  A sum's node is
+//     t = s + s2;  c = finite(t) ? (c + c2) + err(s, s2, t) : 0;  s = t
+// with err the exact two-sum residual, larger magnitude first, +0 for a zero
+// residual (hawk/_cells.py:44-49).  Max/min nodes keep the NaN-ignoring
+// extreme of (lower lane, upper lane).
+//
+// Rows are then finished into the cell by the ``ordered`` tree of
+// hawk/_cells.py:71-119: leaves of 4096 rows (256 slots x 16 terms, the terms
+// of a slot added in order with a Neumaier step), a halving tree over the 256
+// slots, then pairwise levels over the leaves (an odd last one carried up),
+// and hi + comp at the root.  The device kernels that run that tree live in
+// the runtime library; the node arithmetic is here so the two agree.
+#pragma once
+#include "base.cuh"
+
+namespace hk {
+namespace ss {
+
+enum Op { kSum = 0, kMax = 1, kMin = 2 };
+
+template <class T> HK_HD bool finite(T x) { return (x - x) == (x - x); }
+
+// Exact residual of s == a + b (|a| >= |b| ordering), +0 for a zero residual.
+template <class T> HK_HD T two_sum_err(T a, T b, T s) {
+    const bool a_big = (a < T(0) ? -a : a) >= (b < T(0) ? -b : b);
+    const T big = a_big ? a : b;
+    const T small = a_big ? b : a;
+    return (small - (s - big)) + T(0);
+}
+
+template <class T> HK_HD T extreme(int op, T a, T b) {
+    if (a != a) return b;
+    if (b != b) return a;
+    return op == kMax ? (b > a ? b : a) : (b < a ? b : a);
+}
+
+template <class T> HK_HD T identity(int op) {
+    if (op == kSum) return T(0);
+    const T inf = T(1) / T(0);
+    return op == kMax ? -inf : inf;
+}
+
+// One node of a row: (s, c) of the lower lane joined with (s2, c2) of the upper.
+template <int OP, class T> HK_HD void pair_combine(T& s, T& c, T s2, T c2) {
+    if constexpr (OP != kSum) {
+        s = extreme(OP, s, s2);
+        return;
+    } else {
+        const T t = s + s2;
+        const T e = two_sum_err(s, s2, t);
+        c = finite(t) ? (c + c2) + e : T(0);
+        s = t;
+    }
+}
+
+// The finish tree's two node kinds (hawk/_cells.py:52-68).
+template <int OP, class T> HK_HD void neumaier_add(T& h, T& c, T x, T xc) {
+    if constexpr (OP == kSum) {
+        const T s = h + x;
+        const bool f = finite(s);
+        c = f ? c + two_sum_err(h, x, s) : T(0);
+        c = f ? c + xc : T(0);
+        h = s;
+    } else if constexpr (OP == kMax) {
+        h = (h > x) ? h : x;
+    } else {
+        h = (h < x) ? h : x;
+    }
+}
+template <int OP, class T> HK_HD void tree_join(T& h, T& c, T x, T xc) {
+    if constexpr (OP == kSum) {
+        const T s = h + x;
+        c = finite(s) ? (c + xc) + two_sum_err(h, x, s) : T(0);
+        h = s;
+    } else if constexpr (OP == kMax) {
+        h = (h > x) ? h : x;
+    } else {
+        h = (h < x) ? h : x;
+    }
+}
+
+constexpr int kSlots = 256;
+constexpr int kTerms = 16;
+constexpr int kLeaf = kSlots * kTerms;   // rows per leaf
+
+#if defined(__CUDACC__) || defined(__CUDACC_RTC__)
+// The row of the calling warp: every lane passes its sample's W terms (the
+// identity for a lane past the last sample); after five butterfly rounds every
+// lane holds every column's (sum, compensation), and lane k < W calls
+// store(k, sum, comp) for column k.  All 32 lanes of the warp must call it.
+template <int W, int OP, class T, class Store>
+__device__ __forceinline__ void row_reduce(T (&h)[W], Store&& store) {
+    T c[W];
+#pragma unroll
+    for (int k = 0; k < W; ++k) c[k] = T(0);
+    const unsigned lane = threadIdx.x & 31u;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const bool lower = (lane & static_cast<unsigned>(off)) == 0u;
+#pragma unroll
+        for (int k = 0; k < W; ++k) {
+            const T rh = __shfl_xor_sync(0xffffffffu, h[k], off);
+            const T rc = __shfl_xor_sync(0xffffffffu, c[k], off);
+            T s = lower ? h[k] : rh, sc = lower ? c[k] : rc;
+            pair_combine<OP>(s, sc, lower ? rh : h[k], lower ? rc : c[k]);
+            h[k] = s;
+            c[k] = sc;
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < W; ++k)
+        if (static_cast<int>(lane) == (k & 31)) store(k, h[k], c[k]);
+}
+#endif
+
+}  // namespace ss
+}  // namespace hk

@@ -1,0 +1,197 @@
+// hawk_b200 device library: plane views.
+//
+// A plane is component-major structure-of-arrays with unit sample stride
+// (hawk/emit/wrapper.py:1029-1066): component k of sample i of a Vector[W]
+// plane sits at data[k * pitch + i], pitch = the mirror's compStride_; a
+// Matrix[R, C] plane at data[(r * C + c) * pitch + i]; a Scalar plane at
+// data[i].  Consecutive threads take consecutive samples, so every warp-wide
+// access to one component is one contiguous 256-byte (f64) run.
+//
+// Reads of input planes go through the read-only data path and writes of
+// output planes are streaming (evict-first) stores: every plane byte is
+// touched exactly once per launch, so neither should displace reused lines
+// (the lookup cells) from L1/L2.
+//
+// The body indexes a view with the sample index ``i`` its frame binds:
+//   in[i]          -> the sample's value (Item for rank >= 1), eagerly loaded;
+//   in[i].get()    -> the same value; scalar in[i].eval() -> the scalar;
+//   out[i] = v     -> store;  out[i].get()/.eval() -> the value the plane held
+//                     when the launch began (a Mutable read), out[i][k] /
+//                     out[i](r, c) -> a reference to one component (a solve
+//                     writes its result through it);
+//   rows.data()[r] -> a row plane's element r (sample-sum rows).
+#pragma once
+#include "abi.cuh"
+#include "item.cuh"
+
+namespace hk {
+
+struct SampleIndex {
+    i64 g;   // the global sample index
+
+    static HK_FI SampleIndex make(usize k) { return SampleIndex{static_cast<i64>(k)}; }
+    HK_FI i64 global() const { return g; }
+};
+
+template <class T> HK_FI T ld_in(const T* p) {
+#if defined(__CUDA_ARCH__)
+    return __ldg(p);
+#else
+    return *p;
+#endif
+}
+
+template <class T> HK_FI void st_out(T* p, T v) {
+#if defined(__CUDA_ARCH__)
+    __stcs(p, v);
+#else
+    *p = v;
+#endif
+}
+
+// A rank-0 value read from a plane.
+template <class T> struct Val {
+    T x;
+    HK_FI T eval() const { return x; }
+    HK_FI T get() const { return x; }
+    HK_FI operator T() const { return x; }
+};
+
+// ------------------------------------------------------------------ inputs
+
+// per_sample and lookup roles: one element per sample (or a one-cell plane).
+template <class T> struct ScalarIn {
+    const T* p;
+    u64 n;
+    HK_FI explicit ScalarIn(const abi::ScalarHandle& h) : p(static_cast<const T*>(h.data)), n(h.samples) {}
+    HK_FI explicit ScalarIn(const abi::IntHandle& h) : p(static_cast<const T*>(h.data)), n(h.samples) {}
+    HK_FI Val<T> operator[](const SampleIndex& i) const { return Val<T>{ld_in(p + i.g)}; }
+    HK_FI T cell() const { return ld_in(p); }
+    HK_FI const T* data() const { return p; }
+    HK_FI u64 samples() const { return n; }
+};
+
+template <class T, int N> struct VecIn {
+    const T* p;
+    u64 pitch;
+    u64 n;
+    HK_FI explicit VecIn(const abi::GRefMirror& m)
+        : p(reinterpret_cast<const T*>(m.data_)), pitch(m.compStride_), n(m.samples_) {}
+    HK_FI Item<T, N> operator[](const SampleIndex& i) const {
+        Item<T, N> r;
+#pragma unroll
+        for (int k = 0; k < N; ++k) r.v[k] = ld_in(p + static_cast<u64>(k) * pitch + i.g);
+        return r;
+    }
+    HK_FI const T* data() const { return p; }
+    HK_FI u64 samples() const { return n; }
+};
+
+template <class T, int R, int C> struct MatIn {
+    const T* p;
+    u64 pitch;
+    u64 n;
+    HK_FI explicit MatIn(const abi::GRefMirror& m)
+        : p(reinterpret_cast<const T*>(m.data_)), pitch(m.compStride_), n(m.samples_) {}
+    HK_FI Item<T, R, C> operator[](const SampleIndex& i) const {
+        Item<T, R, C> a;
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int c = 0; c < C; ++c)
+                a.m[r][c] = ld_in(p + static_cast<u64>(r * C + c) * pitch + i.g);
+        return a;
+    }
+    HK_FI const T* data() const { return p; }
+    HK_FI u64 samples() const { return n; }
+};
+
+// ------------------------------------------------------------------ sinks
+
+// A scalar Mutable / out plane, or a row plane of a sample sum.
+template <class T> struct ScalarOut {
+    T* p;
+    u64 n;
+    struct Ref {
+        T* q;
+        HK_FI void operator=(T v) const { st_out(q, v); }
+        HK_FI void operator+=(T v) const { *q = *q + v; }
+        HK_FI T eval() const { return *q; }
+        HK_FI T get() const { return *q; }
+        HK_FI operator T() const { return *q; }
+    };
+    HK_FI explicit ScalarOut(const abi::ScalarHandle& h) : p(static_cast<T*>(h.data)), n(h.samples) {}
+    HK_FI explicit ScalarOut(const abi::IntHandle& h) : p(static_cast<T*>(h.data)), n(h.samples) {}
+    HK_FI Ref operator[](const SampleIndex& i) const { return Ref{p + i.g}; }
+    HK_FI T* data() const { return p; }
+    HK_FI u64 samples() const { return n; }
+};
+
+template <class T, int N> struct VecOut {
+    T* p;
+    u64 pitch;
+    u64 n;
+    struct Ref {
+        T* q;
+        u64 pitch;
+        HK_FI void operator=(const Item<T, N>& v) const {
+#pragma unroll
+            for (int k = 0; k < N; ++k) st_out(q + static_cast<u64>(k) * pitch, v.v[k]);
+        }
+        HK_FI void operator+=(const Item<T, N>& v) const {
+#pragma unroll
+            for (int k = 0; k < N; ++k) q[static_cast<u64>(k) * pitch] += v.v[k];
+        }
+        HK_FI T& operator[](int k) const { return q[static_cast<u64>(k) * pitch]; }
+        HK_FI T& operator()(int k) const { return q[static_cast<u64>(k) * pitch]; }
+        HK_FI T& at(int k) const { return q[static_cast<u64>(k) * pitch]; }
+        HK_FI Item<T, N> get() const {
+            Item<T, N> r;
+#pragma unroll
+            for (int k = 0; k < N; ++k) r.v[k] = q[static_cast<u64>(k) * pitch];
+            return r;
+        }
+        HK_FI Item<T, N> eval() const { return get(); }
+        HK_FI operator Item<T, N>() const { return get(); }
+    };
+    HK_FI explicit VecOut(const abi::GRefMirror& m)
+        : p(reinterpret_cast<T*>(m.data_)), pitch(m.compStride_), n(m.samples_) {}
+    HK_FI Ref operator[](const SampleIndex& i) const { return Ref{p + i.g, pitch}; }
+    HK_FI T* data() const { return p; }
+    HK_FI u64 samples() const { return n; }
+};
+
+template <class T, int R, int C> struct MatOut {
+    T* p;
+    u64 pitch;
+    u64 n;
+    struct Ref {
+        T* q;
+        u64 pitch;
+        HK_FI void operator=(const Item<T, R, C>& a) const {
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+#pragma unroll
+                for (int c = 0; c < C; ++c) st_out(q + static_cast<u64>(r * C + c) * pitch, a.m[r][c]);
+        }
+        HK_FI T& operator()(int r, int c) const { return q[static_cast<u64>(r * C + c) * pitch]; }
+        HK_FI T& at(int r, int c) const { return q[static_cast<u64>(r * C + c) * pitch]; }
+        HK_FI Item<T, R, C> get() const {
+            Item<T, R, C> a;
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+#pragma unroll
+                for (int c = 0; c < C; ++c) a.m[r][c] = q[static_cast<u64>(r * C + c) * pitch];
+            return a;
+        }
+        HK_FI Item<T, R, C> eval() const { return get(); }
+        HK_FI operator Item<T, R, C>() const { return get(); }
+    };
+    HK_FI explicit MatOut(const abi::GRefMirror& m)
+        : p(reinterpret_cast<T*>(m.data_)), pitch(m.compStride_), n(m.samples_) {}
+    HK_FI Ref operator[](const SampleIndex& i) const { return Ref{p + i.g, pitch}; }
+    HK_FI T* data() const { return p; }
+    HK_FI u64 samples() const { return n; }
+};
+
+}  // namespace hk

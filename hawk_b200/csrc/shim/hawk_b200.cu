@@ -1,0 +1,587 @@
+// libhawk_b200: the C ABI declared in include/hawk_b200.h.
+//
+// Artifacts are sm_100a CUBINs compiled by NVRTC from b200 units; they are
+// loaded with the CUDA runtime's context-independent library API
+// (cudaLibraryLoadData / cudaLibraryGetKernel / cudaLibraryGetGlobal) and
+// launched with cudaLaunchKernel.  The CUDA runtime is linked statically, so
+// the library loads (and reports its build facts) on a machine without a GPU
+// driver; every device call then fails with HKB_ERR_CUDA and a message.
+//
+// The finish-tree kernels (hkb_cells_*) are compiled into this library.
+#include "hawk_b200.h"
+
+#include "hk/abi.cuh"
+#include "hk/sample_sum.cuh"
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#ifndef HKB_BUILD_DIGEST
+#define HKB_BUILD_DIGEST "unstamped"
+#endif
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int status, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_error = buf;
+    return status;
+}
+
+int cuda_fail(cudaError_t err, const char* what) {
+    return fail(HKB_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(err), cudaGetErrorName(err));
+}
+
+#define HKB_CUDA(call, what)                               \
+    do {                                                   \
+        cudaError_t hkb_err_ = (call);                     \
+        if (hkb_err_ != cudaSuccess) return cuda_fail(hkb_err_, what); \
+    } while (0)
+
+enum class Kind { GRef, Handle, IntHandle, F64, F32, Int, NSamples };
+
+bool kind_from_name(const char* name, Kind* out) {
+    static const struct { const char* name; Kind kind; } table[] = {
+        {"gref", Kind::GRef}, {"handle", Kind::Handle}, {"int_handle", Kind::IntHandle},
+        {"f64", Kind::F64}, {"f32", Kind::F32}, {"int", Kind::Int}, {"nsamples", Kind::NSamples}};
+    for (const auto& row : table)
+        if (std::strcmp(row.name, name) == 0) {
+            *out = row.kind;
+            return true;
+        }
+    return false;
+}
+
+const uint64_t kLayout[5] = {sizeof(hk::abi::GRefMirror), sizeof(hk::abi::ScalarHandle),
+                             sizeof(hk::abi::IntHandle), sizeof(hk::abi::index_t),
+                             sizeof(hk::abi::PartitionTriple)};
+const char* const kLayoutField[5] = {"GRefMirror", "ScalarHandle", "IntHandle", "index type",
+                                     "PartitionTriple"};
+const char kAbiTag[] = "aether-abi/2";
+
+constexpr int kBlock = 256;   // every b200 entry is compiled __launch_bounds__(256)
+
+// Sets `device` current for the scope, restoring the caller's on exit.
+struct DeviceScope {
+    int previous = -1;
+    cudaError_t err = cudaSuccess;
+    explicit DeviceScope(int device) {
+        err = cudaGetDevice(&previous);
+        if (err == cudaSuccess && previous != device) err = cudaSetDevice(device);
+    }
+    ~DeviceScope() {
+        int now = -1;
+        if (previous >= 0 && cudaGetDevice(&now) == cudaSuccess && now != previous) cudaSetDevice(previous);
+    }
+};
+
+}  // namespace
+
+struct hkb_library {
+    cudaLibrary_t lib = nullptr;
+    int device = 0;
+    int sms = 0;
+};
+
+struct hkb_entry {
+    hkb_library* lib = nullptr;
+    cudaKernel_t kernel = nullptr;
+    std::string name;
+    int regs = 0;
+    int blocks_per_sm = 0;
+};
+
+struct hkb_argblock {
+    struct Cell {
+        alignas(8) unsigned char bytes[40];
+        Kind kind;
+    };
+    std::vector<Cell> cells;
+    std::vector<void*> params;
+};
+
+extern "C" {
+
+const char* hkb_last_error(void) { return g_error.c_str(); }
+
+const char* hkb_build_digest(void) { return HKB_BUILD_DIGEST; }
+
+int hkb_layout_sizes(uint64_t out[5]) {
+    if (out == nullptr) return fail(HKB_ERR_ARGUMENT, "hkb_layout_sizes: null output");
+    for (int k = 0; k < 5; ++k) out[k] = kLayout[k];
+    return HKB_OK;
+}
+
+int hkb_device_count(int* count) {
+    if (count == nullptr) return fail(HKB_ERR_ARGUMENT, "hkb_device_count: null output");
+    *count = 0;
+    const cudaError_t err = cudaGetDeviceCount(count);
+    if (err != cudaSuccess) {
+        *count = 0;
+        cudaGetLastError();   // a machine without a driver: zero devices, not an error
+    }
+    return HKB_OK;
+}
+
+// ------------------------------------------------------------------ library
+
+static int check_exports(hkb_library* lib) {
+    void* dptr = nullptr;
+    size_t bytes = 0;
+    cudaError_t err = cudaLibraryGetGlobal(&dptr, &bytes, lib->lib, "eagle_abi_tag");
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(HKB_ERR_ABI, "the artifact exports no eagle_abi_tag: it is not a b200 unit");
+    }
+    char tag[64] = {0};
+    if (bytes == 0 || bytes > sizeof tag)
+        return fail(HKB_ERR_ABI, "the artifact's eagle_abi_tag has %zu bytes", bytes);
+    HKB_CUDA(cudaMemcpy(tag, dptr, bytes, cudaMemcpyDeviceToHost), "reading eagle_abi_tag");
+    if (std::strncmp(tag, kAbiTag, sizeof kAbiTag) != 0)
+        return fail(HKB_ERR_ABI, "the artifact's eagle_abi_tag is '%s', this library packs '%s'", tag, kAbiTag);
+    err = cudaLibraryGetGlobal(&dptr, &bytes, lib->lib, "eagle_layout_sizes");
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(HKB_ERR_ABI, "the artifact exports no eagle_layout_sizes");
+    }
+    if (bytes != sizeof kLayout)
+        return fail(HKB_ERR_ABI, "the artifact's eagle_layout_sizes has %zu bytes, not %zu", bytes, sizeof kLayout);
+    uint64_t sizes[5];
+    HKB_CUDA(cudaMemcpy(sizes, dptr, bytes, cudaMemcpyDeviceToHost), "reading eagle_layout_sizes");
+    for (int k = 0; k < 5; ++k)
+        if (sizes[k] != kLayout[k])
+            return fail(HKB_ERR_ABI, "layout mismatch in sizeof(%s): the artifact was built with %llu bytes, "
+                        "this library packs %llu", kLayoutField[k], (unsigned long long)sizes[k],
+                        (unsigned long long)kLayout[k]);
+    return HKB_OK;
+}
+
+int hkb_library_load(const void* image, size_t size, int device, hkb_library** out) {
+    if (image == nullptr || size == 0 || out == nullptr)
+        return fail(HKB_ERR_ARGUMENT, "hkb_library_load: empty image or null output");
+    *out = nullptr;
+    DeviceScope scope(device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "selecting the device");
+    auto* lib = new (std::nothrow) hkb_library();
+    if (lib == nullptr) return fail(HKB_ERR_ARGUMENT, "out of host memory");
+    lib->device = device;
+    cudaError_t err = cudaLibraryLoadData(&lib->lib, image, nullptr, nullptr, 0, nullptr, nullptr, 0);
+    if (err != cudaSuccess) {
+        delete lib;
+        return cuda_fail(err, "loading the sm_100a image");
+    }
+    err = cudaDeviceGetAttribute(&lib->sms, cudaDevAttrMultiProcessorCount, device);
+    if (err != cudaSuccess) {
+        cudaLibraryUnload(lib->lib);
+        delete lib;
+        return cuda_fail(err, "reading the SM count");
+    }
+    const int status = check_exports(lib);
+    if (status != HKB_OK) {
+        cudaLibraryUnload(lib->lib);
+        delete lib;
+        return status;
+    }
+    *out = lib;
+    return HKB_OK;
+}
+
+int hkb_library_load_file(const char* path, int device, hkb_library** out) {
+    if (path == nullptr) return fail(HKB_ERR_ARGUMENT, "hkb_library_load_file: null path");
+    FILE* f = std::fopen(path, "rb");
+    if (f == nullptr) return fail(HKB_ERR_NOT_FOUND, "cannot open artifact '%s'", path);
+    std::vector<unsigned char> image;
+    unsigned char buf[1 << 16];
+    size_t n;
+    while ((n = std::fread(buf, 1, sizeof buf, f)) > 0) image.insert(image.end(), buf, buf + n);
+    std::fclose(f);
+    return hkb_library_load(image.data(), image.size(), device, out);
+}
+
+void hkb_library_free(hkb_library* lib) {
+    if (lib == nullptr) return;
+    if (lib->lib != nullptr) cudaLibraryUnload(lib->lib);
+    delete lib;
+}
+
+int hkb_library_entry(hkb_library* lib, const char* name, hkb_entry** out) {
+    if (lib == nullptr || name == nullptr || out == nullptr)
+        return fail(HKB_ERR_ARGUMENT, "hkb_library_entry: null argument");
+    *out = nullptr;
+    DeviceScope scope(lib->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "selecting the device");
+    cudaKernel_t kernel = nullptr;
+    const cudaError_t err = cudaLibraryGetKernel(&kernel, lib->lib, name);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(HKB_ERR_NOT_FOUND, "the artifact has no entry '%s'", name);
+    }
+    auto* entry = new (std::nothrow) hkb_entry();
+    if (entry == nullptr) return fail(HKB_ERR_ARGUMENT, "out of host memory");
+    entry->lib = lib;
+    entry->kernel = kernel;
+    entry->name = name;
+    cudaFuncAttributes attr;
+    cudaError_t e2 = cudaFuncGetAttributes(&attr, reinterpret_cast<const void*>(kernel));
+    if (e2 != cudaSuccess) {
+        delete entry;
+        return cuda_fail(e2, "reading the entry's attributes");
+    }
+    entry->regs = attr.numRegs;
+    e2 = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&entry->blocks_per_sm,
+                                                       reinterpret_cast<const void*>(kernel), kBlock, 0);
+    if (e2 != cudaSuccess) {
+        delete entry;
+        return cuda_fail(e2, "computing the entry's occupancy");
+    }
+    if (entry->blocks_per_sm < 1) entry->blocks_per_sm = 1;
+    *out = entry;
+    return HKB_OK;
+}
+
+static int64_t grid_for(const hkb_entry* entry, int64_t count) {
+    const int64_t cap = static_cast<int64_t>(entry->lib->sms) * entry->blocks_per_sm;
+    int64_t need = (count + kBlock - 1) / kBlock;
+    if (need < 1) need = 1;
+    return need < cap ? need : cap;
+}
+
+int hkb_entry_info(hkb_entry* entry, int* regs, int* blocks_per_sm, int* block, int64_t count,
+                   int64_t* grid) {
+    if (entry == nullptr) return fail(HKB_ERR_ARGUMENT, "hkb_entry_info: null entry");
+    if (regs) *regs = entry->regs;
+    if (blocks_per_sm) *blocks_per_sm = entry->blocks_per_sm;
+    if (block) *block = kBlock;
+    if (grid) *grid = grid_for(entry, count);
+    return HKB_OK;
+}
+
+// ------------------------------------------------------------ argument block
+
+int hkb_argblock_create(const char* const* kinds, size_t n, hkb_argblock** out) {
+    if (out == nullptr || (n > 0 && kinds == nullptr))
+        return fail(HKB_ERR_ARGUMENT, "hkb_argblock_create: null argument");
+    *out = nullptr;
+    auto* block = new (std::nothrow) hkb_argblock();
+    if (block == nullptr) return fail(HKB_ERR_ARGUMENT, "out of host memory");
+    block->cells.resize(n);
+    block->params.resize(n, nullptr);
+    for (size_t k = 0; k < n; ++k) {
+        auto& cell = block->cells[k];
+        if (kinds[k] == nullptr || !kind_from_name(kinds[k], &cell.kind)) {
+            delete block;
+            return fail(HKB_ERR_ARGUMENT, "slot %zu: unknown descriptor kind '%s'", k,
+                        kinds[k] ? kinds[k] : "(null)");
+        }
+        std::memset(cell.bytes, 0, sizeof cell.bytes);
+        // A fresh mirror is the POD's default: unit stride, a CUDA device.
+        if (cell.kind == Kind::Handle || cell.kind == Kind::IntHandle) {
+            auto* m = reinterpret_cast<hk::abi::ScalarHandle*>(cell.bytes);
+            m->stride = 1;
+            m->deviceType = 2;
+        } else if (cell.kind == Kind::GRef) {
+            auto* m = reinterpret_cast<hk::abi::GRefMirror*>(cell.bytes);
+            m->sampleStride_ = 1;
+            m->deviceType_ = 2;
+        }
+        block->params[k] = cell.bytes;
+    }
+    *out = block;
+    return HKB_OK;
+}
+
+void hkb_argblock_free(hkb_argblock* block) { delete block; }
+
+int hkb_argblock_bind(hkb_argblock* block, size_t slot, uintptr_t ptr, uint64_t samples,
+                      uint64_t stride, int32_t device_type, int32_t device_id) {
+    if (block == nullptr) return fail(HKB_ERR_ARGUMENT, "hkb_argblock_bind: null block");
+    if (slot >= block->cells.size())
+        return fail(HKB_ERR_ARGUMENT, "slot %zu is outside this block's %zu slots", slot, block->cells.size());
+    auto& cell = block->cells[slot];
+    switch (cell.kind) {
+        case Kind::GRef: {
+            auto* m = reinterpret_cast<hk::abi::GRefMirror*>(cell.bytes);
+            m->data_ = reinterpret_cast<double*>(ptr);
+            m->samples_ = samples;
+            m->compStride_ = samples * stride;
+            m->sampleStride_ = stride;
+            m->deviceType_ = device_type;
+            m->deviceId_ = device_id;
+            return HKB_OK;
+        }
+        case Kind::Handle:
+        case Kind::IntHandle: {
+            auto* m = reinterpret_cast<hk::abi::ScalarHandle*>(cell.bytes);
+            m->data = reinterpret_cast<void*>(ptr);
+            m->samples = samples;
+            m->stride = stride;
+            m->deviceType = device_type;
+            m->deviceId = device_id;
+            return HKB_OK;
+        }
+        default:
+            break;
+    }
+    // A by-value slot copies the value at `ptr` (a caller's temporary).
+    if (ptr == 0)
+        return fail(HKB_ERR_ARGUMENT, "slot %zu is a by-value slot and needs the address of its value", slot);
+    const void* src = reinterpret_cast<const void*>(ptr);
+    switch (cell.kind) {
+        case Kind::F64: std::memcpy(cell.bytes, src, sizeof(double)); break;
+        case Kind::F32: std::memcpy(cell.bytes, src, sizeof(float)); break;
+        case Kind::Int: std::memcpy(cell.bytes, src, sizeof(long long)); break;
+        case Kind::NSamples: std::memcpy(cell.bytes, src, sizeof(hk::abi::index_t)); break;
+        default: break;
+    }
+    return HKB_OK;
+}
+
+int hkb_argblock_rebind(hkb_argblock* block, const int64_t* slots, const int64_t* ptrs, size_t n) {
+    if (block == nullptr || (n > 0 && (slots == nullptr || ptrs == nullptr)))
+        return fail(HKB_ERR_ARGUMENT, "hkb_argblock_rebind: null argument");
+    for (size_t i = 0; i < n; ++i) {
+        const int64_t s = slots[i];
+        if (s < 0 || static_cast<size_t>(s) >= block->cells.size())
+            return fail(HKB_ERR_ARGUMENT, "rebind: slot %lld is outside this block's %zu slots",
+                        (long long)s, block->cells.size());
+        auto& cell = block->cells[static_cast<size_t>(s)];
+        if (cell.kind == Kind::GRef) {
+            reinterpret_cast<hk::abi::GRefMirror*>(cell.bytes)->data_ = reinterpret_cast<double*>(ptrs[i]);
+        } else if (cell.kind == Kind::Handle || cell.kind == Kind::IntHandle) {
+            reinterpret_cast<hk::abi::ScalarHandle*>(cell.bytes)->data = reinterpret_cast<void*>(ptrs[i]);
+        } else {
+            return fail(HKB_ERR_ARGUMENT, "rebind: slot %lld is a by-value slot and carries no pointer; "
+                        "set it with bind (rebind is the pointer path)", (long long)s);
+        }
+    }
+    return HKB_OK;
+}
+
+// --------------------------------------------------------------------- launch
+
+int hkb_entry_launch(hkb_entry* entry, hkb_argblock* block, int64_t base, int64_t count,
+                     int64_t n_samples, void* stream) {
+    if (entry == nullptr || block == nullptr) return fail(HKB_ERR_ARGUMENT, "hkb_entry_launch: null argument");
+    if (base < 0 || count < 0 || base + count > n_samples)
+        return fail(HKB_ERR_RANGE, "partition [%lld, %lld) is outside the %lld samples",
+                    (long long)base, (long long)(base + count), (long long)n_samples);
+    if (count == 0) return HKB_OK;
+    DeviceScope scope(entry->lib->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "selecting the device");
+    std::vector<void*> args(block->params);
+    long long b = base, c = count, ns = n_samples;
+    args.push_back(&b);
+    args.push_back(&c);
+    args.push_back(&ns);
+    const dim3 grid(static_cast<unsigned>(grid_for(entry, count)));
+    const cudaError_t err = cudaLaunchKernel(reinterpret_cast<const void*>(entry->kernel), grid, dim3(kBlock),
+                                             args.data(), 0, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "launching the entry");
+    return HKB_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------ the finish tree
+
+namespace {
+
+constexpr int kMaxCols = 8;
+
+struct Columns {
+    const void* hi[kMaxCols];
+    const void* comp[kMaxCols];
+};
+
+// One block per (leaf, column): the slot walk (16 terms per slot, Neumaier
+// steps in order), then the halving tree over the 256 slots
+// (hawk/_cells.py:71-91).
+template <class T, int OP>
+__global__ void __launch_bounds__(hk::ss::kSlots) leaves_kernel(Columns cols, long long rows, long long leaves,
+                                                                  T* leaf_hi, T* leaf_comp) {
+    __shared__ T sh[hk::ss::kSlots];
+    __shared__ T sc[hk::ss::kSlots];
+    const int col = blockIdx.y;
+    const long long leaf = blockIdx.x;
+    const T* hi = static_cast<const T*>(cols.hi[col]);
+    const T* comp = static_cast<const T*>(cols.comp[col]);
+    const long long r0 = leaf * hk::ss::kLeaf;
+    const long long left = rows - r0;
+    const int cnt = static_cast<int>(left < hk::ss::kLeaf ? left : hk::ss::kLeaf);
+    const int live = cnt < hk::ss::kSlots ? cnt : hk::ss::kSlots;
+    const int s = threadIdx.x;
+    T h = T(0), c = T(0);
+    if (s < live) {
+        h = hi[r0 + s];
+        c = (OP == hk::ss::kSum && comp != nullptr) ? comp[r0 + s] : T(0);
+        if (!hk::ss::finite(h)) c = T(0);
+#pragma unroll 1
+        for (int k = 1; k < hk::ss::kTerms; ++k) {
+            const int rest = cnt - k * hk::ss::kSlots;
+            const int m = rest < live ? rest : live;
+            if (m <= 0) break;
+            if (s < m) {
+                const long long r = r0 + static_cast<long long>(k) * hk::ss::kSlots + s;
+                const T xc = (OP == hk::ss::kSum && comp != nullptr) ? comp[r] : T(0);
+                hk::ss::neumaier_add<OP>(h, c, hi[r], xc);
+            }
+        }
+    }
+    sh[s] = h;
+    sc[s] = c;
+    __syncthreads();
+#pragma unroll 1
+    for (int off = hk::ss::kSlots / 2; off > 0; off >>= 1) {
+        const int lim = live > off ? (off < live - off ? off : live - off) : 0;
+        T a = T(0), ac = T(0);
+        if (s < lim) {
+            a = sh[s];
+            ac = sc[s];
+            hk::ss::tree_join<OP>(a, ac, sh[s + off], sc[s + off]);
+        }
+        __syncthreads();
+        if (s < lim) {
+            sh[s] = a;
+            sc[s] = ac;
+        }
+        __syncthreads();
+    }
+    if (s == 0) {
+        leaf_hi[col * leaves + leaf] = sh[0];
+        leaf_comp[col * leaves + leaf] = sc[0];
+    }
+}
+
+// One block per column: the pairwise levels over the leaves, in place (the
+// partial of level s sits at index k * 2^s), then hi + comp (hawk/_cells.py:108-119).
+template <class T, int OP>
+__global__ void __launch_bounds__(1024) tree_kernel(T* leaf_hi, T* leaf_comp, long long leaves, T* out) {
+    const int col = blockIdx.x;
+    T* h = leaf_hi + col * leaves;
+    T* c = leaf_comp + col * leaves;
+    for (long long st = 1; st < leaves; st <<= 1) {
+        for (long long idx = static_cast<long long>(threadIdx.x) * 2 * st; idx < leaves;
+             idx += static_cast<long long>(blockDim.x) * 2 * st) {
+            if (idx + st < leaves) {
+                T a = h[idx], ac = c[idx];
+                hk::ss::tree_join<OP>(a, ac, h[idx + st], c[idx + st]);
+                h[idx] = a;
+                c[idx] = ac;
+            }
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        const T v = h[0];
+        out[col] = (OP == hk::ss::kSum) ? (hk::ss::finite(v) ? v + c[0] : v) : v;
+    }
+}
+
+template <class T>
+int launch_leaves(int op, const Columns& cols, int ncols, int64_t rows, int64_t leaves, void* lh, void* lc,
+                  cudaStream_t stream) {
+    const dim3 grid(static_cast<unsigned>(leaves), static_cast<unsigned>(ncols));
+    T* h = static_cast<T*>(lh);
+    T* c = static_cast<T*>(lc);
+    switch (op) {
+        case HKB_OP_SUM: leaves_kernel<T, hk::ss::kSum><<<grid, hk::ss::kSlots, 0, stream>>>(cols, rows, leaves, h, c); break;
+        case HKB_OP_MAX: leaves_kernel<T, hk::ss::kMax><<<grid, hk::ss::kSlots, 0, stream>>>(cols, rows, leaves, h, c); break;
+        default: leaves_kernel<T, hk::ss::kMin><<<grid, hk::ss::kSlots, 0, stream>>>(cols, rows, leaves, h, c); break;
+    }
+    HKB_CUDA(cudaGetLastError(), "launching the leaf stage");
+    return HKB_OK;
+}
+
+template <class T>
+int launch_tree(int op, int ncols, void* lh, void* lc, int64_t leaves, void* out, cudaStream_t stream) {
+    T* h = static_cast<T*>(lh);
+    T* c = static_cast<T*>(lc);
+    T* o = static_cast<T*>(out);
+    const int threads = 1024;
+    switch (op) {
+        case HKB_OP_SUM: tree_kernel<T, hk::ss::kSum><<<ncols, threads, 0, stream>>>(h, c, leaves, o); break;
+        case HKB_OP_MAX: tree_kernel<T, hk::ss::kMax><<<ncols, threads, 0, stream>>>(h, c, leaves, o); break;
+        default: tree_kernel<T, hk::ss::kMin><<<ncols, threads, 0, stream>>>(h, c, leaves, o); break;
+    }
+    HKB_CUDA(cudaGetLastError(), "launching the tree stage");
+    return HKB_OK;
+}
+
+int check_cells(int op, int dtype, int ncols) {
+    if (op != HKB_OP_SUM && op != HKB_OP_MAX && op != HKB_OP_MIN) return fail(HKB_ERR_ARGUMENT, "unknown op %d", op);
+    if (dtype != HKB_F64 && dtype != HKB_F32) return fail(HKB_ERR_ARGUMENT, "unknown dtype %d", dtype);
+    if (ncols < 1 || ncols > kMaxCols) return fail(HKB_ERR_RANGE, "ncols %d is outside 1..%d", ncols, kMaxCols);
+    return HKB_OK;
+}
+
+int64_t leaves_of(int64_t rows) { return (rows + HKB_LEAF_ROWS - 1) / HKB_LEAF_ROWS; }
+
+}  // namespace
+
+extern "C" {
+
+int hkb_cells_leaves(int op, int dtype, int ncols, const void* const* hi, const void* const* comp,
+                     int64_t rows, void* leaf_hi, void* leaf_comp, void* stream) {
+    int status = check_cells(op, dtype, ncols);
+    if (status != HKB_OK) return status;
+    if (rows < 1) return fail(HKB_ERR_RANGE, "a finish needs at least one row, got %lld", (long long)rows);
+    if (hi == nullptr || leaf_hi == nullptr || leaf_comp == nullptr)
+        return fail(HKB_ERR_ARGUMENT, "hkb_cells_leaves: null pointer");
+    const int64_t leaves = leaves_of(rows);
+    if (leaves > 2147483647LL) return fail(HKB_ERR_RANGE, "too many leaves (%lld)", (long long)leaves);
+    Columns cols;
+    for (int k = 0; k < kMaxCols; ++k) {
+        cols.hi[k] = k < ncols ? hi[k] : nullptr;
+        cols.comp[k] = (k < ncols && comp != nullptr) ? comp[k] : nullptr;
+        if (k < ncols && cols.hi[k] == nullptr) return fail(HKB_ERR_ARGUMENT, "column %d has no rows", k);
+        if (k < ncols && op == HKB_OP_SUM && cols.comp[k] == nullptr)
+            return fail(HKB_ERR_ARGUMENT, "column %d of a sum has no compensation rows", k);
+    }
+    auto s = static_cast<cudaStream_t>(stream);
+    return dtype == HKB_F64 ? launch_leaves<double>(op, cols, ncols, rows, leaves, leaf_hi, leaf_comp, s)
+                            : launch_leaves<float>(op, cols, ncols, rows, leaves, leaf_hi, leaf_comp, s);
+}
+
+int hkb_cells_tree(int op, int dtype, int ncols, void* leaf_hi, void* leaf_comp, int64_t leaves, void* out,
+                   void* stream) {
+    int status = check_cells(op, dtype, ncols);
+    if (status != HKB_OK) return status;
+    if (leaves < 1) return fail(HKB_ERR_RANGE, "a tree needs at least one leaf");
+    if (leaf_hi == nullptr || leaf_comp == nullptr || out == nullptr)
+        return fail(HKB_ERR_ARGUMENT, "hkb_cells_tree: null pointer");
+    auto s = static_cast<cudaStream_t>(stream);
+    return dtype == HKB_F64 ? launch_tree<double>(op, ncols, leaf_hi, leaf_comp, leaves, out, s)
+                            : launch_tree<float>(op, ncols, leaf_hi, leaf_comp, leaves, out, s);
+}
+
+size_t hkb_cells_scratch_bytes(int dtype, int ncols, int64_t rows) {
+    const size_t elem = dtype == HKB_F32 ? sizeof(float) : sizeof(double);
+    const int64_t leaves = rows < 1 ? 1 : leaves_of(rows);
+    return 2 * static_cast<size_t>(ncols < 1 ? 1 : ncols) * static_cast<size_t>(leaves) * elem;
+}
+
+int hkb_cells_finish(int op, int dtype, int ncols, const void* const* hi, const void* const* comp,
+                     int64_t rows, void* scratch, void* out, void* stream) {
+    if (scratch == nullptr) return fail(HKB_ERR_ARGUMENT, "hkb_cells_finish: null scratch");
+    const size_t elem = dtype == HKB_F32 ? sizeof(float) : sizeof(double);
+    const int64_t leaves = leaves_of(rows < 1 ? 1 : rows);
+    char* lh = static_cast<char*>(scratch);
+    char* lc = lh + static_cast<size_t>(ncols < 1 ? 1 : ncols) * static_cast<size_t>(leaves) * elem;
+    int status = hkb_cells_leaves(op, dtype, ncols, hi, comp, rows, lh, lc, stream);
+    if (status != HKB_OK) return status;
+    return hkb_cells_tree(op, dtype, ncols, lh, lc, leaves, out, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,339 @@
+"""Load and run b200 artifacts on device planes: the device twin of ``hawk.load`` / ``hawk.run``.
+
+The reference's runtime (hawk/runtime.py:494-602) loads a host artifact,
+validates every bound plane against the sidecar (hawk/_bind_checks.py:436),
+binds each slot into an argument block and calls the entry once over
+``[base, base + count)``; a kernel that reduces over samples into cells gets
+its row scratch from the runtime, and the rows are finished into the caller's
+cells (hawk/runtime.py:345-360, :588-602, hawk/_cells.py).
+
+This module does the same for the b200 target, with device planes:
+
+* ``load(directory, kernel, mode=..., device=...)`` loads ``<kernel>.<mode>.cubin``
+  through the C ABI (which self-checks its exports) and builds the argument
+  block from the sidecar's slot descriptors;
+* ``run(kernel, **planes)`` validates and binds the planes (dtype, shape,
+  device, contiguity, writability -- every failing argument named in one
+  refusal), launches on the caller's stream and, for a kernel with cells,
+  finishes the rows on the device (``hkb_cells_finish``) into the cells.
+
+Launches are asynchronous on the stream (the current torch stream of the
+kernel's device unless ``stream=`` names one); the cells hold their values
+when the stream reaches them.  One ``DeviceKernel`` shared by threads
+serialises its bind+launch under its lock, as the reference's HostKernel does
+(hawk/runtime.py:46-54).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import json
+import threading
+from pathlib import Path
+
+from . import abi
+from .errors import HawkError
+from .planes import Plane, as_plane
+
+#: Roles whose plane's trailing extent is the sample count (they vote on n).
+PER_SAMPLE_ROLES = ("mutable", "out", "vec_in", "mat_in", "per_sample")
+#: Roles that are written by the kernel (their plane must be writable).
+SINK_ROLES = ("mutable", "out", "accum_out")
+ROW = 32
+
+_WIRE_OF_MODE = {"float64": "float64", "float32": "float32"}
+_INT_DTYPES = ("i32", "i64", "int32", "uint32")
+
+
+def descriptor_for_sidecar(sidecar: dict) -> list:
+    """The argument-block kind of every slot, in arg_spec order (the rule of
+    the reference's ``kind_for``, hawk/runtime.py:96-118)."""
+    mode = sidecar.get("scalar_type", "float64")
+    kinds = []
+    for slot in sidecar["b200"]["slots"]:
+        role, dtype, shape = slot["role"], slot["dtype"], slot["shape"]
+        if role == "nsamples":
+            kinds.append("nsamples")
+        elif role == "uniform":
+            kinds.append("int" if dtype in _INT_DTYPES else ("f32" if mode == "float32" else "f64"))
+        elif role in ("vec_in", "mat_in", "out") or (role == "mutable" and shape):
+            kinds.append("gref")
+        elif dtype in _INT_DTYPES:
+            kinds.append("int_handle")
+        else:
+            kinds.append("handle")
+    return kinds
+
+
+def _box(kind: str, value):
+    if kind == "f64":
+        return ctypes.c_double(float(value))
+    if kind == "f32":
+        return ctypes.c_float(float(value))
+    if kind in ("int", "nsamples"):
+        return ctypes.c_longlong(int(value))
+    raise HawkError(f"slot kind {kind!r} is not a by-value slot")
+
+
+class DeviceKernel:
+    """One b200 artifact's entry on one device, self-checked at load."""
+
+    def __init__(self, directory, kernel: str, mode: str = "float64", device: int | None = None,
+                 sidecar: dict | None = None) -> None:
+        self.directory = Path(directory)
+        stem = f"{kernel}.{mode}"
+        if sidecar is None:
+            path = self.directory / f"{stem}.json"
+            if not path.exists():
+                raise HawkError(f"no b200 artifact {stem!r} in {self.directory} (no {path.name})")
+            sidecar = json.loads(path.read_text())
+        if "b200" not in sidecar:
+            raise HawkError(f"{stem}: its sidecar carries no 'b200' block; it was not built for the b200 target")
+        self.sidecar = sidecar
+        self.name = sidecar["kernel"]
+        self.mode = sidecar.get("scalar_type", mode)
+        b200 = sidecar["b200"]
+        self.frame = b200["frame"]
+        self.sums = b200["sample_sums"]
+        self.slots = [(s["role"], s["name"], s["dtype"], tuple(s["shape"])) for s in b200["slots"]]
+        self.arg_spec = tuple((r, n) for r, n, _d, _s in self.slots)
+        self.cells = sidecar.get("cells") or {}
+        if device is None:
+            device = _current_device()
+        self.device = int(device)
+        self.library = abi.Library(self.directory / b200["cubin"], self.device)
+        self.entry = self.library.entry(b200["entry"])
+        self.descriptor = descriptor_for_sidecar(sidecar)
+        self.block = abi.ArgBlock(self.descriptor)
+        self._lock = threading.Lock()
+        self._held: list = []
+        self._scratch: dict = {}
+
+    # -- validation ---------------------------------------------------------
+    def _wire(self, name: str, dtype: str) -> str:
+        if dtype in _INT_DTYPES:
+            return {"i32": "int32", "i64": "int64"}.get(dtype, dtype)
+        return self.sidecar.get("arg_dtypes", {}).get(name) or _WIRE_OF_MODE[self.mode]
+
+    def n_from(self, planes: dict) -> int:
+        """The sample count every bound per-sample plane agrees on."""
+        votes = {}
+        for role, name, _dtype, shape in self.slots:
+            if role not in PER_SAMPLE_ROLES or name not in planes:
+                continue
+            p = planes[name]
+            if len(p.shape) != len(shape) + 1:
+                continue                    # refused with its shape by the checks
+            votes[name] = p.shape[-1]
+        if not votes:
+            raise HawkError(f"kernel {self.name!r}: no bound per-sample plane to read the sample count "
+                            "from; pass n_samples= explicitly")
+        if len(set(votes.values())) != 1:
+            raise HawkError(f"kernel {self.name!r}: the bound per-sample planes disagree on the sample "
+                            f"count: {sorted(votes.items())} -- pass n_samples= explicitly")
+        return next(iter(votes.values()))
+
+    def check(self, planes: dict, values: dict, n: int) -> None:
+        """Every slot against its declaration; one refusal naming every failure."""
+        errors = []
+        for role, name, dtype, shape in self.slots:
+            if role == "nsamples":
+                continue
+            if role == "uniform":
+                if name not in values:
+                    errors.append(f"argument {name!r}: this kernel declares a 'uniform' slot for it, "
+                                  "but no value was bound")
+                elif dtype in _INT_DTYPES and isinstance(values[name], float):
+                    errors.append(f"argument {name!r}: expected an int uniform, got a float value")
+                continue
+            if name not in planes:
+                errors.append(f"argument {name!r}: this kernel declares a {role!r} slot for it, "
+                              "but no plane was bound")
+                continue
+            p: Plane = planes[name]
+            want = self._wire(name, dtype)
+            if p.dtype != want:
+                errors.append(f"argument {name!r}: expected dtype {want}, got {p.dtype}")
+            if p.device is None:
+                errors.append(f"argument {name!r}: a host array; the b200 path binds device planes only")
+            elif p.device != self.device:
+                errors.append(f"argument {name!r}: on device {p.device}, the kernel is loaded on "
+                              f"device {self.device}")
+            if not p.contiguous:
+                errors.append(f"argument {name!r}: the plane is bound by address at computed sample "
+                              "offsets, so it must be C-contiguous")
+            if role in SINK_ROLES and p.readonly:
+                errors.append(f"argument {name!r}: a {role!r} plane is written and must be writable")
+            if role == "accum_out":
+                rows = -(-n // ROW)
+                if len(p.shape) != 1 or p.shape[0] < rows:
+                    errors.append(f"argument {name!r}: a row plane of {rows} rows (one per 32 samples) "
+                                  f"is expected, got shape {p.shape}")
+            elif role == "lookup":
+                if len(p.shape) != 1 or p.shape[0] < 1:
+                    errors.append(f"argument {name!r}: a lookup plane is 1-D and non-empty, got shape {p.shape}")
+            else:
+                want_shape = (*shape, "L")
+                if len(p.shape) != len(shape) + 1 or tuple(p.shape[:-1]) != tuple(shape):
+                    errors.append(f"argument {name!r}: expected shape {want_shape} (samples last), "
+                                  f"got {p.shape}")
+                elif p.shape[-1] < n:
+                    errors.append(f"argument {name!r}: holds {p.shape[-1]} samples, fewer than "
+                                  f"n_samples={n}")
+        if errors:
+            if len(errors) == 1:
+                raise HawkError(f"kernel {self.name!r}: {errors[0]}")
+            raise HawkError(f"kernel {self.name!r}: {len(errors)} arguments failed validation:\n"
+                            + "\n".join(f"  - {e}" for e in errors))
+
+    # -- bind + launch ------------------------------------------------------
+    def bind_all(self, planes: dict, values: dict, n: int) -> None:
+        """Bind every slot (planes already validated)."""
+        held = []
+        for slot, (role, name, _dtype, _shape) in enumerate(self.slots):
+            kind = self.descriptor[slot]
+            if role == "nsamples":
+                box = _box(kind, n)
+                held.append(box)
+                self.block.bind(slot, ctypes.addressof(box), n, 1, 1, 0)
+            elif role == "uniform":
+                box = _box(kind, values[name])
+                held.append(box)
+                self.block.bind(slot, ctypes.addressof(box), n, 1, 1, 0)
+            else:
+                p = planes[name]
+                samples = p.shape[-1] if p.shape else 1
+                self.block.bind(slot, p.ptr, samples, 1, 2, self.device)
+                held.append(p.keep)
+        self._held = held
+
+    def launch(self, base: int, count: int, n_samples: int, stream: int | None = None) -> None:
+        """The launch crossing over ``[base, base + count)`` of the bound planes."""
+        if self.frame == "row" and base % ROW:
+            raise HawkError(f"kernel {self.name!r} reduces over 32-sample rows, so a partition must "
+                            f"start on a row (base % 32 == 0), got base={base}")
+        self.entry.launch(self.block, base, count, n_samples, _stream(stream, self.device))
+
+    def _rows_for(self, n: int):
+        """The row scratch of every cell at sample count ``n`` (made once per n)."""
+        import torch
+
+        if n not in self._scratch:
+            rows = -(-n // ROW)
+            dt = torch.float64 if self.mode == "float64" else torch.float32
+            dev = torch.device("cuda", self.device)
+            planes = {}
+            for s in self.sums:
+                planes[s["name"]] = torch.empty(rows, dtype=dt, device=dev)
+                if s["companion"]:
+                    planes[s["companion"]] = torch.empty(rows, dtype=dt, device=dev)
+            scratch = torch.empty(abi.cells_scratch_bytes(self.mode, max(len(self.sums), 1), rows),
+                                  dtype=torch.uint8, device=dev)
+            self._scratch[n] = (planes, scratch)
+        return self._scratch[n]
+
+    def finish_cells(self, rows: dict, scratch, outputs: dict, lo: int, hi: int,
+                     stream: int | None = None) -> None:
+        """Rows ``[lo, hi)`` of every cell finished into ``outputs`` (device pointers)."""
+        itemsize = 8 if self.mode == "float64" else 4
+        op = self.sums[0]["op"] if self.sums else "sum"
+        his = [rows[s["name"]].data_ptr() + lo * itemsize for s in self.sums]
+        comps = ([rows[s["companion"]].data_ptr() + lo * itemsize for s in self.sums]
+                 if op == "sum" else None)
+        # cells are written one per column; each cell plane here is its own output
+        for k, s in enumerate(self.sums):
+            out = outputs[s["name"]]
+            abi.cells_finish(op, self.mode, [his[k]], None if comps is None else [comps[k]], hi - lo,
+                             scratch.data_ptr(), out.ptr, _stream(stream, self.device))
+
+
+def _current_device() -> int:
+    try:
+        import torch
+        if torch.cuda.is_available():
+            return torch.cuda.current_device()
+    except ImportError:                                 # pragma: no cover
+        pass
+    return 0
+
+
+def _stream(stream, device: int) -> int:
+    if stream is not None:
+        return int(getattr(stream, "cuda_stream", stream))
+    try:
+        import torch
+        return int(torch.cuda.current_stream(device).cuda_stream)
+    except Exception:                                   # noqa: BLE001
+        return 0
+
+
+_CACHE: dict = {}
+_CACHE_LOCK = threading.Lock()
+
+
+def load(directory, kernel: str, mode: str = "float64", device: int | None = None) -> DeviceKernel:
+    """Load ``<directory>/<kernel>.<mode>.cubin`` on ``device`` (cached per process)."""
+    key = (str(Path(directory).resolve()), kernel, mode, device if device is not None else _current_device())
+    with _CACHE_LOCK:
+        if key not in _CACHE:
+            _CACHE[key] = DeviceKernel(directory, kernel, mode, key[3])
+        return _CACHE[key]
+
+
+def run(kernel: DeviceKernel, *, base: int = 0, count: int | None = None, n_samples: int | None = None,
+        stream=None, **arrays) -> None:
+    """Bind ``arrays`` and run the whole range in one launch (asynchronous on ``stream``).
+
+    ``count`` defaults to ``n_samples``, ``n_samples`` to the count every bound
+    per-sample plane agrees on.  A kernel with cells takes each cell as a
+    one-element device plane (not its rows, as hawk/runtime.py:345-360 rules);
+    the runtime owns the rows and finishes them on the device."""
+    declared = {name for _r, name in kernel.arg_spec} | set(kernel.cells)
+    unknown = sorted(set(arrays) - declared)
+    if unknown:
+        raise HawkError(f"kernel {kernel.name!r}: {unknown} are not planes it declares "
+                        f"(declared: {sorted(declared)})")
+    values = {}
+    planes = {}
+    uniforms = {n for r, n in kernel.arg_spec if r == "uniform"}
+    for name, obj in arrays.items():
+        if name in uniforms:
+            values[name] = obj
+        else:
+            planes[name] = as_plane(name, obj)
+    cells = kernel.cells
+    if cells:
+        rows_bound = [c for c in cells if c in planes and planes[c].size > 1]
+        missing = [c for c in cells if c not in planes]
+        if missing or rows_bound:
+            raise HawkError(f"kernel {kernel.name!r}: this kernel reduces over samples into the cells "
+                            f"{sorted(cells)}; bind each cell (one value per column), not its rows"
+                            + (f" (missing: {missing})" if missing else ""))
+    with kernel._lock:
+        if n_samples is None:
+            n_samples = kernel.n_from(planes)
+        count = n_samples - base if count is None else count
+        if base < 0 or count < 0 or base + count > n_samples:
+            raise HawkError(f"kernel {kernel.name!r}: partition [{base}, {base + count}) is outside "
+                            f"the {n_samples} samples")
+        outputs = {}
+        scratch = None
+        if cells:
+            for c in cells:
+                p = planes[c]
+                want = kernel.mode
+                if p.dtype != want or p.device != kernel.device:
+                    raise HawkError(f"kernel {kernel.name!r}: cell {c!r} must be a {want} plane on device "
+                                    f"{kernel.device}, got {p.dtype} on {p.device}")
+                outputs[c] = p
+            rows, scratch = kernel._rows_for(n_samples)
+            bound = {k: v for k, v in planes.items() if k not in cells}
+            from .planes import from_torch
+            bound.update({k: from_torch(v) for k, v in rows.items()})
+        else:
+            bound = planes
+        kernel.check(bound, values, n_samples)
+        kernel.bind_all(bound, values, n_samples)
+        kernel.launch(base, count, n_samples, stream)
+        if cells and count > 0:
+            kernel.finish_cells(rows, scratch, outputs, base // ROW, -(-(base + count) // ROW), stream)

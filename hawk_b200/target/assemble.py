@@ -1,0 +1,124 @@
+"""One b200 translation unit around the reference renderer's body.
+
+The b200 counterpart of the reference's ``render_source``
+(hawk/emit/wrapper.py:1132-1271): the body STRING is rendered by the
+reference's one renderer (``render_body``, hawk/emit/render.py:140) through the
+b200 writer; the unit around it -- prelude, self-check exports, entry
+signature, unpack, frame -- is this build's.  The prelude includes the
+hand-written sm_100a device library (``hk/hawk_b200.cuh``) instead of the
+reference's third-party numerics headers, so the unit compiles under NVRTC with
+nothing else on the include path.
+
+Everything the b200 target does not build is refused here, by name, before any
+text reaches a compiler.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import re
+from dataclasses import dataclass, field
+
+from ..errors import HawkError
+from .wrapper import B200, sample_sum_store
+from .writer import B200_WRITER, body_text
+
+#: Scalar modes the b200 target builds: the reference's float64 and float32
+#: (hawk/emit/wrapper.py:136-143).  The banded mode is a host/cells form.
+MODES = {"float64": "double", "float32": "float"}
+
+#: Library namespaces the device library does not provide: a body naming one is
+#: refused with the construct it stands for.
+_UNBUILT = {
+    "hk::rt::": "runtime-index stores and rolled products (aether::rt)",
+    "hk::geometry::": "ray primitives",
+    "hk::banded::": "the banded scalar mode",
+    "hk::random::": "in-kernel random draws",
+    "hk::accum::": "run and compensated scatter commits",
+    "hk::linalg::team::": "team linear algebra (n > 32)",
+    "hk::linalg::eigh": "the symmetric eigensolver",
+    "hawk_abi::accum_": "scattered accumulates",
+    "hawk_abi::finish_count": "kernels that finish their own samples",
+    "hawk_abi::mix_count": "auto dispatch branch counts",
+    "hawk_abi::tiled": "wide (tiled) scratch planes",
+    "hawk_abi::warp_sum": "warp-per-lane sums",
+    "hawk_abi::spacing": "the spacing op",
+}
+
+
+@dataclass(frozen=True)
+class Unit:
+    """One emitted unit: its text, the entry name, and the facts the sidecar records."""
+
+    name: str
+    mode: str
+    text: str
+    body: str
+    frame: str                      # "lane" or "row"
+    sums: tuple = ()                # ((name, op, companion or None), ...) in column order
+    digest: str = ""
+    notes: dict = field(default_factory=dict)
+
+
+def _refuse(name: str, walk) -> None:
+    if getattr(walk, "finish", None) is not None:
+        raise HawkError(f"{name!r}: a kernel that finishes its own samples is not built on the b200 target")
+    if walk.companions:
+        raise HawkError(f"{name!r}: compensated keyed sums (owned companions) are not built on the b200 target")
+    for role, slot in walk.arg_spec:
+        if role in ("terminated", "wide_in", "wide_out"):
+            raise HawkError(f"{name!r}: slot {slot!r} has role {role!r}, which the b200 target does not build")
+
+
+def render_unit(kernel, name: str | None = None, mode: str = "float64") -> Unit:
+    """The b200 unit of a traced kernel (``hawk.Kernel``) in scalar mode ``mode``."""
+    from hawk.ir.nodes import sample_sums
+    from hawk.emit.render import render_body
+    from hawk.emit.spelling import element_spelling
+
+    if mode not in MODES:
+        raise HawkError(f"scalar mode {mode!r} is not built on the b200 target (built: {sorted(MODES)})")
+    name = name or kernel.name
+    walk, sinks = kernel.walk, kernel.sinks
+    _refuse(name, walk)
+    rendered = render_body(sinks, walk, indent="        ", writer=B200_WRITER)
+    body = body_text(rendered.text)
+    for token, what in _UNBUILT.items():
+        if token in body:
+            raise HawkError(f"{name!r}: its body uses {what}, which the b200 target does not build yet")
+    sums = sample_sums(sinks)
+    if len({s.op for s in sums}) > 1:
+        raise HawkError(f"{name!r}: one kernel reduces over samples with one op (sum, max or min)")
+    wrapper = B200
+    if sums:
+        elem = element_spelling(sums[0].ttype.dtype)
+        opened, closed = wrapper.sample_sum_frame(len(sums), elem, sample_sum_store(sums), sums[0].op)
+        loop = [opened, body, closed]
+        frame = "row"
+    else:
+        loop = [wrapper.index_prologue(), body, wrapper.index_epilogue()]
+        frame = "lane"
+    parts = [
+        f"// hawk_b200 unit {name!r} (scalar mode {mode}), sm_100a.",
+        "// Body text: the reference renderer's; entry, views and frame: the b200 wrapper.",
+        '#include "hk/hawk_b200.cuh"',
+        "",
+        f"using Real = {MODES[mode]};",
+        "using Int = long long;",
+        "",
+        "HK_SELF_CHECK_EXPORTS",
+        "",
+        wrapper.entry_signature(walk, name),
+        "{",
+        wrapper.unpack(walk),
+        *loop,
+        "}",
+        "",
+    ]
+    text = "\n".join(parts)
+    records = tuple((s.name, s.op, s.companion.name if s.op == "sum" else None) for s in sums)
+    return Unit(name=name, mode=mode, text=text, body=body, frame=frame, sums=records,
+                digest=hashlib.sha256(text.encode()).hexdigest())
+
+
+_IDENT = re.compile(r"[A-Za-z_][A-Za-z0-9_]*")

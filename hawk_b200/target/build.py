@@ -1,0 +1,113 @@
+"""Build b200 bundles: unit text, CUBIN and sidecar per kernel and scalar mode.
+
+The b200 counterpart of the reference's ``build_bundle``
+(hawk/artifact/bundle.py:1349) for one row: for each kernel it renders the
+unit (``assemble.render_unit``), compiles it with NVRTC at sm_100a, and writes
+
+* ``<name>.<mode>.cu``   the unit text (what was compiled),
+* ``<name>.<mode>.cubin`` the sm_100a image the runtime loads,
+* ``<name>.<mode>.json`` the sidecar: the reference's v2 sidecar fields the
+  runtime binds from (``arg_spec``, ``arg_shapes``, ``arg_dtypes``,
+  ``mutables``, ``vec_widths``, ``mat_shapes``, ``params``, ``param_planes``,
+  ``accum_outputs``, ``digest`` ..., hawk/artifact/sidecar.py:348-486) plus a
+  ``b200`` block (entry, frame, sample sums, arch, NVRTC options, ptxas report).
+"""
+
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+from ..errors import HawkError
+from .assemble import render_unit
+from .nvrtc import ARCH, compile_cubin, options
+
+
+def _reference_sidecar(name: str, walk, mode: str) -> dict:
+    """The reference's v2 sidecar for the kernel (its own function), or the
+    subset this runtime reads when that function needs the reference's
+    third-party packages."""
+    from unittest import mock
+
+    try:
+        from hawk.artifact import sidecar as sc
+
+        # The reference records where its third-party headers came from; a b200
+        # unit includes only this build's device library, so that is recorded.
+        with mock.patch.object(sc, "_root_or_sealed_marker", lambda resolver: "hawk_b200/csrc/include"):
+            return sc.sidecar_meta(name, walk, fmt="cubin", scalar_type=mode, exec_targets=("device",))
+    except Exception:                                   # noqa: BLE001 -- fall back to the read subset
+        return _subset_sidecar(name, walk, mode)
+
+
+def _subset_sidecar(name: str, walk, mode: str) -> dict:
+    from hawk.artifact import sidecar as sc
+
+    return {
+        "format": "cubin",
+        "kernel": name,
+        "scalar_type": mode,
+        "arg_spec": [list(p) for p in walk.arg_spec],
+        "arg_shapes": sc._arg_shapes(walk),
+        "arg_dtypes": sc._arg_dtypes(walk, mode),
+        "mutables": sc._mutables(walk),
+        "vec_widths": {n: int(walk.slot_types[("vec_in", n)].shape[0])
+                       for r, n in walk.arg_spec if r == "vec_in"},
+        "mat_shapes": {n: list(walk.slot_types[("mat_in", n)].shape)
+                       for r, n in walk.arg_spec if r == "mat_in"},
+        "params": sc._params(walk),
+        "accum_outputs": [n for r, n in walk.arg_spec if r == "accum_out"],
+        **({"param_planes": list(walk.param_planes)} if walk.param_planes else {}),
+        **({"cells": walk.cells} if walk.cells else {}),
+        "digest": walk.digest,
+    }
+
+
+def _slot_records(walk) -> list:
+    """Per slot, in arg_spec order: role, name, dtype and shape of the plane."""
+    out = []
+    for role, name in walk.arg_spec:
+        t = walk.slot_types[(role, name)]
+        out.append({"role": role, "name": name, "dtype": t.dtype,
+                    "shape": [int(e) for e in t.shape]})
+    return out
+
+
+def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "float64") -> dict:
+    """Render, compile and write one kernel's b200 artifact; returns its sidecar."""
+    directory = Path(directory)
+    directory.mkdir(parents=True, exist_ok=True)
+    name = name or kernel.name
+    unit = render_unit(kernel, name, mode)
+    cubin, log, ptxas = compile_cubin(unit.text, name)
+    stem = f"{name}.{mode}"
+    (directory / f"{stem}.cu").write_text(unit.text)
+    (directory / f"{stem}.cubin").write_bytes(cubin)
+    sidecar = _reference_sidecar(name, kernel.walk, mode)
+    sidecar = json.loads(json.dumps(sidecar, default=str))
+    sidecar["b200"] = {
+        "entry": name,
+        "arch": ARCH,
+        "unit": f"{stem}.cu",
+        "cubin": f"{stem}.cubin",
+        "unit_digest": unit.digest,
+        "frame": unit.frame,
+        "sample_sums": [{"name": n, "op": op, "companion": comp} for n, op, comp in unit.sums],
+        "slots": _slot_records(kernel.walk),
+        "nvrtc_options": [o for o in options() if not o.startswith("-I")],
+        "ptxas": ptxas,
+    }
+    (directory / f"{stem}.json").write_text(json.dumps(sidecar, indent=1, sort_keys=True))
+    return sidecar
+
+
+def build(kernels, directory, *, modes=("float64",)) -> dict:
+    """Build every kernel in every mode; ``{(name, mode): sidecar}``."""
+    out = {}
+    for kernel in kernels:
+        for mode in modes:
+            try:
+                out[(kernel.name, mode)] = build_kernel(kernel, directory, mode=mode)
+            except HawkError:
+                raise
+    return out

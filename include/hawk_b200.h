@@ -1,0 +1,141 @@
+/*
+ * hawk_b200.h -- the C ABI of the B200 (sm_100a) execution path for hawk kernels.
+ *
+ * The reference runs a built kernel through its native binding hawk._core
+ * (src/hawk_core.cpp, a nanobind module): it loads the artifact, self-checks
+ * its ABI exports, packs every plane into a by-value mirror in an argument
+ * block and calls the entry over a partition [base, base + count) of nSamples.
+ * This library is the device twin of that binding, with plain C types only:
+ * each entry point below names the hawk._core member it replaces.  Beyond it,
+ * the library finishes sample-sum rows into cells on the device (the
+ * reference does that in numpy, hawk/_cells.py:94-119).
+ *
+ * Conventions.
+ *   - Every function returns HKB_OK (0) or a nonzero status; the message of
+ *     the last failure on the calling thread is hkb_last_error().
+ *   - Pointers to planes are device pointers (CUDA unified addressing);
+ *     `stream` is a cudaStream_t (NULL: the legacy default stream).  Launch
+ *     entry points are asynchronous on that stream and allocate nothing.
+ *   - A library handle is usable from any thread; an argument block is not
+ *     synchronised -- one block per thread, or the caller orders the calls
+ *     (the reference's HostKernel lock, hawk/runtime.py:46-54).
+ */
+#ifndef HAWK_B200_H
+#define HAWK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+#define HKB_OK 0
+#define HKB_ERR_ARGUMENT 1   /* a bad argument (slot out of range, null pointer, unknown kind) */
+#define HKB_ERR_CUDA 2       /* a CUDA runtime call failed (message names it) */
+#define HKB_ERR_ABI 3        /* an artifact whose self-check exports disagree */
+#define HKB_ERR_NOT_FOUND 4  /* no such entry in the artifact */
+#define HKB_ERR_RANGE 5      /* a partition or size outside what the call accepts */
+
+/* Sample-sum ops (hawk/emit/wrapper.py:719 SAMPLE_SUM_OP_CODE) and element types. */
+#define HKB_OP_SUM 0
+#define HKB_OP_MAX 1
+#define HKB_OP_MIN 2
+#define HKB_F64 0
+#define HKB_F32 1
+
+/* Rows per leaf of the ordered finish tree (hawk/_cells.py:25-27: 256 slots x 16 terms). */
+#define HKB_LEAF_ROWS 4096
+
+typedef struct hkb_library hkb_library;   /* one loaded sm_100a artifact (CUBIN) */
+typedef struct hkb_entry hkb_entry;       /* one __global__ entry of it */
+typedef struct hkb_argblock hkb_argblock; /* the by-value argument cells of an entry */
+
+/* The message of the last failed call on this thread ("" if none). */
+const char* hkb_last_error(void);
+
+/* ----------------------------------------------------------- build facts */
+
+/* hawk._core.build_digest() (src/hawk_core.cpp:523-530): the sha256 of the
+ * sources this library was built from. */
+const char* hkb_build_digest(void);
+
+/* hawk._core.layout_sizes() (src/hawk_core.cpp:531-537): sizeof GRefMirror,
+ * ScalarHandle, IntHandle, the index type and PartitionTriple -- 40, 32, 32, 8, 24. */
+int hkb_layout_sizes(uint64_t out[5]);
+
+/* The number of CUDA devices this process sees (0 without a driver). */
+int hkb_device_count(int* count);
+
+/* -------------------------------------------------------------- library */
+
+/* hawk._core.HostLibrary(path) (src/hawk_core.cpp:354-427, :654-662): load an sm_100a
+ * CUBIN image onto `device` and check its exports eagle_abi_tag ==
+ * "aether-abi/2" and eagle_layout_sizes == hkb_layout_sizes; a mismatch is
+ * HKB_ERR_ABI naming the field. */
+int hkb_library_load(const void* image, size_t size, int device, hkb_library** out);
+int hkb_library_load_file(const char* path, int device, hkb_library** out);
+void hkb_library_free(hkb_library* lib);
+
+/* HostLibrary.entry(name) (src/hawk_core.cpp:663-667): the entry `name`. */
+int hkb_library_entry(hkb_library* lib, const char* name, hkb_entry** out);
+
+/* Facts of an entry: registers per thread, resident blocks per SM at its
+ * block size, the block size, and the grid a launch of `count` samples takes. */
+int hkb_entry_info(hkb_entry* entry, int* regs, int* blocks_per_sm, int* block, int64_t count,
+                   int64_t* grid);
+
+/* --------------------------------------------------------- argument block */
+
+/* hawk._core.ArgBlock(descriptor) (src/hawk_core.cpp:185-226, :598-604): one cell per
+ * slot, in arg_spec order; kinds are "gref", "handle", "int_handle", "f64",
+ * "f32", "int", "nsamples" (hawk/runtime.py:96-118). */
+int hkb_argblock_create(const char* const* kinds, size_t n, hkb_argblock** out);
+void hkb_argblock_free(hkb_argblock* block);
+
+/* ArgBlock.bind(slot, ptr, samples, stride, device_type, device_id)
+ * (src/hawk_core.cpp:228-273, :605-613): a plane slot takes the device pointer and the
+ * plane's sample extent (a GRef plane's component pitch is samples * stride);
+ * a by-value slot copies the value at host address `ptr`. */
+int hkb_argblock_bind(hkb_argblock* block, size_t slot, uintptr_t ptr, uint64_t samples,
+                      uint64_t stride, int32_t device_type, int32_t device_id);
+
+/* ArgBlock.rebind(slots, ptrs) (src/hawk_core.cpp:275-305, :614-630): swap the data
+ * pointers of plane slots in one call; a by-value slot is refused. */
+int hkb_argblock_rebind(hkb_argblock* block, const int64_t* slots, const int64_t* ptrs, size_t n);
+
+/* ------------------------------------------------------------------ launch */
+
+/* HostEntry.run(block, base, count, nSamples) (src/hawk_core.cpp:431-442, :642-653):
+ * run the entry over samples [base, base + count) of nSamples on `stream`
+ * (asynchronous).  A kernel with sample sums needs base % 32 == 0. */
+int hkb_entry_launch(hkb_entry* entry, hkb_argblock* block, int64_t base, int64_t count,
+                     int64_t n_samples, void* stream);
+
+/* ---------------------------------------------- cells: the ordered finish */
+
+/* The device form of hawk/_cells.py:finish for `ncols` columns (<= 8) of
+ * `rows` rows each: stage one writes one (hi, comp) partial per leaf of
+ * HKB_LEAF_ROWS rows, stage two folds the leaves pairwise and writes the cell.
+ * hi[k] / comp[k] are device pointers to column k's rows (comp may be NULL for
+ * max/min); dtype is HKB_F64 or HKB_F32; op is an HKB_OP_*.
+ *
+ * hkb_cells_leaves: leaf_hi / leaf_comp hold ncols * ceil(rows / 4096) values
+ *   (column k at k * leaves).
+ * hkb_cells_tree: reads ncols * leaves partials from leaf_hi / leaf_comp
+ *   (overwritten), writes out[k] = the cell of column k.
+ * hkb_cells_finish: both; `scratch` holds hkb_cells_scratch_bytes(...) bytes. */
+int hkb_cells_leaves(int op, int dtype, int ncols, const void* const* hi, const void* const* comp,
+                     int64_t rows, void* leaf_hi, void* leaf_comp, void* stream);
+int hkb_cells_tree(int op, int dtype, int ncols, void* leaf_hi, void* leaf_comp, int64_t leaves,
+                   void* out, void* stream);
+size_t hkb_cells_scratch_bytes(int dtype, int ncols, int64_t rows);
+int hkb_cells_finish(int op, int dtype, int ncols, const void* const* hi, const void* const* comp,
+                     int64_t rows, void* scratch, void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HAWK_B200_H */

@@ -1,0 +1,269 @@
+"""TEST INFRASTRUCTURE ONLY: the CPU oracle of the b200 path.
+
+A plain-C restatement (hawk_oracle.c) of what the reference's host target
+computes for the five benchmark kernels, loaded with ctypes.  Only the tests,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg import this
+package -- as the checker and the timed CPU baseline, never as part of the
+product path.
+
+Parity is pinned by golden vectors made from the reference's own numpy IR
+interpreter (tests/_eval.py in the reference, run on the reference's traced and
+derived IR; tests/golden/make_golden.py) and by the reference's known answers
+(README.md:80-99 energy; the Kepler (e=0.5, M=1) root).
+
+The library is built per host CPU (``-march=native`` like the reference's
+`native` host profile), on first use, under ``oracle/_build/<cpu key>/``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import os
+import subprocess
+import threading
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+MATH_LIBM, MATH_CR = 0, 1
+OP = {"sum": 0, "max": 1, "min": 2}
+_LOCK = threading.Lock()
+_LIB = None
+
+
+def _cpu_key() -> str:
+    try:
+        text = Path("/proc/cpuinfo").read_text()
+    except OSError:
+        text = ""
+    model = next((ln.split(":", 1)[1].strip() for ln in text.splitlines() if ln.startswith("model name")), "")
+    flags = next((ln.split(":", 1)[1].strip() for ln in text.splitlines() if ln.startswith("flags")), "")
+    return hashlib.sha256((model + "|" + flags).encode()).hexdigest()[:12]
+
+
+def library_path() -> Path:
+    return HERE / "_build" / _cpu_key() / "libhawk_oracle.so"
+
+
+def build() -> Path:
+    """Compile the oracle for this host's CPU (once)."""
+    out = library_path()
+    src = [HERE / "hawk_oracle.c", HERE / "hawk_oracle.h"]
+    if out.exists() and out.stat().st_mtime >= max(p.stat().st_mtime for p in src):
+        return out
+    out.parent.mkdir(parents=True, exist_ok=True)
+    cmd = ["gcc", "-O3", "-march=native", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-std=c11",
+           "-shared", str(HERE / "hawk_oracle.c"), "-o", str(out), "-lquadmath", "-lm"]
+    env = dict(os.environ)
+    env.pop("CC", None)
+    run = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    if run.returncode != 0:
+        raise RuntimeError(f"oracle build failed:\n{run.stderr}")
+    return out
+
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int64
+_D = ctypes.c_double
+_F = ctypes.c_float
+_SIGS = {
+    "hko_set_math": (None, [ctypes.c_int]),
+    "hko_get_math": (ctypes.c_int, []),
+    "hko_energy": (None, [_P, _I, _P, _I, _I]),
+    "hko_energy_vjp": (None, [_P, _I, _P, _P, _I, _I, _I]),
+    "hko_energy_jvp": (None, [_P, _I, _P, _I, _P, _I, _I]),
+    "hko_poly_loss_f64": (None, [_P, _P, _D, _D, _D, _P, _I, _I]),
+    "hko_poly_loss_f32": (None, [_P, _P, _F, _F, _F, _P, _I, _I]),
+    "hko_poly_loss_vjp_rows_f64": (None, [_P, _P, _P, _D, _D, _D, _I, _I, _I, _P, _P]),
+    "hko_poly_loss_vjp_rows_f32": (None, [_P, _P, _P, _F, _F, _F, _I, _I, _I, _P, _P]),
+    "hko_cells_finish_f64": (_D, [ctypes.c_int, _P, _P, _I]),
+    "hko_cells_finish_f32": (_F, [ctypes.c_int, _P, _P, _I]),
+    "hko_gravity": (None, [_P, _P, _I, _P, _P, _D, _P, _I, _P, _I, _I]),
+    "hko_gravity_jvp": (None, [_P, _P, _P, _P, _I, _P, _P, _D, _P, _I, _P, _I, _I]),
+    "hko_gravity_vjp": (None, [_P, _P, _P, _I, _P, _P, _P, _D, _P, _P, _I, _I, _I]),
+    "hko_spd_solve": (None, [_P, _P, _I, _P, _I, _I, _I]),
+    "hko_spd_solve_vjp": (None, [_P, _P, _P, _I, _P, _P, _I, _I, _I]),
+    "hko_kepler": (None, [_P, _P, _P, _P, _I, _I]),
+    "hko_kepler_vjp": (None, [_P, _P, _P, _P, _P, _I, _I]),
+}
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    with _LOCK:
+        if _LIB is None:
+            handle = ctypes.CDLL(str(build()))
+            for name, (res, args) in _SIGS.items():
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+            _LIB = handle
+        return _LIB
+
+
+def _p(a: np.ndarray):
+    assert a.flags.c_contiguous
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def set_math(mode: int) -> None:
+    lib().hko_set_math(int(mode))
+
+
+class math_mode:
+    """``with math_mode(MATH_CR): ...`` -- sin/cos correctly rounded inside."""
+
+    def __init__(self, mode: int) -> None:
+        self.mode = mode
+
+    def __enter__(self):
+        self.prev = lib().hko_get_math()
+        lib().hko_set_math(self.mode)
+
+    def __exit__(self, *exc):
+        lib().hko_set_math(self.prev)
+
+
+def tiles(n: int, threads: int, align: int = 1):
+    """Contiguous [base, base+count) tiles of n samples, ``align``-aligned starts
+    (eagle's host team tiles the partition the same way, hawk/emit/host.py:8-12)."""
+    threads = max(1, int(threads))
+    step = -(-n // threads)
+    step = -(-step // align) * align
+    return [(b, min(step, n - b)) for b in range(0, n, step)] or [(0, 0)]
+
+
+def parallel(fn, n: int, threads: int = 1, align: int = 1) -> None:
+    """Run ``fn(base, count)`` over tiles on ``threads`` host threads (ctypes
+    releases the GIL for the duration of each C call)."""
+    parts = tiles(n, threads, align)
+    if len(parts) == 1:
+        fn(*parts[0])
+        return
+    with ThreadPoolExecutor(len(parts)) as pool:
+        list(pool.map(lambda bc: fn(*bc), parts))
+
+
+# ------------------------------------------------------------- kernels
+def energy(v: np.ndarray, threads: int = 1) -> np.ndarray:
+    n = v.shape[-1]
+    out = np.empty(n)
+    parallel(lambda b, c: lib().hko_energy(_p(v), n, _p(out), b, c), n, threads)
+    return out
+
+
+def energy_vjp(v: np.ndarray, bar_out: np.ndarray, threads: int = 1) -> np.ndarray:
+    n = v.shape[-1]
+    bar_v = np.empty_like(v)
+    parallel(lambda b, c: lib().hko_energy_vjp(_p(v), n, _p(bar_out), _p(bar_v), n, b, c), n, threads)
+    return bar_v
+
+
+def energy_jvp(v: np.ndarray, dot_v: np.ndarray, threads: int = 1) -> np.ndarray:
+    n = v.shape[-1]
+    out = np.empty(n)
+    parallel(lambda b, c: lib().hko_energy_jvp(_p(v), n, _p(dot_v), n, _p(out), b, c), n, threads)
+    return out
+
+
+def poly_loss(x, t, a, b, c, threads: int = 1) -> np.ndarray:
+    n = x.shape[0]
+    r = np.empty_like(x)
+    fn = lib().hko_poly_loss_f64 if x.dtype == np.float64 else lib().hko_poly_loss_f32
+    parallel(lambda bb, cc: fn(_p(x), _p(t), a, b, c, _p(r), bb, cc), n, threads)
+    return r
+
+
+def poly_loss_vjp_rows(x, t, bar_r, a, b, c, threads: int = 1):
+    """``(hi, comp)`` of shape (3, rows): the 32-sample rows of the 3 Param gradients."""
+    n = x.shape[0]
+    rows = -(-n // 32)
+    hi = np.empty((3, rows), dtype=x.dtype)
+    comp = np.empty((3, rows), dtype=x.dtype)
+    fn = lib().hko_poly_loss_vjp_rows_f64 if x.dtype == np.float64 else lib().hko_poly_loss_vjp_rows_f32
+
+    def tile(r0, nr):
+        h = np.empty((3, nr), dtype=x.dtype)
+        cc = np.empty((3, nr), dtype=x.dtype)
+        fn(_p(x), _p(t), _p(bar_r), a, b, c, n, r0, nr, _p(h), _p(cc))
+        hi[:, r0:r0 + nr] = h
+        comp[:, r0:r0 + nr] = cc
+
+    parallel(tile, rows, threads)
+    return hi, comp
+
+
+def cells_finish(hi: np.ndarray, comp: np.ndarray | None, op: str = "sum"):
+    hi = np.ascontiguousarray(hi)
+    comp = None if comp is None else np.ascontiguousarray(comp)
+    fn = lib().hko_cells_finish_f64 if hi.dtype == np.float64 else lib().hko_cells_finish_f32
+    return fn(OP[op], _p(hi), None if comp is None else _p(comp), hi.shape[0])
+
+
+def poly_loss_vjp(x, t, bar_r, a, b, c, threads: int = 1):
+    """The three Param gradients (cells) and the rows they were finished from."""
+    hi, comp = poly_loss_vjp_rows(x, t, bar_r, a, b, c, threads)
+    cells = [cells_finish(hi[k], comp[k]) for k in range(3)]
+    return cells, (hi, comp)
+
+
+def gravity(r1, r2, m1, m2, G, threads: int = 1):
+    n = r1.shape[-1]
+    f = np.empty_like(r1)
+    u = np.empty(n)
+    parallel(lambda b, c: lib().hko_gravity(_p(r1), _p(r2), n, _p(m1), _p(m2), G, _p(f), n, _p(u), b, c),
+             n, threads)
+    return f, u
+
+
+def gravity_jvp(r1, r2, dr1, dr2, m1, m2, G, threads: int = 1):
+    n = r1.shape[-1]
+    df = np.empty_like(r1)
+    du = np.empty(n)
+    parallel(lambda b, c: lib().hko_gravity_jvp(_p(r1), _p(r2), _p(dr1), _p(dr2), n, _p(m1), _p(m2), G,
+                                               _p(df), n, _p(du), b, c), n, threads)
+    return df, du
+
+
+def gravity_vjp(r1, r2, bar_f, bar_u, m1, m2, G, threads: int = 1):
+    n = r1.shape[-1]
+    b1 = np.empty_like(r1)
+    b2 = np.empty_like(r1)
+    parallel(lambda b, c: lib().hko_gravity_vjp(_p(r1), _p(r2), _p(bar_f), n, _p(bar_u), _p(m1), _p(m2), G,
+                                               _p(b1), _p(b2), n, b, c), n, threads)
+    return b1, b2
+
+
+def spd_solve(A, b, threads: int = 1):
+    n = A.shape[-1]
+    x = np.empty_like(b)
+    parallel(lambda bb, c: lib().hko_spd_solve(_p(A), _p(b), n, _p(x), n, bb, c), n, threads)
+    return x
+
+
+def spd_solve_vjp(A, b, bar_x, threads: int = 1):
+    n = A.shape[-1]
+    bar_A = np.empty_like(A)
+    bar_b = np.empty_like(b)
+    parallel(lambda bb, c: lib().hko_spd_solve_vjp(_p(A), _p(b), _p(bar_x), n, _p(bar_A), _p(bar_b), n, bb, c),
+             n, threads)
+    return bar_A, bar_b
+
+
+def kepler(e, M, threads: int = 1):
+    n = e.shape[0]
+    E = np.empty(n)
+    it = np.empty(n, dtype=np.int32)
+    parallel(lambda b, c: lib().hko_kepler(_p(e), _p(M), _p(E), _p(it), b, c), n, threads)
+    return E, it
+
+
+def kepler_vjp(e, M, bar_E, threads: int = 1):
+    n = e.shape[0]
+    be = np.empty(n)
+    bM = np.empty(n)
+    parallel(lambda b, c: lib().hko_kepler_vjp(_p(e), _p(M), _p(bar_E), _p(be), _p(bM), b, c), n, threads)
+    return be, bM

@@ -1,0 +1,466 @@
+/*
+ * hawk_oracle.c -- TEST INFRASTRUCTURE ONLY (see hawk_oracle.h): the CPU
+ * restatement of the reference's host target for the five benchmark kernels.
+ *
+ * Built with -O2 -ffp-contract=off (no FMA contraction), the reference's
+ * `native` host profile (hawk/compile/toolchain.py:897-900).  Each kernel
+ * function below states the body the reference renderer writes for the kernel
+ * (hawk/emit/render.py:140; the kernels are the ones in hawk_b200/configs.py),
+ * operation for operation, inside the serial host loop of
+ * hawk/emit/host.py:1386-1495.  Vector helpers follow the library order the
+ * reference restates for its own C export: dot products and sums ascending,
+ * hawk/embedded/writer.py:603-625.
+ */
+#include "hawk_oracle.h"
+
+#include <math.h>
+#include <quadmath.h>
+#include <stdlib.h>
+#include <string.h>
+
+static int g_math = HKO_MATH_LIBM;
+
+void hko_set_math(int mode) { g_math = mode; }
+int hko_get_math(void) { return g_math; }
+
+static double o_sin(double x) { return g_math == HKO_MATH_CR ? (double)sinq((__float128)x) : sin(x); }
+static double o_cos(double x) { return g_math == HKO_MATH_CR ? (double)cosq((__float128)x) : cos(x); }
+
+/* ------------------------------------------------------------------ c1 energy */
+
+/* out = (0.5 * v.dot(v)) */
+void hko_energy(const double* v, int64_t pitch, double* out, int64_t base, int64_t count) {
+    for (int64_t i = base; i < base + count; ++i) {
+        const double v0 = v[i], v1 = v[pitch + i], v2 = v[2 * pitch + i];
+        const double d = ((v0 * v0) + (v1 * v1)) + (v2 * v2);
+        out[i] = 0.5 * d;
+    }
+}
+
+/* t4 = (bar_out * 0.5) * v;  bar_v = t4 + t4 */
+void hko_energy_vjp(const double* v, int64_t pitch, const double* bar_out, double* bar_v, int64_t bar_pitch,
+                    int64_t base, int64_t count) {
+    for (int64_t i = base; i < base + count; ++i) {
+        const double s = bar_out[i] * 0.5;
+        for (int k = 0; k < 3; ++k) {
+            const double t4 = s * v[k * pitch + i];
+            bar_v[k * bar_pitch + i] = t4 + t4;
+        }
+    }
+}
+
+/* dot_out = 0.5 * (dot_v.dot(v) + v.dot(dot_v)) */
+void hko_energy_jvp(const double* v, int64_t pitch, const double* dot_v, int64_t dot_pitch, double* dot_out,
+                    int64_t base, int64_t count) {
+    for (int64_t i = base; i < base + count; ++i) {
+        const double v0 = v[i], v1 = v[pitch + i], v2 = v[2 * pitch + i];
+        const double d0 = dot_v[i], d1 = dot_v[dot_pitch + i], d2 = dot_v[2 * dot_pitch + i];
+        const double a = ((d0 * v0) + (d1 * v1)) + (d2 * v2);
+        const double b = ((v0 * d0) + (v1 * d1)) + (v2 * d2);
+        dot_out[i] = 0.5 * (a + b);
+    }
+}
+
+/* --------------------------------------------------------- c2 affine polynomial */
+
+/* t11 = (((((a*x)*x)*x) + (b*x)) + c) - t;  r = t11 * t11 */
+#define POLY_BODY(T)                                                               \
+    for (int64_t i = base; i < base + count; ++i) {                                \
+        const T xi = x[i];                                                         \
+        const T t11 = ((((((a * xi) * xi) * xi) + (b * xi)) + c) - t[i]);          \
+        r[i] = t11 * t11;                                                          \
+    }
+
+void hko_poly_loss_f64(const double* x, const double* t, double a, double b, double c, double* r,
+                       int64_t base, int64_t count) {
+    POLY_BODY(double)
+}
+
+void hko_poly_loss_f32(const float* x, const float* t, float a, float b, float c, float* r,
+                       int64_t base, int64_t count) {
+    POLY_BODY(float)
+}
+
+/*
+ * The host sample-sum frame (hawk/emit/host.py:1499-1530) with the row tree of
+ * sampleSumRow_ (hawk/emit/wrapper.py:578-592): 32 slots per row, a slot past
+ * the last sample holding 0, slot l joined with slot l + off (lower first) for
+ * off = 16, 8, 4, 2, 1 by pairCombine_ (hawk/emit/wrapper.py:561-576), whose
+ * residual is the two-sum error with the larger magnitude first, +0 for zero
+ * (hawk/_cells.py:44-49).
+ */
+#define DEFINE_PAIR(T, SUF)                                                                \
+    static int finite_##SUF(T x) { return (x - x) == (x - x); }                           \
+    static T two_sum_err_##SUF(T a, T b, T s) {                                           \
+        const int a_big = (a < 0 ? -a : a) >= (b < 0 ? -b : b);                           \
+        const T big = a_big ? a : b, small = a_big ? b : a;                                \
+        return (small - (s - big)) + (T)0;                                                 \
+    }                                                                                      \
+    static void pair_##SUF(T* s, T* c, T s2, T c2) {                                      \
+        const T t = *s + s2;                                                               \
+        const T e = two_sum_err_##SUF(*s, s2, t);                                          \
+        *c = finite_##SUF(t) ? (*c + c2) + e : (T)0;                                       \
+        *s = t;                                                                            \
+    }
+DEFINE_PAIR(double, d)
+DEFINE_PAIR(float, f)
+
+/* row j: terms of samples 32j .. 32j+31 (0 past n), columns k = 0..2 */
+#define POLY_VJP_ROWS(T, SUF)                                                              \
+    for (int64_t j = 0; j < nrows; ++j) {                                                  \
+        T h[32][3], cc[32][3];                                                             \
+        const int64_t row = row0 + j;                                                      \
+        for (int l = 0; l < 32; ++l) {                                                     \
+            const int64_t i = row * 32 + l;                                                \
+            for (int k = 0; k < 3; ++k) { h[l][k] = 0; cc[l][k] = 0; }                     \
+            if (i < n) {                                                                   \
+                const T xi = x[i];                                                         \
+                const T t17 = (bar_r[i] * ((((((a * xi) * xi) * xi) + (b * xi)) + c) - t[i])); \
+                const T t18 = t17 + t17;                                                   \
+                const T t19 = t18 * xi;                                                    \
+                h[l][0] = (t19 * xi) * xi;                                                 \
+                h[l][1] = t19;                                                             \
+                h[l][2] = t18;                                                             \
+            }                                                                              \
+        }                                                                                  \
+        for (int off = 16; off >= 1; off >>= 1)                                            \
+            for (int l = 0; l < off; ++l)                                                  \
+                for (int k = 0; k < 3; ++k)                                                \
+                    pair_##SUF(&h[l][k], &cc[l][k], h[l + off][k], cc[l + off][k]);        \
+        for (int k = 0; k < 3; ++k) {                                                      \
+            hi[k * nrows + j] = h[0][k];                                                   \
+            comp[k * nrows + j] = cc[0][k];                                                \
+        }                                                                                  \
+    }
+
+void hko_poly_loss_vjp_rows_f64(const double* x, const double* t, const double* bar_r, double a, double b,
+                                double c, int64_t n, int64_t row0, int64_t nrows, double* hi, double* comp) {
+    POLY_VJP_ROWS(double, d)
+}
+
+void hko_poly_loss_vjp_rows_f32(const float* x, const float* t, const float* bar_r, float a, float b, float c,
+                                int64_t n, int64_t row0, int64_t nrows, float* hi, float* comp) {
+    POLY_VJP_ROWS(float, f)
+}
+
+/*
+ * hawk/_cells.py:94-119 -- leaves of 4096 rows: slot s of 256 walks rows
+ * s, s+256, ... with a Neumaier step (_neumaier, :52-55), then a halving tree
+ * over the slots (_pair, :58-60); then pairwise levels over the leaves, an odd
+ * last one carried; hi + comp at the root for a sum.  Max/min keep `a > b ? a : b`
+ * (`a < b ? a : b`) on both node kinds.
+ */
+#define DEFINE_FINISH(T, SUF)                                                              \
+    static void nadd_##SUF(int op, T* h, T* c, T x, T xc) {                               \
+        if (op == HKO_OP_MAX) { *h = (*h > x) ? *h : x; return; }                          \
+        if (op == HKO_OP_MIN) { *h = (*h < x) ? *h : x; return; }                          \
+        const T s = *h + x;                                                                \
+        const int f = finite_##SUF(s);                                                     \
+        *c = f ? *c + two_sum_err_##SUF(*h, x, s) : (T)0;                                  \
+        *c = f ? *c + xc : (T)0;                                                           \
+        *h = s;                                                                            \
+    }                                                                                      \
+    static void join_##SUF(int op, T* h, T* c, T x, T xc) {                               \
+        if (op == HKO_OP_MAX) { *h = (*h > x) ? *h : x; return; }                          \
+        if (op == HKO_OP_MIN) { *h = (*h < x) ? *h : x; return; }                          \
+        const T s = *h + x;                                                                \
+        *c = finite_##SUF(s) ? (*c + xc) + two_sum_err_##SUF(*h, x, s) : (T)0;             \
+        *h = s;                                                                            \
+    }                                                                                      \
+    T hko_cells_finish_##SUF##_impl(int op, const T* hi, const T* comp, int64_t n) {       \
+        const int64_t leaves = (n + 4095) / 4096;                                          \
+        T* lh = (T*)malloc(sizeof(T) * (size_t)(leaves > 0 ? leaves : 1));                 \
+        T* lc = (T*)malloc(sizeof(T) * (size_t)(leaves > 0 ? leaves : 1));                 \
+        for (int64_t L = 0; L < leaves; ++L) {                                             \
+            const int64_t r0 = L * 4096;                                                   \
+            const int64_t cnt = (n - r0) < 4096 ? (n - r0) : 4096;                         \
+            const int live = (int)(cnt < 256 ? cnt : 256);                                 \
+            T sh[256], sc[256];                                                            \
+            for (int s = 0; s < live; ++s) {                                               \
+                sh[s] = hi[r0 + s];                                                        \
+                sc[s] = (op == HKO_OP_SUM && comp) ? comp[r0 + s] : (T)0;                  \
+                if (!finite_##SUF(sh[s])) sc[s] = 0;                                       \
+            }                                                                              \
+            for (int k = 1; k < 16; ++k) {                                                 \
+                const int64_t rest = cnt - (int64_t)k * 256;                               \
+                const int m = (int)(rest < live ? rest : live);                            \
+                if (m <= 0) break;                                                         \
+                for (int s = 0; s < m; ++s) {                                              \
+                    const int64_t r = r0 + (int64_t)k * 256 + s;                           \
+                    nadd_##SUF(op, &sh[s], &sc[s], hi[r],                                  \
+                               (op == HKO_OP_SUM && comp) ? comp[r] : (T)0);               \
+                }                                                                          \
+            }                                                                              \
+            for (int off = 128; off > 0; off >>= 1) {                                      \
+                const int lim = live > off ? (off < live - off ? off : live - off) : 0;    \
+                for (int s = 0; s < lim; ++s) join_##SUF(op, &sh[s], &sc[s], sh[s + off], sc[s + off]); \
+            }                                                                              \
+            lh[L] = sh[0];                                                                 \
+            lc[L] = sc[0];                                                                 \
+        }                                                                                  \
+        int64_t m = leaves;                                                                \
+        while (m > 1) {                                                                    \
+            const int64_t pairs = m / 2;                                                   \
+            for (int64_t j = 0; j < pairs; ++j) {                                          \
+                T h = lh[2 * j], c = lc[2 * j];                                            \
+                join_##SUF(op, &h, &c, lh[2 * j + 1], lc[2 * j + 1]);                      \
+                lh[j] = h;                                                                 \
+                lc[j] = c;                                                                 \
+            }                                                                              \
+            if (m & 1) { lh[pairs] = lh[m - 1]; lc[pairs] = lc[m - 1]; }                   \
+            m = pairs + (m & 1);                                                           \
+        }                                                                                  \
+        const T root = lh[0], rc = lc[0];                                                  \
+        free(lh);                                                                          \
+        free(lc);                                                                          \
+        if (op == HKO_OP_SUM) return finite_##SUF(root) ? root + rc : root;                \
+        return root;                                                                       \
+    }
+DEFINE_FINISH(double, d)
+DEFINE_FINISH(float, f)
+
+double hko_cells_finish_f64(int op, const double* hi, const double* comp, int64_t nrows) {
+    return hko_cells_finish_d_impl(op, hi, comp, nrows);
+}
+float hko_cells_finish_f32(int op, const float* hi, const float* comp, int64_t nrows) {
+    return hko_cells_finish_f_impl(op, hi, comp, nrows);
+}
+
+/* --------------------------------------------------------------- c3 gravity */
+
+static double norm3(const double d[3]) { return sqrt(((d[0] * d[0]) + (d[1] * d[1])) + (d[2] * d[2])); }
+
+/* t4 = (G*m1)*m2; t7 = r2 - r1; t8 = |t7|; f = (t4 / ((t8*t8)*t8)) * t7; u = (-t4) / t8 */
+void hko_gravity(const double* r1, const double* r2, int64_t pitch, const double* m1, const double* m2,
+                 double G, double* f, int64_t f_pitch, double* u, int64_t base, int64_t count) {
+    for (int64_t i = base; i < base + count; ++i) {
+        const double t4 = (G * m1[i]) * m2[i];
+        double t7[3];
+        for (int k = 0; k < 3; ++k) t7[k] = r2[k * pitch + i] - r1[k * pitch + i];
+        const double t8 = norm3(t7);
+        const double s = t4 / ((t8 * t8) * t8);
+        for (int k = 0; k < 3; ++k) f[k * f_pitch + i] = s * t7[k];
+        u[i] = (-t4) / t8;
+    }
+}
+
+/*
+ * t15 = dr2 + dr1 * -1;  t17 = t7.dot(t15) / t8;
+ * dot_f = (-((t11 * ((((t17*t8) + (t8*t17)) * t8) + (t9*t17))) / t10)) * t7 + t11 * t15
+ * dot_u = -((((-t4) / t8) * t17) / t8)
+ */
+void hko_gravity_jvp(const double* r1, const double* r2, const double* dr1, const double* dr2, int64_t pitch,
+                     const double* m1, const double* m2, double G, double* dot_f, int64_t f_pitch,
+                     double* dot_u, int64_t base, int64_t count) {
+    for (int64_t i = base; i < base + count; ++i) {
+        const double t4 = (G * m1[i]) * m2[i];
+        double t7[3], t15[3];
+        for (int k = 0; k < 3; ++k) {
+            t7[k] = r2[k * pitch + i] - r1[k * pitch + i];
+            t15[k] = dr2[k * pitch + i] + (dr1[k * pitch + i] * -1.0);
+        }
+        const double t8 = norm3(t7);
+        const double t9 = t8 * t8;
+        const double t10 = t9 * t8;
+        const double t11 = t4 / t10;
+        const double dot = ((t7[0] * t15[0]) + (t7[1] * t15[1])) + (t7[2] * t15[2]);
+        const double t17 = dot / t8;
+        const double s = -((t11 * ((((t17 * t8) + (t8 * t17)) * t8) + (t9 * t17))) / t10);
+        for (int k = 0; k < 3; ++k) dot_f[k * f_pitch + i] = (s * t7[k]) + (t11 * t15[k]);
+        dot_u[i] = -((((-t4) / t8) * t17) / t8);
+    }
+}
+
+/*
+ * t24 = -((bar_f.cwiseMul(t8).sum() * t12) / t11);  t28 = (t24*t9)*t9;
+ * t33 = bar_f * t12 + ((((((-((bar_u * ((-t5)/t9)) / t9)) + (t24*t10)) + t28) + t28) / t9) * t8;
+ * bar_r2 = t33;  bar_r1 = t33 * -1
+ */
+void hko_gravity_vjp(const double* r1, const double* r2, const double* bar_f, int64_t pitch,
+                     const double* bar_u, const double* m1, const double* m2, double G, double* bar_r1,
+                     double* bar_r2, int64_t out_pitch, int64_t base, int64_t count) {
+    for (int64_t i = base; i < base + count; ++i) {
+        double bf[3], t8[3];
+        for (int k = 0; k < 3; ++k) {
+            bf[k] = bar_f[k * pitch + i];
+            t8[k] = r2[k * pitch + i] - r1[k * pitch + i];
+        }
+        const double t5 = (G * m1[i]) * m2[i];
+        const double t9 = norm3(t8);
+        const double t10 = t9 * t9;
+        const double t11 = t10 * t9;
+        const double t12 = t5 / t11;
+        const double cs = ((bf[0] * t8[0]) + (bf[1] * t8[1])) + (bf[2] * t8[2]);
+        const double t24 = -((cs * t12) / t11);
+        const double t28 = (t24 * t9) * t9;
+        const double s = (((((-((bar_u[i] * ((-t5) / t9)) / t9)) + (t24 * t10)) + t28) + t28) / t9);
+        for (int k = 0; k < 3; ++k) {
+            const double t33 = (bf[k] * t12) + (s * t8[k]);
+            bar_r2[k * out_pitch + i] = t33;
+            bar_r1[k * out_pitch + i] = t33 * -1.0;
+        }
+    }
+}
+
+/* ------------------------------------------------------------ c4 SPD solve */
+
+/* Cholesky of the symmetric part, column by column (hawk/embedded/linalg.py:233-271). */
+static int chol6(const double a[6][6], double l[6][6]) {
+    int info = 0;
+    memset(l, 0, sizeof(double) * 36);
+    for (int j = 0; j < 6; ++j) {
+        if (info != 0) continue;
+        double d = (0.5 * a[j][j]) + (0.5 * a[j][j]);
+        for (int k = 0; k < j; ++k) d = d - (l[j][k] * l[j][k]);
+        if (d > 0.0) {
+            const double ljj = sqrt(d);
+            l[j][j] = ljj;
+            for (int i = j + 1; i < 6; ++i) {
+                double acc = (0.5 * a[i][j]) + (0.5 * a[j][i]);
+                for (int k = 0; k < j; ++k) acc = acc - (l[i][k] * l[j][k]);
+                l[i][j] = acc / ljj;
+            }
+        } else {
+            info = j + 1;
+        }
+    }
+    return info;
+}
+
+/* cho_solve: forward sweep on L, backward on L^T, zeros on a failed factor
+ * (hawk/embedded/linalg.py:443-520). */
+static void cho_solve6(const double l[6][6], int info, const double b[6], double x[6]) {
+    if (info != 0) {
+        for (int i = 0; i < 6; ++i) x[i] = 0.0;
+        return;
+    }
+    for (int i = 0; i < 6; ++i) {
+        double acc = b[i];
+        for (int j = 0; j < i; ++j) acc = acc - (l[i][j] * x[j]);
+        x[i] = acc / l[i][i];
+    }
+    for (int r = 0; r < 6; ++r) {
+        const int i = 5 - r;
+        double acc = x[i];
+        for (int j = i + 1; j < 6; ++j) acc = acc - (l[j][i] * x[j]);
+        x[i] = acc / l[i][i];
+    }
+}
+
+static void load6x6(const double* A, int64_t pitch, int64_t i, double a[6][6]) {
+    for (int r = 0; r < 6; ++r)
+        for (int c = 0; c < 6; ++c) a[r][c] = A[(r * 6 + c) * pitch + i];
+}
+
+void hko_spd_solve(const double* A, const double* b, int64_t pitch, double* x, int64_t x_pitch,
+                   int64_t base, int64_t count) {
+    for (int64_t i = base; i < base + count; ++i) {
+        double a[6][6], l[6][6], bb[6], xx[6];
+        load6x6(A, pitch, i, a);
+        for (int k = 0; k < 6; ++k) bb[k] = b[k * pitch + i];
+        const int info = chol6(a, l);
+        cho_solve6(l, info, bb, xx);
+        for (int k = 0; k < 6; ++k) x[k * x_pitch + i] = xx[k];
+    }
+}
+
+/* la1 = cho_solve(L, bar_x) -> bar_b;  la2 = cho_solve(L, b);
+ * t6 = outer(la1, la2);  bar_A = ((t6 + t6^T) * 0.5) * -1 */
+void hko_spd_solve_vjp(const double* A, const double* b, const double* bar_x, int64_t pitch, double* bar_A,
+                       double* bar_b, int64_t out_pitch, int64_t base, int64_t count) {
+    for (int64_t i = base; i < base + count; ++i) {
+        double a[6][6], l[6][6], bx[6], bb[6], la1[6], la2[6];
+        load6x6(A, pitch, i, a);
+        const int info = chol6(a, l);
+        for (int k = 0; k < 6; ++k) {
+            bx[k] = bar_x[k * pitch + i];
+            bb[k] = b[k * pitch + i];
+        }
+        cho_solve6(l, info, bx, la1);
+        for (int k = 0; k < 6; ++k) bar_b[k * out_pitch + i] = la1[k];
+        cho_solve6(l, info, bb, la2);
+        for (int r = 0; r < 6; ++r)
+            for (int c = 0; c < 6; ++c) {
+                const double t6 = la1[r] * la2[c];
+                const double t6t = la1[c] * la2[r];
+                bar_A[(r * 6 + c) * out_pitch + i] = ((t6 + t6t) * 0.5) * -1.0;
+            }
+    }
+}
+
+/* ---------------------------------------------------------------- c5 Kepler */
+
+/*
+ * E = M, n = 0; up to 32 trips:
+ *   tb0 = ((E - (e * sin E)) - M) / (1 - (e * cos E));  E' = E - tb0;  n' = n + 1;
+ *   leave after the trip when |tb0| < 1e-14.
+ */
+void hko_kepler(const double* e, const double* M, double* E, int32_t* iters, int64_t base, int64_t count) {
+    for (int64_t i = base; i < base + count; ++i) {
+        const double Mi = M[i], ei = e[i];
+        double Ek = Mi;
+        int32_t n = 0;
+        for (int k = 0; k < 32; ++k) {
+            const double tb0 = ((Ek - (ei * o_sin(Ek))) - Mi) / (1.0 - (ei * o_cos(Ek)));
+            const double tb1 = fabs(tb0);
+            const double nE = Ek - tb0;
+            const int32_t nn = (int32_t)((uint32_t)n + 1u);
+            const int x = tb1 < 1e-14;
+            Ek = nE;
+            n = nn;
+            if (x) break;
+        }
+        E[i] = Ek;
+        iters[i] = n;
+    }
+}
+
+/*
+ * The forward loop with its tape (E at the start of each trip) and trip count
+ * c, then the reverse loop over the trips taken, k = c - 1 .. 0, as the
+ * reference's reverse_loop renders it (hawk/diff/loops.py:384):
+ *   tb2 = -bE; tb3 = tape[k]; tb4 = sin tb3; tb5 = cos tb3; tb6 = 1 - e tb5;
+ *   tb7 = -(-((tb2 * (((tb3 - e tb4) - M) / tb6)) / tb6)); tb8 = tb2 / tb6;
+ *   tb9 = (bE + ((tb7 e) * (-sin tb3))) + tb8; tb10 = -tb8; tb11 = (tb10 e) cos tb3;
+ *   tb13 = (tb7 tb5) + (tb10 tb4); bE = tb9 + tb11; bM += -tb8; be += tb13
+ * bar_M = bE + bM, bar_e = be.
+ */
+void hko_kepler_vjp(const double* e, const double* M, const double* bar_E, double* bar_e, double* bar_M,
+                    int64_t base, int64_t count) {
+    for (int64_t i = base; i < base + count; ++i) {
+        const double Mi = M[i], ei = e[i];
+        double tape[32];
+        double Ek = Mi;
+        int64_t c = 0;
+        for (int k = 0; k < 32; ++k) {
+            tape[k] = Ek;
+            const double tb0 = ((Ek - (ei * o_sin(Ek))) - Mi) / (1.0 - (ei * o_cos(Ek)));
+            const double tb1 = fabs(tb0);
+            const double nE = Ek - tb0;
+            const int x = tb1 < 1e-14;
+            Ek = nE;
+            ++c;
+            if (x) break;
+        }
+        double bE = bar_E[i], bM = 0.0, be = 0.0;
+        for (int k = (int)(31 - (32 - c) * 1); k > -1; --k) {
+            const double tb2 = -bE;
+            const double tb3 = tape[k];
+            const double tb4 = o_sin(tb3);
+            const double tb5 = o_cos(tb3);
+            const double tb6 = 1.0 - (ei * tb5);
+            const double tb7 = -(-((tb2 * (((tb3 - (ei * tb4)) - Mi) / tb6)) / tb6));
+            const double tb8 = tb2 / tb6;
+            const double tb9 = (bE + ((tb7 * ei) * (-o_sin(tb3)))) + tb8;
+            const double tb10 = -tb8;
+            const double tb11 = (tb10 * ei) * o_cos(tb3);
+            const double tb12 = -tb8;
+            const double tb13 = (tb7 * tb5) + (tb10 * tb4);
+            bE = tb9 + tb11;
+            bM = bM + tb12;
+            be = be + tb13;
+        }
+        bar_M[i] = bE + bM;
+        bar_e[i] = be;
+    }
+}

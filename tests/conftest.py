@@ -1,0 +1,37 @@
+"""Test configuration: the ``gpu`` marker and shared fixtures.
+
+``-m "not gpu"`` runs on a host without a GPU: the oracle against the golden
+vectors, the emitter (where the hawk front end is importable), the runtime's
+host-side logic, the C-ABI library's exports, multi-rank logic over gloo.
+``-m gpu`` runs the parity tests proper on a B200, through the C ABI.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+REPO = Path(__file__).resolve().parent.parent
+GOLDEN = REPO / "tests" / "golden"
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (a B200); run with -m gpu")
+
+
+@pytest.fixture(scope="session")
+def golden():
+    cache = {}
+
+    def load(name: str):
+        if name not in cache:
+            with np.load(GOLDEN / f"{name}.npz") as z:
+                cache[name] = {k: z[k] for k in z.files}
+        return cache[name]
+
+    return load

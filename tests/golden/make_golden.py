@@ -1,0 +1,120 @@
+"""Make the golden vectors the oracle is pinned against.
+
+Every kernel of ``hawk_b200.configs`` (fwd, VJP, JVP) is evaluated sample by
+sample by the reference's own numpy IR interpreter -- ``evaluate`` in the
+reference's tests/_eval.py:264, "deliberately naive ... independent of the
+emitter" -- on seeded inputs drawn by ``hawk_b200.workloads``, and the inputs
+and outputs are written to ``tests/golden/<config>.npz``.  The VJP of the
+affine polynomial is evaluated on its un-promoted form (Params by value), which
+gives the per-sample gradient terms the 32-sample rows sum.
+
+Needs the reference checkout (its front end and tests/ directory); the
+fixtures it writes are committed and are all the test suite reads.
+
+    python tests/golden/make_golden.py
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parent.parent))
+
+N = {"energy": 96, "poly_loss": 160, "gravity": 96, "spd_solve": 48, "kepler": 128}
+SEED = 20261201
+
+
+def main() -> int:
+    from hawk_b200 import frontend, workloads
+
+    hawk = frontend.load()
+    root = Path(hawk.__file__).resolve().parent.parent
+    sys.path.insert(0, str(root / "tests"))
+    from _eval import evaluate  # the reference's IR interpreter
+
+    from hawk import Kernel
+    from hawk.diff import jvp, vjp
+
+    from hawk_b200 import configs
+
+    def per_sample(kernel_sinks, envs, names):
+        out = {k: [] for k in names}
+        for env in envs:
+            got = evaluate(kernel_sinks, env)
+            for k in names:
+                out[k].append(np.asarray(got[k], dtype=float))
+        return {k: np.stack(v, axis=-1) for k, v in out.items()}
+
+    # c1 energy
+    w = workloads.energy(N["energy"], SEED)
+    envs = [{"v": w["v"][:, i], "bar_out": w["bar_out"][i], "dot_v": w["dot_v"][:, i]} for i in range(N["energy"])]
+    g = {}
+    g.update({"out": per_sample(configs.energy.sinks, envs, ["out"])["out"]})
+    g.update({"bar_v": per_sample(configs.KERNELS["energy_vjp"][0].sinks, envs, ["bar_v"])["bar_v"]})
+    g.update({"dot_out": per_sample(configs.KERNELS["energy_jvp"][0].sinks, envs, ["dot_out"])["dot_out"]})
+    np.savez(HERE / "energy.npz", v=w["v"], bar_out=w["bar_out"], dot_v=w["dot_v"], **g)
+
+    # c2 affine polynomial (and the per-sample terms of its Param VJP)
+    w = workloads.poly_loss(N["poly_loss"], SEED)
+    plain_vjp = vjp(configs.poly_loss, wrt=("a", "b", "c"))
+    envs = [{"x": w["x"][i], "t": w["t"][i], "a": w["a"], "b": w["b"], "c": w["c"], "bar_r": w["bar_r"][i]}
+            for i in range(N["poly_loss"])]
+    r = per_sample(configs.poly_loss.sinks, envs, ["r"])["r"]
+    terms = per_sample(plain_vjp, envs, ["bar_a", "bar_b", "bar_c"])
+    np.savez(HERE / "poly_loss.npz", x=w["x"], t=w["t"], bar_r=w["bar_r"], a=w["a"], b=w["b"], c=w["c"], r=r,
+             term_a=terms["bar_a"], term_b=terms["bar_b"], term_c=terms["bar_c"])
+
+    # c3 gravity
+    w = workloads.gravity(N["gravity"], SEED)
+    envs = [{"r1": w["r1"][:, i], "r2": w["r2"][:, i], "m1": w["m1"][i], "m2": w["m2"][i], "G": w["G"],
+             "dot_r1": w["dr1"][:, i], "dot_r2": w["dr2"][:, i], "bar_f": w["bar_f"][:, i],
+             "bar_u": w["bar_u"][i]} for i in range(N["gravity"])]
+    fwd = per_sample(configs.gravity.sinks, envs, ["f", "u"])
+    tan = per_sample(configs.KERNELS["gravity_jvp"][0].sinks, envs, ["dot_f", "dot_u"])
+    adj = per_sample(configs.KERNELS["gravity_vjp"][0].sinks, envs, ["bar_r1", "bar_r2"])
+    np.savez(HERE / "gravity.npz", **{k: w[k] for k in ("r1", "r2", "m1", "m2", "dr1", "dr2", "bar_f", "bar_u")},
+             G=w["G"], **fwd, **tan, **adj)
+
+    # c4 SPD solve
+    w = workloads.spd_solve(N["spd_solve"], SEED)
+    envs = [{"A": w["A"][:, :, i], "b": w["b"][:, i], "bar_x": w["bar_x"][:, i]} for i in range(N["spd_solve"])]
+    fwd = per_sample(configs.spd_solve.sinks, envs, ["x"])
+    adj = per_sample(configs.KERNELS["spd_solve_vjp"][0].sinks, envs, ["bar_A", "bar_b"])
+    np.savez(HERE / "spd_solve.npz", A=w["A"], b=w["b"], bar_x=w["bar_x"], **fwd, **adj)
+
+    # c5 Kepler
+    w = workloads.kepler(N["kepler"], SEED)
+    envs = [{"e": w["e"][i], "M": w["M"][i], "bar_E": w["bar_E"][i]} for i in range(N["kepler"])]
+    fwd = per_sample(configs.kepler.sinks, envs, ["E", "iters"])
+    adj = per_sample(configs.KERNELS["kepler_vjp"][0].sinks, envs, ["bar_e", "bar_M"])
+    # the reference's known answer: e = 0.5, M = 1.0
+    known = evaluate(configs.kepler.sinks, {"e": 0.5, "M": 1.0, "bar_E": 1.0})
+    np.savez(HERE / "kepler.npz", e=w["e"], M=w["M"], bar_E=w["bar_E"], E=fwd["E"],
+             iters=fwd["iters"].astype(np.int32), bar_e=adj["bar_e"], bar_M=adj["bar_M"],
+             known_E=float(known["E"]), known_iters=int(known["iters"]))
+    # the ordered finish of rows into a cell (the reference's hawk/_cells.py:94-119)
+    from hawk import _cells
+
+    rng = np.random.default_rng(SEED)
+    cells = {}
+    for n in (1, 2, 31, 255, 256, 257, 4095, 4096, 4097, 12289, 16385):
+        hi = rng.standard_normal(n) * np.exp(rng.uniform(-20, 20, n))
+        comp = rng.standard_normal(n) * np.abs(hi) * 1e-17
+        cells[f"hi_{n}"] = hi
+        cells[f"comp_{n}"] = comp
+        for op in ("sum", "max", "min"):
+            cells[f"{op}_{n}"] = np.float64(_cells.finish(hi, comp, op))
+        cells[f"sum32_{n}"] = np.float32(_cells.finish(hi.astype(np.float32), comp.astype(np.float32), "sum"))
+    np.savez(HERE / "cells.npz", **cells)
+    _ = Kernel, jvp
+    for p in sorted(HERE.glob("*.npz")):
+        print(p.name, p.stat().st_size)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

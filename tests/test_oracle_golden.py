@@ -1,0 +1,124 @@
+"""The CPU oracle against the reference's own answers.
+
+Golden vectors come from the reference's numpy IR interpreter evaluating the
+traced kernels (tests/golden/make_golden.py); the ordered-finish fixtures from
+the reference's ``hawk._cells.finish``; the known answers from the reference's
+README (energy) and a Kepler root.  Tolerances: 1e-12 relative for float64
+values (the interpreter's numpy/LAPACK order differs from the host unit's),
+exact for integer planes and for the finish tree (same operations, same order).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+
+RTOL = 1e-12
+
+
+def close(got, want, rtol=RTOL, atol=0.0):
+    np.testing.assert_allclose(got, want, rtol=rtol, atol=atol)
+
+
+def test_energy_known_answer():
+    # README.md:80-99 of the reference: energy of these four samples and its gradient
+    v = np.array([[1.0, 2.0, 3.0, 4.0], [0.0, 1.0, 0.0, 1.0], [0.0, 0.0, 1.0, 1.0]])
+    np.testing.assert_array_equal(oracle.energy(v), [0.5, 2.5, 5.0, 9.0])
+    np.testing.assert_array_equal(oracle.energy_vjp(v, np.ones(4)), v)
+
+
+def test_energy_golden(golden):
+    g = golden("energy")
+    close(oracle.energy(g["v"]), g["out"])
+    close(oracle.energy_vjp(g["v"], g["bar_out"]), g["bar_v"])
+    close(oracle.energy_jvp(g["v"], g["dot_v"]), g["dot_out"])
+
+
+def test_poly_loss_golden(golden):
+    g = golden("poly_loss")
+    close(oracle.poly_loss(g["x"], g["t"], float(g["a"]), float(g["b"]), float(g["c"])), g["r"])
+
+
+def test_poly_loss_rows_are_per_32_sums_of_the_gradient_terms(golden):
+    # hawk tests/test_sample_sum.py:38, :96-123: rows equal the float64 per-32
+    # sums within 1e-14 of the row's sum of |term|
+    g = golden("poly_loss")
+    hi, comp = oracle.poly_loss_vjp_rows(g["x"], g["t"], g["bar_r"], float(g["a"]), float(g["b"]), float(g["c"]))
+    n = g["x"].shape[0]
+    for k, name in enumerate(("term_a", "term_b", "term_c")):
+        terms = g[name]
+        for j in range(hi.shape[1]):
+            seg = terms[32 * j:min(32 * j + 32, n)]
+            want = float(np.sum(seg.astype(np.longdouble)))
+            assert abs((hi[k, j] + comp[k, j]) - want) <= 1e-14 * float(np.sum(np.abs(seg))) + 1e-300
+
+
+def test_poly_loss_param_gradients_are_the_sums_of_the_terms(golden):
+    g = golden("poly_loss")
+    cells, _ = oracle.poly_loss_vjp(g["x"], g["t"], g["bar_r"], float(g["a"]), float(g["b"]), float(g["c"]))
+    for k, name in enumerate(("term_a", "term_b", "term_c")):
+        want = float(np.sum(g[name].astype(np.longdouble)))
+        assert abs(cells[k] - want) <= 1e-14 * float(np.sum(np.abs(g[name])))
+
+
+@pytest.mark.parametrize("n", [1, 2, 31, 255, 256, 257, 4095, 4096, 4097, 12289, 16385])
+def test_cells_finish_is_the_reference_tree_bit_for_bit(golden, n):
+    g = golden("cells")
+    hi, comp = g[f"hi_{n}"], g[f"comp_{n}"]
+    for op in ("sum", "max", "min"):
+        got = oracle.cells_finish(hi, comp if op == "sum" else None, op)
+        assert got == float(g[f"{op}_{n}"]), (op, n)
+    got32 = oracle.cells_finish(hi.astype(np.float32), comp.astype(np.float32), "sum")
+    assert np.float32(got32) == g[f"sum32_{n}"]
+
+
+def test_gravity_golden(golden):
+    g = golden("gravity")
+    f, u = oracle.gravity(g["r1"], g["r2"], g["m1"], g["m2"], float(g["G"]))
+    close(f, g["f"])
+    close(u, g["u"])
+    df, du = oracle.gravity_jvp(g["r1"], g["r2"], g["dr1"], g["dr2"], g["m1"], g["m2"], float(g["G"]))
+    close(df, g["dot_f"], rtol=1e-11)
+    close(du, g["dot_u"], rtol=1e-11)
+    b1, b2 = oracle.gravity_vjp(g["r1"], g["r2"], g["bar_f"], g["bar_u"], g["m1"], g["m2"], float(g["G"]))
+    close(b1, g["bar_r1"], rtol=1e-11)
+    close(b2, g["bar_r2"], rtol=1e-11)
+
+
+def test_spd_solve_golden(golden):
+    g = golden("spd_solve")
+    close(oracle.spd_solve(g["A"], g["b"]), g["x"])
+    bar_A, bar_b = oracle.spd_solve_vjp(g["A"], g["b"], g["bar_x"])
+    close(bar_b, g["bar_b"])
+    close(bar_A, g["bar_A"])
+
+
+@pytest.mark.parametrize("mode", [oracle.MATH_LIBM, oracle.MATH_CR])
+def test_kepler_golden(golden, mode):
+    g = golden("kepler")
+    with oracle.math_mode(mode):
+        E, it = oracle.kepler(g["e"], g["M"])
+        close(E, g["E"])
+        np.testing.assert_array_equal(it, g["iters"])
+        be, bM = oracle.kepler_vjp(g["e"], g["M"], g["bar_E"])
+        close(be, g["bar_e"], rtol=1e-10)
+        close(bM, g["bar_M"], rtol=1e-10)
+
+
+def test_kepler_known_answer(golden):
+    g = golden("kepler")
+    E, it = oracle.kepler(np.array([0.5]), np.array([1.0]))
+    assert E[0] == float(g["known_E"]) == 1.4987011335178484
+    assert it[0] == int(g["known_iters"]) == 6
+
+
+def test_a_planted_fault_in_the_oracle_is_caught(golden):
+    # non-vacuity (the reference's tests/test_serial_oracle.py:33-48 plants one too):
+    # a perturbed input must move the output beyond the tolerance used above
+    g = golden("energy")
+    v = g["v"].copy()
+    v[0, 5] *= 1.0 + 1e-9
+    with pytest.raises(AssertionError):
+        close(oracle.energy(v), g["out"])
