@@ -55,11 +55,14 @@ extern "C" __global__ void __launch_bounds__(256) poly_loss_vjp(
     const auto lut_c_cell = lut_c.cell();
     (void)lut_c_cell;
     const long long hawk_rows = (count + 31) >> 5;
-    for (long long hawk_r = hk::warp_first(); hawk_r < hawk_rows; hawk_r += hk::warp_step()) {
-        Real hawk_ss[3];
+    for (long long hawk_r0 = hk::warp_first() * 8; hawk_r0 < hawk_rows; hawk_r0 += hk::warp_step() * 8) {
+        Real hawk_terms[24];
 #pragma unroll
-        for (int hawk_k = 0; hawk_k < 3; ++hawk_k) hawk_ss[hawk_k] = hk::ss::identity<Real>(hk::ss::kSum);
-        const long long hawk_flat = (hawk_r << 5) + static_cast<long long>(threadIdx.x & 31u);
+        for (int hawk_k = 0; hawk_k < 24; ++hawk_k) hawk_terms[hawk_k] = hk::ss::identity<Real>(hk::ss::kSum);
+#pragma unroll
+        for (int hawk_q = 0; hawk_q < 8; ++hawk_q) {
+        Real* const hawk_ss = hawk_terms + hawk_q * 3;
+        const long long hawk_flat = ((hawk_r0 + hawk_q) << 5) + static_cast<long long>(threadIdx.x & 31u);
         if (hawk_flat < count) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
@@ -73,9 +76,13 @@ extern "C" __global__ void __launch_bounds__(256) poly_loss_vjp(
         hawk_ss[1] = t19;
         hawk_ss[2] = t18;
         }
-        const long long hawk_row = (base >> 5) + hawk_r;
+        }
         auto hawk_ss_store = [&](int hawk_col, auto hawk_s, auto hawk_c) {
             (void)hawk_c;
+            const int hawk_q = hawk_col / 3;
+            if (hawk_r0 + hawk_q >= hawk_rows) return;
+            const long long hawk_row = (base >> 5) + hawk_r0 + hawk_q;
+            hawk_col -= hawk_q * 3;
             if (hawk_col == 0) {
                 aout_bar_a.data()[hawk_row] = hawk_s;
                 aout_bar_a_comp.data()[hawk_row] = hawk_c;
@@ -89,6 +96,6 @@ extern "C" __global__ void __launch_bounds__(256) poly_loss_vjp(
                 aout_bar_c_comp.data()[hawk_row] = hawk_c;
             }
         };
-        hk::ss::row_reduce<3, hk::ss::kSum>(hawk_ss, hawk_ss_store);
+        hk::ss::rows_reduce<8, 3, hk::ss::kSum>(hawk_terms, hawk_ss_store);
     }
 }

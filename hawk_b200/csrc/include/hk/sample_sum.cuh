@@ -118,6 +118,84 @@ __device__ __forceinline__ void row_reduce(T (&h)[W], Store&& store) {
     for (int k = 0; k < W; ++k)
         if (static_cast<int>(lane) == (k & 31)) store(k, h[k], c[k]);
 }
+
+// One round of the halving butterfly: the lane holds M slots; the lower lane
+// of the pair (bit `off` clear) keeps slots [0, M/2), the upper lane slots
+// [M/2, M); each sends the other half to its partner and joins the kept half
+// with the partner's copy (lower lane's value first).  The kept slots move to
+// [0, M - M/2); a lower lane's extra slot (M odd) is padding that only ever
+// meets the same padding on its later partners.
+template <int M, int OP, class T>
+__device__ __forceinline__ void halve(T* h, T* c, int off, bool upper) {
+    constexpr int LO = M / 2, UP = M - M / 2;
+    const T pad = identity<T>(OP);
+#pragma unroll
+    for (int j = 0; j < UP; ++j) {
+        const T gh = upper ? (j < LO ? h[j] : pad) : h[LO + j];
+        const T gc = upper ? (j < LO ? c[j] : T(0)) : c[LO + j];
+        const T rh = __shfl_xor_sync(0xffffffffu, gh, off);
+        const T rc = __shfl_xor_sync(0xffffffffu, gc, off);
+        if (upper) {
+            T s = rh, sc = rc;
+            pair_combine<OP>(s, sc, h[LO + j], c[LO + j]);
+            h[LO + j] = s;
+            c[LO + j] = sc;
+        } else if (j < LO) {
+            pair_combine<OP>(h[j], c[j], rh, rc);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < UP; ++j) {
+        h[j] = upper ? h[LO + j] : (j < LO ? h[j] : pad);
+        c[j] = upper ? c[LO + j] : (j < LO ? c[j] : T(0));
+    }
+}
+
+// The rows of K consecutive 32-sample rows at once: every lane passes its
+// samples' W terms for each of the K rows (h[q * W + k], identity past the
+// last sample).  Each column's tree is the row tree above (lanes paired across
+// bit 4, then 3, ..., 0), but each round a lane keeps only half of its columns,
+// so a lane joins about K*W/16 pairs instead of 5*K*W.  Afterwards a lane
+// holds at most ceil(K*W / 32) columns and calls store(col, sum, comp) for
+// each, col = q * W + k.  All 32 lanes of the warp must call it.
+template <int K, int W, int OP, class T, class Store>
+__device__ __forceinline__ void rows_reduce(T (&h)[K * W], Store&& store) {
+    constexpr int N = K * W;
+    constexpr int M2 = N - N / 2, M3 = M2 - M2 / 2, M4 = M3 - M3 / 2, M5 = M4 - M4 / 2, M6 = M5 - M5 / 2;
+    T c[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k) c[k] = T(0);
+    const unsigned lane = threadIdx.x & 31u;
+    halve<N, OP>(h, c, 16, (lane & 16u) != 0u);
+    halve<M2, OP>(h, c, 8, (lane & 8u) != 0u);
+    halve<M3, OP>(h, c, 4, (lane & 4u) != 0u);
+    halve<M4, OP>(h, c, 2, (lane & 2u) != 0u);
+    halve<M5, OP>(h, c, 1, (lane & 1u) != 0u);
+    // which columns this lane ended with: [first, first + held)
+    int first = 0, held = N;
+    auto keep = [&](bool upper, int half) {
+        if (upper) {
+            first += half;
+            held -= half;
+        } else if (held > half) {
+            held = half;
+        }
+    };
+    keep((lane & 16u) != 0u, N / 2);
+    keep((lane & 8u) != 0u, M2 / 2);
+    keep((lane & 4u) != 0u, M3 / 2);
+    keep((lane & 2u) != 0u, M4 / 2);
+    keep((lane & 1u) != 0u, M5 / 2);
+#pragma unroll
+    for (int j = 0; j < M6; ++j)
+        if (j < held) store(first + j, h[j], c[j]);
+}
+
+// Rows of 32 samples one warp folds per trip for a sink of W columns: the
+// largest power of two K <= 8 with K * W <= 32 (1 when W > 16).
+constexpr int rows_per_warp(int w) {
+    return w <= 4 ? 8 : (w <= 8 ? 4 : (w <= 16 ? 2 : 1));
+}
 #endif
 
 }  // namespace ss

@@ -15,7 +15,9 @@ This module does the same for the b200 target, with device planes:
 * ``run(kernel, **planes)`` validates and binds the planes (dtype, shape,
   device, contiguity, writability -- every failing argument named in one
   refusal), launches on the caller's stream and, for a kernel with cells,
-  finishes the rows on the device (``hkb_cells_finish``) into the cells.
+  finishes the rows on the device into the cells: one launch folds every
+  column's rows into leaf partials (``hkb_cells_leaves``), one folds the leaves
+  (``hkb_cells_tree``).
 
 Launches are asynchronous on the stream (the current torch stream of the
 kernel's device unless ``stream=`` names one); the cells hold their values
@@ -214,12 +216,15 @@ class DeviceKernel:
                             f"start on a row (base % 32 == 0), got base={base}")
         self.entry.launch(self.block, base, count, n_samples, _stream(stream, self.device))
 
-    def _rows_for(self, n: int):
-        """The row scratch of every cell at sample count ``n`` (made once per n)."""
+    def cells_state(self, n: int):
+        """The kernel's own cell scratch at sample count ``n`` (made once per n):
+        the row planes of every sink (and companion), the leaf partials of the
+        finish (``(cols, leaves)`` each) and the finished column values."""
         import torch
 
         if n not in self._scratch:
             rows = -(-n // ROW)
+            leaves = -(-rows // abi.LEAF_ROWS)
             dt = torch.float64 if self.mode == "float64" else torch.float32
             dev = torch.device("cuda", self.device)
             planes = {}
@@ -227,24 +232,54 @@ class DeviceKernel:
                 planes[s["name"]] = torch.empty(rows, dtype=dt, device=dev)
                 if s["companion"]:
                     planes[s["companion"]] = torch.empty(rows, dtype=dt, device=dev)
-            scratch = torch.empty(abi.cells_scratch_bytes(self.mode, max(len(self.sums), 1), rows),
-                                  dtype=torch.uint8, device=dev)
-            self._scratch[n] = (planes, scratch)
+            cols = max(len(self.sums), 1)
+            self._scratch[n] = {"rows": planes,
+                                "leaf_hi": torch.empty((cols, leaves), dtype=dt, device=dev),
+                                "leaf_comp": torch.empty((cols, leaves), dtype=dt, device=dev),
+                                "values": torch.empty(cols, dtype=dt, device=dev)}
         return self._scratch[n]
 
-    def finish_cells(self, rows: dict, scratch, outputs: dict, lo: int, hi: int,
-                     stream: int | None = None) -> None:
-        """Rows ``[lo, hi)`` of every cell finished into ``outputs`` (device pointers)."""
+    def cells_leaves(self, state: dict, lo: int, hi: int, stream=None) -> int:
+        """Rows ``[lo, hi)`` of every column folded into one partial per leaf
+        (one launch for all columns); returns the leaf count."""
         itemsize = 8 if self.mode == "float64" else 4
         op = self.sums[0]["op"] if self.sums else "sum"
+        rows = state["rows"]
         his = [rows[s["name"]].data_ptr() + lo * itemsize for s in self.sums]
-        comps = ([rows[s["companion"]].data_ptr() + lo * itemsize for s in self.sums]
-                 if op == "sum" else None)
-        # cells are written one per column; each cell plane here is its own output
-        for k, s in enumerate(self.sums):
-            out = outputs[s["name"]]
-            abi.cells_finish(op, self.mode, [his[k]], None if comps is None else [comps[k]], hi - lo,
-                             scratch.data_ptr(), out.ptr, _stream(stream, self.device))
+        comps = [rows[s["companion"]].data_ptr() + lo * itemsize for s in self.sums] if op == "sum" else None
+        count = hi - lo
+        leaves = -(-count // abi.LEAF_ROWS)
+        leaf_hi, leaf_comp = state["leaf_hi"], state["leaf_comp"]
+        # the partials of column k start at k * leaves (a (cols, leaves) view)
+        abi.cells_leaves(op, self.mode, his, comps, count, leaf_hi.data_ptr(), leaf_comp.data_ptr(),
+                         _stream(stream, self.device))
+        return leaves
+
+    def cells_tree(self, leaf_hi, leaf_comp, leaves: int, values, stream=None) -> None:
+        """The pairwise levels over ``leaves`` partials per column, into ``values``."""
+        op = self.sums[0]["op"] if self.sums else "sum"
+        abi.cells_tree(op, self.mode, len(self.sums), leaf_hi.data_ptr(), leaf_comp.data_ptr(), leaves,
+                       values.data_ptr(), _stream(stream, self.device))
+
+    def write_cells(self, values, outputs: dict, stream=None) -> None:
+        """The finished column values into the caller's cell planes."""
+        import torch
+
+        with torch.cuda.stream(_torch_stream(stream, self.device)):
+            for k, s in enumerate(self.sums):
+                keep = outputs[s["name"]].keep
+                cell = keep if torch.is_tensor(keep) else torch.as_tensor(keep, device=f"cuda:{self.device}")
+                cell.view(-1)[:1].copy_(values[k:k + 1])
+
+
+def _torch_stream(stream, device: int):
+    import torch
+
+    if stream is None:
+        return torch.cuda.current_stream(device)
+    if isinstance(stream, torch.cuda.Stream):
+        return stream
+    return torch.cuda.ExternalStream(int(getattr(stream, "cuda_stream", stream)), device=device)
 
 
 def _current_device() -> int:
@@ -280,14 +315,10 @@ def load(directory, kernel: str, mode: str = "float64", device: int | None = Non
         return _CACHE[key]
 
 
-def run(kernel: DeviceKernel, *, base: int = 0, count: int | None = None, n_samples: int | None = None,
-        stream=None, **arrays) -> None:
-    """Bind ``arrays`` and run the whole range in one launch (asynchronous on ``stream``).
-
-    ``count`` defaults to ``n_samples``, ``n_samples`` to the count every bound
-    per-sample plane agrees on.  A kernel with cells takes each cell as a
-    one-element device plane (not its rows, as hawk/runtime.py:345-360 rules);
-    the runtime owns the rows and finishes them on the device."""
+def launch_cells(kernel: DeviceKernel, *, base: int = 0, count: int | None = None,
+                 n_samples: int | None = None, stream=None, **arrays):
+    """Validate, bind and launch (the body of ``run``); for a kernel with cells,
+    return ``(state, outputs, lo_row, hi_row)`` for the caller to finish, else None."""
     declared = {name for _r, name in kernel.arg_spec} | set(kernel.cells)
     unknown = sorted(set(arrays) - declared)
     if unknown:
@@ -309,31 +340,50 @@ def run(kernel: DeviceKernel, *, base: int = 0, count: int | None = None, n_samp
             raise HawkError(f"kernel {kernel.name!r}: this kernel reduces over samples into the cells "
                             f"{sorted(cells)}; bind each cell (one value per column), not its rows"
                             + (f" (missing: {missing})" if missing else ""))
+    if n_samples is None:
+        n_samples = kernel.n_from(planes)
+    count = n_samples - base if count is None else count
+    if base < 0 or count < 0 or base + count > n_samples:
+        raise HawkError(f"kernel {kernel.name!r}: partition [{base}, {base + count}) is outside "
+                        f"the {n_samples} samples")
+    outputs = {}
+    state = None
+    if cells:
+        for c in cells:
+            p = planes[c]
+            if p.dtype != kernel.mode or p.device != kernel.device:
+                raise HawkError(f"kernel {kernel.name!r}: cell {c!r} must be a {kernel.mode} plane on device "
+                                f"{kernel.device}, got {p.dtype} on {p.device}")
+            outputs[c] = p
+        state = kernel.cells_state(n_samples)
+        from .planes import from_torch
+        bound = {k: v for k, v in planes.items() if k not in cells}
+        bound.update({k: from_torch(v) for k, v in state["rows"].items()})
+    else:
+        bound = planes
+    kernel.check(bound, values, n_samples)
+    kernel.bind_all(bound, values, n_samples)
+    kernel.launch(base, count, n_samples, stream)
+    if not cells:
+        return None
+    return state, outputs, base // ROW, -(-(base + count) // ROW)
+
+
+def run(kernel: DeviceKernel, *, base: int = 0, count: int | None = None, n_samples: int | None = None,
+        stream=None, **arrays) -> None:
+    """Bind ``arrays`` and run the whole range in one launch (asynchronous on ``stream``).
+
+    ``count`` defaults to ``n_samples``, ``n_samples`` to the count every bound
+    per-sample plane agrees on.  A kernel with cells takes each cell as a
+    one-element device plane (not its rows, as hawk/runtime.py:345-360 rules);
+    the runtime owns the rows and finishes them on the device: one leaf launch
+    and one tree launch for all columns."""
     with kernel._lock:
-        if n_samples is None:
-            n_samples = kernel.n_from(planes)
-        count = n_samples - base if count is None else count
-        if base < 0 or count < 0 or base + count > n_samples:
-            raise HawkError(f"kernel {kernel.name!r}: partition [{base}, {base + count}) is outside "
-                            f"the {n_samples} samples")
-        outputs = {}
-        scratch = None
-        if cells:
-            for c in cells:
-                p = planes[c]
-                want = kernel.mode
-                if p.dtype != want or p.device != kernel.device:
-                    raise HawkError(f"kernel {kernel.name!r}: cell {c!r} must be a {want} plane on device "
-                                    f"{kernel.device}, got {p.dtype} on {p.device}")
-                outputs[c] = p
-            rows, scratch = kernel._rows_for(n_samples)
-            bound = {k: v for k, v in planes.items() if k not in cells}
-            from .planes import from_torch
-            bound.update({k: from_torch(v) for k, v in rows.items()})
-        else:
-            bound = planes
-        kernel.check(bound, values, n_samples)
-        kernel.bind_all(bound, values, n_samples)
-        kernel.launch(base, count, n_samples, stream)
-        if cells and count > 0:
-            kernel.finish_cells(rows, scratch, outputs, base // ROW, -(-(base + count) // ROW), stream)
+        pending = launch_cells(kernel, base=base, count=count, n_samples=n_samples, stream=stream, **arrays)
+        if pending is None:
+            return
+        state, outputs, lo, hi = pending
+        if hi > lo:
+            leaves = kernel.cells_leaves(state, lo, hi, stream)
+            kernel.cells_tree(state["leaf_hi"], state["leaf_comp"], leaves, state["values"], stream)
+            kernel.write_cells(state["values"], outputs, stream)

@@ -133,26 +133,35 @@ class B200Wrapper:
         return "\n".join(lines)
 
     def fold_rows(self, width: int) -> int:
-        """One row per warp per trip: the butterfly already carries every column."""
-        return 1
+        """Rows one warp folds per trip: the largest power of two K <= 8 with
+        K * width <= 32 shuffle columns (hk::ss::rows_per_warp)."""
+        return 8 if width <= 4 else 4 if width <= 8 else 2 if width <= 16 else 1
 
     def sample_sum_frame(self, width: int, elem: str, store: str,
                          op: str = "sum", live: str | None = None) -> tuple:
         """The row frame around a body writing ``width`` terms into ``hawk_ss``.
 
-        ``store`` is the body of ``hawk_ss_store(hawk_col, hawk_s, hawk_c)`` at
-        row ``hawk_row``; a lane past ``count`` adds the identity."""
+        A warp takes K consecutive rows per trip (lane l on sample 32 * row + l
+        of each, loads of all K rows in flight together); the K rows' columns
+        are reduced in one halving butterfly (hk::ss::rows_reduce).  ``store``
+        is the body of ``hawk_ss_store(hawk_col, hawk_s, hawk_c)`` at row
+        ``hawk_row``; a lane past ``count`` adds the identity."""
         if live is not None:
             raise HawkError("a sample sum over an active-set prefix is not built on the b200 target")
         code = _OP_CODE[op]
+        k = self.fold_rows(width)
         opened = (
             "    const long long hawk_rows = (count + 31) >> 5;\n"
-            "    for (long long hawk_r = hk::warp_first(); hawk_r < hawk_rows; hawk_r += hk::warp_step()) {\n"
-            f"        {elem} hawk_ss[{width}];\n"
+            f"    for (long long hawk_r0 = hk::warp_first() * {k}; hawk_r0 < hawk_rows; "
+            f"hawk_r0 += hk::warp_step() * {k}) {{\n"
+            f"        {elem} hawk_terms[{k * width}];\n"
             "#pragma unroll\n"
-            f"        for (int hawk_k = 0; hawk_k < {width}; ++hawk_k) hawk_ss[hawk_k] = "
+            f"        for (int hawk_k = 0; hawk_k < {k * width}; ++hawk_k) hawk_terms[hawk_k] = "
             f"hk::ss::identity<{elem}>({code});\n"
-            "        const long long hawk_flat = (hawk_r << 5) + static_cast<long long>(threadIdx.x & 31u);\n"
+            "#pragma unroll\n"
+            f"        for (int hawk_q = 0; hawk_q < {k}; ++hawk_q) {{\n"
+            f"        {elem}* const hawk_ss = hawk_terms + hawk_q * {width};\n"
+            "        const long long hawk_flat = ((hawk_r0 + hawk_q) << 5) + static_cast<long long>(threadIdx.x & 31u);\n"
             "        if (hawk_flat < count) {\n"
             "        const long long hawk_i = base + hawk_flat;\n"
             "        const hk::SampleIndex i{hawk_i};\n"
@@ -160,9 +169,9 @@ class B200Wrapper:
             "        (void)nSamples;")
         closed = (
             "        }\n"
-            "        const long long hawk_row = (base >> 5) + hawk_r;\n"
-            f"{store}\n"
-            f"        hk::ss::row_reduce<{width}, {code}>(hawk_ss, hawk_ss_store);\n"
+            "        }\n"
+            f"{store.replace('__K__', str(k)).replace('__W__', str(width))}\n"
+            f"        hk::ss::rows_reduce<{k}, {width}, {code}>(hawk_terms, hawk_ss_store);\n"
             "    }")
         return opened, closed
 
@@ -174,11 +183,17 @@ class B200Wrapper:
 
 
 def sample_sum_store(sums) -> str:
-    """``hawk_ss_store``: column ``k`` to the ``k``-th sink's row plane (and its
-    companion for a sum) at ``hawk_row``."""
+    """``hawk_ss_store``: butterfly column ``q * W + k`` is sink ``k``'s term of
+    the trip's row ``q``; it goes to that sink's row plane (and its companion
+    for a sum) at ``hawk_row``.  A row past the last is not stored.  ``__K__``
+    and ``__W__`` are filled by the frame."""
     sp = _spelling()
     lines = ["        auto hawk_ss_store = [&](int hawk_col, auto hawk_s, auto hawk_c) {",
-             "            (void)hawk_c;"]
+             "            (void)hawk_c;",
+             "            const int hawk_q = hawk_col / __W__;",
+             "            if (hawk_r0 + hawk_q >= hawk_rows) return;",
+             "            const long long hawk_row = (base >> 5) + hawk_r0 + hawk_q;",
+             "            hawk_col -= hawk_q * __W__;"]
     for k, sink in enumerate(sums):
         hi = sp.binding_name(sink.role, sink.name)
         lines.append(f"            {'else ' if k else ''}if (hawk_col == {k}) {{")

@@ -81,6 +81,8 @@ _SIGS = {
     "hko_poly_loss_vjp_rows_f32": (None, [_P, _P, _P, _F, _F, _F, _I, _I, _I, _P, _P]),
     "hko_cells_finish_f64": (_D, [ctypes.c_int, _P, _P, _I]),
     "hko_cells_finish_f32": (_F, [ctypes.c_int, _P, _P, _I]),
+    "hko_cells_leaves_d": (None, [ctypes.c_int, _P, _P, _I, _P, _P]),
+    "hko_cells_tree_d": (_D, [ctypes.c_int, _P, _P, _I]),
     "hko_gravity": (None, [_P, _P, _I, _P, _P, _D, _P, _I, _P, _I, _I]),
     "hko_gravity_jvp": (None, [_P, _P, _P, _P, _I, _P, _P, _D, _P, _I, _P, _I, _I]),
     "hko_gravity_vjp": (None, [_P, _P, _P, _I, _P, _P, _P, _D, _P, _P, _I, _I, _I]),
@@ -201,6 +203,20 @@ def cells_finish(hi: np.ndarray, comp: np.ndarray | None, op: str = "sum"):
     comp = None if comp is None else np.ascontiguousarray(comp)
     fn = lib().hko_cells_finish_f64 if hi.dtype == np.float64 else lib().hko_cells_finish_f32
     return fn(OP[op], _p(hi), None if comp is None else _p(comp), hi.shape[0])
+
+
+def cells_leaves(hi: np.ndarray, comp: np.ndarray, op: str = "sum"):
+    """The leaf partials ``(leaf_hi, leaf_comp)`` of float64 rows (4096 rows a leaf)."""
+    hi, comp = np.ascontiguousarray(hi), np.ascontiguousarray(comp)
+    leaves = -(-hi.shape[0] // 4096)
+    lh, lc = np.empty(leaves), np.empty(leaves)
+    lib().hko_cells_leaves_d(OP[op], _p(hi), _p(comp), hi.shape[0], _p(lh), _p(lc))
+    return lh, lc
+
+
+def cells_tree(leaf_hi: np.ndarray, leaf_comp: np.ndarray, op: str = "sum") -> float:
+    lh, lc = np.array(leaf_hi, dtype=np.float64), np.array(leaf_comp, dtype=np.float64)
+    return lib().hko_cells_tree_d(OP[op], _p(lh), _p(lc), lh.shape[0])
 
 
 def poly_loss_vjp(x, t, bar_r, a, b, c, threads: int = 1):

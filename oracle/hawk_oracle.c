@@ -167,10 +167,8 @@ void hko_poly_loss_vjp_rows_f32(const float* x, const float* t, const float* bar
         *c = finite_##SUF(s) ? (*c + xc) + two_sum_err_##SUF(*h, x, s) : (T)0;             \
         *h = s;                                                                            \
     }                                                                                      \
-    T hko_cells_finish_##SUF##_impl(int op, const T* hi, const T* comp, int64_t n) {       \
+    void hko_cells_leaves_##SUF(int op, const T* hi, const T* comp, int64_t n, T* lh, T* lc) {  \
         const int64_t leaves = (n + 4095) / 4096;                                          \
-        T* lh = (T*)malloc(sizeof(T) * (size_t)(leaves > 0 ? leaves : 1));                 \
-        T* lc = (T*)malloc(sizeof(T) * (size_t)(leaves > 0 ? leaves : 1));                 \
         for (int64_t L = 0; L < leaves; ++L) {                                             \
             const int64_t r0 = L * 4096;                                                   \
             const int64_t cnt = (n - r0) < 4096 ? (n - r0) : 4096;                         \
@@ -198,6 +196,8 @@ void hko_poly_loss_vjp_rows_f32(const float* x, const float* t, const float* bar
             lh[L] = sh[0];                                                                 \
             lc[L] = sc[0];                                                                 \
         }                                                                                  \
+    }                                                                                      \
+    T hko_cells_tree_##SUF(int op, T* lh, T* lc, int64_t leaves) {                        \
         int64_t m = leaves;                                                                \
         while (m > 1) {                                                                    \
             const int64_t pairs = m / 2;                                                   \
@@ -210,10 +210,17 @@ void hko_poly_loss_vjp_rows_f32(const float* x, const float* t, const float* bar
             if (m & 1) { lh[pairs] = lh[m - 1]; lc[pairs] = lc[m - 1]; }                   \
             m = pairs + (m & 1);                                                           \
         }                                                                                  \
-        const T root = lh[0], rc = lc[0];                                                  \
+        if (op == HKO_OP_SUM) return finite_##SUF(lh[0]) ? lh[0] + lc[0] : lh[0];          \
+        return lh[0];                                                                      \
+    }                                                                                      \
+    T hko_cells_finish_##SUF##_impl(int op, const T* hi, const T* comp, int64_t n) {       \
+        const int64_t leaves = (n + 4095) / 4096;                                          \
+        T* lh = (T*)malloc(sizeof(T) * (size_t)(leaves > 0 ? leaves : 1));                 \
+        T* lc = (T*)malloc(sizeof(T) * (size_t)(leaves > 0 ? leaves : 1));                 \
+        hko_cells_leaves_##SUF(op, hi, comp, n, lh, lc);                                   \
+        const T root = hko_cells_tree_##SUF(op, lh, lc, leaves);                           \
         free(lh);                                                                          \
         free(lc);                                                                          \
-        if (op == HKO_OP_SUM) return finite_##SUF(root) ? root + rc : root;                \
         return root;                                                                       \
     }
 DEFINE_FINISH(double, d)

@@ -54,7 +54,12 @@ void hko_poly_loss_vjp_rows_f64(const double* x, const double* t, const double* 
 void hko_poly_loss_vjp_rows_f32(const float* x, const float* t, const float* bar_r, float a, float b, float c,
                                 int64_t n, int64_t row0, int64_t nrows, float* hi, float* comp);
 
-/* the ordered finish of hawk/_cells.py over nrows rows */
+/* the ordered finish of hawk/_cells.py over nrows rows; and its two stages: one
+ * (hi, comp) partial per leaf of 4096 rows, then the pairwise levels (the leaf
+ * arrays are overwritten) and hi + comp */
+void hko_cells_leaves_d(int op, const double* hi, const double* comp, int64_t nrows, double* leaf_hi,
+                        double* leaf_comp);
+double hko_cells_tree_d(int op, double* leaf_hi, double* leaf_comp, int64_t leaves);
 double hko_cells_finish_f64(int op, const double* hi, const double* comp, int64_t nrows);
 float hko_cells_finish_f32(int op, const float* hi, const float* comp, int64_t nrows);
 

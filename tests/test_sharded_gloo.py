@@ -1,0 +1,93 @@
+"""The multi-GPU exchange, run as 2 CPU ranks over gloo.
+
+Shards start on leaf boundaries, so every rank's leaf partials, gathered in
+rank order, are the unsharded rows' leaves and the final tree is bit-identical
+to one device's finish (hawk/_cells.py:94-119 over all rows).  The device
+kernels are replaced by the oracle's two finish stages; what is tested is the
+host logic: the shard cut, the gather and its ordering, uneven last shards.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from hawk_b200 import sharded
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, n, queue):
+    import oracle
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(77)
+        x = rng.uniform(-2, 2, n)
+        t = x + 0.1 * rng.standard_normal(n)
+        bar_r = np.ones(n)
+        hi_all, comp_all = oracle.poly_loss_vjp_rows(x, t, bar_r, 0.5, -1.0, 2.0)
+        base, count = sharded.shard_range(n, world, rank)
+        lo, hi = base // 32, -(-(base + count) // 32)
+        leaves = sharded.leaves_of(count) if count else 0
+        counts = [0] * world
+        for r in range(world):
+            counts[r] = sharded.leaves_of(sharded.shard_range(n, world, r)[1])
+        width = max(counts)
+        lh = np.zeros((3, width))
+        lc = np.zeros((3, width))
+        for k in range(3):
+            if count:
+                a, b = oracle.cells_leaves(hi_all[k, lo:hi], comp_all[k, lo:hi])
+                lh[k, :leaves], lc[k, :leaves] = a, b
+        g_hi, g_comp = sharded.gather_leaves(torch.from_numpy(lh), torch.from_numpy(lc), counts)
+        got = [oracle.cells_tree(g_hi[k].numpy(), g_comp[k].numpy()) for k in range(3)]
+        want = [oracle.cells_finish(hi_all[k], comp_all[k]) for k in range(3)]
+        queue.put((rank, got, want, base, count))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("n", [131072 * 3 + 5000, 4096 * 32 * 2, 1000])
+def test_two_ranks_gather_leaves_bit_identical_to_one(n):
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, n, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [queue.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    shards = sorted((r[3], r[4]) for r in results)
+    assert shards[0][0] == 0 and shards[0][0] + shards[0][1] == shards[1][0]
+    assert shards[1][0] + shards[1][1] == n
+    assert shards[0][1] % sharded.LEAF_SAMPLES == 0 or shards[1][1] == 0
+    for rank, got, want, _b, _c in results:
+        assert got == want, (rank, got, want)
+
+
+def test_shard_ranges_cover_and_align():
+    for n in (1, 131071, 131072, 131073, 10 ** 7):
+        for world in (1, 2, 3, 4, 8):
+            cuts = [sharded.shard_range(n, world, r) for r in range(world)]
+            pos = 0
+            for base, count in cuts:
+                assert base == pos and count >= 0
+                pos += count
+                if base + count < n:
+                    assert (base + count) % sharded.LEAF_SAMPLES == 0
+            assert pos == n
