@@ -414,6 +414,53 @@ def run_configs(local: int) -> dict:
     return out
 
 
+def run_only(name: str, n: int, steps: int, warmup: int, local: int) -> dict:
+    """One benchmark kernel (``name`` of the bundles, float64) at ``n`` samples:
+    seeded inputs, ``warmup`` + ``steps`` launches, the mean device time."""
+    import torch
+
+    from hawk_b200 import runtime, workloads
+    from hawk_b200.planes import from_torch
+
+    dev = torch.device("cuda", local)
+    base = name.split("_")[0] if not name.startswith(("poly_loss", "spd_solve")) else \
+        ("poly_loss" if name.startswith("poly_loss") else "spd_solve")
+    w = workloads.MAKERS[base](n, 1)
+    k = runtime.load(BUNDLES, name, "float64", local)
+    rename = {"dr1": "dot_r1", "dr2": "dot_r2"}
+    planes, values = {}, {}
+    for role, slot, dtype, shape in k.slots:
+        if role == "uniform":
+            values[slot] = w.get(slot, 1.0)
+        elif role in ("per_sample", "vec_in", "mat_in"):
+            src = next(v for key, v in w.items() if rename.get(key, key) == slot)
+            planes[slot] = torch.as_tensor(np.ascontiguousarray(src), device=dev)
+        elif role == "lookup":
+            planes[slot] = torch.tensor([w[slot]], dtype=torch.float64, device=dev)
+        elif role == "accum_out":
+            planes[slot] = torch.empty(-(-n // 32), dtype=torch.float64, device=dev)
+        else:
+            dt = torch.int32 if dtype in ("int32", "i32") else torch.float64
+            planes[slot] = torch.empty((*shape, n), dtype=dt, device=dev)
+    bound = {key: from_torch(v) for key, v in planes.items()}
+    k.check(bound, values, n)
+    k.bind_all(bound, values, n)
+    stream = torch.cuda.current_stream(local).cuda_stream
+    for _ in range(warmup):
+        k.launch(0, n, n, stream)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(steps):
+        k.launch(0, n, n, stream)
+    b.record()
+    b.synchronize()
+    ms = a.elapsed_time(b) / steps
+    gbs = BYTES_F64[name] * n / (ms * 1e-3) / 1e9
+    return {"kernel": name, "n": n, "ms": ms, "gbs": gbs, "hbm_frac": gbs / peaks()["hbm_gbs"],
+            "launches": warmup + steps}
+
+
 # ---------------------------------------------------------------- CPU arms
 def cpu_poly_step(n: int, threads: int, mode: str):
     """One fwd + VJP (rows and cells) of the workload on the CPU oracle."""
@@ -484,6 +531,7 @@ def main() -> int:
     ap.add_argument("--mode", default="float64", choices=("float64", "float32"))
     ap.add_argument("--no-configs", action="store_true", help="skip the per-config table")
     ap.add_argument("--cpu-sample", type=int, default=1 << 23)
+    ap.add_argument("--only", default=None, help="time one benchmark kernel at --n samples (profiling runs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_env()
@@ -492,6 +540,9 @@ def main() -> int:
         return 0
     import torch
 
+    if args.only:
+        print(json.dumps(run_only(args.only, args.n, args.steps, args.warmup, local)), flush=True)
+        return 0
     dist = init_dist(world, local)
     torch.cuda.set_device(local)
     res = run_headline(args, world, rank, local, dist)

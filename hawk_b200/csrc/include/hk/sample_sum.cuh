@@ -47,6 +47,23 @@ template <class T> HK_HD T identity(int op) {
     return op == kMax ? -inf : inf;
 }
 
+// A row node whose finiteness is checked once, at the row's root: a
+// non-finite node makes every ancestor non-finite, so testing t at every node
+// (as pair_combine does) and testing only the root's t give the same row --
+// the root's compensation is zeroed by root_comp when its sum is not finite.
+template <int OP, class T> HK_HD void pair_combine_unchecked(T& s, T& c, T s2, T c2) {
+    if constexpr (OP != kSum) {
+        s = extreme(OP, s, s2);
+    } else {
+        const T t = s + s2;
+        c = (c + c2) + two_sum_err(s, s2, t);
+        s = t;
+    }
+}
+template <int OP, class T> HK_HD T root_comp(T s, T c) {
+    return (OP != kSum || finite(s)) ? c : T(0);
+}
+
 // One node of a row: (s, c) of the lower lane joined with (s2, c2) of the upper.
 template <int OP, class T> HK_HD void pair_combine(T& s, T& c, T s2, T c2) {
     if constexpr (OP != kSum) {
@@ -120,34 +137,36 @@ __device__ __forceinline__ void row_reduce(T (&h)[W], Store&& store) {
 }
 
 // One round of the halving butterfly: the lane holds M slots; the lower lane
-// of the pair (bit `off` clear) keeps slots [0, M/2), the upper lane slots
-// [M/2, M); each sends the other half to its partner and joins the kept half
-// with the partner's copy (lower lane's value first).  The kept slots move to
-// [0, M - M/2); a lower lane's extra slot (M odd) is padding that only ever
-// meets the same padding on its later partners.
+// of the pair (bit `off` clear) keeps columns [0, M/2), the upper lane columns
+// [M/2, M); each sends the other half to its partner and joins the kept column
+// with the partner's copy into slot j.  A sum node is symmetric in its two
+// operands (t = s + s2, the ordered two-sum residual, c + c2), so both lanes
+// compute the same node without caring which holds the lower lane's value; a
+// max/min node takes the lower lane's value first.  A lower lane's extra slot
+// (M odd) is padding that only ever meets the same padding on later partners.
 template <int M, int OP, class T>
 __device__ __forceinline__ void halve(T* h, T* c, int off, bool upper) {
     constexpr int LO = M / 2, UP = M - M / 2;
     const T pad = identity<T>(OP);
 #pragma unroll
     for (int j = 0; j < UP; ++j) {
-        const T gh = upper ? (j < LO ? h[j] : pad) : h[LO + j];
-        const T gc = upper ? (j < LO ? c[j] : T(0)) : c[LO + j];
+        const T lo_h = j < LO ? h[j] : pad;
+        const T lo_c = j < LO ? c[j] : T(0);
+        const T kh = upper ? h[LO + j] : lo_h;     // the column this lane keeps
+        const T kc = upper ? c[LO + j] : lo_c;
+        const T gh = upper ? lo_h : h[LO + j];     // the one it gives away
+        const T gc = upper ? lo_c : c[LO + j];
         const T rh = __shfl_xor_sync(0xffffffffu, gh, off);
         const T rc = __shfl_xor_sync(0xffffffffu, gc, off);
-        if (upper) {
-            T s = rh, sc = rc;
-            pair_combine<OP>(s, sc, h[LO + j], c[LO + j]);
-            h[LO + j] = s;
-            c[LO + j] = sc;
-        } else if (j < LO) {
-            pair_combine<OP>(h[j], c[j], rh, rc);
+        T s = kh, sc = kc;
+        if constexpr (OP == kSum) {
+            pair_combine_unchecked<OP>(s, sc, rh, rc);
+        } else {
+            s = upper ? rh : kh;
+            pair_combine_unchecked<OP>(s, sc, upper ? kh : rh, rc);
         }
-    }
-#pragma unroll
-    for (int j = 0; j < UP; ++j) {
-        h[j] = upper ? h[LO + j] : (j < LO ? h[j] : pad);
-        c[j] = upper ? c[LO + j] : (j < LO ? c[j] : T(0));
+        h[j] = s;
+        c[j] = sc;
     }
 }
 
@@ -188,13 +207,13 @@ __device__ __forceinline__ void rows_reduce(T (&h)[K * W], Store&& store) {
     keep((lane & 1u) != 0u, M5 / 2);
 #pragma unroll
     for (int j = 0; j < M6; ++j)
-        if (j < held) store(first + j, h[j], c[j]);
+        if (j < held) store(first + j, h[j], root_comp<OP>(h[j], c[j]));
 }
 
 // Rows of 32 samples one warp folds per trip for a sink of W columns: the
-// largest power of two K <= 8 with K * W <= 32 (1 when W > 16).
+// largest power of two K <= 8 with K * W <= 16 (1 when W > 8).
 constexpr int rows_per_warp(int w) {
-    return w <= 4 ? 8 : (w <= 8 ? 4 : (w <= 16 ? 2 : 1));
+    return w <= 2 ? 8 : (w <= 4 ? 4 : (w <= 8 ? 2 : 1));
 }
 #endif
 
