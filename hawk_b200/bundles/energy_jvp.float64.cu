@@ -22,14 +22,6 @@ extern "C" __global__ void __launch_bounds__(256) energy_jvp(
     const hk::VecIn<Real, 3> vin_v(p_vin_v);
     (void)vin_v;
     for (long long hawk_flat = hk::lane_first(); hawk_flat < count; hawk_flat += hk::lane_step()) {
-        if ((threadIdx.x & 31u) == 0u) {
-            const long long hawk_pf = (hawk_flat & ~31LL) + 2LL * hk::lane_step();
-            if (hawk_pf < count) {
-                const long long hawk_pfn = (count - hawk_pf) < 32 ? (count - hawk_pf) : 32;
-                vin_dot_v.prefetch(base + hawk_pf, hawk_pfn);
-                vin_v.prefetch(base + hawk_pf, hawk_pfn);
-            }
-        }
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
         (void)hawk_i;

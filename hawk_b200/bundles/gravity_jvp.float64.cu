@@ -40,18 +40,6 @@ extern "C" __global__ void __launch_bounds__(256) gravity_jvp(
     const Real uni_G = p_uni_G;
     (void)uni_G;
     for (long long hawk_flat = hk::lane_first(); hawk_flat < count; hawk_flat += hk::lane_step()) {
-        if ((threadIdx.x & 31u) == 0u) {
-            const long long hawk_pf = (hawk_flat & ~31LL) + 2LL * hk::lane_step();
-            if (hawk_pf < count) {
-                const long long hawk_pfn = (count - hawk_pf) < 32 ? (count - hawk_pf) : 32;
-                vin_dot_r1.prefetch(base + hawk_pf, hawk_pfn);
-                vin_dot_r2.prefetch(base + hawk_pf, hawk_pfn);
-                vin_r1.prefetch(base + hawk_pf, hawk_pfn);
-                vin_r2.prefetch(base + hawk_pf, hawk_pfn);
-                psc_m1.prefetch(base + hawk_pf, hawk_pfn);
-                psc_m2.prefetch(base + hawk_pf, hawk_pfn);
-            }
-        }
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
         (void)hawk_i;

@@ -28,15 +28,6 @@ extern "C" __global__ void __launch_bounds__(256) kepler_vjp(
     const hk::ScalarIn<Real> psc_e(p_psc_e);
     (void)psc_e;
     for (long long hawk_flat = hk::lane_first(); hawk_flat < count; hawk_flat += hk::lane_step()) {
-        if ((threadIdx.x & 31u) == 0u) {
-            const long long hawk_pf = (hawk_flat & ~31LL) + 2LL * hk::lane_step();
-            if (hawk_pf < count) {
-                const long long hawk_pfn = (count - hawk_pf) < 32 ? (count - hawk_pf) : 32;
-                psc_M.prefetch(base + hawk_pf, hawk_pfn);
-                psc_bar_E.prefetch(base + hawk_pf, hawk_pfn);
-                psc_e.prefetch(base + hawk_pf, hawk_pfn);
-            }
-        }
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
         (void)hawk_i;

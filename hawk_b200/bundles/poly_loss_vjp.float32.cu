@@ -55,21 +55,12 @@ extern "C" __global__ void __launch_bounds__(256) poly_loss_vjp(
     const auto lut_c_cell = lut_c.cell();
     (void)lut_c_cell;
     const long long hawk_rows = (count + 31) >> 5;
-    for (long long hawk_r0 = hk::warp_first() * 4; hawk_r0 < hawk_rows; hawk_r0 += hk::warp_step() * 4) {
-        if ((threadIdx.x & 31u) == 0u) {
-            const long long hawk_pf = (hawk_r0 + 2LL * 4 * hk::warp_step()) << 5;
-            if (hawk_pf < count) {
-                const long long hawk_pfn = (count - hawk_pf) < 128 ? (count - hawk_pf) : 128;
-                psc_bar_r.prefetch(base + hawk_pf, hawk_pfn);
-                psc_t.prefetch(base + hawk_pf, hawk_pfn);
-                psc_x.prefetch(base + hawk_pf, hawk_pfn);
-            }
-        }
-        Real hawk_terms[12];
+    for (long long hawk_r0 = hk::warp_first() * 8; hawk_r0 < hawk_rows; hawk_r0 += hk::warp_step() * 8) {
+        Real hawk_terms[24];
 #pragma unroll
-        for (int hawk_k = 0; hawk_k < 12; ++hawk_k) hawk_terms[hawk_k] = hk::ss::identity<Real>(hk::ss::kSum);
+        for (int hawk_k = 0; hawk_k < 24; ++hawk_k) hawk_terms[hawk_k] = hk::ss::identity<Real>(hk::ss::kSum);
 #pragma unroll
-        for (int hawk_q = 0; hawk_q < 4; ++hawk_q) {
+        for (int hawk_q = 0; hawk_q < 8; ++hawk_q) {
         Real* const hawk_ss = hawk_terms + hawk_q * 3;
         const long long hawk_flat = ((hawk_r0 + hawk_q) << 5) + static_cast<long long>(threadIdx.x & 31u);
         if (hawk_flat < count) {
@@ -105,6 +96,6 @@ extern "C" __global__ void __launch_bounds__(256) poly_loss_vjp(
                 aout_bar_c_comp.data()[hawk_row] = hawk_c;
             }
         };
-        hk::ss::rows_reduce<4, 3, hk::ss::kSum>(hawk_terms, hawk_ss_store);
+        hk::ss::rows_reduce<8, 3, hk::ss::kSum>(hawk_terms, hawk_ss_store);
     }
 }

@@ -49,23 +49,6 @@ template <class T> HK_FI void st_out(T* p, T v) {
 #endif
 }
 
-// An asynchronous prefetch into L2 of `bytes` bytes at `p` (the TMA unit's
-// bulk prefetch: one instruction for a whole run, no registers, no completion
-// to wait for).  The run must start on a 16-byte boundary and its length is
-// taken down to a multiple of 16; anything else is skipped -- it is a hint.
-HK_FI void prefetch_l2(const void* p, long long bytes) {
-#if defined(__CUDA_ARCH__)
-    const unsigned long long a = reinterpret_cast<unsigned long long>(p);
-    const unsigned n = static_cast<unsigned>(bytes > 0 ? (bytes & ~15LL) : 0LL);
-    if (n == 0 || (a & 15ull) != 0ull) return;
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(__cvta_generic_to_global(p)), "r"(n)
-                 : "memory");
-#else
-    (void)p;
-    (void)bytes;
-#endif
-}
-
 // A rank-0 value read from a plane.
 template <class T> struct Val {
     T x;
@@ -84,10 +67,6 @@ template <class T> struct ScalarIn {
     HK_FI explicit ScalarIn(const abi::IntHandle& h) : p(static_cast<const T*>(h.data)), n(h.samples) {}
     HK_FI Val<T> operator[](const SampleIndex& i) const { return Val<T>{ld_in(p + i.g)}; }
     HK_FI T cell() const { return ld_in(p); }
-    // samples [first, first + count) into L2
-    HK_FI void prefetch(i64 first, i64 count) const {
-        prefetch_l2(p + first, count * static_cast<i64>(sizeof(T)));
-    }
     HK_FI const T* data() const { return p; }
     HK_FI u64 samples() const { return n; }
 };
@@ -103,11 +82,6 @@ template <class T, int N> struct VecIn {
 #pragma unroll
         for (int k = 0; k < N; ++k) r.v[k] = ld_in(p + static_cast<u64>(k) * pitch + i.g);
         return r;
-    }
-    HK_FI void prefetch(i64 first, i64 count) const {
-#pragma unroll
-        for (int k = 0; k < N; ++k)
-            prefetch_l2(p + static_cast<u64>(k) * pitch + first, count * static_cast<i64>(sizeof(T)));
     }
     HK_FI const T* data() const { return p; }
     HK_FI u64 samples() const { return n; }
@@ -127,11 +101,6 @@ template <class T, int R, int C> struct MatIn {
             for (int c = 0; c < C; ++c)
                 a.m[r][c] = ld_in(p + static_cast<u64>(r * C + c) * pitch + i.g);
         return a;
-    }
-    HK_FI void prefetch(i64 first, i64 count) const {
-#pragma unroll
-        for (int k = 0; k < R * C; ++k)
-            prefetch_l2(p + static_cast<u64>(k) * pitch + first, count * static_cast<i64>(sizeof(T)));
     }
     HK_FI const T* data() const { return p; }
     HK_FI u64 samples() const { return n; }

@@ -20,7 +20,7 @@ import re
 from dataclasses import dataclass, field
 
 from ..errors import HawkError
-from .wrapper import B200, prefetch_lines, sample_sum_store
+from .wrapper import B200, sample_sum_store
 from .writer import B200_WRITER, body_text
 
 #: Scalar modes the b200 target builds: the reference's float64 and float32
@@ -93,16 +93,10 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64") -> Unit:
     if sums:
         elem = element_spelling(sums[0].ttype.dtype)
         opened, closed = wrapper.sample_sum_frame(len(sums), elem, sample_sum_store(sums), sums[0].op)
-        rows = wrapper.fold_rows(len(sums))
-        head, rest = opened.split("\n", 2)[:2], opened.split("\n", 2)[2]
-        pf = prefetch_lines(walk, "row", rows)
-        loop = ["\n".join(head + ([pf] if pf else []) + [rest]), body, closed]
+        loop = [opened, body, closed]
         frame = "row"
     else:
-        opened = wrapper.index_prologue()
-        head, rest = opened.split("\n", 1)
-        pf = prefetch_lines(walk, "lane")
-        loop = ["\n".join([head] + ([pf] if pf else []) + [rest]), body, wrapper.index_epilogue()]
+        loop = [wrapper.index_prologue(), body, wrapper.index_epilogue()]
         frame = "lane"
     parts = [
         f"// hawk_b200 unit {name!r} (scalar mode {mode}), sm_100a.",

@@ -134,8 +134,11 @@ class B200Wrapper:
 
     def fold_rows(self, width: int) -> int:
         """Rows one warp folds per trip: the largest power of two K <= 8 with
-        K * width <= 16 shuffle columns (hk::ss::rows_per_warp)."""
-        return 8 if width <= 2 else 4 if width <= 4 else 2 if width <= 8 else 1
+        K * width <= 32 butterfly columns (hk::ss::rows_per_warp).  Measured on
+        the B200 for the 3-column Param-gradient VJP at 2^26 samples: K = 2, 4,
+        8 take 0.58, 0.57, 0.36 ms -- more rows give each halving round more
+        independent columns to overlap."""
+        return 8 if width <= 4 else 4 if width <= 8 else 2 if width <= 16 else 1
 
     def sample_sum_frame(self, width: int, elem: str, store: str,
                          op: str = "sum", live: str | None = None) -> tuple:
@@ -180,36 +183,6 @@ class B200Wrapper:
         identical on every target (hawk/emit/wrapper.py:276-281)."""
         from hawk.emit.dispatch import render_dispatch_rank0
         return render_dispatch_rank0(kind_spelling, branch_spellings, policy, **kw)
-
-
-#: Trips ahead a warp prefetches its input planes into L2.
-PREFETCH_TRIPS = 2
-
-
-def prefetch_lines(walk, frame: str, rows: int = 1) -> str:
-    """Lane 0 of each warp prefetches, into L2, the samples the warp takes
-    ``PREFETCH_TRIPS`` trips ahead from every input plane (one bulk prefetch
-    per component, hk::prefetch_l2), so a warp's next loads are in flight while
-    it computes.  ``frame`` is "lane" (32 samples a trip, ``hawk_flat``) or
-    "row" (``rows`` rows of 32 a trip, ``hawk_r0``)."""
-    sp = _spelling()
-    views = [sp.binding_name(role, name) for role, name in walk.arg_spec
-             if role in ("vec_in", "mat_in", "per_sample")]
-    if not views:
-        return ""
-    if frame == "lane":
-        first = f"(hawk_flat & ~31LL) + {PREFETCH_TRIPS}LL * hk::lane_step()"
-        span = 32
-    else:
-        first = f"(hawk_r0 + {PREFETCH_TRIPS}LL * {rows} * hk::warp_step()) << 5"
-        span = 32 * rows
-    lines = ["        if ((threadIdx.x & 31u) == 0u) {",
-             f"            const long long hawk_pf = {first};",
-             "            if (hawk_pf < count) {",
-             f"                const long long hawk_pfn = (count - hawk_pf) < {span} ? (count - hawk_pf) : {span};"]
-    lines += [f"                {v}.prefetch(base + hawk_pf, hawk_pfn);" for v in views]
-    lines += ["            }", "        }"]
-    return "\n".join(lines)
 
 
 def sample_sum_store(sums) -> str:
