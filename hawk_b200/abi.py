@@ -46,6 +46,8 @@ SIGNATURES = {
     "hkb_cells_scratch_bytes": (_c.c_size_t, [_c.c_int, _c.c_int, _c.c_int64]),
     "hkb_cells_finish": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _c.POINTER(_P), _c.POINTER(_P),
                                     _c.c_int64, _P, _P, _P]),
+    "hkb_cells_finish_noalloc": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _c.POINTER(_P), _c.POINTER(_P),
+                                            _c.c_int64, _P, _P]),
 }
 
 _LOCK = threading.Lock()
@@ -173,6 +175,20 @@ def cells_finish(op: str, dtype: str, hi, comp, rows: int, scratch: int, out: in
                                  _ptr_array(comp) if comp is not None else None, int(rows),
                                  ctypes.c_void_p(int(scratch)), ctypes.c_void_p(int(out)),
                                  ctypes.c_void_p(int(stream) or None)), "hkb_cells_finish")
+
+
+def cells_finish_noalloc(op: str, dtype: str, hi, comp, rows: int, out: int, stream: int = 0) -> None:
+    """``cells_finish`` with the leaf partials in the library's static device
+    array: for callers that cannot allocate device memory at finish time.  At
+    most ``NOALLOC_LEAF_CAP`` leaf partials (all columns together) per call;
+    calls that can overlap on the GPU share the array and race."""
+    check(lib().hkb_cells_finish_noalloc(OP[op], DTYPE[dtype], len(hi), _ptr_array(hi),
+                                         _ptr_array(comp) if comp is not None else None, int(rows),
+                                         ctypes.c_void_p(int(out)), ctypes.c_void_p(int(stream) or None)),
+          "hkb_cells_finish_noalloc")
+
+
+NOALLOC_LEAF_CAP = 8192
 
 
 def cells_leaves(op: str, dtype: str, hi, comp, rows: int, leaf_hi: int, leaf_comp: int, stream: int = 0) -> None:

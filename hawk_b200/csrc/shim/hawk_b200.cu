@@ -18,6 +18,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -585,3 +586,68 @@ int hkb_cells_finish(int op, int dtype, int ncols, const void* const* hi, const 
 }
 
 }  // extern "C"
+
+// ------------------------------------------------ the allocation-free finish
+//
+// hkb_cells_finish needs its caller to hand it scratch for the leaf partials.
+// Some callers have no way to get device memory at the point they finish a
+// reduction: a host framework that owns every device allocation and hands its
+// plugins only their inputs and outputs, or a real-time loop whose memory
+// budget is fixed before it starts and which must never enter the CUDA
+// allocator.  For them, hkb_cells_finish_noalloc keeps the leaf partials in
+// the array below, which lives in this library's device image: every GPU that
+// loads the library holds it (HKB_NOALLOC_LEAF_CAP partials of hi and comp,
+// 128 KiB) until the process exits, and nothing is allocated per call.
+
+namespace {
+
+static __device__ __align__(256) double g_noalloc_leaves[2 * HKB_NOALLOC_LEAF_CAP];
+
+constexpr int kMaxDevices = 128;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// The device address of g_noalloc_leaves on the current device, resolved once
+// per device (host code cannot use the symbol itself as an address).
+int noalloc_scratch(void** out) {
+    int device = -1;
+    HKB_CUDA(cudaGetDevice(&device), "reading the current device");
+    if (device < 0 || device >= kMaxDevices)
+        return fail(HKB_ERR_RANGE, "device %d is beyond the %d devices the static scratch table covers",
+                    device, kMaxDevices);
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_ptr[device] == nullptr) {
+        void* p = nullptr;
+        HKB_CUDA(cudaGetSymbolAddress(&p, g_noalloc_leaves), "resolving the static leaf scratch");
+        g_noalloc_ptr[device] = p;
+    }
+    *out = g_noalloc_ptr[device];
+    return HKB_OK;
+}
+
+}  // namespace
+
+extern "C" int hkb_cells_finish_noalloc(int op, int dtype, int ncols, const void* const* hi,
+                                         const void* const* comp, int64_t rows, void* out, void* stream) {
+    int status = check_cells(op, dtype, ncols);
+    if (status != HKB_OK) return status;
+    if (rows < 1) return fail(HKB_ERR_RANGE, "a finish needs at least one row, got %lld", (long long)rows);
+    const int64_t leaves = leaves_of(rows);
+    if (leaves * ncols > HKB_NOALLOC_LEAF_CAP)
+        return fail(HKB_ERR_RANGE,
+                    "%d columns of %lld rows need %lld leaf partials, more than the %d the static scratch "
+                    "holds (at most %lld rows per column at this column count); use hkb_cells_finish with "
+                    "caller scratch", ncols, (long long)rows, (long long)(leaves * ncols), HKB_NOALLOC_LEAF_CAP,
+                    (long long)(HKB_NOALLOC_LEAF_CAP / ncols) * HKB_LEAF_ROWS);
+    void* scratch = nullptr;
+    status = noalloc_scratch(&scratch);
+    if (status != HKB_OK) return status;
+    // Every partial the tree stage reads is written by the leaf stage of the
+    // same call first, so nothing in the scratch has to start at zero.
+    const size_t elem = dtype == HKB_F32 ? sizeof(float) : sizeof(double);
+    char* lh = static_cast<char*>(scratch);
+    char* lc = lh + static_cast<size_t>(HKB_NOALLOC_LEAF_CAP) * elem;
+    status = hkb_cells_leaves(op, dtype, ncols, hi, comp, rows, lh, lc, stream);
+    if (status != HKB_OK) return status;
+    return hkb_cells_tree(op, dtype, ncols, lh, lc, leaves, out, stream);
+}

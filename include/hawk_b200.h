@@ -134,6 +134,27 @@ size_t hkb_cells_scratch_bytes(int dtype, int ncols, int64_t rows);
 int hkb_cells_finish(int op, int dtype, int ncols, const void* const* hi, const void* const* comp,
                      int64_t rows, void* scratch, void* out, void* stream);
 
+/* ---------------------------------------------- cells without allocation */
+
+/* No counterpart in the reference: hkb_cells_finish for callers that cannot
+ * allocate device memory when they finish a reduction (a host framework that
+ * owns every device allocation and gives its plugins only their inputs and
+ * outputs; a loop whose memory budget is fixed before it starts).  The leaf
+ * partials live in a static device array of the library, 2 x
+ * HKB_NOALLOC_LEAF_CAP doubles (128 KiB), which every GPU that loads the
+ * library holds until the process exits; the call allocates nothing.
+ *
+ * Limit: ncols * ceil(rows / 4096) <= HKB_NOALLOC_LEAF_CAP, else HKB_ERR_RANGE
+ * (8192 leaves: 33.5M rows for one column).  The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress) and caches it; make
+ * that first call before capturing any stream.  All calls share the one array:
+ * calls that can overlap on the GPU (different streams, different host threads)
+ * race on it and must be ordered by the caller.  Every partial is written
+ * before it is read within a call, so no state carries between calls. */
+#define HKB_NOALLOC_LEAF_CAP 8192
+int hkb_cells_finish_noalloc(int op, int dtype, int ncols, const void* const* hi, const void* const* comp,
+                             int64_t rows, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
