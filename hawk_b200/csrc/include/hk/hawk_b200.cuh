@@ -33,6 +33,11 @@ HK_FI i64 warp_step() { return lane_step() >> 5; }
 
 }  // namespace hk
 
+// The dynamic shared memory every block of the unit's entry uses, exported
+// for the loader, which sets the entry's limit and passes it at launch (a
+// unit that exports nothing uses none).
+#define HK_DYNAMIC_SMEM(BYTES) extern "C" __device__ const unsigned int hk_dynamic_smem_bytes = (BYTES);
+
 // The layout self-check exports: the loader reads them and refuses a unit whose
 // mirrors are not the sizes it packs (hawk/artifact/layout.py:35-61).
 #define HK_ABI_TAG "aether-abi/2"

@@ -211,9 +211,9 @@ __device__ __forceinline__ void rows_reduce(T (&h)[K * W], Store&& store) {
 }
 
 // Rows of 32 samples one warp folds per trip for a sink of W columns: the
-// largest power of two K <= 8 with K * W <= 32 (1 when W > 16).
+// largest power of two K <= 32 with K * W <= 32.
 constexpr int rows_per_warp(int w) {
-    return w <= 4 ? 8 : (w <= 8 ? 4 : (w <= 16 ? 2 : 1));
+    return w <= 1 ? 32 : (w <= 2 ? 16 : (w <= 4 ? 8 : (w <= 8 ? 4 : (w <= 16 ? 2 : 1))));
 }
 #endif
 

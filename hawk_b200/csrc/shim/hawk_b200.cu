@@ -102,6 +102,7 @@ struct hkb_entry {
     std::string name;
     int regs = 0;
     int blocks_per_sm = 0;
+    unsigned dynamic_smem = 0;   // bytes per block the unit exports (hk_dynamic_smem_bytes)
 };
 
 struct hkb_argblock {
@@ -241,8 +242,28 @@ int hkb_library_entry(hkb_library* lib, const char* name, hkb_entry** out) {
         return cuda_fail(e2, "reading the entry's attributes");
     }
     entry->regs = attr.numRegs;
+    // A unit whose entry stages through dynamic shared memory exports its size.
+    void* sptr = nullptr;
+    size_t sbytes = 0;
+    if (cudaLibraryGetGlobal(&sptr, &sbytes, lib->lib, "hk_dynamic_smem_bytes") == cudaSuccess &&
+        sbytes == sizeof(unsigned)) {
+        e2 = cudaMemcpy(&entry->dynamic_smem, sptr, sizeof(unsigned), cudaMemcpyDeviceToHost);
+        if (e2 != cudaSuccess) {
+            delete entry;
+            return cuda_fail(e2, "reading the entry's shared-memory size");
+        }
+        e2 = cudaFuncSetAttribute(reinterpret_cast<const void*>(kernel),
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(entry->dynamic_smem));
+        if (e2 != cudaSuccess) {
+            delete entry;
+            return cuda_fail(e2, "raising the entry's shared-memory limit");
+        }
+    } else {
+        cudaGetLastError();
+    }
     e2 = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&entry->blocks_per_sm,
-                                                       reinterpret_cast<const void*>(kernel), kBlock, 0);
+                                                       reinterpret_cast<const void*>(kernel), kBlock,
+                                                       entry->dynamic_smem);
     if (e2 != cudaSuccess) {
         delete entry;
         return cuda_fail(e2, "computing the entry's occupancy");
@@ -388,7 +409,7 @@ int hkb_entry_launch(hkb_entry* entry, hkb_argblock* block, int64_t base, int64_
     args.push_back(&ns);
     const dim3 grid(static_cast<unsigned>(grid_for(entry, count)));
     const cudaError_t err = cudaLaunchKernel(reinterpret_cast<const void*>(entry->kernel), grid, dim3(kBlock),
-                                             args.data(), 0, static_cast<cudaStream_t>(stream));
+                                             args.data(), entry->dynamic_smem, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return cuda_fail(err, "launching the entry");
     return HKB_OK;
 }
@@ -424,7 +445,20 @@ __global__ void __launch_bounds__(hk::ss::kSlots) leaves_kernel(Columns cols, lo
     const int live = cnt < hk::ss::kSlots ? cnt : hk::ss::kSlots;
     const int s = threadIdx.x;
     T h = T(0), c = T(0);
-    if (s < live) {
+    if (cnt == hk::ss::kLeaf) {
+        // A full leaf: all 16 terms of the slot (and their compensations) are
+        // loaded before the first step, so the loads are in flight together.
+        T xh[hk::ss::kTerms], xc[hk::ss::kTerms];
+#pragma unroll
+        for (int k = 0; k < hk::ss::kTerms; ++k) {
+            xh[k] = hi[r0 + k * hk::ss::kSlots + s];
+            xc[k] = (OP == hk::ss::kSum && comp != nullptr) ? comp[r0 + k * hk::ss::kSlots + s] : T(0);
+        }
+        h = xh[0];
+        c = hk::ss::finite(h) ? xc[0] : T(0);
+#pragma unroll
+        for (int k = 1; k < hk::ss::kTerms; ++k) hk::ss::neumaier_add<OP>(h, c, xh[k], xc[k]);
+    } else if (s < live) {
         h = hi[r0 + s];
         c = (OP == hk::ss::kSum && comp != nullptr) ? comp[r0 + s] : T(0);
         if (!hk::ss::finite(h)) c = T(0);

@@ -90,6 +90,7 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64") -> Unit:
     if len({s.op for s in sums}) > 1:
         raise HawkError(f"{name!r}: one kernel reduces over samples with one op (sum, max or min)")
     wrapper = B200
+    smem = 0
     if sums:
         elem = element_spelling(sums[0].ttype.dtype)
         opened, closed = wrapper.sample_sum_frame(len(sums), elem, sample_sum_store(sums), sums[0].op)
@@ -107,6 +108,7 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64") -> Unit:
         "using Int = long long;",
         "",
         "HK_SELF_CHECK_EXPORTS",
+        *([f"HK_DYNAMIC_SMEM({smem})"] if smem else []),
         "",
         wrapper.entry_signature(walk, name),
         "{",
@@ -118,7 +120,7 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64") -> Unit:
     text = "\n".join(parts)
     records = tuple((s.name, s.op, s.companion.name if s.op == "sum" else None) for s in sums)
     return Unit(name=name, mode=mode, text=text, body=body, frame=frame, sums=records,
-                digest=hashlib.sha256(text.encode()).hexdigest())
+                digest=hashlib.sha256(text.encode()).hexdigest(), notes={"dynamic_smem": smem})
 
 
 _IDENT = re.compile(r"[A-Za-z_][A-Za-z0-9_]*")

@@ -92,6 +92,7 @@ def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "flo
         "cubin": f"{stem}.cubin",
         "unit_digest": unit.digest,
         "frame": unit.frame,
+        "dynamic_smem": unit.notes.get("dynamic_smem", 0),
         "sample_sums": [{"name": n, "op": op, "companion": comp} for n, op, comp in unit.sums],
         "slots": _slot_records(kernel.walk),
         "nvrtc_options": [o for o in options() if not o.startswith("-I")],

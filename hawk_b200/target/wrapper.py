@@ -133,12 +133,15 @@ class B200Wrapper:
         return "\n".join(lines)
 
     def fold_rows(self, width: int) -> int:
-        """Rows one warp folds per trip: the largest power of two K <= 8 with
-        K * width <= 32 butterfly columns (hk::ss::rows_per_warp).  Measured on
+        """Rows one warp folds per trip: the largest power of two K with
+        K * width <= 32 butterfly columns (hk::ss::rows_reduce).  Measured on
         the B200 for the 3-column Param-gradient VJP at 2^26 samples: K = 2, 4,
-        8 take 0.58, 0.57, 0.36 ms -- more rows give each halving round more
-        independent columns to overlap."""
-        return 8 if width <= 4 else 4 if width <= 8 else 2 if width <= 16 else 1
+        8, 16 take 0.58, 0.57, 0.36, 0.53 ms; a shared-memory variant in which
+        each lane evaluates one whole (row, column) tree took 0.375 ms."""
+        k = 1
+        while k < 32 and 2 * k * width <= 32:
+            k *= 2
+        return k
 
     def sample_sum_frame(self, width: int, elem: str, store: str,
                          op: str = "sum", live: str | None = None) -> tuple:
