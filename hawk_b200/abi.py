@@ -31,6 +31,7 @@ SIGNATURES = {
     "hkb_library_load": (_c.c_int, [_P, _c.c_size_t, _c.c_int, _c.POINTER(_P)]),
     "hkb_library_load_file": (_c.c_int, [_c.c_char_p, _c.c_int, _c.POINTER(_P)]),
     "hkb_library_free": (None, [_P]),
+    "hkb_library_errors": (_c.c_int, [_P, _c.POINTER(_c.c_uint), _c.c_int]),
     "hkb_library_entry": (_c.c_int, [_P, _c.c_char_p, _c.POINTER(_P)]),
     "hkb_entry_info": (_c.c_int, [_P, _c.POINTER(_c.c_int), _c.POINTER(_c.c_int), _c.POINTER(_c.c_int),
                                   _c.c_int64, _c.POINTER(_c.c_int64)]),
@@ -105,6 +106,12 @@ class Library:
 
     def entry(self, name: str) -> "Entry":
         return Entry(self, name)
+
+    def errors(self, clear: bool = True) -> int:
+        """The unit's error word (0: every bounded device wait completed)."""
+        flags = ctypes.c_uint(0)
+        check(lib().hkb_library_errors(self._h, ctypes.byref(flags), 1 if clear else 0), "hkb_library_errors")
+        return int(flags.value)
 
     def __del__(self):
         h = getattr(self, "_h", None)

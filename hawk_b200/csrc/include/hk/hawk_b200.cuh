@@ -19,6 +19,7 @@
 #include "linalg.cuh"
 #include "ints.cuh"
 #include "sample_sum.cuh"
+#include "stage.cuh"
 
 namespace hk {
 
@@ -39,9 +40,12 @@ HK_FI i64 warp_step() { return lane_step() >> 5; }
 #define HK_DYNAMIC_SMEM(BYTES) extern "C" __device__ const unsigned int hk_dynamic_smem_bytes = (BYTES);
 
 // The layout self-check exports: the loader reads them and refuses a unit whose
-// mirrors are not the sizes it packs (hawk/artifact/layout.py:35-61).
+// mirrors are not the sizes it packs (hawk/artifact/layout.py:35-61).  Every
+// unit also defines its error word, which a bounded wait that ran out sets
+// (hk/stage.cuh) and the host reads with hkb_library_errors.
 #define HK_ABI_TAG "aether-abi/2"
 #define HK_SELF_CHECK_EXPORTS                                                        \
+    extern "C" __device__ unsigned int hk_error_flags = 0u;                          \
     extern "C" __device__ const char eagle_abi_tag[] = HK_ABI_TAG;                   \
     extern "C" __device__ unsigned long long eagle_layout_sizes[5] = {               \
         sizeof(hk::abi::GRefMirror), sizeof(hk::abi::ScalarHandle),                  \

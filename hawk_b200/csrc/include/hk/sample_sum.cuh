@@ -108,34 +108,6 @@ constexpr int kTerms = 16;
 constexpr int kLeaf = kSlots * kTerms;   // rows per leaf
 
 #if defined(__CUDACC__) || defined(__CUDACC_RTC__)
-// The row of the calling warp: every lane passes its sample's W terms (the
-// identity for a lane past the last sample); after five butterfly rounds every
-// lane holds every column's (sum, compensation), and lane k < W calls
-// store(k, sum, comp) for column k.  All 32 lanes of the warp must call it.
-template <int W, int OP, class T, class Store>
-__device__ __forceinline__ void row_reduce(T (&h)[W], Store&& store) {
-    T c[W];
-#pragma unroll
-    for (int k = 0; k < W; ++k) c[k] = T(0);
-    const unsigned lane = threadIdx.x & 31u;
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-        const bool lower = (lane & static_cast<unsigned>(off)) == 0u;
-#pragma unroll
-        for (int k = 0; k < W; ++k) {
-            const T rh = __shfl_xor_sync(0xffffffffu, h[k], off);
-            const T rc = __shfl_xor_sync(0xffffffffu, c[k], off);
-            T s = lower ? h[k] : rh, sc = lower ? c[k] : rc;
-            pair_combine<OP>(s, sc, lower ? rh : h[k], lower ? rc : c[k]);
-            h[k] = s;
-            c[k] = sc;
-        }
-    }
-#pragma unroll
-    for (int k = 0; k < W; ++k)
-        if (static_cast<int>(lane) == (k & 31)) store(k, h[k], c[k]);
-}
-
 // One round of the halving butterfly: the lane holds M slots; the lower lane
 // of the pair (bit `off` clear) keeps columns [0, M/2), the upper lane columns
 // [M/2, M); each sends the other half to its partner and joins the kept column
@@ -210,11 +182,6 @@ __device__ __forceinline__ void rows_reduce(T (&h)[K * W], Store&& store) {
         if (j < held) store(first + j, h[j], root_comp<OP>(h[j], c[j]));
 }
 
-// Rows of 32 samples one warp folds per trip for a sink of W columns: the
-// largest power of two K <= 32 with K * W <= 32.
-constexpr int rows_per_warp(int w) {
-    return w <= 1 ? 32 : (w <= 2 ? 16 : (w <= 4 ? 8 : (w <= 8 ? 4 : (w <= 16 ? 2 : 1))));
-}
 #endif
 
 }  // namespace ss

@@ -20,6 +20,11 @@
 //                     out[i](r, c) -> a reference to one component (a solve
 //                     writes its result through it);
 //   rows.data()[r] -> a row plane's element r (sample-sum rows).
+//
+// An input view may be staged (hk/stage.cuh): the frame copies each tile of
+// its components into shared memory, `stage_off` bytes into the stage and
+// `comp_bytes` apart, and the sample index carries the tile; a read then comes
+// from shared memory, and from global memory when the index carries none.
 #pragma once
 #include "abi.cuh"
 #include "item.cuh"
@@ -27,7 +32,9 @@
 namespace hk {
 
 struct SampleIndex {
-    i64 g;   // the global sample index
+    i64 g;                                // the global sample index
+    const unsigned char* st = nullptr;    // the staged tile holding the sample, if any
+    int local = 0;                        // the sample's place in that tile
 
     static HK_FI SampleIndex make(usize k) { return SampleIndex{static_cast<i64>(k)}; }
     HK_FI i64 global() const { return g; }
@@ -63,9 +70,15 @@ template <class T> struct Val {
 template <class T> struct ScalarIn {
     const T* p;
     u64 n;
-    HK_FI explicit ScalarIn(const abi::ScalarHandle& h) : p(static_cast<const T*>(h.data)), n(h.samples) {}
-    HK_FI explicit ScalarIn(const abi::IntHandle& h) : p(static_cast<const T*>(h.data)), n(h.samples) {}
-    HK_FI Val<T> operator[](const SampleIndex& i) const { return Val<T>{ld_in(p + i.g)}; }
+    unsigned stage_off;
+    HK_FI explicit ScalarIn(const abi::ScalarHandle& h, unsigned off = 0)
+        : p(static_cast<const T*>(h.data)), n(h.samples), stage_off(off) {}
+    HK_FI explicit ScalarIn(const abi::IntHandle& h, unsigned off = 0)
+        : p(static_cast<const T*>(h.data)), n(h.samples), stage_off(off) {}
+    HK_FI Val<T> operator[](const SampleIndex& i) const {
+        if (i.st) return Val<T>{reinterpret_cast<const T*>(i.st + stage_off)[i.local]};
+        return Val<T>{ld_in(p + i.g)};
+    }
     HK_FI T cell() const { return ld_in(p); }
     HK_FI const T* data() const { return p; }
     HK_FI u64 samples() const { return n; }
@@ -75,10 +88,18 @@ template <class T, int N> struct VecIn {
     const T* p;
     u64 pitch;
     u64 n;
-    HK_FI explicit VecIn(const abi::GRefMirror& m)
-        : p(reinterpret_cast<const T*>(m.data_)), pitch(m.compStride_), n(m.samples_) {}
+    unsigned stage_off, comp_bytes;
+    HK_FI explicit VecIn(const abi::GRefMirror& m, unsigned off = 0, unsigned cb = 0)
+        : p(reinterpret_cast<const T*>(m.data_)), pitch(m.compStride_), n(m.samples_), stage_off(off),
+          comp_bytes(cb) {}
     HK_FI Item<T, N> operator[](const SampleIndex& i) const {
         Item<T, N> r;
+        if (i.st) {
+#pragma unroll
+            for (int k = 0; k < N; ++k)
+                r.v[k] = reinterpret_cast<const T*>(i.st + stage_off + static_cast<unsigned>(k) * comp_bytes)[i.local];
+            return r;
+        }
 #pragma unroll
         for (int k = 0; k < N; ++k) r.v[k] = ld_in(p + static_cast<u64>(k) * pitch + i.g);
         return r;
@@ -91,10 +112,21 @@ template <class T, int R, int C> struct MatIn {
     const T* p;
     u64 pitch;
     u64 n;
-    HK_FI explicit MatIn(const abi::GRefMirror& m)
-        : p(reinterpret_cast<const T*>(m.data_)), pitch(m.compStride_), n(m.samples_) {}
+    unsigned stage_off, comp_bytes;
+    HK_FI explicit MatIn(const abi::GRefMirror& m, unsigned off = 0, unsigned cb = 0)
+        : p(reinterpret_cast<const T*>(m.data_)), pitch(m.compStride_), n(m.samples_), stage_off(off),
+          comp_bytes(cb) {}
     HK_FI Item<T, R, C> operator[](const SampleIndex& i) const {
         Item<T, R, C> a;
+        if (i.st) {
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+#pragma unroll
+                for (int c = 0; c < C; ++c)
+                    a.m[r][c] = reinterpret_cast<const T*>(
+                        i.st + stage_off + static_cast<unsigned>(r * C + c) * comp_bytes)[i.local];
+            return a;
+        }
 #pragma unroll
         for (int r = 0; r < R; ++r)
 #pragma unroll

@@ -218,6 +218,22 @@ void hkb_library_free(hkb_library* lib) {
     delete lib;
 }
 
+int hkb_library_errors(hkb_library* lib, unsigned* flags, int clear) {
+    if (lib == nullptr || flags == nullptr) return fail(HKB_ERR_ARGUMENT, "hkb_library_errors: null argument");
+    *flags = 0;
+    DeviceScope scope(lib->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "selecting the device");
+    void* dptr = nullptr;
+    size_t bytes = 0;
+    if (cudaLibraryGetGlobal(&dptr, &bytes, lib->lib, "hk_error_flags") != cudaSuccess || bytes != sizeof(unsigned)) {
+        cudaGetLastError();
+        return HKB_OK;
+    }
+    HKB_CUDA(cudaMemcpy(flags, dptr, sizeof(unsigned), cudaMemcpyDeviceToHost), "reading hk_error_flags");
+    if (clear) HKB_CUDA(cudaMemset(dptr, 0, sizeof(unsigned)), "clearing hk_error_flags");
+    return HKB_OK;
+}
+
 int hkb_library_entry(hkb_library* lib, const char* name, hkb_entry** out) {
     if (lib == nullptr || name == nullptr || out == nullptr)
         return fail(HKB_ERR_ARGUMENT, "hkb_library_entry: null argument");

@@ -20,7 +20,7 @@ import re
 from dataclasses import dataclass, field
 
 from ..errors import HawkError
-from .wrapper import B200, sample_sum_store
+from .wrapper import B200, StagePlan, lane_frame_staged, sample_sum_store
 from .writer import B200_WRITER, body_text
 
 #: Scalar modes the b200 target builds: the reference's float64 and float32
@@ -70,8 +70,10 @@ def _refuse(name: str, walk) -> None:
             raise HawkError(f"{name!r}: slot {slot!r} has role {role!r}, which the b200 target does not build")
 
 
-def render_unit(kernel, name: str | None = None, mode: str = "float64") -> Unit:
-    """The b200 unit of a traced kernel (``hawk.Kernel``) in scalar mode ``mode``."""
+def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: bool = True) -> Unit:
+    """The b200 unit of a traced kernel (``hawk.Kernel``) in scalar mode ``mode``;
+    ``staged`` streams its inputs through shared-memory stages filled by the
+    TMA unit (hk/stage.cuh) where the stage plan fits."""
     from hawk.ir.nodes import sample_sums
     from hawk.emit.render import render_body
     from hawk.emit.spelling import element_spelling
@@ -91,13 +93,28 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64") -> Unit:
         raise HawkError(f"{name!r}: one kernel reduces over samples with one op (sum, max or min)")
     wrapper = B200
     smem = 0
+    elem_bytes = 8 if mode == "float64" else 4
     if sums:
         elem = element_spelling(sums[0].ttype.dtype)
-        opened, closed = wrapper.sample_sum_frame(len(sums), elem, sample_sum_store(sums), sums[0].op)
+        plan = StagePlan(walk, elem_bytes, 256 * wrapper.fold_rows(len(sums))) if staged else None
+        if plan is not None and plan.enabled:
+            opened, closed = wrapper.sample_sum_frame_staged(plan, len(sums), elem, sample_sum_store(sums),
+                                                             sums[0].op)
+            smem = plan.smem_bytes
+        else:
+            plan = None
+            opened, closed = wrapper.sample_sum_frame(len(sums), elem, sample_sum_store(sums), sums[0].op)
         loop = [opened, body, closed]
         frame = "row"
     else:
-        loop = [wrapper.index_prologue(), body, wrapper.index_epilogue()]
+        plan = StagePlan(walk, elem_bytes, 256) if staged else None
+        if plan is not None and plan.enabled:
+            opened, closed = lane_frame_staged(plan)
+            loop = [opened, body, closed]
+            smem = plan.smem_bytes
+        else:
+            plan = None
+            loop = [wrapper.index_prologue(), body, wrapper.index_epilogue()]
         frame = "lane"
     parts = [
         f"// hawk_b200 unit {name!r} (scalar mode {mode}), sm_100a.",
@@ -112,7 +129,7 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64") -> Unit:
         "",
         wrapper.entry_signature(walk, name),
         "{",
-        wrapper.unpack(walk),
+        wrapper.unpack(walk, plan),
         *loop,
         "}",
         "",
@@ -120,7 +137,9 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64") -> Unit:
     text = "\n".join(parts)
     records = tuple((s.name, s.op, s.companion.name if s.op == "sum" else None) for s in sums)
     return Unit(name=name, mode=mode, text=text, body=body, frame=frame, sums=records,
-                digest=hashlib.sha256(text.encode()).hexdigest(), notes={"dynamic_smem": smem})
+                digest=hashlib.sha256(text.encode()).hexdigest(),
+                notes={"dynamic_smem": smem, "staged": plan is not None,
+                       "stages": plan.stages if plan is not None else 0})
 
 
 _IDENT = re.compile(r"[A-Za-z_][A-Za-z0-9_]*")

@@ -53,8 +53,9 @@ def param_type(role: str, ttype) -> str:
     return f"hk::abi::{shape}"
 
 
-def view_decl(role: str, name: str, ttype) -> list:
-    """The unpack lines of one slot: its view (or by-value local)."""
+def view_decl(role: str, name: str, ttype, stage=None) -> list:
+    """The unpack lines of one slot: its view (or by-value local).  ``stage`` is
+    ``(offset, component bytes)`` of a staged input in its CTA's stage."""
     sp = _spelling()
     ident = sp.binding_name(role, name)
     src = sp.param_name(role, name)
@@ -71,7 +72,10 @@ def view_decl(role: str, name: str, ttype) -> list:
             view = f"hk::MatIn<{elem}, {shape[0]}, {shape[1]}>"
         else:
             raise HawkError(f"slot {name!r}: a rank-{len(shape)} input plane is not built on the b200 target")
-        return [f"    const {view} {ident}({src});", f"    (void){ident};"]
+        args = src
+        if stage is not None:
+            args += f", {stage[0]}u" + (f", {stage[1]}u" if shape else "")
+        return [f"    const {view} {ident}({args});", f"    (void){ident};"]
     if role in _SINK_ROLES:
         if len(shape) == 0:
             view = f"hk::ScalarOut<{elem}>"
@@ -118,14 +122,16 @@ class B200Wrapper:
     def index_epilogue(self) -> str:
         return "    }"
 
-    def unpack(self, walk) -> str:
+    def unpack(self, walk, plan: "StagePlan | None" = None) -> str:
         """Every slot's view, in ``arg_spec`` order; a promoted Param's one-cell
-        plane is read once, ahead of the loop (hawk/emit/wrapper.py:1599-1605)."""
+        plane is read once, ahead of the loop (hawk/emit/wrapper.py:1599-1605).
+        With a stage plan, each staged input knows its place in the stage."""
         sp = _spelling()
         lines = []
         for role, name in walk.arg_spec:
             ttype = walk.slot_types[(role, name)]
-            lines += view_decl(role, name, ttype)
+            stage = plan.offsets.get((role, name)) if plan is not None and plan.enabled else None
+            lines += view_decl(role, name, ttype, stage)
             if role == "lookup" and name in walk.param_planes:
                 cell = sp.param_cell_binding(name)
                 lines += [f"    const auto {cell} = {sp.binding_name(role, name)}.cell();",
@@ -181,11 +187,180 @@ class B200Wrapper:
             "    }")
         return opened, closed
 
+    def sample_sum_frame_staged(self, plan: StagePlan, width: int, elem: str, store: str,
+                                op: str = "sum") -> tuple:
+        """The row frame over tiles of 8 warps x K rows staged through shared
+        memory: warp w of the CTA takes rows [w K, (w + 1) K) of each tile."""
+        code = _OP_CODE[op]
+        k = self.fold_rows(width)
+        span = 256 * k
+        opened = "\n".join([
+            "    const long long hawk_rows = (count + 31) >> 5;",
+            plan.setup_lines(f"(hawk_rows + {8 * k - 1}) / {8 * k}", f"count / {span}",
+                             f"(static_cast<long long>(blockIdx.x) + hk_jj * gridDim.x) * {span}"),
+            plan.loop_head(),
+            f"        const long long hawk_r0 = hk_t * {8 * k} + static_cast<long long>(threadIdx.x >> 5) * {k};",
+            f"        {elem} hawk_terms[{k * width}];",
+            "#pragma unroll",
+            f"        for (int hawk_k = 0; hawk_k < {k * width}; ++hawk_k) hawk_terms[hawk_k] = "
+            f"hk::ss::identity<{elem}>({code});",
+            "#pragma unroll",
+            f"        for (int hawk_q = 0; hawk_q < {k}; ++hawk_q) {{",
+            f"        {elem}* const hawk_ss = hawk_terms + hawk_q * {width};",
+            "        const long long hawk_flat = ((hawk_r0 + hawk_q) << 5) + static_cast<long long>(threadIdx.x & 31u);",
+            "        if (hawk_flat < count) {",
+            "        const long long hawk_i = base + hawk_flat;",
+            f"        const hk::SampleIndex i{{hawk_i, hk_st, static_cast<int>((((threadIdx.x >> 5) * {k} + hawk_q) << 5) "
+            "+ (threadIdx.x & 31u))};",
+            "        (void)hawk_i;",
+            "        (void)nSamples;",
+        ])
+        closed = "\n".join([
+            "        }",
+            "        }",
+            "        if (hawk_r0 < hawk_rows) {",
+            store.replace("__K__", str(k)).replace("__W__", str(width)),
+            f"        hk::ss::rows_reduce<{k}, {width}, {code}>(hawk_terms, hawk_ss_store);",
+            "        }",
+            plan.loop_tail(),
+        ])
+        return opened, closed
+
     def dispatch(self, kind_spelling, branch_spellings, policy, **kw):
         """The per-node ``predicated``/``switch`` text: the reference's own,
         identical on every target (hawk/emit/wrapper.py:276-281)."""
         from hawk.emit.dispatch import render_dispatch_rank0
         return render_dispatch_rank0(kind_spelling, branch_spellings, policy, **kw)
+
+
+#: Shared memory the stages of one CTA may take (the buffers; barriers aside).
+STAGE_BUDGET = 96 * 1024
+#: Largest stage set a CTA may take at all (two stages of a wide matrix plane).
+STAGE_MAX = 200 * 1024
+
+
+class StagePlan:
+    """Which input components a CTA stages, where, and in how many stages.
+
+    Staged are the per-sample inputs (``vec_in``, ``mat_in``, ``per_sample``),
+    each component one contiguous run of ``tile`` samples per tile.  ``stages``
+    is as many as fit STAGE_BUDGET, at least 2 and at most 4; a kernel whose two
+    stages would pass STAGE_MAX is not staged."""
+
+    def __init__(self, walk, elem_bytes: int, tile: int) -> None:
+        sp = _spelling()
+        self.tile = tile
+        self.comp_bytes = tile * elem_bytes
+        self.elem_bytes = elem_bytes
+        self.views = []          # (binding, ncomps, rank)
+        offset = 0
+        self.offsets = {}
+        for role, name in walk.arg_spec:
+            if role not in ("vec_in", "mat_in", "per_sample"):
+                continue
+            shape = tuple(int(e) for e in walk.slot_types[(role, name)].shape)
+            ncomp = 1
+            for e in shape:
+                ncomp *= e
+            binding = sp.binding_name(role, name)
+            self.views.append((binding, ncomp, len(shape)))
+            self.offsets[(role, name)] = (offset, self.comp_bytes)
+            offset += ncomp * self.comp_bytes
+        self.tx_bytes = offset
+        self.stage_bytes = -(-offset // 128) * 128
+        fit = STAGE_BUDGET // self.stage_bytes if self.stage_bytes else 0
+        self.stages = max(2, min(4, fit))
+        self.enabled = bool(self.views) and self.stages * self.stage_bytes <= STAGE_MAX
+
+    @property
+    def smem_bytes(self) -> int:
+        return 128 + self.stages * self.stage_bytes if self.enabled else 0
+
+    def setup_lines(self, tiles: str, full_tiles: str, first_of: str) -> str:
+        """The pipe, the alignment test, the per-CTA tile counts and the
+        copies of one tile (``hk_issue``), in the entry before its loop."""
+        checks = []
+        copies = []
+        for binding, ncomp, rank in self.views:
+            offset = self.offsets_by_binding[binding]
+            pitch = f"{binding}.pitch * sizeof(*{binding}.data())" if rank else "0ull"
+            checks.append(f"hk::stage::aligned({binding}.data(), {pitch}, base * "
+                          f"static_cast<long long>(sizeof(*{binding}.data())))")
+            for k in range(ncomp):
+                src = (f"{binding}.data() + {k}ull * {binding}.pitch + base + hk_first" if rank
+                       else f"{binding}.data() + base + hk_first")
+                copies.append(f"        hk::stage::copy(hk_to + {offset + k * self.comp_bytes}u, {src}, "
+                              f"{self.comp_bytes}u, hk_bar);")
+        return "\n".join([
+            "    extern __shared__ __align__(128) unsigned char hk_smem[];",
+            f"    hk::stage::Pipe<{self.stages}> hk_pipe(hk_smem, {self.stage_bytes}u, {self.tx_bytes}u);",
+            "    const bool hk_aligned = " + " && ".join(checks) + ";",
+            f"    const long long hk_tiles = {tiles};",
+            "    const long long hk_mine = hk_tiles > static_cast<long long>(blockIdx.x)"
+            " ? (hk_tiles - 1 - static_cast<long long>(blockIdx.x)) / gridDim.x + 1 : 0;",
+            f"    const long long hk_full = {full_tiles};",
+            "    const long long hk_staged = (!hk_aligned || hk_full <= static_cast<long long>(blockIdx.x)) ? 0"
+            " : (hk_full - 1 - static_cast<long long>(blockIdx.x)) / gridDim.x + 1;",
+            "    auto hk_issue = [&](long long hk_jj, unsigned char* hk_to, unsigned long long* hk_bar) {",
+            f"        const long long hk_first = {first_of};",
+            *copies,
+            "    };",
+            "    hk_pipe.setup(8u);",
+            "    bool hk_ok = true;",
+            "    if (threadIdx.x == 0)",
+            f"        for (long long hk_jj = 0; hk_jj < {self.stages} && hk_jj < hk_staged && hk_ok; ++hk_jj)",
+            "            hk_ok = hk_pipe.fill(hk_jj, [&](unsigned char* a, unsigned long long* b) { hk_issue(hk_jj, a, b); });",
+            "    hk_ok = __shfl_sync(0xffffffffu, hk_ok, 0);",
+        ])
+
+    @property
+    def offsets_by_binding(self) -> dict:
+        sp = _spelling()
+        return {sp.binding_name(r, n): off for (r, n), (off, _cb) in self.offsets.items()}
+
+    def loop_head(self) -> str:
+        return "\n".join([
+            "    for (long long hk_j = 0; hk_j < hk_mine && hk_ok; ++hk_j) {",
+            "        const long long hk_t = static_cast<long long>(blockIdx.x) + hk_j * gridDim.x;",
+            "        const bool hk_use = hk_j < hk_staged;",
+            "        const unsigned char* hk_st = nullptr;",
+            "        if (hk_use) {",
+            "            const unsigned char* hk_got = hk_pipe.acquire(hk_j);",
+            "            if (!__all_sync(0xffffffffu, hk_got != nullptr)) break;",
+            "            hk_st = hk_got;",
+            "        }",
+        ])
+
+    def loop_tail(self) -> str:
+        return "\n".join([
+            "        if (hk_use) {",
+            "            hk_pipe.release(hk_j);",
+            f"            if (threadIdx.x == 0 && hk_j + {self.stages} < hk_staged)",
+            f"                hk_ok = hk_pipe.fill(hk_j + {self.stages}, [&](unsigned char* a, unsigned long long* b) "
+            f"{{ hk_issue(hk_j + {self.stages}, a, b); }});",
+            "            hk_ok = __shfl_sync(0xffffffffu, hk_ok, 0);",
+            "        }",
+            "    }",
+            "    if (threadIdx.x == 0) hk_pipe.drain();",
+        ])
+
+
+def lane_frame_staged(plan: StagePlan) -> tuple:
+    """The lane frame over 256-sample tiles staged through shared memory:
+    thread t takes sample t of each of its CTA's tiles."""
+    opened = "\n".join([
+        plan.setup_lines("(count + 255) >> 8", "count >> 8",
+                         "(static_cast<long long>(blockIdx.x) + hk_jj * gridDim.x) << 8"),
+        plan.loop_head(),
+        "        const long long hawk_flat = (hk_t << 8) + static_cast<long long>(threadIdx.x);",
+        "        if (hawk_flat < count) {",
+        "        const long long hawk_i = base + hawk_flat;",
+        "        const hk::SampleIndex i{hawk_i, hk_st, static_cast<int>(threadIdx.x)};",
+        "        (void)hawk_i;",
+        "        (void)nSamples;",
+    ])
+    closed = "\n".join(["        }", plan.loop_tail()])
+    return opened, closed
 
 
 def sample_sum_store(sums) -> str:

@@ -78,6 +78,13 @@ int hkb_library_load(const void* image, size_t size, int device, hkb_library** o
 int hkb_library_load_file(const char* path, int device, hkb_library** out);
 void hkb_library_free(hkb_library* lib);
 
+/* The unit's error word (0 when every bounded wait of its entries completed;
+ * bit 1: a staged tile did not arrive in time, 2: a stage was not released in
+ * time, 4: copies were still in flight when a CTA gave up), read after the
+ * launches it covers have completed; `clear` resets it.  A unit without the
+ * word reads 0.  The reference's host target has no device waits to report. */
+int hkb_library_errors(hkb_library* lib, unsigned* flags, int clear);
+
 /* HostLibrary.entry(name) (src/hawk_core.cpp:663-667): the entry `name`. */
 int hkb_library_entry(hkb_library* lib, const char* name, hkb_entry** out);
 
