@@ -1,0 +1,94 @@
+"""Cells over samples sharded across GPUs, one process per GPU over NCCL.
+
+Each rank binds its contiguous shard (``sharded.shard_range``), writes its
+32-sample rows, folds them into leaf partials, all-gathers the partials and
+runs the same pairwise tree; every rank's Param gradients must be
+bit-identical to the oracle's finish over all samples (hawk/_cells.py:94-119
+over the unsharded rows).  Skipped with fewer GPUs than ranks.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import REPO
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+BUNDLES = REPO / "hawk_b200" / "bundles"
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, n, queue):
+    import torch.distributed as dist
+
+    from hawk_b200 import runtime, sharded, workloads
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        w = workloads.poly_loss(n, seed=n)
+        base, count = sharded.shard_range(n, world, rank)
+
+        def dev(a):
+            return torch.as_tensor(np.ascontiguousarray(a), device=f"cuda:{rank}")
+
+        sl = slice(base, base + count)
+        cells = {k: torch.full((1,), float("nan"), dtype=torch.float64, device=f"cuda:{rank}")
+                 for k in ("bar_a", "bar_b", "bar_c")}
+        abc = {k: dev(np.array([w[k]])) for k in ("a", "b", "c")}
+        vjp = runtime.load(BUNDLES, "poly_loss_vjp", "float64", rank)
+        sharded.run_cells(vjp, x=dev(w["x"][sl]), t=dev(w["t"][sl]), bar_r=dev(w["bar_r"][sl]), **abc, **cells)
+        torch.cuda.synchronize(rank)
+        queue.put((rank, base, count, [float(cells[k].cpu()[0]) for k in ("bar_a", "bar_b", "bar_c")]))
+    finally:
+        dist.destroy_process_group()
+
+
+def _worlds():
+    count = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    return [w for w in (2, 4, 8) if w <= max(count, 2)]
+
+
+@pytest.mark.parametrize("world", _worlds())
+def test_sharded_param_gradients_bit_identical_to_one_device(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs, {torch.cuda.device_count()} visible")
+    import torch.multiprocessing as mp
+
+    from hawk_b200 import sharded, workloads
+
+    # every rank holds at least one leaf; the last shard is ragged
+    n = 2 * world * sharded.LEAF_SAMPLES - 1000
+    w = workloads.poly_loss(n, seed=n)
+    want, _rows = oracle.poly_loss_vjp(w["x"], w["t"], w["bar_r"], w["a"], w["b"], w["c"])
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, n, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [queue.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    results.sort()
+    assert sum(r[2] for r in results) == n
+    for rank, _base, count, got in results:
+        assert count > 0
+        assert got == [float(v) for v in want], (rank, got, want)
