@@ -27,12 +27,17 @@ enum Op { kSum = 0, kMax = 1, kMin = 2 };
 
 template <class T> HK_HD bool finite(T x) { return (x - x) == (x - x); }
 
-// Exact residual of s == a + b (|a| >= |b| ordering), +0 for a zero residual.
+// Exact residual a + b - s of s == fl(a + b), +0 for a zero residual.  The
+// reference orders the operands by magnitude and takes Fast2Sum's
+// small - (s - big); Knuth's 2Sum below needs no compare or select and yields
+// the same exact residual for all finite a, b whose sum s does not overflow
+// (Knuth, TAOCP vol. 2, 4.2.2 Theorem B; no intermediate of 2Sum overflows
+// unless s does: Boldo, Graillat and Muller, ACM TOMS 44(1), 2017).  Where s
+// is not finite the residual is discarded by every caller (the node's
+// compensation becomes 0).
 template <class T> HK_HD T two_sum_err(T a, T b, T s) {
-    const bool a_big = (a < T(0) ? -a : a) >= (b < T(0) ? -b : b);
-    const T big = a_big ? a : b;
-    const T small = a_big ? b : a;
-    return (small - (s - big)) + T(0);
+    const T bb = s - a;
+    return ((a - (s - bb)) + (b - bb)) + T(0);
 }
 
 template <class T> HK_HD T extreme(int op, T a, T b) {
@@ -116,20 +121,29 @@ constexpr int kLeaf = kSlots * kTerms;   // rows per leaf
 // compute the same node without caring which holds the lower lane's value; a
 // max/min node takes the lower lane's value first.  A lower lane's extra slot
 // (M odd) is padding that only ever meets the same padding on later partners.
-template <int M, int OP, class T>
+// FIRST (the round across bit 4): every compensation is still +0, so a sum
+// node's (c + c2) + err is err exactly (err is never -0) and no compensation
+// travels.
+template <int M, int OP, bool FIRST = false, class T>
 __device__ __forceinline__ void halve(T* h, T* c, int off, bool upper) {
     constexpr int LO = M / 2, UP = M - M / 2;
     const T pad = identity<T>(OP);
 #pragma unroll
     for (int j = 0; j < UP; ++j) {
         const T lo_h = j < LO ? h[j] : pad;
-        const T lo_c = j < LO ? c[j] : T(0);
         const T kh = upper ? h[LO + j] : lo_h;     // the column this lane keeps
-        const T kc = upper ? c[LO + j] : lo_c;
         const T gh = upper ? lo_h : h[LO + j];     // the one it gives away
-        const T gc = upper ? lo_c : c[LO + j];
         const T rh = __shfl_xor_sync(0xffffffffu, gh, off);
-        const T rc = __shfl_xor_sync(0xffffffffu, gc, off);
+        if constexpr (OP == kSum && FIRST) {
+            const T t = kh + rh;
+            c[j] = two_sum_err(kh, rh, t);
+            h[j] = t;
+            continue;
+        }
+        const T lo_c = j < LO ? c[j] : T(0);
+        const T kc = upper ? c[LO + j] : lo_c;
+        const T gc = upper ? lo_c : c[LO + j];
+        const T rc = OP == kSum ? __shfl_xor_sync(0xffffffffu, gc, off) : T(0);
         T s = kh, sc = kc;
         if constexpr (OP == kSum) {
             pair_combine_unchecked<OP>(s, sc, rh, rc);
@@ -157,7 +171,7 @@ __device__ __forceinline__ void rows_reduce(T (&h)[K * W], Store&& store) {
 #pragma unroll
     for (int k = 0; k < N; ++k) c[k] = T(0);
     const unsigned lane = threadIdx.x & 31u;
-    halve<N, OP>(h, c, 16, (lane & 16u) != 0u);
+    halve<N, OP, true>(h, c, 16, (lane & 16u) != 0u);
     halve<M2, OP>(h, c, 8, (lane & 8u) != 0u);
     halve<M3, OP>(h, c, 4, (lane & 4u) != 0u);
     halve<M4, OP>(h, c, 2, (lane & 2u) != 0u);

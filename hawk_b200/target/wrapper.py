@@ -141,9 +141,10 @@ class B200Wrapper:
     def fold_rows(self, width: int) -> int:
         """Rows one warp folds per trip: the largest power of two K with
         K * width <= 32 butterfly columns (hk::ss::rows_reduce).  Measured on
-        the B200 for the 3-column Param-gradient VJP at 2^26 samples: K = 2, 4,
-        8, 16 take 0.58, 0.57, 0.36, 0.53 ms; a shared-memory variant in which
-        each lane evaluates one whole (row, column) tree took 0.375 ms."""
+        the B200 for the 3-column Param-gradient VJP at 2^26 samples: K = 4,
+        8, 16 take 0.429, 0.283, 0.399 ms; a shared-memory variant in which
+        each lane evaluates one whole (row, column) tree took 0.375 ms, and
+        lane-permuted rows (select-free row rounds, 8 rows per load) 0.387 ms."""
         k = 1
         while k < 32 and 2 * k * width <= 32:
             k *= 2
