@@ -10,16 +10,17 @@
 // iteration count is an int32 output plane), so a last-bit difference from
 // glibc can change an integer result.  They are therefore computed here to
 // double-double accuracy and rounded once, which gives the correctly rounded
-// result except with probability ~2^-40 per call; glibc's sin/cos are
+// result except with probability ~2^-45 per call; glibc's sin/cos are
 // correctly rounded on the same inputs except in rare cases.  Method:
 //   * Cody-Waite reduction x = k*pi/2 + r with pi/2 held as three doubles and
 //     every product formed exactly with an FMA (two-product),
-//   * the Taylor series of sin r and cos r, |r| <= pi/4, whose terms above
-//     r^13 (sin) / r^14 (cos) are summed in double and the rest in
-//     double-double (Dekker/Knuth two-sum and two-product),
+//   * Tang's table method on |r| <= pi/4: sin and cos of j/32 from a
+//     double-double table, short Taylor series of the remainder |d| <= 1/64
+//     (Dekker/Knuth two-sum and two-product for the double-double steps),
 //   * one final rounding of the double-double value.
-// The coefficients are exact reciprocals of factorials and pi/2 is computed
-// from Machin's formula (gen_sincos_consts.py).  Arguments beyond 2^20 in
+// The coefficients are exact reciprocals of factorials, the table entries
+// are sin/cos of exact rationals and pi/2 is computed from Machin's formula
+// (gen_sincos_consts.py).  Arguments beyond 2^20 in
 // magnitude, infinities and NaN take the platform's sin/cos.
 //
 // Every other function calls the CUDA math library directly.
@@ -103,75 +104,115 @@ HK_HD dd fact_inv(int n, double sign) {
     return dd{sign * inv_fact(n, 0), sign * inv_fact(n, 1)};
 }
 
-// sin r and cos r of the reduced argument r (|r| <= pi/4 + eps), both as
-// double-doubles; z = r*r is shared.
+// sin(j/32) and cos(j/32) for j = 0..26 as double-doubles {sin hi, sin lo,
+// cos hi, cos lo} (gen_sincos_consts.py: Taylor series of exact rationals).
+#if defined(__CUDACC__) || defined(__CUDACC_RTC__)
+static __device__ const double __align__(16) kSinCosTableDev[27][4] = {HK_SINCOS_TABLE_DATA};
+#endif
+#if !defined(__CUDACC_RTC__)
+alignas(16) static const double kSinCosTableHost[27][4] = {HK_SINCOS_TABLE_DATA};
+#endif
+
+HK_HD void sincos_row(int j, dd* sa, dd* ca) {
+#if defined(__CUDA_ARCH__)
+    const double2 lo = __ldg(reinterpret_cast<const double2*>(kSinCosTableDev[j]));
+    const double2 hi = __ldg(reinterpret_cast<const double2*>(kSinCosTableDev[j]) + 1);
+    *sa = dd{lo.x, lo.y};
+    *ca = dd{hi.x, hi.y};
+#else
+    *sa = dd{kSinCosTableHost[j][0], kSinCosTableHost[j][1]};
+    *ca = dd{kSinCosTableHost[j][2], kSinCosTableHost[j][3]};
+#endif
+}
+
+// a * b for double-doubles, unnormalised: |l| may reach a few ulp(h)/2, which
+// the sums below absorb (relative error about 2^-104).
+HK_HD dd dd_mul_loose(dd a, dd b) {
+    const double p = a.h * b.h;
+    double e = fma_(a.h, b.h, -p);
+    e = fma_(a.h, b.l, e);
+    e = fma_(a.l, b.h, e);
+    return dd{p, e};
+}
+
+// a + b where |b.h| <= |a.h| / 2 (or a.h == 0): no cancellation of the high parts.
+HK_HD dd dd_add_small(dd a, dd b) {
+    const dd s = fast_two_sum(a.h, b.h);
+    return dd{s.h, s.l + (a.l + b.l)};
+}
+
+// sin r and cos r of the reduced argument r (|r| <= pi/4 + eps) as
+// double-doubles, by Tang's table method: r = a + d with a = j/32 from the
+// table and |d| <= 1/64, then
+//   sin r = sin a + (sin a (cos d - 1) + cos a sin d),
+//   cos r = cos a + (cos a (cos d - 1) - sin a sin d),
+//   sin d = d + d z S(z),  cos d - 1 = z C(z),  z = d^2,
+// with the Taylor series of S and C cut where the next term is below 2^-100
+// of the result.  The three leading coefficients of S and C are carried in
+// double-double; the rest, below 2^-17 of the part they are added to, in
+// double.  Relative error below 2^-99 (2^-99.8 worst in 4M arguments checked
+// against binary128 sin/cos).
 HK_HD void sincos_reduced(dd r, dd* s, dd* c) {
-    const dd z = dd_mul(r, r);
-    // sin: r * sum_{n=0..13} (-1)^n z^n / (2n+1)!.  Terms n >= 7 (below 2^-45
-    // of the result) are summed in double, the rest in double-double.
-    double ts = -inv_fact(27, 0);
-#pragma unroll
-    for (int n = 12; n >= 7; --n)
-        ts = fma_(ts, z.h, ((n & 1) ? -1.0 : 1.0) * inv_fact(2 * n + 1, 0));
-    dd ps = two_prod(ts, z.h);
-#pragma unroll
-    for (int n = 6; n >= 0; --n) {
-        ps = dd_add(ps, fact_inv(2 * n + 1, (n & 1) ? -1.0 : 1.0));
-        if (n > 0) ps = dd_mul(ps, z);
-    }
-    *s = dd_mul(ps, r);
-    // cos: sum_{n=0..14} (-1)^n z^n / (2n)!.  Terms n >= 8 in double.
-    double tc = inv_fact(28, 0);
-#pragma unroll
-    for (int n = 13; n >= 8; --n)
-        tc = fma_(tc, z.h, ((n & 1) ? -1.0 : 1.0) * inv_fact(2 * n, 0));
-    dd pc = two_prod(tc, z.h);
-#pragma unroll
-    for (int n = 7; n >= 0; --n) {
-        pc = dd_add(pc, fact_inv(2 * n, (n & 1) ? -1.0 : 1.0));
-        if (n > 0) pc = dd_mul(pc, z);
-    }
-    *c = pc;
+    const double jd = rint_(r.h * 32.0);
+    const dd d = fast_two_sum(r.h - jd * 0.03125, r.l);    // r.h - j/32 is exact
+    const double ah = fabs_(jd);
+    dd sa, ca;
+    sincos_row(static_cast<int>(ah), &sa, &ca);
+    if (jd < 0.0) sa = dd_neg(sa);
+    const dd z = dd_mul_loose(d, d);
+    // S(z) = -1/3! + z/5! - z^2/7! + z^3/9! - z^4/11!
+    const double s3 = fma_(-inv_fact(11, 0), z.h, inv_fact(9, 0));
+    const dd s2 = dd_add_small(fact_inv(7, -1.0), dd{z.h * s3, 0.0});
+    const dd s1 = dd_add_small(fact_inv(5, 1.0), dd_mul_loose(z, s2));
+    const dd sz = dd_add_small(fact_inv(3, -1.0), dd_mul_loose(z, s1));
+    // C(z) = -1/2! + z/4! - z^2/6! + z^3/8! - z^4/10!
+    const double c3 = fma_(-inv_fact(10, 0), z.h, inv_fact(8, 0));
+    const dd c2 = dd_add_small(fact_inv(6, -1.0), dd{z.h * c3, 0.0});
+    const dd c1 = dd_add_small(fact_inv(4, 1.0), dd_mul_loose(z, c2));
+    const dd cz = dd_add_small(fact_inv(2, -1.0), dd_mul_loose(z, c1));
+    const dd sd = dd_add_small(d, dd_mul_loose(d, dd_mul_loose(z, sz)));   // sin d
+    const dd cm = dd_mul_loose(z, cz);                                       // cos d - 1
+    const dd ts = dd_add(dd_mul_loose(sa, cm), dd_mul_loose(ca, sd));
+    const dd tc = dd_add(dd_mul_loose(ca, cm), dd_neg(dd_mul_loose(sa, sd)));
+    *s = dd_add(sa, ts);                     // sa == 0 (j == 0) leaves sd exactly
+    *c = dd_add(ca, tc);
 }
 
 // Largest |x| reduced here; beyond it the platform's functions are used.
 constexpr double kCrMax = 1048576.0;   // 2^20
 
-// sin x and cos x, each correctly rounded (see the file comment).
+// sin x and cos x, each correctly rounded (see the file comment).  The common
+// path is straight-line code, so a body that takes sin and cos of the same
+// argument evaluates it once; only arguments beyond 2^20, infinities and NaN
+// branch to the platform's functions at the end.
 HK_HD void sincos_cr(double x, double* sx, double* cx) {
     const double ax = fabs_(x);
-    if (!(ax <= kCrMax)) {                 // NaN, infinities, huge arguments
-        *sx = libm_sin(x);
-        *cx = libm_cos(x);
-        return;
-    }
-    if (ax < 0x1p-27) {                    // sin x = x, cos x = 1 after rounding
-        *sx = x;
-        *cx = 1.0;
-        return;
-    }
-    const double kd = rint_(x * kTwoOverPi);
-    dd r;
-    if (kd == 0.0) {
-        r = dd{x, 0.0};
-    } else {
-        const dd p = two_prod(kd, kPio2Hi);
-        const double a = x - p.h;          // exact: x and p.h are within a factor 2
-        r = two_sum(a, -p.l);
-        r = dd_add_accurate(r, dd_neg(two_prod(kd, kPio2Mid)));
-        r = dd_add_accurate(r, dd{-kd * kPio2Lo, 0.0});
-    }
+    const bool in_range = ax <= kCrMax;      // false for NaN and infinities
+    const double xr = in_range ? x : 0.0;
+    const double kd = rint_(xr * kTwoOverPi);
+    const dd p = two_prod(kd, kPio2Hi);
+    const double a = xr - p.h;               // exact: x and p.h are within a factor 2 (or kd == 0)
+    dd r = two_sum(a, -p.l);
+    r = dd_add_accurate(r, dd_neg(two_prod(kd, kPio2Mid)));
+    r = dd_add_accurate(r, dd{-kd * kPio2Lo, 0.0});
     dd s, c;
     sincos_reduced(r, &s, &c);
-    const long long q = static_cast<long long>(kd) & 3;
+    const int q = static_cast<int>(static_cast<long long>(kd) & 3);
     const double sr = s.h + s.l;
     const double cr = c.h + c.l;
-    switch (q) {
-        case 0: *sx = sr; *cx = cr; break;
-        case 1: *sx = cr; *cx = -sr; break;
-        case 2: *sx = -sr; *cx = -cr; break;
-        default: *sx = -cr; *cx = sr; break;
+    const double s1 = (q & 1) ? cr : sr;
+    const double c1 = (q & 1) ? sr : cr;
+    double so = (q & 2) ? -s1 : s1;
+    double co = ((q + 1) & 2) ? -c1 : c1;
+    const bool tiny = ax < 0x1p-27;          // sin x = x, cos x = 1 after rounding
+    so = tiny ? x : so;
+    co = tiny ? 1.0 : co;
+    if (!in_range) {
+        so = libm_sin(x);
+        co = libm_cos(x);
     }
+    *sx = so;
+    *cx = co;
 }
 
 }  // namespace detail
