@@ -20,8 +20,9 @@
 //   * one final rounding of the double-double value.
 // The coefficients are exact reciprocals of factorials, the table entries
 // are sin/cos of exact rationals and pi/2 is computed from Machin's formula
-// (gen_sincos_consts.py).  Arguments beyond 2^20 in
-// magnitude, infinities and NaN take the platform's sin/cos.
+// (gen_sincos_consts.py).  Arguments beyond 2^20 in magnitude are reduced by
+// Payne and Hanek's method with the bits of 2/pi (also generated there);
+// infinities and NaN give NaN.
 //
 // Every other function calls the CUDA math library directly.
 #pragma once
@@ -39,14 +40,10 @@ namespace detail {
 HK_HD double fma_(double a, double b, double c) { return __fma_rn(a, b, c); }
 HK_HD double rint_(double x) { return ::rint(x); }
 HK_HD double fabs_(double x) { return ::fabs(x); }
-HK_HD double libm_sin(double x) { return ::sin(x); }
-HK_HD double libm_cos(double x) { return ::cos(x); }
 #else
 HK_HD double fma_(double a, double b, double c) { return std::fma(a, b, c); }
 HK_HD double rint_(double x) { return std::rint(x); }
 HK_HD double fabs_(double x) { return std::fabs(x); }
-HK_HD double libm_sin(double x) { return std::sin(x); }
-HK_HD double libm_cos(double x) { return std::cos(x); }
 #endif
 
 // An unevaluated sum h + l with |l| <= ulp(h) / 2.
@@ -178,14 +175,139 @@ HK_HD void sincos_reduced(dd r, dd* s, dd* c) {
     *c = dd_add(ca, tc);
 }
 
-// Largest |x| reduced here; beyond it the platform's functions are used.
+// The 32-bit words of 2/pi, most significant first.
+#if defined(__CUDACC__) || defined(__CUDACC_RTC__)
+static __device__ const unsigned kTwoOverPiDev[40] = {HK_TWO_OVER_PI_WORDS};
+#endif
+#if !defined(__CUDACC_RTC__)
+static const unsigned kTwoOverPiHost[40] = {HK_TWO_OVER_PI_WORDS};
+#endif
+
+HK_HD unsigned two_over_pi_word(int i) {
+#if defined(__CUDA_ARCH__)
+    return __ldg(kTwoOverPiDev + i);
+#else
+    return kTwoOverPiHost[i];
+#endif
+}
+
+HK_HD unsigned long long bits_of(double x) {
+#if defined(__CUDA_ARCH__)
+    return static_cast<unsigned long long>(__double_as_longlong(x));
+#else
+    unsigned long long b;
+    __builtin_memcpy(&b, &x, sizeof b);
+    return b;
+#endif
+}
+
+HK_HD double from_bits(unsigned long long b) {
+#if defined(__CUDA_ARCH__)
+    return __longlong_as_double(static_cast<long long>(b));
+#else
+    double x;
+    __builtin_memcpy(&x, &b, sizeof x);
+    return x;
+#endif
+}
+
+HK_HD int clz64(unsigned long long v) {
+#if defined(__CUDA_ARCH__)
+    return __clzll(static_cast<long long>(v));
+#else
+    return v ? __builtin_clzll(v) : 64;
+#endif
+}
+
+HK_HD unsigned long long mul_hi64(unsigned long long a, unsigned long long b) {
+#if defined(__CUDA_ARCH__)
+    return __umul64hi(a, b);
+#else
+    return static_cast<unsigned long long>((static_cast<unsigned __int128>(a) * b) >> 64);
+#endif
+}
+
+// Bits [bit, bit + 64) of the 128-bit lo + hi 2^64 (0 <= bit < 64).
+HK_HD unsigned long long funnel64(unsigned long long lo, unsigned long long hi, int bit) {
+    return bit ? (lo >> bit) | (hi << (64 - bit)) : lo;
+}
+
+// Payne and Hanek's reduction of a finite ax >= 2^20: ax = (4n + q) pi/2 + r
+// with |r| <= pi/4, r as a double-double (relative error about 2^-104).
+// With ax = m 2^e (m < 2^53), y = ax 2/pi needs only the 8 words of 2/pi
+// from i0 = floor((e - 2) / 32): earlier words contribute multiples of 4 and
+// later ones less than 2^-165.  P = m * (those 256 bits) is exact in five
+// 64-bit limbs; its two bits at the binary point are the quadrant, the 192
+// bits below it the fraction, rounded to the nearest quadrant and multiplied
+// by pi/2.
+HK_HD void reduce_payne_hanek(double ax, int* quadrant, dd* r) {
+    typedef unsigned long long u64;
+    const u64 b = bits_of(ax);
+    const int e = static_cast<int>((b >> 52) & 0x7ff) - 1075;
+    const u64 m = (b & ((1ull << 52) - 1ull)) | (1ull << 52);
+    const int i0 = e >= 2 ? (e - 2) / 32 : 0;
+    u64 p[5];                                       // P, least significant limb first
+    u64 carry_hi = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {                   // limb k: words i0 + 7 - 2k (low), i0 + 6 - 2k (high)
+        const u64 w = (static_cast<u64>(two_over_pi_word(i0 + 6 - 2 * k)) << 32) |
+                      two_over_pi_word(i0 + 7 - 2 * k);
+        const u64 lo = m * w;
+        const u64 hi = mul_hi64(m, w);              // < 2^53
+        const u64 s = lo + carry_hi;
+        p[k] = s;
+        carry_hi = hi + (s < lo ? 1ull : 0ull);
+    }
+    p[4] = carry_hi;
+    // binary point at bit 32 (i0 + 8) - e, in (222, 288]; take bits [point - 192, point + 2)
+    const int sh = 32 * (i0 + 8) - e - 192;         // in (30, 96]
+    const bool up = sh >= 64;
+    const int bit = sh & 63;
+    const u64 f0 = funnel64(up ? p[1] : p[0], up ? p[2] : p[1], bit);
+    u64 f1 = funnel64(up ? p[2] : p[1], up ? p[3] : p[2], bit);
+    u64 f2 = funnel64(up ? p[3] : p[2], up ? p[4] : p[3], bit);
+    const u64 f3 = funnel64(up ? p[4] : p[3], up ? 0ull : p[4], bit);
+    int quad = static_cast<int>(f3 & 3ull);
+    u64 g0 = f0;
+    const bool upper = (f2 >> 63) != 0ull;          // fraction >= 1/2: round up a quadrant
+    if (upper) {                                     // |fraction - 1| = 2^192 - F
+        quad = (quad + 1) & 3;
+        g0 = ~f0 + 1ull;
+        f1 = ~f1 + (g0 == 0ull ? 1ull : 0ull);
+        f2 = ~f2 + ((g0 == 0ull && f1 == 0ull) ? 1ull : 0ull);
+    }
+    // normalise (the fraction of a double argument is above 2^-62, so f2 != 0)
+    const int lz = clz64(f2);
+    const u64 top = lz ? (f2 << lz) | (f1 >> (64 - lz)) : f2;
+    const u64 mid = lz ? (f1 << lz) | (g0 >> (64 - lz)) : f1;
+    const double scale = from_bits(static_cast<u64>(1023 - 53 - lz) << 52);   // 2^(-53 - lz)
+    const double fh = static_cast<double>(top >> 11) * scale;
+    const double fl = static_cast<double>(((top & 0x7ffull) << 42) | (mid >> 22)) * scale * 0x1p-53;
+    dd f = dd_mul(dd{fh, fl}, dd{kPio2Hi, kPio2Mid});
+    if (upper) f = dd_neg(f);
+    *quadrant = quad;
+    *r = f;
+}
+
+// Largest |x| reduced by Cody and Waite's three-part pi/2; beyond it
+// reduce_payne_hanek.
 constexpr double kCrMax = 1048576.0;   // 2^20
 
-// sin x and cos x, each correctly rounded (see the file comment).  The common
-// path is straight-line code, so a body that takes sin and cos of the same
-// argument evaluates it once; only arguments beyond 2^20, infinities and NaN
-// branch to the platform's functions at the end.
-HK_HD void sincos_cr(double x, double* sx, double* cx) {
+// The rounded sin and cos of r (double-double) in quadrant q.
+HK_HD void sincos_quadrant(dd r, int q, double* sx, double* cx) {
+    dd s, c;
+    sincos_reduced(r, &s, &c);
+    const double sr = s.h + s.l;
+    const double cr = c.h + c.l;
+    const double s1 = (q & 1) ? cr : sr;
+    const double c1 = (q & 1) ? sr : cr;
+    *sx = (q & 2) ? -s1 : s1;
+    *cx = ((q + 1) & 2) ? -c1 : c1;
+}
+
+// sin x and cos x, each correctly rounded (see the file comment); arguments
+// beyond 2^20, infinities and NaN branch at the end.
+HK_HD void sincos_eval(double x, double* sx, double* cx) {
     const double ax = fabs_(x);
     const bool in_range = ax <= kCrMax;      // false for NaN and infinities
     const double xr = in_range ? x : 0.0;
@@ -195,24 +317,57 @@ HK_HD void sincos_cr(double x, double* sx, double* cx) {
     dd r = two_sum(a, -p.l);
     r = dd_add_accurate(r, dd_neg(two_prod(kd, kPio2Mid)));
     r = dd_add_accurate(r, dd{-kd * kPio2Lo, 0.0});
-    dd s, c;
-    sincos_reduced(r, &s, &c);
-    const int q = static_cast<int>(static_cast<long long>(kd) & 3);
-    const double sr = s.h + s.l;
-    const double cr = c.h + c.l;
-    const double s1 = (q & 1) ? cr : sr;
-    const double c1 = (q & 1) ? sr : cr;
-    double so = (q & 2) ? -s1 : s1;
-    double co = ((q + 1) & 2) ? -c1 : c1;
+    double so, co;
+    sincos_quadrant(r, static_cast<int>(static_cast<long long>(kd) & 3), &so, &co);
     const bool tiny = ax < 0x1p-27;          // sin x = x, cos x = 1 after rounding
     so = tiny ? x : so;
     co = tiny ? 1.0 : co;
     if (!in_range) {
-        so = libm_sin(x);
-        co = libm_cos(x);
+        if (ax - ax == 0.0) {                // finite: Payne-Hanek, then the sign of x
+            int q;
+            dd rr;
+            reduce_payne_hanek(ax, &q, &rr);
+            if (x < 0.0) {
+                q = (4 - q) & 3;
+                rr = dd_neg(rr);
+            }
+            sincos_quadrant(rr, q, &so, &co);
+        } else {                             // NaN and infinities: NaN
+            so = x - x;
+            co = x - x;
+        }
     }
     *sx = so;
     *cx = co;
+}
+
+struct SinCos {
+    double s, c;
+};
+
+// The one evaluation of sincos_eval for an argument, out of line and marked
+// pure (it reads only the constant tables): a body that takes sin and cos of
+// the same argument calls it once (the compiler merges calls with equal
+// arguments), and the Payne-Hanek branch does not add to the registers of the
+// calling kernel.
+#if defined(__CUDA_ARCH__)
+__device__ __noinline__ __attribute__((pure)) SinCos sincos_pure(double x) {
+    SinCos r;
+    sincos_eval(x, &r.s, &r.c);
+    return r;
+}
+#else
+inline SinCos sincos_pure(double x) {
+    SinCos r;
+    sincos_eval(x, &r.s, &r.c);
+    return r;
+}
+#endif
+
+HK_HD void sincos_cr(double x, double* sx, double* cx) {
+    const SinCos r = sincos_pure(x);
+    *sx = r.s;
+    *cx = r.c;
 }
 
 }  // namespace detail

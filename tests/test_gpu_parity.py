@@ -199,6 +199,25 @@ def test_kepler_against_the_glibc_oracle():
     assert int((host(it) != wit).sum()) <= 2
 
 
+def test_kepler_beyond_two_to_the_twenty():
+    """Mean anomalies from 2^20 to 1e300 (sin/cos through the Payne-Hanek
+    reduction), infinities and NaN: bit-identical to the correctly rounded
+    oracle, iteration counts included."""
+    rng = np.random.default_rng(5)
+    # below 2^52 or so e*sin(E) still moves E, so the exact sin/cos bits show
+    M = np.concatenate([np.ldexp(rng.uniform(1, 2, 4000), rng.integers(20, 52, 4000)),
+                        np.ldexp(rng.uniform(1, 2, 1000), rng.integers(52, 997, 1000)),
+                        [1048576.0, 1048577.5, 6381956970095103.0 * 2.0 ** 797, 1e300, np.inf, -np.inf, np.nan]])
+    e = rng.uniform(0, 0.95, M.shape[0])
+    n = M.shape[0]
+    E, it = nan_like((n,)), torch.full((n,), -1, dtype=torch.int32, device="cuda")
+    runtime.run(runtime.load(BUNDLES, "kepler"), e=dev(e), M=dev(M), E=E, iters=it)
+    with oracle.math_mode(oracle.MATH_CR):
+        wE, wit = oracle.kepler(e, M)
+    np.testing.assert_array_equal(host(it), wit)
+    same(host(E), wE)
+
+
 def test_kepler_known_answer():
     E, it = nan_like((1,)), torch.full((1,), -1, dtype=torch.int32, device="cuda")
     runtime.run(runtime.load(BUNDLES, "kepler"), e=dev([0.5]), M=dev([1.0]), E=E, iters=it)
