@@ -11,11 +11,14 @@
 // glibc can change an integer result.  They are therefore computed here to
 // double-double accuracy and rounded once, which gives the correctly rounded
 // result except with probability ~2^-45 per call; glibc's sin/cos are
-// correctly rounded on the same inputs except in rare cases.  Method:
+// correctly rounded on the same inputs except in rare cases.  Ziv's strategy:
+// a cheap evaluation (sincos_fast_parts, error below 2^-65) is rounded when a
+// rounding test proves the result (all but ~0.08 % of arguments), else the
+// accurate one below runs.  Method of the accurate evaluation:
 //   * Cody-Waite reduction x = k*pi/2 + r with pi/2 held as three doubles and
 //     every product formed exactly with an FMA (two-product),
-//   * Tang's table method on |r| <= pi/4: sin and cos of j/32 from a
-//     double-double table, short Taylor series of the remainder |d| <= 1/64
+//   * Tang's table method on |r| <= pi/4: sin and cos of j/64 from a
+//     double-double table, short Taylor series of the remainder |d| <= 1/128
 //     (Dekker/Knuth two-sum and two-product for the double-double steps),
 //   * one final rounding of the double-double value.
 // The coefficients are exact reciprocals of factorials, the table entries
@@ -101,13 +104,13 @@ HK_HD dd fact_inv(int n, double sign) {
     return dd{sign * inv_fact(n, 0), sign * inv_fact(n, 1)};
 }
 
-// sin(j/32) and cos(j/32) for j = 0..26 as double-doubles {sin hi, sin lo,
+// sin(j/64) and cos(j/64) for j = 0..52 as double-doubles {sin hi, sin lo,
 // cos hi, cos lo} (gen_sincos_consts.py: Taylor series of exact rationals).
 #if defined(__CUDACC__) || defined(__CUDACC_RTC__)
-static __device__ const double __align__(16) kSinCosTableDev[27][4] = {HK_SINCOS_TABLE_DATA};
+static __device__ const double __align__(16) kSinCosTableDev[53][4] = {HK_SINCOS_TABLE_DATA};
 #endif
 #if !defined(__CUDACC_RTC__)
-alignas(16) static const double kSinCosTableHost[27][4] = {HK_SINCOS_TABLE_DATA};
+alignas(16) static const double kSinCosTableHost[53][4] = {HK_SINCOS_TABLE_DATA};
 #endif
 
 HK_HD void sincos_row(int j, dd* sa, dd* ca) {
@@ -139,19 +142,19 @@ HK_HD dd dd_add_small(dd a, dd b) {
 }
 
 // sin r and cos r of the reduced argument r (|r| <= pi/4 + eps) as
-// double-doubles, by Tang's table method: r = a + d with a = j/32 from the
-// table and |d| <= 1/64, then
+// double-doubles, by Tang's table method: r = a + d with a = j/64 from the
+// table and |d| <= 1/128, then
 //   sin r = sin a + (sin a (cos d - 1) + cos a sin d),
 //   cos r = cos a + (cos a (cos d - 1) - sin a sin d),
 //   sin d = d + d z S(z),  cos d - 1 = z C(z),  z = d^2,
 // with the Taylor series of S and C cut where the next term is below 2^-100
 // of the result.  The three leading coefficients of S and C are carried in
-// double-double; the rest, below 2^-17 of the part they are added to, in
-// double.  Relative error below 2^-99 (2^-99.8 worst in 4M arguments checked
-// against binary128 sin/cos).
+// double-double; the rest, below 2^-19 of the part they are added to, in
+// double.  Relative error below 2^-100 (2^-104.5 worst in 2 M arguments
+// checked against binary128 sin/cos).
 HK_HD void sincos_reduced(dd r, dd* s, dd* c) {
-    const double jd = rint_(r.h * 32.0);
-    const dd d = fast_two_sum(r.h - jd * 0.03125, r.l);    // r.h - j/32 is exact
+    const double jd = rint_(r.h * 64.0);
+    const dd d = fast_two_sum(r.h - jd * 0.015625, r.l);   // r.h - j/64 is exact
     const double ah = fabs_(jd);
     dd sa, ca;
     sincos_row(static_cast<int>(ah), &sa, &ca);
@@ -305,9 +308,77 @@ HK_HD void sincos_quadrant(dd r, int q, double* sx, double* cx) {
     *cx = ((q + 1) & 2) ? -c1 : c1;
 }
 
+// The cheap first try of Ziv's strategy: sin r and cos r for 2^-27 <= |x| <=
+// 2^20 with |r| >= 2^-20, each as h + l with |error| <= 2^-65 |h| (2^-67.3
+// worst in 3.8 M arguments against binary128; the error analysis bounds it
+// near 2^-66: the d^3 term, about 2^-23.6 of a result >= 2^-7, carries
+// three roundings of 2^-53); returns the
+// quadrant, or -1 where it does not apply.  The reduction uses pi/2 = C1 + C2
+// + C3 with C1 and C2 of 33 bits, so k C1 and k C2 are exact for |k| < 2^20
+// and x - k C1 is exact (Sterbenz); the evaluation is the table method of
+// sincos_reduced with only the products of the leading terms kept exactly.
+HK_HD int sincos_fast_parts(double x, dd* s, dd* c) {
+    const double ax = fabs_(x);
+    const double kd = rint_(x * kTwoOverPi);
+    const double a = x - kd * kPio2C1;                 // both steps exact
+    const dd s2 = two_sum(a, -(kd * kPio2C2));         // kd * C2 exact
+    const dd r = fast_two_sum(s2.h, s2.l - kd * kPio2C3);
+    if (!(ax <= kCrMax) || ax < 0x1p-27 || !(fabs_(r.h) >= 0x1p-20)) return -1;
+    const double jd = rint_(r.h * 64.0);
+    const double dh = r.h - jd * 0.015625;             // exact
+    const double dl = r.l;
+    dd sa, ca;
+    sincos_row(static_cast<int>(fabs_(jd)), &sa, &ca);
+    if (jd < 0.0) sa = dd_neg(sa);
+    const double z = dh * dh;
+    const double zl = fma_(dh, dh, -z);
+    // sin d = dh + sdl;  cos d - 1 = -z/2 + cml
+    const double sp = fma_(fma_(fma_(inv_fact(9, 0), z, -inv_fact(7, 0)), z, inv_fact(5, 0)), z, -inv_fact(3, 0));
+    const double sdl = fma_(dh * z, sp, dl - dl * z * 0.5);
+    const double cp = fma_(fma_(-inv_fact(10, 0), z, inv_fact(8, 0)), z, -inv_fact(6, 0));
+    const double cq = fma_(cp, z, inv_fact(4, 0));
+    const double cmh = -0.5 * z;
+    const double cml = fma_(z * z, cq, -0.5 * zl - dh * dl);
+    // sin r = sa + sa (cos d - 1) + ca sin d
+    const dd p1 = two_prod(ca.h, dh);
+    const dd p2 = two_prod(sa.h, cmh);
+    const dd u = fast_two_sum(sa.h, p1.h);             // |sa.h| >= sin(1/64) > |p1.h|, or sa.h == 0
+    const dd v = fast_two_sum(u.h, p2.h);
+    const double sl = (u.l + v.l) + (p1.l + p2.l) + (sa.l + sa.l * cmh) + (ca.h * sdl + ca.l * dh) + sa.h * cml;
+    // cos r = ca + ca (cos d - 1) - sa sin d
+    const dd p3 = two_prod(ca.h, cmh);
+    const dd p4 = two_prod(sa.h, dh);
+    const dd u2 = fast_two_sum(ca.h, p3.h);            // ca.h >= 0.69
+    const dd v2 = fast_two_sum(u2.h, -p4.h);
+    const double cl = (u2.l + v2.l) + (p3.l - p4.l) + (ca.l + ca.l * cmh) + (ca.h * cml - sa.h * sdl) - sa.l * dh;
+    *s = dd{v.h, sl};
+    *c = dd{v2.h, cl};
+    return static_cast<int>(static_cast<long long>(kd) & 3);
+}
+
+// h + l rounded, when every value within 2^-65 |h| of it rounds the same.
+HK_HD bool round_sure(dd v, double* out) {
+    const double e = 0x1p-65 * fabs_(v.h);
+    const double up = v.h + (v.l + e);
+    *out = v.h + v.l;
+    return up == v.h + (v.l - e) && up == *out;
+}
+
 // sin x and cos x, each correctly rounded (see the file comment); arguments
 // beyond 2^20, infinities and NaN branch at the end.
 HK_HD void sincos_eval(double x, double* sx, double* cx) {
+    {
+        dd fs, fc;
+        const int q = sincos_fast_parts(x, &fs, &fc);
+        double sr, cr;
+        if (q >= 0 && round_sure(fs, &sr) && round_sure(fc, &cr)) {
+            const double s1 = (q & 1) ? cr : sr;
+            const double c1 = (q & 1) ? sr : cr;
+            *sx = (q & 2) ? -s1 : s1;
+            *cx = ((q + 1) & 2) ? -c1 : c1;
+            return;
+        }
+    }
     const double ax = fabs_(x);
     const bool in_range = ax <= kCrMax;      // false for NaN and infinities
     const double xr = in_range ? x : 0.0;
