@@ -71,7 +71,7 @@ def build_cubins(force: bool = False) -> list:
 
     headers_mtime = max(p.stat().st_mtime for p in HEADERS)
     built = []
-    for unit in sorted(BUNDLES.glob("*.cu")):
+    for unit in sorted(BUNDLES.glob("*.cu")) + sorted((BUNDLES / "staged").glob("*.cu")):
         cubin = unit.with_suffix(".cubin")
         if (not force and cubin.exists()
                 and cubin.stat().st_mtime >= max(unit.stat().st_mtime, headers_mtime)):

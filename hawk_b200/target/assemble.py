@@ -70,10 +70,12 @@ def _refuse(name: str, walk) -> None:
             raise HawkError(f"{name!r}: slot {slot!r} has role {role!r}, which the b200 target does not build")
 
 
-def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: bool = True) -> Unit:
+def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: bool = True,
+                min_blocks: int | None = None) -> Unit:
     """The b200 unit of a traced kernel (``hawk.Kernel``) in scalar mode ``mode``;
     ``staged`` streams its inputs through shared-memory stages filled by the
-    TMA unit (hk/stage.cuh) where the stage plan fits."""
+    TMA unit (hk/stage.cuh) where the stage plan fits; ``min_blocks`` caps the
+    entry's registers so that many 256-thread blocks stay resident per SM."""
     from hawk.ir.nodes import sample_sums
     from hawk.emit.render import render_body
     from hawk.emit.spelling import element_spelling
@@ -127,7 +129,7 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
         "HK_SELF_CHECK_EXPORTS",
         *([f"HK_DYNAMIC_SMEM({smem})"] if smem else []),
         "",
-        wrapper.entry_signature(walk, name),
+        wrapper.entry_signature(walk, name, min_blocks),
         "{",
         wrapper.unpack(walk, plan),
         *loop,
@@ -139,7 +141,7 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
     return Unit(name=name, mode=mode, text=text, body=body, frame=frame, sums=records,
                 digest=hashlib.sha256(text.encode()).hexdigest(),
                 notes={"dynamic_smem": smem, "staged": plan is not None,
-                       "stages": plan.stages if plan is not None else 0})
+                       "stages": plan.stages if plan is not None else 0, "min_blocks": min_blocks or 0})
 
 
 _IDENT = re.compile(r"[A-Za-z_][A-Za-z0-9_]*")

@@ -73,12 +73,20 @@ def _slot_records(walk) -> list:
     return out
 
 
-#: Registers per thread above which an entry's inputs are staged through
-#: shared memory (at most one 256-thread block is resident per SM then, too few
-#: warps for plain loads to keep HBM busy).  Measured on the B200: the staged
-#: SPD-solve VJP (227 registers unstaged) ran at 73 % of HBM against 59 %
-#: unstaged, while every kernel with 2+ resident blocks lost 5-20 % staged.
-STAGE_ABOVE_REGS = 128
+#: Registers per thread above which an entry is register-bound: at most one
+#: 256-thread block is resident per SM, too few warps for plain loads to keep
+#: HBM busy.  Such an entry is rebuilt with two resident blocks asked of the
+#: compiler (a 128-register cap); if that build spills, its inputs are staged
+#: through shared memory instead.  Measured on the B200 for the SPD-solve VJP
+#: (227 registers uncapped): capped to 102 registers without a spill it
+#: ran at 83 % of HBM, staged at 73 %, uncapped at 59 %; every kernel with two
+#: or more resident blocks lost 5-20 % staged and gained nothing from a cap.
+REGISTER_BOUND = 128
+
+
+def _spills(ptxas: dict, name: str) -> bool:
+    r = ptxas.get(name, {})
+    return bool(r.get("spill_store_B") or r.get("spill_load_B"))
 
 
 def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "float64",
@@ -91,11 +99,16 @@ def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "flo
     name = name or kernel.name
     unit = render_unit(kernel, name, mode, staged=bool(staged))
     cubin, log, ptxas = compile_cubin(unit.text, name)
-    if staged is None and ptxas.get(name, {}).get("regs", 0) > STAGE_ABOVE_REGS:
-        trial = render_unit(kernel, name, mode, staged=True)
-        if trial.notes.get("staged"):
-            unit = trial
-            cubin, log, ptxas = compile_cubin(unit.text, name)
+    if staged is None and ptxas.get(name, {}).get("regs", 0) > REGISTER_BOUND:
+        capped = render_unit(kernel, name, mode, staged=False, min_blocks=2)
+        c_cubin, c_log, c_ptxas = compile_cubin(capped.text, name)
+        if not _spills(c_ptxas, name):
+            unit, cubin, log, ptxas = capped, c_cubin, c_log, c_ptxas
+        else:
+            trial = render_unit(kernel, name, mode, staged=True)
+            if trial.notes.get("staged"):
+                unit = trial
+                cubin, log, ptxas = compile_cubin(unit.text, name)
     stem = f"{name}.{mode}"
     (directory / f"{stem}.cu").write_text(unit.text)
     (directory / f"{stem}.cubin").write_bytes(cubin)
@@ -110,6 +123,7 @@ def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "flo
         "frame": unit.frame,
         "dynamic_smem": unit.notes.get("dynamic_smem", 0),
         "stages": unit.notes.get("stages", 0),
+        "min_blocks": unit.notes.get("min_blocks", 0),
         "sample_sums": [{"name": n, "op": op, "companion": comp} for n, op, comp in unit.sums],
         "slots": _slot_records(kernel.walk),
         "nvrtc_options": [o for o in options() if not o.startswith("-I")],

@@ -96,14 +96,16 @@ class B200Wrapper:
 
     qualifier = "__device__ __forceinline__"
 
-    def entry_signature(self, walk, name: str) -> str:
+    def entry_signature(self, walk, name: str, min_blocks: int | None = None) -> str:
         """``extern "C" __global__`` entry: role mirrors by value in ``arg_spec``
-        order, then the int64 partition triple."""
+        order, then the int64 partition triple.  ``min_blocks`` asks the
+        compiler to keep that many blocks resident per SM (a register cap)."""
         sp = _spelling()
         params = [f"    {param_type(role, walk.slot_types[(role, n)])} {sp.param_name(role, n)}"
                   for role, n in walk.arg_spec]
         params += ["    long long base", "    long long count", "    long long nSamples"]
-        return (f'extern "C" __global__ void __launch_bounds__({BLOCK}) {name}(\n'
+        bounds = f"{BLOCK}, {min_blocks}" if min_blocks else f"{BLOCK}"
+        return (f'extern "C" __global__ void __launch_bounds__({bounds}) {name}(\n'
                 + ",\n".join(params) + ")")
 
     def index_prologue(self, segment=None, *, active=None, box=None, team=None) -> str:

@@ -269,3 +269,30 @@ def test_bind_refusals_name_every_argument():
         runtime.run(k, **good, bogus=nan_like((n,)))
     with pytest.raises(HawkError, match="disagree"):
         runtime.run(k, **{**good, "u": nan_like((n + 1,))})
+
+
+STAGED = BUNDLES / "staged"
+
+
+@pytest.mark.parametrize("n", [1, 33, 1000, 65536 + 17, 300000])
+def test_staged_units_match_the_oracle(n):
+    """The shared-memory staged entries (cp.async.bulk into stages, mbarrier
+    waits): the SPD VJP (lane frame) and the Param-gradient VJP (row frame)
+    bit-identical to the oracle, with the unit's error word still clear."""
+    w = workloads.spd_solve(n, seed=n + 1)
+    k = runtime.load(STAGED, "spd_solve_vjp")
+    assert k.sidecar["b200"]["stages"] >= 2
+    bar_A, bar_b = nan_like((6, 6, n)), nan_like((6, n))
+    runtime.run(k, A=dev(w["A"]), b=dev(w["b"]), bar_x=dev(w["bar_x"]), bar_A=bar_A, bar_b=bar_b)
+    wA, wb = oracle.spd_solve_vjp(w["A"], w["b"], w["bar_x"])
+    same(host(bar_A), wA)
+    same(host(bar_b), wb)
+    assert k.library.errors() == 0
+    p = workloads.poly_loss(n, seed=n + 2)
+    v = runtime.load(STAGED, "poly_loss_vjp")
+    cells = {c: nan_like((1,)) for c in ("bar_a", "bar_b", "bar_c")}
+    abc = {c: dev(np.array([p[c]])) for c in ("a", "b", "c")}
+    runtime.run(v, x=dev(p["x"]), t=dev(p["t"]), bar_r=dev(p["bar_r"]), **abc, **cells)
+    want, _rows = oracle.poly_loss_vjp(p["x"], p["t"], p["bar_r"], p["a"], p["b"], p["c"])
+    assert [host(cells[c])[0] for c in ("bar_a", "bar_b", "bar_c")] == [float(x) for x in want]
+    assert v.library.errors() == 0
