@@ -41,6 +41,8 @@ SIGNATURES = {
                                      _c.c_int32, _c.c_int32]),
     "hkb_argblock_rebind": (_c.c_int, [_P, _c.POINTER(_c.c_int64), _c.POINTER(_c.c_int64), _c.c_size_t]),
     "hkb_entry_launch": (_c.c_int, [_P, _P, _c.c_int64, _c.c_int64, _c.c_int64, _P]),
+    "hkb_entry_launch_persist": (_c.c_int, [_P, _P, _c.c_int64, _c.c_int64, _c.c_int64, _P, _P, _P, _P,
+                                            _c.c_uint32, _c.c_int64, _P]),
     "hkb_cells_leaves": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _c.POINTER(_P), _c.POINTER(_P),
                                     _c.c_int64, _P, _P, _P]),
     "hkb_cells_tree": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _P, _P, _c.c_int64, _P, _P]),
@@ -138,6 +140,17 @@ class Entry:
     def launch(self, block: "ArgBlock", base: int, count: int, n_samples: int, stream: int = 0) -> None:
         check(lib().hkb_entry_launch(self._h, block._h, int(base), int(count), int(n_samples),
                                      ctypes.c_void_p(int(stream) or None)),
+              f"launching {self.name!r}")
+
+    def launch_persist(self, block: "ArgBlock", base: int, count: int, n_samples: int, next_ptr: int,
+                       util: int = 0, steps: int = 0, stepsum: int = 0, chunk: int = 32, grid: int = 0,
+                       stream: int = 0) -> None:
+        """The persistent entry over ``[base, base + count)``; the pointers are
+        device addresses (0 for an optional one left out)."""
+        vp = lambda v: ctypes.c_void_p(int(v) or None)   # noqa: E731
+        check(lib().hkb_entry_launch_persist(self._h, block._h, int(base), int(count), int(n_samples),
+                                             vp(next_ptr), vp(util), vp(steps), vp(stepsum), int(chunk),
+                                             int(grid), vp(stream)),
               f"launching {self.name!r}")
 
 

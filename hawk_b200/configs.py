@@ -14,6 +14,17 @@ c3 gravity         f = G m1 m2 / |d|^3 * d, u = -G m1 m2 / |d|, d = r2 - r1
 c4 spd_solve       x = cho_solve(cholesky(A), b) for a 6x6 SPD A
 c5 kepler          Newton on E - e sin E = M from E = M, at most 32 trips,
                    leaving when |dE| < 1e-14; E and the trip count (int32)
+
+Stepping kernels (automatic, ``steps="auto"``: each launch runs up to the
+``fused_steps`` word of steps per sample, a sample leaving at its own finish;
+hawk/trace/steps.py):
+
+s1 oscillator      one classic RK4 step of x'' = -w^2 x - 2 z w x' per step,
+                   finishing at the sample's own stop step
+s2 orbit           one adaptive Fehlberg 7(8) attempt on the two-body problem
+                   (GM = 1) per step, finishing at the sample's final time;
+                   the step-size factor is 0.9 * err^(-1/8), clamped to
+                   [0.2, 5], with err^(-1/8) taken as three square roots
 """
 
 from __future__ import annotations
@@ -23,7 +34,7 @@ from .frontend import load
 hawk = load()
 
 import hawk.math as m  # noqa: E402
-from hawk import Int32, Kernel, Matrix, Mutable, Param, Scalar, Vector  # noqa: E402
+from hawk import Int32, Kernel, Matrix, Mutable, Param, Scalar, Terminated, Vector  # noqa: E402
 from hawk.diff import jvp, param_planes, vjp  # noqa: E402
 
 
@@ -69,6 +80,117 @@ def kepler(e: Scalar, M: Scalar, E: Mutable[Scalar], iters: Mutable[Int32]):
     iters = n
 
 
+def _rk4_accel(stiff, damp, p, q):
+    return stiff * p - damp * q
+
+
+@hawk.kernel
+def oscillator(omega: Scalar, zeta: Scalar, nstop: Scalar, dt: Param, terminated: Terminated,
+               x: Mutable[Scalar], v: Mutable[Scalar], k: Mutable[Scalar]):
+    x0 = x
+    v0 = v
+    stiff = -(omega * omega)
+    damp = 2.0 * zeta * omega
+    half = 0.5 * dt
+    a1 = _rk4_accel(stiff, damp, x0, v0)
+    v2 = v0 + half * a1
+    a2 = _rk4_accel(stiff, damp, x0 + half * v0, v2)
+    v3 = v0 + half * a2
+    a3 = _rk4_accel(stiff, damp, x0 + half * v2, v3)
+    v4 = v0 + dt * a3
+    a4 = _rk4_accel(stiff, damp, x0 + dt * v3, v4)
+    sixth = dt / 6.0
+    x = x0 + sixth * (v0 + 2.0 * (v2 + v3) + v4)
+    v = v0 + sixth * (a1 + 2.0 * (a2 + a3) + a4)
+    kn = k + 1.0
+    k = kn
+    terminated = kn >= nstop
+
+
+#: Fehlberg's 7(8) pair (NASA TR R-287, 1968): the stage matrix (row j: the
+#: weights of stages 0 .. j-1 in stage j), the 8th-order weights, and the
+#: error weight 41/840 of stages 0, 10, 11, 12 (+, +, -, -).
+RKF78_A = (
+    (2.0 / 27.0,),
+    (1.0 / 36.0, 1.0 / 12.0),
+    (1.0 / 24.0, 0.0, 1.0 / 8.0),
+    (5.0 / 12.0, 0.0, -25.0 / 16.0, 25.0 / 16.0),
+    (1.0 / 20.0, 0.0, 0.0, 1.0 / 4.0, 1.0 / 5.0),
+    (-25.0 / 108.0, 0.0, 0.0, 125.0 / 108.0, -65.0 / 27.0, 125.0 / 54.0),
+    (31.0 / 300.0, 0.0, 0.0, 0.0, 61.0 / 225.0, -2.0 / 9.0, 13.0 / 900.0),
+    (2.0, 0.0, 0.0, -53.0 / 6.0, 704.0 / 45.0, -107.0 / 9.0, 67.0 / 90.0, 3.0),
+    (-91.0 / 108.0, 0.0, 0.0, 23.0 / 108.0, -976.0 / 135.0, 311.0 / 54.0, -19.0 / 60.0, 17.0 / 6.0,
+     -1.0 / 12.0),
+    (2383.0 / 4100.0, 0.0, 0.0, -341.0 / 164.0, 4496.0 / 1025.0, -301.0 / 82.0, 2133.0 / 4100.0,
+     45.0 / 82.0, 45.0 / 164.0, 18.0 / 41.0),
+    (3.0 / 205.0, 0.0, 0.0, 0.0, 0.0, -6.0 / 41.0, -3.0 / 205.0, -3.0 / 41.0, 3.0 / 41.0, 6.0 / 41.0, 0.0),
+    (-1777.0 / 4100.0, 0.0, 0.0, -341.0 / 164.0, 4496.0 / 1025.0, -289.0 / 82.0, 2193.0 / 4100.0,
+     51.0 / 82.0, 33.0 / 164.0, 12.0 / 41.0, 0.0, 1.0),
+)
+RKF78_B = {5: 34.0 / 105.0, 6: 9.0 / 35.0, 7: 9.0 / 35.0, 8: 9.0 / 280.0, 9: 9.0 / 280.0,
+           11: 41.0 / 840.0, 12: 41.0 / 840.0}
+RKF78_ERR = ((0, 1.0), (10, 1.0), (11, -1.0), (12, -1.0))
+ORBIT_TOL = 1e-10
+
+
+def _orbit_rate(s):
+    """d/dt of the two-body state (position, velocity) with GM = 1."""
+    rr = s[0] * s[0] + s[1] * s[1] + s[2] * s[2]
+    w = 1.0 / (rr * m.sqrt(rr))
+    return [s[3], s[4], s[5], -(s[0] * w), -(s[1] * w), -(s[2] * w)]
+
+
+def _weighted(terms):
+    """sum of weight * stage over the nonzero weights, in stage order."""
+    acc = None
+    for wgt, val in terms:
+        t = wgt * val
+        acc = t if acc is None else acc + t
+    return acc
+
+
+def _rkf78(s0, h):
+    """The 8th-order state and the error estimate of one attempt of step h."""
+    ks = [_orbit_rate(s0)]
+    for row in RKF78_A:
+        y = [s0[d] + h * _weighted([(a, ks[j][d]) for j, a in enumerate(row) if a != 0.0])
+             for d in range(6)]
+        ks.append(_orbit_rate(y))
+    s8 = [s0[d] + h * _weighted([(b, ks[j][d]) for j, b in sorted(RKF78_B.items())]) for d in range(6)]
+    err = [h * (41.0 / 840.0) * _weighted([(sg, ks[j][d]) for j, sg in RKF78_ERR]) for d in range(6)]
+    return s8, err
+
+
+def _err_norm(s0, s8, err):
+    """max over components of |err| / (tol + tol * max(|s8|, |s0|))."""
+    worst = None
+    for d in range(6):
+        q = m.abs(err[d]) / (ORBIT_TOL + ORBIT_TOL * m.max(m.abs(s8[d]), m.abs(s0[d])))
+        worst = q if worst is None else m.max(worst, q)
+    return worst
+
+
+@hawk.kernel
+def orbit(t_end: Scalar, terminated: Terminated, s: Mutable[Vector[6]], t: Mutable[Scalar],
+          h: Mutable[Scalar], n_acc: Mutable[Scalar], n_rej: Mutable[Scalar]):
+    s0 = s
+    t0 = t
+    rest = t_end - t0
+    final = h >= rest
+    step = m.where(final, rest, h)
+    s8, err = _rkf78(s0, step)
+    worst = _err_norm(s0, s8, err)
+    ok = worst < 1.0
+    shrink = 1.0 / m.sqrt(m.sqrt(m.sqrt(worst)))
+    h = step * m.min(5.0, m.max(0.2, 0.9 * shrink))
+    s = m.where(ok, m.vec(s8), s0)
+    t_next = m.where(ok, m.where(final, t_end, t0 + step), t0)
+    t = t_next
+    n_acc = n_acc + m.where(ok, 1.0, 0.0)
+    n_rej = n_rej + m.where(ok, 0.0, 1.0)
+    terminated = t_next >= t_end
+
+
 #: Every kernel the bundles hold, by name, with the scalar modes each is built in.
 KERNELS = {
     "energy": (energy, ("float64",)),
@@ -84,4 +206,6 @@ KERNELS = {
     "spd_solve_vjp": (Kernel("spd_solve_vjp", vjp(spd_solve, wrt=("A", "b"))), ("float64",)),
     "kepler": (kepler, ("float64",)),
     "kepler_vjp": (Kernel("kepler_vjp", vjp(kepler, wrt=("e", "M"))), ("float64",)),
+    "oscillator": (oscillator, ("float64",)),
+    "orbit": (orbit, ("float64",)),
 }

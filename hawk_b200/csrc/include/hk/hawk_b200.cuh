@@ -20,6 +20,7 @@
 #include "ints.cuh"
 #include "sample_sum.cuh"
 #include "stage.cuh"
+#include "steps.cuh"
 
 namespace hk {
 

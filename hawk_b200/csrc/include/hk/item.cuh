@@ -39,6 +39,9 @@ struct Item<T, N> {
     HK_FI const T* data() const { return v; }
     HK_FI const Item& get() const { return *this; }
     HK_FI const Item& eval() const { return *this; }
+    HK_FI Item operator()() const { return *this; }      // a Mutable read's value: plane[i].get()()
+    // component K of a Mutable read's value, as the body spells it: plane_i.eval<K>(i)
+    template <int K, class I> HK_FI T eval(const I&) const { return v[K]; }
     static HK_HD constexpr int size() { return N; }
 
     HK_FI T dot(const Item& o) const {
@@ -82,6 +85,7 @@ struct Item<T, R, C> {
     HK_FI const T* data() const { return &m[0][0]; }
     HK_FI const Item& get() const { return *this; }
     HK_FI const Item& eval() const { return *this; }
+    HK_FI Item operator()() const { return *this; }
 
     HK_FI Item<T, C, R> transpose() const {
         Item<T, C, R> t;
@@ -214,6 +218,9 @@ template <int... D, class T> struct Constant<extents<D...>, T> {
         for (int k = 0; k < (D * ...); ++k) p[k] = x;
         return y;
     }
+};
+template <class T> struct Constant<extents<>, T> {     // rank 0: the scalar itself
+    static HK_FI T make(T x) { return x; }
 };
 template <class E, class T>
 HK_FI auto constant(T x) -> decltype(Constant<E, T>::make(x)) { return Constant<E, T>::make(x); }

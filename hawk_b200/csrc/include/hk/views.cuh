@@ -61,6 +61,7 @@ template <class T> struct Val {
     T x;
     HK_FI T eval() const { return x; }
     HK_FI T get() const { return x; }
+    HK_FI T operator()() const { return x; }
     HK_FI operator T() const { return x; }
 };
 
@@ -149,13 +150,31 @@ template <class T> struct ScalarOut {
         HK_FI void operator=(T v) const { st_out(q, v); }
         HK_FI void operator+=(T v) const { *q = *q + v; }
         HK_FI T eval() const { return *q; }
-        HK_FI T get() const { return *q; }
+        HK_FI Val<T> get() const { return Val<T>{*q}; }   // a Mutable read: plane[i].get()()
         HK_FI operator T() const { return *q; }
     };
     HK_FI explicit ScalarOut(const abi::ScalarHandle& h) : p(static_cast<T*>(h.data)), n(h.samples) {}
     HK_FI explicit ScalarOut(const abi::IntHandle& h) : p(static_cast<T*>(h.data)), n(h.samples) {}
     HK_FI Ref operator[](const SampleIndex& i) const { return Ref{p + i.g}; }
     HK_FI T* data() const { return p; }
+    HK_FI u64 samples() const { return n; }
+};
+
+// A finishing kernel's mask (the Terminated plane, one bool per sample): read
+// at the top of the step and set by its finish epilogue in the same launch, so
+// both go through the coherent path (never the read-only one).
+struct MaskView {
+    bool* p;
+    u64 n;
+    struct Ref {
+        bool* q;
+        HK_FI void operator=(bool v) const { *q = v; }
+        HK_FI bool eval() const { return *q; }
+        HK_FI operator bool() const { return *q; }
+    };
+    HK_FI explicit MaskView(const abi::ScalarHandle& h) : p(static_cast<bool*>(h.data)), n(h.samples) {}
+    HK_FI Ref operator[](const SampleIndex& i) const { return Ref{p + i.g}; }
+    HK_FI bool* data() const { return p; }
     HK_FI u64 samples() const { return n; }
 };
 

@@ -430,6 +430,41 @@ int hkb_entry_launch(hkb_entry* entry, hkb_argblock* block, int64_t base, int64_
     return HKB_OK;
 }
 
+int hkb_entry_launch_persist(hkb_entry* entry, hkb_argblock* block, int64_t base, int64_t count,
+                             int64_t n_samples, uint32_t* next, uint64_t* util, uint32_t* steps,
+                             uint64_t* stepsum, uint32_t chunk, int64_t grid, void* stream) {
+    if (entry == nullptr || block == nullptr || next == nullptr)
+        return fail(HKB_ERR_ARGUMENT, "hkb_entry_launch_persist: null entry, block or claim counter");
+    if (base < 0 || count < 0 || base + count > n_samples)
+        return fail(HKB_ERR_RANGE, "partition [%lld, %lld) is outside the %lld samples",
+                    (long long)base, (long long)(base + count), (long long)n_samples);
+    if (count >= (int64_t(1) << 31))
+        return fail(HKB_ERR_RANGE, "a persistent launch claims samples with a 32-bit counter: %lld samples "
+                    "is 2^31 or more; split the range", (long long)count);
+    if (grid < 0) return fail(HKB_ERR_ARGUMENT, "hkb_entry_launch_persist: negative grid %lld", (long long)grid);
+    if (count == 0) return HKB_OK;
+    DeviceScope scope(entry->lib->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "selecting the device");
+    std::vector<void*> args(block->params);
+    long long b = base, c = count, ns = n_samples;
+    unsigned ch = chunk;
+    args.push_back(&b);
+    args.push_back(&c);
+    args.push_back(&ns);
+    args.push_back(&next);
+    args.push_back(&util);
+    args.push_back(&steps);
+    args.push_back(&stepsum);
+    args.push_back(&ch);
+    // a resident grid: every claim loop runs until the counter passes count
+    const int64_t g = grid > 0 ? grid : grid_for(entry, count);
+    const cudaError_t err = cudaLaunchKernel(reinterpret_cast<const void*>(entry->kernel),
+                                             dim3(static_cast<unsigned>(g)), dim3(kBlock), args.data(),
+                                             entry->dynamic_smem, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "launching the persistent entry");
+    return HKB_OK;
+}
+
 }  // extern "C"
 
 // ------------------------------------------------------------ the finish tree

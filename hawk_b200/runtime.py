@@ -38,9 +38,11 @@ from .errors import HawkError
 from .planes import Plane, as_plane
 
 #: Roles whose plane's trailing extent is the sample count (they vote on n).
-PER_SAMPLE_ROLES = ("mutable", "out", "vec_in", "mat_in", "per_sample")
+PER_SAMPLE_ROLES = ("mutable", "out", "vec_in", "mat_in", "per_sample", "terminated")
 #: Roles that are written by the kernel (their plane must be writable).
-SINK_ROLES = ("mutable", "out", "accum_out")
+SINK_ROLES = ("mutable", "out", "accum_out", "terminated")
+#: The automatic kernel's trip-budget word (hawk/ir/nodes.py FUSED_STEPS_PLANE).
+FUSED_STEPS = "fused_steps"
 ROW = 32
 
 _WIRE_OF_MODE = {"float64": "float64", "float32": "float32"}
@@ -105,17 +107,48 @@ class DeviceKernel:
         self.device = int(device)
         self.library = abi.Library(self.directory / b200["cubin"], self.device)
         self.entry = self.library.entry(b200["entry"])
+        # an automatic stepping kernel's persistent entry (<name>_persist)
+        self.persist = self.library.entry(b200["persist"]) if b200.get("persist") else None
         self.descriptor = descriptor_for_sidecar(sidecar)
         self.block = abi.ArgBlock(self.descriptor)
         self._lock = threading.Lock()
         self._held: list = []
         self._scratch: dict = {}
+        self.finished = None            # the finished_count cell a run bound by default
+        self._one_step = None           # the fused_steps word of 1 a run bound by default
 
     # -- validation ---------------------------------------------------------
     def _wire(self, name: str, dtype: str) -> str:
+        wire = self.sidecar.get("arg_dtypes", {}).get(name)
+        if wire:
+            return wire                     # an index word rides 64 bits (hawk/runtime.py:221-225)
         if dtype in _INT_DTYPES:
             return {"i32": "int32", "i64": "int64"}.get(dtype, dtype)
-        return self.sidecar.get("arg_dtypes", {}).get(name) or _WIRE_OF_MODE[self.mode]
+        return _WIRE_OF_MODE[self.mode]
+
+    def default_words(self, arrays: dict, stream=None) -> dict:
+        """``arrays`` plus the reserved one-cell planes a runner normally binds,
+        for each one this kernel declares and the caller leaves out
+        (hawk/runtime.py:237-265): a ``fused_steps`` word of 1 (a launch
+        outside a runner takes exactly one step) and a ``finished_count``
+        counter reset to 0 (``self.finished`` holds it after the launch)."""
+        import torch
+
+        declared = {n for _r, n in self.arg_spec}
+        counter = (self.sidecar.get("finish") or {}).get("counter")
+        extra = {}
+        dev = torch.device("cuda", self.device)
+        if FUSED_STEPS in declared and FUSED_STEPS not in arrays:
+            if getattr(self, "_one_step", None) is None:
+                self._one_step = torch.ones(1, dtype=torch.int64, device=dev)
+            extra[FUSED_STEPS] = self._one_step
+        if counter and counter in declared and counter not in arrays:
+            if getattr(self, "finished", None) is None:
+                self.finished = torch.zeros(1, dtype=torch.uint32, device=dev)
+            with torch.cuda.stream(_torch_stream(stream, self.device)):
+                self.finished.zero_()
+            extra[counter] = self.finished
+        return {**arrays, **extra} if extra else arrays
 
     def n_from(self, planes: dict) -> int:
         """The sample count every bound per-sample plane agrees on."""
@@ -316,9 +349,12 @@ def load(directory, kernel: str, mode: str = "float64", device: int | None = Non
 
 
 def launch_cells(kernel: DeviceKernel, *, base: int = 0, count: int | None = None,
-                 n_samples: int | None = None, stream=None, **arrays):
+                 n_samples: int | None = None, stream=None, persist: dict | None = None, **arrays):
     """Validate, bind and launch (the body of ``run``); for a kernel with cells,
-    return ``(state, outputs, lo_row, hi_row)`` for the caller to finish, else None."""
+    return ``(state, outputs, lo_row, hi_row)`` for the caller to finish, else None.
+    ``persist`` launches the persistent entry instead, with those keyword
+    arguments of ``abi.Entry.launch_persist``."""
+    arrays = kernel.default_words(arrays, stream)
     declared = {name for _r, name in kernel.arg_spec} | set(kernel.cells)
     unknown = sorted(set(arrays) - declared)
     if unknown:
@@ -363,10 +399,51 @@ def launch_cells(kernel: DeviceKernel, *, base: int = 0, count: int | None = Non
         bound = planes
     kernel.check(bound, values, n_samples)
     kernel.bind_all(bound, values, n_samples)
+    if persist is not None:
+        kernel.persist.launch_persist(kernel.block, base, count, n_samples,
+                                      stream=_stream(stream, kernel.device), **persist)
+        return None
     kernel.launch(base, count, n_samples, stream)
     if not cells:
         return None
     return state, outputs, base // ROW, -(-(base + count) // ROW)
+
+
+def run_persist(kernel: DeviceKernel, *, base: int = 0, count: int | None = None,
+                n_samples: int | None = None, chunk: int = 32, grid: int = 0, steps=None, stepsum=None,
+                util=None, stream=None, **arrays):
+    """Run an automatic stepping kernel's persistent entry over ``[base, base + count)``.
+
+    Each sample runs to its finish or the ``fused_steps`` budget (a word of 1
+    when left out), exactly as one launch of the kernel's own entry with that
+    word would run it; lanes claim samples off a fresh counter, ``chunk``
+    trips between claims.  ``steps`` (uint32, one cell), ``stepsum`` (uint64)
+    and ``util`` (two uint64) receive the longest per-sample trip count, the
+    steps run and the slot fill when given (each zeroed by the caller).  The
+    finished counter -- bound, or ``kernel.finished`` -- holds the batch's
+    finished count afterwards, samples finished on entry included.  Returns
+    the claim counter (a device uint32)."""
+    import torch
+
+    if kernel.persist is None:
+        raise HawkError(f"kernel {kernel.name!r} is not an automatic stepping kernel; it has no persistent entry")
+    if chunk < 0:
+        raise HawkError(f"chunk={chunk}: the trips between claims is a count (0: whole samples)")
+    for label, t, dtype, cells in (("steps", steps, torch.uint32, 1), ("stepsum", stepsum, torch.uint64, 1),
+                                   ("util", util, torch.uint64, 2)):
+        if t is not None and (not torch.is_tensor(t) or t.dtype != dtype or t.numel() < cells
+                              or t.device != torch.device("cuda", kernel.device)):
+            raise HawkError(f"{label}=: a device {dtype} tensor of {cells} cell(s) on cuda:{kernel.device}")
+    with kernel._lock:
+        claim = torch.zeros(1, dtype=torch.uint32, device=torch.device("cuda", kernel.device))
+        with torch.cuda.stream(_torch_stream(stream, kernel.device)):
+            claim.zero_()
+        ptr = lambda t: 0 if t is None else t.data_ptr()   # noqa: E731
+        launch_cells(kernel, base=base, count=count, n_samples=n_samples, stream=stream,
+                     persist={"next_ptr": claim.data_ptr(), "util": ptr(util), "steps": ptr(steps),
+                              "stepsum": ptr(stepsum), "chunk": chunk, "grid": grid}, **arrays)
+        kernel._held.append(claim)
+    return claim
 
 
 def run(kernel: DeviceKernel, *, base: int = 0, count: int | None = None, n_samples: int | None = None,

@@ -20,6 +20,7 @@ import re
 from dataclasses import dataclass, field
 
 from ..errors import HawkError
+from .persist import SUFFIX as PERSIST_SUFFIX, persist_entry
 from .wrapper import B200, StagePlan, lane_frame_staged, sample_sum_store
 from .writer import B200_WRITER, body_text
 
@@ -38,7 +39,6 @@ _UNBUILT = {
     "hk::linalg::team::": "team linear algebra (n > 32)",
     "hk::linalg::eigh": "the symmetric eigensolver",
     "hawk_abi::accum_": "scattered accumulates",
-    "hawk_abi::finish_count": "kernels that finish their own samples",
     "hawk_abi::mix_count": "auto dispatch branch counts",
     "hawk_abi::tiled": "wide (tiled) scratch planes",
     "hawk_abi::warp_sum": "warp-per-lane sums",
@@ -61,13 +61,19 @@ class Unit:
 
 
 def _refuse(name: str, walk) -> None:
-    if getattr(walk, "finish", None) is not None:
-        raise HawkError(f"{name!r}: a kernel that finishes its own samples is not built on the b200 target")
     if walk.companions:
         raise HawkError(f"{name!r}: compensated keyed sums (owned companions) are not built on the b200 target")
     for role, slot in walk.arg_spec:
-        if role in ("terminated", "wide_in", "wide_out"):
+        if role in ("wide_in", "wide_out"):
             raise HawkError(f"{name!r}: slot {slot!r} has role {role!r}, which the b200 target does not build")
+
+
+def _word_read() -> str:
+    """The automatic kernel's ``fused_steps`` word, read once per launch."""
+    from hawk.emit.spelling import binding_name
+    from hawk.ir.nodes import FUSED_STEPS_PLANE
+
+    return f"{binding_name('lookup', FUSED_STEPS_PLANE)}[hk::SampleIndex::make(0)].eval()"
 
 
 def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: bool = True,
@@ -93,6 +99,9 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
     sums = sample_sums(sinks)
     if len({s.op for s in sums}) > 1:
         raise HawkError(f"{name!r}: one kernel reduces over samples with one op (sum, max or min)")
+    one_step = getattr(kernel, "one_step", None)
+    if one_step is not None and sums:
+        raise HawkError(f"{name!r}: an automatic stepping kernel with sample sums is not built on the b200 target")
     wrapper = B200
     smem = 0
     elem_bytes = 8 if mode == "float64" else 4
@@ -117,6 +126,17 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
         else:
             plan = None
             loop = [wrapper.index_prologue(), body, wrapper.index_epilogue()]
+        if one_step is not None:
+            # an automatic kernel (steps="auto", hawk/trace/steps.py): one uniform
+            # branch per launch on the fused_steps word -- 1 runs the single step's
+            # body, any other word the fused loop (hawk/emit/wrapper.py:1507-1545)
+            plan, smem = None, 0
+            single = render_body(one_step.sinks, one_step.walk, indent="        ", writer=B200_WRITER)
+            loop = [f"    if ({_word_read()} == 1) {{",
+                    wrapper.index_prologue(), body_text(single.text), wrapper.index_epilogue(),
+                    "    } else {",
+                    wrapper.index_prologue(), body, wrapper.index_epilogue(),
+                    "    }"]
         frame = "lane"
     parts = [
         f"// hawk_b200 unit {name!r} (scalar mode {mode}), sm_100a.",
@@ -136,12 +156,16 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
         "}",
         "",
     ]
+    persist = persist_entry(kernel, name, wrapper) if one_step is not None else None
+    if persist is not None:
+        parts += [persist, ""]
     text = "\n".join(parts)
     records = tuple((s.name, s.op, s.companion.name if s.op == "sum" else None) for s in sums)
     return Unit(name=name, mode=mode, text=text, body=body, frame=frame, sums=records,
                 digest=hashlib.sha256(text.encode()).hexdigest(),
                 notes={"dynamic_smem": smem, "staged": plan is not None,
-                       "stages": plan.stages if plan is not None else 0, "min_blocks": min_blocks or 0})
+                       "stages": plan.stages if plan is not None else 0, "min_blocks": min_blocks or 0,
+                       "persist": f"{name}{PERSIST_SUFFIX}" if persist is not None else None})
 
 
 _IDENT = re.compile(r"[A-Za-z_][A-Za-z0-9_]*")

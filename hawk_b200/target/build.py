@@ -124,6 +124,7 @@ def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "flo
         "dynamic_smem": unit.notes.get("dynamic_smem", 0),
         "stages": unit.notes.get("stages", 0),
         "min_blocks": unit.notes.get("min_blocks", 0),
+        "persist": unit.notes.get("persist"),
         "sample_sums": [{"name": n, "op": op, "companion": comp} for n, op, comp in unit.sums],
         "slots": _slot_records(kernel.walk),
         "nvrtc_options": [o for o in options() if not o.startswith("-I")],

@@ -63,6 +63,12 @@ def view_decl(role: str, name: str, ttype, stage=None) -> list:
     shape = tuple(int(e) for e in ttype.shape)
     if role in _VALUE_ROLES:
         return [f"    const {param_type(role, ttype)} {ident} = {src};", f"    (void){ident};"]
+    if role == "terminated":
+        # the mask is read through one binding and set through its writable
+        # twin (hawk/emit/spelling.py:171-173); both are the same plane
+        twin = sp.finish_binding(name)
+        return [f"    const hk::MaskView {ident}({src});", f"    (void){ident};",
+                f"    const hk::MaskView {twin}({src});", f"    (void){twin};"]
     if role in _INPUT_ROLES:
         if len(shape) == 0:
             view = f"hk::ScalarIn<{elem}>"

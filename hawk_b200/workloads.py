@@ -68,4 +68,41 @@ def kepler(n: int, seed: int = 0) -> dict:
             "bar_E": rng.standard_normal(n)}
 
 
-MAKERS = {"energy": energy, "poly_loss": poly_loss, "gravity": gravity, "spd_solve": spd_solve, "kepler": kepler}
+def oscillator(n: int, seed: int = 0, stop_max: int = 64, done_every: int = 0) -> dict:
+    """Damped oscillators: w in [0.5, 3], z in [0, 0.3], x(0) ~ N(0, 1), v(0) = 0,
+    each stopping after its own 1..stop_max steps; every ``done_every``-th sample
+    starts finished (0: none).  dt = 0.01."""
+    rng = np.random.default_rng(seed)
+    term = np.zeros(n, dtype=bool)
+    if done_every:
+        term[3::done_every] = True
+    return {"omega": rng.uniform(0.5, 3.0, n), "zeta": rng.uniform(0.0, 0.3, n),
+            "nstop": rng.integers(1, stop_max + 1, n).astype(np.float64), "x": rng.standard_normal(n),
+            "v": np.zeros(n), "k": np.zeros(n), "terminated": term, "dt": 0.01}
+
+
+def orbit(n: int, seed: int = 0, done_every: int = 0) -> dict:
+    """Two-body orbits (GM = 1, semi-major axis 1): eccentricity in [0, 0.7],
+    starting at periapsis in a random orientation, integrated from t = 0 to
+    t_end in [0.5, 2 pi] with a first step h in [0.02, 0.5] (the larger ones
+    are rejected before the controller settles)."""
+    rng = np.random.default_rng(seed)
+    e = rng.uniform(0.0, 0.7, n)
+    rp = 1.0 - e
+    vp = np.sqrt((1.0 + e) / (1.0 - e))
+    # a random orthonormal frame per sample: periapsis direction p, velocity direction q
+    a = rng.standard_normal((3, n))
+    p = a / np.linalg.norm(a, axis=0)
+    b = rng.standard_normal((3, n))
+    b -= p * np.sum(b * p, axis=0)
+    q = b / np.linalg.norm(b, axis=0)
+    s = np.concatenate([p * rp, q * vp])
+    term = np.zeros(n, dtype=bool)
+    if done_every:
+        term[3::done_every] = True
+    return {"s": np.ascontiguousarray(s), "t": np.zeros(n), "h": rng.uniform(0.02, 0.5, n), "n_acc": np.zeros(n),
+            "n_rej": np.zeros(n), "t_end": rng.uniform(0.5, 2.0 * np.pi, n), "terminated": term}
+
+
+MAKERS = {"energy": energy, "poly_loss": poly_loss, "gravity": gravity, "spd_solve": spd_solve, "kepler": kepler,
+          "oscillator": oscillator, "orbit": orbit}

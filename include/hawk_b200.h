@@ -120,6 +120,20 @@ int hkb_argblock_rebind(hkb_argblock* block, const int64_t* slots, const int64_t
 int hkb_entry_launch(hkb_entry* entry, hkb_argblock* block, int64_t base, int64_t count,
                      int64_t n_samples, void* stream);
 
+/* The persistent entry of an automatic stepping kernel, `<kernel>_persist`
+ * (the reference emits it in hawk/emit/cuda.py:464-707; its runner lives in the
+ * absent eagle package): a resident grid whose lanes claim samples of
+ * [base, base + count) off `*next` (a uint32 the caller zeroes), run each to
+ * its finish or the `fused_steps` budget, write it back and claim the next.
+ * `util` (two uint64: steps run, lane slots offered), `steps` (uint32, maxed
+ * with the longest per-sample trip count) and `stepsum` (uint64) may be null;
+ * `chunk` is the trips between claims (0: whole samples); `grid` the blocks
+ * (0: every resident slot the entry's occupancy allows, capped by count).
+ * count must be below 2^31. */
+int hkb_entry_launch_persist(hkb_entry* entry, hkb_argblock* block, int64_t base, int64_t count,
+                             int64_t n_samples, uint32_t* next, uint64_t* util, uint32_t* steps,
+                             uint64_t* stepsum, uint32_t chunk, int64_t grid, void* stream);
+
 /* ---------------------------------------------- cells: the ordered finish */
 
 /* The device form of hawk/_cells.py:finish for `ncols` columns (<= 8) of

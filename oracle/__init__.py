@@ -90,6 +90,8 @@ _SIGS = {
     "hko_spd_solve_vjp": (None, [_P, _P, _P, _I, _P, _P, _I, _I, _I]),
     "hko_kepler": (None, [_P, _P, _P, _P, _I, _I]),
     "hko_kepler_vjp": (None, [_P, _P, _P, _P, _P, _I, _I]),
+    "hko_oscillator": (ctypes.c_uint32, [_P, _P, _P, _P, _P, _P, _P, _D, _I, _I, _I]),
+    "hko_orbit": (ctypes.c_uint32, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I]),
 }
 
 
@@ -283,3 +285,41 @@ def kepler_vjp(e, M, bar_E, threads: int = 1):
     bM = np.empty(n)
     parallel(lambda b, c: lib().hko_kepler_vjp(_p(e), _p(M), _p(bar_E), _p(be), _p(bM), b, c), n, threads)
     return be, bM
+
+
+# ------------------------------------------------------------- stepping kernels
+def _stepped(fn, n: int, threads: int) -> int:
+    counts = []
+    lock = threading.Lock()
+
+    def tile(b, c):
+        got = fn(b, c)
+        with lock:
+            counts.append(int(got))
+
+    parallel(tile, n, threads)
+    return sum(counts)
+
+
+def oscillator(planes: dict, dt: float, word: int, threads: int = 1) -> int:
+    """One launch of the automatic RK4 oscillator with the fused_steps ``word``,
+    in place on ``planes`` (x, v, k, nstop, omega, zeta float64; terminated
+    uint8/bool); returns the samples it newly finished."""
+    x, v, k = planes["x"], planes["v"], planes["k"]
+    term = planes["terminated"].view(np.uint8)
+    n = x.shape[0]
+    return _stepped(lambda b, c: lib().hko_oscillator(_p(x), _p(v), _p(k), _p(planes["nstop"]), _p(planes["omega"]),
+                                                      _p(planes["zeta"]), _p(term), float(dt), int(word), b, c),
+                    n, threads)
+
+
+def orbit(planes: dict, word: int, threads: int = 1) -> int:
+    """One launch of the automatic Fehlberg 7(8) orbit kernel with ``word``, in
+    place on ``planes`` (s (6, n), t, h, n_acc, n_rej, t_end float64;
+    terminated); returns the samples it newly finished."""
+    s = planes["s"]
+    term = planes["terminated"].view(np.uint8)
+    n = s.shape[1]
+    return _stepped(lambda b, c: lib().hko_orbit(_p(s), n, _p(planes["t"]), _p(planes["h"]), _p(planes["n_acc"]),
+                                                 _p(planes["n_rej"]), _p(planes["t_end"]), _p(term), int(word), b, c),
+                    n, threads)

@@ -471,3 +471,185 @@ void hko_kepler_vjp(const double* e, const double* M, const double* bar_E, doubl
         bar_e[i] = be;
     }
 }
+
+/* ------------------------------------------------------ stepping kernels
+ *
+ * An automatic kernel (steps="auto", hawk/trace/steps.py) run by the host
+ * target's two-path entry (hawk/emit/wrapper.py:1507-1545): a sample finished
+ * on entry is skipped; the fused_steps word 1 runs the single step, any other
+ * word max(word, 0) trips (at most INT_MAX, hawk_clamp_count) of the fused loop,
+ * leaving after the trip whose finish condition holds (a tail break); the
+ * carried values commit to the planes after the loop, and a sample whose
+ * carried finish flag is set is marked in the mask and counted (one count per
+ * newly finished sample).  The single step and one trip of the fused loop are
+ * the same operations, so one trip function serves both.  Each function
+ * returns the samples it newly finished in [base, base + count).
+ */
+static int64_t clamp_trips(int64_t word) {
+    if (word == 1) return 1;
+    if (word < 0) return 0;
+    return word < 2147483647LL ? word : 2147483647LL;
+}
+
+/*
+ * s1 oscillator, one trip:
+ *   t3 = dt * 0.16666666666666666; t7 = 0.5 * dt; t10 = -(w*w); t14 = (2 z) w;
+ *   t16 = t10 x - t14 v; t18 = v + t7 t16; t23 = t10 (x + t7 v) - t14 t18;
+ *   t25 = v + t7 t23; t33 = t10 (x + t7 t18) - t14 t25; t35 = v + dt t33;
+ *   x' = x + t3 ((v + 2 (t18 + t25)) + t35);
+ *   v' = v + t3 ((t16 + 2 (t23 + t33)) + (t10 (x + dt t25) - t14 t35));
+ *   k' = k + 1; finished when k' >= nstop.
+ */
+uint32_t hko_oscillator(double* x, double* v, double* k, const double* nstop, const double* omega,
+                        const double* zeta, uint8_t* term, double dt, int64_t word, int64_t base,
+                        int64_t count) {
+    uint32_t fin = 0;
+    const int64_t trips = clamp_trips(word);
+    const double t3 = dt * 0.16666666666666666, t7 = 0.5 * dt;
+    for (int64_t i = base; i < base + count; ++i) {
+        if (term[i]) continue;
+        const double w = omega[i];
+        const double t10 = -(w * w);
+        const double t14 = (2.0 * zeta[i]) * w;
+        double xs = x[i], vs = v[i], ks = k[i];
+        int done = 0;
+        for (int64_t trip = 0; trip < trips; ++trip) {
+            const double t16 = (t10 * xs) - (t14 * vs);
+            const double t18 = vs + (t7 * t16);
+            const double t23 = (t10 * (xs + (t7 * vs))) - (t14 * t18);
+            const double t25 = vs + (t7 * t23);
+            const double t33 = (t10 * (xs + (t7 * t18))) - (t14 * t25);
+            const double t35 = vs + (dt * t33);
+            const double nx = xs + (t3 * ((vs + (2.0 * (t18 + t25))) + t35));
+            const double nv = vs + (t3 * ((t16 + (2.0 * (t23 + t33))) + ((t10 * (xs + (dt * t25))) - (t14 * t35))));
+            const double nk = ks + 1.0;
+            done = nk >= nstop[i];
+            xs = nx;
+            vs = nv;
+            ks = nk;
+            if (done) break;
+        }
+        x[i] = xs;
+        v[i] = vs;
+        k[i] = ks;
+        if (done) {
+            term[i] = 1;
+            ++fin;
+        }
+    }
+    return fin;
+}
+
+/* Fehlberg's 7(8) pair: stage rows, the 8th-order weights and the error signs
+ * (hawk_b200/configs.py states the same table). */
+static const double RKF_A[12][12] = {
+    {2.0 / 27.0},
+    {1.0 / 36.0, 1.0 / 12.0},
+    {1.0 / 24.0, 0.0, 1.0 / 8.0},
+    {5.0 / 12.0, 0.0, -25.0 / 16.0, 25.0 / 16.0},
+    {1.0 / 20.0, 0.0, 0.0, 1.0 / 4.0, 1.0 / 5.0},
+    {-25.0 / 108.0, 0.0, 0.0, 125.0 / 108.0, -65.0 / 27.0, 125.0 / 54.0},
+    {31.0 / 300.0, 0.0, 0.0, 0.0, 61.0 / 225.0, -2.0 / 9.0, 13.0 / 900.0},
+    {2.0, 0.0, 0.0, -53.0 / 6.0, 704.0 / 45.0, -107.0 / 9.0, 67.0 / 90.0, 3.0},
+    {-91.0 / 108.0, 0.0, 0.0, 23.0 / 108.0, -976.0 / 135.0, 311.0 / 54.0, -19.0 / 60.0, 17.0 / 6.0, -1.0 / 12.0},
+    {2383.0 / 4100.0, 0.0, 0.0, -341.0 / 164.0, 4496.0 / 1025.0, -301.0 / 82.0, 2133.0 / 4100.0, 45.0 / 82.0,
+     45.0 / 164.0, 18.0 / 41.0},
+    {3.0 / 205.0, 0.0, 0.0, 0.0, 0.0, -6.0 / 41.0, -3.0 / 205.0, -3.0 / 41.0, 3.0 / 41.0, 6.0 / 41.0, 0.0},
+    {-1777.0 / 4100.0, 0.0, 0.0, -341.0 / 164.0, 4496.0 / 1025.0, -289.0 / 82.0, 2193.0 / 4100.0, 51.0 / 82.0,
+     33.0 / 164.0, 12.0 / 41.0, 0.0, 1.0},
+};
+static const int RKF_BJ[7] = {5, 6, 7, 8, 9, 11, 12};
+static const double RKF_BW[7] = {34.0 / 105.0, 9.0 / 35.0, 9.0 / 35.0, 9.0 / 280.0, 9.0 / 280.0,
+                                 41.0 / 840.0, 41.0 / 840.0};
+
+/* The two-body rate (GM = 1): rr = (x x + y y) + z z; w = 1 / (rr sqrt rr). */
+static void orbit_rate(const double s[6], double out[6]) {
+    const double rr = ((s[0] * s[0]) + (s[1] * s[1])) + (s[2] * s[2]);
+    const double w = 1.0 / (rr * sqrt(rr));
+    out[0] = s[3];
+    out[1] = s[4];
+    out[2] = s[5];
+    out[3] = -(s[0] * w);
+    out[4] = -(s[1] * w);
+    out[5] = -(s[2] * w);
+}
+
+/*
+ * s2 orbit, one trip (an adaptive Fehlberg 7(8) attempt):
+ *   rest = t_end - t; final = h >= rest; step = final ? rest : h;
+ *   stage j: y = s + step * (sum_l a_jl k_l over the nonzero a_jl, in l order);
+ *   s8 = s + step * (sum of the 8th-order weights' terms); err_d = (step 41/840) *
+ *   (((1 k0 + 1 k10) + -1 k11) + -1 k12); worst = fmax over d of
+ *   |err_d| / (1e-10 + 1e-10 fmax(|s8_d|, |s_d|)); ok = worst < 1;
+ *   h' = step fmin(5, fmax(0.2, 0.9 (1 / sqrt(sqrt(sqrt worst)))));
+ *   s' = ok ? s8 : s; t' = ok ? (final ? t_end : t + step) : t;
+ *   n_acc += ok ? 1 : 0; n_rej += ok ? 0 : 1; finished when t' >= t_end.
+ */
+static int orbit_trip(double s[6], double* t, double* h, double* na, double* nr, double t_end) {
+    const double rest = t_end - *t;
+    const int final = *h >= rest;
+    const double step = final ? rest : *h;
+    double k[13][6], y[6];
+    orbit_rate(s, k[0]);
+    for (int j = 0; j < 12; ++j) {
+        for (int d = 0; d < 6; ++d) {
+            double acc = 0.0;
+            int any = 0;
+            for (int l = 0; l <= j; ++l) {
+                if (RKF_A[j][l] == 0.0) continue;
+                const double term = RKF_A[j][l] * k[l][d];
+                acc = any ? acc + term : term;
+                any = 1;
+            }
+            y[d] = s[d] + (step * acc);
+        }
+        orbit_rate(y, k[j + 1]);
+    }
+    double s8[6], worst = 0.0;
+    const double he = step * (41.0 / 840.0);
+    for (int d = 0; d < 6; ++d) {
+        double acc = RKF_BW[0] * k[RKF_BJ[0]][d];
+        for (int m = 1; m < 7; ++m) acc = acc + (RKF_BW[m] * k[RKF_BJ[m]][d]);
+        s8[d] = s[d] + (step * acc);
+        const double e = he * ((((1.0 * k[0][d]) + (1.0 * k[10][d])) + (-1.0 * k[11][d])) + (-1.0 * k[12][d]));
+        const double q = fabs(e) / (1e-10 + (1e-10 * fmax(fabs(s8[d]), fabs(s[d]))));
+        worst = d == 0 ? q : fmax(worst, q);
+    }
+    const int ok = worst < 1.0;
+    const double shrink = 1.0 / sqrt(sqrt(sqrt(worst)));
+    *h = step * fmin(5.0, fmax(0.2, 0.9 * shrink));
+    if (ok)
+        for (int d = 0; d < 6; ++d) s[d] = s8[d];
+    const double tn = ok ? (final ? t_end : *t + step) : *t;
+    *t = tn;
+    *na = *na + (ok ? 1.0 : 0.0);
+    *nr = *nr + (ok ? 0.0 : 1.0);
+    return tn >= t_end;
+}
+
+uint32_t hko_orbit(double* s, int64_t pitch, double* t, double* h, double* n_acc, double* n_rej,
+                   const double* t_end, uint8_t* term, int64_t word, int64_t base, int64_t count) {
+    uint32_t fin = 0;
+    const int64_t trips = clamp_trips(word);
+    for (int64_t i = base; i < base + count; ++i) {
+        if (term[i]) continue;
+        double st[6];
+        for (int d = 0; d < 6; ++d) st[d] = s[d * pitch + i];
+        double ts = t[i], hs = h[i], na = n_acc[i], nr = n_rej[i];
+        int done = 0;
+        for (int64_t trip = 0; trip < trips; ++trip) {
+            done = orbit_trip(st, &ts, &hs, &na, &nr, t_end[i]);
+            if (done) break;
+        }
+        for (int d = 0; d < 6; ++d) s[d * pitch + i] = st[d];
+        t[i] = ts;
+        h[i] = hs;
+        n_acc[i] = na;
+        n_rej[i] = nr;
+        if (done) {
+            term[i] = 1;
+            ++fin;
+        }
+    }
+    return fin;
+}

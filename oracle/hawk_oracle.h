@@ -84,6 +84,15 @@ void hko_kepler(const double* e, const double* M, double* E, int32_t* iters, int
 void hko_kepler_vjp(const double* e, const double* M, const double* bar_E, double* bar_e, double* bar_M,
                     int64_t base, int64_t count);
 
+/* Stepping kernels (automatic: the fused_steps word `word`; hawk/trace/steps.py):
+ * advance the samples of [base, base + count) not finished on entry, mark and
+ * count the ones that finish; returns that count. */
+uint32_t hko_oscillator(double* x, double* v, double* k, const double* nstop, const double* omega,
+                        const double* zeta, uint8_t* term, double dt, int64_t word, int64_t base,
+                        int64_t count);
+uint32_t hko_orbit(double* s, int64_t pitch, double* t, double* h, double* n_acc, double* n_rej,
+                   const double* t_end, uint8_t* term, int64_t word, int64_t base, int64_t count);
+
 #ifdef __cplusplus
 }
 #endif

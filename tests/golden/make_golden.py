@@ -26,6 +26,10 @@ sys.path.insert(0, str(HERE.parent.parent))
 
 N = {"energy": 96, "poly_loss": 160, "gravity": 96, "spd_solve": 48, "kepler": 128}
 SEED = 20261201
+#: fused_steps words of the stepping fixtures (1: the single step; 0 and a
+#: negative word run no trip; the rest run up to that many).
+OSC_WORDS = (1, 0, -2, 5, 30)
+ORB_WORDS = (1, 9, 40)
 
 
 def main() -> int:
@@ -110,6 +114,35 @@ def main() -> int:
             cells[f"{op}_{n}"] = np.float64(_cells.finish(hi, comp, op))
         cells[f"sum32_{n}"] = np.float32(_cells.finish(hi.astype(np.float32), comp.astype(np.float32), "sum"))
     np.savez(HERE / "cells.npz", **cells)
+
+    # s1/s2 automatic stepping kernels: one launch per fused_steps word, each
+    # sample evaluated from the same start (the interpreter runs the fused
+    # loop's trips; word 1 is the single step).  Samples finished on entry are
+    # left out: the mask guard is the entry's, not the IR's.
+    steps = {}
+    w = workloads.oscillator(48, SEED, stop_max=24)
+    osc = configs.KERNELS["oscillator"][0]
+    steps.update({f"osc_{k}": (np.asarray(v) if k != "dt" else np.float64(v)) for k, v in w.items()})
+    for word in OSC_WORDS:
+        sinks = osc.one_step.sinks if word == 1 else osc.sinks
+        envs = [{**{k: w[k][i] for k in ("omega", "zeta", "nstop", "x", "v", "k")}, "dt": w["dt"],
+                 "terminated": False, "fused_steps": np.array([word]),
+                 "finished_count": np.array([0], dtype=np.uint32)} for i in range(48)]
+        got = per_sample(sinks, envs, ["x", "v", "k", "terminated"])
+        for k in ("x", "v", "k", "terminated"):
+            steps[f"osc_w{word}_{k}"] = got[k]
+    w = workloads.orbit(12, SEED)
+    orb = configs.KERNELS["orbit"][0]
+    steps.update({f"orb_{k}": np.asarray(v) for k, v in w.items()})
+    for word in ORB_WORDS:
+        sinks = orb.one_step.sinks if word == 1 else orb.sinks
+        envs = [{"s": w["s"][:, i], **{k: w[k][i] for k in ("t", "h", "n_acc", "n_rej", "t_end")},
+                 "terminated": False, "fused_steps": np.array([word]),
+                 "finished_count": np.array([0], dtype=np.uint32)} for i in range(12)]
+        got = per_sample(sinks, envs, ["s", "t", "h", "n_acc", "n_rej", "terminated"])
+        for k in ("s", "t", "h", "n_acc", "n_rej", "terminated"):
+            steps[f"orb_w{word}_{k}"] = got[k]
+    np.savez(HERE / "steps.npz", **steps)
     _ = Kernel, jvp
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)

@@ -122,3 +122,55 @@ def test_a_planted_fault_in_the_oracle_is_caught(golden):
     v[0, 5] *= 1.0 + 1e-9
     with pytest.raises(AssertionError):
         close(oracle.energy(v), g["out"])
+
+
+OSC_WORDS = (1, 0, -2, 5, 30)
+ORB_WORDS = (1, 9, 40)
+
+
+@pytest.mark.parametrize("word", OSC_WORDS)
+def test_oscillator_golden(golden, word):
+    """The automatic RK4 oscillator, one launch with each fused_steps word, against
+    the interpreter's single step (word 1) and fused loop: bit-identical (the
+    same operations in the same order), finished samples marked and counted."""
+    g = golden("steps")
+    planes = {k: np.array(g[f"osc_{k}"], copy=True) for k in ("x", "v", "k", "nstop", "omega", "zeta")}
+    planes["terminated"] = np.zeros(planes["x"].shape[0], dtype=bool)
+    fin = oracle.oscillator(planes, float(g["osc_dt"]), word)
+    for k in ("x", "v", "k"):
+        np.testing.assert_array_equal(planes[k], g[f"osc_w{word}_{k}"])
+    want_term = g[f"osc_w{word}_terminated"].astype(bool)
+    np.testing.assert_array_equal(planes["terminated"], want_term)
+    assert fin == int(want_term.sum())
+
+
+@pytest.mark.parametrize("word", ORB_WORDS)
+def test_orbit_golden(golden, word):
+    """The automatic Fehlberg 7(8) orbit kernel (accepted and rejected attempts,
+    samples finishing at their final time) against the interpreter: bit-identical."""
+    g = golden("steps")
+    planes = {k: np.array(g[f"orb_{k}"], copy=True) for k in ("s", "t", "h", "n_acc", "n_rej", "t_end")}
+    planes["terminated"] = np.zeros(planes["t"].shape[0], dtype=bool)
+    fin = oracle.orbit(planes, word)
+    for k in ("s", "t", "h", "n_acc", "n_rej"):
+        np.testing.assert_array_equal(planes[k], g[f"orb_w{word}_{k}"])
+    want_term = g[f"orb_w{word}_terminated"].astype(bool)
+    np.testing.assert_array_equal(planes["terminated"], want_term)
+    assert fin == int(want_term.sum())
+    if word == 40:
+        assert planes["n_rej"].sum() > 0 and fin > 0          # the fixture exercises rejects and finishes
+
+
+def test_stepping_samples_finished_on_entry_are_left_alone(golden):
+    """A sample finished on entry is skipped: no plane moves and it is not counted."""
+    g = golden("steps")
+    planes = {k: np.array(g[f"osc_{k}"], copy=True) for k in ("x", "v", "k", "nstop", "omega", "zeta")}
+    n = planes["x"].shape[0]
+    planes["terminated"] = (np.arange(n) % 5) == 2
+    before = {k: planes[k].copy() for k in ("x", "v", "k")}
+    fin = oracle.oscillator(planes, float(g["osc_dt"]), 30)
+    skip = (np.arange(n) % 5) == 2
+    for k in ("x", "v", "k"):
+        np.testing.assert_array_equal(planes[k][skip], before[k][skip])
+        np.testing.assert_array_equal(planes[k][~skip], g[f"osc_w30_{k}"][~skip])
+    assert fin == int(g["osc_w30_terminated"].astype(bool)[~skip].sum())
