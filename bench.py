@@ -414,6 +414,112 @@ def run_configs(local: int) -> dict:
     return out
 
 
+# ------------------------------------------------------------ stepping kernels
+def run_steps(local: int, cpu_threads: int | None = None) -> dict:
+    """The automatic stepping kernels integrated to completion: every sample from
+    its start until it finishes, (a) by a runner of fused launches of up to 64
+    steps (the reference's runner bound, hawk/trace/steps.py AUTO_K_MAX), one
+    4-byte counter read per launch, and (b) by one persistent launch.  Reports
+    samples/s, steps/s (steps = trips run), the persistent entry's lane fill
+    (steps run / lane slots offered), and the oracle on the host cores over a
+    sample of the same ensemble."""
+    import torch
+
+    from hawk_b200 import runtime, workloads
+
+    dev = torch.device("cuda", local)
+    out = {}
+    threads = cpu_threads or os.cpu_count() or 1
+    for name, names, extra in (("oscillator", ("x", "v", "k", "nstop", "omega", "zeta", "terminated"), ("dt",)),
+                               ("orbit", ("s", "t", "h", "n_acc", "n_rej", "t_end", "terminated"), ())):
+        n = workloads.FULL_N[name]
+        w = (workloads.oscillator(n, seed=1, stop_max=256) if name == "oscillator" else workloads.orbit(n, seed=1))
+        k = runtime.load(BUNDLES, name, "float64", local)
+        values = {e: w[e] for e in extra}
+
+        def fresh():
+            return {key: torch.as_tensor(np.ascontiguousarray(w[key]), device=dev) for key in names}
+
+        def word(v):
+            return torch.tensor([v], dtype=torch.int64, device=dev)
+
+        res = {"n": n}
+        # (a) runner of fused launches, up to 64 steps each
+        for rep in range(2):                         # the first run warms up
+            planes = fresh()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            launches, done = 0, int(w["terminated"].sum())
+            fin = torch.zeros(1, dtype=torch.uint32, device=dev)
+            while done < n and launches < 10000:
+                fin.zero_()
+                runtime.run(k, **planes, **values, fused_steps=word(64), finished_count=fin)
+                done += int(fin.item())
+                launches += 1
+            b.record()
+            b.synchronize()
+            ms_fused = a.elapsed_time(b)
+        steps_taken = _trips(name, w, {key: v.cpu().numpy() for key, v in planes.items()})
+        res["fused_runner"] = {"ms": round(ms_fused, 3), "launches": launches,
+                               "samples_per_s": n / (ms_fused * 1e-3), "steps_per_s": steps_taken / (ms_fused * 1e-3)}
+        # (b) one persistent launch, every sample to its finish
+        for rep in range(2):
+            planes = fresh()
+            util = torch.zeros(2, dtype=torch.uint64, device=dev)
+            stepsum = torch.zeros(1, dtype=torch.uint64, device=dev)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            runtime.run_persist(k, **planes, **values, fused_steps=word(1 << 20), util=util, stepsum=stepsum)
+            b.record()
+            b.synchronize()
+            ms_p = a.elapsed_time(b)
+        u = util.cpu().numpy().astype(np.float64)
+        steps_p = float(stepsum.cpu().numpy()[0])
+        res["persistent"] = {"ms": round(ms_p, 3), "samples_per_s": n / (ms_p * 1e-3),
+                             "steps_per_s": steps_p / (ms_p * 1e-3), "lane_fill": round(u[0] / max(u[1], 1.0), 4),
+                             "grid": k.persist.info(n)["grid"], "regs": k.persist.info(n)["regs"],
+                             "chunk": runtime.default_chunk(k),
+                             "step_fp64_ops": k.sidecar["b200"].get("step_fp64_ops")}
+        res["steps"] = int(steps_p)
+        res["mean_steps"] = round(steps_p / n, 3)
+        ops = k.sidecar["b200"].get("step_fp64_ops") or 0
+        # FP64 ops/s against the nominal non-FMA issue rate: 64 FP64 lanes per SM
+        # per clock (the body is compiled without contraction, one op per instruction)
+        sms = torch.cuda.get_device_properties(local).multi_processor_count
+        nominal = sms * 64 * 1.965e9
+        res["persistent"]["fp64_ops_per_s"] = ops * steps_p / (ms_p * 1e-3)
+        res["persistent"]["fp64_frac_of_nominal"] = round(ops * steps_p / (ms_p * 1e-3) / nominal, 4)
+        # the oracle on the host cores, a bounded sample of the ensemble
+        import oracle
+
+        m = min(n, 1 << 18) if name == "oscillator" else min(n, 1 << 14)
+        warm = {key: np.array(np.asarray(w[key])[..., :1], copy=True) for key in names}
+        if name == "oscillator":                     # builds and loads the oracle before the clock starts
+            oracle.oscillator(warm, w["dt"], 1)
+        else:
+            oracle.orbit(warm, 1)
+        ws = {key: np.array(np.asarray(w[key])[..., :m], copy=True) for key in names}
+        t0 = time.perf_counter()
+        if name == "oscillator":
+            oracle.oscillator(ws, w["dt"], 1 << 20, threads=threads)
+        else:
+            oracle.orbit(ws, 1 << 20, threads=threads)
+        dt = time.perf_counter() - t0
+        res["cpu"] = {"samples_per_s": m / dt, "steps_per_s": _trips(name, {key: np.asarray(w[key])[..., :m]
+                                                                              for key in names}, ws) / dt,
+                      "cores": threads, "sample": m, "kind": "port"}
+        out[name] = res
+    return out
+
+
+def _trips(name, before, after) -> float:
+    if name == "oscillator":
+        return float(np.sum(after["k"] - np.asarray(before["k"])))
+    return float(np.sum((after["n_acc"] + after["n_rej"]) - (np.asarray(before["n_acc"]) + np.asarray(before["n_rej"]))))
+
+
 def run_only(name: str, n: int, steps: int, warmup: int, local: int) -> dict:
     """One benchmark kernel (``name`` of the bundles, float64) at ``n`` samples:
     seeded inputs, ``warmup`` + ``steps`` launches, the mean device time."""
@@ -549,6 +655,7 @@ def main() -> int:
     configs = None
     if world == 1 and not args.no_configs:
         configs = run_configs(local)
+        configs["stepping"] = run_steps(local)
     cpu = cpu_baseline(args.mode, args.cpu_sample) if (rank == 0 and world == 1) else None
     if rank == 0:
         line = {

@@ -409,8 +409,22 @@ def launch_cells(kernel: DeviceKernel, *, base: int = 0, count: int | None = Non
     return state, outputs, base // ROW, -(-(base + count) // ROW)
 
 
+#: Step cost (64-bit floating-point operations) from which the persistent entry
+#: claims every 4 trips instead of every 32.  Measured on the B200: the RK4
+#: oscillator (~30 per step) took 1.93 / 3.30 / 11.7 ms at chunks 32 / 4 / 1
+#: (claims cost more than idle lanes), the Fehlberg 7(8) orbit (~1000 per step)
+#: 4.24 / 3.20 / 3.57 ms (a finished lane idling to the chunk's end costs more).
+HEAVY_STEP_FP64_OPS = 256
+
+
+def default_chunk(kernel: DeviceKernel) -> int:
+    """Trips between claims for ``kernel``'s persistent entry (see HEAVY_STEP_FP64_OPS)."""
+    ops = kernel.sidecar["b200"].get("step_fp64_ops") or 0
+    return 4 if ops >= HEAVY_STEP_FP64_OPS else 32
+
+
 def run_persist(kernel: DeviceKernel, *, base: int = 0, count: int | None = None,
-                n_samples: int | None = None, chunk: int = 32, grid: int = 0, steps=None, stepsum=None,
+                n_samples: int | None = None, chunk: int | None = None, grid: int = 0, steps=None, stepsum=None,
                 util=None, stream=None, **arrays):
     """Run an automatic stepping kernel's persistent entry over ``[base, base + count)``.
 
@@ -422,11 +436,14 @@ def run_persist(kernel: DeviceKernel, *, base: int = 0, count: int | None = None
     steps run and the slot fill when given (each zeroed by the caller).  The
     finished counter -- bound, or ``kernel.finished`` -- holds the batch's
     finished count afterwards, samples finished on entry included.  Returns
-    the claim counter (a device uint32)."""
+    the claim counter (a device uint32).  ``chunk`` defaults by the step's cost
+    (``default_chunk``)."""
     import torch
 
     if kernel.persist is None:
         raise HawkError(f"kernel {kernel.name!r} is not an automatic stepping kernel; it has no persistent entry")
+    if chunk is None:
+        chunk = default_chunk(kernel)
     if chunk < 0:
         raise HawkError(f"chunk={chunk}: the trips between claims is a count (0: whole samples)")
     for label, t, dtype, cells in (("steps", steps, torch.uint32, 1), ("stepsum", stepsum, torch.uint64, 1),

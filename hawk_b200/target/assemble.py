@@ -20,7 +20,7 @@ import re
 from dataclasses import dataclass, field
 
 from ..errors import HawkError
-from .persist import SUFFIX as PERSIST_SUFFIX, persist_entry
+from .persist import SUFFIX as PERSIST_SUFFIX, persist_entry, step_fp64_ops
 from .wrapper import B200, StagePlan, lane_frame_staged, sample_sum_store
 from .writer import B200_WRITER, body_text
 
@@ -165,7 +165,8 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
                 digest=hashlib.sha256(text.encode()).hexdigest(),
                 notes={"dynamic_smem": smem, "staged": plan is not None,
                        "stages": plan.stages if plan is not None else 0, "min_blocks": min_blocks or 0,
-                       "persist": f"{name}{PERSIST_SUFFIX}" if persist is not None else None})
+                       "persist": f"{name}{PERSIST_SUFFIX}" if persist is not None else None,
+                       "step_fp64_ops": step_fp64_ops(kernel) if persist is not None else None})
 
 
 _IDENT = re.compile(r"[A-Za-z_][A-Za-z0-9_]*")

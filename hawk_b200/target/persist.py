@@ -62,6 +62,17 @@ def _carry_type(ttype) -> str:
     return body_text(carry_type(ttype))
 
 
+def step_fp64_ops(kernel) -> int | None:
+    """The 64-bit floating-point operations of one step of an automatic kernel
+    (the renderer's count, ``LaneSplit.fp64_ops``), else ``None``."""
+    from hawk.emit.render import render_lane_split
+
+    if getattr(kernel, "one_step", None) is None or getattr(kernel.walk, "finish", None) is None:
+        return None
+    split = render_lane_split(kernel.sinks, kernel.walk, kind=getattr(kernel, "kind", None), writer=B200_WRITER)
+    return None if split is None else int(split.fp64_ops)
+
+
 def persist_entry(kernel, name: str, wrapper) -> str | None:
     """The text of ``<name>_persist`` for an automatic kernel, else ``None``."""
     from hawk.emit.render import render_lane_split

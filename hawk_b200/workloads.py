@@ -20,7 +20,8 @@ from __future__ import annotations
 
 import numpy as np
 
-FULL_N = {"energy": 1 << 24, "poly_loss": 1 << 26, "gravity": 1 << 23, "spd_solve": 1 << 20, "kepler": 1 << 24}
+FULL_N = {"energy": 1 << 24, "poly_loss": 1 << 26, "gravity": 1 << 23, "spd_solve": 1 << 20, "kepler": 1 << 24,
+          "oscillator": 1 << 22, "orbit": 1 << 20}
 
 
 def energy(n: int, seed: int = 0) -> dict:
