@@ -520,6 +520,40 @@ def _trips(name, before, after) -> float:
     return float(np.sum((after["n_acc"] + after["n_rej"]) - (np.asarray(before["n_acc"]) + np.asarray(before["n_rej"]))))
 
 
+def run_only_steps(name: str, n: int, steps: int, warmup: int, local: int, persist: bool) -> dict:
+    """A stepping kernel's ensemble of ``n`` samples integrated to completion,
+    ``warmup`` + ``steps`` times from the same start: by one persistent launch
+    each (``persist``), else by one fused launch of 64 steps (the samples that
+    finish within it).  The mean device time of a timed run."""
+    import torch
+
+    from hawk_b200 import runtime, workloads
+
+    dev = torch.device("cuda", local)
+    w = workloads.oscillator(n, seed=1, stop_max=256) if name == "oscillator" else workloads.orbit(n, seed=1)
+    names = (("x", "v", "k", "nstop", "omega", "zeta", "terminated") if name == "oscillator"
+             else ("s", "t", "h", "n_acc", "n_rej", "t_end", "terminated"))
+    values = {"dt": w["dt"]} if name == "oscillator" else {}
+    k = runtime.load(BUNDLES, name, "float64", local)
+    word = torch.tensor([1 << 20 if persist else 64], dtype=torch.int64, device=dev)
+    times = []
+    for rep in range(warmup + steps):
+        planes = {key: torch.as_tensor(np.ascontiguousarray(w[key]), device=dev) for key in names}
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        if persist:
+            runtime.run_persist(k, **planes, **values, fused_steps=word)
+        else:
+            runtime.run(k, **planes, **values, fused_steps=word)
+        b.record()
+        b.synchronize()
+        if rep >= warmup:
+            times.append(a.elapsed_time(b))
+    return {"kernel": name + ("_persist" if persist else ""), "n": n, "ms": statistics.mean(times),
+            "launches": warmup + steps}
+
+
 def run_only(name: str, n: int, steps: int, warmup: int, local: int) -> dict:
     """One benchmark kernel (``name`` of the bundles, float64) at ``n`` samples:
     seeded inputs, ``warmup`` + ``steps`` launches, the mean device time."""
@@ -594,9 +628,16 @@ def cpu_baseline(mode: str, sample_n: int) -> dict:
         run()
         times.append(time.perf_counter() - t0)
     best = min(times)
+    # the serial oracle shape (one host thread), on a quarter of the sample
+    one = cpu_poly_step(max(sample_n // 4, 1), 1, mode)
+    t0 = time.perf_counter()
+    one()
+    serial = max(sample_n // 4, 1) / (time.perf_counter() - t0)
     return {"value": sample_n / best, "unit": UNIT, "cores": threads, "kind": "port",
+            "value_1_thread": serial,
             "sample": f"{sample_n} samples of the same fwd+VJP (rows + cells), best of 3, "
-                      f"oracle/hawk_oracle.c -O3 -march=native -ffp-contract=off on {threads} threads"}
+                      f"oracle/hawk_oracle.c -O3 -march=native -ffp-contract=off on {threads} threads; "
+                      f"value_1_thread: {max(sample_n // 4, 1)} samples on one thread"}
 
 
 def run_reference(args, world, rank) -> None:
@@ -638,6 +679,8 @@ def main() -> int:
     ap.add_argument("--no-configs", action="store_true", help="skip the per-config table")
     ap.add_argument("--cpu-sample", type=int, default=1 << 23)
     ap.add_argument("--only", default=None, help="time one benchmark kernel at --n samples (profiling runs)")
+    ap.add_argument("--persist", action="store_true",
+                    help="with --only oscillator|orbit: the persistent entry, every sample to its finish")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_env()
@@ -646,6 +689,10 @@ def main() -> int:
         return 0
     import torch
 
+    if args.only in ("oscillator", "orbit"):
+        print(json.dumps(run_only_steps(args.only, args.n, args.steps, args.warmup, local, args.persist)),
+              flush=True)
+        return 0
     if args.only:
         print(json.dumps(run_only(args.only, args.n, args.steps, args.warmup, local)), flush=True)
         return 0
