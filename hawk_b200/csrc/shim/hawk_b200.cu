@@ -102,6 +102,7 @@ struct hkb_entry {
     std::string name;
     int regs = 0;
     int blocks_per_sm = 0;
+    int block = kBlock;          // threads per block this entry launches with
     unsigned dynamic_smem = 0;   // bytes per block the unit exports (hk_dynamic_smem_bytes)
 };
 
@@ -277,12 +278,27 @@ int hkb_library_entry(hkb_library* lib, const char* name, hkb_entry** out) {
     } else {
         cudaGetLastError();
     }
-    e2 = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&entry->blocks_per_sm,
-                                                       reinterpret_cast<const void*>(kernel), kBlock,
-                                                       entry->dynamic_smem);
-    if (e2 != cudaSuccess) {
-        delete entry;
-        return cuda_fail(e2, "computing the entry's occupancy");
+    // Threads per block: the size that keeps the most warps resident per SM (the
+    // register file is the limit of a heavy entry: at 98 registers, 256-thread
+    // blocks leave 16 warps, 32-thread blocks 19), the larger on a tie.  Every
+    // frame indexes by blockDim; a staged entry's tiles assume 256 threads.
+    const int candidates[] = {256, 128, 96, 64, 32};
+    int best_warps = -1;
+    for (int b : candidates) {
+        if (entry->dynamic_smem != 0 && b != kBlock) continue;
+        int bps = 0;
+        e2 = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, reinterpret_cast<const void*>(kernel), b,
+                                                           entry->dynamic_smem);
+        if (e2 != cudaSuccess) {
+            delete entry;
+            return cuda_fail(e2, "computing the entry's occupancy");
+        }
+        const int warps = bps * (b / 32);
+        if (warps > best_warps) {
+            best_warps = warps;
+            entry->block = b;
+            entry->blocks_per_sm = bps;
+        }
     }
     if (entry->blocks_per_sm < 1) entry->blocks_per_sm = 1;
     *out = entry;
@@ -291,7 +307,7 @@ int hkb_library_entry(hkb_library* lib, const char* name, hkb_entry** out) {
 
 static int64_t grid_for(const hkb_entry* entry, int64_t count) {
     const int64_t cap = static_cast<int64_t>(entry->lib->sms) * entry->blocks_per_sm;
-    int64_t need = (count + kBlock - 1) / kBlock;
+    int64_t need = (count + entry->block - 1) / entry->block;
     if (need < 1) need = 1;
     return need < cap ? need : cap;
 }
@@ -301,7 +317,7 @@ int hkb_entry_info(hkb_entry* entry, int* regs, int* blocks_per_sm, int* block, 
     if (entry == nullptr) return fail(HKB_ERR_ARGUMENT, "hkb_entry_info: null entry");
     if (regs) *regs = entry->regs;
     if (blocks_per_sm) *blocks_per_sm = entry->blocks_per_sm;
-    if (block) *block = kBlock;
+    if (block) *block = entry->block;
     if (grid) *grid = grid_for(entry, count);
     return HKB_OK;
 }
@@ -424,7 +440,7 @@ int hkb_entry_launch(hkb_entry* entry, hkb_argblock* block, int64_t base, int64_
     args.push_back(&c);
     args.push_back(&ns);
     const dim3 grid(static_cast<unsigned>(grid_for(entry, count)));
-    const cudaError_t err = cudaLaunchKernel(reinterpret_cast<const void*>(entry->kernel), grid, dim3(kBlock),
+    const cudaError_t err = cudaLaunchKernel(reinterpret_cast<const void*>(entry->kernel), grid, dim3(entry->block),
                                              args.data(), entry->dynamic_smem, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return cuda_fail(err, "launching the entry");
     return HKB_OK;
@@ -459,7 +475,7 @@ int hkb_entry_launch_persist(hkb_entry* entry, hkb_argblock* block, int64_t base
     // a resident grid: every claim loop runs until the counter passes count
     const int64_t g = grid > 0 ? grid : grid_for(entry, count);
     const cudaError_t err = cudaLaunchKernel(reinterpret_cast<const void*>(entry->kernel),
-                                             dim3(static_cast<unsigned>(g)), dim3(kBlock), args.data(),
+                                             dim3(static_cast<unsigned>(g)), dim3(entry->block), args.data(),
                                              entry->dynamic_smem, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return cuda_fail(err, "launching the persistent entry");
     return HKB_OK;

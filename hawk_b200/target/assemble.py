@@ -21,6 +21,7 @@ from dataclasses import dataclass, field
 
 from ..errors import HawkError
 from .persist import SUFFIX as PERSIST_SUFFIX, persist_entry, step_fp64_ops
+from .refill import refill_frame
 from .wrapper import B200, StagePlan, lane_frame_staged, sample_sum_store
 from .writer import B200_WRITER, body_text
 
@@ -104,6 +105,7 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
         raise HawkError(f"{name!r}: an automatic stepping kernel with sample sums is not built on the b200 target")
     wrapper = B200
     smem = 0
+    frame_note = None
     elem_bytes = 8 if mode == "float64" else 4
     if sums:
         elem = element_spelling(sums[0].ttype.dtype)
@@ -125,7 +127,10 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
             smem = plan.smem_bytes
         else:
             plan = None
-            loop = [wrapper.index_prologue(), body, wrapper.index_epilogue()]
+            refill = refill_frame(kernel, walk) if one_step is None else None
+            loop = [refill] if refill is not None else [wrapper.index_prologue(), body, wrapper.index_epilogue()]
+            if refill is not None:
+                frame_note = "refill"
         if one_step is not None:
             # an automatic kernel (steps="auto", hawk/trace/steps.py): one uniform
             # branch per launch on the fused_steps word -- 1 runs the single step's
@@ -166,7 +171,8 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
                 notes={"dynamic_smem": smem, "staged": plan is not None,
                        "stages": plan.stages if plan is not None else 0, "min_blocks": min_blocks or 0,
                        "persist": f"{name}{PERSIST_SUFFIX}" if persist is not None else None,
-                       "step_fp64_ops": step_fp64_ops(kernel) if persist is not None else None})
+                       "step_fp64_ops": step_fp64_ops(kernel) if persist is not None else None,
+                       "lane_refill": frame_note == "refill"})
 
 
 _IDENT = re.compile(r"[A-Za-z_][A-Za-z0-9_]*")

@@ -126,6 +126,7 @@ def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "flo
         "min_blocks": unit.notes.get("min_blocks", 0),
         "persist": unit.notes.get("persist"),
         "step_fp64_ops": unit.notes.get("step_fp64_ops"),
+        "lane_refill": unit.notes.get("lane_refill", False),
         "sample_sums": [{"name": n, "op": op, "companion": comp} for n, op, comp in unit.sums],
         "slots": _slot_records(kernel.walk),
         "nvrtc_options": [o for o in options() if not o.startswith("-I")],
