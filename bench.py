@@ -133,8 +133,20 @@ def init_dist(world: int, local: int):
 
     if world > 1 and not dist.is_initialized():
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        # the communicators come up here (device_id: eager init); what the library
+        # prints while they do goes to stderr, so stdout holds the one JSON line
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     return dist if world > 1 else None
 
 
@@ -199,6 +211,8 @@ class PolyStep:
         self.leaf_hi = torch.empty((3, self.leaves), dtype=self.tdt, device=self.dev)
         self.leaf_comp = torch.empty((3, self.leaves), dtype=self.tdt, device=self.dev)
         self.cells = torch.empty(3, dtype=self.tdt, device=self.dev)
+        self.pack = torch.empty((2, 3), dtype=self.tdt, device=self.dev)
+        self.gathered = torch.empty((max(world, 1), 2, 3), dtype=self.tdt, device=self.dev)
         self.hi_ptrs = [self.row_planes[k].data_ptr() for k in ("bar_a", "bar_b", "bar_c")]
         self.comp_ptrs = [self.row_planes[k + "_comp"].data_ptr() for k in ("bar_a", "bar_b", "bar_c")]
 
@@ -218,6 +232,10 @@ class PolyStep:
                          self.leaf_hi.data_ptr(), self.leaf_comp.data_ptr(), stream)
         if marks:
             marks[3].record()
+        if self.world > 1 and sharded.aligned(self.counts):
+            sharded.finish_subtrees("sum", self.mode, 3, self.leaf_hi, self.leaf_comp, self.leaves, self.cells,
+                                    stream=stream, pack=self.pack, gathered=self.gathered)
+            return
         if self.world > 1:
             hi, comp = sharded.gather_leaves(self.leaf_hi, self.leaf_comp, self.counts)
             total = hi.shape[1]

@@ -46,6 +46,8 @@ SIGNATURES = {
     "hkb_cells_leaves": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _c.POINTER(_P), _c.POINTER(_P),
                                     _c.c_int64, _P, _P, _P]),
     "hkb_cells_tree": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _P, _P, _c.c_int64, _P, _P]),
+    "hkb_cells_tree_ex": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _P, _P, _c.c_int64, _c.c_int64, _c.c_int64,
+                                     _P, _P, _P]),
     "hkb_cells_scratch_bytes": (_c.c_size_t, [_c.c_int, _c.c_int, _c.c_int64]),
     "hkb_cells_finish": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _c.POINTER(_P), _c.POINTER(_P),
                                     _c.c_int64, _P, _P, _P]),
@@ -223,3 +225,13 @@ def cells_tree(op: str, dtype: str, ncols: int, leaf_hi: int, leaf_comp: int, le
     check(lib().hkb_cells_tree(OP[op], DTYPE[dtype], int(ncols), ctypes.c_void_p(int(leaf_hi)),
                                ctypes.c_void_p(int(leaf_comp)), int(leaves), ctypes.c_void_p(int(out)),
                                ctypes.c_void_p(int(stream) or None)), "hkb_cells_tree")
+
+
+def cells_tree_ex(op: str, dtype: str, ncols: int, hi: int, comp: int, count: int, elem_stride: int,
+                  col_stride: int, out: int, out_comp: int = 0, stream: int = 0) -> None:
+    """The pairwise levels over strided partials; the root's (hi, comp) pair into
+    ``out`` / ``out_comp`` when ``out_comp`` is given, else hi + comp into ``out``."""
+    vp = lambda v: ctypes.c_void_p(int(v) or None)   # noqa: E731
+    check(lib().hkb_cells_tree_ex(OP[op], DTYPE[dtype], int(ncols), vp(hi), vp(comp), int(count),
+                                  int(elem_stride), int(col_stride), vp(out), vp(out_comp), vp(stream)),
+          "hkb_cells_tree_ex")

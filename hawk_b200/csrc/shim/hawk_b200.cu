@@ -568,26 +568,35 @@ __global__ void __launch_bounds__(hk::ss::kSlots) leaves_kernel(Columns cols, lo
 
 // One block per column: the pairwise levels over the leaves, in place (the
 // partial of level s sits at index k * 2^s), then hi + comp (hawk/_cells.py:108-119).
+// Leaf j of column k is at [k * col_stride + j * elem_stride].  With out_comp
+// the root's (hi, comp) pair is written instead of hi + comp: the root of an
+// aligned subtree, which a later tree joins with the others.
 template <class T, int OP>
-__global__ void __launch_bounds__(1024) tree_kernel(T* leaf_hi, T* leaf_comp, long long leaves, T* out) {
+__global__ void __launch_bounds__(1024) tree_kernel(T* leaf_hi, T* leaf_comp, long long leaves, long long elem_stride,
+                                                   long long col_stride, T* out, T* out_comp) {
     const int col = blockIdx.x;
-    T* h = leaf_hi + col * leaves;
-    T* c = leaf_comp + col * leaves;
+    T* h = leaf_hi + col * col_stride;
+    T* c = leaf_comp + col * col_stride;
     for (long long st = 1; st < leaves; st <<= 1) {
         for (long long idx = static_cast<long long>(threadIdx.x) * 2 * st; idx < leaves;
              idx += static_cast<long long>(blockDim.x) * 2 * st) {
             if (idx + st < leaves) {
-                T a = h[idx], ac = c[idx];
-                hk::ss::tree_join<OP>(a, ac, h[idx + st], c[idx + st]);
-                h[idx] = a;
-                c[idx] = ac;
+                T a = h[idx * elem_stride], ac = c[idx * elem_stride];
+                hk::ss::tree_join<OP>(a, ac, h[(idx + st) * elem_stride], c[(idx + st) * elem_stride]);
+                h[idx * elem_stride] = a;
+                c[idx * elem_stride] = ac;
             }
         }
         __syncthreads();
     }
     if (threadIdx.x == 0) {
         const T v = h[0];
-        out[col] = (OP == hk::ss::kSum) ? (hk::ss::finite(v) ? v + c[0] : v) : v;
+        if (out_comp != nullptr) {
+            out[col] = v;
+            out_comp[col] = c[0];
+        } else {
+            out[col] = (OP == hk::ss::kSum) ? (hk::ss::finite(v) ? v + c[0] : v) : v;
+        }
     }
 }
 
@@ -607,15 +616,23 @@ int launch_leaves(int op, const Columns& cols, int ncols, int64_t rows, int64_t 
 }
 
 template <class T>
-int launch_tree(int op, int ncols, void* lh, void* lc, int64_t leaves, void* out, cudaStream_t stream) {
+int launch_tree(int op, int ncols, void* lh, void* lc, int64_t leaves, int64_t elem_stride, int64_t col_stride,
+                void* out, void* out_comp, cudaStream_t stream) {
     T* h = static_cast<T*>(lh);
     T* c = static_cast<T*>(lc);
     T* o = static_cast<T*>(out);
+    T* oc = static_cast<T*>(out_comp);
     const int threads = 1024;
     switch (op) {
-        case HKB_OP_SUM: tree_kernel<T, hk::ss::kSum><<<ncols, threads, 0, stream>>>(h, c, leaves, o); break;
-        case HKB_OP_MAX: tree_kernel<T, hk::ss::kMax><<<ncols, threads, 0, stream>>>(h, c, leaves, o); break;
-        default: tree_kernel<T, hk::ss::kMin><<<ncols, threads, 0, stream>>>(h, c, leaves, o); break;
+        case HKB_OP_SUM:
+            tree_kernel<T, hk::ss::kSum><<<ncols, threads, 0, stream>>>(h, c, leaves, elem_stride, col_stride, o, oc);
+            break;
+        case HKB_OP_MAX:
+            tree_kernel<T, hk::ss::kMax><<<ncols, threads, 0, stream>>>(h, c, leaves, elem_stride, col_stride, o, oc);
+            break;
+        default:
+            tree_kernel<T, hk::ss::kMin><<<ncols, threads, 0, stream>>>(h, c, leaves, elem_stride, col_stride, o, oc);
+            break;
     }
     HKB_CUDA(cudaGetLastError(), "launching the tree stage");
     return HKB_OK;
@@ -664,8 +681,24 @@ int hkb_cells_tree(int op, int dtype, int ncols, void* leaf_hi, void* leaf_comp,
     if (leaf_hi == nullptr || leaf_comp == nullptr || out == nullptr)
         return fail(HKB_ERR_ARGUMENT, "hkb_cells_tree: null pointer");
     auto s = static_cast<cudaStream_t>(stream);
-    return dtype == HKB_F64 ? launch_tree<double>(op, ncols, leaf_hi, leaf_comp, leaves, out, s)
-                            : launch_tree<float>(op, ncols, leaf_hi, leaf_comp, leaves, out, s);
+    return dtype == HKB_F64 ? launch_tree<double>(op, ncols, leaf_hi, leaf_comp, leaves, 1, leaves, out, nullptr, s)
+                            : launch_tree<float>(op, ncols, leaf_hi, leaf_comp, leaves, 1, leaves, out, nullptr, s);
+}
+
+int hkb_cells_tree_ex(int op, int dtype, int ncols, void* hi, void* comp, int64_t count, int64_t elem_stride,
+                      int64_t col_stride, void* out, void* out_comp, void* stream) {
+    int status = check_cells(op, dtype, ncols);
+    if (status != HKB_OK) return status;
+    if (count < 1) return fail(HKB_ERR_RANGE, "a tree needs at least one leaf");
+    if (elem_stride < 1 || col_stride < 0)
+        return fail(HKB_ERR_RANGE, "strides %lld, %lld: the element stride is positive", (long long)elem_stride,
+                    (long long)col_stride);
+    if (hi == nullptr || comp == nullptr || out == nullptr)
+        return fail(HKB_ERR_ARGUMENT, "hkb_cells_tree_ex: null pointer");
+    auto s = static_cast<cudaStream_t>(stream);
+    return dtype == HKB_F64
+               ? launch_tree<double>(op, ncols, hi, comp, count, elem_stride, col_stride, out, out_comp, s)
+               : launch_tree<float>(op, ncols, hi, comp, count, elem_stride, col_stride, out, out_comp, s);
 }
 
 size_t hkb_cells_scratch_bytes(int dtype, int ncols, int64_t rows) {

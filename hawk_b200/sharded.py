@@ -8,8 +8,12 @@ exchange is for cells (sample sums such as Param gradients):
 
 1. each rank writes the 32-sample rows of its shard and folds them into one
    (hi, comp) partial per leaf of 4096 rows (``hkb_cells_leaves``);
-2. the ranks all-gather their leaf partials (NCCL over NVLink on B200s);
-3. every rank folds all leaves in rank order with the same pairwise tree
+2. when every rank holds the same power-of-two number of leaves, each folds
+   its own leaves to one (hi, comp) pair per column (an aligned subtree of the
+   one-device tree), the ranks all-gather the pairs and every rank runs the
+   last levels over them; otherwise the ranks all-gather their leaf partials
+   (NCCL over NVLink on B200s)
+3. and every rank folds all leaves in rank order with the same pairwise tree
    (``hkb_cells_tree``).
 
 Shards start on leaf boundaries (4096 rows = 131072 samples), so the gathered
@@ -64,6 +68,42 @@ def gather_leaves(leaf_hi, leaf_comp, counts, group=None):
     return both[0].contiguous(), both[1].contiguous()
 
 
+def aligned(counts) -> bool:
+    """Whether every rank holds the same power-of-two number of leaves: then each
+    rank's leaves are an aligned subtree of the one-device tree."""
+    first = counts[0]
+    return first > 0 and (first & (first - 1)) == 0 and all(c == first for c in counts)
+
+
+def finish_subtrees(op: str, mode: str, cols: int, leaf_hi, leaf_comp, leaves: int, values, group=None,
+                    stream: int = 0, pack=None, gathered=None) -> None:
+    """The cells of ``cols`` columns from every rank's ``leaves`` partials
+    (``(cols, leaves)`` tensors; ``leaves`` a power of two, the same on every
+    rank), into ``values``: this rank's tree over its own leaves to one (hi,
+    comp) pair per column, an all-gather of the pairs (``world * cols * 2``
+    values over NVLink), and the last pairwise levels over the ranks' roots.
+    The pairwise levels of the one-device tree over ``world * leaves`` leaves
+    join each rank's leaves among themselves first, so this is the same tree,
+    bit for bit (hawk/_cells.py:108-119).  ``pack`` ``(2, cols)`` and
+    ``gathered`` ``(world, 2, cols)`` may be passed preallocated."""
+    import torch
+    import torch.distributed as dist
+
+    from . import abi
+
+    world = dist.get_world_size(group)
+    if pack is None:
+        pack = torch.empty((2, cols), dtype=leaf_hi.dtype, device=leaf_hi.device)
+    if gathered is None:
+        gathered = torch.empty((world, 2, cols), dtype=leaf_hi.dtype, device=leaf_hi.device)
+    item = leaf_hi.element_size()
+    abi.cells_tree_ex(op, mode, cols, leaf_hi.data_ptr(), leaf_comp.data_ptr(), leaves, 1, leaves,
+                      pack.data_ptr(), pack.data_ptr() + cols * item, stream)
+    dist.all_gather_into_tensor(gathered, pack, group=group)
+    abi.cells_tree_ex(op, mode, cols, gathered.data_ptr(), gathered.data_ptr() + cols * item, world, 2 * cols, 1,
+                      values.data_ptr(), 0, stream)
+
+
 def run_cells(kernel, *, group=None, base: int = 0, count: int | None = None, n_samples: int | None = None,
               stream=None, **arrays) -> None:
     """``hawk_b200.runtime.run`` of a kernel with cells over this rank's shard,
@@ -91,6 +131,12 @@ def run_cells(kernel, *, group=None, base: int = 0, count: int | None = None, n_
             every = [torch.zeros_like(counts_t) for _ in range(world)]
             dist.all_gather(every, counts_t, group=group)
             counts = [int(c.item()) for c in every]
+            if aligned(counts):
+                op = kernel.sums[0]["op"] if kernel.sums else "sum"
+                finish_subtrees(op, kernel.mode, cols, state["leaf_hi"], state["leaf_comp"], leaves,
+                                state["values"], group, runtime._stream(stream, kernel.device))
+                kernel.write_cells(state["values"], outputs, stream)
+                return
             width = max(max(counts), 1)
             flat_hi = state["leaf_hi"].view(-1)
             flat_comp = state["leaf_comp"].view(-1)

@@ -151,6 +151,17 @@ int hkb_cells_leaves(int op, int dtype, int ncols, const void* const* hi, const 
                      int64_t rows, void* leaf_hi, void* leaf_comp, void* stream);
 int hkb_cells_tree(int op, int dtype, int ncols, void* leaf_hi, void* leaf_comp, int64_t leaves,
                    void* out, void* stream);
+
+/* The same pairwise levels over `count` partials per column, leaf j of column k
+ * at element [k * col_stride + j * elem_stride] of hi / comp (in place).  With
+ * out_comp non-null the root's (hi, comp) pair of each column is written to
+ * out[k] / out_comp[k] instead of hi + comp: the root of an aligned subtree of
+ * a larger tree (every rank holding the same power-of-two leaf count is one),
+ * which a later call over the subtree roots finishes bit-identically to one
+ * tree over all leaves (no counterpart in the reference: its finish is one
+ * host tree, hawk/_cells.py:94-119). */
+int hkb_cells_tree_ex(int op, int dtype, int ncols, void* hi, void* comp, int64_t count, int64_t elem_stride,
+                      int64_t col_stride, void* out, void* out_comp, void* stream);
 size_t hkb_cells_scratch_bytes(int dtype, int ncols, int64_t rows);
 int hkb_cells_finish(int op, int dtype, int ncols, const void* const* hi, const void* const* comp,
                      int64_t rows, void* scratch, void* out, void* stream);

@@ -221,6 +221,14 @@ def cells_tree(leaf_hi: np.ndarray, leaf_comp: np.ndarray, op: str = "sum") -> f
     return lib().hko_cells_tree_d(OP[op], _p(lh), _p(lc), lh.shape[0])
 
 
+def cells_tree_pair(leaf_hi: np.ndarray, leaf_comp: np.ndarray, op: str = "sum") -> tuple:
+    """The tree's root (hi, comp) pair before its final rounding (the compacting
+    levels leave it at index 0)."""
+    lh, lc = np.array(leaf_hi, dtype=np.float64), np.array(leaf_comp, dtype=np.float64)
+    lib().hko_cells_tree_d(OP[op], _p(lh), _p(lc), lh.shape[0])
+    return float(lh[0]), float(lc[0])
+
+
 def poly_loss_vjp(x, t, bar_r, a, b, c, threads: int = 1):
     """The three Param gradients (cells) and the rows they were finished from."""
     hi, comp = poly_loss_vjp_rows(x, t, bar_r, a, b, c, threads)

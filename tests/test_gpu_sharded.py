@@ -65,16 +65,19 @@ def _worlds():
     return [w for w in (2, 4, 8) if w <= max(count, 2)]
 
 
+@pytest.mark.parametrize("shape", ["ragged", "aligned"])
 @pytest.mark.parametrize("world", _worlds())
-def test_sharded_param_gradients_bit_identical_to_one_device(world):
+def test_sharded_param_gradients_bit_identical_to_one_device(world, shape):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs, {torch.cuda.device_count()} visible")
     import torch.multiprocessing as mp
 
     from hawk_b200 import sharded, workloads
 
-    # every rank holds at least one leaf; the last shard is ragged
-    n = 2 * world * sharded.LEAF_SAMPLES - 1000
+    # ragged: every rank holds at least one leaf and the last shard is short (the
+    # full gather of leaf partials); aligned: 4 leaves on every rank (each rank's
+    # subtree root is exchanged, sharded.finish_subtrees)
+    n = 2 * world * sharded.LEAF_SAMPLES - 1000 if shape == "ragged" else 4 * world * sharded.LEAF_SAMPLES
     w = workloads.poly_loss(n, seed=n)
     want, _rows = oracle.poly_loss_vjp(w["x"], w["t"], w["bar_r"], w["a"], w["b"], w["c"])
     ctx = mp.get_context("spawn")

@@ -91,3 +91,30 @@ def test_shard_ranges_cover_and_align():
                 if base + count < n:
                     assert (base + count) % sharded.LEAF_SAMPLES == 0
             assert pos == n
+
+
+@pytest.mark.parametrize("world,per", [(2, 4), (4, 8), (8, 1), (3, 16), (8, 512)])
+@pytest.mark.parametrize("op", ["sum", "max", "min"])
+def test_aligned_subtrees_finish_like_one_tree(world, per, op):
+    """When every rank holds the same power-of-two number of leaves, its leaves
+    are an aligned subtree of the one-device tree: the ranks' subtree roots
+    (hi, comp), joined by the same pairwise levels, give the one tree's cell
+    bit for bit (the exchange ``sharded.finish_subtrees`` runs on the device)."""
+    import oracle
+
+    rng = np.random.default_rng(world * 1000 + per)
+    n = world * per
+    hi = rng.standard_normal(n) * np.exp(rng.uniform(-30, 30, n))
+    comp = hi * rng.standard_normal(n) * 1e-17 if op == "sum" else np.zeros(n)
+    assert sharded.aligned([per] * world)
+    roots = [oracle.cells_tree_pair(hi[r * per:(r + 1) * per], comp[r * per:(r + 1) * per], op) for r in range(world)]
+    rh = np.array([h for h, _c in roots])
+    rc = np.array([c for _h, c in roots])
+    assert oracle.cells_tree(rh, rc, op) == oracle.cells_tree(hi, comp, op)
+
+
+def test_unequal_or_odd_leaf_counts_take_the_full_gather():
+    assert not sharded.aligned([4, 4, 3])
+    assert not sharded.aligned([6, 6])
+    assert not sharded.aligned([0, 0])
+    assert sharded.aligned([16, 16, 16])
