@@ -373,8 +373,8 @@ def run_configs(local: int) -> dict:
     def e(shape, dtype=torch.float64):
         return torch.empty(shape, dtype=dtype, device=dev)
 
-    def time_kernel(name, planes, values, n):
-        k = runtime.load(BUNDLES, name, "float64", local)
+    def time_kernel(name, planes, values, n, mode="float64", key=None):
+        k = runtime.load(BUNDLES, name, mode, local)
         bound = {key: from_torch(v) for key, v in planes.items()}
         k.check(bound, values, n)
         k.bind_all(bound, values, n)
@@ -390,11 +390,13 @@ def run_configs(local: int) -> dict:
             b.synchronize()
             times.append(a.elapsed_time(b))
         ms = statistics.median(times)
-        gbs = BYTES_F64[name] * n / (ms * 1e-3) / 1e9
+        per = BYTES_F64[name] * (0.5 if mode == "float32" else 1.0)
+        gbs = per * n / (ms * 1e-3) / 1e9
         info = k.entry.info(n)
-        out[name] = {"n": n, "ms": round(ms, 5), "samples_per_s": n / (ms * 1e-3), "gbs": round(gbs, 1),
-                     "hbm_frac": round(gbs / pk["hbm_gbs"], 4), "bytes_per_sample": BYTES_F64[name],
-                     "regs": info["regs"], "blocks_per_sm": info["blocks_per_sm"], "grid": info["grid"]}
+        out[key or name] = {"n": n, "ms": round(ms, 5), "samples_per_s": n / (ms * 1e-3), "gbs": round(gbs, 1),
+                            "hbm_frac": round(gbs / pk["hbm_gbs"], 4), "bytes_per_sample": per,
+                            "regs": info["regs"], "blocks_per_sm": info["blocks_per_sm"], "grid": info["grid"],
+                            "block": info["block"]}
 
     n = workloads.FULL_N["energy"]
     w = workloads.energy(n, 1)
@@ -403,6 +405,21 @@ def run_configs(local: int) -> dict:
     time_kernel("energy_vjp", {"v": v, "bar_out": t(w["bar_out"]), "bar_v": e((3, n))}, {}, n)
     time_kernel("energy_jvp", {"v": v, "dot_v": t(w["dot_v"]), "dot_out": e(n)}, {}, n)
     del v, w
+    # c2 in both scalar modes: the forward and the Param-gradient VJP (rows; the
+    # finish is the headline step's)
+    n = workloads.FULL_N["poly_loss"]
+    for mode, dt in (("float64", np.float64), ("float32", np.float32)):
+        w = workloads.poly_loss(n, 1, dtype=dt)
+        tdt = torch.float64 if mode == "float64" else torch.float32
+        x, tt = t(w["x"]), t(w["t"])
+        time_kernel("poly_loss", {"x": x, "t": tt, "r": e(n, tdt)}, {k: w[k] for k in ("a", "b", "c")}, n, mode,
+                    f"poly_loss.{mode}")
+        rows = -(-n // 32)
+        vp = {"x": x, "t": tt, "bar_r": t(w["bar_r"]),
+              **{k: torch.tensor([w[k]], dtype=tdt, device=dev) for k in ("a", "b", "c")},
+              **{k: e(rows, tdt) for k in ("bar_a", "bar_a_comp", "bar_b", "bar_b_comp", "bar_c", "bar_c_comp")}}
+        time_kernel("poly_loss_vjp", vp, {}, n, mode, f"poly_loss_vjp.{mode}")
+        del x, tt, vp, w
     n = workloads.FULL_N["gravity"]
     w = workloads.gravity(n, 1)
     g = {k: t(w[k]) for k in ("r1", "r2", "m1", "m2")}

@@ -25,6 +25,16 @@ s2 orbit           one adaptive Fehlberg 7(8) attempt on the two-body problem
                    (GM = 1) per step, finishing at the sample's final time;
                    the step-size factor is 0.9 * err^(-1/8), clamped to
                    [0.2, 5], with err^(-1/8) taken as three square roots
+
+Scattered commits (hawk.scatter, the VJP of a table read; several samples add
+into one slot, hk/accum.cuh):
+
+g1 gather          y = w * table[idx]; its VJP adds bar_y * w into bar_table[idx]
+g2 segment_sum     acc[i / 256] += x, the default (compensated) policy: the key
+                   is constant over aligned runs of lanes
+g3 keyed_sum       acc[key] += x over a Sorted key (runs found per warp)
+g4 histogram       acc[key] += x over any key, compensated
+g5 bitmask         acc[key] |= bits (32-bit words)
 """
 
 from __future__ import annotations
@@ -34,7 +44,7 @@ from .frontend import load
 hawk = load()
 
 import hawk.math as m  # noqa: E402
-from hawk import Int32, Kernel, Matrix, Mutable, Param, Scalar, Terminated, Vector  # noqa: E402
+from hawk import Index, Int32, Kernel, Matrix, Mutable, Param, Scalar, Sorted, Table, Terminated, UInt32, Vector  # noqa: E402,E501
 from hawk.diff import jvp, param_planes, vjp  # noqa: E402
 
 
@@ -191,6 +201,35 @@ def orbit(t_end: Scalar, terminated: Terminated, s: Mutable[Vector[6]], t: Mutab
     terminated = t_next >= t_end
 
 
+from .workloads import SEGMENT  # noqa: E402  -- samples per segment of segment_sum
+
+
+@hawk.kernel
+def gather(idx: Index, w: Scalar, table: Table[Scalar], y: Mutable[Scalar]):
+    y = w * table[idx]
+
+
+@hawk.kernel
+def segment_sum(x: Scalar, acc: Mutable[Scalar]):
+    seg, _pos = m.split_index(SEGMENT)
+    hawk.scatter(acc)[seg] += x
+
+
+@hawk.kernel
+def keyed_sum(x: Scalar, key: Sorted[Index], acc: Mutable[Scalar]):
+    hawk.scatter(acc, policy="plain")[key] += x
+
+
+@hawk.kernel
+def histogram(x: Scalar, key: Index, acc: Mutable[Scalar]):
+    hawk.scatter(acc, policy="compensated")[key] += x
+
+
+@hawk.kernel
+def bitmask(bits: UInt32, key: Index, acc: Mutable[UInt32]):
+    hawk.scatter(acc, policy="or")[key] |= bits
+
+
 #: Every kernel the bundles hold, by name, with the scalar modes each is built in.
 KERNELS = {
     "energy": (energy, ("float64",)),
@@ -208,4 +247,10 @@ KERNELS = {
     "kepler_vjp": (Kernel("kepler_vjp", vjp(kepler, wrt=("e", "M"))), ("float64",)),
     "oscillator": (oscillator, ("float64",)),
     "orbit": (orbit, ("float64",)),
+    "gather": (gather, ("float64",)),
+    "gather_vjp": (Kernel("gather_vjp", vjp(gather, wrt=("table", "w"))), ("float64",)),
+    "segment_sum": (segment_sum, ("float64",)),
+    "keyed_sum": (keyed_sum, ("float64",)),
+    "histogram": (histogram, ("float64",)),
+    "bitmask": (bitmask, ("float64",)),
 }

@@ -21,6 +21,7 @@
 #include "sample_sum.cuh"
 #include "stage.cuh"
 #include "steps.cuh"
+#include "accum.cuh"
 
 namespace hk {
 

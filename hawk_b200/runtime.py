@@ -102,6 +102,8 @@ class DeviceKernel:
         self.slots = [(s["role"], s["name"], s["dtype"], tuple(s["shape"])) for s in b200["slots"]]
         self.arg_spec = tuple((r, n) for r, n, _d, _s in self.slots)
         self.cells = sidecar.get("cells") or {}
+        # the accum_out planes that are sample-sum rows (the rest are scatter targets)
+        self.row_planes = {x for sm in self.sums for x in (sm["name"], sm.get("companion")) if x}
         if device is None:
             device = _current_device()
         self.device = int(device)
@@ -109,6 +111,8 @@ class DeviceKernel:
         self.entry = self.library.entry(b200["entry"])
         # an automatic stepping kernel's persistent entry (<name>_persist)
         self.persist = self.library.entry(b200["persist"]) if b200.get("persist") else None
+        # the fold of each compensated scatter target's companion (<name>__fold_<target>)
+        self.folds = {t: self.library.entry(e) for t, e in (b200.get("folds") or {}).items()}
         self.descriptor = descriptor_for_sidecar(sidecar)
         self.block = abi.ArgBlock(self.descriptor)
         self._lock = threading.Lock()
@@ -125,6 +129,35 @@ class DeviceKernel:
         if dtype in _INT_DTYPES:
             return {"i32": "int32", "i64": "int64"}.get(dtype, dtype)
         return _WIRE_OF_MODE[self.mode]
+
+    def own_companions(self, arrays: dict, stream=None) -> tuple:
+        """``(arrays, owned)``: ``arrays`` plus a zeroed companion, the target's
+        shape, for each compensated scatter target whose companion the caller
+        left out -- the run owns it (hawk/runtime.py:516-528)."""
+        import torch
+
+        owned = {comp: target for comp, target in (self.sidecar.get("companions") or {}).items()
+                 if comp not in arrays and target in arrays}
+        if not owned:
+            return arrays, owned
+        extra = {}
+        for comp, target in owned.items():
+            t = arrays[target]
+            if not torch.is_tensor(t):
+                raise HawkError(f"kernel {self.name!r}: bind the companion {comp!r} of {target!r} (the runtime "
+                                "makes one only beside a torch tensor target)")
+            with torch.cuda.stream(_torch_stream(stream, self.device)):
+                extra[comp] = torch.zeros_like(t)
+        self._held.append(extra)
+        return {**arrays, **extra}, owned
+
+    def fold_companions(self, arrays: dict, owned: dict, stream=None) -> None:
+        """Each owned companion into its target after the launch, through the
+        unit's fold entry over the target's slots (hawk/runtime.py:531-540): the
+        target then holds the compensated sum."""
+        for target in owned.values():
+            size = int(arrays[target].numel())
+            self.folds[target].launch(self.block, 0, size, size, _stream(stream, self.device))
 
     def default_words(self, arrays: dict, stream=None) -> dict:
         """``arrays`` plus the reserved one-cell planes a runner normally binds,
@@ -199,11 +232,16 @@ class DeviceKernel:
                               "offsets, so it must be C-contiguous")
             if role in SINK_ROLES and p.readonly:
                 errors.append(f"argument {name!r}: a {role!r} plane is written and must be writable")
-            if role == "accum_out":
+            if role == "accum_out" and name in self.row_planes:
                 rows = -(-n // ROW)
                 if len(p.shape) != 1 or p.shape[0] < rows:
                     errors.append(f"argument {name!r}: a row plane of {rows} rows (one per 32 samples) "
                                   f"is expected, got shape {p.shape}")
+            elif role == "accum_out":
+                # a scattered commit's target: any number of slots, the key's range
+                if len(p.shape) != len(shape) + 1 or tuple(p.shape[:-1]) != tuple(shape) or p.shape[-1] < 1:
+                    errors.append(f"argument {name!r}: a scatter target of shape ({', '.join(map(str, shape))}"
+                                  f"{', ' if shape else ''}slots) is expected, got {p.shape}")
             elif role == "lookup":
                 if len(p.shape) != 1 or p.shape[0] < 1:
                     errors.append(f"argument {name!r}: a lookup plane is 1-D and non-empty, got shape {p.shape}")
@@ -473,7 +511,10 @@ def run(kernel: DeviceKernel, *, base: int = 0, count: int | None = None, n_samp
     the runtime owns the rows and finishes them on the device: one leaf launch
     and one tree launch for all columns."""
     with kernel._lock:
+        arrays, owned = kernel.own_companions(arrays, stream)
         pending = launch_cells(kernel, base=base, count=count, n_samples=n_samples, stream=stream, **arrays)
+        if owned:
+            kernel.fold_companions(arrays, owned, stream)
         if pending is None:
             return
         state, outputs, lo, hi = pending

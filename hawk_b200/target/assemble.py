@@ -36,10 +36,8 @@ _UNBUILT = {
     "hk::geometry::": "ray primitives",
     "hk::banded::": "the banded scalar mode",
     "hk::random::": "in-kernel random draws",
-    "hk::accum::": "run and compensated scatter commits",
     "hk::linalg::team::": "team linear algebra (n > 32)",
     "hk::linalg::eigh": "the symmetric eigensolver",
-    "hawk_abi::accum_": "scattered accumulates",
     "hawk_abi::mix_count": "auto dispatch branch counts",
     "hawk_abi::tiled": "wide (tiled) scratch planes",
     "hawk_abi::warp_sum": "warp-per-lane sums",
@@ -62,8 +60,6 @@ class Unit:
 
 
 def _refuse(name: str, walk) -> None:
-    if walk.companions:
-        raise HawkError(f"{name!r}: compensated keyed sums (owned companions) are not built on the b200 target")
     for role, slot in walk.arg_spec:
         if role in ("wide_in", "wide_out"):
             raise HawkError(f"{name!r}: slot {slot!r} has role {role!r}, which the b200 target does not build")
@@ -143,6 +139,9 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
                     wrapper.index_prologue(), body, wrapper.index_epilogue(),
                     "    }"]
         frame = "lane"
+    # the run state of each keyed commit target the body names (hk/accum.cuh)
+    states = sorted(set(re.findall(r"\bhawk_run_(\w+)\b", "\n".join(loop))))
+    run_states = [f"    hk::accum::run::State hawk_run_{t}{{}};" for t in states]
     parts = [
         f"// hawk_b200 unit {name!r} (scalar mode {mode}), sm_100a.",
         "// Body text: the reference renderer's; entry, views and frame: the b200 wrapper.",
@@ -157,10 +156,23 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
         wrapper.entry_signature(walk, name, min_blocks),
         "{",
         wrapper.unpack(walk, plan),
+        *run_states,
         *loop,
         "}",
         "",
     ]
+    folds = {}
+    for comp, target in (walk.companions or {}).items():
+        # the owned companion's fold: one lane per slot of the target, launched
+        # after the kernel (hawk/emit/wrapper.py:1274-1293)
+        from hawk.emit.spelling import binding_name
+
+        fold = f"{name}__fold_{target}"
+        folds[target] = fold
+        parts += [wrapper.entry_signature(walk, fold), "{", wrapper.unpack(walk, None), wrapper.index_prologue(),
+                  f"        hawk_abi::fold_companion({binding_name('accum_out', target)}, "
+                  f"{binding_name('accum_out', comp)}, i);",
+                  wrapper.index_epilogue(), "}", ""]
     persist = persist_entry(kernel, name, wrapper) if one_step is not None else None
     if persist is not None:
         parts += [persist, ""]
@@ -172,7 +184,7 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
                        "stages": plan.stages if plan is not None else 0, "min_blocks": min_blocks or 0,
                        "persist": f"{name}{PERSIST_SUFFIX}" if persist is not None else None,
                        "step_fp64_ops": step_fp64_ops(kernel) if persist is not None else None,
-                       "lane_refill": frame_note == "refill"})
+                       "lane_refill": frame_note == "refill", "folds": folds})
 
 
 _IDENT = re.compile(r"[A-Za-z_][A-Za-z0-9_]*")

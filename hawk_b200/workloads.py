@@ -105,5 +105,22 @@ def orbit(n: int, seed: int = 0, done_every: int = 0) -> dict:
             "n_rej": np.zeros(n), "t_end": rng.uniform(0.5, 2.0 * np.pi, n), "terminated": term}
 
 
+#: Samples per segment of the segment_sum kernel (its key is sample // SEGMENT).
+SEGMENT = 256
+
+
+def scatter(n: int, seed: int = 0, slots: int = 1000) -> dict:
+    """Terms x ~ U[0.5, 1.5] (positive: the per-slot bound is relative to the
+    sum), keys uniform over ``slots`` (``key``), the same keys sorted
+    (``sorted_key``), a table of ``slots`` values with indices that also fall
+    outside it (clamped), and 32-bit words with one random bit each."""
+    rng = np.random.default_rng(seed)
+    key = rng.integers(0, slots, n).astype(np.int32)
+    return {"x": rng.uniform(0.5, 1.5, n), "key": key, "sorted_key": np.sort(key),
+            "idx": rng.integers(-3, slots + 3, n).astype(np.int32), "w": rng.standard_normal(n),
+            "table": rng.standard_normal(slots), "bar_y": rng.uniform(0.5, 1.5, n),
+            "bits": (np.uint32(1) << rng.integers(0, 32, n).astype(np.uint32)).astype(np.uint32), "slots": slots}
+
+
 MAKERS = {"energy": energy, "poly_loss": poly_loss, "gravity": gravity, "spd_solve": spd_solve, "kepler": kepler,
-          "oscillator": oscillator, "orbit": orbit}
+          "oscillator": oscillator, "orbit": orbit, "scatter": scatter}
