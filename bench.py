@@ -50,7 +50,12 @@ BYTES_F64 = {
     "gravity": 96, "gravity_jvp": 144, "gravity_vjp": 144,
     "spd_solve": 384, "spd_solve_vjp": 720,
     "kepler": 28, "kepler_vjp": 40,
+    # scattered commits: the streamed per-sample planes (the slot planes stay in L2)
+    "segment_sum": 8, "keyed_sum": 12, "histogram": 12, "bitmask": 8, "gather": 20, "gather_vjp": 28,
 }
+
+#: Slots of the scatter benchmark kernels' target planes (random keys over them).
+SCATTER_SLOTS = 1000
 
 
 def peaks() -> dict:
@@ -446,6 +451,24 @@ def run_configs(local: int) -> dict:
     out["kepler"]["mean_trips"] = round(mean_trips, 4)
     out["kepler"]["bound"] = "fp64"
     out["kepler_vjp"]["bound"] = "fp64"
+    del kp, iters, w
+    # scattered commits (hk/accum.cuh): 2^24 samples into SCATTER_SLOTS slots,
+    # random keys for the atomics, sorted keys for the warp-run commit
+    n = 1 << 24
+    w = workloads.scatter(n, 1, slots=SCATTER_SLOTS)
+    x, key, skey = t(w["x"]), t(w["key"]), t(w["sorted_key"])
+    segs = -(-n // workloads.SEGMENT)
+    time_kernel("segment_sum", {"x": x, "acc": e(segs), "acc_c": e(segs)}, {}, n)
+    time_kernel("keyed_sum", {"x": x, "key": skey, "acc": e(SCATTER_SLOTS)}, {}, n)
+    time_kernel("histogram", {"x": x, "key": key, "acc": e(SCATTER_SLOTS), "acc_c": e(SCATTER_SLOTS)}, {}, n)
+    time_kernel("bitmask", {"bits": t(w["bits"]), "key": key, "acc": e(SCATTER_SLOTS, torch.uint32)}, {}, n)
+    idx, wt, table = t(w["idx"]), t(w["w"]), t(w["table"])
+    time_kernel("gather", {"idx": idx, "w": wt, "table": table, "y": e(n)}, {}, n)
+    time_kernel("gather_vjp", {"idx": idx, "w": wt, "table": table, "bar_y": t(w["bar_y"]), "bar_w": e(n),
+                               "bar_table": e(SCATTER_SLOTS)}, {}, n)
+    for name in ("segment_sum", "keyed_sum", "histogram", "bitmask", "gather", "gather_vjp"):
+        out[name]["slots"] = SCATTER_SLOTS if name != "segment_sum" else segs
+        out[name]["bound"] = "atomics" if name in ("histogram", "bitmask", "gather_vjp") else "hbm"
     return out
 
 
