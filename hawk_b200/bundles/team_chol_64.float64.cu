@@ -1,0 +1,145 @@
+// hawk_b200 unit 'team_chol_64' (scalar mode float64), sm_100a.
+// Body text: the reference renderer's; entry, views and frame: the b200 wrapper.
+#include "hk/hawk_b200.cuh"
+
+using Real = double;
+using Int = long long;
+
+HK_SELF_CHECK_EXPORTS
+
+extern "C" __device__ const unsigned int hk_team_threads__team_chol_64 = 256u;
+extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_chol_64 = 0u;
+extern "C" __global__ void __launch_bounds__(256) team_chol_64(
+    hk::abi::ScalarHandle p_wout_tm0_a,
+    hk::abi::ScalarHandle p_wout_tm0_x0,
+    hk::abi::ScalarHandle p_wout_tm0_x1,
+    hk::abi::GRefMirror p_vin_b,
+    hk::abi::GRefMirror p_mtx_A,
+    hk::abi::GRefMirror p_mtx_B,
+    long long base,
+    long long count,
+    long long nSamples)
+{
+    const hk::ScalarOut<Real> wout_tm0_a(p_wout_tm0_a);
+    (void)wout_tm0_a;
+    const hk::ScalarOut<Real> wout_tm0_x0(p_wout_tm0_x0);
+    (void)wout_tm0_x0;
+    const hk::ScalarOut<Real> wout_tm0_x1(p_wout_tm0_x1);
+    (void)wout_tm0_x1;
+    const hk::VecIn<Real, 64> vin_b(p_vin_b);
+    (void)vin_b;
+    const hk::MatIn<Real, 64, 64> mtx_A(p_mtx_A);
+    (void)mtx_A;
+    const hk::MatIn<Real, 64, 2> mtx_B(p_mtx_B);
+    (void)mtx_B;
+    for (long long hawk_flat = blockIdx.x; hawk_flat < count; hawk_flat += gridDim.x) {
+        const long long hawk_i = base + hawk_flat;
+        const hk::SampleIndex i{hawk_i};
+        (void)hawk_i;
+        (void)nSamples;
+        const auto mtx_A_i = mtx_A[i].get();
+        const auto vin_b_i = vin_b[i].get();
+        const auto mtx_B_i = mtx_B[i].get();
+        { const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here(); for (Int hawk_lk = hawk_tm.rank; hawk_lk < 4096; hawk_lk += hawk_tm.size) wout_tm0_a.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 4096 + hawk_lk] = mtx_A[i].at(hawk_lk / 64, hawk_lk % 64); }
+        { const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here(); for (Int hawk_lk = hawk_tm.rank; hawk_lk < 64; hawk_lk += hawk_tm.size) wout_tm0_x0.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 64 + hawk_lk] = vin_b[i].at(hawk_lk); }
+        { const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here(); for (Int hawk_lk = hawk_tm.rank; hawk_lk < 128; hawk_lk += hawk_tm.size) wout_tm0_x1.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 128 + hawk_lk] = mtx_B[i].at(hawk_lk / 2, hawk_lk % 2); }
+        __syncthreads();
+    }
+}
+
+extern "C" __device__ const unsigned int hk_team_threads__team_chol_64_2 = 128u;
+extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_chol_64_2 = 35840u;
+extern "C" __global__ void __launch_bounds__(128) team_chol_64_2(
+    hk::abi::ScalarHandle p_wout_tm0_a,
+    hk::abi::ScalarHandle p_wout_tm0_info,
+    hk::abi::ScalarHandle p_wout_tm0_x0,
+    hk::abi::ScalarHandle p_wout_tm0_x1,
+    long long base,
+    long long count,
+    long long nSamples)
+{
+    const hk::ScalarOut<Real> wout_tm0_a(p_wout_tm0_a);
+    (void)wout_tm0_a;
+    const hk::ScalarOut<std::int32_t> wout_tm0_info(p_wout_tm0_info);
+    (void)wout_tm0_info;
+    const hk::ScalarOut<Real> wout_tm0_x0(p_wout_tm0_x0);
+    (void)wout_tm0_x0;
+    const hk::ScalarOut<Real> wout_tm0_x1(p_wout_tm0_x1);
+    (void)wout_tm0_x1;
+    for (long long hawk_flat = blockIdx.x; hawk_flat < count; hawk_flat += gridDim.x) {
+        const long long hawk_i = base + hawk_flat;
+        const hk::SampleIndex i{hawk_i};
+        (void)hawk_i;
+        (void)nSamples;
+        const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here();
+        const long long hawk_lane = hawk_i;
+        {  // chol, n = 64
+            Real* const hawk_a = wout_tm0_a.data() + static_cast<std::size_t>(hawk_lane) * 4096;
+            std::int32_t* const hawk_info = wout_tm0_info.data() + static_cast<std::size_t>(hawk_lane) * 1;
+            const auto hawk_f = hk::linalg::team::TeamCholesky<Real, 64>{hawk_a, hawk_info};
+            hk::linalg::team::cholesky<64>(hawk_tm, hawk_f, hawk_a);
+        }
+        {  // cho_solve, n = 64
+            Real* const hawk_a = wout_tm0_a.data() + static_cast<std::size_t>(hawk_lane) * 4096;
+            std::int32_t* const hawk_info = wout_tm0_info.data() + static_cast<std::size_t>(hawk_lane) * 1;
+            Real* const hawk_x = wout_tm0_x0.data() + static_cast<std::size_t>(hawk_lane) * 64;
+            const auto hawk_f = hk::linalg::team::TeamCholesky<Real, 64>{hawk_a, hawk_info};
+            hk::linalg::team::choSolve<64>(hawk_tm, hawk_f, hawk_x, hawk_x, 1);
+        }
+        {  // cho_solve, n = 64
+            Real* const hawk_a = wout_tm0_a.data() + static_cast<std::size_t>(hawk_lane) * 4096;
+            std::int32_t* const hawk_info = wout_tm0_info.data() + static_cast<std::size_t>(hawk_lane) * 1;
+            Real* const hawk_x = wout_tm0_x1.data() + static_cast<std::size_t>(hawk_lane) * 128;
+            const auto hawk_f = hk::linalg::team::TeamCholesky<Real, 64>{hawk_a, hawk_info};
+            hk::linalg::team::choSolve<64>(hawk_tm, hawk_f, hawk_x, hawk_x, 2);
+        }
+        __syncthreads();
+    }
+}
+
+extern "C" __global__ void __launch_bounds__(256) team_chol_64_3(
+    hk::abi::GRefMirror p_mut_L,
+    hk::abi::GRefMirror p_mut_X,
+    hk::abi::ScalarHandle p_mut_info,
+    hk::abi::GRefMirror p_mut_x,
+    hk::abi::ScalarHandle p_lut_tm0_a,
+    hk::abi::ScalarHandle p_lut_tm0_info,
+    hk::abi::ScalarHandle p_lut_tm0_x0,
+    hk::abi::ScalarHandle p_lut_tm0_x1,
+    long long base,
+    long long count,
+    long long nSamples)
+{
+    const hk::MatOut<Real, 64, 64> mut_L(p_mut_L);
+    (void)mut_L;
+    const hk::MatOut<Real, 64, 2> mut_X(p_mut_X);
+    (void)mut_X;
+    const hk::ScalarOut<std::int32_t> mut_info(p_mut_info);
+    (void)mut_info;
+    const hk::VecOut<Real, 64> mut_x(p_mut_x);
+    (void)mut_x;
+    const hk::ScalarIn<Real> lut_tm0_a(p_lut_tm0_a);
+    (void)lut_tm0_a;
+    const hk::ScalarIn<std::int32_t> lut_tm0_info(p_lut_tm0_info);
+    (void)lut_tm0_info;
+    const hk::ScalarIn<Real> lut_tm0_x0(p_lut_tm0_x0);
+    (void)lut_tm0_x0;
+    const hk::ScalarIn<Real> lut_tm0_x1(p_lut_tm0_x1);
+    (void)lut_tm0_x1;
+    for (long long hawk_flat = hk::lane_first(); hawk_flat < count; hawk_flat += hk::lane_step()) {
+        const long long hawk_i = base + hawk_flat;
+        const hk::SampleIndex i{hawk_i};
+        (void)hawk_i;
+        (void)nSamples;
+        const hk::Slice<Real, 64> hawk_la0{lut_tm0_x0.data() + static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 64};
+        const auto t2 = hawk_la0;
+        mut_x[i] = t2;
+        const hk::Slice<Real, 64, 2> hawk_la1{lut_tm0_x1.data() + static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 128};
+        const auto t5 = hawk_la1;
+        mut_X[i] = t5;
+        const hk::Slice<Real, 64, 64> hawk_la2{lut_tm0_a.data() + static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 4096};
+        const auto t8 = hawk_la2;
+        mut_L[i] = t8;
+        mut_info[i] = lut_tm0_info[hk::SampleIndex::make(static_cast<std::size_t>(static_cast<Int>(hawk_i)))].eval();
+    }
+}

@@ -230,6 +230,102 @@ def bitmask(bits: UInt32, key: Index, acc: Mutable[UInt32]):
     hawk.scatter(acc, policy="or")[key] |= bits
 
 
+@hawk.kernel
+def team_chol_33(A: Matrix[33, 33], b: Vector[33], B: Matrix[33, 2], x: Mutable[Vector[33]],
+                 X: Mutable[Matrix[33, 2]], L: Mutable[Matrix[33, 33]], info: Mutable[Int32]):
+    f, status = m.cholesky(A)
+    x = m.cho_solve(f, b)
+    X = m.cho_solve(f, B)
+    L = f
+    info = status
+
+
+@hawk.kernel
+def team_lu_33(A: Matrix[33, 33], b: Vector[33], B: Matrix[33, 2], x: Mutable[Vector[33]],
+               X: Mutable[Matrix[33, 2]], det: Mutable[Scalar], info: Mutable[Int32]):
+    f, status = m.lu(A)
+    x = m.lu_solve(f, b)
+    X = m.lu_solve(f, B)
+    det = m.det(A)
+    info = status
+
+
+@hawk.kernel
+def team_chol_64(A: Matrix[64, 64], b: Vector[64], B: Matrix[64, 2], x: Mutable[Vector[64]],
+                 X: Mutable[Matrix[64, 2]], L: Mutable[Matrix[64, 64]], info: Mutable[Int32]):
+    f, status = m.cholesky(A)
+    x = m.cho_solve(f, b)
+    X = m.cho_solve(f, B)
+    L = f
+    info = status
+
+
+@hawk.kernel
+def team_lu_64(A: Matrix[64, 64], b: Vector[64], B: Matrix[64, 2], x: Mutable[Vector[64]],
+               X: Mutable[Matrix[64, 2]], det: Mutable[Scalar], info: Mutable[Int32]):
+    f, status = m.lu(A)
+    x = m.lu_solve(f, b)
+    X = m.lu_solve(f, B)
+    det = m.det(A)
+    info = status
+
+
+@hawk.kernel
+def team_chol_128(A: Matrix[128, 128], b: Vector[128], B: Matrix[128, 2], x: Mutable[Vector[128]],
+                  X: Mutable[Matrix[128, 2]], L: Mutable[Matrix[128, 128]], info: Mutable[Int32]):
+    f, status = m.cholesky(A)
+    x = m.cho_solve(f, b)
+    X = m.cho_solve(f, B)
+    L = f
+    info = status
+
+
+@hawk.kernel
+def team_lu_128(A: Matrix[128, 128], b: Vector[128], B: Matrix[128, 2], x: Mutable[Vector[128]],
+                X: Mutable[Matrix[128, 2]], det: Mutable[Scalar], info: Mutable[Int32]):
+    f, status = m.lu(A)
+    x = m.lu_solve(f, b)
+    X = m.lu_solve(f, B)
+    det = m.det(A)
+    info = status
+
+
+@hawk.kernel
+def team_chol_from_64(A: Matrix[64, 64], b: Vector[64], x: Mutable[Vector[64]], L: Mutable[Matrix[64, 64]],
+                      info: Mutable[Int32]):
+    f, status = m.chol_from(A)
+    x = m.cho_solve(f, b)
+    L = f
+    info = status
+
+
+@hawk.kernel
+def team_chol_512(A: Matrix[512, 512], b: Vector[512], x: Mutable[Vector[512]], info: Mutable[Int32]):
+    f, status = m.cholesky(A)
+    x = m.cho_solve(f, b)
+    info = status
+
+
+@hawk.kernel
+def team_lu_160(A: Matrix[160, 160], b: Vector[160], x: Mutable[Vector[160]], det: Mutable[Scalar],
+                info: Mutable[Int32]):
+    f, status = m.lu(A)
+    x = m.lu_solve(f, b)
+    det = m.det(A)
+    info = status
+
+
+#: The team-form kernels: per sample, Cholesky solves (x, X, the factor L and
+#: its status) and LU solves with partial pivoting (x, X, det(A) -- its own
+#: factor, as hawk.math.det spells it -- and the status), at sizes above the
+#: one-thread cap of 32 (hawk/ir/linalg.py:33-36), and solves against a given
+#: lower-triangular factor (chol_from).  At 512 (Cholesky) and 160 (LU) the
+#: matrix does not fit a block's shared memory and the team works it in place
+#: in its scratch plane.
+TEAM_KERNELS = {k.name: k for k in (team_chol_33, team_lu_33, team_chol_64, team_lu_64, team_chol_128,
+                                    team_lu_128, team_chol_from_64, team_chol_512, team_lu_160)}
+
+
 #: Every kernel the bundles hold, by name, with the scalar modes each is built in.
 KERNELS = {
     "energy": (energy, ("float64",)),
@@ -253,4 +349,5 @@ KERNELS = {
     "keyed_sum": (keyed_sum, ("float64",)),
     "histogram": (histogram, ("float64",)),
     "bitmask": (bitmask, ("float64",)),
+    **{name: (k, ("float64",)) for name, k in TEAM_KERNELS.items()},
 }

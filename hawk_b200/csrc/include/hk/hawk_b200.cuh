@@ -22,6 +22,7 @@
 #include "stage.cuh"
 #include "steps.cuh"
 #include "accum.cuh"
+#include "team.cuh"
 
 namespace hk {
 

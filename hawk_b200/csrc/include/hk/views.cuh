@@ -85,6 +85,28 @@ template <class T> struct ScalarIn {
     HK_FI u64 samples() const { return n; }
 };
 
+// A sample of a vector or matrix input plane of more than kLazyElems elements,
+// read element by element where it is used (a whole value that size would not
+// fit a thread's registers).  Element (r, c) is component r * C + c.
+constexpr int kLazyElems = 48;
+
+template <class T, int R, int C> struct Slice;
+
+template <class T, int R, int C> struct InRef {
+    const T* q;
+    u64 pitch;
+    HK_FI T flat(int k) const { return ld_in(q + static_cast<u64>(k) * pitch); }
+    HK_FI T at(int k) const { return flat(k); }
+    HK_FI T at(int r, int c) const { return flat(r * C + c); }
+    HK_FI T operator()(int k) const { return flat(k); }
+    HK_FI T operator()(int r, int c) const { return flat(r * C + c); }
+    HK_FI T operator[](int k) const { return flat(k); }
+    static HK_HD constexpr int size() { return R * C; }
+    // a read of the whole value stays this reference (element reads where used)
+    HK_FI const InRef& get() const { return *this; }
+    HK_FI const InRef& eval() const { return *this; }
+};
+
 template <class T, int N> struct VecIn {
     const T* p;
     u64 pitch;
@@ -93,7 +115,10 @@ template <class T, int N> struct VecIn {
     HK_FI explicit VecIn(const abi::GRefMirror& m, unsigned off = 0, unsigned cb = 0)
         : p(reinterpret_cast<const T*>(m.data_)), pitch(m.compStride_), n(m.samples_), stage_off(off),
           comp_bytes(cb) {}
-    HK_FI Item<T, N> operator[](const SampleIndex& i) const {
+    HK_FI auto operator[](const SampleIndex& i) const {
+        if constexpr (N > kLazyElems) {
+            return InRef<T, N, 1>{p + i.g, pitch};
+        } else {
         Item<T, N> r;
         if (i.st) {
 #pragma unroll
@@ -104,6 +129,7 @@ template <class T, int N> struct VecIn {
 #pragma unroll
         for (int k = 0; k < N; ++k) r.v[k] = ld_in(p + static_cast<u64>(k) * pitch + i.g);
         return r;
+        }
     }
     HK_FI const T* data() const { return p; }
     HK_FI u64 samples() const { return n; }
@@ -117,7 +143,10 @@ template <class T, int R, int C> struct MatIn {
     HK_FI explicit MatIn(const abi::GRefMirror& m, unsigned off = 0, unsigned cb = 0)
         : p(reinterpret_cast<const T*>(m.data_)), pitch(m.compStride_), n(m.samples_), stage_off(off),
           comp_bytes(cb) {}
-    HK_FI Item<T, R, C> operator[](const SampleIndex& i) const {
+    HK_FI auto operator[](const SampleIndex& i) const {
+        if constexpr (R * C > kLazyElems) {
+            return InRef<T, R, C>{p + i.g, pitch};
+        } else {
         Item<T, R, C> a;
         if (i.st) {
 #pragma unroll
@@ -134,6 +163,7 @@ template <class T, int R, int C> struct MatIn {
             for (int c = 0; c < C; ++c)
                 a.m[r][c] = ld_in(p + static_cast<u64>(r * C + c) * pitch + i.g);
         return a;
+        }
     }
     HK_FI const T* data() const { return p; }
     HK_FI u64 samples() const { return n; }
@@ -193,8 +223,15 @@ template <class T, int N> struct VecOut {
 #pragma unroll
             for (int k = 0; k < N; ++k) q[static_cast<u64>(k) * pitch] += v.v[k];
         }
+        // a value that lives in a scratch slice: copied element by element
+        template <int C2> HK_FI void operator=(const Slice<T, N, C2>& v) const {
+#pragma unroll 1
+            for (int k = 0; k < N; ++k) st_out(q + static_cast<u64>(k) * pitch, v.flat(k));
+        }
         HK_FI T& operator[](int k) const { return q[static_cast<u64>(k) * pitch]; }
         HK_FI T& operator()(int k) const { return q[static_cast<u64>(k) * pitch]; }
+        HK_FI T& flat(int k) const { return q[static_cast<u64>(k) * pitch]; }
+        static HK_HD constexpr int size() { return N; }
         HK_FI T& at(int k) const { return q[static_cast<u64>(k) * pitch]; }
         HK_FI Item<T, N> get() const {
             Item<T, N> r;
@@ -225,8 +262,15 @@ template <class T, int R, int C> struct MatOut {
 #pragma unroll
                 for (int c = 0; c < C; ++c) st_out(q + static_cast<u64>(r * C + c) * pitch, a.m[r][c]);
         }
+        // a value that lives in a scratch slice: copied element by element
+        HK_FI void operator=(const Slice<T, R, C>& a) const {
+#pragma unroll 1
+            for (int k = 0; k < R * C; ++k) st_out(q + static_cast<u64>(k) * pitch, a.flat(k));
+        }
         HK_FI T& operator()(int r, int c) const { return q[static_cast<u64>(r * C + c) * pitch]; }
         HK_FI T& at(int r, int c) const { return q[static_cast<u64>(r * C + c) * pitch]; }
+        HK_FI T& flat(int k) const { return q[static_cast<u64>(k) * pitch]; }
+        static HK_HD constexpr int size() { return R * C; }
         HK_FI Item<T, R, C> get() const {
             Item<T, R, C> a;
 #pragma unroll
@@ -244,5 +288,50 @@ template <class T, int R, int C> struct MatOut {
     HK_FI T* data() const { return p; }
     HK_FI u64 samples() const { return n; }
 };
+
+
+// A vector or matrix a team stage left row-major in the lane's slice of a
+// scratch plane (the reader stage's view of it): element k is p[k].
+template <class T, int R, int C = 1> struct Slice {
+    const T* p;
+    HK_FI T flat(int k) const { return p[k]; }
+    HK_FI T at(int k) const { return p[k]; }
+    HK_FI T at(int r, int c) const { return p[r * C + c]; }
+    HK_FI T operator()(int k) const { return p[k]; }
+    HK_FI T operator()(int r, int c) const { return p[r * C + c]; }
+    HK_FI T operator[](int k) const { return p[k]; }
+    HK_FI const T* data() const { return p; }
+    static HK_HD constexpr int size() { return R * C; }
+    // the whole value, for an operation on all of it (held in registers or
+    // local memory: what the one-thread form of the same value costs)
+    HK_FI auto expr() const {
+        if constexpr (C == 1) {
+            Item<T, R> v;
+            for (int k = 0; k < R; ++k) v.v[k] = p[k];
+            return v;
+        } else {
+            Item<T, R, C> v;
+            for (int k = 0; k < R * C; ++k) v.data()[k] = p[k];
+            return v;
+        }
+    }
+    HK_FI auto get() const { return expr(); }
+    HK_FI auto eval() const { return expr(); }
+};
+
+namespace rt {
+namespace detail {
+template <class S> HK_FI auto flat_of(const S& s, int k) -> decltype(s.flat(k)) { return s.flat(k); }
+template <class T, int... D> HK_FI T flat_of(const Item<T, D...>& s, int k) { return s.data()[k]; }
+}  // namespace detail
+
+// dst = src element by element in a rolled loop: a value of hundreds or
+// thousands of elements (a factor read back from a team stage) is copied
+// straight from where it lives into the output plane, never held whole.
+template <class Dst, class Src> HK_FI void store(const Dst& dst, const Src& src) {
+#pragma unroll 1
+    for (int k = 0; k < Dst::size(); ++k) dst.flat(k) = detail::flat_of(src, k);
+}
+}  // namespace rt
 
 }  // namespace hk

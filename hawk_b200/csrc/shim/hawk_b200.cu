@@ -104,6 +104,7 @@ struct hkb_entry {
     int blocks_per_sm = 0;
     int block = kBlock;          // threads per block this entry launches with
     unsigned dynamic_smem = 0;   // bytes per block the unit exports (hk_dynamic_smem_bytes)
+    int team = 0;                // a team entry's threads (one block per lane), else 0
 };
 
 struct hkb_argblock {
@@ -259,11 +260,38 @@ int hkb_library_entry(hkb_library* lib, const char* name, hkb_entry** out) {
         return cuda_fail(e2, "reading the entry's attributes");
     }
     entry->regs = attr.numRegs;
+    // A team entry (one block per lane) exports its threads per block,
+    // hk_team_threads__<entry>; an entry of a unit with several entries its own
+    // dynamic shared memory, hk_dynamic_smem_bytes__<entry>.
+    const std::string team_sym = std::string("hk_team_threads__") + name;
+    const std::string smem_sym = std::string("hk_dynamic_smem_bytes__") + name;
+    void* tptr = nullptr;
+    size_t tbytes = 0;
+    if (cudaLibraryGetGlobal(&tptr, &tbytes, lib->lib, team_sym.c_str()) == cudaSuccess &&
+        tbytes == sizeof(unsigned)) {
+        unsigned threads = 0;
+        e2 = cudaMemcpy(&threads, tptr, sizeof(unsigned), cudaMemcpyDeviceToHost);
+        if (e2 != cudaSuccess) {
+            delete entry;
+            return cuda_fail(e2, "reading the team entry's threads");
+        }
+        if (threads == 0 || threads > 1024 || threads % 32 != 0) {
+            delete entry;
+            return fail(HKB_ERR_ABI, "entry '%s': a team of %u threads is not 1 to 32 whole warps", name, threads);
+        }
+        entry->team = static_cast<int>(threads);
+    } else {
+        cudaGetLastError();
+    }
     // A unit whose entry stages through dynamic shared memory exports its size.
     void* sptr = nullptr;
     size_t sbytes = 0;
-    if (cudaLibraryGetGlobal(&sptr, &sbytes, lib->lib, "hk_dynamic_smem_bytes") == cudaSuccess &&
-        sbytes == sizeof(unsigned)) {
+    cudaError_t found = cudaLibraryGetGlobal(&sptr, &sbytes, lib->lib, smem_sym.c_str());
+    if (found != cudaSuccess) {
+        cudaGetLastError();
+        found = cudaLibraryGetGlobal(&sptr, &sbytes, lib->lib, "hk_dynamic_smem_bytes");
+    }
+    if (found == cudaSuccess && sbytes == sizeof(unsigned)) {
         e2 = cudaMemcpy(&entry->dynamic_smem, sptr, sizeof(unsigned), cudaMemcpyDeviceToHost);
         if (e2 != cudaSuccess) {
             delete entry;
@@ -285,7 +313,8 @@ int hkb_library_entry(hkb_library* lib, const char* name, hkb_entry** out) {
     const int candidates[] = {256, 128, 96, 64, 32};
     int best_warps = -1;
     for (int b : candidates) {
-        if (entry->dynamic_smem != 0 && b != kBlock) continue;
+        if (entry->team != 0) b = entry->team;          // a team is its block
+        else if (entry->dynamic_smem != 0 && b != kBlock) continue;
         int bps = 0;
         e2 = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, reinterpret_cast<const void*>(kernel), b,
                                                            entry->dynamic_smem);
@@ -299,6 +328,7 @@ int hkb_library_entry(hkb_library* lib, const char* name, hkb_entry** out) {
             entry->block = b;
             entry->blocks_per_sm = bps;
         }
+        if (entry->team != 0) break;
     }
     if (entry->blocks_per_sm < 1) entry->blocks_per_sm = 1;
     *out = entry;
@@ -307,7 +337,9 @@ int hkb_library_entry(hkb_library* lib, const char* name, hkb_entry** out) {
 
 static int64_t grid_for(const hkb_entry* entry, int64_t count) {
     const int64_t cap = static_cast<int64_t>(entry->lib->sms) * entry->blocks_per_sm;
-    int64_t need = (count + entry->block - 1) / entry->block;
+    // a team entry takes one lane per block per trip; every other entry one
+    // sample (or row) per thread
+    int64_t need = entry->team != 0 ? count : (count + entry->block - 1) / entry->block;
     if (need < 1) need = 1;
     return need < cap ? need : cap;
 }

@@ -373,16 +373,108 @@ def _stream(stream, device: int) -> int:
         return 0
 
 
+class SplitKernel:
+    """A kernel run as stages (team-form linear algebra, hawk/ir/team.py): the
+    device twin of the reference runtime's ``_run_stages``
+    (hawk/runtime.py:699-748).  Every stage is an entry of the one unit; the
+    runtime owns the scratch planes the stages pass the lanes' matrices through
+    (``team_planes``: ``per_lane`` elements per sample, made once per sample
+    count, hawk/runtime.py:675-696) and launches the stages in order on the
+    stream -- a team stage with one block of its team per lane."""
+
+    def __init__(self, directory, kernel: str, mode: str = "float64", device: int | None = None) -> None:
+        self.directory = Path(directory)
+        stem = f"{kernel}.{mode}"
+        path = self.directory / f"{stem}.json"
+        if not path.exists():
+            raise HawkError(f"no b200 artifact {stem!r} in {self.directory} (no {path.name})")
+        sidecar = json.loads(path.read_text())
+        self.sidecar = sidecar
+        self.name = sidecar["kernel"]
+        self.mode = sidecar.get("scalar_type", mode)
+        b200 = sidecar["b200"]
+        self.device = int(device if device is not None else _current_device())
+        self.team_planes = sidecar.get("team_planes") or {}
+        self.stages = []
+        for st in b200["split"]:
+            stage_sidecar = {"kernel": st["entry"], "scalar_type": self.mode, "cells": {},
+                             "arg_dtypes": {}, "b200": {"entry": st["entry"], "cubin": b200["cubin"],
+                                                         "frame": "lane", "sample_sums": [], "slots": st["slots"],
+                                                         "persist": None, "folds": {}}}
+            self.stages.append(DeviceKernel(self.directory, st["entry"], self.mode, self.device,
+                                            sidecar=stage_sidecar))
+        self.slots = [(s["role"], s["name"], s["dtype"], tuple(s["shape"])) for s in b200["slots"]]
+        self.arg_spec = tuple((r, n) for r, n, _d, _s in self.slots)
+        self.cells = {}
+        self._lock = threading.Lock()
+        self._scratch: dict = {}
+
+    def scratch(self, n: int) -> dict:
+        """The stages' scratch planes at ``n`` samples (made once per n)."""
+        import torch
+
+        if n not in self._scratch:
+            dev = torch.device("cuda", self.device)
+            real = torch.float64 if self.mode == "float64" else torch.float32
+            self._scratch[n] = {
+                name: torch.empty(int(spec.get("per_lane", 1)) * n,
+                                  dtype=torch.int32 if spec.get("dtype") == "int32" else real, device=dev)
+                for name, spec in self.team_planes.items()}
+        return self._scratch[n]
+
+    def run(self, *, base: int = 0, count: int | None = None, n_samples: int | None = None, stream=None,
+            **arrays) -> None:
+        from .planes import from_torch
+
+        declared = {n for _r, n in self.arg_spec}
+        unknown = sorted(set(arrays) - declared)
+        if unknown:
+            raise HawkError(f"kernel {self.name!r}: {unknown} are not planes it declares "
+                            f"(declared: {sorted(declared)})")
+        uniforms = {n for r, n in self.arg_spec if r == "uniform"}
+        values = {k: v for k, v in arrays.items() if k in uniforms}
+        planes = {k: as_plane(k, v) for k, v in arrays.items() if k not in uniforms}
+        missing = sorted(declared - set(arrays))
+        if missing:
+            raise HawkError(f"kernel {self.name!r}: {missing} are declared but not bound")
+        if n_samples is None:
+            n_samples = self.stages[0].n_from(planes)
+        count = n_samples - base if count is None else count
+        if base < 0 or count < 0 or base + count > n_samples:
+            raise HawkError(f"kernel {self.name!r}: partition [{base}, {base + count}) is outside "
+                            f"the {n_samples} samples")
+        with self._lock:
+            scratch = {k: from_torch(v) for k, v in self.scratch(n_samples).items()}
+            for stage in self.stages:
+                names = {n for _r, n in stage.arg_spec}
+                bound = {k: v for k, v in planes.items() if k in names}
+                bound.update({k: v for k, v in scratch.items() if k in names})
+                stage.check(bound, values, n_samples)
+                stage.bind_all(bound, values, n_samples)
+                stage.launch(base, count, n_samples, stream)
+
+    def errors(self, clear: bool = True) -> int:
+        """The unit's error word (hkb_library_errors) after the stream's launches."""
+        flags = 0
+        for stage in self.stages:
+            flags |= stage.library.errors(clear)
+        return flags
+
+
 _CACHE: dict = {}
 _CACHE_LOCK = threading.Lock()
 
 
-def load(directory, kernel: str, mode: str = "float64", device: int | None = None) -> DeviceKernel:
-    """Load ``<directory>/<kernel>.<mode>.cubin`` on ``device`` (cached per process)."""
+def load(directory, kernel: str, mode: str = "float64", device: int | None = None):
+    """Load ``<directory>/<kernel>.<mode>.cubin`` on ``device`` (cached per
+    process): a ``DeviceKernel``, or a ``SplitKernel`` for a kernel built as
+    stages."""
     key = (str(Path(directory).resolve()), kernel, mode, device if device is not None else _current_device())
     with _CACHE_LOCK:
         if key not in _CACHE:
-            _CACHE[key] = DeviceKernel(directory, kernel, mode, key[3])
+            path = Path(directory) / f"{kernel}.{mode}.json"
+            split = path.exists() and "split" in json.loads(path.read_text()).get("b200", {})
+            _CACHE[key] = (SplitKernel if split else DeviceKernel)(directory, kernel, mode, key[3])
         return _CACHE[key]
 
 
@@ -509,7 +601,11 @@ def run(kernel: DeviceKernel, *, base: int = 0, count: int | None = None, n_samp
     per-sample plane agrees on.  A kernel with cells takes each cell as a
     one-element device plane (not its rows, as hawk/runtime.py:345-360 rules);
     the runtime owns the rows and finishes them on the device: one leaf launch
-    and one tree launch for all columns."""
+    and one tree launch for all columns.  A kernel built as stages runs them
+    in order (``SplitKernel.run``)."""
+    if isinstance(kernel, SplitKernel):
+        kernel.run(base=base, count=count, n_samples=n_samples, stream=stream, **arrays)
+        return
     with kernel._lock:
         arrays, owned = kernel.own_companions(arrays, stream)
         pending = launch_cells(kernel, base=base, count=count, n_samples=n_samples, stream=stream, **arrays)

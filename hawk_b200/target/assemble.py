@@ -32,17 +32,37 @@ MODES = {"float64": "double", "float32": "float"}
 #: Library namespaces the device library does not provide: a body naming one is
 #: refused with the construct it stands for.
 _UNBUILT = {
-    "hk::rt::": "runtime-index stores and rolled products (aether::rt)",
+    "hk::rt::": "runtime-index stores and rolled products (aether::rt) other than the rolled store",
     "hk::geometry::": "ray primitives",
     "hk::banded::": "the banded scalar mode",
     "hk::random::": "in-kernel random draws",
-    "hk::linalg::team::": "team linear algebra (n > 32)",
     "hk::linalg::eigh": "the symmetric eigensolver",
     "hawk_abi::mix_count": "auto dispatch branch counts",
     "hawk_abi::tiled": "wide (tiled) scratch planes",
     "hawk_abi::warp_sum": "warp-per-lane sums",
     "hawk_abi::spacing": "the spacing op",
 }
+
+
+#: The team-form calls the device library builds (hk/team.cuh).
+TEAM_BUILT = frozenset({"Team", "TeamCholesky", "TeamLu", "cholesky", "choleskyFrom", "choSolve", "triLower",
+                        "triUpperT", "lu", "luSolve", "luSolveT", "luInverse", "luDet"})
+_TEAM_NAME = re.compile(r"hk::linalg::team::(\w+)")
+
+
+def refuse_unbuilt(name: str, body: str) -> None:
+    """Refuse, by the construct it stands for, a body naming what the device
+    library does not provide."""
+    for token, what in _UNBUILT.items():
+        if token == "hk::rt::":
+            if re.search(r"hk::rt::(?!store\()", body):
+                raise HawkError(f"{name!r}: its body uses {what}, which the b200 target does not build yet")
+            continue
+        if token in body:
+            raise HawkError(f"{name!r}: its body uses {what}, which the b200 target does not build yet")
+    for call in sorted(set(_TEAM_NAME.findall(body)) - TEAM_BUILT):
+        raise HawkError(f"{name!r}: its team stage calls hk::linalg::team::{call} (team-form "
+                        f"{'eigensolver' if 'eigh' in call.lower() else 'QR' if 'qr' in call.lower() else 'block sums' if 'block' in call.lower() else call}), which the b200 target does not build yet")
 
 
 @dataclass(frozen=True)
@@ -57,11 +77,33 @@ class Unit:
     sums: tuple = ()                # ((name, op, companion or None), ...) in column order
     digest: str = ""
     notes: dict = field(default_factory=dict)
+    entries: str = ""               # the text after the prelude: the entry (and its fold / persist entries)
+
+
+def prelude_lines(name: str, mode: str) -> list:
+    """The head of a unit: the device library, the scalar-mode aliases and the
+    self-check exports (hawk/artifact/layout.py:35-61)."""
+    return [
+        f"// hawk_b200 unit {name!r} (scalar mode {mode}), sm_100a.",
+        "// Body text: the reference renderer's; entry, views and frame: the b200 wrapper.",
+        '#include "hk/hawk_b200.cuh"',
+        "",
+        f"using Real = {MODES[mode]};",
+        "using Int = long long;",
+        "",
+        "HK_SELF_CHECK_EXPORTS",
+    ]
+
+
+def _team_prefix() -> str:
+    from hawk.ir.team import PLANE_PREFIX
+    return PLANE_PREFIX
 
 
 def _refuse(name: str, walk) -> None:
     for role, slot in walk.arg_spec:
-        if role in ("wide_in", "wide_out"):
+        # a team stage's scratch plane (hawk/ir/team.py PLANE_PREFIX) is the split's; any other wide plane is not built
+        if role == "wide_in" or (role == "wide_out" and not slot.startswith(_team_prefix())):
             raise HawkError(f"{name!r}: slot {slot!r} has role {role!r}, which the b200 target does not build")
 
 
@@ -90,9 +132,7 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
     _refuse(name, walk)
     rendered = render_body(sinks, walk, indent="        ", writer=B200_WRITER)
     body = body_text(rendered.text)
-    for token, what in _UNBUILT.items():
-        if token in body:
-            raise HawkError(f"{name!r}: its body uses {what}, which the b200 target does not build yet")
+    refuse_unbuilt(name, body)
     sums = sample_sums(sinks)
     if len({s.op for s in sums}) > 1:
         raise HawkError(f"{name!r}: one kernel reduces over samples with one op (sum, max or min)")
@@ -142,17 +182,8 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
     # the run state of each keyed commit target the body names (hk/accum.cuh)
     states = sorted(set(re.findall(r"\bhawk_run_(\w+)\b", "\n".join(loop))))
     run_states = [f"    hk::accum::run::State hawk_run_{t}{{}};" for t in states]
+    prelude = [*prelude_lines(name, mode), *([f"HK_DYNAMIC_SMEM({smem})"] if smem else []), ""]
     parts = [
-        f"// hawk_b200 unit {name!r} (scalar mode {mode}), sm_100a.",
-        "// Body text: the reference renderer's; entry, views and frame: the b200 wrapper.",
-        '#include "hk/hawk_b200.cuh"',
-        "",
-        f"using Real = {MODES[mode]};",
-        "using Int = long long;",
-        "",
-        "HK_SELF_CHECK_EXPORTS",
-        *([f"HK_DYNAMIC_SMEM({smem})"] if smem else []),
-        "",
         wrapper.entry_signature(walk, name, min_blocks),
         "{",
         wrapper.unpack(walk, plan),
@@ -176,9 +207,10 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
     persist = persist_entry(kernel, name, wrapper) if one_step is not None else None
     if persist is not None:
         parts += [persist, ""]
-    text = "\n".join(parts)
+    entries = "\n".join(parts)
+    text = "\n".join(prelude) + "\n" + entries
     records = tuple((s.name, s.op, s.companion.name if s.op == "sum" else None) for s in sums)
-    return Unit(name=name, mode=mode, text=text, body=body, frame=frame, sums=records,
+    return Unit(name=name, mode=mode, text=text, body=body, frame=frame, sums=records, entries=entries,
                 digest=hashlib.sha256(text.encode()).hexdigest(),
                 notes={"dynamic_smem": smem, "staged": plan is not None,
                        "stages": plan.stages if plan is not None else 0, "min_blocks": min_blocks or 0,

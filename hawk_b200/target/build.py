@@ -89,14 +89,61 @@ def _spills(ptxas: dict, name: str) -> bool:
     return bool(r.get("spill_store_B") or r.get("spill_load_B"))
 
 
+def build_split_kernel(kernel, directory, *, name: str | None = None, mode: str = "float64") -> dict:
+    """A kernel the reference's split cuts into stages (team-form linear
+    algebra): one unit holding every stage's entry, one CUBIN, one sidecar
+    listing the stages and the scratch planes (target/split.py)."""
+    from .split import render_split_unit, user_slots
+
+    directory = Path(directory)
+    directory.mkdir(parents=True, exist_ok=True)
+    name = name or kernel.name
+    unit, stages, block, members = render_split_unit(kernel, name, mode)
+    cubin, _log, ptxas = compile_cubin(unit.text, name)
+    stem = f"{name}.{mode}"
+    (directory / f"{stem}.cu").write_text(unit.text)
+    (directory / f"{stem}.cubin").write_bytes(cubin)
+    sidecar = _reference_sidecar(name, members[0].walk, mode)
+    sidecar = json.loads(json.dumps(sidecar, default=str))
+    sidecar.update(json.loads(json.dumps(block, default=str)))
+    scratch = set(block.get("team_planes") or {})
+    sidecar["b200"] = {
+        "entry": name,
+        "arch": ARCH,
+        "unit": f"{stem}.cu",
+        "cubin": f"{stem}.cubin",
+        "unit_digest": unit.digest,
+        "frame": "split",
+        "dynamic_smem": 0,
+        "stages": 0,
+        "min_blocks": 0,
+        "persist": None,
+        "step_fp64_ops": None,
+        "lane_refill": False,
+        "folds": {},
+        "sample_sums": [],
+        "split": stages,
+        "slots": user_slots(stages, scratch),
+        "nvrtc_options": [o for o in options() if not o.startswith("-I")],
+        "ptxas": ptxas,
+    }
+    (directory / f"{stem}.json").write_text(json.dumps(sidecar, indent=1, sort_keys=True))
+    return sidecar
+
+
 def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "float64",
                  staged: bool | None = None) -> dict:
     """Render, compile and write one kernel's b200 artifact; returns its sidecar.
     ``staged`` streams the inputs through TMA-filled shared-memory stages;
-    ``None`` decides by the unstaged entry's register count."""
+    ``None`` decides by the unstaged entry's register count.  A kernel the
+    reference's split cuts into stages is built by ``build_split_kernel``."""
+    from .split import expand
+
+    name = name or kernel.name
+    if expand(kernel, name) is not None:
+        return build_split_kernel(kernel, directory, name=name, mode=mode)
     directory = Path(directory)
     directory.mkdir(parents=True, exist_ok=True)
-    name = name or kernel.name
     unit = render_unit(kernel, name, mode, staged=bool(staged))
     cubin, log, ptxas = compile_cubin(unit.text, name)
     if staged is None and ptxas.get(name, {}).get("regs", 0) > REGISTER_BOUND:

@@ -1,0 +1,168 @@
+"""Split kernels on the b200 target: every stage of a kernel in one unit.
+
+A kernel whose team-form linear algebra (a matrix above the one-thread cap,
+hawk/ir/team.py) cannot run in one launch is cut by the reference's own split
+(``_expand_split``, hawk/artifact/bundle.py:1177-1275; hawk/ir/split.py:304)
+into stages named ``<name>``, ``<name>_2``, ...:
+
+* a copy stage (a plain kernel with a team): the lane's operands stored
+  row-major into runtime-owned scratch planes (``tm*``), one block per lane;
+* a team stage (``TeamStage``): the reference's team body
+  (hawk/emit/team.py:466), collective calls into ``hk::linalg::team``;
+* a reader stage: a plain per-lane kernel that reads the results back.
+
+The reference builds each stage as an artifact of its own and its runtime
+launches them in order over scratch it allocates (hawk/runtime.py:675-748).
+Here the stages are the entries of ONE unit (one CUBIN, one sidecar): a team
+entry exports its block size (``hk_team_threads__<entry>``) and the dynamic
+shared memory its calls stage into (``hk_dynamic_smem_bytes__<entry>``), which
+the loader reads; the sidecar lists the stages, their slots and the scratch
+planes (``team_planes``) for the runtime's split runner.
+"""
+
+from __future__ import annotations
+
+import hashlib
+
+from ..errors import HawkError
+from .assemble import MODES, Unit, prelude_lines, refuse_unbuilt, render_unit
+from .wrapper import B200
+from .writer import B200_WRITER, body_text
+
+#: Dynamic shared memory a team entry may stage into (of the 227 KB a block
+#: can have): above it the calls work on the scratch planes in place.
+TEAM_SMEM_LIMIT = 200 * 1024
+
+
+def _round16(b: int) -> int:
+    return (b + 15) & ~15
+
+
+def _staged_bytes(n: int, k: int, elem: int) -> int:
+    """hk::linalg::team::staged_bytes: scratch, running sums, matrix (stride n + 1), right-hand sides."""
+    return 1024 + _round16(elem * n) + _round16(elem * n * (n + 1)) + _round16(elem * n * k)
+
+
+def _base_bytes(n: int, elem: int) -> int:
+    return 1024 + _round16(elem * n)
+
+
+def team_smem(spec, elem: int) -> int:
+    """The dynamic shared memory of a team stage: the largest staged need of
+    its calls when that fits TEAM_SMEM_LIMIT, else the scratch and running
+    sums every call needs (the calls then work in place)."""
+    needs, bases = [], []
+    for step in spec.steps:
+        n = int(step.n)
+        k = n if step.op == "lu_inverse" else int(step.k or 0)
+        needs.append(_staged_bytes(n, k, elem))
+        bases.append(_base_bytes(n, elem))
+    if not needs:
+        return 0
+    return max(needs) if max(needs) <= TEAM_SMEM_LIMIT else max(bases)
+
+
+def expand(kernel, name: str):
+    """``(members, block)``: the stage kernels and the reference's sidecar block
+    (stages, cells, team_planes), or None for a kernel that runs in one launch."""
+    from hawk.artifact.bundle import _expand_split
+
+    members, names, _kinds, blocks = _expand_split([kernel], [name], [None], device=True, device_only=False)
+    block = blocks.get(name)
+    if block is None or len(members) < 2 or not any(getattr(m, "team", None) is not None for m in members):
+        return None
+    return members, block
+
+
+def _threads(member) -> int | None:
+    team = getattr(member, "team", None)
+    if team is None:
+        return None
+    t = int(team.threads)
+    if t % 32 or t <= 0 or t > 1024:
+        raise HawkError(f"{member.name!r}: a team of {t} threads is not whole warps (1 to 32 of them)")
+    return t
+
+
+def render_split_unit(kernel, name: str, mode: str = "float64"):
+    """``(unit, stages, block)``: the unit holding every stage's entry, the
+    per-stage records and the reference's split block."""
+    from hawk.trace.kernel import TeamStage
+
+    if mode not in MODES:
+        raise HawkError(f"scalar mode {mode!r} is not built on the b200 target (built: {sorted(MODES)})")
+    found = expand(kernel, name)
+    if found is None:
+        raise HawkError(f"{name!r} runs in one launch; it is not a split kernel")
+    members, block = found
+    elem = 8 if mode == "float64" else 4
+    parts, stages = [], []
+    for member, record in zip(members, block["stages"]):
+        if record.get("cells_in") or record.get("cells_out"):
+            raise HawkError(f"{name!r}: stage {member.name!r} passes a sample sum between launches, which the "
+                            "b200 target does not build yet")
+        if getattr(member, "one_step", None) is not None:
+            raise HawkError(f"{name!r}: an automatic stepping kernel's stages are not built on the b200 target")
+        threads = _threads(member)
+        walk = member.walk
+        if threads is None:
+            unit = render_unit(member, member.name, mode, staged=False)
+            if unit.frame != "lane" or unit.notes.get("persist") or unit.notes.get("folds"):
+                raise HawkError(f"{name!r}: stage {member.name!r} needs a {unit.frame} frame, which a split "
+                                "kernel's stage does not build yet")
+            parts.append(unit.entries)
+            stages.append({"entry": member.name, "kind": "lane", "threads": None, "dynamic_smem": 0,
+                           "slots": _slot_records(walk), "lane_refill": unit.notes.get("lane_refill", False)})
+            continue
+        if isinstance(member, TeamStage):
+            body = body_text(member.fused_body().text)
+            smem = team_smem(member.team, elem)
+        else:                       # a copy stage: the stage's own sinks, a block per lane
+            from hawk.emit.render import render_body
+
+            body = body_text(render_body(member.sinks, walk, indent="        ", writer=B200_WRITER).text)
+            smem = 0
+        refuse_unbuilt(member.name, body)
+        parts += [
+            f'extern "C" __device__ const unsigned int hk_team_threads__{member.name} = {threads}u;',
+            f'extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__{member.name} = {smem}u;',
+            B200.entry_signature(walk, member.name, threads=threads),
+            "{",
+            B200.unpack(walk),
+            B200.team_prologue(),
+            body,
+            B200.team_epilogue(),
+            "}",
+            "",
+        ]
+        stages.append({"entry": member.name, "kind": "team", "threads": threads, "dynamic_smem": smem,
+                       "slots": _slot_records(walk)})
+    text = "\n".join([*prelude_lines(name, mode), "", *parts])
+    unit = Unit(name=name, mode=mode, text=text, body="", frame="split",
+                digest=hashlib.sha256(text.encode()).hexdigest(), entries="\n".join(parts),
+                notes={"dynamic_smem": 0, "staged": False, "stages": 0, "min_blocks": 0, "persist": None,
+                       "step_fp64_ops": None, "lane_refill": False, "folds": {}})
+    return unit, stages, block, members
+
+
+def _slot_records(walk) -> list:
+    out = []
+    for role, name in walk.arg_spec:
+        t = walk.slot_types[(role, name)]
+        out.append({"role": role, "name": name, "dtype": t.dtype, "shape": [int(e) for e in t.shape]})
+    return out
+
+
+def user_slots(stages: list, scratch) -> list:
+    """The slots a caller binds: every stage's, less the runtime's scratch
+    planes (``scratch``), each once (its first stage's record)."""
+    seen, out = set(), []
+    for st in stages:
+        for slot in st["slots"]:
+            if slot["name"] in scratch:
+                continue
+            if slot["name"] in seen:
+                continue
+            seen.add(slot["name"])
+            out.append(slot)
+    return out

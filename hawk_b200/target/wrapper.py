@@ -30,7 +30,7 @@ BLOCK = 256
 
 #: The roles this wrapper builds, by the view it unpacks them into.
 _INPUT_ROLES = ("vec_in", "mat_in", "per_sample", "lookup")
-_SINK_ROLES = ("mutable", "out", "accum_out")
+_SINK_ROLES = ("mutable", "out", "accum_out", "wide_out")
 _VALUE_ROLES = ("uniform", "nsamples")
 
 _OP_CODE = {"sum": "hk::ss::kSum", "max": "hk::ss::kMax", "min": "hk::ss::kMin"}
@@ -102,24 +102,27 @@ class B200Wrapper:
 
     qualifier = "__device__ __forceinline__"
 
-    def entry_signature(self, walk, name: str, min_blocks: int | None = None) -> str:
+    def entry_signature(self, walk, name: str, min_blocks: int | None = None, threads: int | None = None) -> str:
         """``extern "C" __global__`` entry: role mirrors by value in ``arg_spec``
         order, then the int64 partition triple.  ``min_blocks`` asks the
-        compiler to keep that many blocks resident per SM (a register cap)."""
+        compiler to keep that many blocks resident per SM (a register cap);
+        ``threads`` is a team entry's block (one team per lane)."""
         sp = _spelling()
         params = [f"    {param_type(role, walk.slot_types[(role, n)])} {sp.param_name(role, n)}"
                   for role, n in walk.arg_spec]
         params += ["    long long base", "    long long count", "    long long nSamples"]
-        bounds = f"{BLOCK}, {min_blocks}" if min_blocks else f"{BLOCK}"
+        bounds = f"{threads or BLOCK}, {min_blocks}" if min_blocks else f"{threads or BLOCK}"
         return (f'extern "C" __global__ void __launch_bounds__({bounds}) {name}(\n'
                 + ",\n".join(params) + ")")
 
     def index_prologue(self, segment=None, *, active=None, box=None, team=None) -> str:
-        """The lane frame: a grid-stride loop binding ``hawk_i`` and ``i``."""
-        for label, value in (("segmented", segment), ("active-set", active),
-                             ("thread-box", box), ("team", team)):
+        """The lane frame: a grid-stride loop binding ``hawk_i`` and ``i``;
+        with ``team`` (the team's threads) the team frame."""
+        for label, value in (("segmented", segment), ("active-set", active), ("thread-box", box)):
             if value is not None:
                 raise HawkError(f"the {label} entry is not built on the b200 target")
+        if team is not None:
+            return self.team_prologue()
         return ("    for (long long hawk_flat = hk::lane_first(); hawk_flat < count; "
                 "hawk_flat += hk::lane_step()) {\n"
                 "        const long long hawk_i = base + hawk_flat;\n"
@@ -129,6 +132,22 @@ class B200Wrapper:
 
     def index_epilogue(self) -> str:
         return "    }"
+
+    def team_prologue(self) -> str:
+        """The team frame (hawk/emit/cuda.py:82-92 makes the lane the block): a
+        block-stride loop over the partition's lanes, one lane per block per
+        trip, every thread of the block on the same lane (the team's calls are
+        collective); the grid is the runtime's, at most the resident blocks."""
+        return ("    for (long long hawk_flat = blockIdx.x; hawk_flat < count; hawk_flat += gridDim.x) {\n"
+                "        const long long hawk_i = base + hawk_flat;\n"
+                "        const hk::SampleIndex i{hawk_i};\n"
+                "        (void)hawk_i;\n"
+                "        (void)nSamples;")
+
+    def team_epilogue(self) -> str:
+        """The end of a team trip: the block leaves the lane together (its
+        shared memory is the next lane's)."""
+        return "        __syncthreads();\n    }"
 
     def unpack(self, walk, plan: "StagePlan | None" = None) -> str:
         """Every slot's view, in ``arg_spec`` order; a promoted Param's one-cell

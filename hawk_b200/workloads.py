@@ -122,5 +122,42 @@ def scatter(n: int, seed: int = 0, slots: int = 1000) -> dict:
             "bits": (np.uint32(1) << rng.integers(0, 32, n).astype(np.uint32)).astype(np.uint32), "slots": slots}
 
 
+#: The lane given an input its factorisation fails on, in the team workloads.
+TEAM_BAD = 2
+
+
+def team(n: int, lanes: int, kind: str, seed: int = 0, bad: int | None = TEAM_BAD) -> dict:
+    """Per-lane n x n matrices (A, (n, n, lanes)), a right-hand side b (n, lanes)
+    and a two-column one B (n, 2, lanes), the distributions of the reference's
+    team-form tests: ``spd`` g g^T + I with g ~ N(0, 1/n) (lane ``bad``: a
+    negative diagonal entry at n // 2, so the leading minor n // 2 + 1 fails);
+    ``general`` N(0, 1/n) + 0.5 I (lane ``bad``: column 1 zero, singular);
+    ``lower`` a lower triangle with diagonal in [1, 2) and noise above it, which
+    chol_from ignores (lane ``bad``: a zero first diagonal entry)."""
+    rng = np.random.default_rng(seed)
+    mats = np.empty((lanes, n, n))
+    for lane in range(lanes):
+        if kind == "spd":
+            g = rng.standard_normal((n, n)) / np.sqrt(n)
+            a = g @ g.T + np.eye(n)
+            if lane == bad:
+                a[n // 2, n // 2] = -1.0
+        elif kind == "general":
+            a = rng.standard_normal((n, n)) / np.sqrt(n) + 0.5 * np.eye(n)
+            if lane == bad:
+                a[:, min(1, n - 1)] = 0.0
+        elif kind == "lower":
+            a = np.tril(rng.standard_normal((n, n)), -1) / np.sqrt(n) + np.diag(1.0 + rng.random(n))
+            a += 0.5 * np.triu(rng.standard_normal((n, n)), 1)
+            if lane == bad:
+                a[0, 0] = 0.0
+        else:
+            raise ValueError(kind)
+        mats[lane] = a
+    return {"A": np.ascontiguousarray(np.moveaxis(mats, 0, -1)),
+            "b": np.ascontiguousarray(rng.standard_normal((n, lanes))),
+            "B": np.ascontiguousarray(rng.standard_normal((n, 2, lanes)))}
+
+
 MAKERS = {"energy": energy, "poly_loss": poly_loss, "gravity": gravity, "spd_solve": spd_solve, "kepler": kepler,
           "oscillator": oscillator, "orbit": orbit, "scatter": scatter}

@@ -80,12 +80,17 @@ void hkb_library_free(hkb_library* lib);
 
 /* The unit's error word (0 when every bounded wait of its entries completed;
  * bit 1: a staged tile did not arrive in time, 2: a stage was not released in
- * time, 4: copies were still in flight when a CTA gave up), read after the
+ * time, 4: copies were still in flight when a CTA gave up, 8: a team-form call
+ * was launched with less shared memory than its scratch needs), read after the
  * launches it covers have completed; `clear` resets it.  A unit without the
  * word reads 0.  The reference's host target has no device waits to report. */
 int hkb_library_errors(hkb_library* lib, unsigned* flags, int clear);
 
-/* HostLibrary.entry(name) (src/hawk_core.cpp:663-667): the entry `name`. */
+/* HostLibrary.entry(name) (src/hawk_core.cpp:663-667): the entry `name`.  A
+ * team entry (a stage of team-form linear algebra, hawk/ir/team.py) exports
+ * its threads per block as hk_team_threads__<name> and launches one block per
+ * lane; an entry's dynamic shared memory is hk_dynamic_smem_bytes__<name>,
+ * else the unit's hk_dynamic_smem_bytes. */
 int hkb_library_entry(hkb_library* lib, const char* name, hkb_entry** out);
 
 /* Facts of an entry: registers per thread, resident blocks per SM at its
@@ -116,7 +121,8 @@ int hkb_argblock_rebind(hkb_argblock* block, const int64_t* slots, const int64_t
 
 /* HostEntry.run(block, base, count, nSamples) (src/hawk_core.cpp:431-442, :642-653):
  * run the entry over samples [base, base + count) of nSamples on `stream`
- * (asynchronous).  A kernel with sample sums needs base % 32 == 0. */
+ * (asynchronous).  A kernel with sample sums needs base % 32 == 0.  A team
+ * entry runs lanes [base, base + count), each by one block of its team. */
 int hkb_entry_launch(hkb_entry* entry, hkb_argblock* block, int64_t base, int64_t count,
                      int64_t n_samples, void* stream);
 

@@ -92,6 +92,9 @@ _SIGS = {
     "hko_kepler_vjp": (None, [_P, _P, _P, _P, _P, _I, _I]),
     "hko_oscillator": (ctypes.c_uint32, [_P, _P, _P, _P, _P, _P, _P, _D, _I, _I, _I]),
     "hko_orbit": (ctypes.c_uint32, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I]),
+    "hko_team_chol": (None, [ctypes.c_int, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I]),
+    "hko_team_lu": (None, [ctypes.c_int, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I]),
+    "hko_team_chol_from": (None, [ctypes.c_int, _P, _P, _I, _P, _P, _P, _I, _I]),
 }
 
 
@@ -277,6 +280,35 @@ def spd_solve_vjp(A, b, bar_x, threads: int = 1):
     parallel(lambda bb, c: lib().hko_spd_solve_vjp(_p(A), _p(b), _p(bar_x), n, _p(bar_A), _p(bar_b), n, bb, c),
              n, threads)
     return bar_A, bar_b
+
+
+def team_chol(A, b, B, threads: int = 1):
+    """(x, X, L, info) of the team-form Cholesky kernel: A (n, n, N), b (n, N), B (n, 2, N)."""
+    k, n = A.shape[0], A.shape[-1]
+    x, X, L = np.empty((k, n)), np.empty((k, 2, n)), np.empty((k, k, n))
+    info = np.empty(n, dtype=np.int32)
+    parallel(lambda bb, c: lib().hko_team_chol(k, _p(A), _p(b), _p(B), n, _p(x), _p(X), _p(L), _p(info), bb, c),
+             n, threads)
+    return x, X, L, info
+
+
+def team_lu(A, b, B, threads: int = 1):
+    """(x, X, det, info) of the team-form LU kernel."""
+    k, n = A.shape[0], A.shape[-1]
+    x, X, det = np.empty((k, n)), np.empty((k, 2, n)), np.empty(n)
+    info = np.empty(n, dtype=np.int32)
+    parallel(lambda bb, c: lib().hko_team_lu(k, _p(A), _p(b), _p(B), n, _p(x), _p(X), _p(det), _p(info), bb, c),
+             n, threads)
+    return x, X, det, info
+
+
+def team_chol_from(A, b, threads: int = 1):
+    """(x, L, info) of the chol_from kernel."""
+    k, n = A.shape[0], A.shape[-1]
+    x, L = np.empty((k, n)), np.empty((k, k, n))
+    info = np.empty(n, dtype=np.int32)
+    parallel(lambda bb, c: lib().hko_team_chol_from(k, _p(A), _p(b), n, _p(x), _p(L), _p(info), bb, c), n, threads)
+    return x, L, info
 
 
 def kepler(e, M, threads: int = 1):

@@ -395,6 +395,226 @@ void hko_spd_solve_vjp(const double* A, const double* b, const double* bar_x, in
     }
 }
 
+/* ------------------------------------------- team-form linear algebra (any n) */
+
+/* Cholesky of the symmetric part, column by column, for any n (the order of
+ * hawk/embedded/linalg.py:233-271); l is row-major n x n, zeroed first; the
+ * factor as a matrix is l when info == 0, else zeros. */
+static int chol_n(int n, const double* a, double* l) {
+    int info = 0;
+    memset(l, 0, sizeof(double) * (size_t)n * (size_t)n);
+    for (int j = 0; j < n; ++j) {
+        if (info != 0) continue;
+        double d = (0.5 * a[j * n + j]) + (0.5 * a[j * n + j]);
+        for (int k = 0; k < j; ++k) d = d - (l[j * n + k] * l[j * n + k]);
+        if (d > 0.0) {
+            const double ljj = sqrt(d);
+            l[j * n + j] = ljj;
+            for (int i = j + 1; i < n; ++i) {
+                double acc = (0.5 * a[i * n + j]) + (0.5 * a[j * n + i]);
+                for (int k = 0; k < j; ++k) acc = acc - (l[i * n + k] * l[j * n + k]);
+                l[i * n + j] = acc / ljj;
+            }
+        } else {
+            info = j + 1;
+        }
+    }
+    return info;
+}
+
+/* cho_solve on k right-hand sides (row-major n x k), one column at a time:
+ * forward sweep on L, backward on L^T (hawk/embedded/linalg.py:443-520). */
+static void cho_solve_n(int n, const double* l, int info, const double* b, double* x, int k) {
+    for (int e = 0; e < n * k; ++e) x[e] = info != 0 ? 0.0 : b[e];
+    if (info != 0) return;
+    for (int c = 0; c < k; ++c) {
+        for (int i = 0; i < n; ++i) {
+            double acc = x[i * k + c];
+            for (int j = 0; j < i; ++j) acc = acc - (l[i * n + j] * x[j * k + c]);
+            x[i * k + c] = acc / l[i * n + i];
+        }
+        for (int r = 0; r < n; ++r) {
+            const int i = n - 1 - r;
+            double acc = x[i * k + c];
+            for (int j = i + 1; j < n; ++j) acc = acc - (l[j * n + i] * x[j * k + c]);
+            x[i * k + c] = acc / l[i * n + i];
+        }
+    }
+}
+
+/* P A = L U, Crout, column by column; the pivot is the first row of largest
+ * magnitude (hawk/embedded/linalg.py:188-231). */
+static int lu_n(int n, const double* a, double* f, int32_t* piv) {
+    memcpy(f, a, sizeof(double) * (size_t)n * (size_t)n);
+    int info = 0;
+    if (n == 1) {
+        piv[0] = 0;
+        return f[0] != 0.0 ? 0 : 1;
+    }
+    for (int j = 0; j < n; ++j) {
+        for (int i = 0; i < n; ++i) {
+            const int m = i < j ? i : j;
+            double acc = 0.0;
+            for (int k = 0; k < m; ++k) acc = acc + (f[i * n + k] * f[k * n + j]);
+            f[i * n + j] = f[i * n + j] - acc;
+        }
+        int p = j;
+        double big = fabs(f[j * n + j]);
+        for (int i = j + 1; i < n; ++i) {
+            const double mag = fabs(f[i * n + j]);
+            if (mag > big) {
+                big = mag;
+                p = i;
+            }
+        }
+        piv[j] = p;
+        if (f[p * n + j] != 0.0) {
+            if (p != j)
+                for (int c = 0; c < n; ++c) {
+                    const double t = f[j * n + c];
+                    f[j * n + c] = f[p * n + c];
+                    f[p * n + c] = t;
+                }
+            const double rcp = 1.0 / f[j * n + j];
+            for (int i = j + 1; i < n; ++i) f[i * n + j] = f[i * n + j] * rcp;
+        } else if (info == 0) {
+            info = j + 1;
+        }
+    }
+    return info;
+}
+
+/* lu_solve on k right-hand sides: the exchanges in step order, the unit-lower
+ * forward sweep, the backward sweep on U; zeros on a failed factor. */
+static void lu_solve_n(int n, const double* f, const int32_t* piv, int info, const double* b, double* x, int k) {
+    for (int e = 0; e < n * k; ++e) x[e] = info != 0 ? 0.0 : b[e];
+    if (info != 0) return;
+    if (n > 1)
+        for (int s = 0; s < n; ++s) {
+            const int p = piv[s];
+            if (p != s)
+                for (int c = 0; c < k; ++c) {
+                    const double t = x[s * k + c];
+                    x[s * k + c] = x[p * k + c];
+                    x[p * k + c] = t;
+                }
+        }
+    for (int c = 0; c < k; ++c) {
+        if (n > 1)
+            for (int i = 0; i < n; ++i) {
+                double acc = x[i * k + c];
+                for (int j = 0; j < i; ++j) acc = acc - (f[i * n + j] * x[j * k + c]);
+                x[i * k + c] = acc;
+            }
+        for (int r = 0; r < n; ++r) {
+            const int i = n - 1 - r;
+            double acc = x[i * k + c];
+            for (int j = i + 1; j < n; ++j) acc = acc - (f[i * n + j] * x[j * k + c]);
+            x[i * k + c] = acc / f[i * n + i];
+        }
+    }
+}
+
+/* det from the factor: U's diagonal product, negated per exchange as it is met
+ * (hawk/embedded/linalg.py:402-418); 0 on a failed factor. */
+static double lu_det_n(int n, const double* f, const int32_t* piv, int info) {
+    if (info != 0) return 0.0;
+    double d = 1.0;
+    for (int k = 0; k < n; ++k) {
+        d = d * f[k * n + k];
+        if (piv[k] != k) d = -d;
+    }
+    return d;
+}
+
+static void load_nxm(const double* P, int64_t pitch, int64_t i, int r, int c, double* out) {
+    for (int e = 0; e < r * c; ++e) out[e] = P[(int64_t)e * pitch + i];
+}
+
+static void store_nxm(double* P, int64_t pitch, int64_t i, int r, int c, const double* in) {
+    for (int e = 0; e < r * c; ++e) P[(int64_t)e * pitch + i] = in[e];
+}
+
+void hko_team_chol(int n, const double* A, const double* b, const double* B, int64_t pitch, double* x, double* X,
+                   double* L, int32_t* info, int64_t base, int64_t count) {
+    double* a = malloc(sizeof(double) * (size_t)n * (size_t)n);
+    double* l = malloc(sizeof(double) * (size_t)n * (size_t)n);
+    double* v = malloc(sizeof(double) * (size_t)n * 2);
+    double* y = malloc(sizeof(double) * (size_t)n * 2);
+    for (int64_t i = base; i < base + count; ++i) {
+        load_nxm(A, pitch, i, n, n, a);
+        const int inf = chol_n(n, a, l);
+        load_nxm(b, pitch, i, n, 1, v);
+        cho_solve_n(n, l, inf, v, y, 1);
+        store_nxm(x, pitch, i, n, 1, y);
+        load_nxm(B, pitch, i, n, 2, v);
+        cho_solve_n(n, l, inf, v, y, 2);
+        store_nxm(X, pitch, i, n, 2, y);
+        if (inf != 0) memset(l, 0, sizeof(double) * (size_t)n * (size_t)n);
+        store_nxm(L, pitch, i, n, n, l);
+        info[i] = inf;
+    }
+    free(a);
+    free(l);
+    free(v);
+    free(y);
+}
+
+void hko_team_lu(int n, const double* A, const double* b, const double* B, int64_t pitch, double* x, double* X,
+                 double* det, int32_t* info, int64_t base, int64_t count) {
+    double* a = malloc(sizeof(double) * (size_t)n * (size_t)n);
+    double* f = malloc(sizeof(double) * (size_t)n * (size_t)n);
+    int32_t* piv = malloc(sizeof(int32_t) * (size_t)n);
+    double* v = malloc(sizeof(double) * (size_t)n * 2);
+    double* y = malloc(sizeof(double) * (size_t)n * 2);
+    for (int64_t i = base; i < base + count; ++i) {
+        load_nxm(A, pitch, i, n, n, a);
+        const int inf = lu_n(n, a, f, piv);
+        load_nxm(b, pitch, i, n, 1, v);
+        lu_solve_n(n, f, piv, inf, v, y, 1);
+        store_nxm(x, pitch, i, n, 1, y);
+        load_nxm(B, pitch, i, n, 2, v);
+        lu_solve_n(n, f, piv, inf, v, y, 2);
+        store_nxm(X, pitch, i, n, 2, y);
+        det[i] = lu_det_n(n, f, piv, inf);
+        info[i] = inf;
+    }
+    free(a);
+    free(f);
+    free(piv);
+    free(v);
+    free(y);
+}
+
+/* chol_from: the lower triangle of A is the factor; info = first column whose
+ * diagonal is not positive and finite (hawk/embedded/linalg.py:274-299). */
+void hko_team_chol_from(int n, const double* A, const double* b, int64_t pitch, double* x, double* L,
+                        int32_t* info, int64_t base, int64_t count) {
+    double* a = malloc(sizeof(double) * (size_t)n * (size_t)n);
+    double* l = malloc(sizeof(double) * (size_t)n * (size_t)n);
+    double* v = malloc(sizeof(double) * (size_t)n);
+    double* y = malloc(sizeof(double) * (size_t)n);
+    for (int64_t i = base; i < base + count; ++i) {
+        load_nxm(A, pitch, i, n, n, a);
+        int inf = 0;
+        for (int j = 0; j < n && inf == 0; ++j) {
+            const double d = a[j * n + j];
+            if ((d <= 0.0) || !isfinite(d)) inf = j + 1;
+        }
+        for (int r = 0; r < n; ++r)
+            for (int c = 0; c < n; ++c) l[r * n + c] = (inf == 0 && c <= r) ? a[r * n + c] : 0.0;
+        load_nxm(b, pitch, i, n, 1, v);
+        cho_solve_n(n, l, inf, v, y, 1);
+        store_nxm(x, pitch, i, n, 1, y);
+        store_nxm(L, pitch, i, n, n, l);
+        info[i] = inf;
+    }
+    free(a);
+    free(l);
+    free(v);
+    free(y);
+}
+
 /* ---------------------------------------------------------------- c5 Kepler */
 
 /*

@@ -93,6 +93,21 @@ uint32_t hko_oscillator(double* x, double* v, double* k, const double* nstop, co
 uint32_t hko_orbit(double* s, int64_t pitch, double* t, double* h, double* n_acc, double* n_rej,
                    const double* t_end, uint8_t* term, int64_t word, int64_t base, int64_t count);
 
+/* Team-form linear algebra (n x n per sample, any n): what the reference's
+ * stages compute per lane -- the one-thread form's operation order for every
+ * n (hawk/embedded/linalg.py:188-520).  Planes are component-major: A is
+ * (n, n, pitch), b and x (n, pitch), B and X (n, 2, pitch), L (n, n, pitch);
+ * info is int32 per sample.
+ *   team_chol:      L, info = cholesky(A); x = cho_solve(L, b); X = cho_solve(L, B)
+ *   team_lu:        f, info = lu(A); x = lu_solve(f, b); X = lu_solve(f, B); det = det(A)
+ *   team_chol_from: f, info = chol_from(A); x = cho_solve(f, b); L = f */
+void hko_team_chol(int n, const double* A, const double* b, const double* B, int64_t pitch, double* x, double* X,
+                   double* L, int32_t* info, int64_t base, int64_t count);
+void hko_team_lu(int n, const double* A, const double* b, const double* B, int64_t pitch, double* x, double* X,
+                 double* det, int32_t* info, int64_t base, int64_t count);
+void hko_team_chol_from(int n, const double* A, const double* b, int64_t pitch, double* x, double* L,
+                        int32_t* info, int64_t base, int64_t count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -11,7 +11,8 @@ gives the per-sample gradient terms the 32-sample rows sum.
 Needs the reference checkout (its front end and tests/ directory); the
 fixtures it writes are committed and are all the test suite reads.
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py          # every fixture
+    python tests/golden/make_golden.py team     # the team-form fixtures only
 """
 
 from __future__ import annotations
@@ -32,8 +33,45 @@ OSC_WORDS = (1, 0, -2, 5, 30)
 ORB_WORDS = (1, 9, 40)
 
 
+#: Team-form fixtures: (kernel, workload kind, n, lanes); lane TEAM_BAD fails.
+TEAM_CASES = (("team_chol", "spd", 33, 5), ("team_lu", "general", 33, 5), ("team_chol", "spd", 64, 3),
+              ("team_chol_from", "lower", 64, 3))
+
+
+def team_fixtures(evaluate) -> None:
+    """team.npz: the team-form kernels' inputs and the interpreter's outputs
+    (its linear algebra is scipy's LAPACK, so these pin the oracle within the
+    reference's tolerances, and the status words exactly)."""
+    from hawk_b200 import configs, workloads
+
+    out = {}
+    for kernel, kind, n, lanes in TEAM_CASES:
+        name = f"{kernel}_{n}"
+        k = configs.TEAM_KERNELS[name]
+        w = workloads.team(n, lanes, kind, SEED + n)
+        outs = [o for r, o in k.walk.arg_spec if r == "mutable"]
+        got = {o: [] for o in outs}
+        for i in range(lanes):
+            env = {"A": w["A"][..., i], "b": w["b"][:, i], "B": w["B"][..., i]}
+            res = evaluate(k.sinks, env)
+            for o in outs:
+                got[o].append(np.asarray(res[o], dtype=np.int32 if o == "info" else float))
+        for key in ("A", "b", "B"):
+            out[f"{name}_{key}"] = w[key]
+        for o in outs:
+            out[f"{name}_{o}"] = np.stack(got[o], axis=-1)
+    np.savez(HERE / "team.npz", **out)
+
+
 def main() -> int:
     from hawk_b200 import frontend, workloads
+
+    if sys.argv[1:] == ["team"]:
+        hawk = frontend.load()
+        sys.path.insert(0, str(Path(hawk.__file__).resolve().parent.parent / "tests"))
+        from _eval import evaluate
+        team_fixtures(evaluate)
+        return 0
 
     hawk = frontend.load()
     root = Path(hawk.__file__).resolve().parent.parent
@@ -143,6 +181,7 @@ def main() -> int:
         for k in ("s", "t", "h", "n_acc", "n_rej", "terminated"):
             steps[f"orb_w{word}_{k}"] = got[k]
     np.savez(HERE / "steps.npz", **steps)
+    team_fixtures(evaluate)
     _ = Kernel, jvp
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)

@@ -174,3 +174,48 @@ def test_stepping_samples_finished_on_entry_are_left_alone(golden):
         np.testing.assert_array_equal(planes[k][skip], before[k][skip])
         np.testing.assert_array_equal(planes[k][~skip], g[f"osc_w30_{k}"][~skip])
     assert fin == int(g["osc_w30_terminated"].astype(bool)[~skip].sum())
+
+
+EPS = np.finfo(np.float64).eps
+
+
+def _team(g, name):
+    return {k[len(name) + 1:]: v for k, v in g.items() if k.startswith(name + "_")}
+
+
+@pytest.mark.parametrize("name", ["team_chol_33", "team_chol_64"])
+def test_team_cholesky_golden(golden, name):
+    """The team-form Cholesky kernel against the interpreter (scipy LAPACK):
+    the status exactly, the factor within 50 n eps |A|, the solves to the
+    interpreter's within 1e-10 relative (the tolerances of the reference's
+    tests/test_team_linalg.py)."""
+    g = _team(golden("team"), name)
+    n = g["A"].shape[0]
+    x, X, L, info = oracle.team_chol(g["A"], g["b"], g["B"])
+    np.testing.assert_array_equal(info, g["info"])
+    scale = np.abs(g["A"]).max()
+    assert np.abs(L - g["L"]).max() <= 50 * n * EPS * scale
+    close(x, g["x"], rtol=1e-10, atol=1e-13)
+    close(X, g["X"], rtol=1e-10, atol=1e-13)
+    bad = np.flatnonzero(info)
+    assert bad.tolist() == [2] and info[2] == n // 2 + 1
+    assert not np.any(x[:, 2]) and not np.any(X[..., 2]) and not np.any(L[..., 2])
+
+
+def test_team_lu_golden(golden):
+    g = _team(golden("team"), "team_lu_33")
+    x, X, det, info = oracle.team_lu(g["A"], g["b"], g["B"])
+    np.testing.assert_array_equal(info, g["info"])
+    assert info[2] > 0 and not np.any(x[:, 2]) and det[2] == 0.0
+    close(x, g["x"], rtol=1e-10, atol=1e-13)
+    close(X, g["X"], rtol=1e-10, atol=1e-13)
+    close(det, g["det"], rtol=1e-9 * 33)
+
+
+def test_team_chol_from_golden(golden):
+    g = _team(golden("team"), "team_chol_from_64")
+    x, L, info = oracle.team_chol_from(g["A"], g["b"])
+    np.testing.assert_array_equal(info, g["info"])
+    np.testing.assert_array_equal(L, g["L"])
+    close(x, g["x"], rtol=1e-10, atol=1e-13)
+    assert info[2] == 1 and not np.any(x[:, 2])
