@@ -472,6 +472,101 @@ def run_configs(local: int) -> dict:
     return out
 
 
+# -------------------------------------------------- team-form linear algebra
+#: Lanes of the team-form benchmark kernels: 2^14 matrices of 64 x 64 and
+#: 2^12 of 128 x 128 (the A plane is 512 MiB either way).
+TEAM_LANES = {64: 1 << 14, 128: 1 << 12}
+
+
+def team_bytes(kernel: str, n: int) -> int:
+    """Algorithmic bytes per lane: every input plane read once, every output
+    written once (f64 = 8 B, int32 = 4 B)."""
+    if kernel == "team_chol":
+        return 8 * (n * n + n + 2 * n) + 8 * (n + 2 * n + n * n) + 4
+    return 8 * (n * n + n + 2 * n) + 8 * (n + 2 * n + 1) + 4
+
+
+def team_flops(kernel: str, n: int) -> float:
+    """Floating-point operations per lane of the factor and its solves (add,
+    multiply, divide, square root one each): Cholesky n^3/3, LU 2n^3/3, a solve
+    2n^2 per right-hand side (three of them), det n."""
+    return (n ** 3 / 3.0 if kernel == "team_chol" else 2.0 * n ** 3 / 3.0) + 3 * 2.0 * n * n
+
+
+def run_team(local: int, cpu_threads: int | None = None) -> dict:
+    """The team-form kernels (Cholesky and LU solves of 64 x 64 and 128 x 128
+    matrices, one per lane): lanes/s of a whole run (copy, team and reader
+    stages), each stage's device time, algorithmic GB/s against the HBM peak,
+    and the oracle on the host cores over a sample of the lanes."""
+    import torch
+
+    import oracle
+    from hawk_b200 import runtime, workloads
+    from hawk_b200.planes import from_torch
+
+    dev = torch.device("cuda", local)
+    pk = peaks()
+    threads = cpu_threads or os.cpu_count() or 1
+    out = {}
+    for n, lanes in TEAM_LANES.items():
+        for kernel, kind in (("team_chol", "spd"), ("team_lu", "general")):
+            name = f"{kernel}_{n}"
+            w = workloads.team(n, lanes, kind, seed=n, bad=None)
+            k = runtime.load(BUNDLES, name, "float64", local)
+            planes = {key: torch.as_tensor(w[key], device=dev) for key in ("A", "b", "B")}
+            planes.update({"x": torch.empty((n, lanes), dtype=torch.float64, device=dev),
+                           "X": torch.empty((n, 2, lanes), dtype=torch.float64, device=dev),
+                           "info": torch.empty(lanes, dtype=torch.int32, device=dev)})
+            if kernel == "team_chol":
+                planes["L"] = torch.empty((n, n, lanes), dtype=torch.float64, device=dev)
+            else:
+                planes["det"] = torch.empty(lanes, dtype=torch.float64, device=dev)
+            for _ in range(3):
+                runtime.run(k, **planes)
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(10):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                runtime.run(k, **planes)
+                b.record()
+                b.synchronize()
+                times.append(a.elapsed_time(b))
+            ms = statistics.median(times)
+            # each stage alone, bound as the run bound it
+            stage_ms = []
+            for stage in k.stages:
+                sa, sb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                stream = torch.cuda.current_stream(local).cuda_stream
+                reps = []
+                for _ in range(5):
+                    sa.record()
+                    stage.launch(0, lanes, lanes, stream)
+                    sb.record()
+                    sb.synchronize()
+                    reps.append(sa.elapsed_time(sb))
+                info = stage.entry.info(lanes)
+                stage_ms.append({"entry": stage.name, "ms": round(statistics.median(reps), 5),
+                                 "regs": info["regs"], "block": info["block"], "grid": info["grid"],
+                                 "blocks_per_sm": info["blocks_per_sm"]})
+            gbs = team_bytes(kernel, n) * lanes / (ms * 1e-3) / 1e9
+            sample = max(1, min(lanes, 256 if n == 64 else 64))
+            sub = {key: np.ascontiguousarray(w[key][..., :sample]) for key in ("A", "b", "B")}
+            fn = oracle.team_chol if kernel == "team_chol" else oracle.team_lu
+            t0 = time.perf_counter()
+            fn(sub["A"], sub["b"], sub["B"], threads=threads)
+            cpu_s = time.perf_counter() - t0
+            out[name] = {"lanes": lanes, "n": n, "ms": round(ms, 5), "lanes_per_s": lanes / (ms * 1e-3),
+                         "gbs": round(gbs, 1), "hbm_frac": round(gbs / pk["hbm_gbs"], 4),
+                         "bytes_per_lane": team_bytes(kernel, n),
+                         "fp64_tflops": round(team_flops(kernel, n) * lanes / (ms * 1e-3) / 1e12, 3),
+                         "stages": stage_ms,
+                         "cpu_baseline": {"lanes_per_s": sample / cpu_s, "threads": threads, "sample_lanes": sample,
+                                          "kind": "port"}}
+            del planes, w
+    return out
+
+
 # ------------------------------------------------------------ stepping kernels
 def run_steps(local: int, cpu_threads: int | None = None) -> dict:
     """The automatic stepping kernels integrated to completion: every sample from
@@ -761,6 +856,7 @@ def main() -> int:
     if world == 1 and not args.no_configs:
         configs = run_configs(local)
         configs["stepping"] = run_steps(local)
+        configs["team"] = run_team(local)
     cpu = cpu_baseline(args.mode, args.cpu_sample) if (rank == 0 and world == 1) else None
     if rank == 0:
         line = {

@@ -32,7 +32,9 @@ extern "C" __global__ void __launch_bounds__(256) team_chol_33(
     (void)mtx_A;
     const hk::MatIn<Real, 33, 2> mtx_B(p_mtx_B);
     (void)mtx_B;
-    for (long long hawk_flat = blockIdx.x; hawk_flat < count; hawk_flat += gridDim.x) {
+    hk::linalg::team::begin_entry();
+    const long long hawk_teams = static_cast<long long>(blockDim.x >> 5);
+    for (long long hawk_flat = static_cast<long long>(blockIdx.x) * hawk_teams + (threadIdx.x >> 5); hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
         (void)hawk_i;
@@ -43,13 +45,13 @@ extern "C" __global__ void __launch_bounds__(256) team_chol_33(
         { const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here(); for (Int hawk_lk = hawk_tm.rank; hawk_lk < 1089; hawk_lk += hawk_tm.size) wout_tm0_a.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 1089 + hawk_lk] = mtx_A[i].at(hawk_lk / 33, hawk_lk % 33); }
         { const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here(); for (Int hawk_lk = hawk_tm.rank; hawk_lk < 33; hawk_lk += hawk_tm.size) wout_tm0_x0.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 33 + hawk_lk] = vin_b[i].at(hawk_lk); }
         { const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here(); for (Int hawk_lk = hawk_tm.rank; hawk_lk < 66; hawk_lk += hawk_tm.size) wout_tm0_x1.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 66 + hawk_lk] = mtx_B[i].at(hawk_lk / 2, hawk_lk % 2); }
-        __syncthreads();
+        __syncwarp();
     }
 }
 
-extern "C" __device__ const unsigned int hk_team_threads__team_chol_33_2 = 128u;
-extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_chol_33_2 = 10800u;
-extern "C" __global__ void __launch_bounds__(128) team_chol_33_2(
+extern "C" __device__ const unsigned int hk_team_threads__team_chol_33_2 = 32u;
+extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_chol_33_2 = 9904u;
+extern "C" __global__ void __launch_bounds__(32) team_chol_33_2(
     hk::abi::ScalarHandle p_wout_tm0_a,
     hk::abi::ScalarHandle p_wout_tm0_info,
     hk::abi::ScalarHandle p_wout_tm0_x0,
@@ -66,7 +68,9 @@ extern "C" __global__ void __launch_bounds__(128) team_chol_33_2(
     (void)wout_tm0_x0;
     const hk::ScalarOut<Real> wout_tm0_x1(p_wout_tm0_x1);
     (void)wout_tm0_x1;
-    for (long long hawk_flat = blockIdx.x; hawk_flat < count; hawk_flat += gridDim.x) {
+    hk::linalg::team::begin_entry();
+    const long long hawk_teams = static_cast<long long>(blockDim.x >> 5);
+    for (long long hawk_flat = static_cast<long long>(blockIdx.x) * hawk_teams + (threadIdx.x >> 5); hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
         (void)hawk_i;
@@ -93,7 +97,7 @@ extern "C" __global__ void __launch_bounds__(128) team_chol_33_2(
             const auto hawk_f = hk::linalg::team::TeamCholesky<Real, 33>{hawk_a, hawk_info};
             hk::linalg::team::choSolve<33>(hawk_tm, hawk_f, hawk_x, hawk_x, 2);
         }
-        __syncthreads();
+        __syncwarp();
     }
 }
 

@@ -26,7 +26,9 @@ extern "C" __global__ void __launch_bounds__(256) team_chol_512(
     (void)vin_b;
     const hk::MatIn<Real, 512, 512> mtx_A(p_mtx_A);
     (void)mtx_A;
-    for (long long hawk_flat = blockIdx.x; hawk_flat < count; hawk_flat += gridDim.x) {
+    hk::linalg::team::begin_entry();
+    const long long hawk_teams = static_cast<long long>(blockDim.x >> 5);
+    for (long long hawk_flat = static_cast<long long>(blockIdx.x) * hawk_teams + (threadIdx.x >> 5); hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
         (void)hawk_i;
@@ -35,13 +37,13 @@ extern "C" __global__ void __launch_bounds__(256) team_chol_512(
         const auto vin_b_i = vin_b[i].get();
         { const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here(); for (Int hawk_lk = hawk_tm.rank; hawk_lk < 262144; hawk_lk += hawk_tm.size) wout_tm0_a.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 262144 + hawk_lk] = mtx_A[i].at(hawk_lk / 512, hawk_lk % 512); }
         { const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here(); for (Int hawk_lk = hawk_tm.rank; hawk_lk < 512; hawk_lk += hawk_tm.size) wout_tm0_x0.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 512 + hawk_lk] = vin_b[i].at(hawk_lk); }
-        __syncthreads();
+        __syncwarp();
     }
 }
 
-extern "C" __device__ const unsigned int hk_team_threads__team_chol_512_2 = 256u;
-extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_chol_512_2 = 5120u;
-extern "C" __global__ void __launch_bounds__(256) team_chol_512_2(
+extern "C" __device__ const unsigned int hk_team_threads__team_chol_512_2 = 128u;
+extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_chol_512_2 = 16896u;
+extern "C" __global__ void __launch_bounds__(128) team_chol_512_2(
     hk::abi::ScalarHandle p_wout_tm0_a,
     hk::abi::ScalarHandle p_wout_tm0_info,
     hk::abi::ScalarHandle p_wout_tm0_x0,
@@ -55,7 +57,9 @@ extern "C" __global__ void __launch_bounds__(256) team_chol_512_2(
     (void)wout_tm0_info;
     const hk::ScalarOut<Real> wout_tm0_x0(p_wout_tm0_x0);
     (void)wout_tm0_x0;
-    for (long long hawk_flat = blockIdx.x; hawk_flat < count; hawk_flat += gridDim.x) {
+    hk::linalg::team::begin_entry();
+    const long long hawk_teams = static_cast<long long>(blockDim.x >> 5);
+    for (long long hawk_flat = static_cast<long long>(blockIdx.x) * hawk_teams + (threadIdx.x >> 5); hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
         (void)hawk_i;
@@ -75,7 +79,7 @@ extern "C" __global__ void __launch_bounds__(256) team_chol_512_2(
             const auto hawk_f = hk::linalg::team::TeamCholesky<Real, 512>{hawk_a, hawk_info};
             hk::linalg::team::choSolve<512>(hawk_tm, hawk_f, hawk_x, hawk_x, 1);
         }
-        __syncthreads();
+        __syncwarp();
     }
 }
 

@@ -29,7 +29,9 @@ extern "C" __global__ void __launch_bounds__(256) team_lu_160(
     (void)vin_b;
     const hk::MatIn<Real, 160, 160> mtx_A(p_mtx_A);
     (void)mtx_A;
-    for (long long hawk_flat = blockIdx.x; hawk_flat < count; hawk_flat += gridDim.x) {
+    hk::linalg::team::begin_entry();
+    const long long hawk_teams = static_cast<long long>(blockDim.x >> 5);
+    for (long long hawk_flat = static_cast<long long>(blockIdx.x) * hawk_teams + (threadIdx.x >> 5); hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
         (void)hawk_i;
@@ -39,13 +41,13 @@ extern "C" __global__ void __launch_bounds__(256) team_lu_160(
         { const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here(); for (Int hawk_lk = hawk_tm.rank; hawk_lk < 25600; hawk_lk += hawk_tm.size) wout_tm0_a.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 25600 + hawk_lk] = mtx_A[i].at(hawk_lk / 160, hawk_lk % 160); }
         { const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here(); for (Int hawk_lk = hawk_tm.rank; hawk_lk < 160; hawk_lk += hawk_tm.size) wout_tm0_x0.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 160 + hawk_lk] = vin_b[i].at(hawk_lk); }
         { const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here(); for (Int hawk_lk = hawk_tm.rank; hawk_lk < 25600; hawk_lk += hawk_tm.size) wout_tm1_a.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 25600 + hawk_lk] = mtx_A[i].at(hawk_lk / 160, hawk_lk % 160); }
-        __syncthreads();
+        __syncwarp();
     }
 }
 
-extern "C" __device__ const unsigned int hk_team_threads__team_lu_160_2 = 256u;
-extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_lu_160_2 = 2304u;
-extern "C" __global__ void __launch_bounds__(256) team_lu_160_2(
+extern "C" __device__ const unsigned int hk_team_threads__team_lu_160_2 = 128u;
+extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_lu_160_2 = 5632u;
+extern "C" __global__ void __launch_bounds__(128) team_lu_160_2(
     hk::abi::ScalarHandle p_wout_tm0_a,
     hk::abi::ScalarHandle p_wout_tm0_info,
     hk::abi::ScalarHandle p_wout_tm0_piv,
@@ -74,7 +76,9 @@ extern "C" __global__ void __launch_bounds__(256) team_lu_160_2(
     (void)wout_tm1_info;
     const hk::ScalarOut<std::int32_t> wout_tm1_piv(p_wout_tm1_piv);
     (void)wout_tm1_piv;
-    for (long long hawk_flat = blockIdx.x; hawk_flat < count; hawk_flat += gridDim.x) {
+    hk::linalg::team::begin_entry();
+    const long long hawk_teams = static_cast<long long>(blockDim.x >> 5);
+    for (long long hawk_flat = static_cast<long long>(blockIdx.x) * hawk_teams + (threadIdx.x >> 5); hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
         (void)hawk_i;
@@ -111,7 +115,7 @@ extern "C" __global__ void __launch_bounds__(256) team_lu_160_2(
             const auto hawk_f = hk::linalg::team::TeamLu<Real, 160>{hawk_a, hawk_piv, hawk_info};
             if (hawk_tm.rank == 0) *hawk_x = hk::linalg::team::luDet<160>(hawk_f);
         }
-        __syncthreads();
+        __syncwarp();
     }
 }
 

@@ -35,7 +35,9 @@ extern "C" __global__ void __launch_bounds__(256) team_lu_64(
     (void)mtx_A;
     const hk::MatIn<Real, 64, 2> mtx_B(p_mtx_B);
     (void)mtx_B;
-    for (long long hawk_flat = blockIdx.x; hawk_flat < count; hawk_flat += gridDim.x) {
+    hk::linalg::team::begin_entry();
+    const long long hawk_teams = static_cast<long long>(blockDim.x >> 5);
+    for (long long hawk_flat = static_cast<long long>(blockIdx.x) * hawk_teams + (threadIdx.x >> 5); hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
         (void)hawk_i;
@@ -47,12 +49,12 @@ extern "C" __global__ void __launch_bounds__(256) team_lu_64(
         { const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here(); for (Int hawk_lk = hawk_tm.rank; hawk_lk < 64; hawk_lk += hawk_tm.size) wout_tm0_x0.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 64 + hawk_lk] = vin_b[i].at(hawk_lk); }
         { const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here(); for (Int hawk_lk = hawk_tm.rank; hawk_lk < 128; hawk_lk += hawk_tm.size) wout_tm0_x1.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 128 + hawk_lk] = mtx_B[i].at(hawk_lk / 2, hawk_lk % 2); }
         { const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here(); for (Int hawk_lk = hawk_tm.rank; hawk_lk < 4096; hawk_lk += hawk_tm.size) wout_tm1_a.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 4096 + hawk_lk] = mtx_A[i].at(hawk_lk / 64, hawk_lk % 64); }
-        __syncthreads();
+        __syncwarp();
     }
 }
 
 extern "C" __device__ const unsigned int hk_team_threads__team_lu_64_2 = 128u;
-extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_lu_64_2 = 35840u;
+extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_lu_64_2 = 2560u;
 extern "C" __global__ void __launch_bounds__(128) team_lu_64_2(
     hk::abi::ScalarHandle p_wout_tm0_a,
     hk::abi::ScalarHandle p_wout_tm0_info,
@@ -85,7 +87,9 @@ extern "C" __global__ void __launch_bounds__(128) team_lu_64_2(
     (void)wout_tm1_info;
     const hk::ScalarOut<std::int32_t> wout_tm1_piv(p_wout_tm1_piv);
     (void)wout_tm1_piv;
-    for (long long hawk_flat = blockIdx.x; hawk_flat < count; hawk_flat += gridDim.x) {
+    hk::linalg::team::begin_entry();
+    const long long hawk_teams = static_cast<long long>(blockDim.x >> 5);
+    for (long long hawk_flat = static_cast<long long>(blockIdx.x) * hawk_teams + (threadIdx.x >> 5); hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
         (void)hawk_i;
@@ -130,7 +134,7 @@ extern "C" __global__ void __launch_bounds__(128) team_lu_64_2(
             const auto hawk_f = hk::linalg::team::TeamLu<Real, 64>{hawk_a, hawk_piv, hawk_info};
             if (hawk_tm.rank == 0) *hawk_x = hk::linalg::team::luDet<64>(hawk_f);
         }
-        __syncthreads();
+        __syncwarp();
     }
 }
 

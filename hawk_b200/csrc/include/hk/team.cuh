@@ -1,5 +1,5 @@
 // hawk_b200 device library: team-form linear algebra (one matrix per lane, a
-// block of threads per matrix).
+// team of threads -- one warp -- per matrix).
 //
 // A factorisation too large for one thread's registers (n above the one-thread
 // cap of 32, hawk/ir/linalg.py:33-36, or any n under linalg_form="team") is
@@ -15,11 +15,14 @@
 //     choSolve<n>(hawk_tm, hawk_f, hawk_x, hawk_x, k);     // k right-hand sides, row-major n x k
 //     ...
 //
-// and every call is collective over the block.  The b200 team is the CTA: a
-// call stages the lane's matrix (row stride n + 1, so a column walk is free of
+// and every call is collective over the team.  The b200 team is one warp (a
+// block of the entry serves one lane per warp, so many lanes are in flight
+// per SM and a call's barriers are the warp's): a call stages the lane's matrix (row stride n + 1, so a column walk is free of
 // bank conflicts) and its right-hand sides into the block's dynamic shared
 // memory when the entry was given room for them, works there and writes the
-// results back; otherwise it works in place on the scratch plane (L1/L2).
+// results back; otherwise it works in place on the scratch plane (L1/L2).  A
+// factor left staged by its factorisation is reused by the solves after it
+// (a tag holds the scratch-plane address the staged copy stands for).
 //
 // Bits.  Every element receives the operations of the one-thread form
 // (hk/linalg.cuh, the order hawk/embedded/linalg.py:188-520 restates) in the
@@ -28,12 +31,13 @@
 //  * Cholesky, right-looking: after column k is final, every trailing entry
 //    (i, j) subtracts l_ik * l_jk -- the same ascending-k chain of subtractions
 //    the one-thread form's dot product applies, from the same symmetrised start
-//    0.5 a_ij + 0.5 a_ji; a failed factor (info > 0) is all zeros;
-//  * LU, Crout: column j's running sums acc_i = sum_{k < min(i, j)} a_ik u_kj
-//    start at 0 and add in ascending k (one barrier per k: u_kj is a_kj - acc_k,
-//    final once step k - 1 is done), then a_ij - acc_i; the pivot is the first
-//    row of largest magnitude (a NaN diagonal keeps row j); the pivot value
-//    travels with the reduction so no thread reads a row being swapped;
+//    0.5 a_ij + 0.5 a_ji; one barrier per column; a failed factor (info > 0)
+//    is all zeros;
+//  * LU, Crout, by the team's first warp: column j's running sums
+//    acc_i = sum_{k < min(i, j)} a_ik u_kj start at 0 and add in ascending k
+//    (u_kj = a_kj - acc_k is final once k - 1 is done), then a_ij - acc_i; the
+//    pivot is the first row of largest magnitude (a NaN diagonal keeps row j),
+//    its value travels with the warp reduction;
 //  * forward sweeps run column-oriented (each x_i subtracts l_ij x_j as x_j
 //    becomes final, ascending j, then divides); backward sweeps keep the
 //    one-thread form's ascending-j dot product per row, so they run one thread
@@ -41,7 +45,6 @@
 #pragma once
 #include "base.cuh"
 #include "math.cuh"
-#include "stage.cuh"
 
 namespace hk {
 namespace linalg {
@@ -49,9 +52,9 @@ namespace team {
 
 #if defined(__CUDACC__) || defined(__CUDACC_RTC__)
 
-// The reduction scratch at the head of the dynamic shared memory: one slot per
-// warp (key, value, index) for the pivot search.
-constexpr unsigned kScratchBytes = 1024u;
+// The head of a team entry's dynamic shared memory: the staged-factor tag
+// (below) in its last 16 bytes; the staged matrix and right-hand sides follow.
+constexpr unsigned kScratchBytes = 128u;
 
 HK_FI unsigned char* dynamic_smem() {
     extern __shared__ __align__(16) unsigned char hk_team_dyn[];
@@ -66,26 +69,47 @@ HK_FI unsigned dynamic_smem_bytes() {
 
 HK_HD constexpr unsigned round16(unsigned long long b) { return static_cast<unsigned>((b + 15ull) & ~15ull); }
 
-// Bytes of dynamic shared memory a call on an n x n matrix with k right-hand
-// sides stages into: scratch, the LU running sums, the matrix (row stride
-// n + 1) and the right-hand sides.  The build gives a team entry the largest of
-// its calls' needs when that fits, else only the first two parts.
+// Bytes of dynamic shared memory a team's calls on an n x n matrix with k
+// right-hand sides use: the head and the products row of the backward sweeps
+// (inplace_bytes), plus, to stage, the matrix (row stride n + 1) and the
+// right-hand sides.  The build gives each team of an entry the largest staged
+// need of its calls when that fits, else the in-place need.
+template <class T> HK_HD constexpr unsigned inplace_bytes(int n) { return kScratchBytes + round16(sizeof(T) * n); }
 template <class T> HK_HD constexpr unsigned staged_bytes(int n, int k) {
-    return kScratchBytes + round16(sizeof(T) * n) + round16(sizeof(T) * n * (n + 1)) + round16(sizeof(T) * n * k);
+    return inplace_bytes<T>(n) + round16(sizeof(T) * n * (n + 1)) + round16(sizeof(T) * n * k);
 }
-template <class T> HK_HD constexpr unsigned base_bytes(int n) { return kScratchBytes + round16(sizeof(T) * n); }
 
-// The error bit a team call sets in the unit's hk_error_flags when its entry
-// was launched with less dynamic shared memory than the call's scratch needs
-// (the call then writes nothing but info = -1).
-constexpr unsigned kErrTeamSmem = 8u;
-
+// The team of a lane: one warp.  A team entry's block holds several warps,
+// each on a lane of its own (the team frame), so a call's barrier is the
+// warp's and many lanes are in flight per SM; the block's dynamic shared
+// memory is split evenly between its warps, each staging into its own part.
 struct Team {
-    int rank;
-    int size;
-    static HK_FI Team here() { return Team{static_cast<int>(threadIdx.x), static_cast<int>(blockDim.x)}; }
-    HK_FI void sync() const { __syncthreads(); }
+    int rank;                   // the thread's place in the team (its lane in the warp)
+    int size;                   // 32
+    unsigned char* smem;        // this team's part of the block's dynamic shared memory
+    unsigned bytes;             // its size
+    static HK_FI Team here() {
+        const unsigned warps = blockDim.x >> 5;
+        const unsigned part = (dynamic_smem_bytes() / (warps ? warps : 1u)) & ~15u;
+        return Team{static_cast<int>(threadIdx.x & 31u), 32, dynamic_smem() + (threadIdx.x >> 5) * part, part};
+    }
+    HK_FI void sync() const { __syncwarp(); }
 };
+
+// The staged-factor tag at the end of a team's head: the scratch-plane
+// address of the matrix its staged copy holds (a factor a solve can reuse).
+constexpr unsigned kTagOffset = kScratchBytes - 16u;
+HK_FI const void* volatile* tag_slot(const Team& tm) {
+    return reinterpret_cast<const void* volatile*>(tm.smem + kTagOffset);
+}
+
+// At the start of a team entry: no staged copy is held yet.  Every thread of
+// the block calls it.
+HK_FI void begin_entry() {
+    const Team tm = Team::here();
+    if (tm.bytes >= kScratchBytes && tm.rank == 0) *tag_slot(tm) = nullptr;
+    __syncwarp();
+}
 
 template <class T, int N> struct TeamCholesky {
     T* a;
@@ -107,8 +131,6 @@ template <class T> struct Mat {
     HK_FI T& operator()(int i, int j) const { return p[static_cast<long long>(i) * ld + j]; }
 };
 
-template <class T> HK_FI T* acc_of(int) { return reinterpret_cast<T*>(dynamic_smem() + kScratchBytes); }
-
 // The working copy of a call: the matrix (staged or the scratch plane itself)
 // and the right-hand sides (staged or in place).
 template <class T, int N> struct Work {
@@ -117,20 +139,45 @@ template <class T, int N> struct Work {
     bool staged;
 };
 
-template <class T, int N> HK_FI Work<T, N> work(T* a, T* x, int k) {
-    const bool staged = dynamic_smem_bytes() >= staged_bytes<T>(N, k);
+template <class T, int N> HK_FI Work<T, N> work(const Team& tm, T* a, T* x, int k) {
+    const bool staged = tm.bytes >= staged_bytes<T>(N, k);
     if (!staged) return Work<T, N>{Mat<T>{a, N}, x, false};
-    unsigned char* base = dynamic_smem() + kScratchBytes + round16(sizeof(T) * N);
+    unsigned char* base = tm.smem + inplace_bytes<T>(N);
     T* m = reinterpret_cast<T*>(base);
     T* xs = reinterpret_cast<T*>(base + round16(sizeof(T) * N * (N + 1)));
     return Work<T, N>{Mat<T>{m, N + 1}, xs, true};
 }
 
-// matrix: plane (stride N) -> working copy, then a barrier
+// An elementwise pass over e in [0, count) by the team, U entries of a thread
+// at a time with every load of the batch issued before any store (the
+// compiler cannot tell the two sides apart, and in place they may be the same
+// array): value(e) is read, store(e, v) written.
+template <int U, class V, class S> HK_FI void batched(const Team& tm, int count, V value, S store) {
+    for (int e0 = tm.rank; e0 < count; e0 += U * tm.size) {
+        decltype(value(0)) v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (e0 + u * tm.size < count) v[u] = value(e0 + u * tm.size);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (e0 + u * tm.size < count) store(e0 + u * tm.size, v[u]);
+    }
+}
+
+// matrix: plane (stride N) -> working copy, then a barrier; a copy the
+// staged area already holds (the factor the previous call made) is kept
 template <class T, int N> HK_FI void load_matrix(const Team& tm, const Work<T, N>& w, const T* a) {
-    if (w.staged)
-        for (int e = tm.rank; e < N * N; e += tm.size) w.m(e / N, e % N) = a[e];
+    if (w.staged && *tag_slot(tm) != static_cast<const void*>(a)) {
+        tm.sync();              // every thread has read the tag before it changes
+        batched<8>(tm, N * N, [&](int e) { return a[e]; }, [&](int e, T v) { w.m(e / N, e % N) = v; });
+        if (tm.rank == 0) *tag_slot(tm) = a;
+    }
     tm.sync();
+}
+
+// the staged area now holds the final matrix of plane address a (or nothing)
+template <class T> HK_FI void set_tag(const Team& tm, const T* a) {
+    if (tm.rank == 0) *tag_slot(tm) = a;
 }
 
 template <class T, int N> HK_FI void load_rhs(const Team& tm, const Work<T, N>& w, const T* x, int k) {
@@ -185,13 +232,36 @@ HK_FI void forward(const Team& tm, T* x, int k, E entry, D diag) {
 
 // Backward sweep: for i descending, acc = x_i; acc -= e(i, j) * x_j over
 // j = i + 1 .. N - 1 ascending; x_i = acc (/ d(i) when `div`).  The one-thread
-// form's order, one thread per right-hand-side column.
+// form's order: the subtractions of a row are one chain, so one thread runs
+// it; the products it subtracts (independent of one another, all of final
+// x_j) are made by the whole team into the products row first.
 template <class T, int N, bool DIV, class E, class D>
 HK_FI void backward(const Team& tm, T* x, int k, E entry, D diag) {
+    if (tm.bytes >= inplace_bytes<T>(N)) {
+        T* prod = reinterpret_cast<T*>(tm.smem + kScratchBytes);
+        for (int c = 0; c < k; ++c) {
+            for (int r = 0; r < N; ++r) {
+                const int i = N - 1 - r;
+                for (int j = i + 1 + tm.rank; j < N; j += tm.size) prod[j] = entry(i, j) * x[j * k + c];
+                tm.sync();
+                if (tm.rank == 0) {
+                    T acc = x[i * k + c];
+#pragma unroll 8
+                    for (int j = i + 1; j < N; ++j) acc = acc - prod[j];
+                    x[i * k + c] = DIV ? acc / diag(i) : acc;
+                }
+                tm.sync();
+            }
+        }
+        return;
+    }
     for (int c = tm.rank; c < k; c += tm.size) {
         for (int r = 0; r < N; ++r) {
             const int i = N - 1 - r;
             T acc = x[i * k + c];
+            // the products are independent of the chain: unrolled so their loads
+            // are in flight while the subtractions run in order
+#pragma unroll 8
             for (int j = i + 1; j < N; ++j) acc = acc - (entry(i, j) * x[j * k + c]);
             x[i * k + c] = DIV ? acc / diag(i) : acc;
         }
@@ -225,40 +295,99 @@ template <class T, int N> HK_FI void swaps(const Team& tm, T* x, int k, const st
 // zeros (what the one-thread form's factor reads as).
 template <int N, class T>
 HK_FI void cholesky(const Team& tm, const TeamCholesky<T, N>& f, T* a) {
-    const detail::Work<T, N> w = detail::work<T, N>(a, nullptr, 0);
+    const detail::Work<T, N> w = detail::work<T, N>(tm, a, nullptr, 0);
+    if (w.staged) {
+        tm.sync();              // every thread has read the tag before it changes
+        detail::set_tag(tm, static_cast<const T*>(nullptr));
+    }
     // the symmetrised lower triangle: (0.5 a_ij) + (0.5 a_ji); the reads of the
     // upper triangle are not overwritten by this pass
-    for (int e = tm.rank; e < N * N; e += tm.size) {
-        const int i = e / N, j = e % N;
-        if (j <= i) w.m(i, j) = (T(0.5) * a[i * N + j]) + (T(0.5) * a[j * N + i]);
+    detail::batched<8>(tm, N * N,
+               [&](int e) {
+                   const int i = e / N, j = e % N;
+                   return j <= i ? (T(0.5) * a[i * N + j]) + (T(0.5) * a[j * N + i]) : T(0);
+               },
+               [&](int e, T v) {
+                   if (e % N <= e / N) w.m(e / N, e % N) = v;
+               });
+    tm.sync();
+    // column 0: its diagonal and the division of the entries below it
+    int info = 0;
+    T d = w.m(0, 0);
+    T lkk = T(0);
+    if (!(d > T(0))) {
+        info = 1;
+    } else {
+        lkk = math::sqrt(d);
+        for (int i = 1 + tm.rank; i < N; i += tm.size) w.m(i, 0) = w.m(i, 0) / lkk;
     }
     tm.sync();
-    int info = 0;
-    for (int k = 0; k < N; ++k) {
-        const T d = w.m(k, k);
+    // step k: column k is final below its diagonal and l_kk is every thread's;
+    // each thread works out d_{k+1} (the diagonal's last subtraction) and its
+    // root, then every trailing entry subtracts l_ik l_jk, the entries of
+    // column k + 1 also dividing by l_{k+1}: one barrier per column.  The
+    // diagonal entry (k+1, k+1) is written as l_{k+1} in the next step, when
+    // no thread reads its old value any more.
+    for (int k = 0; info == 0 && k + 1 < N; ++k) {
+        if (tm.rank == 0) w.m(k, k) = lkk;
+        const T lk1 = w.m(k + 1, k);
+        d = w.m(k + 1, k + 1) - (lk1 * lk1);
         if (!(d > T(0))) {
-            info = k + 1;
+            info = k + 2;
             break;
         }
-        const T lkk = math::sqrt(d);
-        for (int i = k + 1 + tm.rank; i < N; i += tm.size) w.m(i, k) = w.m(i, k) / lkk;
-        tm.sync();
-        if (tm.rank == 0) w.m(k, k) = lkk;
+        const T lnext = math::sqrt(d);
         const int m = N - 1 - k;
         const int tri = m * (m + 1) / 2;
-        for (int e = tm.rank; e < tri; e += tm.size) {
-            int r, c;
-            detail::tri_index(e, &r, &c);
-            const int i = k + 1 + r, j = k + 1 + c;
-            w.m(i, j) = w.m(i, j) - (w.m(i, k) * w.m(j, k));
+        int r = 0, c = 0;
+        if (tm.rank < tri) detail::tri_index(tm.rank, &r, &c);
+        // the entries of one step are independent: four of a thread's at a
+        // time, every load issued before any store
+        for (int e0 = tm.rank; e0 < tri; e0 += 4 * tm.size) {
+            int ii[4], jj[4];
+            bool live[4];
+            T aij[4], aik[4], ajk[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                ii[u] = k + 1 + r;
+                jj[u] = k + 1 + c;
+                live[u] = e0 + u * tm.size < tri && !(ii[u] == k + 1 && jj[u] == k + 1);
+                c += tm.size;                     // the next entry of this thread
+                while (c > r) {
+                    c -= r + 1;
+                    ++r;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (live[u]) {
+                    aij[u] = w.m(ii[u], jj[u]);
+                    aik[u] = w.m(ii[u], k);
+                    ajk[u] = w.m(jj[u], k);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (live[u]) {
+                    T v = aij[u] - (aik[u] * ajk[u]);
+                    if (jj[u] == k + 1) v = v / lnext;
+                    w.m(ii[u], jj[u]) = v;
+                }
+            }
         }
+        lkk = lnext;
         tm.sync();
     }
-    for (int e = tm.rank; e < N * N; e += tm.size) {
-        const int i = e / N, j = e % N;
-        a[e] = (info == 0 && j <= i) ? w.m(i, j) : T(0);
-    }
+    if (info == 0 && tm.rank == 0) w.m(N - 1, N - 1) = lkk;
+    tm.sync();
+    detail::batched<8>(tm, N * N,
+                       [&](int e) {
+                           const int i = e / N, j = e % N;
+                           return (info == 0 && j <= i) ? w.m(i, j) : T(0);
+                       },
+                       [&](int e, T v) { a[e] = v; });
     if (tm.rank == 0) *f.info = info;
+    if (w.staged && info == 0) detail::set_tag(tm, static_cast<const T*>(a));
     tm.sync();
 }
 
@@ -275,12 +404,13 @@ HK_FI void choleskyFrom(const Team& tm, const TeamCholesky<T, N>& f, T* a) {
             break;
         }
     }
-    tm.sync();                  // every thread has read the diagonal before it changes
+    tm.sync();                  // every thread has read the diagonal (and the tag) before they change
     for (int e = tm.rank; e < N * N; e += tm.size) {
         const int i = e / N, j = e % N;
         if (info != 0 || j > i) a[e] = T(0);
     }
     if (tm.rank == 0) *f.info = info;
+    if (tm.bytes >= kScratchBytes) detail::set_tag(tm, static_cast<const T*>(nullptr));
     tm.sync();
 }
 
@@ -296,7 +426,7 @@ HK_FI void choSolve(const Team& tm, const TeamCholesky<T, N>& f, const T* b, T* 
         for (int e = tm.rank; e < N * k; e += tm.size) x[e] = b[e];
         tm.sync();
     }
-    const detail::Work<T, N> w = detail::work<T, N>(f.a, x, k);
+    const detail::Work<T, N> w = detail::work<T, N>(tm, f.a, x, k);
     detail::load_matrix<T, N>(tm, w, f.a);
     detail::load_rhs<T, N>(tm, w, x, k);
     const detail::Mat<T> l = w.m;
@@ -312,7 +442,7 @@ HK_FI void triLower(const Team& tm, const TeamCholesky<T, N>& f, const T* b, T* 
         for (int e = tm.rank; e < N * k; e += tm.size) x[e] = b[e];
         tm.sync();
     }
-    const detail::Work<T, N> w = detail::work<T, N>(f.a, x, k);
+    const detail::Work<T, N> w = detail::work<T, N>(tm, f.a, x, k);
     detail::load_matrix<T, N>(tm, w, f.a);
     detail::load_rhs<T, N>(tm, w, x, k);
     const detail::Mat<T> l = w.m;
@@ -326,7 +456,7 @@ HK_FI void triUpperT(const Team& tm, const TeamCholesky<T, N>& f, const T* b, T*
         for (int e = tm.rank; e < N * k; e += tm.size) x[e] = b[e];
         tm.sync();
     }
-    const detail::Work<T, N> w = detail::work<T, N>(f.a, x, k);
+    const detail::Work<T, N> w = detail::work<T, N>(tm, f.a, x, k);
     detail::load_matrix<T, N>(tm, w, f.a);
     detail::load_rhs<T, N>(tm, w, x, k);
     const detail::Mat<T> l = w.m;
@@ -337,107 +467,111 @@ HK_FI void triUpperT(const Team& tm, const TeamCholesky<T, N>& f, const T* b, T*
 // ------------------------------------------------------------------------ LU
 
 // P A = L U in place (Crout, column by column); piv[j] = the row exchanged
-// with row j at step j; info = first zero pivot column (1-based).
+// with row j at step j; info = first zero pivot column (1-based).  Row i's
+// running sum lives in the registers of lane i % 32, u_kj goes from the lane
+// owning row k to the others by a shuffle, the pivot is a warp reduction.
 template <int N, class T>
 HK_FI void lu(const Team& tm, const TeamLu<T, N>& f, T* a) {
-    if (dynamic_smem_bytes() < base_bytes<T>(N)) {
-        if (tm.rank == 0) {
-            stage::fail(kErrTeamSmem);
-            *f.info = -1;
-        }
+    const detail::Work<T, N> w = detail::work<T, N>(tm, a, nullptr, 0);
+    if (w.staged) {
+        tm.sync();              // every thread has read the tag before it changes
+        detail::set_tag(tm, static_cast<const T*>(nullptr));
         tm.sync();
-        return;
     }
-    const detail::Work<T, N> w = detail::work<T, N>(a, nullptr, 0);
     detail::load_matrix<T, N>(tm, w, a);
-    T* acc = detail::acc_of<T>(N);
-    T* red_key = reinterpret_cast<T*>(dynamic_smem());
-    T* red_val = red_key + 32;
-    int* red_idx = reinterpret_cast<int*>(red_val + 32);
-    for (int i = tm.rank; i < N; i += tm.size) acc[i] = T(0);
-    tm.sync();
+    constexpr int R = (N + 31) / 32;        // rows per lane
+    constexpr unsigned kAll = 0xffffffffu;
     int info = 0;
-    const int lane = tm.rank & 31, warp = tm.rank >> 5, warps = (tm.size + 31) >> 5;
-    for (int j = 0; j < N; ++j) {
-        // running sums: acc_i += a_ik * u_kj once u_kj = a_kj - acc_k is final
-        for (int k = 0; k + 1 < N && k < j; ++k) {
-            const T ukj = w.m(k, j) - acc[k];
-            for (int i = k + 1 + tm.rank; i < N; i += tm.size) acc[i] = acc[i] + (w.m(i, k) * ukj);
-            tm.sync();
-        }
-        for (int i = tm.rank; i < N; i += tm.size) {
-            w.m(i, j) = w.m(i, j) - acc[i];
-            acc[i] = T(0);
-        }
-        tm.sync();
-        // pivot: the first row of largest magnitude at or below the diagonal
-        const T ajj = w.m(j, j);
-        T bkey = T(-2), bval = T(0);
-        int bidx = N;
-        for (int i = j + tm.rank; i < N; i += tm.size) {
-            const T v = w.m(i, j);
-            const T mag = math::abs(v);
-            const T key = math::isnan(mag) ? T(-1) : mag;
-            if (key > bkey) {
-                bkey = key;
-                bval = v;
-                bidx = i;
-            }
-        }
-        for (int off = 16; off > 0; off >>= 1) {
-            const T ok = __shfl_down_sync(0xffffffffu, bkey, off);
-            const T ov = __shfl_down_sync(0xffffffffu, bval, off);
-            const int oi = __shfl_down_sync(0xffffffffu, bidx, off);
-            if (lane + off < 32 && (ok > bkey || (ok == bkey && oi < bidx))) {
-                bkey = ok;
-                bval = ov;
-                bidx = oi;
-            }
-        }
-        if (lane == 0) {
-            red_key[warp] = bkey;
-            red_val[warp] = bval;
-            red_idx[warp] = bidx;
-        }
-        tm.sync();
-        T pkey = red_key[0], pj = red_val[0];
-        int p = red_idx[0];
-        for (int q = 1; q < warps; ++q) {
-            const T ok = red_key[q];
-            const int oi = red_idx[q];
-            if (ok > pkey || (ok == pkey && oi < p)) {
-                pkey = ok;
-                pj = red_val[q];
-                p = oi;
-            }
-        }
-        if (math::isnan(math::abs(ajj))) {
-            p = j;
-            pj = ajj;
-        }
-        if (tm.rank == 0) f.piv[j] = p;
-        if (pj != T(0)) {
-            const T rcp = T(1) / pj;
-            if (p != j)
-                for (int c = tm.rank; c < N; c += tm.size) {
-                    if (c == j) continue;
-                    const T t = w.m(j, c);
-                    w.m(j, c) = w.m(p, c);
-                    w.m(p, c) = t;
+    if (tm.rank < 32) {
+        const int lane = tm.rank;
+        for (int j = 0; j < N; ++j) {
+            T acc[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) acc[r] = T(0);
+            // Crout: acc_i = sum_{k < min(i, j)} a_ik u_kj, ascending k from 0;
+            // u_kj = a_kj - acc_k is final once every k' < k was added
+            for (int k = 0; k < j; ++k) {
+                const int slot = k >> 5;
+                T mine = T(0);
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+                    if (r == slot) mine = acc[r];
+                const T ukj = __shfl_sync(kAll, w.m(k, j) - mine, k & 31);
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int i = lane + 32 * r;
+                    if (i > k && i < N) acc[r] = acc[r] + (w.m(i, k) * ukj);
                 }
-            for (int i = j + 1 + tm.rank; i < N; i += tm.size)
-                if (i != p) w.m(i, j) = w.m(i, j) * rcp;
-            if (tm.rank == 0 && p != j) {
-                w.m(p, j) = ajj * rcp;
-                w.m(j, j) = pj;
             }
-        } else if (info == 0) {
-            info = j + 1;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int i = lane + 32 * r;
+                if (i < N) w.m(i, j) = w.m(i, j) - acc[r];
+            }
+            __syncwarp();
+            // pivot: the first row of largest magnitude at or below the diagonal
+            const T ajj = w.m(j, j);
+            T bkey = T(-2), bval = T(0);
+            int bidx = N;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int i = lane + 32 * r;
+                if (i >= j && i < N) {
+                    const T v = w.m(i, j);
+                    const T mag = math::abs(v);
+                    const T key = math::isnan(mag) ? T(-1) : mag;
+                    if (key > bkey) {
+                        bkey = key;
+                        bval = v;
+                        bidx = i;
+                    }
+                }
+            }
+            for (int off = 16; off > 0; off >>= 1) {
+                const T ok = __shfl_xor_sync(kAll, bkey, off);
+                const T ov = __shfl_xor_sync(kAll, bval, off);
+                const int oi = __shfl_xor_sync(kAll, bidx, off);
+                if (ok > bkey || (ok == bkey && oi < bidx)) {
+                    bkey = ok;
+                    bval = ov;
+                    bidx = oi;
+                }
+            }
+            int p = bidx;
+            T pj = bval;
+            if (math::isnan(math::abs(ajj))) {
+                p = j;
+                pj = ajj;
+            }
+            __syncwarp();       // every lane has read a_jj before it changes
+            if (lane == 0) f.piv[j] = p;
+            if (pj != T(0)) {
+                const T rcp = T(1) / pj;
+                if (p != j)
+                    for (int c = lane; c < N; c += 32) {
+                        if (c == j) continue;
+                        const T t = w.m(j, c);
+                        w.m(j, c) = w.m(p, c);
+                        w.m(p, c) = t;
+                    }
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int i = lane + 32 * r;
+                    if (i > j && i < N && i != p) w.m(i, j) = w.m(i, j) * rcp;
+                }
+                if (lane == 0 && p != j) {
+                    w.m(p, j) = ajj * rcp;
+                    w.m(j, j) = pj;
+                }
+            } else if (info == 0) {
+                info = j + 1;
+            }
+            __syncwarp();
         }
-        tm.sync();
     }
+    tm.sync();
     if (w.staged)
-        for (int e = tm.rank; e < N * N; e += tm.size) a[e] = w.m(e / N, e % N);
+        detail::batched<8>(tm, N * N, [&](int e) { return w.m(e / N, e % N); }, [&](int e, T v) { a[e] = v; });
     if (tm.rank == 0) *f.info = info;
     tm.sync();
 }
@@ -454,7 +588,7 @@ HK_FI void luSolve(const Team& tm, const TeamLu<T, N>& f, const T* b, T* x, int 
         for (int e = tm.rank; e < N * k; e += tm.size) x[e] = b[e];
         tm.sync();
     }
-    const detail::Work<T, N> w = detail::work<T, N>(f.a, x, k);
+    const detail::Work<T, N> w = detail::work<T, N>(tm, f.a, x, k);
     detail::load_matrix<T, N>(tm, w, f.a);
     detail::load_rhs<T, N>(tm, w, x, k);
     const detail::Mat<T> u = w.m;
@@ -476,7 +610,7 @@ HK_FI void luSolveT(const Team& tm, const TeamLu<T, N>& f, const T* b, T* x, int
         for (int e = tm.rank; e < N * k; e += tm.size) x[e] = b[e];
         tm.sync();
     }
-    const detail::Work<T, N> w = detail::work<T, N>(f.a, x, k);
+    const detail::Work<T, N> w = detail::work<T, N>(tm, f.a, x, k);
     detail::load_matrix<T, N>(tm, w, f.a);
     detail::load_rhs<T, N>(tm, w, x, k);
     const detail::Mat<T> u = w.m;

@@ -225,7 +225,7 @@ template <class T, int N> struct VecOut {
         }
         // a value that lives in a scratch slice: copied element by element
         template <int C2> HK_FI void operator=(const Slice<T, N, C2>& v) const {
-#pragma unroll 1
+#pragma unroll 16
             for (int k = 0; k < N; ++k) st_out(q + static_cast<u64>(k) * pitch, v.flat(k));
         }
         HK_FI T& operator[](int k) const { return q[static_cast<u64>(k) * pitch]; }
@@ -264,7 +264,7 @@ template <class T, int R, int C> struct MatOut {
         }
         // a value that lives in a scratch slice: copied element by element
         HK_FI void operator=(const Slice<T, R, C>& a) const {
-#pragma unroll 1
+#pragma unroll 16
             for (int k = 0; k < R * C; ++k) st_out(q + static_cast<u64>(k) * pitch, a.flat(k));
         }
         HK_FI T& operator()(int r, int c) const { return q[static_cast<u64>(r * C + c) * pitch]; }
@@ -329,7 +329,7 @@ template <class T, int... D> HK_FI T flat_of(const Item<T, D...>& s, int k) { re
 // thousands of elements (a factor read back from a team stage) is copied
 // straight from where it lives into the output plane, never held whole.
 template <class Dst, class Src> HK_FI void store(const Dst& dst, const Src& src) {
-#pragma unroll 1
+#pragma unroll 16
     for (int k = 0; k < Dst::size(); ++k) dst.flat(k) = detail::flat_of(src, k);
 }
 }  // namespace rt

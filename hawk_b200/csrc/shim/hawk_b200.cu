@@ -337,9 +337,10 @@ int hkb_library_entry(hkb_library* lib, const char* name, hkb_entry** out) {
 
 static int64_t grid_for(const hkb_entry* entry, int64_t count) {
     const int64_t cap = static_cast<int64_t>(entry->lib->sms) * entry->blocks_per_sm;
-    // a team entry takes one lane per block per trip; every other entry one
+    // a team entry takes one lane per warp per trip; every other entry one
     // sample (or row) per thread
-    int64_t need = entry->team != 0 ? count : (count + entry->block - 1) / entry->block;
+    const int64_t per_block = entry->team != 0 ? entry->block / 32 : entry->block;
+    int64_t need = (count + per_block - 1) / per_block;
     if (need < 1) need = 1;
     return need < cap ? need : cap;
 }
@@ -471,8 +472,21 @@ int hkb_entry_launch(hkb_entry* entry, hkb_argblock* block, int64_t base, int64_
     args.push_back(&b);
     args.push_back(&c);
     args.push_back(&ns);
-    const dim3 grid(static_cast<unsigned>(grid_for(entry, count)));
-    const cudaError_t err = cudaLaunchKernel(reinterpret_cast<const void*>(entry->kernel), grid, dim3(entry->block),
+    // A launch of fewer samples than one block per SM (a reader stage of a few
+    // thousand lanes, a small partition) runs in smaller blocks, so that every
+    // SM takes a share: whole warps, at least 32 threads.  Entries that stage
+    // through shared memory keep their block.
+    int threads = entry->block;
+    if (entry->team == 0 && entry->dynamic_smem == 0 && count < static_cast<int64_t>(entry->lib->sms) * threads) {
+        const int64_t per_sm = (count + entry->lib->sms - 1) / entry->lib->sms;
+        const int64_t warps = (per_sm + 31) / 32;
+        threads = static_cast<int>(warps < 1 ? 32 : (warps * 32 < threads ? warps * 32 : threads));
+    }
+    const int64_t per_block = entry->team != 0 ? threads / 32 : threads;
+    const int64_t need = (count + per_block - 1) / per_block;
+    const int64_t cap = static_cast<int64_t>(entry->lib->sms) * entry->blocks_per_sm * (entry->block / threads);
+    const dim3 grid(static_cast<unsigned>(need < 1 ? 1 : (need < cap ? need : cap)));
+    const cudaError_t err = cudaLaunchKernel(reinterpret_cast<const void*>(entry->kernel), grid, dim3(threads),
                                              args.data(), entry->dynamic_smem, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return cuda_fail(err, "launching the entry");
     return HKB_OK;

@@ -29,37 +29,48 @@ from .assemble import MODES, Unit, prelude_lines, refuse_unbuilt, render_unit
 from .wrapper import B200
 from .writer import B200_WRITER, body_text
 
-#: Dynamic shared memory a team entry may stage into (of the 227 KB a block
-#: can have): above it the calls work on the scratch planes in place.
-TEAM_SMEM_LIMIT = 200 * 1024
+#: Dynamic shared memory the teams of one SM may stage into (of its 228 KB).
+TEAM_SMEM_LIMIT = 220 * 1024
+#: Teams (warps, one lane each) per SM that must fit staged for a stage to
+#: stage at all: below it, working in place through L1/L2 with more lanes in
+#: flight is the faster of the two.
+TEAM_STAGED_WARPS = 16
+#: Warps per block of a team entry that works in place (a staged one takes one
+#: warp per block, so as many blocks as fit share an SM).
+TEAM_WARPS_IN_PLACE = 4
 
 
 def _round16(b: int) -> int:
     return (b + 15) & ~15
 
 
+def _inplace_bytes(n: int, elem: int) -> int:
+    """hk::linalg::team::inplace_bytes: the head (the staged-factor tag) and
+    the products row of the backward sweeps."""
+    return 128 + _round16(elem * n)
+
+
 def _staged_bytes(n: int, k: int, elem: int) -> int:
-    """hk::linalg::team::staged_bytes: scratch, running sums, matrix (stride n + 1), right-hand sides."""
-    return 1024 + _round16(elem * n) + _round16(elem * n * (n + 1)) + _round16(elem * n * k)
+    """hk::linalg::team::staged_bytes: the in-place part, the matrix (row
+    stride n + 1), the right-hand sides."""
+    return _inplace_bytes(n, elem) + _round16(elem * n * (n + 1)) + _round16(elem * n * k)
 
 
-def _base_bytes(n: int, elem: int) -> int:
-    return 1024 + _round16(elem * n)
-
-
-def team_smem(spec, elem: int) -> int:
-    """The dynamic shared memory of a team stage: the largest staged need of
-    its calls when that fits TEAM_SMEM_LIMIT, else the scratch and running
-    sums every call needs (the calls then work in place)."""
-    needs, bases = [], []
+def team_geometry(spec, elem: int) -> tuple:
+    """``(threads, smem)`` of a team stage's block.  A team is one warp
+    (hk/team.cuh).  When the largest staged need of the stage's calls leaves
+    room for TEAM_STAGED_WARPS teams per SM, a block is one team with that much
+    dynamic shared memory; else a block is TEAM_WARPS_IN_PLACE teams with none
+    (the calls work in place on the scratch planes, through L1 and L2)."""
+    needs, inplace = [], [0]
     for step in spec.steps:
         n = int(step.n)
         k = n if step.op == "lu_inverse" else int(step.k or 0)
         needs.append(_staged_bytes(n, k, elem))
-        bases.append(_base_bytes(n, elem))
-    if not needs:
-        return 0
-    return max(needs) if max(needs) <= TEAM_SMEM_LIMIT else max(bases)
+        inplace.append(_inplace_bytes(n, elem))
+    if needs and max(needs) * TEAM_STAGED_WARPS <= TEAM_SMEM_LIMIT:
+        return 32, max(needs)
+    return 32 * TEAM_WARPS_IN_PLACE, max(inplace) * TEAM_WARPS_IN_PLACE
 
 
 def expand(kernel, name: str):
@@ -116,7 +127,7 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
             continue
         if isinstance(member, TeamStage):
             body = body_text(member.fused_body().text)
-            smem = team_smem(member.team, elem)
+            threads, smem = team_geometry(member.team, elem)
         else:                       # a copy stage: the stage's own sinks, a block per lane
             from hawk.emit.render import render_body
 

@@ -134,20 +134,25 @@ class B200Wrapper:
         return "    }"
 
     def team_prologue(self) -> str:
-        """The team frame (hawk/emit/cuda.py:82-92 makes the lane the block): a
-        block-stride loop over the partition's lanes, one lane per block per
-        trip, every thread of the block on the same lane (the team's calls are
-        collective); the grid is the runtime's, at most the resident blocks."""
-        return ("    for (long long hawk_flat = blockIdx.x; hawk_flat < count; hawk_flat += gridDim.x) {\n"
+        """The team frame.  The reference makes the lane the block
+        (hawk/emit/cuda.py:82-92); here the team of a lane is one warp
+        (hk/team.cuh), so a block of the entry's threads serves one lane per
+        warp: a grid-stride loop over the partition's lanes by warps, every
+        thread of a warp on the same lane (the team's calls are collective);
+        the grid is the runtime's, at most the resident blocks."""
+        return ("    hk::linalg::team::begin_entry();\n"
+                "    const long long hawk_teams = static_cast<long long>(blockDim.x >> 5);\n"
+                "    for (long long hawk_flat = static_cast<long long>(blockIdx.x) * hawk_teams + (threadIdx.x >> 5); "
+                "hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {\n"
                 "        const long long hawk_i = base + hawk_flat;\n"
                 "        const hk::SampleIndex i{hawk_i};\n"
                 "        (void)hawk_i;\n"
                 "        (void)nSamples;")
 
     def team_epilogue(self) -> str:
-        """The end of a team trip: the block leaves the lane together (its
-        shared memory is the next lane's)."""
-        return "        __syncthreads();\n    }"
+        """The end of a team trip: the warp leaves the lane together (its part
+        of the shared memory is its next lane's)."""
+        return "        __syncwarp();\n    }"
 
     def unpack(self, walk, plan: "StagePlan | None" = None) -> str:
         """Every slot's view, in ``arg_spec`` order; a promoted Param's one-cell

@@ -80,8 +80,7 @@ void hkb_library_free(hkb_library* lib);
 
 /* The unit's error word (0 when every bounded wait of its entries completed;
  * bit 1: a staged tile did not arrive in time, 2: a stage was not released in
- * time, 4: copies were still in flight when a CTA gave up, 8: a team-form call
- * was launched with less shared memory than its scratch needs), read after the
+ * time, 4: copies were still in flight when a CTA gave up), read after the
  * launches it covers have completed; `clear` resets it.  A unit without the
  * word reads 0.  The reference's host target has no device waits to report. */
 int hkb_library_errors(hkb_library* lib, unsigned* flags, int clear);
