@@ -49,9 +49,9 @@ extern "C" __global__ void __launch_bounds__(256) team_chol_64(
     }
 }
 
-extern "C" __device__ const unsigned int hk_team_threads__team_chol_64_2 = 128u;
-extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_chol_64_2 = 2560u;
-extern "C" __global__ void __launch_bounds__(128) team_chol_64_2(
+extern "C" __device__ const unsigned int hk_team_threads__team_chol_64_2 = 32u;
+extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_chol_64_2 = 34944u;
+extern "C" __global__ void __launch_bounds__(32) team_chol_64_2(
     hk::abi::ScalarHandle p_wout_tm0_a,
     hk::abi::ScalarHandle p_wout_tm0_info,
     hk::abi::ScalarHandle p_wout_tm0_x0,

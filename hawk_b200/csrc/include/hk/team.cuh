@@ -28,11 +28,10 @@
 // (hk/linalg.cuh, the order hawk/embedded/linalg.py:188-520 restates) in the
 // same order, so the team form equals the one-thread form bit for bit and no
 // result depends on the team size:
-//  * Cholesky, right-looking: after column k is final, every trailing entry
-//    (i, j) subtracts l_ik * l_jk -- the same ascending-k chain of subtractions
-//    the one-thread form's dot product applies, from the same symmetrised start
-//    0.5 a_ij + 0.5 a_ji; one barrier per column; a failed factor (info > 0)
-//    is all zeros;
+//  * Cholesky, column by column: row i >= j of column j starts from the
+//    symmetrised 0.5 a_ij + 0.5 a_ji and subtracts l_ik * l_jk in ascending k
+//    in a register (the one-thread form's dot product, lanes over rows), then
+//    divides by l_jj; a failed factor (info > 0) is all zeros;
 //  * LU, Crout, by the team's first warp: column j's running sums
 //    acc_i = sum_{k < min(i, j)} a_ik u_kj start at 0 and add in ascending k
 //    (u_kj = a_kj - acc_k is final once k - 1 is done), then a_ij - acc_i; the
@@ -197,16 +196,6 @@ template <class T, int N> HK_FI void zero_rhs(const Team& tm, T* x, int k) {
     tm.sync();
 }
 
-// Row i and column j of entry e of the lower triangle (diagonal included) of
-// an m x m matrix, e in [0, m (m + 1) / 2), rows in ascending order.
-HK_FI void tri_index(int e, int* i, int* j) {
-    int r = static_cast<int>((sqrtf(8.0f * static_cast<float>(e) + 1.0f) - 1.0f) * 0.5f);
-    while (r * (r + 1) / 2 > e) --r;
-    while ((r + 1) * (r + 2) / 2 <= e) ++r;
-    *i = r;
-    *j = e - r * (r + 1) / 2;
-}
-
 // Forward sweep, column-oriented: for j ascending, x_j is final (divided by
 // d(j) when `div`), then every row i > j subtracts e(i, j) * x_j.  Row i's
 // subtractions come in ascending j, as the one-thread dot product makes them;
@@ -303,82 +292,78 @@ HK_FI void cholesky(const Team& tm, const TeamCholesky<T, N>& f, T* a) {
     // the symmetrised lower triangle: (0.5 a_ij) + (0.5 a_ji); the reads of the
     // upper triangle are not overwritten by this pass
     detail::batched<8>(tm, N * N,
-               [&](int e) {
-                   const int i = e / N, j = e % N;
-                   return j <= i ? (T(0.5) * a[i * N + j]) + (T(0.5) * a[j * N + i]) : T(0);
-               },
-               [&](int e, T v) {
-                   if (e % N <= e / N) w.m(e / N, e % N) = v;
-               });
+                       [&](int e) {
+                           const int i = e / N, j = e % N;
+                           return j <= i ? (T(0.5) * a[i * N + j]) + (T(0.5) * a[j * N + i]) : T(0);
+                       },
+                       [&](int e, T v) {
+                           if (e % N <= e / N) w.m(e / N, e % N) = v;
+                       });
     tm.sync();
-    // column 0: its diagonal and the division of the entries below it
+    // Column by column, the one-thread form's own order: row i >= j of column
+    // j starts from its symmetrised entry and subtracts l_ik * l_jk for
+    // k = 0 .. j - 1 in a register (the diagonal's terms are l_jk * l_jk),
+    // then divides by l_jj = sqrt of the diagonal's result.  Rows are the
+    // lanes' (row i on lane i % 32); one warp barrier per column.
+    constexpr int R = (N + 31) / 32;
+    constexpr unsigned kAll = 0xffffffffu;
+    const int lane = tm.rank;
     int info = 0;
-    T d = w.m(0, 0);
-    T lkk = T(0);
-    if (!(d > T(0))) {
-        info = 1;
-    } else {
-        lkk = math::sqrt(d);
-        for (int i = 1 + tm.rank; i < N; i += tm.size) w.m(i, 0) = w.m(i, 0) / lkk;
-    }
-    tm.sync();
-    // step k: column k is final below its diagonal and l_kk is every thread's;
-    // each thread works out d_{k+1} (the diagonal's last subtraction) and its
-    // root, then every trailing entry subtracts l_ik l_jk, the entries of
-    // column k + 1 also dividing by l_{k+1}: one barrier per column.  The
-    // diagonal entry (k+1, k+1) is written as l_{k+1} in the next step, when
-    // no thread reads its old value any more.
-    for (int k = 0; info == 0 && k + 1 < N; ++k) {
-        if (tm.rank == 0) w.m(k, k) = lkk;
-        const T lk1 = w.m(k + 1, k);
-        d = w.m(k + 1, k + 1) - (lk1 * lk1);
+    for (int j = 0; j < N; ++j) {
+        T acc[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int i = lane + 32 * r;
+            acc[r] = (i >= j && i < N) ? w.m(i, j) : T(0);
+        }
+        // four k at a time: the loads and products of a group are issued
+        // ahead of its chain of subtractions (which keeps ascending k)
+        int k = 0;
+        for (; k + 4 <= j; k += 4) {
+            T lj[4], p[R][4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) lj[u] = w.m(j, k + u);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int i = lane + 32 * r;
+                const int ii = (i >= j && i < N) ? i : j;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) p[r][u] = w.m(ii, k + u) * lj[u];
+            }
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int i = lane + 32 * r;
+                if (i >= j && i < N)
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) acc[r] = acc[r] - p[r][u];
+            }
+        }
+        for (; k < j; ++k) {
+            const T ljk = w.m(j, k);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int i = lane + 32 * r;
+                if (i >= j && i < N) acc[r] = acc[r] - (w.m(i, k) * ljk);
+            }
+        }
+        T mine = T(0);
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            if (r == (j >> 5)) mine = acc[r];
+        const T d = __shfl_sync(kAll, mine, j & 31);
         if (!(d > T(0))) {
-            info = k + 2;
+            info = j + 1;
             break;
         }
-        const T lnext = math::sqrt(d);
-        const int m = N - 1 - k;
-        const int tri = m * (m + 1) / 2;
-        int r = 0, c = 0;
-        if (tm.rank < tri) detail::tri_index(tm.rank, &r, &c);
-        // the entries of one step are independent: four of a thread's at a
-        // time, every load issued before any store
-        for (int e0 = tm.rank; e0 < tri; e0 += 4 * tm.size) {
-            int ii[4], jj[4];
-            bool live[4];
-            T aij[4], aik[4], ajk[4];
+        const T ljj = math::sqrt(d);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                ii[u] = k + 1 + r;
-                jj[u] = k + 1 + c;
-                live[u] = e0 + u * tm.size < tri && !(ii[u] == k + 1 && jj[u] == k + 1);
-                c += tm.size;                     // the next entry of this thread
-                while (c > r) {
-                    c -= r + 1;
-                    ++r;
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                if (live[u]) {
-                    aij[u] = w.m(ii[u], jj[u]);
-                    aik[u] = w.m(ii[u], k);
-                    ajk[u] = w.m(jj[u], k);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                if (live[u]) {
-                    T v = aij[u] - (aik[u] * ajk[u]);
-                    if (jj[u] == k + 1) v = v / lnext;
-                    w.m(ii[u], jj[u]) = v;
-                }
-            }
+        for (int r = 0; r < R; ++r) {
+            const int i = lane + 32 * r;
+            if (i > j && i < N) w.m(i, j) = acc[r] / ljj;
         }
-        lkk = lnext;
+        if (lane == (j & 31)) w.m(j, j) = ljj;
         tm.sync();
     }
-    if (info == 0 && tm.rank == 0) w.m(N - 1, N - 1) = lkk;
     tm.sync();
     detail::batched<8>(tm, N * N,
                        [&](int e) {
@@ -485,9 +470,13 @@ HK_FI void lu(const Team& tm, const TeamLu<T, N>& f, T* a) {
     if (tm.rank < 32) {
         const int lane = tm.rank;
         for (int j = 0; j < N; ++j) {
-            T acc[R];
+            T acc[R], col[R];
 #pragma unroll
-            for (int r = 0; r < R; ++r) acc[r] = T(0);
+            for (int r = 0; r < R; ++r) {
+                const int i = lane + 32 * r;
+                acc[r] = T(0);
+                col[r] = i < N ? w.m(i, j) : T(0);       // column j, held for the chain below
+            }
             // Crout: acc_i = sum_{k < min(i, j)} a_ik u_kj, ascending k from 0;
             // u_kj = a_kj - acc_k is final once every k' < k was added
             for (int k = 0; k < j; ++k) {
@@ -495,8 +484,8 @@ HK_FI void lu(const Team& tm, const TeamLu<T, N>& f, T* a) {
                 T mine = T(0);
 #pragma unroll
                 for (int r = 0; r < R; ++r)
-                    if (r == slot) mine = acc[r];
-                const T ukj = __shfl_sync(kAll, w.m(k, j) - mine, k & 31);
+                    if (r == slot) mine = col[r] - acc[r];
+                const T ukj = __shfl_sync(kAll, mine, k & 31);
 #pragma unroll
                 for (int r = 0; r < R; ++r) {
                     const int i = lane + 32 * r;
@@ -506,7 +495,7 @@ HK_FI void lu(const Team& tm, const TeamLu<T, N>& f, T* a) {
 #pragma unroll
             for (int r = 0; r < R; ++r) {
                 const int i = lane + 32 * r;
-                if (i < N) w.m(i, j) = w.m(i, j) - acc[r];
+                if (i < N) w.m(i, j) = col[r] - acc[r];
             }
             __syncwarp();
             // pivot: the first row of largest magnitude at or below the diagonal

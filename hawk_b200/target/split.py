@@ -34,7 +34,7 @@ TEAM_SMEM_LIMIT = 220 * 1024
 #: Teams (warps, one lane each) per SM that must fit staged for a stage to
 #: stage at all: below it, working in place through L1/L2 with more lanes in
 #: flight is the faster of the two.
-TEAM_STAGED_WARPS = 16
+TEAM_STAGED_WARPS = 6
 #: Warps per block of a team entry that works in place (a staged one takes one
 #: warp per block, so as many blocks as fit share an SM).
 TEAM_WARPS_IN_PLACE = 4
