@@ -300,6 +300,32 @@ def team_chol_from_64(A: Matrix[64, 64], b: Vector[64], x: Mutable[Vector[64]], 
 
 
 @hawk.kernel
+def share(x: Scalar, z: Mutable[Scalar]):
+    z = x / hawk.sum(x)
+
+
+@hawk.kernel
+def standard(x: Scalar, mu: Mutable[Scalar], z: Mutable[Scalar], t: Mutable[Scalar]):
+    mu = hawk.mean(x)
+    v = hawk.mean((x - mu) * (x - mu))
+    z = (x - mu) / m.sqrt(v)
+    t = hawk.sum(z * z)
+
+
+@hawk.kernel
+def centred(x: Scalar, z: Mutable[Vector[3]]):
+    v = m.vec(x, x * x, 2.0 * x)
+    z = v - hawk.mean(v)
+
+
+#: Sums over samples read back in the body (hawk/ir/split.py): each runs as
+#: stages with the cell finished on the device between them -- x / sum(x),
+#: the standardised x with its mean stored and the sum of squares of the
+#: result, a vector's components centred on their means.
+READBACK_KERNELS = {k.name: k for k in (share, standard, centred)}
+
+
+@hawk.kernel
 def team_chol_512(A: Matrix[512, 512], b: Vector[512], x: Mutable[Vector[512]], info: Mutable[Int32]):
     f, status = m.cholesky(A)
     x = m.cho_solve(f, b)
@@ -350,4 +376,6 @@ KERNELS = {
     "histogram": (histogram, ("float64",)),
     "bitmask": (bitmask, ("float64",)),
     **{name: (k, ("float64",)) for name, k in TEAM_KERNELS.items()},
+    **{name: (k, ("float64",)) for name, k in READBACK_KERNELS.items()},
+    "share_vjp": (Kernel("share_vjp", vjp(share, wrt=("x",))), ("float64",)),
 }

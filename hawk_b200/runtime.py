@@ -374,13 +374,23 @@ def _stream(stream, device: int) -> int:
 
 
 class SplitKernel:
-    """A kernel run as stages (team-form linear algebra, hawk/ir/team.py): the
-    device twin of the reference runtime's ``_run_stages``
-    (hawk/runtime.py:699-748).  Every stage is an entry of the one unit; the
-    runtime owns the scratch planes the stages pass the lanes' matrices through
-    (``team_planes``: ``per_lane`` elements per sample, made once per sample
-    count, hawk/runtime.py:675-696) and launches the stages in order on the
-    stream -- a team stage with one block of its team per lane."""
+    """A kernel run as stages: the device twin of the reference runtime's
+    ``_run_stages`` (hawk/runtime.py:699-748).  Its stages are the entries of
+    one unit (hawk/ir/split.py cuts them):
+
+    * a value reduced over samples and read later is finished between two
+      stages: the stage that makes it runs the row frame into rows the runtime
+      owns, the rows are finished on the device (the ordered tree of
+      hawk/_cells.py, bit for bit) and every later stage that reads the cell
+      binds it as a one-cell lookup plane; a cell the kernel also stores is
+      copied into the caller's plane, one only a later stage reads is the
+      kernel's own;
+    * team-form linear algebra (hawk/ir/team.py) passes the lanes' matrices
+      through scratch planes the runtime owns (``team_planes``: ``per_lane``
+      elements per sample, made once per sample count, hawk/runtime.py:675-696),
+      a team stage running one lane per warp.
+
+    The stages launch in order on the stream."""
 
     def __init__(self, directory, kernel: str, mode: str = "float64", device: int | None = None) -> None:
         self.directory = Path(directory)
@@ -395,19 +405,27 @@ class SplitKernel:
         b200 = sidecar["b200"]
         self.device = int(device if device is not None else _current_device())
         self.team_planes = sidecar.get("team_planes") or {}
+        self.cell_specs = sidecar.get("cells") or {}
+        self.records = b200["split"]
         self.stages = []
-        for st in b200["split"]:
-            stage_sidecar = {"kernel": st["entry"], "scalar_type": self.mode, "cells": {},
+        for st in self.records:
+            stage_sidecar = {"kernel": st["entry"], "scalar_type": self.mode,
+                             "cells": {c: self.cell_specs[c] for c in st.get("cells_out") or ()},
                              "arg_dtypes": {}, "b200": {"entry": st["entry"], "cubin": b200["cubin"],
-                                                         "frame": "lane", "sample_sums": [], "slots": st["slots"],
-                                                         "persist": None, "folds": {}}}
+                                                         "frame": st.get("kind", "lane"),
+                                                         "sample_sums": st.get("sample_sums") or [],
+                                                         "slots": st["slots"], "persist": None, "folds": {}}}
+            if stage_sidecar["b200"]["frame"] == "team":
+                stage_sidecar["b200"]["frame"] = "lane"
             self.stages.append(DeviceKernel(self.directory, st["entry"], self.mode, self.device,
                                             sidecar=stage_sidecar))
         self.slots = [(s["role"], s["name"], s["dtype"], tuple(s["shape"])) for s in b200["slots"]]
         self.arg_spec = tuple((r, n) for r, n, _d, _s in self.slots)
-        self.cells = {}
+        # the cells a caller binds (one value per column); the rest are the kernel's own
+        self.cells = {c: spec for c, spec in self.cell_specs.items() if not spec.get("internal")}
         self._lock = threading.Lock()
         self._scratch: dict = {}
+        self._values: dict = {}
 
     def scratch(self, n: int) -> dict:
         """The stages' scratch planes at ``n`` samples (made once per n)."""
@@ -422,36 +440,86 @@ class SplitKernel:
                 for name, spec in self.team_planes.items()}
         return self._scratch[n]
 
+    def cell_values(self) -> dict:
+        """One device plane per cell (its columns), where a finished cell lives
+        for the stages that read it."""
+        import torch
+
+        if not self._values:
+            real = torch.float64 if self.mode == "float64" else torch.float32
+            self._values = {c: torch.empty(int(spec.get("columns", 1)), dtype=real,
+                                           device=torch.device("cuda", self.device))
+                            for c, spec in self.cell_specs.items()}
+        return self._values
+
     def run(self, *, base: int = 0, count: int | None = None, n_samples: int | None = None, stream=None,
             **arrays) -> None:
+        import torch
+
         from .planes import from_torch
 
-        declared = {n for _r, n in self.arg_spec}
+        declared = {n for r, n in self.arg_spec if r != "nsamples"} | set(self.cells)
         unknown = sorted(set(arrays) - declared)
         if unknown:
             raise HawkError(f"kernel {self.name!r}: {unknown} are not planes it declares "
                             f"(declared: {sorted(declared)})")
-        uniforms = {n for r, n in self.arg_spec if r == "uniform"}
-        values = {k: v for k, v in arrays.items() if k in uniforms}
-        planes = {k: as_plane(k, v) for k, v in arrays.items() if k not in uniforms}
         missing = sorted(declared - set(arrays))
         if missing:
             raise HawkError(f"kernel {self.name!r}: {missing} are declared but not bound")
+        uniforms = {n for r, n in self.arg_spec if r == "uniform"}
+        values = {k: v for k, v in arrays.items() if k in uniforms}
+        planes = {k: as_plane(k, v) for k, v in arrays.items() if k not in uniforms}
+        for c, spec in self.cells.items():
+            p = planes[c]
+            if p.dtype != self.mode or p.device != self.device or p.size < int(spec.get("columns", 1)):
+                raise HawkError(f"kernel {self.name!r}: cell {c!r} must be a {self.mode} plane of "
+                                f"{spec.get('columns', 1)} value(s) on device {self.device}, got {p.dtype} "
+                                f"{p.shape} on {p.device}")
         if n_samples is None:
             n_samples = self.stages[0].n_from(planes)
         count = n_samples - base if count is None else count
         if base < 0 or count < 0 or base + count > n_samples:
             raise HawkError(f"kernel {self.name!r}: partition [{base}, {base + count}) is outside "
                             f"the {n_samples} samples")
+        if self.cell_specs and base % ROW:
+            raise HawkError(f"kernel {self.name!r} reduces over 32-sample rows, so a partition must "
+                            f"start on a row (base % 32 == 0), got base={base}")
         with self._lock:
             scratch = {k: from_torch(v) for k, v in self.scratch(n_samples).items()}
-            for stage in self.stages:
+            cells = self.cell_values()
+            for stage, record in zip(self.stages, self.records):
                 names = {n for _r, n in stage.arg_spec}
-                bound = {k: v for k, v in planes.items() if k in names}
+                bound = {k: v for k, v in planes.items() if k in names and k not in self.cells}
                 bound.update({k: v for k, v in scratch.items() if k in names})
+                for cell in record.get("cells_in") or ():
+                    cols = int(self.cell_specs[cell].get("columns", 1))
+                    plane_names = (cell,) if cols == 1 else tuple(f"{cell}_{k}" for k in range(cols))
+                    for k, plane in enumerate(plane_names):
+                        bound[plane] = from_torch(cells[cell][k:k + 1])
+                state = None
+                if record.get("cells_out"):
+                    state = stage.cells_state(n_samples)
+                    bound.update({k: from_torch(v) for k, v in state["rows"].items()})
                 stage.check(bound, values, n_samples)
                 stage.bind_all(bound, values, n_samples)
                 stage.launch(base, count, n_samples, stream)
+                if state is None:
+                    continue
+                lo, hi = base // ROW, -(-(base + count) // ROW)
+                sums = [s["name"] for s in stage.sums]
+                if hi > lo:
+                    leaves = stage.cells_leaves(state, lo, hi, stream)
+                    stage.cells_tree(state["leaf_hi"], state["leaf_comp"], leaves, state["values"], stream)
+                with torch.cuda.stream(_torch_stream(stream, self.device)):
+                    for cell in record["cells_out"]:
+                        cols = int(self.cell_specs[cell].get("columns", 1))
+                        plane_names = (cell,) if cols == 1 else tuple(f"{cell}_{k}" for k in range(cols))
+                        for k, plane in enumerate(plane_names):
+                            cells[cell][k:k + 1].copy_(state["values"][sums.index(plane):sums.index(plane) + 1])
+                        if cell in self.cells:
+                            keep = planes[cell].keep
+                            out = keep if torch.is_tensor(keep) else torch.as_tensor(keep, device=f"cuda:{self.device}")
+                            out.view(-1)[:cols].copy_(cells[cell])
 
     def errors(self, clear: bool = True) -> int:
         """The unit's error word (hkb_library_errors) after the stream's launches."""

@@ -93,7 +93,7 @@ def build_split_kernel(kernel, directory, *, name: str | None = None, mode: str 
     """A kernel the reference's split cuts into stages (team-form linear
     algebra): one unit holding every stage's entry, one CUBIN, one sidecar
     listing the stages and the scratch planes (target/split.py)."""
-    from .split import render_split_unit, user_slots
+    from .split import cell_planes, render_split_unit, user_slots
 
     directory = Path(directory)
     directory.mkdir(parents=True, exist_ok=True)
@@ -106,7 +106,7 @@ def build_split_kernel(kernel, directory, *, name: str | None = None, mode: str 
     sidecar = _reference_sidecar(name, members[0].walk, mode)
     sidecar = json.loads(json.dumps(sidecar, default=str))
     sidecar.update(json.loads(json.dumps(block, default=str)))
-    scratch = set(block.get("team_planes") or {})
+    scratch = set(block.get("team_planes") or {}) | cell_planes(block.get("cells") or {})
     sidecar["b200"] = {
         "entry": name,
         "arch": ARCH,

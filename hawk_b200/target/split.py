@@ -80,7 +80,7 @@ def expand(kernel, name: str):
 
     members, names, _kinds, blocks = _expand_split([kernel], [name], [None], device=True, device_only=False)
     block = blocks.get(name)
-    if block is None or len(members) < 2 or not any(getattr(m, "team", None) is not None for m in members):
+    if block is None or len(members) < 2:
         return None
     return members, block
 
@@ -109,22 +109,27 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
     elem = 8 if mode == "float64" else 4
     parts, stages = [], []
     for member, record in zip(members, block["stages"]):
-        if record.get("cells_in") or record.get("cells_out"):
-            raise HawkError(f"{name!r}: stage {member.name!r} passes a sample sum between launches, which the "
-                            "b200 target does not build yet")
         if getattr(member, "one_step", None) is not None:
             raise HawkError(f"{name!r}: an automatic stepping kernel's stages are not built on the b200 target")
         threads = _threads(member)
         walk = member.walk
         if threads is None:
+            # a per-lane stage: the lane frame, or the row frame of the sample
+            # sums it reduces into cells a later stage reads
             unit = render_unit(member, member.name, mode, staged=False)
-            if unit.frame != "lane" or unit.notes.get("persist") or unit.notes.get("folds"):
-                raise HawkError(f"{name!r}: stage {member.name!r} needs a {unit.frame} frame, which a split "
-                                "kernel's stage does not build yet")
+            if unit.notes.get("persist") or unit.notes.get("folds"):
+                raise HawkError(f"{name!r}: stage {member.name!r} commits into a compensated scatter target, "
+                                "which a split kernel's stage does not build yet")
             parts.append(unit.entries)
-            stages.append({"entry": member.name, "kind": "lane", "threads": None, "dynamic_smem": 0,
-                           "slots": _slot_records(walk), "lane_refill": unit.notes.get("lane_refill", False)})
+            stages.append({"entry": member.name, "kind": unit.frame, "threads": None, "dynamic_smem": 0,
+                           "slots": _slot_records(walk), "lane_refill": unit.notes.get("lane_refill", False),
+                           "sample_sums": [{"name": n, "op": op, "companion": comp} for n, op, comp in unit.sums],
+                           "cells_in": list(record.get("cells_in") or ()),
+                           "cells_out": list(record.get("cells_out") or ())})
             continue
+        if record.get("cells_in") or record.get("cells_out"):
+            raise HawkError(f"{name!r}: team stage {member.name!r} reads or makes a sample sum, which the b200 "
+                            "target does not build yet")
         if isinstance(member, TeamStage):
             body = body_text(member.fused_body().text)
             threads, smem = team_geometry(member.team, elem)
@@ -147,7 +152,7 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
             "",
         ]
         stages.append({"entry": member.name, "kind": "team", "threads": threads, "dynamic_smem": smem,
-                       "slots": _slot_records(walk)})
+                       "slots": _slot_records(walk), "sample_sums": [], "cells_in": [], "cells_out": []})
     text = "\n".join([*prelude_lines(name, mode), "", *parts])
     unit = Unit(name=name, mode=mode, text=text, body="", frame="split",
                 digest=hashlib.sha256(text.encode()).hexdigest(), entries="\n".join(parts),
@@ -164,9 +169,23 @@ def _slot_records(walk) -> list:
     return out
 
 
+def cell_planes(cells: dict) -> set:
+    """Every plane name a cell stands for between stages: its row planes and
+    their companions (hawk/_cells.py:34-36) and the one-cell lookup planes a
+    later stage reads (the same names)."""
+    out = set()
+    for cell, spec in cells.items():
+        cols = int(spec.get("columns", 1))
+        names = (cell,) if cols == 1 else tuple(f"{cell}_{k}" for k in range(cols))
+        out.update(names)
+        out.update(f"{n}_comp" for n in names)
+    return out
+
+
 def user_slots(stages: list, scratch) -> list:
     """The slots a caller binds: every stage's, less the runtime's scratch
-    planes (``scratch``), each once (its first stage's record)."""
+    planes and the planes of cells (``scratch``), each once (its first
+    stage's record).  A cell the caller stores is bound by its own name."""
     seen, out = set(), []
     for st in stages:
         for slot in st["slots"]:

@@ -92,6 +92,7 @@ _SIGS = {
     "hko_kepler_vjp": (None, [_P, _P, _P, _P, _P, _I, _I]),
     "hko_oscillator": (ctypes.c_uint32, [_P, _P, _P, _P, _P, _P, _P, _D, _I, _I, _I]),
     "hko_orbit": (ctypes.c_uint32, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I]),
+    "hko_rows_f64": (None, [ctypes.c_int, _P, _I, _P, _P]),
     "hko_team_chol": (None, [ctypes.c_int, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I]),
     "hko_team_lu": (None, [ctypes.c_int, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I]),
     "hko_team_chol_from": (None, [ctypes.c_int, _P, _P, _I, _P, _P, _P, _I, _I]),
@@ -282,6 +283,47 @@ def spd_solve_vjp(A, b, bar_x, threads: int = 1):
     return bar_A, bar_b
 
 
+OPS = {"sum": 0, "max": 1, "min": 2}
+
+
+def sample_sum(terms, op: str = "sum") -> float:
+    """A reduction over samples as a kernel makes it: the 32-sample rows of
+    the terms, then the ordered finish of the rows into the cell."""
+    terms = np.ascontiguousarray(terms, dtype=np.float64)
+    n = terms.shape[0]
+    rows = -(-n // 32)
+    hi, comp = np.empty(max(rows, 1)), np.empty(max(rows, 1))
+    lib().hko_rows_f64(OPS[op], _p(terms), n, _p(hi), _p(comp))
+    return float(lib().hko_cells_finish_f64(OPS[op], _p(hi), _p(comp), rows))
+
+
+def share(x):
+    """z = x / sum(x)."""
+    return x / sample_sum(x)
+
+
+def standard(x):
+    """mu = mean(x); v = mean((x - mu)^2); z = (x - mu) / sqrt(v); t = sum(z^2):
+    the stages' bodies, each a mean as the sum of x_i / n."""
+    n = float(x.shape[0])
+    mu = sample_sum(x / n)
+    d = x - mu
+    v = sample_sum((d * d) / n)
+    z = (x - mu) / np.sqrt(v)
+    t = sample_sum(z * z)
+    return mu, z, t
+
+
+def centred(x):
+    """v = (x, x^2, 2x); z = v - mean(v) per component (a vector divided by the
+    count is multiplied by its reciprocal)."""
+    n = x.shape[0]
+    v = np.stack([x, x * x, 2.0 * x])
+    r = 1.0 / float(n)
+    mean = np.array([sample_sum(v[k] * r) for k in range(3)])
+    return v - mean[:, None]
+
+
 def team_chol(A, b, B, threads: int = 1):
     """(x, X, L, info) of the team-form Cholesky kernel: A (n, n, N), b (n, N), B (n, 2, N)."""
     k, n = A.shape[0], A.shape[-1]
@@ -363,3 +405,11 @@ def orbit(planes: dict, word: int, threads: int = 1) -> int:
     return _stepped(lambda b, c: lib().hko_orbit(_p(s), n, _p(planes["t"]), _p(planes["h"]), _p(planes["n_acc"]),
                                                  _p(planes["n_rej"]), _p(planes["t_end"]), _p(term), int(word), b, c),
                     n, threads)
+
+
+def share_vjp(x, bar_z):
+    """The VJP of share wrt x, as its stages compute it: S = sum(x),
+    c = sum(-((bar_z (x / S)) / S)), bar_x = bar_z / S + c."""
+    s = sample_sum(x)
+    c = sample_sum(-((bar_z * (x / s)) / s))
+    return (bar_z / s) + c

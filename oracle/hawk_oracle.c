@@ -143,6 +143,37 @@ void hko_poly_loss_vjp_rows_f32(const float* x, const float* t, const float* bar
     POLY_VJP_ROWS(float, f)
 }
 
+/* The rows of one column of per-sample terms (the host sample-sum frame,
+ * hawk/emit/host.py:1499-1530, around any body): 32 slots per row, a slot
+ * past the last sample holding the identity of the op (0, -inf, +inf), the
+ * slots joined by sampleSumRow_'s pairs (hawk/emit/wrapper.py:561-592); max
+ * and min ignore a NaN operand (ssExtreme_, :544-550). */
+static double extreme_d(int op, double a, double b) {
+    if (a != a) return b;
+    if (b != b) return a;
+    return op == HKO_OP_MAX ? (b > a ? b : a) : (b < a ? b : a);
+}
+
+void hko_rows_f64(int op, const double* terms, int64_t n, double* hi, double* comp) {
+    const int64_t nrows = (n + 31) / 32;
+    const double ident = op == HKO_OP_SUM ? 0.0 : (op == HKO_OP_MAX ? -INFINITY : INFINITY);
+    for (int64_t j = 0; j < nrows; ++j) {
+        double h[32], c[32];
+        for (int l = 0; l < 32; ++l) {
+            const int64_t i = j * 32 + l;
+            h[l] = i < n ? terms[i] : ident;
+            c[l] = 0.0;
+        }
+        for (int off = 16; off >= 1; off >>= 1)
+            for (int l = 0; l < off; ++l) {
+                if (op == HKO_OP_SUM) pair_d(&h[l], &c[l], h[l + off], c[l + off]);
+                else h[l] = extreme_d(op, h[l], h[l + off]);
+            }
+        hi[j] = h[0];
+        comp[j] = c[0];
+    }
+}
+
 /*
  * hawk/_cells.py:94-119 -- leaves of 4096 rows: slot s of 256 walks rows
  * s, s+256, ... with a Neumaier step (_neumaier, :52-55), then a halving tree

@@ -93,6 +93,10 @@ uint32_t hko_oscillator(double* x, double* v, double* k, const double* nstop, co
 uint32_t hko_orbit(double* s, int64_t pitch, double* t, double* h, double* n_acc, double* n_rej,
                    const double* t_end, uint8_t* term, int64_t word, int64_t base, int64_t count);
 
+/* The 32-sample rows (sum, compensation) of one column of per-sample terms,
+ * any op: what a kernel's sample sum stores before the finish. */
+void hko_rows_f64(int op, const double* terms, int64_t n, double* hi, double* comp);
+
 /* Team-form linear algebra (n x n per sample, any n): what the reference's
  * stages compute per lane -- the one-thread form's operation order for every
  * n (hawk/embedded/linalg.py:188-520).  Planes are component-major: A is

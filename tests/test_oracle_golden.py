@@ -219,3 +219,35 @@ def test_team_chol_from_golden(golden):
     np.testing.assert_array_equal(L, g["L"])
     close(x, g["x"], rtol=1e-10, atol=1e-13)
     assert info[2] == 1 and not np.any(x[:, 2])
+
+
+def test_read_back_sums_match_numpy():
+    """The oracle's read-back kernels (rows + ordered finish, then the reading
+    bodies) against numpy with exact sums (math.fsum): within the reference's
+    sample-sum tolerance, 1e-14 relative to the sum of magnitudes
+    (tests/test_sample_sum.py:38 of the reference)."""
+    import math
+
+    rng = np.random.default_rng(7)
+    for n in (1, 33, 5000, 270000):
+        x = rng.uniform(0.5, 1.5, n)
+        s = math.fsum(x)
+        close(oracle.share(x), x / s, rtol=1e-14)
+        y = rng.normal(3.0, 2.0, n)
+        mu, z, t = oracle.standard(y)
+        want_mu = math.fsum(y / n)
+        assert abs(mu - want_mu) <= 1e-14 * math.fsum(np.abs(y / n))
+        if n > 1:
+            d = y - want_mu
+            v = math.fsum(d * d / n)
+            close(z, d / math.sqrt(v), rtol=1e-12)
+            assert abs(t - math.fsum(z * z)) <= 1e-14 * math.fsum(z * z)
+        v3 = np.stack([x, x * x, 2 * x])
+        want = v3 - np.array([math.fsum(v3[k] / n) for k in range(3)])[:, None]
+        close(oracle.centred(x), want, rtol=1e-12, atol=1e-15)
+
+
+def test_sample_sum_max_and_min_ignore_nan():
+    x = np.array([1.0, np.nan, 3.0, -2.0] * 20)
+    assert oracle.sample_sum(x, "max") == 3.0
+    assert oracle.sample_sum(x, "min") == -2.0
