@@ -7,6 +7,7 @@ using Int = long long;
 
 HK_SELF_CHECK_EXPORTS
 
+extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__gather_vjp = 32768u;
 extern "C" __global__ void __launch_bounds__(256) gather_vjp(
     hk::abi::ScalarHandle p_mut_bar_w,
     hk::abi::ScalarHandle p_aout_bar_table,
@@ -30,6 +31,11 @@ extern "C" __global__ void __launch_bounds__(256) gather_vjp(
     (void)psc_w;
     const hk::ScalarIn<Real> lut_table(p_lut_table);
     (void)lut_table;
+    hk::accum::PrivSpace hawk_ps = hk::accum::private_space();
+    const auto hawk_pv_aout_bar_table = hk::accum::privatise(hawk_ps, aout_bar_table);
+    __syncthreads();
+    {
+    const auto& aout_bar_table = hawk_pv_aout_bar_table;
     for (long long hawk_flat = hk::lane_first(); hawk_flat < count; hawk_flat += hk::lane_step()) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
@@ -40,4 +46,7 @@ extern "C" __global__ void __launch_bounds__(256) gather_vjp(
         mut_bar_w[i] = (psc_bar_y_i * lut_table[hk::SampleIndex::make(static_cast<std::size_t>(t5))].eval());
         hawk_abi::accum_add(aout_bar_table, hk::SampleIndex::make(static_cast<std::size_t>(t5)), (psc_bar_y_i * psc_w[i].eval()));
     }
+    }
+    __syncthreads();
+    hk::accum::flush_add(hawk_pv_aout_bar_table);
 }

@@ -7,6 +7,7 @@ using Int = long long;
 
 HK_SELF_CHECK_EXPORTS
 
+extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__histogram = 32768u;
 extern "C" __global__ void __launch_bounds__(256) histogram(
     hk::abi::ScalarHandle p_aout_acc,
     hk::abi::ScalarHandle p_aout_acc_c,
@@ -24,6 +25,13 @@ extern "C" __global__ void __launch_bounds__(256) histogram(
     (void)psc_key;
     const hk::ScalarIn<Real> psc_x(p_psc_x);
     (void)psc_x;
+    hk::accum::PrivSpace hawk_ps = hk::accum::private_space();
+    const auto hawk_pv_aout_acc = hk::accum::privatise(hawk_ps, aout_acc);
+    const auto hawk_pv_aout_acc_c = hk::accum::privatise(hawk_ps, aout_acc_c);
+    __syncthreads();
+    {
+    const auto& aout_acc = hawk_pv_aout_acc;
+    const auto& aout_acc_c = hawk_pv_aout_acc_c;
     for (long long hawk_flat = hk::lane_first(); hawk_flat < count; hawk_flat += hk::lane_step()) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
@@ -32,6 +40,9 @@ extern "C" __global__ void __launch_bounds__(256) histogram(
         const auto t2 = static_cast<Int>(psc_key[i].eval());
         hawk_abi::accum_add_compensated(aout_acc, aout_acc_c, hk::SampleIndex::make(static_cast<std::size_t>(t2)), psc_x[i].eval());
     }
+    }
+    __syncthreads();
+    hk::accum::flush_compensated(hawk_pv_aout_acc, hawk_pv_aout_acc_c);
 }
 
 extern "C" __global__ void __launch_bounds__(256) histogram__fold_acc(

@@ -7,6 +7,7 @@ using Int = long long;
 
 HK_SELF_CHECK_EXPORTS
 
+extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__keyed_sum = 32768u;
 extern "C" __global__ void __launch_bounds__(256) keyed_sum(
     hk::abi::ScalarHandle p_aout_acc,
     hk::abi::ScalarHandle p_psc_key,
@@ -22,6 +23,11 @@ extern "C" __global__ void __launch_bounds__(256) keyed_sum(
     const hk::ScalarIn<Real> psc_x(p_psc_x);
     (void)psc_x;
     hk::accum::run::State hawk_run_aout_acc{};
+    hk::accum::PrivSpace hawk_ps = hk::accum::private_space();
+    const auto hawk_pv_aout_acc = hk::accum::privatise(hawk_ps, aout_acc);
+    __syncthreads();
+    {
+    const auto& aout_acc = hawk_pv_aout_acc;
     for (long long hawk_flat = hk::lane_first(); hawk_flat < count; hawk_flat += hk::lane_step()) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
@@ -29,4 +35,7 @@ extern "C" __global__ void __launch_bounds__(256) keyed_sum(
         (void)nSamples;
         hk::accum::run::addSorted(aout_acc, hk::SampleIndex::make(static_cast<std::size_t>(static_cast<Int>(psc_key[i].eval()))), psc_x[i].eval(), hawk_run_aout_acc);
     }
+    }
+    __syncthreads();
+    hk::accum::flush_add(hawk_pv_aout_acc);
 }

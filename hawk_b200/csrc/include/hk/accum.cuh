@@ -38,6 +38,32 @@ template <class T> struct Pointee<T*> { typedef T type; };
 }  // namespace detail
 }  // namespace hk
 
+namespace hk {
+namespace accum {
+
+// A scatter target a block commits into through a private copy in its shared
+// memory (when the plane fits the entry's share): commits land in the copy at
+// shared-memory atomic rates, and the block adds its copy into the plane once,
+// slot by slot, when it leaves (flush_*).  A key past the copy commits to the
+// plane directly.  `n` is the plane's slots.
+template <class T> struct PrivOut {
+    T* global;
+    T* local;
+    u64 n;
+    bool priv;
+    HK_HD T* data() const { return global; }
+    HK_HD u64 samples() const { return n; }
+};
+
+// The slot of key k: the plane's, or a private copy's.
+template <class V> HK_HD auto slot(const V& v, i64 k) -> decltype(v.data()) { return v.data() + k; }
+template <class T> HK_HD T* slot(const PrivOut<T>& v, i64 k) {
+    return (v.priv && static_cast<u64>(k) < v.n) ? v.local + k : v.global + k;
+}
+
+}  // namespace accum
+}  // namespace hk
+
 namespace hawk_abi {
 
 #if defined(__CUDACC__) || defined(__CUDACC_RTC__)
@@ -51,20 +77,20 @@ template <class E> HK_FI void atomic_add_compensated(E* slot, E* comp, E t) {
 }
 
 template <class V, class T> HK_FI void accum_add(const V& target, const hk::SampleIndex& at, T term) {
-    auto* slot = target.data() + at.g;
+    auto* slot = hk::accum::slot(target, at.g);
     using E = typename hk::detail::Pointee<decltype(slot)>::type;
     atomicAdd(slot, static_cast<E>(term));
 }
 
-template <class V, class T>
-HK_FI void accum_add_compensated(const V& target, const V& comp, const hk::SampleIndex& at, T term) {
-    auto* slot = target.data() + at.g;
+template <class V, class C, class T>
+HK_FI void accum_add_compensated(const V& target, const C& comp, const hk::SampleIndex& at, T term) {
+    auto* slot = hk::accum::slot(target, at.g);
     using E = typename hk::detail::Pointee<decltype(slot)>::type;
-    atomic_add_compensated(slot, comp.data() + at.g, static_cast<E>(term));
+    atomic_add_compensated(slot, hk::accum::slot(comp, at.g), static_cast<E>(term));
 }
 
 template <class V, class T> HK_FI void accum_or(const V& target, const hk::SampleIndex& at, T bits) {
-    atomicOr(reinterpret_cast<unsigned*>(target.data() + at.g), static_cast<unsigned>(bits));
+    atomicOr(reinterpret_cast<unsigned*>(hk::accum::slot(target, at.g)), static_cast<unsigned>(bits));
 }
 #endif
 
@@ -97,10 +123,16 @@ template <class E> HK_FI void commit(E* slot, E* comp, E v) {
     else atomicAdd(slot, v);
 }
 
+// The slot of key k in a target or its companion (none: null).
+template <class V> HK_FI auto at_key(const V& v, i64 k) -> decltype(slot(v, k)) { return slot(v, k); }
+struct NoComp {};
+template <class E> HK_FI E* at_key_comp(const NoComp&, i64) { return nullptr; }
+template <class E, class V> HK_FI E* at_key_comp(const V& v, i64 k) { return slot(v, k); }
+
 // Aligned groups of W lanes whose keys are equal: each group's total, one
 // commit per group.  False (nothing committed) when the warp is not fully
 // converged or a group's keys differ.
-template <int W, class E> HK_FI bool groups(E* target, E* comp, long long key, E term) {
+template <int W, class E, class V, class C> HK_FI bool groups(const V& target, const C& comp, long long key, E term) {
     static_assert(W >= 1 && W <= 32 && (W & (W - 1)) == 0, "a run is a power-of-two number of lanes");
     if (__activemask() != kFull) return false;
     const unsigned lane = threadIdx.x & 31u;
@@ -109,14 +141,14 @@ template <int W, class E> HK_FI bool groups(E* target, E* comp, long long key, E
     E v = term;
 #pragma unroll
     for (int o = W / 2; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
-    if ((lane & static_cast<unsigned>(W - 1)) == 0u) commit(target + key, comp == nullptr ? comp : comp + key, v);
+    if ((lane & static_cast<unsigned>(W - 1)) == 0u) commit(at_key(target, key), at_key_comp<E>(comp, key), v);
     return true;
 }
 
 // Keys non-decreasing along the warp: each run of equal keys sums to its first
 // lane (a segmented doubling sum), which commits.  False when the warp is not
 // fully converged or its keys are not sorted.
-template <class E> HK_FI bool sorted_runs(E* target, E* comp, long long key, E term) {
+template <class E, class V, class C> HK_FI bool sorted_runs(const V& target, const C& comp, long long key, E term) {
     if (__activemask() != kFull) return false;
     const unsigned lane = threadIdx.x & 31u;
     const long long prev = __shfl_up_sync(kFull, key, 1);
@@ -128,7 +160,7 @@ template <class E> HK_FI bool sorted_runs(E* target, E* comp, long long key, E t
         const long long k2 = __shfl_down_sync(kFull, key, o);
         if (lane + static_cast<unsigned>(o) < 32u && k2 == key) v += u;
     }
-    if (lane == 0u || prev != key) commit(target + key, comp == nullptr ? comp : comp + key, v);
+    if (lane == 0u || prev != key) commit(at_key(target, key), at_key_comp<E>(comp, key), v);
     return true;
 }
 
@@ -137,41 +169,108 @@ template <class V> HK_FI auto slot_of(const V& v) -> decltype(v.data()) { return
 template <int W, class V, class T>
 HK_FI void add(const V& target, const SampleIndex& at, T term, const SampleIndex&, State&) {
     using E = typename detail::Pointee<decltype(slot_of(target))>::type;
-    if (!groups<W, E>(target.data(), static_cast<E*>(nullptr), at.g, static_cast<E>(term)))
-        atomicAdd(target.data() + at.g, static_cast<E>(term));
+    if (!groups<W, E>(target, NoComp{}, at.g, static_cast<E>(term))) atomicAdd(slot(target, at.g), static_cast<E>(term));
 }
 
-template <int W, class V, class T>
-HK_FI void addCompensated(const V& target, const V& comp, const SampleIndex& at, T term, const SampleIndex&,
+template <int W, class V, class C, class T>
+HK_FI void addCompensated(const V& target, const C& comp, const SampleIndex& at, T term, const SampleIndex&,
                           State&) {
     using E = typename detail::Pointee<decltype(slot_of(target))>::type;
-    if (!groups<W, E>(target.data(), comp.data(), at.g, static_cast<E>(term)))
-        hawk_abi::atomic_add_compensated(target.data() + at.g, comp.data() + at.g, static_cast<E>(term));
+    if (!groups<W, E>(target, comp, at.g, static_cast<E>(term)))
+        hawk_abi::atomic_add_compensated(slot(target, at.g), slot(comp, at.g), static_cast<E>(term));
 }
 
 template <class V, class T> HK_FI void addTested(const V& target, const SampleIndex& at, T term, State& s) {
     add<32>(target, at, term, at, s);
 }
 
-template <class V, class T>
-HK_FI void addTestedCompensated(const V& target, const V& comp, const SampleIndex& at, T term, State& s) {
+template <class V, class C, class T>
+HK_FI void addTestedCompensated(const V& target, const C& comp, const SampleIndex& at, T term, State& s) {
     addCompensated<32>(target, comp, at, term, at, s);
 }
 
 template <class V, class T> HK_FI void addSorted(const V& target, const SampleIndex& at, T term, State&) {
     using E = typename detail::Pointee<decltype(slot_of(target))>::type;
-    if (!sorted_runs<E>(target.data(), static_cast<E*>(nullptr), at.g, static_cast<E>(term)))
-        atomicAdd(target.data() + at.g, static_cast<E>(term));
+    if (!sorted_runs<E>(target, NoComp{}, at.g, static_cast<E>(term))) atomicAdd(slot(target, at.g), static_cast<E>(term));
 }
 
-template <class V, class T>
-HK_FI void addSortedCompensated(const V& target, const V& comp, const SampleIndex& at, T term, State&) {
+template <class V, class C, class T>
+HK_FI void addSortedCompensated(const V& target, const C& comp, const SampleIndex& at, T term, State&) {
     using E = typename detail::Pointee<decltype(slot_of(target))>::type;
-    if (!sorted_runs<E>(target.data(), comp.data(), at.g, static_cast<E>(term)))
-        hawk_abi::atomic_add_compensated(target.data() + at.g, comp.data() + at.g, static_cast<E>(term));
+    if (!sorted_runs<E>(target, comp, at.g, static_cast<E>(term)))
+        hawk_abi::atomic_add_compensated(slot(target, at.g), slot(comp, at.g), static_cast<E>(term));
 }
+
 #endif
 
 }  // namespace run
+
+#if defined(__CUDACC__) || defined(__CUDACC_RTC__)
+// ------------------------------------------------- block-private scatter targets
+
+// The shared-memory share of an entry whose targets a block privatises: the
+// block's dynamic shared memory, handed out target by target in unpack order.
+struct PrivSpace {
+    unsigned char* base;
+    unsigned bytes;
+    unsigned used;
+};
+
+HK_FI PrivSpace private_space() {
+    extern __shared__ __align__(16) unsigned char hk_priv_dyn[];
+    unsigned r;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(r));
+    return PrivSpace{hk_priv_dyn, r, 0u};
+}
+
+// A block's private copy of the target `v` (zeroed), when the rest of its
+// share holds the plane's slots; else the plane itself.  Every thread of the
+// block makes the same calls in the same order, then the block waits
+// (__syncthreads) before its first commit.
+template <class T> HK_FI PrivOut<T> privatise(PrivSpace& sp, const ScalarOut<T>& v) {
+    PrivOut<T> o{v.p, nullptr, v.n, false};
+    const unsigned long long need = (v.n * sizeof(T) + 15ull) & ~15ull;
+    if (v.n > 0 && sp.used + need <= sp.bytes) {
+        o.local = reinterpret_cast<T*>(sp.base + sp.used);
+        o.priv = true;
+        sp.used += static_cast<unsigned>(need);
+        for (u64 k = threadIdx.x; k < v.n; k += blockDim.x) o.local[k] = T(0);
+    }
+    return o;
+}
+
+// The block's copies into the planes, after every commit of the block
+// (__syncthreads first): a plain target adds each nonzero slot, a compensated
+// one commits each slot with the compensated add and adds its companion's
+// slot, an OR target ORs each nonzero word.
+template <class T> HK_FI void flush_add(const PrivOut<T>& o) {
+    if (!o.priv) return;
+    for (u64 k = threadIdx.x; k < o.n; k += blockDim.x) {
+        const T v = o.local[k];
+        if (v != T(0)) atomicAdd(o.global + k, v);
+    }
+}
+
+template <class T> HK_FI void flush_compensated(const PrivOut<T>& o, const PrivOut<T>& c) {
+    for (u64 k = threadIdx.x; k < o.n; k += blockDim.x) {
+        if (o.priv) {
+            const T v = o.local[k];
+            if (v != T(0)) hawk_abi::atomic_add_compensated(o.global + k, c.global + k, v);
+        }
+        if (c.priv && k < c.n) {
+            const T e = c.local[k];
+            if (e != T(0)) atomicAdd(c.global + k, e);
+        }
+    }
+}
+
+template <class T> HK_FI void flush_or(const PrivOut<T>& o) {
+    if (!o.priv) return;
+    for (u64 k = threadIdx.x; k < o.n; k += blockDim.x) {
+        const unsigned v = static_cast<unsigned>(o.local[k]);
+        if (v != 0u) atomicOr(reinterpret_cast<unsigned*>(o.global + k), v);
+    }
+}
+#endif
 }  // namespace accum
 }  // namespace hk

@@ -182,8 +182,19 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
     # the run state of each keyed commit target the body names (hk/accum.cuh)
     states = sorted(set(re.findall(r"\bhawk_run_(\w+)\b", "\n".join(loop))))
     run_states = [f"    hk::accum::run::State hawk_run_{t}{{}};" for t in states]
+    private = None
+    if frame == "lane" and not smem and one_step is None and frame_note is None:
+        private = _privatised(walk, body, {x for s in sums for x in (s.name, getattr(s.companion, "name", None))})
+    if private is not None:
+        head, tail, _targets = private
+        loop = [*head, *loop, *tail]
+        smem_entry = PRIVATE_BYTES
+    else:
+        smem_entry = 0
     prelude = [*prelude_lines(name, mode), *([f"HK_DYNAMIC_SMEM({smem})"] if smem else []), ""]
     parts = [
+        *([f'extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__{name} = {smem_entry}u;']
+          if smem_entry else []),
         wrapper.entry_signature(walk, name, min_blocks),
         "{",
         wrapper.unpack(walk, plan),
@@ -216,7 +227,68 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
                        "stages": plan.stages if plan is not None else 0, "min_blocks": min_blocks or 0,
                        "persist": f"{name}{PERSIST_SUFFIX}" if persist is not None else None,
                        "step_fp64_ops": step_fp64_ops(kernel) if persist is not None else None,
-                       "lane_refill": frame_note == "refill", "folds": folds})
+                       "lane_refill": frame_note == "refill", "folds": folds,
+                       "private_targets": [t for t, _k, _c in (private[2] if private else ())],
+                       "private_smem": smem_entry})
 
 
 _IDENT = re.compile(r"[A-Za-z_][A-Za-z0-9_]*")
+
+#: Dynamic shared memory of an entry that privatises its scatter targets: per
+#: block, the targets' copies (a target whose plane does not fit its share
+#: commits to the plane).  At 32 KB, seven 256-thread blocks stay resident.
+PRIVATE_BYTES = 32 * 1024
+
+_COMMITS = (
+    (re.compile(r"hawk_abi::accum_add_compensated\((\w+), (\w+),"), "compensated"),
+    (re.compile(r"hk::accum::run::add(?:Tested|Sorted)?Compensated(?:<\d+>)?\((\w+), (\w+),"), "compensated"),
+    (re.compile(r"hawk_abi::accum_add\((\w+),"), "add"),
+    (re.compile(r"hk::accum::run::add(?:Tested|Sorted)?(?:<\d+>)?\((\w+),"), "add"),
+    (re.compile(r"hawk_abi::accum_or\((\w+),"), "or"),
+)
+
+
+def _privatised(walk, body: str, row_planes: set):
+    """``(head, tail, targets)`` of an entry whose scattered commits go through
+    block-private copies of their targets (hk::accum::privatise), or None.
+    A target the body commits one way only (plain, compensated with its
+    companion, or OR) is privatised; the copies shadow the targets' views for
+    the loop, and the block adds them into the planes when it leaves."""
+    from hawk.emit.spelling import binding_name
+
+    scatter = {binding_name(role, name) for role, name in walk.arg_spec
+               if role == "accum_out" and name not in row_planes}
+    if re.search(r"hk::accum::run::add(?:Compensated)?<\d+>\(", body):
+        return None     # aligned runs already commit once per run of lanes: a copy gains little
+    kinds: dict = {}
+    comps: dict = {}
+    for pattern, kind in _COMMITS:
+        for m in pattern.finditer(body):
+            target = m.group(1)
+            if target not in scatter:
+                return None
+            kinds.setdefault(target, set()).add(kind)
+            if kind == "compensated":
+                comps.setdefault(target, set()).add(m.group(2))
+    if not kinds:
+        return None
+    targets = []
+    for target, ks in sorted(kinds.items()):
+        if len(ks) != 1 or (ks == {"compensated"} and len(comps[target]) != 1):
+            return None
+        kind = next(iter(ks))
+        targets.append((target, kind, next(iter(comps[target])) if kind == "compensated" else None))
+    named = [t for t, _k, _c in targets] + [c for _t, _k, c in targets if c]
+    head = ["    hk::accum::PrivSpace hawk_ps = hk::accum::private_space();"]
+    head += [f"    const auto hawk_pv_{b} = hk::accum::privatise(hawk_ps, {b});" for b in named]
+    head += ["    __syncthreads();", "    {"]
+    head += [f"    const auto& {b} = hawk_pv_{b};" for b in named]
+    tail = ["    }", "    __syncthreads();"]
+    for target, kind, comp in targets:
+        if kind == "compensated":
+            tail.append(f"    hk::accum::flush_compensated(hawk_pv_{target}, hawk_pv_{comp});")
+        elif kind == "or":
+            tail.append(f"    hk::accum::flush_or(hawk_pv_{target});")
+        else:
+            tail.append(f"    hk::accum::flush_add(hawk_pv_{target});")
+    return head, tail, targets

@@ -175,6 +175,7 @@ def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "flo
         "step_fp64_ops": unit.notes.get("step_fp64_ops"),
         "lane_refill": unit.notes.get("lane_refill", False),
         "folds": unit.notes.get("folds") or {},
+        "private_targets": unit.notes.get("private_targets") or [],
         "sample_sums": [{"name": n, "op": op, "companion": comp} for n, op, comp in unit.sums],
         "slots": _slot_records(kernel.walk),
         "nvrtc_options": [o for o in options() if not o.startswith("-I")],

@@ -146,3 +146,29 @@ def test_a_partition_commits_only_its_samples():
                 base=1000, count=30000)
     want, mag, _cnt = exact(w["key"][1000:31000], w["x"][1000:31000], 128)
     within(host(acc), want, mag, 2)
+
+
+@pytest.mark.parametrize("slots", [2048, 3000, 50000])
+def test_histogram_whose_target_fits_a_block_partly_or_not_at_all(slots):
+    """A block commits into shared-memory copies of its targets when they fit
+    its share (2048 slots: the sum and its companion both; 3000: the sum only,
+    the companion's residuals go to the plane; 50000: neither) -- the same
+    contract on every path."""
+    n = 300000
+    w = workloads.scatter(n, seed=slots, slots=slots)
+    prior = np.random.default_rng(slots).uniform(0.0, 1.0, slots)
+    acc = dev(prior.copy())
+    runtime.run(runtime.load(BUNDLES, "histogram"), x=dev(w["x"]), key=dev(w["key"]), acc=acc)
+    want, mag, _cnt = exact(w["key"], w["x"], slots, prior)
+    within(host(acc), want, mag, 2)
+
+
+@pytest.mark.parametrize("slots", [64, 20000])
+def test_bitmask_through_a_private_copy_and_straight_to_the_plane(slots):
+    n = 200000
+    w = workloads.scatter(n, seed=slots + 1, slots=slots)
+    acc = torch.zeros(slots, dtype=torch.uint32, device="cuda")
+    runtime.run(runtime.load(BUNDLES, "bitmask"), bits=dev(w["bits"]), key=dev(w["key"]), acc=acc)
+    want = np.zeros(slots, dtype=np.uint32)
+    np.bitwise_or.at(want, w["key"], w["bits"])
+    np.testing.assert_array_equal(host(acc), want)
