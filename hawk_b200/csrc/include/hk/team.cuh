@@ -226,21 +226,19 @@ HK_FI void forward(const Team& tm, T* x, int k, E entry, D diag) {
 // x_j) are made by the whole team into the products row first.
 template <class T, int N, bool DIV, class E, class D>
 HK_FI void backward(const Team& tm, T* x, int k, E entry, D diag) {
-    if (tm.bytes >= inplace_bytes<T>(N)) {
+    if (tm.bytes >= inplace_bytes<T>(N) && k == 1) {
         T* prod = reinterpret_cast<T*>(tm.smem + kScratchBytes);
-        for (int c = 0; c < k; ++c) {
-            for (int r = 0; r < N; ++r) {
-                const int i = N - 1 - r;
-                for (int j = i + 1 + tm.rank; j < N; j += tm.size) prod[j] = entry(i, j) * x[j * k + c];
-                tm.sync();
-                if (tm.rank == 0) {
-                    T acc = x[i * k + c];
+        for (int r = 0; r < N; ++r) {
+            const int i = N - 1 - r;
+            for (int j = i + 1 + tm.rank; j < N; j += tm.size) prod[j] = entry(i, j) * x[j];
+            tm.sync();
+            if (tm.rank == 0) {
+                T acc = x[i];
 #pragma unroll 8
-                    for (int j = i + 1; j < N; ++j) acc = acc - prod[j];
-                    x[i * k + c] = DIV ? acc / diag(i) : acc;
-                }
-                tm.sync();
+                for (int j = i + 1; j < N; ++j) acc = acc - prod[j];
+                x[i] = DIV ? acc / diag(i) : acc;
             }
+            tm.sync();
         }
         return;
     }
