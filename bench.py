@@ -707,15 +707,66 @@ def run_only_steps(name: str, n: int, steps: int, warmup: int, local: int, persi
             "launches": warmup + steps}
 
 
+def _only_planes(name: str, n: int, dev):
+    """Seeded planes of a scatter or team-form benchmark kernel at ``n``
+    samples (lanes), as ``run_configs`` / ``run_team`` bind them."""
+    import torch
+
+    from hawk_b200 import workloads
+
+    def t(a):
+        return torch.as_tensor(np.ascontiguousarray(a), device=dev)
+
+    def e(shape, dtype=torch.float64):
+        return torch.empty(shape, dtype=dtype, device=dev)
+
+    if name.startswith("team_"):
+        kernel, size = name.rsplit("_", 1)
+        k = int(size)
+        w = workloads.team(k, n, "spd" if kernel == "team_chol" else "general", seed=k, bad=None)
+        planes = {"A": t(w["A"]), "b": t(w["b"]), "B": t(w["B"]), "x": e((k, n)), "X": e((k, 2, n)),
+                  "info": e(n, torch.int32)}
+        planes.update({"L": e((k, k, n))} if kernel == "team_chol" else {"det": e(n)})
+        return planes
+    w = workloads.scatter(n, 1, slots=SCATTER_SLOTS)
+    segs = -(-n // workloads.SEGMENT)
+    return {
+        "segment_sum": lambda: {"x": t(w["x"]), "acc": e(segs), "acc_c": e(segs)},
+        "keyed_sum": lambda: {"x": t(w["x"]), "key": t(w["sorted_key"]), "acc": e(SCATTER_SLOTS)},
+        "histogram": lambda: {"x": t(w["x"]), "key": t(w["key"]), "acc": e(SCATTER_SLOTS),
+                              "acc_c": e(SCATTER_SLOTS)},
+        "bitmask": lambda: {"bits": t(w["bits"]), "key": t(w["key"]), "acc": e(SCATTER_SLOTS, torch.uint32)},
+        "gather": lambda: {"idx": t(w["idx"]), "w": t(w["w"]), "table": t(w["table"]), "y": e(n)},
+        "gather_vjp": lambda: {"idx": t(w["idx"]), "w": t(w["w"]), "table": t(w["table"]), "bar_y": t(w["bar_y"]),
+                               "bar_w": e(n), "bar_table": e(SCATTER_SLOTS)},
+    }[name]()
+
+
 def run_only(name: str, n: int, steps: int, warmup: int, local: int) -> dict:
-    """One benchmark kernel (``name`` of the bundles, float64) at ``n`` samples:
-    seeded inputs, ``warmup`` + ``steps`` launches, the mean device time."""
+    """One benchmark kernel (``name`` of the bundles, float64) at ``n`` samples
+    (lanes, for a team-form kernel): seeded inputs, ``warmup`` + ``steps``
+    runs, the mean device time."""
     import torch
 
     from hawk_b200 import runtime, workloads
     from hawk_b200.planes import from_torch
 
     dev = torch.device("cuda", local)
+    if name.startswith("team_") or name in ("segment_sum", "keyed_sum", "histogram", "bitmask", "gather",
+                                            "gather_vjp"):
+        k = runtime.load(BUNDLES, name, "float64", local)
+        planes = _only_planes(name, n, dev)
+        for _ in range(warmup):
+            runtime.run(k, **planes)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(steps):
+            runtime.run(k, **planes)
+        b.record()
+        b.synchronize()
+        ms = a.elapsed_time(b) / steps
+        return {"kernel": name, "n": n, "ms": ms, "launches": warmup + steps}
     base = name.split("_")[0] if not name.startswith(("poly_loss", "spd_solve")) else \
         ("poly_loss" if name.startswith("poly_loss") else "spd_solve")
     w = workloads.MAKERS[base](n, 1)
