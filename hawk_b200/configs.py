@@ -44,7 +44,7 @@ from .frontend import load
 hawk = load()
 
 import hawk.math as m  # noqa: E402
-from hawk import Index, Int32, Kernel, Matrix, Mutable, Param, Scalar, Sorted, Table, Terminated, UInt32, Vector  # noqa: E402,E501
+from hawk import Grid, Index, Int32, Kernel, Matrix, Mutable, Param, Scalar, Sorted, Table, Terminated, UInt32, Vector  # noqa: E402,E501
 from hawk.diff import jvp, param_planes, vjp  # noqa: E402
 
 
@@ -318,6 +318,22 @@ def centred(x: Scalar, z: Mutable[Vector[3]]):
     z = v - hawk.mean(v)
 
 
+@hawk.kernel
+def key_total(lane: Grid["key", "row":8], x: Scalar) -> Scalar:
+    return hawk.sum(x, over="row")
+
+
+@hawk.kernel
+def key_share(lane: Grid["key", "row":8], x: Scalar, z: Mutable[Scalar]):
+    z = x / hawk.sum(x, over="row")
+
+
+#: Sums over some lane axes (hawk.sum(x, over=...), hawk/trace/reduce.py:
+#: one value per kept key): returned as an output, or read back in the body at
+#: the lane's own key (a keyed plane the runtime owns between two stages).
+KEYED_KERNELS = {k.name: k for k in (key_total, key_share)}
+
+
 #: Sums over samples read back in the body (hawk/ir/split.py): each runs as
 #: stages with the cell finished on the device between them -- x / sum(x),
 #: the standardised x with its mean stored and the sum of squares of the
@@ -377,5 +393,6 @@ KERNELS = {
     "bitmask": (bitmask, ("float64",)),
     **{name: (k, ("float64",)) for name, k in TEAM_KERNELS.items()},
     **{name: (k, ("float64",)) for name, k in READBACK_KERNELS.items()},
+    **{name: (k, ("float64",)) for name, k in KEYED_KERNELS.items()},
     "share_vjp": (Kernel("share_vjp", vjp(share, wrt=("x",))), ("float64",)),
 }

@@ -405,6 +405,9 @@ class SplitKernel:
         b200 = sidecar["b200"]
         self.device = int(device if device is not None else _current_device())
         self.team_planes = sidecar.get("team_planes") or {}
+        self.keyed = sidecar.get("keyed") or {}
+        self.lane_axes = [(a.get("label"), a.get("extent"))
+                          for a in ((sidecar.get("launch") or {}).get("lane_space") or {}).get("axes", [])]
         self.cell_specs = sidecar.get("cells") or {}
         self.records = b200["split"]
         self.stages = []
@@ -439,6 +442,44 @@ class SplitKernel:
                                   dtype=torch.int32 if spec.get("dtype") == "int32" else real, device=dev)
                 for name, spec in self.team_planes.items()}
         return self._scratch[n]
+
+    def keyed_size(self, spec: dict, n: int) -> int:
+        """The elements of a keyed plane at ``n`` lanes: ``width`` payload
+        entries over the kept lane axes, a runtime axis as long as the lane
+        axis allows (hawk/_lane_bind.py:92-98)."""
+        inner = 1
+        for _label, extent in self.lane_axes[1:]:
+            inner *= int(extent)
+        runtime_extent = n // inner if self.lane_axes else n
+        size = int(spec.get("width", 1))
+        for _label, extent in spec.get("axes", []):
+            size *= runtime_extent if extent is None else int(extent)
+        return size
+
+    def keyed_planes(self, n: int, stream=None) -> dict:
+        """The keyed planes the stages pass between them (a sum over some lane
+        axes read back at the lane's key) and their compensated companions:
+        made once per sample count and zeroed for every run
+        (hawk/runtime.py:655-673), in stream order."""
+        import torch
+
+        key = ("keyed", n)
+        if key not in self._scratch:
+            real = torch.float64 if self.mode == "float64" else torch.float32
+            dev = torch.device("cuda", self.device)
+            planes = {}
+            for name, spec in self.keyed.items():
+                planes[name] = torch.empty(self.keyed_size(spec, n), dtype=real, device=dev)
+                for stage in self.stages:
+                    for comp, target in (stage.sidecar.get("companions") or {}).items():
+                        if target == name:
+                            planes[comp] = torch.empty_like(planes[name])
+            self._scratch[key] = planes
+        planes = self._scratch[key]
+        with torch.cuda.stream(_torch_stream(stream, self.device)):
+            for t in planes.values():
+                t.zero_()
+        return planes
 
     def cell_values(self) -> dict:
         """One device plane per cell (its columns), where a finished cell lives
@@ -486,6 +527,7 @@ class SplitKernel:
                             f"start on a row (base % 32 == 0), got base={base}")
         with self._lock:
             scratch = {k: from_torch(v) for k, v in self.scratch(n_samples).items()}
+            scratch.update({k: from_torch(v) for k, v in self.keyed_planes(n_samples, stream).items()})
             cells = self.cell_values()
             for stage, record in zip(self.stages, self.records):
                 names = {n for _r, n in stage.arg_spec}

@@ -23,19 +23,21 @@ from .assemble import render_unit
 from .nvrtc import ARCH, compile_cubin, options
 
 
-def _reference_sidecar(name: str, walk, mode: str) -> dict:
+def _reference_sidecar(name: str, walk, mode: str, lane_space=None) -> dict:
     """The reference's v2 sidecar for the kernel (its own function), or the
     subset this runtime reads when that function needs the reference's
-    third-party packages."""
+    third-party packages.  ``lane_space`` is the kernel's launch shape
+    (``Grid`` axes; the reference's sidecar records it as launch.lane_space)."""
     from unittest import mock
 
     try:
         from hawk.artifact import sidecar as sc
 
+        extra = {} if lane_space is None else {"lane_space": lane_space}
         # The reference records where its third-party headers came from; a b200
         # unit includes only this build's device library, so that is recorded.
         with mock.patch.object(sc, "_root_or_sealed_marker", lambda resolver: "hawk_b200/csrc/include"):
-            return sc.sidecar_meta(name, walk, fmt="cubin", scalar_type=mode, exec_targets=("device",))
+            return sc.sidecar_meta(name, walk, fmt="cubin", scalar_type=mode, exec_targets=("device",), **extra)
     except Exception:                                   # noqa: BLE001 -- fall back to the read subset
         return _subset_sidecar(name, walk, mode)
 
@@ -103,10 +105,12 @@ def build_split_kernel(kernel, directory, *, name: str | None = None, mode: str 
     stem = f"{name}.{mode}"
     (directory / f"{stem}.cu").write_text(unit.text)
     (directory / f"{stem}.cubin").write_bytes(cubin)
-    sidecar = _reference_sidecar(name, members[0].walk, mode)
+    sidecar = _reference_sidecar(name, members[0].walk, mode, getattr(kernel, "lane_space", None))
     sidecar = json.loads(json.dumps(sidecar, default=str))
     sidecar.update(json.loads(json.dumps(block, default=str)))
-    scratch = set(block.get("team_planes") or {}) | cell_planes(block.get("cells") or {})
+    keyed = set(block.get("keyed") or {})
+    keyed |= {c for m in members for c, t in (m.walk.companions or {}).items() if t in keyed}
+    scratch = set(block.get("team_planes") or {}) | cell_planes(block.get("cells") or {}) | keyed
     sidecar["b200"] = {
         "entry": name,
         "arch": ARCH,
@@ -159,7 +163,7 @@ def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "flo
     stem = f"{name}.{mode}"
     (directory / f"{stem}.cu").write_text(unit.text)
     (directory / f"{stem}.cubin").write_bytes(cubin)
-    sidecar = _reference_sidecar(name, kernel.walk, mode)
+    sidecar = _reference_sidecar(name, kernel.walk, mode, getattr(kernel, "lane_space", None))
     sidecar = json.loads(json.dumps(sidecar, default=str))
     sidecar["b200"] = {
         "entry": name,

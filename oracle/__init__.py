@@ -413,3 +413,23 @@ def share_vjp(x, bar_z):
     s = sample_sum(x)
     c = sample_sum(-((bar_z * (x / s)) / s))
     return (bar_z / s) + c
+
+
+def key_sums(x, rows: int = 8):
+    """Per key (``rows`` consecutive lanes), the sum an aligned-run commit makes
+    on a fully converged warp: the xor butterfly over the run's lanes (offsets
+    rows / 2, ..., 1; lane l adds lane l ^ o), then one add into the zeroed slot
+    (hk/accum.cuh groups)."""
+    v = np.ascontiguousarray(x, dtype=np.float64).reshape(-1, rows).copy()
+    o = rows // 2
+    while o >= 1:
+        idx = np.arange(rows) ^ o
+        v = v + v[:, idx]
+        o //= 2
+    return 0.0 + v[:, 0]
+
+
+def key_share(x, rows: int = 8):
+    """z = x / (its key's sum)."""
+    s = key_sums(x, rows)
+    return x / np.repeat(s, rows)

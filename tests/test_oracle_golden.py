@@ -251,3 +251,14 @@ def test_sample_sum_max_and_min_ignore_nan():
     x = np.array([1.0, np.nan, 3.0, -2.0] * 20)
     assert oracle.sample_sum(x, "max") == 3.0
     assert oracle.sample_sum(x, "min") == -2.0
+
+
+def test_key_sums_match_exact_sums():
+    import math
+
+    x = np.random.default_rng(3).normal(0.0, 1.0, 8 * 500)
+    got = oracle.key_sums(x)
+    for k in range(500):
+        seg = x[8 * k:8 * k + 8]
+        assert abs(got[k] - math.fsum(seg)) <= 8 * np.finfo(float).eps * math.fsum(np.abs(seg))
+    close(oracle.key_share(np.ones(16)), np.full(16, 1 / 8.0))
