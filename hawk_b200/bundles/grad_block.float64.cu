@@ -1,0 +1,74 @@
+// hawk_b200 unit 'grad_block' (scalar mode float64), sm_100a.
+// Body text: the reference renderer's; entry, views and frame: the b200 wrapper.
+#include "hk/hawk_b200.cuh"
+
+using Real = double;
+using Int = long long;
+
+HK_SELF_CHECK_EXPORTS
+
+extern "C" __global__ void __launch_bounds__(256) grad_block(
+    hk::abi::ScalarHandle p_wout_tmb0_u,
+    hk::abi::ScalarHandle p_wout_tmb0_v,
+    hk::abi::GRefMirror p_vin_j,
+    hk::abi::ScalarHandle p_psc_r,
+    long long base,
+    long long count,
+    long long nSamples)
+{
+    const hk::ScalarOut<Real> wout_tmb0_u(p_wout_tmb0_u);
+    (void)wout_tmb0_u;
+    const hk::ScalarOut<Real> wout_tmb0_v(p_wout_tmb0_v);
+    (void)wout_tmb0_v;
+    const hk::VecIn<Real, 20> vin_j(p_vin_j);
+    (void)vin_j;
+    const hk::ScalarIn<Real> psc_r(p_psc_r);
+    (void)psc_r;
+    for (long long hawk_flat = hk::lane_first(); hawk_flat < count; hawk_flat += hk::lane_step()) {
+        const long long hawk_i = base + hawk_flat;
+        const hk::SampleIndex i{hawk_i};
+        (void)hawk_i;
+        (void)nSamples;
+        const auto vin_j_i = vin_j[i].get();
+        for (Int hawk_lk = 0; hawk_lk < 20; ++hawk_lk) wout_tmb0_u.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 20 + hawk_lk] = vin_j[i].at(hawk_lk);
+        wout_tmb0_v.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 1] = psc_r[i].eval();
+    }
+}
+
+extern "C" __device__ const unsigned int hk_team_threads__grad_block_2 = 32u;
+extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__grad_block_2 = 3808u;
+extern "C" __global__ void __launch_bounds__(32) grad_block_2(
+    hk::abi::ScalarHandle p_wout_out,
+    hk::abi::ScalarHandle p_wout_tmb0_u,
+    hk::abi::ScalarHandle p_wout_tmb0_v,
+    long long base,
+    long long count,
+    long long nSamples)
+{
+    const hk::ScalarOut<Real> wout_out(p_wout_out);
+    (void)wout_out;
+    const hk::ScalarOut<Real> wout_tmb0_u(p_wout_tmb0_u);
+    (void)wout_tmb0_u;
+    const hk::ScalarOut<Real> wout_tmb0_v(p_wout_tmb0_v);
+    (void)wout_tmb0_v;
+    hk::linalg::team::begin_entry();
+    const long long hawk_teams = static_cast<long long>(blockDim.x >> 5);
+    for (long long hawk_flat = static_cast<long long>(blockIdx.x) * hawk_teams + (threadIdx.x >> 5); hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {
+        const long long hawk_i = base + hawk_flat;
+        const hk::SampleIndex i{hawk_i};
+        (void)hawk_i;
+        (void)nSamples;
+        const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here();
+        const long long hawk_lane = hawk_i;
+        {  // block_sum, n = 20
+            const std::size_t hawk_key = static_cast<std::size_t>(hawk_lane);
+            const std::size_t hawk_keys = static_cast<std::size_t>(count);
+            const std::size_t hawk_rows = static_cast<std::size_t>(nSamples) / hawk_keys;
+            const Real* const hawk_u = wout_tmb0_u.data();
+            const Real* const hawk_v = wout_tmb0_v.data();
+            Real* const hawk_out = wout_out.data();
+            hk::linalg::team::blockSum<20, 1>(hawk_tm, hawk_out + hawk_key, hawk_u, hawk_v, hawk_key * hawk_rows, hawk_rows, 20, 1, nullptr, 1 * hawk_keys, hawk_keys, 1);
+        }
+        __syncwarp();
+    }
+}

@@ -328,10 +328,23 @@ def key_share(lane: Grid["key", "row":8], x: Scalar, z: Mutable[Scalar]):
     z = x / hawk.sum(x, over="row")
 
 
+@hawk.kernel
+def gram_block(lane: Grid["key", "row":8], j: Vector[6]) -> Matrix[6, 6]:
+    return hawk.sum(m.outer(j, j), over="row")
+
+
+@hawk.kernel
+def grad_block(lane: Grid["key", "row":8], j: Vector[20], r: Scalar) -> Vector[20]:
+    return hawk.sum(j * r, over="row")
+
+
 #: Sums over some lane axes (hawk.sum(x, over=...), hawk/trace/reduce.py:
 #: one value per kept key): returned as an output, or read back in the body at
-#: the lane's own key (a keyed plane the runtime owns between two stages).
-KEYED_KERNELS = {k.name: k for k in (key_total, key_share)}
+#: the lane's own key (a keyed plane the runtime owns between two stages); a
+#: per-key block of more than 16 entries (an outer product's Gram block, a
+#: gradient of 20) is a BlockSum: the rows stored by a per-lane stage, each
+#: key's block summed in lane order by a team stage (hawk/ir/team.py:544-600).
+KEYED_KERNELS = {k.name: k for k in (key_total, key_share, gram_block, grad_block)}
 
 
 #: Sums over samples read back in the body (hawk/ir/split.py): each runs as

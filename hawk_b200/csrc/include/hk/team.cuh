@@ -615,6 +615,32 @@ HK_FI void luInverse(const Team& tm, const TeamLu<T, N>& f, T* x) {
     luSolve<N>(tm, f, x, x, N);
 }
 
+// ------------------------------------------------------------ block sums
+
+// The block of one key (a BlockSum, hawk/ir/team.py:544-600): entry (a, b) is
+// the sum over the key's rows r = first .. first + rows - 1, in lane order
+// from 0, of u[row a] * v[row b], where a lane holds `per` rows (row h of
+// lane l at l * per + h; u rows of stride su, v rows of stride sv, sv = 0 for
+// the constant 1); stored at out[a * ors + b * ocs].  The team's threads take
+// entries; each entry's sum is one chain in lane order -- the same bits
+// whatever the team.  An index map (an active-set build) is not built.
+template <int P, int Q, class T>
+HK_FI void blockSum(const Team& tm, T* out, const T* u, const T* v, std::size_t first, std::size_t rows,
+                    std::size_t su, std::size_t sv, const void* index, std::size_t ors, std::size_t ocs, int per) {
+    (void)index;
+    for (int e = tm.rank; e < P * Q; e += tm.size) {
+        const int a = e / Q, b = e % Q;
+        T s = T(0);
+        for (std::size_t r = 0; r < rows; ++r)
+            for (int h = 0; h < per; ++h) {
+                const std::size_t row = (first + r) * static_cast<std::size_t>(per) + static_cast<std::size_t>(h);
+                s = s + (u[row * su + a] * v[row * sv + b]);
+            }
+        out[a * ors + b * ocs] = s;
+    }
+    tm.sync();
+}
+
 // det(A): the product of U's diagonal, negated per exchange as it is met
 // (hawk/embedded/linalg.py:402-418); 0 for a failed factor.  One thread.
 template <int N, class T>

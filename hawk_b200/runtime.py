@@ -481,6 +481,38 @@ class SplitKernel:
                 t.zero_()
         return planes
 
+    def block_outputs(self) -> dict:
+        """The block sums' output planes a caller binds: ``{name: (payload, keyed)}``."""
+        out = {}
+        for record in self.records:
+            if record.get("grid") == "keys" and record.get("keyed"):
+                for slot in record["slots"]:
+                    if slot["role"] == "wide_out" and slot["name"] in {n for _r, n in self.arg_spec}:
+                        out[slot["name"]] = (tuple(record["keyed"].get("payload") or ()), record["keyed"])
+        return out
+
+    def flat_block_outputs(self, arrays: dict, n: int) -> dict:
+        """A block sum's output bound as ``(*payload, keys)`` (payload first,
+        hawk/ir/team.py:591-600), checked and handed to its stage flat."""
+        outs = self.block_outputs()
+        if not outs:
+            return arrays
+        import torch
+
+        arrays = dict(arrays)
+        for name, (payload, keyed) in outs.items():
+            if name not in arrays:
+                continue
+            t = arrays[name]
+            keys = self.keyed_size(keyed, n) // int(keyed.get("width", 1))
+            want = (*payload, keys)
+            if not torch.is_tensor(t) or tuple(t.shape) != want or not t.is_contiguous():
+                raise HawkError(f"kernel {self.name!r}: argument {name!r} is the per-key block sum, a contiguous "
+                                f"device tensor of shape {want} (payload first, one per key), got "
+                                f"{tuple(getattr(t, 'shape', ()))}")
+            arrays[name] = t.reshape(-1)
+        return arrays
+
     def cell_values(self) -> dict:
         """One device plane per cell (its columns), where a finished cell lives
         for the stages that read it."""
@@ -509,6 +541,10 @@ class SplitKernel:
             raise HawkError(f"kernel {self.name!r}: {missing} are declared but not bound")
         uniforms = {n for r, n in self.arg_spec if r == "uniform"}
         values = {k: v for k, v in arrays.items() if k in uniforms}
+        if n_samples is None:
+            n_samples = self.stages[0].n_from({k: as_plane(k, v) for k, v in arrays.items()
+                                               if k not in uniforms and k not in self.block_outputs()})
+        arrays = self.flat_block_outputs(arrays, n_samples)
         planes = {k: as_plane(k, v) for k, v in arrays.items() if k not in uniforms}
         for c, spec in self.cells.items():
             p = planes[c]
@@ -516,8 +552,6 @@ class SplitKernel:
                 raise HawkError(f"kernel {self.name!r}: cell {c!r} must be a {self.mode} plane of "
                                 f"{spec.get('columns', 1)} value(s) on device {self.device}, got {p.dtype} "
                                 f"{p.shape} on {p.device}")
-        if n_samples is None:
-            n_samples = self.stages[0].n_from(planes)
         count = n_samples - base if count is None else count
         if base < 0 or count < 0 or base + count > n_samples:
             raise HawkError(f"kernel {self.name!r}: partition [{base}, {base + count}) is outside "
@@ -542,9 +576,16 @@ class SplitKernel:
                 if record.get("cells_out"):
                     state = stage.cells_state(n_samples)
                     bound.update({k: from_torch(v) for k, v in state["rows"].items()})
-                stage.check(bound, values, n_samples)
-                stage.bind_all(bound, values, n_samples)
-                stage.launch(base, count, n_samples, stream)
+                if record.get("grid") == "keys":
+                    # a block-sum stage: one team per key over the whole run
+                    keys = self.keyed_size(record["keyed"], n_samples) // int(record["keyed"].get("width", 1))
+                    stage.check(bound, values, keys)
+                    stage.bind_all(bound, values, n_samples)
+                    stage.launch(0, keys, n_samples, stream)
+                else:
+                    stage.check(bound, values, n_samples)
+                    stage.bind_all(bound, values, n_samples)
+                    stage.launch(base, count, n_samples, stream)
                 if state is None:
                     continue
                 lo, hi = base // ROW, -(-(base + count) // ROW)

@@ -46,7 +46,7 @@ _UNBUILT = {
 
 #: The team-form calls the device library builds (hk/team.cuh).
 TEAM_BUILT = frozenset({"Team", "TeamCholesky", "TeamLu", "cholesky", "choleskyFrom", "choSolve", "triLower",
-                        "triUpperT", "lu", "luSolve", "luSolveT", "luInverse", "luDet"})
+                        "triUpperT", "lu", "luSolve", "luSolveT", "luInverse", "luDet", "blockSum"})
 _TEAM_NAME = re.compile(r"hk::linalg::team::(\w+)")
 
 

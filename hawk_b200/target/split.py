@@ -133,6 +133,12 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
         if isinstance(member, TeamStage):
             body = body_text(member.fused_body().text)
             threads, smem = team_geometry(member.team, elem)
+            if "__shared__" in body:
+                # the body keeps arrays of its own in shared memory: one team a block
+                threads, smem = 32, (smem // max(threads // 32, 1) if smem else 0)
+            if "hawk_map" in body:
+                raise HawkError(f"{name!r}: a block sum over an index map (an active-set build) is not built "
+                                "on the b200 target")
         else:                       # a copy stage: the stage's own sinks, a block per lane
             from hawk.emit.render import render_body
 
@@ -151,8 +157,10 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
             "}",
             "",
         ]
+        team_record = record.get("team") or {}
         stages.append({"entry": member.name, "kind": "team", "threads": threads, "dynamic_smem": smem,
-                       "slots": _slot_records(walk), "sample_sums": [], "cells_in": [], "cells_out": []})
+                       "slots": _slot_records(walk), "sample_sums": [], "cells_in": [], "cells_out": [],
+                       "grid": team_record.get("grid", "lanes"), "keyed": team_record.get("keyed")})
     text = "\n".join([*prelude_lines(name, mode), "", *parts])
     unit = Unit(name=name, mode=mode, text=text, body="", frame="split",
                 digest=hashlib.sha256(text.encode()).hexdigest(), entries="\n".join(parts),

@@ -433,3 +433,25 @@ def key_share(x, rows: int = 8):
     """z = x / (its key's sum)."""
     s = key_sums(x, rows)
     return x / np.repeat(s, rows)
+
+
+def block_sums(u, v=None, rows: int = 8):
+    """Per key (``rows`` consecutive lanes), the block sum_r u[:, r] v[:, r]^T
+    in lane order from 0 (a BlockSum team stage): ``u`` is (p, lanes), ``v``
+    (q, lanes) or None for the constant 1; the result is (p, q, keys), or
+    (p, keys) when ``v`` is None."""
+    u = np.asarray(u, dtype=np.float64)
+    p, lanes = u.shape
+    keys = lanes // rows
+    uu = u.reshape(p, keys, rows)
+    if v is None:
+        s = np.zeros((p, keys))
+        for r in range(rows):
+            s = s + uu[:, :, r]
+        return s
+    v = np.asarray(v, dtype=np.float64)
+    vv = v.reshape(v.shape[0], keys, rows)
+    s = np.zeros((p, v.shape[0], keys))
+    for r in range(rows):
+        s = s + (uu[:, None, :, r] * vv[None, :, :, r])
+    return s

@@ -69,3 +69,25 @@ def test_a_keyed_sum_read_back_is_two_stages_over_a_zeroed_keyed_plane(n):
         want = oracle.key_share(x)
         np.testing.assert_array_equal(host(z), want)
         np.testing.assert_allclose(host(z), want, rtol=1e-12)
+
+
+@pytest.mark.parametrize("keys", [1, 37, 4096])
+def test_gram_blocks_are_ordered_sums_per_key(keys):
+    """hawk.sum(outer(j, j), over="row") of a 6-vector: a BlockSum (36 entries)
+    -- the rows stored by the first stage, each key's 6 x 6 block summed in
+    lane order by a team stage -- bit-identical to the oracle's ordered sum."""
+    n = 8 * keys
+    j = np.random.default_rng(keys).normal(0.0, 1.0, (6, n))
+    out = torch.full((6, 6, keys), float("nan"), dtype=torch.float64, device="cuda")
+    runtime.run(runtime.load(BUNDLES, "gram_block"), j=dev(j), out=out)
+    np.testing.assert_array_equal(host(out), oracle.block_sums(j, j))
+
+
+@pytest.mark.parametrize("keys", [3, 1000])
+def test_gradient_blocks_are_ordered_sums_per_key(keys):
+    n = 8 * keys
+    rng = np.random.default_rng(keys + 1)
+    j, r = rng.normal(0.0, 1.0, (20, n)), rng.normal(0.0, 1.0, n)
+    out = torch.full((20, keys), float("nan"), dtype=torch.float64, device="cuda")
+    runtime.run(runtime.load(BUNDLES, "grad_block"), j=dev(j), r=dev(r), out=out)
+    np.testing.assert_array_equal(host(out), oracle.block_sums(j, r[None, :])[:, 0, :])

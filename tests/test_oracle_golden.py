@@ -262,3 +262,12 @@ def test_key_sums_match_exact_sums():
         seg = x[8 * k:8 * k + 8]
         assert abs(got[k] - math.fsum(seg)) <= 8 * np.finfo(float).eps * math.fsum(np.abs(seg))
     close(oracle.key_share(np.ones(16)), np.full(16, 1 / 8.0))
+
+
+def test_block_sums_match_numpy():
+    rng = np.random.default_rng(11)
+    j = rng.normal(0.0, 1.0, (6, 8 * 50))
+    got = oracle.block_sums(j, j)
+    jj = j.reshape(6, 50, 8)
+    close(got, np.einsum("akr,bkr->abk", jj, jj), rtol=1e-13, atol=1e-13)
+    close(oracle.block_sums(j), jj.sum(axis=2), rtol=1e-13, atol=1e-13)
