@@ -355,6 +355,21 @@ READBACK_KERNELS = {k.name: k for k in (share, standard, centred)}
 
 
 @hawk.kernel
+def sym_eigen(A: Matrix[6, 6], w: Mutable[Vector[6]], V: Mutable[Matrix[6, 6]], info: Mutable[Int32]):
+    vals, vecs, status = m.eigh(A)
+    w = vals
+    V = vecs
+    info = status
+
+
+@hawk.kernel
+def sym_eigvals(A: Matrix[4, 4], w: Mutable[Vector[4]], info: Mutable[Int32]):
+    vals, _vecs, status = m.eigh(A)
+    w = vals
+    info = status
+
+
+@hawk.kernel
 def team_chol_512(A: Matrix[512, 512], b: Vector[512], x: Mutable[Vector[512]], info: Mutable[Int32]):
     f, status = m.cholesky(A)
     x = m.cho_solve(f, b)
@@ -408,4 +423,6 @@ KERNELS = {
     **{name: (k, ("float64",)) for name, k in READBACK_KERNELS.items()},
     **{name: (k, ("float64",)) for name, k in KEYED_KERNELS.items()},
     "share_vjp": (Kernel("share_vjp", vjp(share, wrt=("x",))), ("float64",)),
+    "sym_eigen": (sym_eigen, ("float64",)),
+    "sym_eigvals": (sym_eigvals, ("float64",)),
 }

@@ -318,5 +318,152 @@ HK_FI T luDet(const Lu<T, N>& f) {
     return d;
 }
 
+// ---------------------------------------------------------------- eigh
+
+// Jacobi sweeps for dimension n (the count hawk/ir/linalg.py:82-84 records).
+HK_HD constexpr int eigh_sweeps(int n) { return n <= 2 ? 2 : n <= 4 ? 6 : n <= 8 ? 8 : n <= 16 ? 12 : 15; }
+
+template <class T> struct EighEps;
+template <> struct EighEps<double> { static HK_HD constexpr double value() { return 2.220446049250313e-16; } };
+template <> struct EighEps<float> { static HK_HD constexpr float value() { return 1.1920928955078125e-07f; } };
+
+// w, V, info of the symmetric part of A: eigenvalues ascending, eigenvectors
+// the columns of V (row-major v[i * N + j]), each signed so its first largest
+// component is positive; info bit 1: the off-diagonal mass did not fall below
+// (n eps)^2 of the Frobenius norm, bit 2: two eigenvalues closer than
+// n eps |A|_F.  Cyclic Jacobi, operation for operation the order
+// hawk/embedded/linalg.py:302-399 restates; the loops stay rolled (the
+// matrix lives in the thread's local memory).
+template <class T, int N> struct Eigh {
+    T w[N];
+    T v[N * N];
+    int info;
+};
+template <class T, int N> struct EighValues {
+    T w[N];
+    T v[N * N];
+    int info;
+};
+
+namespace detail {
+template <int N, class T, class F, class A> HK_FI void eigh_into(F& f, const A& a, bool vectors) {
+    const T zero = T(0), one = T(1), half = T(0.5);
+    f.info = 0;
+    if (N == 1) {
+        f.w[0] = static_cast<T>(el(a, 0, 0));
+        f.v[0] = one;
+        return;
+    }
+    const T eps = EighEps<T>::value();
+    T s[N][N];
+    T fro2 = zero;
+#pragma unroll 1
+    for (int i = 0; i < N; ++i)
+#pragma unroll 1
+        for (int c = 0; c < N; ++c) f.v[i * N + c] = zero;
+#pragma unroll 1
+    for (int i = 0; i < N; ++i) {
+#pragma unroll 1
+        for (int j = 0; j < N; ++j) {
+            if (j >= i) s[i][j] = (half * static_cast<T>(el(a, i, j))) + (half * static_cast<T>(el(a, j, i)));
+            else s[i][j] = s[j][i];
+            fro2 = fro2 + (s[i][j] * s[i][j]);
+        }
+        f.v[i * N + i] = one;
+    }
+#pragma unroll 1
+    for (int sweep = 0; sweep < eigh_sweeps(N); ++sweep)
+#pragma unroll 1
+        for (int p = 0; p < N - 1; ++p)
+#pragma unroll 1
+            for (int q = p + 1; q < N; ++q) {
+                const T app = s[p][p], aqq = s[q][q], apq = s[p][q];
+                if (!(math::abs(apq) <= (eps * math::sqrt(math::abs(app * aqq))))) {
+                    const T theta = (aqq - app) / (T(2) * apq);
+                    const T sg = (theta < zero) ? T(-1) : one;
+                    const T tn = sg / (math::abs(theta) + math::sqrt((theta * theta) + one));
+                    const T cs = one / math::sqrt((tn * tn) + one);
+                    const T sn = tn * cs;
+                    s[p][p] = app - (tn * apq);
+                    s[q][q] = aqq + (tn * apq);
+                    s[p][q] = zero;
+                    s[q][p] = zero;
+#pragma unroll 1
+                    for (int k = 0; k < N; ++k) {
+                        if ((k != p) && (k != q)) {
+                            const T akp = s[k][p], akq = s[k][q];
+                            const T np = (cs * akp) - (sn * akq);
+                            const T nq = (sn * akp) + (cs * akq);
+                            s[k][p] = np;
+                            s[p][k] = np;
+                            s[k][q] = nq;
+                            s[q][k] = nq;
+                        }
+                        if (vectors) {
+                            const T vp = f.v[k * N + p], vq = f.v[k * N + q];
+                            f.v[k * N + p] = (cs * vp) - (sn * vq);
+                            f.v[k * N + q] = (sn * vp) + (cs * vq);
+                        }
+                    }
+                }
+            }
+    T off2 = zero;
+#pragma unroll 1
+    for (int i = 0; i < N; ++i) {
+        f.w[i] = s[i][i];
+#pragma unroll 1
+        for (int j = 0; j < N; ++j)
+            if (j != i) off2 = off2 + (s[i][j] * s[i][j]);
+    }
+    const T tol = static_cast<T>(N) * eps;
+    if (!(off2 <= ((tol * tol) * fro2))) f.info = 1;
+#pragma unroll 1
+    for (int i = 0; i < N - 1; ++i) {
+        int lo = i;
+#pragma unroll 1
+        for (int j = i + 1; j < N; ++j)
+            if (f.w[j] < f.w[lo]) lo = j;
+        if (lo != i) {
+            const T tw = f.w[i];
+            f.w[i] = f.w[lo];
+            f.w[lo] = tw;
+#pragma unroll 1
+            for (int k = 0; k < N; ++k) {
+                const T tv = f.v[k * N + i];
+                f.v[k * N + i] = f.v[k * N + lo];
+                f.v[k * N + lo] = tv;
+            }
+        }
+    }
+    if (vectors) {
+#pragma unroll 1
+        for (int j = 0; j < N; ++j) {
+            int big = 0;
+#pragma unroll 1
+            for (int k = 1; k < N; ++k)
+                if (math::abs(f.v[k * N + j]) > math::abs(f.v[big * N + j])) big = k;
+            if (f.v[big * N + j] < zero)
+#pragma unroll 1
+                for (int k = 0; k < N; ++k) f.v[k * N + j] = -f.v[k * N + j];
+        }
+    }
+    const T gap = tol * math::sqrt(fro2);
+    bool tight = false;
+#pragma unroll 1
+    for (int i = 0; i < N - 1; ++i)
+        if (!((f.w[i + 1] - f.w[i]) > gap)) tight = true;
+    if (tight) f.info = f.info + 2;
+}
+}  // namespace detail
+
+template <int N, class T, class A> HK_FI void eigh(Eigh<T, N>& f, const A& a) {
+    detail::eigh_into<N, T>(f, a, true);
+}
+
+// The eigenvalues only (V is not accumulated; w and info as eigh's).
+template <int N, class T, class A> HK_FI void eighValues(EighValues<T, N>& f, const A& a) {
+    detail::eigh_into<N, T>(f, a, false);
+}
+
 }  // namespace linalg
 }  // namespace hk

@@ -93,6 +93,7 @@ _SIGS = {
     "hko_oscillator": (ctypes.c_uint32, [_P, _P, _P, _P, _P, _P, _P, _D, _I, _I, _I]),
     "hko_orbit": (ctypes.c_uint32, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I]),
     "hko_rows_f64": (None, [ctypes.c_int, _P, _I, _P, _P]),
+    "hko_sym_eigen": (None, [ctypes.c_int, _P, _I, _P, _P, _P, _I, _I]),
     "hko_team_chol": (None, [ctypes.c_int, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I]),
     "hko_team_lu": (None, [ctypes.c_int, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I]),
     "hko_team_chol_from": (None, [ctypes.c_int, _P, _P, _I, _P, _P, _P, _I, _I]),
@@ -455,3 +456,14 @@ def block_sums(u, v=None, rows: int = 8):
     for r in range(rows):
         s = s + (uu[:, None, :, r] * vv[None, :, :, r])
     return s
+
+
+def sym_eigen(A, vectors: bool = True, threads: int = 1):
+    """(w, V, info) of eigh(A) per sample (V None for the values-only kernel)."""
+    k, n = A.shape[0], A.shape[-1]
+    w = np.empty((k, n))
+    V = np.empty((k, k, n)) if vectors else None
+    info = np.empty(n, dtype=np.int32)
+    parallel(lambda b, c: lib().hko_sym_eigen(k, _p(A), n, _p(w), _p(V) if V is not None else None, _p(info), b, c),
+             n, threads)
+    return w, V, info

@@ -646,6 +646,117 @@ void hko_team_chol_from(int n, const double* A, const double* b, int64_t pitch, 
     free(y);
 }
 
+/* ---------------------------------------------- symmetric eigenproblem (any n) */
+
+static int eigh_sweeps(int n) { return n <= 2 ? 2 : n <= 4 ? 6 : n <= 8 ? 8 : n <= 16 ? 12 : 15; }
+
+/* Cyclic Jacobi on the symmetric part, hawk/embedded/linalg.py:302-399:
+ * w ascending, V's columns the eigenvectors (first largest component
+ * positive), info bit 1 / bit 2 as restated there. */
+static int eigh_n(int n, const double* a, double* w, double* v) {
+    const double eps = 2.220446049250313e-16;
+    int info = 0;
+    if (n == 1) {
+        w[0] = a[0];
+        v[0] = 1.0;
+        return 0;
+    }
+    double* s = malloc(sizeof(double) * (size_t)n * (size_t)n);
+    double fro2 = 0.0;
+    for (int e = 0; e < n * n; ++e) v[e] = 0.0;
+    for (int i = 0; i < n; ++i) {
+        for (int j = 0; j < n; ++j) {
+            if (j >= i) s[i * n + j] = (0.5 * a[i * n + j]) + (0.5 * a[j * n + i]);
+            else s[i * n + j] = s[j * n + i];
+            fro2 = fro2 + (s[i * n + j] * s[i * n + j]);
+        }
+        v[i * n + i] = 1.0;
+    }
+    for (int sweep = 0; sweep < eigh_sweeps(n); ++sweep)
+        for (int p = 0; p < n - 1; ++p)
+            for (int q = p + 1; q < n; ++q) {
+                const double app = s[p * n + p], aqq = s[q * n + q], apq = s[p * n + q];
+                if (!(fabs(apq) <= (eps * sqrt(fabs(app * aqq))))) {
+                    const double theta = (aqq - app) / (2.0 * apq);
+                    const double sg = (theta < 0.0) ? -1.0 : 1.0;
+                    const double tn = sg / (fabs(theta) + sqrt((theta * theta) + 1.0));
+                    const double cs = 1.0 / sqrt((tn * tn) + 1.0);
+                    const double sn = tn * cs;
+                    s[p * n + p] = app - (tn * apq);
+                    s[q * n + q] = aqq + (tn * apq);
+                    s[p * n + q] = 0.0;
+                    s[q * n + p] = 0.0;
+                    for (int k = 0; k < n; ++k) {
+                        if ((k != p) && (k != q)) {
+                            const double akp = s[k * n + p], akq = s[k * n + q];
+                            const double np = (cs * akp) - (sn * akq);
+                            const double nq = (sn * akp) + (cs * akq);
+                            s[k * n + p] = np;
+                            s[p * n + k] = np;
+                            s[k * n + q] = nq;
+                            s[q * n + k] = nq;
+                        }
+                        const double vp = v[k * n + p], vq = v[k * n + q];
+                        v[k * n + p] = (cs * vp) - (sn * vq);
+                        v[k * n + q] = (sn * vp) + (cs * vq);
+                    }
+                }
+            }
+    double off2 = 0.0;
+    for (int i = 0; i < n; ++i) {
+        w[i] = s[i * n + i];
+        for (int j = 0; j < n; ++j)
+            if (j != i) off2 = off2 + (s[i * n + j] * s[i * n + j]);
+    }
+    const double tol = (double)n * eps;
+    if (!(off2 <= ((tol * tol) * fro2))) info = 1;
+    for (int i = 0; i < n - 1; ++i) {
+        int lo = i;
+        for (int j = i + 1; j < n; ++j)
+            if (w[j] < w[lo]) lo = j;
+        if (lo != i) {
+            const double tw = w[i];
+            w[i] = w[lo];
+            w[lo] = tw;
+            for (int k = 0; k < n; ++k) {
+                const double tv = v[k * n + i];
+                v[k * n + i] = v[k * n + lo];
+                v[k * n + lo] = tv;
+            }
+        }
+    }
+    for (int j = 0; j < n; ++j) {
+        int big = 0;
+        for (int k = 1; k < n; ++k)
+            if (fabs(v[k * n + j]) > fabs(v[big * n + j])) big = k;
+        if (v[big * n + j] < 0.0)
+            for (int k = 0; k < n; ++k) v[k * n + j] = -v[k * n + j];
+    }
+    const double gap = tol * sqrt(fro2);
+    int tight = 0;
+    for (int i = 0; i < n - 1; ++i)
+        if (!((w[i + 1] - w[i]) > gap)) tight = 1;
+    if (tight) info = info + 2;
+    free(s);
+    return info;
+}
+
+void hko_sym_eigen(int n, const double* A, int64_t pitch, double* w, double* V, int32_t* info, int64_t base,
+                   int64_t count) {
+    double* a = malloc(sizeof(double) * (size_t)n * (size_t)n);
+    double* vv = malloc(sizeof(double) * (size_t)n * (size_t)n);
+    double* ww = malloc(sizeof(double) * (size_t)n);
+    for (int64_t i = base; i < base + count; ++i) {
+        load_nxm(A, pitch, i, n, n, a);
+        info[i] = eigh_n(n, a, ww, vv);
+        store_nxm(w, pitch, i, n, 1, ww);
+        if (V) store_nxm(V, pitch, i, n, n, vv);
+    }
+    free(a);
+    free(vv);
+    free(ww);
+}
+
 /* ---------------------------------------------------------------- c5 Kepler */
 
 /*

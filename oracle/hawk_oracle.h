@@ -112,6 +112,12 @@ void hko_team_lu(int n, const double* A, const double* b, const double* B, int64
 void hko_team_chol_from(int n, const double* A, const double* b, int64_t pitch, double* x, double* L,
                         int32_t* info, int64_t base, int64_t count);
 
+/* w, V, info = eigh(A) per sample (A (n, n, pitch), w (n, pitch), V (n, n, pitch)
+ * or null for the values-only kernel): cyclic Jacobi in the order of
+ * hawk/embedded/linalg.py:302-399. */
+void hko_sym_eigen(int n, const double* A, int64_t pitch, double* w, double* V, int32_t* info, int64_t base,
+                   int64_t count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,6 +13,7 @@ fixtures it writes are committed and are all the test suite reads.
 
     python tests/golden/make_golden.py          # every fixture
     python tests/golden/make_golden.py team     # the team-form fixtures only
+    python tests/golden/make_golden.py eigen    # the symmetric-eigenproblem fixtures only
 """
 
 from __future__ import annotations
@@ -63,8 +64,40 @@ def team_fixtures(evaluate) -> None:
     np.savez(HERE / "team.npz", **out)
 
 
+def eigen_fixtures(evaluate) -> None:
+    """eigen.npz: symmetric 6 x 6 matrices (lane 2: a repeated eigenvalue) and
+    the interpreter's eigh (numpy's, signed so each vector's largest component
+    is positive)."""
+    from hawk_b200 import configs
+
+    rng = np.random.default_rng(SEED)
+    lanes, n = 6, 6
+    mats = []
+    for lane in range(lanes):
+        g = rng.standard_normal((n, n))
+        a = (g + g.T) / 2
+        if lane == 2:
+            q, _ = np.linalg.qr(rng.standard_normal((n, n)))
+            a = (q * np.r_[np.ones(n // 2), np.linspace(2, 3, n - n // 2)]) @ q.T
+        mats.append(a)
+    A = np.ascontiguousarray(np.moveaxis(np.stack(mats), 0, -1))
+    outs = {"w": [], "V": [], "info": []}
+    for i in range(lanes):
+        res = evaluate(configs.sym_eigen.sinks, {"A": A[..., i]})
+        for k in outs:
+            outs[k].append(np.asarray(res[k], dtype=np.int32 if k == "info" else float))
+    np.savez(HERE / "eigen.npz", A=A, **{k: np.stack(v, axis=-1) for k, v in outs.items()})
+
+
 def main() -> int:
     from hawk_b200 import frontend, workloads
+
+    if sys.argv[1:] == ["eigen"]:
+        hawk = frontend.load()
+        sys.path.insert(0, str(Path(hawk.__file__).resolve().parent.parent / "tests"))
+        from _eval import evaluate
+        eigen_fixtures(evaluate)
+        return 0
 
     if sys.argv[1:] == ["team"]:
         hawk = frontend.load()
@@ -182,6 +215,7 @@ def main() -> int:
             steps[f"orb_w{word}_{k}"] = got[k]
     np.savez(HERE / "steps.npz", **steps)
     team_fixtures(evaluate)
+    eigen_fixtures(evaluate)
     _ = Kernel, jvp
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)

@@ -271,3 +271,24 @@ def test_block_sums_match_numpy():
     jj = j.reshape(6, 50, 8)
     close(got, np.einsum("akr,bkr->abk", jj, jj), rtol=1e-13, atol=1e-13)
     close(oracle.block_sums(j), jj.sum(axis=2), rtol=1e-13, atol=1e-13)
+
+
+def test_eigh_golden(golden):
+    """Cyclic Jacobi (the oracle) against numpy's eigh through the reference
+    interpreter: the status exactly (bit 2 marks the repeated eigenvalue), the
+    values and vectors within the reference's tests/test_team_linalg.py bounds
+    (100 n eps |A| n), the vectors orthonormal and signed alike."""
+    g = golden("eigen")
+    w, V, info = oracle.sym_eigen(g["A"])
+    np.testing.assert_array_equal(info & 2, g["info"] & 2)
+    assert (info & 1 == 0).all() and info[2] & 2
+    n = g["A"].shape[0]
+    for lane in range(g["A"].shape[-1]):
+        s = g["A"][..., lane]
+        tol = 100 * n * EPS * np.abs(s).max() * n
+        np.testing.assert_allclose(w[:, lane], g["w"][:, lane], rtol=0, atol=tol)
+        v = V[..., lane]
+        np.testing.assert_allclose(s @ v, v * w[:, lane], rtol=0, atol=tol)
+        np.testing.assert_allclose(v.T @ v, np.eye(n), rtol=0, atol=100 * n * EPS)
+        if lane != 2:           # a repeated eigenvalue's vectors are any basis of its space
+            np.testing.assert_allclose(v, g["V"][..., lane], rtol=0, atol=1e-9)
