@@ -370,6 +370,21 @@ def sym_eigvals(A: Matrix[4, 4], w: Mutable[Vector[4]], info: Mutable[Int32]):
 
 
 @hawk.kernel
+def team_eigh_40(A: Matrix[40, 40], w: Mutable[Vector[40]], V: Mutable[Matrix[40, 40]], info: Mutable[Int32]):
+    vals, vecs, status = m.eigh(A)
+    w = vals
+    V = vecs
+    info = status
+
+
+@hawk.kernel
+def team_lstsq_40(J: Matrix[80, 40], r: Vector[80], x: Mutable[Vector[40]], info: Mutable[Int32]):
+    sol, status = m.lstsq(J, r)
+    x = sol
+    info = status
+
+
+@hawk.kernel
 def team_chol_512(A: Matrix[512, 512], b: Vector[512], x: Mutable[Vector[512]], info: Mutable[Int32]):
     f, status = m.cholesky(A)
     x = m.cho_solve(f, b)
@@ -393,7 +408,8 @@ def team_lu_160(A: Matrix[160, 160], b: Vector[160], x: Mutable[Vector[160]], de
 #: matrix does not fit a block's shared memory and the team works it in place
 #: in its scratch plane.
 TEAM_KERNELS = {k.name: k for k in (team_chol_33, team_lu_33, team_chol_64, team_lu_64, team_chol_128,
-                                    team_lu_128, team_chol_from_64, team_chol_512, team_lu_160)}
+                                    team_lu_128, team_chol_from_64, team_chol_512, team_lu_160, team_eigh_40,
+                                    team_lstsq_40)}
 
 
 #: Every kernel the bundles hold, by name, with the scalar modes each is built in.

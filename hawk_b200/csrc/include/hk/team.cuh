@@ -615,6 +615,251 @@ HK_FI void luInverse(const Team& tm, const TeamLu<T, N>& f, T* x) {
     luSolve<N>(tm, f, x, x, N);
 }
 
+// ----------------------------------------------------- symmetric eigenproblem
+
+template <class T, int N> struct TeamEigh {
+    T* w;
+    T* v;
+    T* work;
+    std::int32_t* info;
+};
+
+// w, V, info of the symmetric part of `a` (n x n, row-major): the one-thread
+// form's cyclic Jacobi (hk/linalg.cuh eigh, hawk/embedded/linalg.py:302-399)
+// with each rotation's row and column updates spread over the team (every k
+// gets the one-thread form's operations), the rotation's own scalars made by
+// every thread alike, and the epilogue (ordering, signs, status) by one thread:
+// the one-thread form's bits.  The working matrix is staged in the team's
+// shared memory when it fits, else kept in `work` (n^2 + 4).
+template <int N, class T>
+HK_FI void eigh(const Team& tm, const TeamEigh<T, N>& f, T* a) {
+    const T zero = T(0), one = T(1), half = T(0.5);
+    const T eps = linalg::EighEps<T>::value();
+    T* s = (tm.bytes >= kScratchBytes + sizeof(T) * N * N) ? reinterpret_cast<T*>(tm.smem + kScratchBytes) : f.work;
+    if (tm.bytes >= kScratchBytes) {
+        tm.sync();
+        detail::set_tag(tm, static_cast<const T*>(nullptr));
+    }
+    for (int e = tm.rank; e < N * N; e += tm.size) {
+        const int i = e / N, j = e % N;
+        s[e] = (j >= i) ? (half * a[i * N + j]) + (half * a[j * N + i]) : T(0);
+        f.v[e] = (i == j) ? one : zero;
+    }
+    tm.sync();
+    T fro2 = zero;
+    if (N == 1) {
+        if (tm.rank == 0) {
+            f.w[0] = a[0];
+            *f.info = 0;
+        }
+        tm.sync();
+        return;
+    }
+    // the lower half mirrors the upper (what the one-thread fill copies), and
+    // the Frobenius sum in the fill's order: one thread
+    if (tm.rank == 0) {
+        for (int i = 0; i < N; ++i)
+            for (int j = 0; j < N; ++j) {
+                if (j < i) s[i * N + j] = s[j * N + i];
+                fro2 = fro2 + (s[i * N + j] * s[i * N + j]);
+            }
+    }
+    tm.sync();
+    for (int sweep = 0; sweep < linalg::eigh_sweeps(N); ++sweep)
+        for (int p = 0; p < N - 1; ++p)
+            for (int q = p + 1; q < N; ++q) {
+                const T app = s[p * N + p], aqq = s[q * N + q], apq = s[p * N + q];
+                tm.sync();              // every thread has read the pivot block before it changes
+                if (!(math::abs(apq) <= (eps * math::sqrt(math::abs(app * aqq))))) {
+                    const T theta = (aqq - app) / (T(2) * apq);
+                    const T sg = (theta < zero) ? T(-1) : one;
+                    const T tn = sg / (math::abs(theta) + math::sqrt((theta * theta) + one));
+                    const T cs = one / math::sqrt((tn * tn) + one);
+                    const T sn = tn * cs;
+                    if (tm.rank == 0) {
+                        s[p * N + p] = app - (tn * apq);
+                        s[q * N + q] = aqq + (tn * apq);
+                        s[p * N + q] = zero;
+                        s[q * N + p] = zero;
+                    }
+                    for (int k = tm.rank; k < N; k += tm.size) {
+                        if ((k != p) && (k != q)) {
+                            const T akp = s[k * N + p], akq = s[k * N + q];
+                            const T np = (cs * akp) - (sn * akq);
+                            const T nq = (sn * akp) + (cs * akq);
+                            s[k * N + p] = np;
+                            s[p * N + k] = np;
+                            s[k * N + q] = nq;
+                            s[q * N + k] = nq;
+                        }
+                        const T vp = f.v[k * N + p], vq = f.v[k * N + q];
+                        f.v[k * N + p] = (cs * vp) - (sn * vq);
+                        f.v[k * N + q] = (sn * vp) + (cs * vq);
+                    }
+                }
+                tm.sync();
+            }
+    if (tm.rank == 0) {
+        int info = 0;
+        T off2 = zero;
+        for (int i = 0; i < N; ++i) {
+            f.w[i] = s[i * N + i];
+            for (int j = 0; j < N; ++j)
+                if (j != i) off2 = off2 + (s[i * N + j] * s[i * N + j]);
+        }
+        const T tol = static_cast<T>(N) * eps;
+        if (!(off2 <= ((tol * tol) * fro2))) info = 1;
+        for (int i = 0; i < N - 1; ++i) {
+            int lo = i;
+            for (int j = i + 1; j < N; ++j)
+                if (f.w[j] < f.w[lo]) lo = j;
+            if (lo != i) {
+                const T tw = f.w[i];
+                f.w[i] = f.w[lo];
+                f.w[lo] = tw;
+                for (int k = 0; k < N; ++k) {
+                    const T tv = f.v[k * N + i];
+                    f.v[k * N + i] = f.v[k * N + lo];
+                    f.v[k * N + lo] = tv;
+                }
+            }
+        }
+        for (int j = 0; j < N; ++j) {
+            int big = 0;
+            for (int k = 1; k < N; ++k)
+                if (math::abs(f.v[k * N + j]) > math::abs(f.v[big * N + j])) big = k;
+            if (f.v[big * N + j] < zero)
+                for (int k = 0; k < N; ++k) f.v[k * N + j] = -f.v[k * N + j];
+        }
+        const T gap = tol * math::sqrt(fro2);
+        bool tight = false;
+        for (int i = 0; i < N - 1; ++i)
+            if (!((f.w[i + 1] - f.w[i]) > gap)) tight = true;
+        *f.info = tight ? info + 2 : info;
+    }
+    tm.sync();
+}
+
+// ------------------------------------------------------ QR least squares
+
+template <class T, int N> struct TeamQr {
+    T* a;
+    T* tau;
+    T* work;
+    std::int32_t* info;
+};
+
+// Householder QR of the m x n matrix `a` (row-major, m >= n) in place: for
+// column j, the sum of squares of a_ij, i >= j (ascending i, one thread),
+// its root `norm`, R_jj = alpha = -sign(a_jj) norm (sign(0) = +1), the
+// reflector v = (a_jj - alpha, a_{j+1..m-1, j}) kept below the diagonal with
+// v_0 in work[j] and tau_j = 2 / v.v; each later column c (one thread per
+// column) takes d = v_0 a_jc + sum_{i>j} a_ij a_ic (ascending i), t = tau_j d,
+// a_jc -= t v_0, a_ic -= t a_ij.  info = first column whose R diagonal is
+// exactly zero (1-based), its reflector the identity.  The reference's own
+// team-form QR is absent (aether-dsc); this order is the b200 build's, pinned
+// by the oracle's restatement and against numpy's least squares.
+template <int N, class T>
+HK_FI void qr(const Team& tm, const TeamQr<T, N>& f, T* a, int m) {
+    int info = 0;
+    for (int j = 0; j < N; ++j) {
+        T norm2 = T(0);
+        for (int i = j; i < m; ++i) norm2 = norm2 + (a[i * N + j] * a[i * N + j]);
+        const T ajj = a[j * N + j];
+        tm.sync();                  // every thread has read the column before it changes
+        if (!(norm2 > T(0))) {
+            if (info == 0) info = j + 1;
+            if (tm.rank == 0) {
+                f.tau[j] = T(0);
+                f.work[j] = T(0);
+            }
+            tm.sync();
+            continue;
+        }
+        const T norm = math::sqrt(norm2);
+        const T alpha = (ajj >= T(0)) ? -norm : norm;
+        const T v0 = ajj - alpha;
+        T vtv = v0 * v0;
+        for (int i = j + 1; i < m; ++i) vtv = vtv + (a[i * N + j] * a[i * N + j]);
+        const T tj = T(2) / vtv;
+        for (int c = j + 1 + tm.rank; c < N; c += tm.size) {
+            T d = v0 * a[j * N + c];
+            for (int i = j + 1; i < m; ++i) d = d + (a[i * N + j] * a[i * N + c]);
+            const T t = tj * d;
+            a[j * N + c] = a[j * N + c] - (t * v0);
+            for (int i = j + 1; i < m; ++i) a[i * N + c] = a[i * N + c] - (t * a[i * N + j]);
+        }
+        tm.sync();
+        if (tm.rank == 0) {
+            a[j * N + j] = alpha;
+            f.tau[j] = tj;
+            f.work[j] = v0;
+        }
+        tm.sync();
+    }
+    if (tm.rank == 0) *f.info = info;
+    tm.sync();
+}
+
+// x = argmin |J x - r| from the factor (k right-hand sides, r m x k, x n x k,
+// row-major): Q^T r by the reflectors in order, worked in place on r (the
+// stage's own copy of it), then R x = (Q^T r)[0:n] backward, each row's dot
+// product in ascending j; one thread per right-hand side; zeros for a
+// rank-deficient factor.
+template <int N, class T>
+HK_FI void qrSolve(const Team& tm, const TeamQr<T, N>& f, int m, T* r, T* x, int k) {
+    if (*f.info != 0) {
+        for (int e = tm.rank; e < N * k; e += tm.size) x[e] = T(0);
+        tm.sync();
+        return;
+    }
+    const T* a = f.a;
+    for (int c = tm.rank; c < k; c += tm.size) {
+        for (int j = 0; j < N; ++j) {
+            const T tj = f.tau[j], v0 = f.work[j];
+            T d = v0 * r[j * k + c];
+            for (int i = j + 1; i < m; ++i) d = d + (a[i * N + j] * r[i * k + c]);
+            const T t = tj * d;
+            r[j * k + c] = r[j * k + c] - (t * v0);
+            for (int i = j + 1; i < m; ++i) r[i * k + c] = r[i * k + c] - (t * a[i * N + j]);
+        }
+        for (int q = 0; q < N; ++q) {
+            const int i = N - 1 - q;
+            T acc = r[i * k + c];
+            for (int jj = i + 1; jj < N; ++jj) acc = acc - (a[i * N + jj] * x[jj * k + c]);
+            x[i * k + c] = acc / a[i * N + i];
+        }
+    }
+    tm.sync();
+}
+
+// x = (J^T J)^{-1} b from R (n x n upper triangle of the factor): R^T z = b
+// forward, R x = z backward (ascending j in each dot product), in place when
+// b == x; one thread per right-hand side; zeros for a rank-deficient factor.
+template <int N, class T>
+HK_FI void qrGramSolve(const Team& tm, const TeamQr<T, N>& f, const T* b, T* x, int k) {
+    if (*f.info != 0) {
+        for (int e = tm.rank; e < N * k; e += tm.size) x[e] = T(0);
+        tm.sync();
+        return;
+    }
+    const T* a = f.a;
+    for (int c = tm.rank; c < k; c += tm.size) {
+        for (int i = 0; i < N; ++i) {
+            T acc = b[i * k + c];
+            for (int jj = 0; jj < i; ++jj) acc = acc - (a[jj * N + i] * x[jj * k + c]);
+            x[i * k + c] = acc / a[i * N + i];
+        }
+        for (int q = 0; q < N; ++q) {
+            const int i = N - 1 - q;
+            T acc = x[i * k + c];
+            for (int jj = i + 1; jj < N; ++jj) acc = acc - (a[i * N + jj] * x[jj * k + c]);
+            x[i * k + c] = acc / a[i * N + i];
+        }
+    }
+    tm.sync();
+}
+
 // ------------------------------------------------------------ block sums
 
 // The block of one key (a BlockSum, hawk/ir/team.py:544-600): entry (a, b) is

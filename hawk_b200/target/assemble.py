@@ -36,6 +36,7 @@ _UNBUILT = {
     "hk::geometry::": "ray primitives",
     "hk::banded::": "the banded scalar mode",
     "hk::random::": "in-kernel random draws",
+    "hk::linalg::warp::": "the warp-form eigensolver (eighValues of n <= 32 under the team form)",
     "hawk_abi::mix_count": "auto dispatch branch counts",
     "hawk_abi::tiled": "wide (tiled) scratch planes",
     "hawk_abi::warp_sum": "warp-per-lane sums",
@@ -45,7 +46,8 @@ _UNBUILT = {
 
 #: The team-form calls the device library builds (hk/team.cuh).
 TEAM_BUILT = frozenset({"Team", "TeamCholesky", "TeamLu", "cholesky", "choleskyFrom", "choSolve", "triLower",
-                        "triUpperT", "lu", "luSolve", "luSolveT", "luInverse", "luDet", "blockSum"})
+                        "triUpperT", "lu", "luSolve", "luSolveT", "luInverse", "luDet", "blockSum",
+                        "TeamEigh", "eigh", "TeamQr", "qr", "qrSolve", "qrGramSolve"})
 _TEAM_NAME = re.compile(r"hk::linalg::team::(\w+)")
 
 

@@ -93,6 +93,7 @@ _SIGS = {
     "hko_oscillator": (ctypes.c_uint32, [_P, _P, _P, _P, _P, _P, _P, _D, _I, _I, _I]),
     "hko_orbit": (ctypes.c_uint32, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I]),
     "hko_rows_f64": (None, [ctypes.c_int, _P, _I, _P, _P]),
+    "hko_lstsq_qr": (None, [ctypes.c_int, ctypes.c_int, _P, _P, _I, _P, _P, _I, _I]),
     "hko_sym_eigen": (None, [ctypes.c_int, _P, _I, _P, _P, _P, _I, _I]),
     "hko_team_chol": (None, [ctypes.c_int, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I]),
     "hko_team_lu": (None, [ctypes.c_int, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I]),
@@ -467,3 +468,12 @@ def sym_eigen(A, vectors: bool = True, threads: int = 1):
     parallel(lambda b, c: lib().hko_sym_eigen(k, _p(A), n, _p(w), _p(V) if V is not None else None, _p(info), b, c),
              n, threads)
     return w, V, info
+
+
+def lstsq_qr(J, r, threads: int = 1):
+    """(x, info) of lstsq(J, r) per sample by the team-form Householder QR."""
+    m, n, lanes = J.shape
+    x = np.empty((n, lanes))
+    info = np.empty(lanes, dtype=np.int32)
+    parallel(lambda b, c: lib().hko_lstsq_qr(m, n, _p(J), _p(r), lanes, _p(x), _p(info), b, c), lanes, threads)
+    return x, info

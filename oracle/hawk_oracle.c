@@ -757,6 +757,81 @@ void hko_sym_eigen(int n, const double* A, int64_t pitch, double* w, double* V, 
     free(ww);
 }
 
+/* ------------------------------------------------- QR least squares (n > 32) */
+
+/* The b200 team-form Householder QR and its solve, restated (hk/team.cuh qr,
+ * qrSolve): the reference's own team QR (aether-dsc) is absent, so this order
+ * is the build's; the tests pin it against numpy's least squares. */
+static int qr_n(int m, int n, double* a, double* tau, double* v0s) {
+    int info = 0;
+    for (int j = 0; j < n; ++j) {
+        double norm2 = 0.0;
+        for (int i = j; i < m; ++i) norm2 = norm2 + (a[i * n + j] * a[i * n + j]);
+        const double ajj = a[j * n + j];
+        if (!(norm2 > 0.0)) {
+            if (info == 0) info = j + 1;
+            tau[j] = 0.0;
+            v0s[j] = 0.0;
+            continue;
+        }
+        const double norm = sqrt(norm2);
+        const double alpha = (ajj >= 0.0) ? -norm : norm;
+        const double v0 = ajj - alpha;
+        double vtv = v0 * v0;
+        for (int i = j + 1; i < m; ++i) vtv = vtv + (a[i * n + j] * a[i * n + j]);
+        const double tj = 2.0 / vtv;
+        for (int c = j + 1; c < n; ++c) {
+            double d = v0 * a[j * n + c];
+            for (int i = j + 1; i < m; ++i) d = d + (a[i * n + j] * a[i * n + c]);
+            const double t = tj * d;
+            a[j * n + c] = a[j * n + c] - (t * v0);
+            for (int i = j + 1; i < m; ++i) a[i * n + c] = a[i * n + c] - (t * a[i * n + j]);
+        }
+        a[j * n + j] = alpha;
+        tau[j] = tj;
+        v0s[j] = v0;
+    }
+    return info;
+}
+
+void hko_lstsq_qr(int m, int n, const double* J, const double* r, int64_t pitch, double* x, int32_t* info,
+                  int64_t base, int64_t count) {
+    double* a = malloc(sizeof(double) * (size_t)m * (size_t)n);
+    double* y = malloc(sizeof(double) * (size_t)m);
+    double* tau = malloc(sizeof(double) * (size_t)n);
+    double* v0 = malloc(sizeof(double) * (size_t)n);
+    double* xx = malloc(sizeof(double) * (size_t)n);
+    for (int64_t s = base; s < base + count; ++s) {
+        load_nxm(J, pitch, s, m, n, a);
+        load_nxm(r, pitch, s, m, 1, y);
+        const int inf = qr_n(m, n, a, tau, v0);
+        if (inf != 0) {
+            for (int i = 0; i < n; ++i) xx[i] = 0.0;
+        } else {
+            for (int j = 0; j < n; ++j) {
+                double d = v0[j] * y[j];
+                for (int i = j + 1; i < m; ++i) d = d + (a[i * n + j] * y[i]);
+                const double t = tau[j] * d;
+                y[j] = y[j] - (t * v0[j]);
+                for (int i = j + 1; i < m; ++i) y[i] = y[i] - (t * a[i * n + j]);
+            }
+            for (int q = 0; q < n; ++q) {
+                const int i = n - 1 - q;
+                double acc = y[i];
+                for (int jj = i + 1; jj < n; ++jj) acc = acc - (a[i * n + jj] * xx[jj]);
+                xx[i] = acc / a[i * n + i];
+            }
+        }
+        store_nxm(x, pitch, s, n, 1, xx);
+        info[s] = inf;
+    }
+    free(a);
+    free(y);
+    free(tau);
+    free(v0);
+    free(xx);
+}
+
 /* ---------------------------------------------------------------- c5 Kepler */
 
 /*

@@ -118,6 +118,11 @@ void hko_team_chol_from(int n, const double* A, const double* b, int64_t pitch, 
 void hko_sym_eigen(int n, const double* A, int64_t pitch, double* w, double* V, int32_t* info, int64_t base,
                    int64_t count);
 
+/* x, info = lstsq(J, r) per sample for n > 32 (J (m, n, pitch), r (m, pitch),
+ * x (n, pitch)): the b200 team-form Householder QR and its solve. */
+void hko_lstsq_qr(int m, int n, const double* J, const double* r, int64_t pitch, double* x, int32_t* info,
+                  int64_t base, int64_t count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,4 +1,4 @@
-"""Team-form linear algebra on the B200: one matrix per lane, a block per matrix.
+"""Team-form linear algebra on the B200: one matrix per lane, a warp per matrix.
 
 Kernels whose factorisation is above the one-thread cap of 32 run as the
 reference's stages (hawk/ir/team.py): a copy stage into runtime-owned scratch,
@@ -8,9 +8,12 @@ compared with the CPU oracle (that order, for any n) bit for bit; the oracle is
 pinned against the reference interpreter's LAPACK results by
 tests/test_oracle_golden.py.  Failing lanes (a non-positive leading minor, a
 singular matrix, a zero diagonal) report the same status and zero solutions.
-Sizes: 33, 64, 128 staged through shared memory; 160 (LU) and 512 (Cholesky)
-worked in place in the scratch planes.  The tolerance the north star states
-(1e-12 relative) is asserted beside the exact comparison.
+Sizes: 33 and 64 staged through shared memory; 128, 160 (LU) and 512
+(Cholesky) worked in place in the scratch planes.  The symmetric eigensolver
+at 40 is the one-thread form's Jacobi spread over the team; least squares
+with 40 unknowns is the build's Householder QR (the reference's team QR is
+absent), pinned by the oracle's restatement and numpy.  The tolerance the
+north star states (1e-12 relative) is asserted beside the exact comparison.
 """
 
 from __future__ import annotations
@@ -160,3 +163,58 @@ def test_two_runs_in_a_row_and_a_single_lane():
         _exact(got["x"], x)
         _exact(got["L"], L)
         np.testing.assert_array_equal(got["info"], info)
+
+
+def test_team_eigh_is_the_one_thread_order_bit_for_bit():
+    """eigh at n = 40 (a team stage): the one-thread form's cyclic Jacobi with
+    each rotation's updates spread over the team -- the oracle's bits, the
+    repeated eigenvalue of lane 2 reported in bit 2."""
+    n, lanes = 40, 7
+    rng = np.random.default_rng(40)
+    mats = []
+    for lane in range(lanes):
+        g = rng.standard_normal((n, n))
+        a = (g + g.T) / 2
+        if lane == 2:
+            q, _ = np.linalg.qr(rng.standard_normal((n, n)))
+            a = (q * np.r_[np.ones(n // 2), np.linspace(2, 3, n - n // 2)]) @ q.T
+        mats.append(a)
+    A = np.ascontiguousarray(np.moveaxis(np.stack(mats), 0, -1))
+    k = runtime.load(BUNDLES, "team_eigh_40")
+    out = {"w": nan((n, lanes)), "V": nan((n, n, lanes)), "info": nan(lanes, torch.int32)}
+    runtime.run(k, A=dev(A), **out)
+    got = {key: host(v) for key, v in out.items()}
+    w, V, info = oracle.sym_eigen(A)
+    np.testing.assert_array_equal(got["info"], info)
+    _exact(got["w"], w)
+    _exact(got["V"], V)
+    assert info[2] & 2
+    for lane in (0, 1, 3):
+        np.testing.assert_allclose(got["w"][:, lane], np.linalg.eigvalsh(mats[lane]), rtol=0,
+                                   atol=100 * n * EPS * np.abs(mats[lane]).max() * n)
+
+
+def test_team_lstsq_by_householder_qr():
+    """lstsq(J, r) with 40 unknowns (80 x 40 J): the team-form Householder QR
+    and its solve -- the oracle's bits; a zero column reports info 2 (the first
+    zero diagonal of R) and a zero solution; the rest within the reference's
+    bound of numpy's least squares (50 n eps cond |x|)."""
+    m_rows, n, lanes = 80, 40, 5
+    rng = np.random.default_rng(80)
+    J = rng.standard_normal((lanes, m_rows, n))
+    r = rng.standard_normal((lanes, m_rows))
+    J[2, :, 1] = 0.0
+    Jp = np.ascontiguousarray(np.moveaxis(J, 0, -1))
+    rp = np.ascontiguousarray(r.T)
+    k = runtime.load(BUNDLES, "team_lstsq_40")
+    out = {"x": nan((n, lanes)), "info": nan(lanes, torch.int32)}
+    runtime.run(k, J=dev(Jp), r=dev(rp), **out)
+    got = {key: host(v) for key, v in out.items()}
+    x, info = oracle.lstsq_qr(Jp, rp)
+    np.testing.assert_array_equal(got["info"], info)
+    _exact(got["x"], x)
+    assert info[2] == 2 and not np.any(got["x"][:, 2])
+    for lane in (0, 1, 3, 4):
+        want = np.linalg.lstsq(J[lane], r[lane], rcond=None)[0]
+        cond = np.linalg.cond(J[lane])
+        assert np.abs(got["x"][:, lane] - want).max() <= 50 * n * EPS * cond * np.abs(want).max()

@@ -292,3 +292,15 @@ def test_eigh_golden(golden):
         np.testing.assert_allclose(v.T @ v, np.eye(n), rtol=0, atol=100 * n * EPS)
         if lane != 2:           # a repeated eigenvalue's vectors are any basis of its space
             np.testing.assert_allclose(v, g["V"][..., lane], rtol=0, atol=1e-9)
+
+
+def test_lstsq_qr_matches_numpy():
+    rng = np.random.default_rng(5)
+    J = rng.standard_normal((80, 40, 3))
+    r = rng.standard_normal((80, 3))
+    x, info = oracle.lstsq_qr(np.ascontiguousarray(J), np.ascontiguousarray(r))
+    assert (info == 0).all()
+    for lane in range(3):
+        want = np.linalg.lstsq(J[..., lane], r[:, lane], rcond=None)[0]
+        cond = np.linalg.cond(J[..., lane])
+        assert np.abs(x[:, lane] - want).max() <= 50 * 40 * EPS * cond * np.abs(want).max()
