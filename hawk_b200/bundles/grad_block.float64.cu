@@ -36,6 +36,7 @@ extern "C" __global__ void __launch_bounds__(256) grad_block(
 }
 
 extern "C" __device__ const unsigned int hk_team_threads__grad_block_2 = 32u;
+extern "C" __device__ const unsigned int hk_team_spans_run__grad_block_2 = 1u;
 extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__grad_block_2 = 3808u;
 extern "C" __global__ void __launch_bounds__(32) grad_block_2(
     hk::abi::ScalarHandle p_wout_out,
@@ -56,7 +57,9 @@ extern "C" __global__ void __launch_bounds__(32) grad_block_2(
     for (long long hawk_flat = static_cast<long long>(blockIdx.x) * hawk_teams + (threadIdx.x >> 5); hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
+        const Int hawk_wl = static_cast<Int>(threadIdx.x & 31);
         (void)hawk_i;
+        (void)hawk_wl;
         (void)nSamples;
         const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here();
         const long long hawk_lane = hawk_i;

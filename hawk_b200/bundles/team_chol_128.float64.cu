@@ -37,7 +37,9 @@ extern "C" __global__ void __launch_bounds__(256) team_chol_128(
     for (long long hawk_flat = static_cast<long long>(blockIdx.x) * hawk_teams + (threadIdx.x >> 5); hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
+        const Int hawk_wl = static_cast<Int>(threadIdx.x & 31);
         (void)hawk_i;
+        (void)hawk_wl;
         (void)nSamples;
         const auto mtx_A_i = mtx_A[i].get();
         const auto vin_b_i = vin_b[i].get();
@@ -73,7 +75,9 @@ extern "C" __global__ void __launch_bounds__(128) team_chol_128_2(
     for (long long hawk_flat = static_cast<long long>(blockIdx.x) * hawk_teams + (threadIdx.x >> 5); hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
+        const Int hawk_wl = static_cast<Int>(threadIdx.x & 31);
         (void)hawk_i;
+        (void)hawk_wl;
         (void)nSamples;
         const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here();
         const long long hawk_lane = hawk_i;

@@ -25,7 +25,9 @@ extern "C" __global__ void __launch_bounds__(256) team_eigh_40(
     for (long long hawk_flat = static_cast<long long>(blockIdx.x) * hawk_teams + (threadIdx.x >> 5); hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
+        const Int hawk_wl = static_cast<Int>(threadIdx.x & 31);
         (void)hawk_i;
+        (void)hawk_wl;
         (void)nSamples;
         const auto mtx_A_i = mtx_A[i].get();
         { const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here(); for (Int hawk_lk = hawk_tm.rank; hawk_lk < 1600; hawk_lk += hawk_tm.size) wout_tm0_a.data()[static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 1600 + hawk_lk] = mtx_A[i].at(hawk_lk / 40, hawk_lk % 40); }
@@ -60,7 +62,9 @@ extern "C" __global__ void __launch_bounds__(32) team_eigh_40_2(
     for (long long hawk_flat = static_cast<long long>(blockIdx.x) * hawk_teams + (threadIdx.x >> 5); hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {
         const long long hawk_i = base + hawk_flat;
         const hk::SampleIndex i{hawk_i};
+        const Int hawk_wl = static_cast<Int>(threadIdx.x & 31);
         (void)hawk_i;
+        (void)hawk_wl;
         (void)nSamples;
         const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here();
         const long long hawk_lane = hawk_i;

@@ -338,13 +338,32 @@ def grad_block(lane: Grid["key", "row":8], j: Vector[20], r: Scalar) -> Vector[2
     return hawk.sum(j * r, over="row")
 
 
+@hawk.kernel
+def ordered_total(lane: Grid["key", "row":8], x: Scalar) -> Scalar:
+    return hawk.sum(x, over="row", policy="ordered")
+
+
+@hawk.kernel
+def ordered_long(lane: Grid["key", "row":197385], x: Scalar) -> Scalar:
+    return hawk.sum(x, over="row", policy="ordered")
+
+
+@hawk.kernel
+def ordered_hist(x: Scalar, key: Index, acc: Mutable[Scalar]):
+    hawk.scatter(acc, policy="ordered")[key] += x
+
+
 #: Sums over some lane axes (hawk.sum(x, over=...), hawk/trace/reduce.py:
 #: one value per kept key): returned as an output, or read back in the body at
 #: the lane's own key (a keyed plane the runtime owns between two stages); a
 #: per-key block of more than 16 entries (an outer product's Gram block, a
 #: gradient of 20) is a BlockSum: the rows stored by a per-lane stage, each
 #: key's block summed in lane order by a team stage (hawk/ir/team.py:544-600).
-KEYED_KERNELS = {k.name: k for k in (key_total, key_share, gram_block, grad_block)}
+#: Under policy="ordered" a plain per-key sum, and a scatter by any key, are
+#: folded without atomics in fixed orders by the reference's ordered stages
+#: (hawk/ir/team.py:602-720): the same bits on every launch.
+KEYED_KERNELS = {k.name: k for k in (key_total, key_share, gram_block, grad_block, ordered_total, ordered_long,
+                                          ordered_hist)}
 
 
 #: Sums over samples read back in the body (hawk/ir/split.py): each runs as

@@ -105,6 +105,7 @@ struct hkb_entry {
     int block = kBlock;          // threads per block this entry launches with
     unsigned dynamic_smem = 0;   // bytes per block the unit exports (hk_dynamic_smem_bytes)
     int team = 0;                // a team entry's threads (one block per lane), else 0
+    bool spans_run = false;      // a team stage over keys, lane chunks or target cells
 };
 
 struct hkb_argblock {
@@ -280,6 +281,24 @@ int hkb_library_entry(hkb_library* lib, const char* name, hkb_entry** out) {
             return fail(HKB_ERR_ABI, "entry '%s': a team of %u threads is not 1 to 32 whole warps", name, threads);
         }
         entry->team = static_cast<int>(threads);
+        // A team stage over a block sum's keys, an ordered scatter's lane chunks
+        // or its target cells exports hk_team_spans_run__<entry> = 1: its count
+        // is those teams, which the run's sample count does not bound.
+        const std::string spans_sym = std::string("hk_team_spans_run__") + name;
+        void* gptr = nullptr;
+        size_t gbytes = 0;
+        if (cudaLibraryGetGlobal(&gptr, &gbytes, lib->lib, spans_sym.c_str()) == cudaSuccess &&
+            gbytes == sizeof(unsigned)) {
+            unsigned spans = 0;
+            e2 = cudaMemcpy(&spans, gptr, sizeof(unsigned), cudaMemcpyDeviceToHost);
+            if (e2 != cudaSuccess) {
+                delete entry;
+                return cuda_fail(e2, "reading the team stage's grid kind");
+            }
+            entry->spans_run = spans != 0;
+        } else {
+            cudaGetLastError();
+        }
     } else {
         cudaGetLastError();
     }
@@ -461,9 +480,14 @@ int hkb_argblock_rebind(hkb_argblock* block, const int64_t* slots, const int64_t
 int hkb_entry_launch(hkb_entry* entry, hkb_argblock* block, int64_t base, int64_t count,
                      int64_t n_samples, void* stream) {
     if (entry == nullptr || block == nullptr) return fail(HKB_ERR_ARGUMENT, "hkb_entry_launch: null argument");
-    if (base < 0 || count < 0 || base + count > n_samples)
+    if (entry->spans_run) {
+        if (base != 0 || count < 0 || n_samples < 0)
+            return fail(HKB_ERR_RANGE, "team stage '%s' spans the run: base must be 0 and count its teams, "
+                        "got base %lld, count %lld", entry->name.c_str(), (long long)base, (long long)count);
+    } else if (base < 0 || count < 0 || base + count > n_samples) {
         return fail(HKB_ERR_RANGE, "partition [%lld, %lld) is outside the %lld samples",
                     (long long)base, (long long)(base + count), (long long)n_samples);
+    }
     if (count == 0) return HKB_OK;
     DeviceScope scope(entry->lib->device);
     if (scope.err != cudaSuccess) return cuda_fail(scope.err, "selecting the device");

@@ -201,9 +201,12 @@ class DeviceKernel:
                             f"count: {sorted(votes.items())} -- pass n_samples= explicitly")
         return next(iter(votes.values()))
 
-    def check(self, planes: dict, values: dict, n: int) -> None:
-        """Every slot against its declaration; one refusal naming every failure."""
+    def check(self, planes: dict, values: dict, n: int, extents: dict | None = None) -> None:
+        """Every slot against its declaration; one refusal naming every failure.
+        ``extents`` gives the trailing extent a plane must hold where it is not
+        ``n`` (a split stage's planes over keys or target cells)."""
         errors = []
+        extents = extents or {}
         for role, name, dtype, shape in self.slots:
             if role == "nsamples":
                 continue
@@ -250,6 +253,10 @@ class DeviceKernel:
                 if len(p.shape) != len(shape) + 1 or tuple(p.shape[:-1]) != tuple(shape):
                     errors.append(f"argument {name!r}: expected shape {want_shape} (samples last), "
                                   f"got {p.shape}")
+                elif name in extents:
+                    if p.shape[-1] < extents[name]:
+                        errors.append(f"argument {name!r}: holds {p.shape[-1]} entries, fewer than the "
+                                      f"{extents[name]} the stage writes")
                 elif p.shape[-1] < n:
                     errors.append(f"argument {name!r}: holds {p.shape[-1]} samples, fewer than "
                                   f"n_samples={n}")
@@ -430,18 +437,63 @@ class SplitKernel:
         self._scratch: dict = {}
         self._values: dict = {}
 
-    def scratch(self, n: int) -> dict:
-        """The stages' scratch planes at ``n`` samples (made once per n)."""
+    #: The most lane chunks an ordered scatter adds in (hawk/_lane_bind.py:107-114).
+    SCATTER_CHUNKS = 256
+
+    @classmethod
+    def scatter_chunks(cls, n: int, targets: int) -> int:
+        """The chunks an ordered scatter of ``n`` lanes into ``targets`` cells adds in."""
+        return min(cls.SCATTER_CHUNKS, max(1, n // max(targets, 1)))
+
+    def team_units(self, spec: dict, n: int, sizes: dict) -> int:
+        """Elements of a team plane per ``per_lane`` (hawk/_lane_bind.py:137-145):
+        lanes, keys, one (``once``), or ``chunks * targets`` cells (``per_target``)."""
+        if spec.get("once"):
+            return 1
+        if "per_target" in spec:
+            size = sizes[spec["per_target"]]
+            return self.scatter_chunks(n, size) * size
+        if "keys" in spec:
+            return self.keyed_size(spec["keys"], n) // int(spec["keys"].get("width", 1))
+        return n
+
+    def grid(self, record: dict, n: int, count: int, sizes: dict) -> int:
+        """The teams a stage launches (hawk/_lane_bind.py:123-134): the
+        partition's lanes, a block sum's keys (times its groups), an ordered
+        scatter's lane chunks or its target's cells."""
+        kind = record.get("grid", "lanes")
+        if kind == "keys":
+            keyed = record["keyed"]
+            return self.keyed_size(keyed, n) // int(keyed.get("width", 1)) * int(record.get("groups") or 1)
+        if kind == "chunks":
+            return self.scatter_chunks(n, sizes[record["of"]])
+        if kind == "targets":
+            return sizes[record["of"]]
+        return count
+
+    def scratch(self, n: int, sizes: dict | None = None, stream=None) -> dict:
+        """The stages' scratch planes at ``n`` samples (and the ordered scatters'
+        target sizes): made once per shape; a plane with a ``fill`` is refilled
+        for every run, in stream order (hawk/runtime.py:675-696)."""
         import torch
 
-        if n not in self._scratch:
+        sizes = sizes or {}
+        key = (n, tuple(sorted(sizes.items())))
+        if key not in self._scratch:
             dev = torch.device("cuda", self.device)
             real = torch.float64 if self.mode == "float64" else torch.float32
-            self._scratch[n] = {
-                name: torch.empty(int(spec.get("per_lane", 1)) * n,
-                                  dtype=torch.int32 if spec.get("dtype") == "int32" else real, device=dev)
+            self._scratch[key] = {
+                name: torch.full((int(spec.get("per_lane", 1)) * self.team_units(spec, n, sizes),),
+                                 spec.get("fill", 0),
+                                 dtype=torch.int32 if spec.get("dtype") == "int32" else real, device=dev)
                 for name, spec in self.team_planes.items()}
-        return self._scratch[n]
+        planes = self._scratch[key]
+        refill = [(planes[name], spec["fill"]) for name, spec in self.team_planes.items() if "fill" in spec]
+        if refill:
+            with torch.cuda.stream(_torch_stream(stream, self.device)):
+                for t, value in refill:
+                    t.fill_(value)
+        return planes
 
     def keyed_size(self, spec: dict, n: int) -> int:
         """The elements of a keyed plane at ``n`` lanes: ``width`` payload
@@ -559,8 +611,11 @@ class SplitKernel:
         if self.cell_specs and base % ROW:
             raise HawkError(f"kernel {self.name!r} reduces over 32-sample rows, so a partition must "
                             f"start on a row (base % 32 == 0), got base={base}")
+        # the cells an ordered scatter adds into: the bound target plane's elements
+        sizes = {r["of"]: planes[r["of"]].size for r in self.records if r.get("of") and r["of"] in planes}
         with self._lock:
-            scratch = {k: from_torch(v) for k, v in self.scratch(n_samples).items()}
+            owned = self.scratch(n_samples, sizes, stream)
+            scratch = {k: from_torch(v) for k, v in owned.items()}
             scratch.update({k: from_torch(v) for k, v in self.keyed_planes(n_samples, stream).items()})
             cells = self.cell_values()
             for stage, record in zip(self.stages, self.records):
@@ -576,12 +631,20 @@ class SplitKernel:
                 if record.get("cells_out"):
                     state = stage.cells_state(n_samples)
                     bound.update({k: from_torch(v) for k, v in state["rows"].items()})
-                if record.get("grid") == "keys":
-                    # a block-sum stage: one team per key over the whole run
-                    keys = self.keyed_size(record["keyed"], n_samples) // int(record["keyed"].get("width", 1))
-                    stage.check(bound, values, keys)
+                if record.get("grid", "lanes") != "lanes":
+                    # a stage over keys, lane chunks or target cells: its teams span the whole run
+                    teams = self.grid(record, n_samples, count, sizes)
+                    if teams == 0:
+                        continue            # an ordered scatter into no cells adds nothing
+                    # per-sample planes hold the run's lanes; scratch holds its own units; a
+                    # block sum's output one entry a key; an ordered scatter's target its cells
+                    keys = teams // int(record.get("groups") or 1) if record["grid"] == "keys" else 0
+                    extents = {name: 0 for name in scratch}
+                    extents.update({name: keys for role, name in stage.arg_spec
+                                    if role == "wide_out" and name not in scratch})
+                    stage.check(bound, values, n_samples, extents)
                     stage.bind_all(bound, values, n_samples)
-                    stage.launch(0, keys, n_samples, stream)
+                    stage.launch(0, teams, n_samples, stream)
                 else:
                     stage.check(bound, values, n_samples)
                     stage.bind_all(bound, values, n_samples)
@@ -603,6 +666,16 @@ class SplitKernel:
                             keep = planes[cell].keep
                             out = keep if torch.is_tensor(keep) else torch.as_tensor(keep, device=f"cuda:{self.device}")
                             out.view(-1)[:cols].copy_(cells[cell])
+            for record in self.records:
+                status = record.get("status")
+                if status and status in owned:
+                    # an ordered scatter's key outside [0, cells) other than -1 is refused by
+                    # name after the run (hawk/_lane_bind.py:148-154): the flags from element 1
+                    flags = owned[status][1:]
+                    if bool(torch.any(flags != 0).item()):
+                        raise HawkError(f"{self.name}: hawk.scatter({record['of']}, policy='ordered') got a key "
+                                        f"outside [0, {sizes.get(record['of'])}) that is not the skip key -1; those "
+                                        f"adds were dropped, the rest are in {record['of']}")
 
     def errors(self, clear: bool = True) -> int:
         """The unit's error word (hkb_library_errors) after the stream's launches."""

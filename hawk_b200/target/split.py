@@ -145,8 +145,11 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
             body = body_text(render_body(member.sinks, walk, indent="        ", writer=B200_WRITER).text)
             smem = 0
         refuse_unbuilt(member.name, body)
+        team_record = record.get("team") or {}
+        spans = team_record.get("grid", "lanes") != "lanes"
         parts += [
             f'extern "C" __device__ const unsigned int hk_team_threads__{member.name} = {threads}u;',
+            *([f'extern "C" __device__ const unsigned int hk_team_spans_run__{member.name} = 1u;'] if spans else []),
             f'extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__{member.name} = {smem}u;',
             B200.entry_signature(walk, member.name, threads=threads),
             "{",
@@ -157,10 +160,11 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
             "}",
             "",
         ]
-        team_record = record.get("team") or {}
         stages.append({"entry": member.name, "kind": "team", "threads": threads, "dynamic_smem": smem,
                        "slots": _slot_records(walk), "sample_sums": [], "cells_in": [], "cells_out": [],
-                       "grid": team_record.get("grid", "lanes"), "keyed": team_record.get("keyed")})
+                       "grid": team_record.get("grid", "lanes"), "keyed": team_record.get("keyed"),
+                       "groups": team_record.get("groups"), "of": team_record.get("of"),
+                       "status": team_record.get("status")})
     text = "\n".join([*prelude_lines(name, mode), "", *parts])
     unit = Unit(name=name, mode=mode, text=text, body="", frame="split",
                 digest=hashlib.sha256(text.encode()).hexdigest(), entries="\n".join(parts),

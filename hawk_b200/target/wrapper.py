@@ -146,7 +146,9 @@ class B200Wrapper:
                 "hawk_flat < count; hawk_flat += static_cast<long long>(gridDim.x) * hawk_teams) {\n"
                 "        const long long hawk_i = base + hawk_flat;\n"
                 "        const hk::SampleIndex i{hawk_i};\n"
+                "        const Int hawk_wl = static_cast<Int>(threadIdx.x & 31);\n"
                 "        (void)hawk_i;\n"
+                "        (void)hawk_wl;\n"
                 "        (void)nSamples;")
 
     def team_epilogue(self) -> str:

@@ -121,7 +121,11 @@ int hkb_argblock_rebind(hkb_argblock* block, const int64_t* slots, const int64_t
 /* HostEntry.run(block, base, count, nSamples) (src/hawk_core.cpp:431-442, :642-653):
  * run the entry over samples [base, base + count) of nSamples on `stream`
  * (asynchronous).  A kernel with sample sums needs base % 32 == 0.  A team
- * entry runs lanes [base, base + count), each by one block of its team. */
+ * entry runs lanes [base, base + count), each by one block of its team.  A
+ * team stage over keys, lane chunks or target cells (it exports
+ * hk_team_spans_run__<entry> = 1; hawk/_lane_bind.py:123-134) takes base 0
+ * and count = its teams, which nSamples does not bound; the caller sizes its
+ * scratch planes for those teams as hawk/_lane_bind.py:137-145 does. */
 int hkb_entry_launch(hkb_entry* entry, hkb_argblock* block, int64_t base, int64_t count,
                      int64_t n_samples, void* stream);
 

@@ -459,6 +459,65 @@ def block_sums(u, v=None, rows: int = 8):
     return s
 
 
+#: The ordered sum's fixed grouping (hawk/emit/team.py:208-240; the numpy
+#: emulation the reference's tests hold it to, tests/test_ordered_fixed_tree.py:21-40).
+ORDERED_VIRTUAL, ORDERED_GROUPS, ORDERED_GROUP_LANES = 65536, 64, 1024
+
+
+def _halving(s):
+    """The halving tree s[i] += s[i + w], w = len/2 ... 1, over the last axis."""
+    w = s.shape[-1] // 2
+    while w:
+        s = s[..., :w] + s[..., w:2 * w]
+        w //= 2
+    return s[..., 0]
+
+
+def ordered_sums(x, rows: int):
+    """Per key (``rows`` consecutive lanes), the ordered sum: virtual lane l
+    of 65536 adds rows l, l + 65536, ... in order from 0; each group of 1024
+    virtual lanes folds by the halving tree (the first stage), the 64 group
+    values by the same tree (the second).  Zero padding adds exactly: a sum
+    started at +0 is never -0 under round to nearest."""
+    v = np.ascontiguousarray(x, dtype=np.float64).reshape(-1, rows)
+    part = np.zeros((v.shape[0], ORDERED_VIRTUAL))
+    for r in range(0, rows, ORDERED_VIRTUAL):
+        blk = v[:, r:r + ORDERED_VIRTUAL]
+        part[:, :blk.shape[1]] += blk
+    groups = _halving(part.reshape(v.shape[0], ORDERED_GROUPS, ORDERED_GROUP_LANES))
+    return _halving(groups)
+
+
+def ordered_scatter(key, x, acc):
+    """``hawk.scatter(acc, policy="ordered")[key] += x`` as the reference's
+    stages fold it (hawk/ir/team.py:716-736; hawk/emit/team.py:322-460):
+    chunks = clamp(n // cells, 1, 256) runs of ceil(n / chunks) lanes; each
+    chunk sums its lanes' values per cell in lane order from 0; each cell adds
+    its chunks' sums in chunk order from 0 and then adds that onto ``acc``.
+    Key -1 is skipped; any other key outside [0, cells) is dropped and
+    reported.  Returns (acc after the run, whether a key was reported)."""
+    key = np.asarray(key, dtype=np.int64)
+    x = np.asarray(x, dtype=np.float64)
+    acc = np.array(acc, dtype=np.float64, copy=True)
+    n, cells = key.shape[0], acc.shape[0]
+    chunks = min(256, max(1, n // max(cells, 1)))
+    span = -(-n // chunks) if n else 0
+    pad = chunks * span - n
+    k = np.concatenate([key, np.full(pad, -1)]).reshape(chunks, span)
+    v = np.concatenate([x, np.zeros(pad)]).reshape(chunks, span)
+    good = (k >= 0) & (k < cells)
+    bad = bool(np.any(~good & (k != -1)))
+    part = np.zeros((cells + 1, chunks))     # row ``cells`` takes the dropped lanes
+    c = np.arange(chunks)
+    for t in range(span):
+        tgt = np.where(good[:, t], k[:, t], cells)
+        part[tgt, c] += v[:, t]
+    s = np.zeros(cells)
+    for b in range(chunks):
+        s = s + part[:cells, b]
+    return acc + s, bad
+
+
 def sym_eigen(A, vectors: bool = True, threads: int = 1):
     """(w, V, info) of eigh(A) per sample (V None for the values-only kernel)."""
     k, n = A.shape[0], A.shape[-1]

@@ -14,6 +14,7 @@ fixtures it writes are committed and are all the test suite reads.
     python tests/golden/make_golden.py          # every fixture
     python tests/golden/make_golden.py team     # the team-form fixtures only
     python tests/golden/make_golden.py eigen    # the symmetric-eigenproblem fixtures only
+    python tests/golden/make_golden.py ordered  # the ordered-sum fixtures only
 """
 
 from __future__ import annotations
@@ -89,8 +90,40 @@ def eigen_fixtures(evaluate) -> None:
     np.savez(HERE / "eigen.npz", A=A, **{k: np.stack(v, axis=-1) for k, v in outs.items()})
 
 
+#: Ordered-sum fixtures: keys of ``rows`` lanes, drawn as the reference's
+#: fixed-tree test draws them (normal times exp(normal), seeded by the count).
+ORDERED_ROWS = ((8, 5), (1, 3), (1000, 2), (65536, 1), (197385, 2), (200003, 1))
+
+
+def ordered_draw(rows: int, keys: int) -> np.ndarray:
+    n = rows * keys
+    return np.random.default_rng(n).normal(size=n) * np.exp(np.random.default_rng(n + 1).normal(size=n))
+
+
+def ordered_fixtures(tree_sum) -> None:
+    """ordered.npz: per (rows, keys) case, each key's ordered sum by the
+    reference's own numpy emulation of the fixed grouping (``tree_sum``,
+    tests/test_ordered_fixed_tree.py:33-40 in the reference) and a digest of
+    the drawn lanes (the fixture keeps the seed, not the lanes)."""
+    import hashlib
+
+    out = {}
+    for rows, keys in ORDERED_ROWS:
+        x = ordered_draw(rows, keys)
+        out[f"sum_{rows}_{keys}"] = np.array([tree_sum(x[k * rows:(k + 1) * rows]) for k in range(keys)])
+        out[f"sha_{rows}_{keys}"] = np.frombuffer(hashlib.sha256(x.tobytes()).digest(), np.uint8)
+    np.savez(HERE / "ordered.npz", **out)
+
+
 def main() -> int:
     from hawk_b200 import frontend, workloads
+
+    if sys.argv[1:] == ["ordered"]:
+        hawk = frontend.load()
+        sys.path.insert(0, str(Path(hawk.__file__).resolve().parent.parent / "tests"))
+        from test_ordered_fixed_tree import tree_sum
+        ordered_fixtures(tree_sum)
+        return 0
 
     if sys.argv[1:] == ["eigen"]:
         hawk = frontend.load()

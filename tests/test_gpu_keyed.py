@@ -9,6 +9,12 @@ warps (a multiple of 32 lanes) every key's sum is one commit, so the device
 equals the oracle bit for bit; a partial last warp commits lane by lane in the
 hardware's order, inside the reference's keyed-commit bound
 (tests/test_keyed_commit.py).
+
+Under ``policy="ordered"`` a per-key sum and a scatter by any key run as the
+reference's ordered stages (hawk/ir/team.py:602-736): a fixed grouping that
+depends on the lane count only, the same bits on every launch, bit-identical
+to the oracle (itself pinned bitwise to the reference's numpy emulation of the
+grouping by tests/test_oracle_golden.py).
 """
 
 from __future__ import annotations
@@ -26,6 +32,7 @@ torch = pytest.importorskip("torch")
 
 import oracle  # noqa: E402
 from hawk_b200 import runtime  # noqa: E402
+from hawk_b200.errors import HawkError  # noqa: E402
 
 BUNDLES = REPO / "hawk_b200" / "bundles"
 EPS = np.finfo(np.float64).eps
@@ -91,3 +98,105 @@ def test_gradient_blocks_are_ordered_sums_per_key(keys):
     out = torch.full((20, keys), float("nan"), dtype=torch.float64, device="cuda")
     runtime.run(runtime.load(BUNDLES, "grad_block"), j=dev(j), r=dev(r), out=out)
     np.testing.assert_array_equal(host(out), oracle.block_sums(j, r[None, :])[:, 0, :])
+
+
+def ordered_draw(rows: int, keys: int) -> np.ndarray:
+    n = rows * keys
+    return np.random.default_rng(n).normal(size=n) * np.exp(np.random.default_rng(n + 1).normal(size=n))
+
+
+@pytest.mark.parametrize("name,rows,keys", [("ordered_total", 8, 5), ("ordered_total", 8, 4096),
+                                            ("ordered_long", 197385, 2)])
+def test_ordered_sums_are_the_fixed_tree_and_replay_bitwise(name, rows, keys):
+    """65536 virtual lanes a key, groups of 1024 by the halving tree, the 64
+    group values by the same tree: three launches, one set of bits, the
+    oracle's (197385 rows: three strides of 65536 and a partial fourth)."""
+    x = ordered_draw(rows, keys)
+    k = runtime.load(BUNDLES, name)
+    runs = []
+    for _ in range(3):
+        out = torch.full((keys,), float("nan"), dtype=torch.float64, device="cuda")
+        runtime.run(k, x=dev(x), out=out)
+        runs.append(host(out))
+    assert runs[0].tobytes() == runs[1].tobytes() == runs[2].tobytes()
+    np.testing.assert_array_equal(runs[0], oracle.ordered_sums(x, rows))
+    assert k.errors() == 0
+
+
+def scatter_case(n, cells, seed, heavy=False):
+    rng = np.random.default_rng(seed)
+    key = rng.integers(0, cells, n).astype(np.int32)
+    if heavy:
+        key[rng.random(n) < 0.9] = cells // 2
+    key[::7] = -1
+    x = rng.normal(size=n) * np.exp(rng.normal(size=n))
+    return key, x
+
+
+def scatter(key, x, acc, **kw):
+    acc = dev(acc)
+    runtime.run(runtime.load(BUNDLES, "ordered_hist"), key=dev(key), x=dev(x), acc=acc, **kw)
+    return host(acc)
+
+
+@pytest.mark.parametrize("n,cells,heavy", [(20000, 7, True), (3000, 1, False), (5000, 40, False),
+                                           (50, 200, False), (1000, 1000, False), (30000, 1500, False),
+                                           (1 << 20, 1000, False)])
+def test_ordered_scatter_is_the_chunk_walk_bitwise_and_replays(n, cells, heavy):
+    """Heavy collisions (256 chunks on a few cells), one cell, more cells than
+    lanes (one chunk), a cell per lane, more cells than the shared bins hold
+    (1500: the serial walk) and 2^20 lanes: the oracle's bits, three launches
+    alike, and onto a plane that held values the same sums added on top."""
+    key, x = scatter_case(n, cells, seed=n + cells, heavy=heavy)
+    want, bad = oracle.ordered_scatter(key, x, np.zeros(cells))
+    assert not bad
+    runs = [scatter(key, x, np.zeros(cells)) for _ in range(3)]
+    assert runs[0].tobytes() == runs[1].tobytes() == runs[2].tobytes()
+    np.testing.assert_array_equal(runs[0], want)
+    base = np.linspace(1.0, 2.0, cells)
+    np.testing.assert_array_equal(scatter(key, x, base), oracle.ordered_scatter(key, x, base)[0])
+
+
+def test_poisoned_partial_sums_do_not_change_the_ordered_scatter():
+    """The partial-sum plane is zeroed by the first team stage every launch:
+    NaN left in it by anything before does not reach the cells."""
+    n, cells = 20000, 7
+    key, x = scatter_case(n, cells, seed=3)
+    k = runtime.load(BUNDLES, "ordered_hist")
+    planes = k.scratch(n, {"acc": cells})
+    planes["tms_acc_p"].fill_(float("nan"))
+    planes["tms_acc_v"].fill_(float("nan"))
+    np.testing.assert_array_equal(scatter(key, x, np.zeros(cells)), oracle.ordered_scatter(key, x, np.zeros(cells))[0])
+
+
+def test_a_partition_of_the_lanes_adds_only_its_lanes():
+    n, cells = 6000, 33
+    key, x = scatter_case(n, cells, seed=5)
+    got = scatter(key, x, np.zeros(cells), base=1000, count=3000)
+    only = np.full(n, -1, np.int32)
+    only[1000:4000] = key[1000:4000]
+    np.testing.assert_array_equal(got, oracle.ordered_scatter(only, x, np.zeros(cells))[0])
+    # the next full launch sees none of the partition's keys left behind
+    np.testing.assert_array_equal(scatter(key, x, np.zeros(cells)), oracle.ordered_scatter(key, x, np.zeros(cells))[0])
+
+
+def test_a_key_out_of_range_is_reported_by_name_and_the_next_launch_is_clean():
+    n, cells = 4000, 9
+    key, x = scatter_case(n, cells, seed=29)
+    for bad in (cells, cells + 5, -2, 2**31 - 2):
+        wild = key.copy()
+        wild[[3, n - 1]] = bad
+        with pytest.raises(HawkError, match=r"hawk.scatter\(acc, policy='ordered'\) got a key outside \[0, 9\)"):
+            scatter(wild, x, np.zeros(cells))
+    np.testing.assert_array_equal(scatter(key, x, np.zeros(cells)), oracle.ordered_scatter(key, x, np.zeros(cells))[0])
+
+
+def test_a_target_of_no_cells_reports_any_key_but_the_skip_key():
+    n = 300
+    x = np.ones(n)
+    scatter(np.full(n, -1, np.int32), x, np.zeros(0))
+    key = np.full(n, -1, np.int32)
+    key[17] = 0
+    with pytest.raises(HawkError, match=r"got a key outside \[0, 0\)"):
+        scatter(key, x, np.zeros(0))
+    scatter(np.full(n, -1, np.int32), x, np.zeros(0))

@@ -304,3 +304,69 @@ def test_lstsq_qr_matches_numpy():
         want = np.linalg.lstsq(J[..., lane], r[:, lane], rcond=None)[0]
         cond = np.linalg.cond(J[..., lane])
         assert np.abs(x[:, lane] - want).max() <= 50 * 40 * EPS * cond * np.abs(want).max()
+
+
+def ordered_draw(rows: int, keys: int) -> np.ndarray:
+    """The lanes of an ordered-sum fixture, drawn as tests/golden/make_golden.py draws them."""
+    n = rows * keys
+    return np.random.default_rng(n).normal(size=n) * np.exp(np.random.default_rng(n + 1).normal(size=n))
+
+
+@pytest.mark.parametrize("rows,keys", [(8, 5), (1, 3), (1000, 2), (65536, 1), (197385, 2), (200003, 1)])
+def test_ordered_sums_are_the_reference_fixed_tree_bitwise(golden, rows, keys):
+    """Every key's ordered sum equals the reference's numpy emulation of the
+    fixed grouping (its tests/test_ordered_fixed_tree.py:33-40) bit for bit:
+    a partial block, a key of one lane, exactly one stride, three strides."""
+    import hashlib
+
+    g = golden("ordered")
+    x = ordered_draw(rows, keys)
+    assert hashlib.sha256(x.tobytes()).digest() == g[f"sha_{rows}_{keys}"].tobytes()
+    np.testing.assert_array_equal(oracle.ordered_sums(x, rows), g[f"sum_{rows}_{keys}"])
+
+
+def test_scatter_chunks_are_the_reference_choice():
+    """clamp(n // cells, 1, 256): the reference's known answers
+    (tests/test_scatter_ordered.py:119-121 there)."""
+    from hawk_b200.runtime import SplitKernel
+
+    cases = ((20000, 7), (50, 200), (1000, 1000), (10**6, 10**4), (10**6, 1), (10, 0))
+    assert [SplitKernel.scatter_chunks(n, t) for n, t in cases] == [256, 1, 1, 100, 256, 10]
+
+
+@pytest.mark.parametrize("n,cells,heavy", [(20000, 7, True), (3000, 1, False), (5000, 40, False),
+                                           (50, 200, False), (1000, 1000, False), (30000, 1500, False)])
+def test_ordered_scatter_is_add_at_within_the_reference_bound(n, cells, heavy):
+    """The chunked walk adds what np.add.at adds (the reference's bound:
+    1e-12 relative to the largest cell), skips key -1, and an empty cell
+    stays exactly 0; onto a plane that held values it adds on top."""
+    rng = np.random.default_rng(n)
+    key = rng.integers(0, cells, n).astype(np.int32)
+    if heavy:
+        key[rng.random(n) < 0.9] = cells // 2
+    if cells == 40:
+        key[key == 13] = 14
+    key[::7] = -1
+    x = rng.normal(size=n) * np.exp(rng.normal(size=n))
+    got, bad = oracle.ordered_scatter(key, x, np.zeros(cells))
+    assert not bad
+    want = np.zeros(cells)
+    np.add.at(want, key[key >= 0], x[key >= 0])
+    np.testing.assert_allclose(got, want, rtol=1e-12, atol=1e-12 * np.abs(want).max(initial=1.0))
+    if cells == 40:
+        assert got[13] == 0.0
+    base = np.linspace(1.0, 2.0, cells)
+    more, _ = oracle.ordered_scatter(key, x, base)
+    np.testing.assert_array_equal(more, base + got)
+
+
+def test_ordered_scatter_reports_a_key_out_of_range():
+    key = np.zeros(300, np.int32)
+    x = np.ones(300)
+    for bad in (9, 14, -2, 2**31 - 2):
+        wild = key.copy()
+        wild[[3, 299]] = bad
+        got, flagged = oracle.ordered_scatter(wild, x, np.zeros(9))
+        assert flagged and got[0] == 298.0
+    assert oracle.ordered_scatter(np.full(300, -1, np.int32), x, np.zeros(0))[1] is False
+    assert oracle.ordered_scatter(key, x, np.zeros(0))[1] is True
