@@ -43,6 +43,7 @@ SIGNATURES = {
     "hkb_entry_launch": (_c.c_int, [_P, _P, _c.c_int64, _c.c_int64, _c.c_int64, _P]),
     "hkb_entry_launch_persist": (_c.c_int, [_P, _P, _c.c_int64, _c.c_int64, _c.c_int64, _P, _P, _P, _P,
                                             _c.c_uint32, _c.c_int64, _P]),
+    "hkb_entry_launch_range": (_c.c_int, [_P, _P, _c.c_int64, _c.c_int64, _c.c_int64, _P, _P, _P]),
     "hkb_cells_leaves": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _c.POINTER(_P), _c.POINTER(_P),
                                     _c.c_int64, _P, _P, _P]),
     "hkb_cells_tree": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _P, _P, _c.c_int64, _P, _P]),
@@ -153,6 +154,15 @@ class Entry:
         check(lib().hkb_entry_launch_persist(self._h, block._h, int(base), int(count), int(n_samples),
                                              vp(next_ptr), vp(util), vp(steps), vp(stepsum), int(chunk),
                                              int(grid), vp(stream)),
+              f"launching {self.name!r}")
+
+    def launch_range(self, block: "ArgBlock", base: int, count: int, n_samples: int, steps: int = 0,
+                     stepsum: int = 0, stream: int = 0) -> None:
+        """The contiguous-range entry over ``[base, base + count)``; ``steps``
+        and ``stepsum`` are device addresses (0 when not reported)."""
+        vp = lambda v: ctypes.c_void_p(int(v) or None)   # noqa: E731
+        check(lib().hkb_entry_launch_range(self._h, block._h, int(base), int(count), int(n_samples),
+                                           vp(steps), vp(stepsum), vp(stream)),
               f"launching {self.name!r}")
 
 

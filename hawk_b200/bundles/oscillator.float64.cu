@@ -316,3 +316,153 @@ extern "C" __global__ void __launch_bounds__(256) oscillator_persist(
     hk::persist_report(hawk_steps, hawk_stepsum, hawk_util, hk_longest, hk_ran);
     hk::persist_finished(lut_finished_count, hk_fin);
 }
+
+extern "C" __global__ void __launch_bounds__(256) oscillator_range(
+    hk::abi::ScalarHandle p_mut_k,
+    hk::abi::ScalarHandle p_mut_v,
+    hk::abi::ScalarHandle p_mut_x,
+    hk::abi::ScalarHandle p_psc_nstop,
+    hk::abi::ScalarHandle p_psc_omega,
+    hk::abi::ScalarHandle p_psc_zeta,
+    hk::abi::ScalarHandle p_lut_finished_count,
+    hk::abi::ScalarHandle p_lut_fused_steps,
+    hk::abi::ScalarHandle p_trm_terminated,
+    Real p_uni_dt,
+    long long base,
+    long long count,
+    long long nSamples,
+    unsigned int* hawk_steps,
+    unsigned long long* hawk_stepsum)
+{
+    const hk::ScalarOut<Real> mut_k(p_mut_k);
+    (void)mut_k;
+    const hk::ScalarOut<Real> mut_v(p_mut_v);
+    (void)mut_v;
+    const hk::ScalarOut<Real> mut_x(p_mut_x);
+    (void)mut_x;
+    const hk::ScalarIn<Real> psc_nstop(p_psc_nstop);
+    (void)psc_nstop;
+    const hk::ScalarIn<Real> psc_omega(p_psc_omega);
+    (void)psc_omega;
+    const hk::ScalarIn<Real> psc_zeta(p_psc_zeta);
+    (void)psc_zeta;
+    const hk::ScalarIn<std::uint32_t> lut_finished_count(p_lut_finished_count);
+    (void)lut_finished_count;
+    const hk::ScalarIn<Int> lut_fused_steps(p_lut_fused_steps);
+    (void)lut_fused_steps;
+    const hk::MaskView trm_terminated(p_trm_terminated);
+    (void)trm_terminated;
+    const hk::MaskView trm_terminated_w(p_trm_terminated);
+    (void)trm_terminated_w;
+    const Real uni_dt = p_uni_dt;
+    (void)uni_dt;
+    unsigned hk_longest = 0u;
+    unsigned long long hk_ran = 0ull;
+    if (lut_fused_steps[hk::SampleIndex::make(0)].eval() == 1) {
+    for (long long hawk_flat = hk::lane_first(); hawk_flat < count; hawk_flat += hk::lane_step()) {
+        const long long hawk_i = base + hawk_flat;
+        const hk::SampleIndex i{hawk_i};
+        (void)hawk_i;
+        (void)nSamples;
+        const bool hk_live = !(trm_terminated[i].eval());
+        if (!trm_terminated[i].eval()) {
+            const auto mut_x_i = mut_x[i].get()();
+            const auto t3 = (uni_dt * static_cast<Real>(0.16666666666666666));
+            const auto mut_v_i = mut_v[i].get()();
+            const auto t7 = (static_cast<Real>(0.5) * uni_dt);
+            const auto psc_omega_i = psc_omega[i].eval();
+            const auto t10 = (-(psc_omega_i * psc_omega_i));
+            const auto t14 = ((static_cast<Real>(2.0) * psc_zeta[i].eval()) * psc_omega_i);
+            const auto t16 = ((t10 * mut_x_i) - (t14 * mut_v_i));
+            const auto t18 = (mut_v_i + (t7 * t16));
+            const auto t23 = ((t10 * (mut_x_i + (t7 * mut_v_i))) - (t14 * t18));
+            const auto t25 = (mut_v_i + (t7 * t23));
+            const auto t33 = ((t10 * (mut_x_i + (t7 * t18))) - (t14 * t25));
+            const auto t35 = (mut_v_i + (uni_dt * t33));
+            const auto t54 = (mut_k[i].get()() + static_cast<Real>(1.0));
+            mut_x[i] = (mut_x_i + (t3 * ((mut_v_i + (static_cast<Real>(2.0) * (t18 + t25))) + t35)));
+            mut_v[i] = (mut_v_i + (t3 * ((t16 + (static_cast<Real>(2.0) * (t23 + t33))) + ((t10 * (mut_x_i + (uni_dt * t25))) - (t14 * t35)))));
+            mut_k[i] = t54;
+            if (!trm_terminated[i].eval() && (t54 >= psc_nstop[i].eval())) { trm_terminated_w[i] = true; hawk_abi::finish_count(lut_finished_count); }
+        }
+        if (hk_live) {
+            hk_longest = 1u;
+            ++hk_ran;
+        } else { hawk_abi::finish_count(lut_finished_count); }
+    }
+    } else {
+    for (long long hawk_flat = hk::lane_first(); hawk_flat < count; hawk_flat += hk::lane_step()) {
+        const long long hawk_i = base + hawk_flat;
+        const hk::SampleIndex i{hawk_i};
+        (void)hawk_i;
+        (void)nSamples;
+        if (!(trm_terminated[i].eval())) {
+                const auto mut_x_i = mut_x[i].get()();
+                const auto mut_v_i = mut_v[i].get()();
+                const auto mut_k_i = mut_k[i].get()();
+                const auto t6 = (uni_dt * static_cast<Real>(0.16666666666666666));
+                const auto t9 = (static_cast<Real>(0.5) * uni_dt);
+                const auto psc_omega_i = psc_omega[i].eval();
+                const auto t12 = (-(psc_omega_i * psc_omega_i));
+                const auto t15 = ((static_cast<Real>(2.0) * psc_zeta[i].eval()) * psc_omega_i);
+                const auto psc_nstop_i = psc_nstop[i].eval();
+                const auto t20 = lut_fused_steps[hk::SampleIndex::make(static_cast<std::size_t>(static_cast<Int>(0)))].eval();
+                const auto t22 = ((t20 < static_cast<Int>(0)) ? static_cast<Int>(0) : t20);
+            Real hk_c0 = mut_x_i;
+            Real hk_c1 = mut_v_i;
+            Real hk_c2 = mut_k_i;
+            Real hk_c3 = static_cast<Real>(0.0);
+            const int hk_cnt = hawk_clamp_count(t22);
+            unsigned hk_trip = 0u;
+            if (hk_cnt > 0)
+            while (true) {
+                const int hawk_k23_step = static_cast<int>(hk_trip);
+                (void)hawk_k23_step;
+                const Real hawk_v23_0_x = hk_c0;
+                const Real hawk_v23_1_v = hk_c1;
+                const Real hawk_v23_2_k = hk_c2;
+                const Real hawk_v23_3_finished = hk_c3;
+                    const auto tb0 = ((t12 * hawk_v23_0_x) - (t15 * hawk_v23_1_v));
+                    const auto tb1 = (hawk_v23_1_v + (t9 * tb0));
+                    const auto tb2 = ((t12 * (hawk_v23_0_x + (t9 * hawk_v23_1_v))) - (t15 * tb1));
+                    const auto tb3 = (hawk_v23_1_v + (t9 * tb2));
+                    const auto tb4 = ((t12 * (hawk_v23_0_x + (t9 * tb1))) - (t15 * tb3));
+                    const auto tb5 = (hawk_v23_1_v + (uni_dt * tb4));
+                    const auto tb6 = (t6 * ((hawk_v23_1_v + (static_cast<Real>(2.0) * (tb1 + tb3))) + tb5));
+                    const auto tb7 = (t6 * ((tb0 + (static_cast<Real>(2.0) * (tb2 + tb4))) + ((t12 * (hawk_v23_0_x + (uni_dt * tb3))) - (t15 * tb5))));
+                    const auto tb8 = (hawk_v23_2_k + static_cast<Real>(1.0));
+                    const auto tb9 = (tb8 >= psc_nstop_i);
+                    const Real hawk_n23_0 = (hawk_v23_0_x + tb6);
+                    const Real hawk_n23_1 = (hawk_v23_1_v + tb7);
+                    const Real hawk_n23_2 = tb8;
+                    const Real hawk_n23_3 = (tb9 ? static_cast<Real>(1.0) : static_cast<Real>(0.0));
+                    const bool hawk_x23 = tb9;
+                hk_c0 = hawk_n23_0;
+                hk_c1 = hawk_n23_1;
+                hk_c2 = hawk_n23_2;
+                hk_c3 = hawk_n23_3;
+                ++hk_trip;
+                if (hawk_x23 || hk_trip >= static_cast<unsigned>(hk_cnt)) break;
+            }
+            {
+                const Real hawk_v23_0_x = hk_c0;
+                const Real hawk_v23_1_v = hk_c1;
+                const Real hawk_v23_2_k = hk_c2;
+                const Real hawk_v23_3_finished = hk_c3;
+                (void)hawk_v23_0_x;
+                (void)hawk_v23_1_v;
+                (void)hawk_v23_2_k;
+                (void)hawk_v23_3_finished;
+                mut_x[i] = hawk_v23_0_x;
+                mut_v[i] = hawk_v23_1_v;
+                mut_k[i] = hawk_v23_2_k;
+                if (!trm_terminated[i].eval() && (hawk_v23_3_finished > static_cast<Real>(0.5))) { trm_terminated_w[i] = true; hawk_abi::finish_count(lut_finished_count); }
+            }
+            hk_longest = hk_trip > hk_longest ? hk_trip : hk_longest;
+            hk_ran += hk_trip;
+        } else { hawk_abi::finish_count(lut_finished_count); }
+    }
+    }
+    // one report per warp: the longest trip count and the steps run
+    hk::persist_report(hawk_steps, hawk_stepsum, nullptr, hk_longest, hk_ran);
+}

@@ -551,6 +551,35 @@ int hkb_entry_launch_persist(hkb_entry* entry, hkb_argblock* block, int64_t base
     return HKB_OK;
 }
 
+int hkb_entry_launch_range(hkb_entry* entry, hkb_argblock* block, int64_t base, int64_t count,
+                           int64_t n_samples, uint32_t* steps, uint64_t* stepsum, void* stream) {
+    if (entry == nullptr || block == nullptr) return fail(HKB_ERR_ARGUMENT, "hkb_entry_launch_range: null argument");
+    if (base < 0 || count < 0 || base + count > n_samples)
+        return fail(HKB_ERR_RANGE, "partition [%lld, %lld) is outside the %lld samples",
+                    (long long)base, (long long)(base + count), (long long)n_samples);
+    if (count == 0) return HKB_OK;
+    DeviceScope scope(entry->lib->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "selecting the device");
+    std::vector<void*> args(block->params);
+    long long b = base, c = count, ns = n_samples;
+    args.push_back(&b);
+    args.push_back(&c);
+    args.push_back(&ns);
+    args.push_back(&steps);
+    args.push_back(&stepsum);
+    // the lane frame's grid: every resident slot, capped by the samples (whole
+    // warps always: the per-warp report after the frame needs all 32 lanes)
+    const int64_t threads = entry->block;
+    const int64_t need = (count + threads - 1) / threads;
+    const int64_t cap = static_cast<int64_t>(entry->lib->sms) * entry->blocks_per_sm;
+    const dim3 grid(static_cast<unsigned>(need < 1 ? 1 : (need < cap ? need : cap)));
+    const cudaError_t err = cudaLaunchKernel(reinterpret_cast<const void*>(entry->kernel), grid,
+                                             dim3(static_cast<unsigned>(threads)), args.data(), entry->dynamic_smem,
+                                             static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "launching the range entry");
+    return HKB_OK;
+}
+
 }  // extern "C"
 
 // ------------------------------------------------------------ the finish tree

@@ -111,6 +111,8 @@ class DeviceKernel:
         self.entry = self.library.entry(b200["entry"])
         # an automatic stepping kernel's persistent entry (<name>_persist)
         self.persist = self.library.entry(b200["persist"]) if b200.get("persist") else None
+        # and its contiguous-range entry (<name>_range)
+        self.ranged = self.library.entry(b200["range"]) if b200.get("range") else None
         # the fold of each compensated scatter target's companion (<name>__fold_<target>)
         self.folds = {t: self.library.entry(e) for t, e in (b200.get("folds") or {}).items()}
         self.descriptor = descriptor_for_sidecar(sidecar)
@@ -703,11 +705,13 @@ def load(directory, kernel: str, mode: str = "float64", device: int | None = Non
 
 
 def launch_cells(kernel: DeviceKernel, *, base: int = 0, count: int | None = None,
-                 n_samples: int | None = None, stream=None, persist: dict | None = None, **arrays):
+                 n_samples: int | None = None, stream=None, persist: dict | None = None,
+                 ranged: dict | None = None, **arrays):
     """Validate, bind and launch (the body of ``run``); for a kernel with cells,
     return ``(state, outputs, lo_row, hi_row)`` for the caller to finish, else None.
     ``persist`` launches the persistent entry instead, with those keyword
-    arguments of ``abi.Entry.launch_persist``."""
+    arguments of ``abi.Entry.launch_persist``; ``ranged`` the range entry, with
+    those of ``abi.Entry.launch_range``."""
     arrays = kernel.default_words(arrays, stream)
     declared = {name for _r, name in kernel.arg_spec} | set(kernel.cells)
     unknown = sorted(set(arrays) - declared)
@@ -756,6 +760,10 @@ def launch_cells(kernel: DeviceKernel, *, base: int = 0, count: int | None = Non
     if persist is not None:
         kernel.persist.launch_persist(kernel.block, base, count, n_samples,
                                       stream=_stream(stream, kernel.device), **persist)
+        return None
+    if ranged is not None:
+        kernel.ranged.launch_range(kernel.block, base, count, n_samples, stream=_stream(stream, kernel.device),
+                                   **ranged)
         return None
     kernel.launch(base, count, n_samples, stream)
     if not cells:
@@ -815,6 +823,35 @@ def run_persist(kernel: DeviceKernel, *, base: int = 0, count: int | None = None
                               "stepsum": ptr(stepsum), "chunk": chunk, "grid": grid}, **arrays)
         kernel._held.append(claim)
     return claim
+
+
+def _report_cells(kernel, **cells) -> None:
+    import torch
+
+    for label, (t, dtype, n) in cells.items():
+        if t is not None and (not torch.is_tensor(t) or t.dtype != dtype or t.numel() < n
+                              or t.device != torch.device("cuda", kernel.device)):
+            raise HawkError(f"{label}=: a device {dtype} tensor of {n} cell(s) on cuda:{kernel.device}")
+
+
+def run_range(kernel: DeviceKernel, *, base: int = 0, count: int | None = None, n_samples: int | None = None,
+              steps=None, stepsum=None, stream=None, **arrays) -> None:
+    """Run an automatic stepping kernel's contiguous-range entry over ``[base, base + count)``.
+
+    The same bits as ``run`` with the same ``fused_steps`` word; ``steps``
+    (uint32, one cell) and ``stepsum`` (uint64) receive the longest per-sample
+    step count of the launch and the steps run, when given (each zeroed by the
+    caller).  The finished counter holds the batch's finished count afterwards,
+    samples finished on entry included (hawk/emit/cuda.py:373-380)."""
+    import torch
+
+    if getattr(kernel, "ranged", None) is None:
+        raise HawkError(f"kernel {kernel.name!r} is not an automatic stepping kernel; it has no range entry")
+    _report_cells(kernel, steps=(steps, torch.uint32, 1), stepsum=(stepsum, torch.uint64, 1))
+    ptr = lambda t: 0 if t is None else t.data_ptr()   # noqa: E731
+    with kernel._lock:
+        launch_cells(kernel, base=base, count=count, n_samples=n_samples, stream=stream,
+                     ranged={"steps": ptr(steps), "stepsum": ptr(stepsum)}, **arrays)
 
 
 def run(kernel: DeviceKernel, *, base: int = 0, count: int | None = None, n_samples: int | None = None,

@@ -20,7 +20,7 @@ import re
 from dataclasses import dataclass, field
 
 from ..errors import HawkError
-from .persist import SUFFIX as PERSIST_SUFFIX, persist_entry, step_fp64_ops
+from .persist import RANGE_SUFFIX, SUFFIX as PERSIST_SUFFIX, persist_entry, range_entry, step_fp64_ops
 from .refill import refill_frame
 from .wrapper import B200, StagePlan, lane_frame_staged, sample_sum_store
 from .writer import B200_WRITER, body_text
@@ -219,6 +219,9 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
     persist = persist_entry(kernel, name, wrapper) if one_step is not None else None
     if persist is not None:
         parts += [persist, ""]
+    ranged = range_entry(kernel, name, wrapper) if one_step is not None else None
+    if ranged is not None:
+        parts += [ranged, ""]
     entries = "\n".join(parts)
     text = "\n".join(prelude) + "\n" + entries
     records = tuple((s.name, s.op, s.companion.name if s.op == "sum" else None) for s in sums)
@@ -227,6 +230,7 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
                 notes={"dynamic_smem": smem, "staged": plan is not None,
                        "stages": plan.stages if plan is not None else 0, "min_blocks": min_blocks or 0,
                        "persist": f"{name}{PERSIST_SUFFIX}" if persist is not None else None,
+                       "range": f"{name}{RANGE_SUFFIX}" if ranged is not None else None,
                        "step_fp64_ops": step_fp64_ops(kernel) if persist is not None else None,
                        "lane_refill": frame_note == "refill", "folds": folds,
                        "private_targets": [t for t, _k, _c in (private[2] if private else ())],

@@ -122,6 +122,7 @@ def build_split_kernel(kernel, directory, *, name: str | None = None, mode: str 
         "stages": 0,
         "min_blocks": 0,
         "persist": None,
+        "range": None,
         "step_fp64_ops": None,
         "lane_refill": False,
         "folds": {},
@@ -176,6 +177,7 @@ def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "flo
         "stages": unit.notes.get("stages", 0),
         "min_blocks": unit.notes.get("min_blocks", 0),
         "persist": unit.notes.get("persist"),
+        "range": unit.notes.get("range"),
         "step_fp64_ops": unit.notes.get("step_fp64_ops"),
         "lane_refill": unit.notes.get("lane_refill", False),
         "folds": unit.notes.get("folds") or {},

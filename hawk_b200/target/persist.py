@@ -50,6 +50,13 @@ from __future__ import annotations
 from ..errors import HawkError
 from .writer import B200_WRITER, body_text
 
+#: The parameters the contiguous-range entry takes after the kernel's own
+#: (hawk/emit/cuda.py:275-279): the longest per-sample trip count and the
+#: steps run, each null when not reported.
+RANGE_PARAMS = ("unsigned int* hawk_steps", "unsigned long long* hawk_stepsum")
+
+RANGE_SUFFIX = "_range"
+
 #: The parameters the persistent entry takes after the kernel's own.
 PERSIST_PARAMS = ("unsigned int* hawk_next", "unsigned long long* hawk_util", "unsigned int* hawk_steps",
                   "unsigned long long* hawk_stepsum", "unsigned int hawk_chunk")
@@ -195,3 +202,96 @@ def _counter_name(kernel) -> str:
     from hawk.ir.nodes import FINISHED_PLANE
 
     return FINISHED_PLANE
+
+
+def range_entry(kernel, name: str, wrapper) -> str | None:
+    """The text of ``<name>_range`` for an automatic kernel, else ``None``.
+
+    The reference's contiguous-range entry (hawk/emit/cuda.py:709-784): the
+    kernel's own parameters, then ``hawk_steps`` (uint32, maxed with each
+    sample's steps this launch) and ``hawk_stepsum`` (uint64, their sum), each
+    null when not reported.  Every sample of ``[base, base + count)`` runs on
+    one lane of the grid-stride frame: the word 1 the single step's body (one
+    step for a sample not finished on entry), any other word the fused body as
+    the renderer cuts it (head, the trips up to the step's exit or the budget,
+    tail) -- the texts the persistent entry runs, so the same bits as one
+    launch of the kernel's own entry with that word.  A sample finished on
+    entry counts into the finished counter with those finishing in the launch.
+    Each lane keeps its longest trip count and its steps in registers; one
+    warp reduction and one atomic each report them after the frame."""
+    from hawk.emit.render import render_body, render_lane_split
+    from hawk.emit.spelling import binding_name
+
+    walk = kernel.walk
+    one_step = getattr(kernel, "one_step", None)
+    if one_step is None or getattr(walk, "finish", None) is None:
+        return None
+    split = render_lane_split(kernel.sinks, walk, indent="            ",
+                              kind=getattr(kernel, "kind", None), writer=B200_WRITER)
+    if split is None or split.count is None:
+        raise HawkError(f"{name!r}: its fused body does not cut into head, trip and tail; "
+                        "the range entry is not built for it")
+    from .assemble import _word_read
+
+    counter = binding_name("lookup", _counter_name(kernel))
+    on_entry = f"hawk_abi::finish_count({counter});"
+    single = body_text(render_body(one_step.sinks, one_step.walk, indent="        ", writer=B200_WRITER).text)
+    pre, step, post = body_text(split.pre), body_text(split.step), body_text(split.post)
+    guard = body_text(split.guard) if split.guard is not None else None
+    carries = [(f"hk_c{j}", _carry_type(t), cname, body_text(init), nxt)
+               for j, (cname, t, init, nxt) in enumerate(split.carries)]
+    head = wrapper.entry_signature(walk, name)
+    assert head.endswith("    long long nSamples)")
+    head = head[:-1] + ",\n" + ",\n".join(f"    {p}" for p in RANGE_PARAMS) + ")"
+    head = head.replace(f" {name}(", f" {name}{RANGE_SUFFIX}(", 1)
+    p12, p16 = " " * 12, " " * 16
+    fused = [
+        *([f"        if (!({guard})) {{"] if guard is not None else ["        {"]),
+        pre.rstrip("\n"),
+        *[f"{p12}{ct} {reg} = {init};" for reg, ct, _c, init, _n in carries],
+        f"{p12}const int hk_cnt = hawk_clamp_count({body_text(split.count)});",
+        f"{p12}unsigned hk_trip = 0u;",
+        f"{p12}if (hk_cnt > 0)",
+        f"{p12}while (true) {{",
+        f"{p16}const int {split.index} = static_cast<int>(hk_trip);",
+        f"{p16}(void){split.index};",
+        *[f"{p16}const {ct} {cname} = {reg};" for reg, ct, cname, _i, _n in carries],
+        step.rstrip("\n"),
+        *[f"{p16}{reg} = {nxt};" for reg, _ct, _c, _i, nxt in carries],
+        f"{p16}++hk_trip;",
+        f"{p16}if ({split.exit} || hk_trip >= static_cast<unsigned>(hk_cnt)) break;",
+        f"{p12}}}",
+        f"{p12}{{",
+        *[f"{p16}const {ct} {cname} = {reg};" for reg, ct, cname, _i, _n in carries],
+        *[f"{p16}(void){cname};" for _r, _c, cname, _i, _n in carries],
+        post.rstrip("\n"),
+        f"{p12}}}",
+        f"{p12}hk_longest = hk_trip > hk_longest ? hk_trip : hk_longest;",
+        f"{p12}hk_ran += hk_trip;",
+        *([f"        }} else {{ {on_entry} }}"] if guard is not None else ["        }"]),
+    ]
+    lines = [
+        head,
+        "{",
+        wrapper.unpack(walk),
+        "    unsigned hk_longest = 0u;",
+        "    unsigned long long hk_ran = 0ull;",
+        f"    if ({_word_read()} == 1) {{",
+        wrapper.index_prologue(),
+        f"        const bool hk_live = !({guard});" if guard is not None else "        const bool hk_live = true;",
+        single.rstrip("\n"),
+        "        if (hk_live) {",
+        "            hk_longest = 1u;",
+        "            ++hk_ran;",
+        *([f"        }} else {{ {on_entry} }}"] if guard is not None else ["        }"]),
+        wrapper.index_epilogue(),
+        "    } else {",
+        wrapper.index_prologue(),
+        *fused,
+        wrapper.index_epilogue(),
+        "    }",
+        "    // one report per warp: the longest trip count and the steps run",
+        "    hk::persist_report(hawk_steps, hawk_stepsum, nullptr, hk_longest, hk_ran);",
+        "}",
+    ]
+    return "\n".join(line for line in lines if line is not None)

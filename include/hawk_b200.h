@@ -143,6 +143,18 @@ int hkb_entry_launch_persist(hkb_entry* entry, hkb_argblock* block, int64_t base
                              int64_t n_samples, uint32_t* next, uint64_t* util, uint32_t* steps,
                              uint64_t* stepsum, uint32_t chunk, int64_t grid, void* stream);
 
+/* The contiguous-range entry of an automatic stepping kernel, `<kernel>_range`
+ * (the reference emits it in hawk/emit/cuda.py:709-784; its runner lives in
+ * the absent eagle package): every sample of [base, base + count) on one lane
+ * of a grid-stride frame, the fused_steps word 1 running the single step, any
+ * other word the fused body's head, trips and tail -- the bits of one launch
+ * of the kernel's own entry with that word.  `steps` (uint32, maxed with each
+ * sample's steps this launch) and `stepsum` (uint64, their sum) may be null;
+ * the caller zeroes them.  Samples finished on entry count into the finished
+ * counter with those finishing in the launch. */
+int hkb_entry_launch_range(hkb_entry* entry, hkb_argblock* block, int64_t base, int64_t count,
+                           int64_t n_samples, uint32_t* steps, uint64_t* stepsum, void* stream);
+
 /* ---------------------------------------------- cells: the ordered finish */
 
 /* The device form of hawk/_cells.py:finish for `ncols` columns (<= 8) of

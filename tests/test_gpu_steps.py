@@ -197,3 +197,61 @@ def test_persistent_entry_refusals():
     with pytest.raises(HawkError, match="steps="):
         runtime.run_persist(runtime.load(BUNDLES, "oscillator"), **to_dev(w, OSC), dt=w["dt"],
                             steps=torch.zeros(1, dtype=torch.int64, device="cuda"))
+
+
+# ----------------------------------------------------------------- range entry
+@pytest.mark.parametrize("name,word", [("oscillator", 1), ("oscillator", 1000), ("oscillator", 13), ("oscillator", 0),
+                                       ("orbit", 1), ("orbit", 1000), ("orbit", 9)])
+def test_range_entry_is_one_fused_launch_and_reports_its_steps(name, word):
+    """<name>_range (hawk/emit/cuda.py:709-784 is the reference's): the bits of
+    one launch of the kernel's own entry with the same word; the finished
+    counter the batch's finished count (on entry included); hawk_steps the
+    longest per-sample step count, hawk_stepsum the steps run."""
+    n = 20000 + 17 if name == "oscillator" else 3000 + 5
+    w = osc_workload(n, seed=9) if name == "oscillator" else orb_workload(n, seed=9)
+    names = OSC if name == "oscillator" else ORB
+    extra = {"dt": w["dt"]} if name == "oscillator" else {}
+    k = runtime.load(BUNDLES, name)
+    fused, ranged = to_dev(w, names), to_dev(w, names)
+    runtime.run(k, **fused, **extra, fused_steps=word_of(word), finished_count=counter())
+    steps = torch.zeros(1, dtype=torch.uint32, device="cuda")
+    stepsum = torch.zeros(1, dtype=torch.uint64, device="cuda")
+    fin = counter()
+    runtime.run_range(k, **ranged, **extra, fused_steps=word_of(word), finished_count=fin, steps=steps,
+                      stepsum=stepsum)
+    same_planes(ranged, {key: host(v) for key, v in fused.items()}, names)
+    before = {key: np.asarray(w[key]) for key in names}
+    after = {key: host(v) for key, v in ranged.items()}
+    trips = trips_of(name, before, after)
+    assert int(host(fin)[0]) == int(after["terminated"].sum())
+    assert int(host(steps)[0]) == int(trips.max())
+    assert int(host(stepsum)[0]) == int(trips.sum())
+    if word == 1:
+        assert set(np.unique(trips)) <= {0, 1}
+
+
+def test_range_entry_runs_its_partition_only_and_reports_nothing_when_asked_nothing():
+    n = 5000
+    w = osc_workload(n, seed=4)
+    k = runtime.load(BUNDLES, "oscillator")
+    planes = to_dev(w, OSC)
+    runtime.run_range(k, **planes, dt=w["dt"], fused_steps=word_of(1000), finished_count=counter(),
+                      base=1000, count=2000)
+    want = oracle_planes(w, OSC)
+    oracle.oscillator(want, w["dt"], 1000)
+    got = {key: host(v) for key, v in planes.items()}
+    for key in OSC:
+        assert np.array_equal(got[key][1000:3000], want[key][1000:3000], equal_nan=True), key
+        assert np.array_equal(got[key][:1000], np.asarray(w[key])[:1000], equal_nan=True), key
+        assert np.array_equal(got[key][3000:], np.asarray(w[key])[3000:], equal_nan=True), key
+
+
+def test_range_entry_refusals():
+    from hawk_b200.errors import HawkError
+
+    with pytest.raises(HawkError, match="no range entry"):
+        runtime.run_range(runtime.load(BUNDLES, "energy"), v=dev(np.zeros((3, 4))), out=dev(np.zeros(4)))
+    w = osc_workload(64)
+    with pytest.raises(HawkError, match="stepsum="):
+        runtime.run_range(runtime.load(BUNDLES, "oscillator"), **to_dev(w, OSC), dt=w["dt"],
+                          stepsum=torch.zeros(1, dtype=torch.uint32, device="cuda"))
