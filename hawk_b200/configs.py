@@ -353,6 +353,40 @@ def ordered_hist(x: Scalar, key: Index, acc: Mutable[Scalar]):
     hawk.scatter(acc, policy="ordered")[key] += x
 
 
+#: The named net axis: K small models in one launch (the reference's
+#: tests/_net_axis_kernels.py:16-27).  Lanes are (net, sample); W[net, :]
+#: holds each net's (a, b, c) per hidden unit, a mask row zeroes the unused
+#: units of a narrower net; the loss keeps the net label.  Its gradient wrt W
+#: is a keyed accumulate into the table: atomic per-warp partials by default,
+#: and under policy="ordered" a per-lane log folded per key in lane order by a
+#: team stage (hawk/diff/ordered.py, hawk/ir/team.py:677-693).
+NET_HIDDEN, NET_WEIGHTS = 8, 24
+
+
+def net_loss_for(samples: int, policy: str = "compensated") -> Kernel:
+    @hawk.kernel
+    def net_loss(lane: Grid["net", "sample":samples], W: Table["net", "p":NET_WEIGHTS],
+                 mask: Table["net", "h":NET_HIDDEN], x: Scalar, y: Scalar) -> Scalar:
+        pred = 0.0 * x
+        for h in range(NET_HIDDEN):
+            a = W.at(net=lane.net, p=3 * h)
+            b = W.at(net=lane.net, p=3 * h + 1)
+            c = W.at(net=lane.net, p=3 * h + 2)
+            pred = pred + mask.at(net=lane.net, h=h) * c * m.tanh(a * x + b)
+        return hawk.sum((pred - y) * (pred - y), over="sample", policy=policy)
+
+    return Kernel(f"net_loss_{samples}" + ("_ordered" if policy == "ordered" else ""),
+                  net_loss.sinks, net_loss.planes)
+
+
+NET_KERNELS = {}
+for _s, _policy in ((40, "compensated"), (40, "ordered"), (48, "ordered")):
+    _loss = net_loss_for(_s, _policy)
+    _grad_name = _loss.name.replace("net_loss", "net_grad")
+    NET_KERNELS[_loss.name] = _loss
+    NET_KERNELS[_grad_name] = Kernel(_grad_name, vjp(_loss, wrt=("W",)))
+
+
 #: Sums over some lane axes (hawk.sum(x, over=...), hawk/trace/reduce.py:
 #: one value per kept key): returned as an output, or read back in the body at
 #: the lane's own key (a keyed plane the runtime owns between two stages); a
@@ -457,6 +491,7 @@ KERNELS = {
     **{name: (k, ("float64",)) for name, k in TEAM_KERNELS.items()},
     **{name: (k, ("float64",)) for name, k in READBACK_KERNELS.items()},
     **{name: (k, ("float64",)) for name, k in KEYED_KERNELS.items()},
+    **{name: (k, ("float64",)) for name, k in NET_KERNELS.items()},
     "share_vjp": (Kernel("share_vjp", vjp(share, wrt=("x",))), ("float64",)),
     "sym_eigen": (sym_eigen, ("float64",)),
     "sym_eigvals": (sym_eigvals, ("float64",)),

@@ -262,6 +262,7 @@ class DeviceKernel:
                 elif p.shape[-1] < n:
                     errors.append(f"argument {name!r}: holds {p.shape[-1]} samples, fewer than "
                                   f"n_samples={n}")
+        errors += adjoint_errors(adjoint_like(self.slots), planes)
         if errors:
             if len(errors) == 1:
                 raise HawkError(f"kernel {self.name!r}: {errors[0]}")
@@ -380,6 +381,25 @@ def _stream(stream, device: int) -> int:
         return int(torch.cuda.current_stream(device).cuda_stream)
     except Exception:                                   # noqa: BLE001
         return 0
+
+
+def adjoint_like(slots) -> dict:
+    """``bar_<plane>`` to ``<plane>`` for each written plane that is the
+    adjoint of a lookup plane (hawk/ir/walk.py:144-152): it must hold as many
+    elements as that plane, since the kernel adds into it by the plane's own
+    index, never by lane."""
+    reads = {n for r, n, *_ in slots if r in ("lookup", "wide_in")}
+    return {n: n[4:] for r, n, *_ in slots
+            if r in ("accum_out", "wide_out") and n.startswith("bar_") and n[4:] in reads}
+
+
+def adjoint_errors(like: dict, planes: dict) -> list:
+    """A gradient plane smaller than the lookup plane it is the adjoint of
+    (hawk/_bind_checks.py:384-395), one message each."""
+    return [f"argument {grad!r}: the gradient of the lookup plane {plane!r} (shape {tuple(planes[plane].shape)}) "
+            f"needs that many elements, got shape {tuple(planes[grad].shape)}"
+            for grad, plane in like.items()
+            if grad in planes and plane in planes and planes[grad].size < planes[plane].size]
 
 
 class SplitKernel:
@@ -539,6 +559,8 @@ class SplitKernel:
         """The block sums' output planes a caller binds: ``{name: (payload, keyed)}``."""
         out = {}
         for record in self.records:
+            if "ordered_fold" in (record.get("ops") or ()):
+                continue            # an ordered gradient's fold stores into its table's gradient
             if record.get("grid") == "keys" and record.get("keyed"):
                 for slot in record["slots"]:
                     if slot["role"] == "wide_out" and slot["name"] in {n for _r, n in self.arg_spec}:
@@ -600,6 +622,9 @@ class SplitKernel:
                                                if k not in uniforms and k not in self.block_outputs()})
         arrays = self.flat_block_outputs(arrays, n_samples)
         planes = {k: as_plane(k, v) for k, v in arrays.items() if k not in uniforms}
+        errors = adjoint_errors(adjoint_like(self.slots), planes)
+        if errors:
+            raise HawkError(f"kernel {self.name!r}: " + "; ".join(errors))
         for c, spec in self.cells.items():
             p = planes[c]
             if p.dtype != self.mode or p.device != self.device or p.size < int(spec.get("columns", 1)):
@@ -648,7 +673,8 @@ class SplitKernel:
                     stage.bind_all(bound, values, n_samples)
                     stage.launch(0, teams, n_samples, stream)
                 else:
-                    stage.check(bound, values, n_samples)
+                    # scratch planes are sized by their units (lanes, keys, once), not checked by lane
+                    stage.check(bound, values, n_samples, {name: 0 for name in scratch})
                     stage.bind_all(bound, values, n_samples)
                     stage.launch(base, count, n_samples, stream)
                 if state is None:

@@ -164,7 +164,8 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
                        "slots": _slot_records(walk), "sample_sums": [], "cells_in": [], "cells_out": [],
                        "grid": team_record.get("grid", "lanes"), "keyed": team_record.get("keyed"),
                        "groups": team_record.get("groups"), "of": team_record.get("of"),
-                       "status": team_record.get("status")})
+                       "status": team_record.get("status"),
+                       "ops": [st.op for st in member.team.steps] if isinstance(member, TeamStage) else []})
     text = "\n".join([*prelude_lines(name, mode), "", *parts])
     unit = Unit(name=name, mode=mode, text=text, body="", frame="split",
                 digest=hashlib.sha256(text.encode()).hexdigest(), entries="\n".join(parts),

@@ -518,6 +518,24 @@ def ordered_scatter(key, x, acc):
     return acc + s, bad
 
 
+def net_axis(w, x, y, mask):
+    """Per-net loss and its gradient wrt the weights, by numpy over the nets
+    (the reference's loop, tests/test_net_axis.py:61-73): ``w`` (K, 24) holds
+    (a, b, c) per hidden unit, ``x``/``y`` (K, S), ``mask`` (K, 8);
+    t = tanh(a x + b), r = (mask c) . t - y, loss = r . r."""
+    w, x, y, mask = (np.asarray(v, dtype=np.float64) for v in (w, x, y, mask))
+    a, b, c = w[:, 0::3], w[:, 1::3], w[:, 2::3]
+    t = np.tanh(a[:, :, None] * x[:, None, :] + b[:, :, None])
+    r = np.einsum("kh,khs->ks", mask * c, t) - y
+    loss = np.einsum("ks,ks->k", r, r)
+    grad = np.zeros_like(w)
+    dt = (2 * mask * c)[:, :, None] * (1 - t * t) * r[:, None, :]
+    grad[:, 0::3] = np.einsum("khs,ks->kh", dt, x)
+    grad[:, 1::3] = dt.sum(axis=2)
+    grad[:, 2::3] = np.einsum("khs,ks->kh", (2 * mask)[:, :, None] * t, r)
+    return loss, grad
+
+
 def sym_eigen(A, vectors: bool = True, threads: int = 1):
     """(w, V, info) of eigh(A) per sample (V None for the values-only kernel)."""
     k, n = A.shape[0], A.shape[-1]

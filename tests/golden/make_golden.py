@@ -15,6 +15,7 @@ fixtures it writes are committed and are all the test suite reads.
     python tests/golden/make_golden.py team     # the team-form fixtures only
     python tests/golden/make_golden.py eigen    # the symmetric-eigenproblem fixtures only
     python tests/golden/make_golden.py ordered  # the ordered-sum fixtures only
+    python tests/golden/make_golden.py net      # the net-axis fixtures only
 """
 
 from __future__ import annotations
@@ -115,8 +116,27 @@ def ordered_fixtures(tree_sum) -> None:
     np.savez(HERE / "ordered.npz", **out)
 
 
+def net_fixtures(problem, loop) -> None:
+    """net.npz: five nets of widths (8, 3, 5, 1, 6) at 40 and 48 samples, drawn
+    by the reference's ``_problem`` and solved by its loop over the nets
+    (``_oracle``, tests/test_net_axis.py:52-73 in the reference)."""
+    out = {}
+    for s in (40, 48):
+        w, x, y, mask = problem(5, (8, 3, 5, 1, 6), seed=3, S=s)
+        loss, grad = loop(w, x, y, mask)
+        out.update({f"w_{s}": w, f"x_{s}": x, f"y_{s}": y, f"mask_{s}": mask, f"loss_{s}": loss, f"grad_{s}": grad})
+    np.savez(HERE / "net.npz", **out)
+
+
 def main() -> int:
     from hawk_b200 import frontend, workloads
+
+    if sys.argv[1:] == ["net"]:
+        hawk = frontend.load()
+        sys.path.insert(0, str(Path(hawk.__file__).resolve().parent.parent / "tests"))
+        from test_net_axis import _oracle, _problem
+        net_fixtures(_problem, _oracle)
+        return 0
 
     if sys.argv[1:] == ["ordered"]:
         hawk = frontend.load()

@@ -370,3 +370,28 @@ def test_ordered_scatter_reports_a_key_out_of_range():
         assert flagged and got[0] == 298.0
     assert oracle.ordered_scatter(np.full(300, -1, np.int32), x, np.zeros(0))[1] is False
     assert oracle.ordered_scatter(key, x, np.zeros(0))[1] is True
+
+
+@pytest.mark.parametrize("s", [40, 48])
+def test_net_axis_golden(golden, s):
+    """Per-net loss and gradient against the reference's loop over the nets."""
+    g = golden("net")
+    loss, grad = oracle.net_axis(g[f"w_{s}"], g[f"x_{s}"], g[f"y_{s}"], g[f"mask_{s}"])
+    close(loss, g[f"loss_{s}"])
+    close(grad, g[f"grad_{s}"], rtol=1e-11, atol=1e-12)
+    dead = np.repeat(g[f"mask_{s}"] == 0.0, 3, axis=1)
+    assert dead.any() and (grad[dead] == 0.0).all()
+
+
+def test_net_axis_gradient_is_the_loss_slope():
+    rng = np.random.default_rng(7)
+    w = rng.normal(size=(3, 24)) * 0.7
+    x, y = rng.normal(size=(3, 40)), rng.normal(size=(3, 40))
+    mask = np.ones((3, 8))
+    _loss, grad = oracle.net_axis(w, x, y, mask)
+    for net, col in ((0, 0), (1, 7), (2, 23), (1, 14)):
+        up, dn = w.copy(), w.copy()
+        up[net, col] += 1e-6
+        dn[net, col] -= 1e-6
+        slope = (oracle.net_axis(up, x, y, mask)[0][net] - oracle.net_axis(dn, x, y, mask)[0][net]) / 2e-6
+        assert abs(grad[net, col] - slope) <= 1e-6 * max(1.0, abs(slope))
