@@ -567,6 +567,116 @@ def run_team(local: int, cpu_threads: int | None = None) -> dict:
     return out
 
 
+# ------------------------------------------------- ordered stages and the net axis
+#: Ordered scatter: lanes and target cells; ordered per-key sum: keys of the
+#: 197385-row kernel; net axis: nets of 40 samples.
+KEYED_SCATTER = (1 << 24, 1000)
+KEYED_LONG_KEYS = 64
+KEYED_NETS = 16384
+
+
+def run_keyed(local: int, cpu_threads: int | None = None) -> dict:
+    """The policy="ordered" stages and the net axis, each a whole run (every
+    stage) timed with CUDA events: lanes/s, algorithmic GB/s against the HBM
+    peak (every per-lane plane read once, tables and outputs once), and the
+    oracle on the host cores over a sample.  The ordered scatter is set beside
+    the atomic scatter of the same lanes (``histogram``); the ordered net loss
+    and gradient beside their atomic forms."""
+    import torch
+
+    import oracle
+    from hawk_b200 import runtime
+
+    dev = torch.device("cuda", local)
+    pk = peaks()
+    out = {}
+
+    def timed(fn, reps=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+        return statistics.median(times)
+
+    def record(name, lanes, ms, per_lane, extra=None):
+        gbs = per_lane * lanes / (ms * 1e-3) / 1e9
+        out[name] = {"lanes": lanes, "ms": round(ms, 5), "lanes_per_s": lanes / (ms * 1e-3),
+                     "gbs": round(gbs, 1), "hbm_frac": round(gbs / pk["hbm_gbs"], 4),
+                     "bytes_per_lane": round(per_lane, 3), **(extra or {})}
+
+    # ordered scatter of 2^24 lanes into 1000 cells (key 4 B + value 8 B a lane)
+    n, cells = KEYED_SCATTER
+    rng = np.random.default_rng(1)
+    key_h = rng.integers(0, cells, n).astype(np.int32)
+    x_h = rng.normal(size=n)
+    key, x = torch.as_tensor(key_h, device=dev), torch.as_tensor(x_h, device=dev)
+    acc = torch.zeros(cells, dtype=torch.float64, device=dev)
+    k = runtime.load(BUNDLES, "ordered_hist", "float64", local)
+    ms = timed(lambda: runtime.run(k, key=key, x=x, acc=acc))
+    sample = 1 << 20
+    t0 = time.perf_counter()
+    oracle.ordered_scatter(key_h[:sample], x_h[:sample], np.zeros(cells))
+    cpu = sample / (time.perf_counter() - t0)
+    record("ordered_hist", n, ms, 12.0, {"cells": cells, "chunks": runtime.SplitKernel.scatter_chunks(n, cells),
+                                         "cpu_baseline": {"lanes_per_s": cpu, "threads": 1, "sample_lanes": sample,
+                                                          "kind": "port"}})
+    atomic = runtime.load(BUNDLES, "histogram", "float64", local)
+    slots = {name for _r, name in atomic.arg_spec}
+    if {"key", "x", "acc"} <= slots:
+        ms = timed(lambda: runtime.run(atomic, key=key, x=x, acc=acc))
+        record("histogram_compensated", n, ms, 12.0)
+    del key, x, acc
+
+    # ordered per-key sum: 64 keys of 197385 rows (8 B a lane)
+    rows = 197385
+    n = rows * KEYED_LONG_KEYS
+    x_h = rng.normal(size=n)
+    x = torch.as_tensor(x_h, device=dev)
+    total = torch.empty(KEYED_LONG_KEYS, dtype=torch.float64, device=dev)
+    k = runtime.load(BUNDLES, "ordered_long", "float64", local)
+    ms = timed(lambda: runtime.run(k, x=x, out=total))
+    t0 = time.perf_counter()
+    oracle.ordered_sums(x_h[:4 * rows], rows)
+    cpu = 4 * rows / (time.perf_counter() - t0)
+    record("ordered_long", n, ms, 8.0, {"keys": KEYED_LONG_KEYS, "rows": rows,
+                                        "cpu_baseline": {"lanes_per_s": cpu, "threads": 1, "sample_lanes": 4 * rows,
+                                                         "kind": "port"}})
+    del x
+
+    # the net axis: 16384 nets x 40 samples, loss and gradient, atomic and ordered
+    nets, s = KEYED_NETS, 40
+    w_h = rng.normal(size=(nets, 24)) * 0.7
+    xs_h, ys_h = rng.normal(size=(nets, s)), rng.normal(size=(nets, s))
+    mask_h = (np.arange(8)[None, :] < np.resize(np.arange(1, 9), nets)[:, None]).astype(np.float64)
+    planes = {"W": torch.as_tensor(w_h.ravel(), device=dev), "mask": torch.as_tensor(mask_h.ravel(), device=dev),
+              "x": torch.as_tensor(xs_h.ravel(), device=dev), "y": torch.as_tensor(ys_h.ravel(), device=dev)}
+    loss = torch.zeros(nets, dtype=torch.float64, device=dev)
+    bar_out = torch.ones(nets, dtype=torch.float64, device=dev)
+    bar_w = torch.zeros(nets * 24, dtype=torch.float64, device=dev)
+    lanes = nets * s
+    loss_bytes = 16.0 + (24 + 8 + 1) * 8.0 / s
+    grad_bytes = 16.0 + (24 + 8 + 1 + 24) * 8.0 / s
+    t0 = time.perf_counter()
+    oracle.net_axis(w_h[:1024], xs_h[:1024], ys_h[:1024], mask_h[:1024])
+    cpu = 1024 * s / (time.perf_counter() - t0)
+    for suffix in ("", "_ordered"):
+        kl = runtime.load(BUNDLES, f"net_loss_{s}{suffix}", "float64", local)
+        kg = runtime.load(BUNDLES, f"net_grad_{s}{suffix}", "float64", local)
+        record(f"net_loss_{s}{suffix}", lanes, timed(lambda: runtime.run(kl, out=loss, **planes)), loss_bytes,
+               {"nets": nets})
+        record(f"net_grad_{s}{suffix}", lanes, timed(lambda: runtime.run(kg, bar_out=bar_out, bar_W=bar_w, **planes)),
+               grad_bytes, {"nets": nets, "cpu_baseline": {"lanes_per_s": cpu, "threads": 1, "sample_lanes": 1024 * s,
+                                                           "kind": "port (numpy, loss and gradient)"}})
+    return out
+
+
 # ------------------------------------------------------------ stepping kernels
 def run_steps(local: int, cpu_threads: int | None = None) -> dict:
     """The automatic stepping kernels integrated to completion: every sample from
@@ -908,6 +1018,7 @@ def main() -> int:
         configs = run_configs(local)
         configs["stepping"] = run_steps(local)
         configs["team"] = run_team(local)
+        configs["keyed"] = run_keyed(local)
     cpu = cpu_baseline(args.mode, args.cpu_sample) if (rank == 0 and world == 1) else None
     if rank == 0:
         line = {

@@ -122,49 +122,12 @@ extern "C" __global__ void __launch_bounds__(32) ordered_hist_3(
             if (hawk_cells <= 1024) {
                 for (std::size_t hawk_j = static_cast<std::size_t>(hawk_tm.rank); hawk_j < static_cast<std::size_t>(hawk_cells); hawk_j += static_cast<std::size_t>(hawk_tm.size)) hawk_bin[hawk_j] = Real(0);
                 hawk_tm.sync();
-                if (hawk_tm.rank < 32) {
-                    const unsigned hawk_ln = static_cast<unsigned>(hawk_tm.rank);
-                    const std::size_t hawk_end = hawk_hi * 1;
-                    for (std::size_t hawk_b = hawk_lo * 1; hawk_b < hawk_end; hawk_b += 32) {
-                        const std::size_t hawk_r = hawk_b + hawk_ln;
-                        const bool hawk_in = hawk_r < hawk_end;
-                        const std::int32_t hawk_mk = hawk_in ? hawk_k[hawk_r] : -1;
-                        const Real hawk_mv = hawk_in ? hawk_v[hawk_r] : Real{};
-                        unsigned hawk_mine = 0u, hawk_bad = 0u;
-                        for (unsigned hawk_i = 0; hawk_i < 32; ++hawk_i) {
-                            const std::int32_t hawk_key = __shfl_sync(0xffffffffu, hawk_mk, hawk_i);
-                            if (hawk_key == -1) continue;
-                            if (hawk_key >= 0 && hawk_key < hawk_cells) {
-                                if ((static_cast<unsigned>(hawk_key) & 31u) == hawk_ln) hawk_mine |= 1u << hawk_i;
-                            } else hawk_bad = 1u;
-                        }
-                        if (hawk_bad && hawk_ln == 0) hawk_m[1 + hawk_lane] = 1;
-                        while (__any_sync(0xffffffffu, hawk_mine != 0u)) {
-                            const unsigned hawk_src = hawk_mine != 0u ? static_cast<unsigned>(__ffs(hawk_mine) - 1) : 0u;
-                            const Real hawk_x = __shfl_sync(0xffffffffu, hawk_mv, hawk_src);
-                            const std::int32_t hawk_key = __shfl_sync(0xffffffffu, hawk_mk, hawk_src);
-                            if (hawk_mine != 0u) {
-                                hawk_bin[hawk_key] += hawk_x;
-                                hawk_mine &= hawk_mine - 1u;
-                            }
-                        }
-                        if (hawk_in && hawk_mk != -1) hawk_k[hawk_r] = -1;
-                    }
-                }
+                hk::linalg::team::scatterWalk<Real>(hawk_tm, hawk_lo * 1, hawk_hi * 1, hawk_k, hawk_v, hawk_bin, 1, hawk_m + 1 + hawk_lane, hawk_cells);
                 hawk_tm.sync();
                 for (std::size_t hawk_j = static_cast<std::size_t>(hawk_tm.rank); hawk_j < static_cast<std::size_t>(hawk_cells); hawk_j += static_cast<std::size_t>(hawk_tm.size))
                     hawk_p[hawk_j * hawk_chunks + static_cast<std::size_t>(hawk_lane)] += hawk_bin[hawk_j];
             } else {
-            if (hawk_tm.rank == 0)
-                for (std::size_t hawk_r = hawk_lo * 1; hawk_r < hawk_hi * 1; ++hawk_r) {
-                    const std::int32_t hawk_key = hawk_k[hawk_r];
-                    if (hawk_key == -1) continue;
-                    if (hawk_key >= 0 && hawk_key < hawk_cells)
-                        hawk_p[static_cast<std::size_t>(hawk_key) * hawk_chunks + static_cast<std::size_t>(hawk_lane)] += hawk_v[hawk_r];
-                    else
-                        hawk_m[1 + hawk_lane] = 1;
-                    hawk_k[hawk_r] = -1;
-                }
+            hk::linalg::team::scatterWalk<Real>(hawk_tm, hawk_lo * 1, hawk_hi * 1, hawk_k, hawk_v, hawk_p + static_cast<std::size_t>(hawk_lane), hawk_chunks, hawk_m + 1 + hawk_lane, hawk_cells);
             hawk_tm.sync();
             }
             #else

@@ -44,12 +44,7 @@ extern "C" __global__ void __launch_bounds__(32) ordered_total(
             Real hawk_sh[1024];
             #endif
             #if defined(__CUDA_ARCH__)
-            for (std::size_t hawk_t = static_cast<std::size_t>(hawk_tm.rank); hawk_t < 1024; hawk_t += static_cast<std::size_t>(hawk_tm.size)) {
-                Real hawk_s = Real(0);
-                for (std::size_t hawk_r = hawk_grp * 1024 + hawk_t; hawk_r < hawk_rows; hawk_r += 65536)
-                    hawk_s += hawk_u[hawk_r];
-                hawk_sh[hawk_t] = hawk_s;
-            }
+            hk::linalg::team::orderedPart<Real>(hawk_tm, hawk_u, hawk_rows, hawk_grp, hawk_sh);
             #else
             for (std::size_t hawk_t = 0; hawk_t < 1024; ++hawk_t) hawk_sh[hawk_t] = Real(0);
             for (std::size_t hawk_b = hawk_grp * 1024; hawk_b < hawk_rows; hawk_b += 65536) {
@@ -59,13 +54,13 @@ extern "C" __global__ void __launch_bounds__(32) ordered_total(
                     hawk_sh[hawk_t] += hawk_u[hawk_r];
                 }
             }
-            #endif
             hawk_tm.sync();
             for (std::size_t hawk_w = 512; hawk_w > 0; hawk_w >>= 1) {
                 for (std::size_t hawk_i = static_cast<std::size_t>(hawk_tm.rank); hawk_i < hawk_w; hawk_i += static_cast<std::size_t>(hawk_tm.size))
                     hawk_sh[hawk_i] += hawk_sh[hawk_i + hawk_w];
                 hawk_tm.sync();
             }
+            #endif
             if (hawk_tm.rank == 0) wout_tmb0_gp.data()[hawk_key * 64 + hawk_grp] = hawk_sh[0];
             hawk_tm.sync();
         }

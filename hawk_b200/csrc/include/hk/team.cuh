@@ -903,6 +903,106 @@ HK_FI T luDet(const TeamLu<T, N>& f) {
 
 #endif  // __CUDACC__
 
+// ------------------------------------------------------ ordered sum, part 1
+
+#if defined(__CUDA_ARCH__)
+// One group of a plain ordered sum's first stage (hawk/emit/team.py:208-240):
+// virtual lane t of group g adds the key's rows g * 1024 + t, + 65536, ... in
+// order from +0, and the group's 1024 values fold by the halving tree
+// s[i] += s[i + w] into sh[0].  A virtual lane past the key's rows holds +0,
+// and a sum started at +0 is never -0 under round to nearest, so adding it is
+// exact: the tree over the first `span` slots (the power of two covering the
+// group's lanes that hold rows) makes the same bits as the tree over all
+// 1024, and a group with no rows is +0 -- a key of 40 rows folds 64 slots in
+// one group, not 64 groups of 1024.
+template <class T>
+HK_FI void orderedPart(const Team& tm, const T* u, std::size_t rows, std::size_t grp, T* sh) {
+    const std::size_t first = grp * 1024;
+    const std::size_t live = rows > first ? (rows - first < 1024 ? rows - first : 1024) : 0;
+    if (live == 0) {
+        if (tm.rank == 0) sh[0] = T(0);
+        tm.sync();
+        return;
+    }
+    std::size_t span = 1;
+    while (span < live) span <<= 1;
+    for (std::size_t t = static_cast<std::size_t>(tm.rank); t < span; t += static_cast<std::size_t>(tm.size)) {
+        T acc = T(0);
+        for (std::size_t r = first + t; r < rows; r += 65536) acc += u[r];
+        sh[t] = acc;
+    }
+    tm.sync();
+    for (std::size_t w = span >> 1; w > 0; w >>= 1) {
+        for (std::size_t i = static_cast<std::size_t>(tm.rank); i < w; i += static_cast<std::size_t>(tm.size))
+            sh[i] += sh[i + w];
+        tm.sync();
+    }
+}
+#endif
+
+// ------------------------------------------------------- ordered scatter walk
+
+#if defined(__CUDA_ARCH__)
+// The walk of one lane chunk of an ordered scatter (hawk/emit/team.py:340-436)
+// on one warp: log slots [lo, hi) in order, 32 a batch, eight batches loaded
+// ahead.  The lanes of a batch holding the same key meet in one
+// __match_any_sync group; the group's lowest lane adds the group's values into
+// the key's bin in slot order.  So every bin gets its slots' values in slot
+// order from its start -- the serial walk's operations, the same bits -- and a
+// batch costs one match and as many shuffle rounds as its largest group, not
+// 32 broadcasts.  A key outside [0, cells) other than the skip key -1 adds
+// nothing and sets `*flag`; every slot read is put back to -1.  The bin of key
+// c is bin[c * stride]: the caller's shared bins (stride 1, up to 1024 cells),
+// or the chunk's own column of the zeroed partial sums (stride = the chunk
+// count), which a sum started at +0 reaches with the same bits.  One team
+// (warp) per chunk.
+template <class T>
+HK_FI void scatterWalk(const Team& tm, std::size_t lo, std::size_t hi, std::int32_t* k, const T* v, T* bin,
+                       std::size_t stride, std::int32_t* flag, std::int64_t cells) {
+    constexpr int kAhead = 8;
+    const unsigned full = 0xffffffffu;
+    const unsigned ln = static_cast<unsigned>(tm.rank) & 31u;
+    unsigned bad = 0u;
+    for (std::size_t b0 = lo; b0 < hi; b0 += 32 * kAhead) {
+        std::int32_t key[kAhead];
+        T val[kAhead];
+#pragma unroll
+        for (int a = 0; a < kAhead; ++a) {
+            const std::size_t r = b0 + static_cast<std::size_t>(a) * 32 + ln;
+            const bool in = r < hi;
+            key[a] = in ? k[r] : -1;
+            val[a] = in ? v[r] : T(0);
+        }
+#pragma unroll
+        for (int a = 0; a < kAhead; ++a) {
+            const bool good = key[a] >= 0 && key[a] < cells;
+            bad |= (!good && key[a] != -1) ? 1u : 0u;
+            const unsigned grp = __match_any_sync(full, good ? key[a] : -1);
+            const bool lead = good && ln == static_cast<unsigned>(__ffs(grp) - 1);
+            unsigned rest = lead ? grp : 0u;
+            T acc = lead ? bin[static_cast<std::size_t>(key[a]) * stride] : T(0);
+            while (__any_sync(full, rest != 0u)) {
+                const int src = rest != 0u ? __ffs(rest) - 1 : static_cast<int>(ln);
+                const T x = __shfl_sync(full, val[a], src);
+                if (rest != 0u) {
+                    acc = acc + x;
+                    rest &= rest - 1u;
+                }
+            }
+            if (lead) bin[static_cast<std::size_t>(key[a]) * stride] = acc;
+            __syncwarp();           // the next batch's leader of a key reads this bin
+        }
+#pragma unroll
+        for (int a = 0; a < kAhead; ++a) {
+            const std::size_t r = b0 + static_cast<std::size_t>(a) * 32 + ln;
+            if (r < hi && key[a] != -1) k[r] = -1;
+        }
+    }
+    if (__any_sync(full, bad != 0u) && ln == 0u) *flag = 1;
+    __syncwarp();
+}
+#endif
+
 }  // namespace team
 }  // namespace linalg
 }  // namespace hk

@@ -139,6 +139,11 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
             if "hawk_map" in body:
                 raise HawkError(f"{name!r}: a block sum over an index map (an active-set build) is not built "
                                 "on the b200 target")
+            for step in member.team.steps:
+                if step.op == "scatter_chunks":
+                    body = _scatter_walk(body, int(step.n), member.name)
+                if step.op == "block_part":
+                    body = _ordered_part(body)
         else:                       # a copy stage: the stage's own sinks, a block per lane
             from hawk.emit.render import render_body
 
@@ -172,6 +177,61 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
                 notes={"dynamic_smem": 0, "staged": False, "stages": 0, "min_blocks": 0, "persist": None,
                        "step_fp64_ops": None, "lane_refill": False, "folds": {}})
     return unit, stages, block, members
+
+
+def _ordered_part(body: str) -> str:
+    """A plain ordered sum's first stage with its device fill and tree (the
+    reference's 1024 virtual lanes a group, hawk/emit/team.py:208-240)
+    replaced by ``hk::linalg::team::orderedPart``, which folds only the slots
+    that can hold rows: the same bits.  A product of two planes' rows keeps
+    the reference's form."""
+    lines = body.split("\n")
+    fill = next((i for i, ln in enumerate(lines) if ln.strip().startswith(
+        "for (std::size_t hawk_t = static_cast<std::size_t>(hawk_tm.rank); hawk_t < 1024;")), None)
+    if fill is None or lines[fill - 1].strip() != "#if defined(__CUDA_ARCH__)" \
+            or lines[fill + 3].strip() != "hawk_s += hawk_u[hawk_r];":
+        return body
+    host = next(i for i in range(fill, len(lines)) if lines[i].strip() == "#else")
+    endif = next(i for i in range(host, len(lines)) if lines[i].strip() == "#endif")
+    tree = next(i for i in range(endif, len(lines))
+                if lines[i].strip() == "for (std::size_t hawk_w = 512; hawk_w > 0; hawk_w >>= 1) {")
+    if lines[endif + 1].strip() != "hawk_tm.sync();" or lines[tree + 4].strip() != "}":
+        return body
+    indent = lines[fill - 1][:len(lines[fill - 1]) - len(lines[fill - 1].lstrip())]
+    device = [lines[fill - 1],
+              f"{indent}hk::linalg::team::orderedPart<Real>(hawk_tm, hawk_u, hawk_rows, hawk_grp, hawk_sh);",
+              lines[host], *lines[host + 1:endif], lines[endif + 1], *lines[tree:tree + 5], lines[endif]]
+    return "\n".join(lines[:fill - 1] + device + lines[tree + 5:])
+
+
+def _scatter_walk(body: str, slots: int, entry: str) -> str:
+    """An ordered scatter's chunk stage with its device walk (the reference's
+    warp walk of 32 broadcasts a batch, hawk/emit/team.py:359-436) replaced by
+    ``hk::linalg::team::scatterWalk``: the same slots in the same order into
+    the same shared bins, so the same bits, with one match a batch."""
+    lines = body.split("\n")
+    start = next((i for i, ln in enumerate(lines) if ln.strip() == "if (hawk_tm.rank < 32) {"), None)
+    if start is None:
+        raise HawkError(f"{entry!r}: the ordered scatter's chunk walk is not where the b200 target expects it")
+    end = next((i for i in range(start + 1, len(lines)) if lines[i].strip() == "hawk_tm.sync();"), None)
+    if end is None or "hawk_bin[hawk_key] += hawk_x;" not in "\n".join(lines[start:end]):
+        raise HawkError(f"{entry!r}: the ordered scatter's chunk walk is not the plain-real form the b200 "
+                        "target replaces")
+    indent = lines[start][:len(lines[start]) - len(lines[start].lstrip())]
+    call = (f"{indent}hk::linalg::team::scatterWalk<Real>(hawk_tm, hawk_lo * {slots}, hawk_hi * {slots}, hawk_k, "
+            "hawk_v, hawk_bin, 1, hawk_m + 1 + hawk_lane, hawk_cells);")
+    lines = lines[:start] + [call] + lines[end:]
+    # the device branch's serial walk of a target above 1024 cells: the same
+    # walk with the chunk's column of partial sums as its bins
+    serial = next((i for i in range(start + 1, len(lines)) if lines[i].strip() == "if (hawk_tm.rank == 0)"), None)
+    host = next((i for i in range(start + 1, len(lines)) if lines[i].strip() == "#else"), None)
+    if serial is None or host is None or serial > host:
+        raise HawkError(f"{entry!r}: the ordered scatter's serial walk is not where the b200 target expects it")
+    stop = next(i for i in range(serial + 1, host) if lines[i].strip() == "hawk_tm.sync();")
+    indent = lines[serial][:len(lines[serial]) - len(lines[serial].lstrip())]
+    wide = (f"{indent}hk::linalg::team::scatterWalk<Real>(hawk_tm, hawk_lo * {slots}, hawk_hi * {slots}, hawk_k, "
+            "hawk_v, hawk_p + static_cast<std::size_t>(hawk_lane), hawk_chunks, hawk_m + 1 + hawk_lane, hawk_cells);")
+    return "\n".join(lines[:serial] + [wide] + lines[stop:])
 
 
 def _slot_records(walk) -> list:
