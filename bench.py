@@ -992,7 +992,8 @@ def main() -> int:
     ap.add_argument("--mode", default="float64", choices=("float64", "float32"))
     ap.add_argument("--no-configs", action="store_true", help="skip the per-config table")
     ap.add_argument("--cpu-sample", type=int, default=1 << 23)
-    ap.add_argument("--only", default=None, help="time one benchmark kernel at --n samples (profiling runs)")
+    ap.add_argument("--only", default=None, help="time one benchmark kernel at --n samples (profiling runs); "
+                    "'keyed': the ordered stages and the net axis")
     ap.add_argument("--persist", action="store_true",
                     help="with --only oscillator|orbit: the persistent entry, every sample to its finish")
     args = ap.parse_args()
@@ -1003,6 +1004,10 @@ def main() -> int:
         return 0
     import torch
 
+    if args.only == "keyed":
+        torch.cuda.set_device(local)
+        print(json.dumps(run_keyed(local)), flush=True)
+        return 0
     if args.only in ("oscillator", "orbit"):
         print(json.dumps(run_only_steps(args.only, args.n, args.steps, args.warmup, local, args.persist)),
               flush=True)
