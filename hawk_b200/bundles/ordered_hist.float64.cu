@@ -107,42 +107,8 @@ extern "C" __global__ void __launch_bounds__(32) ordered_hist_3(
         (void)nSamples;
         const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here();
         const long long hawk_lane = hawk_i;
-        {  // scatter_chunks, n = 1
-            const std::size_t hawk_chunks = static_cast<std::size_t>(count);
-            const std::size_t hawk_span = (static_cast<std::size_t>(nSamples) + hawk_chunks - 1) / hawk_chunks;
-            const std::size_t hawk_lo = static_cast<std::size_t>(hawk_lane) * hawk_span;
-            const std::size_t hawk_hi = hawk_lo + hawk_span < static_cast<std::size_t>(nSamples) ? hawk_lo + hawk_span : static_cast<std::size_t>(nSamples);
-            std::int32_t* const hawk_k = const_cast<std::int32_t*>(wout_tms_acc_k.data());
-            const Real* const hawk_v = wout_tms_acc_v.data();
-            Real* const hawk_p = wout_tms_acc_p.data();
-            std::int32_t* const hawk_m = const_cast<std::int32_t*>(wout_tms_acc_m.data());
-            const std::int64_t hawk_cells = hawk_m[0];
-            #if defined(__CUDA_ARCH__)
-            __shared__ Real hawk_bin[1024];
-            if (hawk_cells <= 1024) {
-                for (std::size_t hawk_j = static_cast<std::size_t>(hawk_tm.rank); hawk_j < static_cast<std::size_t>(hawk_cells); hawk_j += static_cast<std::size_t>(hawk_tm.size)) hawk_bin[hawk_j] = Real(0);
-                hawk_tm.sync();
-                hk::linalg::team::scatterWalk<Real>(hawk_tm, hawk_lo * 1, hawk_hi * 1, hawk_k, hawk_v, hawk_bin, 1, hawk_m + 1 + hawk_lane, hawk_cells);
-                hawk_tm.sync();
-                for (std::size_t hawk_j = static_cast<std::size_t>(hawk_tm.rank); hawk_j < static_cast<std::size_t>(hawk_cells); hawk_j += static_cast<std::size_t>(hawk_tm.size))
-                    hawk_p[hawk_j * hawk_chunks + static_cast<std::size_t>(hawk_lane)] += hawk_bin[hawk_j];
-            } else {
-            hk::linalg::team::scatterWalk<Real>(hawk_tm, hawk_lo * 1, hawk_hi * 1, hawk_k, hawk_v, hawk_p + static_cast<std::size_t>(hawk_lane), hawk_chunks, hawk_m + 1 + hawk_lane, hawk_cells);
-            hawk_tm.sync();
-            }
-            #else
-            if (hawk_tm.rank == 0)
-                for (std::size_t hawk_r = hawk_lo * 1; hawk_r < hawk_hi * 1; ++hawk_r) {
-                    const std::int32_t hawk_key = hawk_k[hawk_r];
-                    if (hawk_key == -1) continue;
-                    if (hawk_key >= 0 && hawk_key < hawk_cells)
-                        hawk_p[static_cast<std::size_t>(hawk_key) * hawk_chunks + static_cast<std::size_t>(hawk_lane)] += hawk_v[hawk_r];
-                    else
-                        hawk_m[1 + hawk_lane] = 1;
-                    hawk_k[hawk_r] = -1;
-                }
-            hawk_tm.sync();
-            #endif
+        {  // scatter_chunks, n = 1: 8 warps a chunk
+            hk::linalg::team::scatterChunk<Real, 8>(hawk_tm, hawk_lane, count, nSamples, 1, wout_tms_acc_k.data(), wout_tms_acc_v.data(), wout_tms_acc_p.data(), const_cast<std::int32_t*>(wout_tms_acc_m.data()));
         }
         __syncwarp();
     }

@@ -944,21 +944,17 @@ HK_FI void orderedPart(const Team& tm, const T* u, std::size_t rows, std::size_t
 
 #if defined(__CUDA_ARCH__)
 // The walk of one lane chunk of an ordered scatter (hawk/emit/team.py:340-436)
-// on one warp: log slots [lo, hi) in order, 32 a batch, eight batches loaded
-// ahead.  The lanes of a batch holding the same key meet in one
-// __match_any_sync group; the group's lowest lane adds the group's values into
-// the key's bin in slot order.  So every bin gets its slots' values in slot
-// order from its start -- the serial walk's operations, the same bits -- and a
-// batch costs one match and as many shuffle rounds as its largest group, not
-// 32 broadcasts.  A key outside [0, cells) other than the skip key -1 adds
-// nothing and sets `*flag`; every slot read is put back to -1.  The bin of key
-// c is bin[c * stride]: the caller's shared bins (stride 1, up to 1024 cells),
-// or the chunk's own column of the zeroed partial sums (stride = the chunk
-// count), which a sum started at +0 reaches with the same bits.  One team
-// (warp) per chunk.
+// on one warp, for the keys it owns (key % G == g): log slots [lo, hi) in
+// order, 32 a batch, eight batches loaded ahead.  The lanes of a batch holding
+// the same owned key meet in one __match_any_sync group; the group's lowest
+// lane adds the group's values into the key's bin in slot order.  So every
+// bin gets its slots' values in slot order from its start -- the serial
+// walk's operations, the same bits.  The bin of key c is
+// bin[(c / div) * stride].  A key outside [0, cells) other than the skip key
+// -1 adds nothing and sets `*flag`.
 template <class T>
-HK_FI void scatterWalk(const Team& tm, std::size_t lo, std::size_t hi, std::int32_t* k, const T* v, T* bin,
-                       std::size_t stride, std::int32_t* flag, std::int64_t cells) {
+HK_FI void scatterWalk(const Team& tm, std::size_t lo, std::size_t hi, const std::int32_t* k, const T* v, T* bin,
+                       std::size_t div, std::size_t stride, int G, int g, std::int32_t* flag, std::int64_t cells) {
     constexpr int kAhead = 8;
     const unsigned full = 0xffffffffu;
     const unsigned ln = static_cast<unsigned>(tm.rank) & 31u;
@@ -975,12 +971,14 @@ HK_FI void scatterWalk(const Team& tm, std::size_t lo, std::size_t hi, std::int3
         }
 #pragma unroll
         for (int a = 0; a < kAhead; ++a) {
-            const bool good = key[a] >= 0 && key[a] < cells;
-            bad |= (!good && key[a] != -1) ? 1u : 0u;
-            const unsigned grp = __match_any_sync(full, good ? key[a] : -1);
-            const bool lead = good && ln == static_cast<unsigned>(__ffs(grp) - 1);
+            const bool inside = key[a] >= 0 && key[a] < cells;
+            bad |= (!inside && key[a] != -1) ? 1u : 0u;
+            const bool mine = inside && (key[a] % G) == g;
+            const unsigned grp = __match_any_sync(full, mine ? key[a] : -1);
+            const bool lead = mine && ln == static_cast<unsigned>(__ffs(grp) - 1);
+            const std::size_t at = lead ? (static_cast<std::size_t>(key[a]) / div) * stride : 0;
             unsigned rest = lead ? grp : 0u;
-            T acc = lead ? bin[static_cast<std::size_t>(key[a]) * stride] : T(0);
+            T acc = lead ? bin[at] : T(0);
             while (__any_sync(full, rest != 0u)) {
                 const int src = rest != 0u ? __ffs(rest) - 1 : static_cast<int>(ln);
                 const T x = __shfl_sync(full, val[a], src);
@@ -989,17 +987,51 @@ HK_FI void scatterWalk(const Team& tm, std::size_t lo, std::size_t hi, std::int3
                     rest &= rest - 1u;
                 }
             }
-            if (lead) bin[static_cast<std::size_t>(key[a]) * stride] = acc;
+            if (lead) bin[at] = acc;
             __syncwarp();           // the next batch's leader of a key reads this bin
-        }
-#pragma unroll
-        for (int a = 0; a < kAhead; ++a) {
-            const std::size_t r = b0 + static_cast<std::size_t>(a) * 32 + ln;
-            if (r < hi && key[a] != -1) k[r] = -1;
         }
     }
     if (__any_sync(full, bad != 0u) && ln == 0u) *flag = 1;
     __syncwarp();
+}
+
+// An ordered scatter's chunk stage (hawk/ir/team.py:716-736) with G warps a
+// chunk: team `lane` is warp g = lane % G of chunk lane / G (of count / G
+// chunks over nSamples lanes, `slots` log slots a lane).  Warp g owns the
+// keys c with c % G == g: up to 1024 cells in its shared bins (bin c / G),
+// added onto the chunk's partial sum of each owned key afterwards; above
+// that, in the chunk's column of the partial sums (zeroed by the first
+// stage) directly.  Each partial sum is its chunk's values of the key in
+// slot order from +0, as the reference's one warp a chunk makes it; the G
+// warps only split the keys.  The slots are not put back to -1: the runtime
+// refills the key log with -1 before every run (the plane's fill).  One team
+// (warp) per block: the bins are the block's.
+template <class T, int G>
+HK_FI void scatterChunk(const Team& tm, long long lane, long long count, long long n_samples, int slots,
+                        const std::int32_t* k, const T* v, T* p, std::int32_t* m) {
+    __shared__ T bin[(1024 + G - 1) / G];
+    const std::size_t chunks = static_cast<std::size_t>(count) / G;
+    const std::size_t chunk = static_cast<std::size_t>(lane) / G;
+    const int g = static_cast<int>(static_cast<std::size_t>(lane) % G);
+    const std::size_t n = static_cast<std::size_t>(n_samples);
+    const std::size_t span = (n + chunks - 1) / chunks;
+    const std::size_t lo = chunk * span;
+    const std::size_t hi = lo + span < n ? lo + span : n;
+    const std::int64_t cells = m[0];
+    std::int32_t* const flag = m + 1 + chunk;
+    const std::size_t s = static_cast<std::size_t>(slots);
+    if (cells <= 1024) {
+        for (int j = tm.rank; j < (1024 + G - 1) / G; j += tm.size) bin[j] = T(0);
+        tm.sync();
+        scatterWalk<T>(tm, lo * s, hi * s, k, v, bin, G, 1, G, g, flag, cells);
+        tm.sync();
+        for (std::int64_t c = g + static_cast<std::int64_t>(G) * tm.rank; c < cells;
+             c += static_cast<std::int64_t>(G) * tm.size)
+            p[static_cast<std::size_t>(c) * chunks + chunk] += bin[static_cast<std::size_t>(c) / G];
+    } else {
+        scatterWalk<T>(tm, lo * s, hi * s, k, v, p + chunk, 1, chunks, G, g, flag, cells);
+    }
+    tm.sync();
 }
 #endif
 

@@ -488,7 +488,8 @@ class SplitKernel:
             keyed = record["keyed"]
             return self.keyed_size(keyed, n) // int(keyed.get("width", 1)) * int(record.get("groups") or 1)
         if kind == "chunks":
-            return self.scatter_chunks(n, sizes[record["of"]])
+            # the b200 chunk stage walks each chunk with ``groups`` warps (one per key residue)
+            return self.scatter_chunks(n, sizes[record["of"]]) * int(record.get("groups") or 1)
         if kind == "targets":
             return sizes[record["of"]]
         return count

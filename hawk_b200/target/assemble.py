@@ -47,7 +47,7 @@ _UNBUILT = {
 #: The team-form calls the device library builds (hk/team.cuh).
 TEAM_BUILT = frozenset({"Team", "TeamCholesky", "TeamLu", "cholesky", "choleskyFrom", "choSolve", "triLower",
                         "triUpperT", "lu", "luSolve", "luSolveT", "luInverse", "luDet", "blockSum",
-                        "TeamEigh", "eigh", "TeamQr", "qr", "qrSolve", "qrGramSolve", "scatterWalk",
+                        "TeamEigh", "eigh", "TeamQr", "qr", "qrSolve", "qrGramSolve", "scatterChunk",
                         "orderedPart"})
 _TEAM_NAME = re.compile(r"hk::linalg::team::(\w+)")
 

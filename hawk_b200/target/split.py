@@ -140,17 +140,23 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
                 raise HawkError(f"{name!r}: a block sum over an index map (an active-set build) is not built "
                                 "on the b200 target")
             for step in member.team.steps:
-                if step.op == "scatter_chunks":
-                    body = _scatter_walk(body, int(step.n), member.name)
                 if step.op == "block_part":
                     body = _ordered_part(body)
+            chunked = [st for st in member.team.steps if st.op == "scatter_chunks"]
+            if chunked:
+                if len(member.team.steps) != 1:
+                    raise HawkError(f"{name!r}: stage {member.name!r} walks an ordered scatter's chunks beside "
+                                    "other steps, which the b200 target does not build")
+                body, threads = _scatter_chunk_body(chunked[0]), 32     # the bins are the block's
         else:                       # a copy stage: the stage's own sinks, a block per lane
             from hawk.emit.render import render_body
 
             body = body_text(render_body(member.sinks, walk, indent="        ", writer=B200_WRITER).text)
             smem = 0
         refuse_unbuilt(member.name, body)
-        team_record = record.get("team") or {}
+        team_record = dict(record.get("team") or {})
+        if isinstance(member, TeamStage) and any(st.op == "scatter_chunks" for st in member.team.steps):
+            team_record["groups"] = SCATTER_WARPS       # teams a chunk (hk::linalg::team::scatterChunk)
         spans = team_record.get("grid", "lanes") != "lanes"
         parts += [
             f'extern "C" __device__ const unsigned int hk_team_threads__{member.name} = {threads}u;',
@@ -204,34 +210,29 @@ def _ordered_part(body: str) -> str:
     return "\n".join(lines[:fill - 1] + device + lines[tree + 5:])
 
 
-def _scatter_walk(body: str, slots: int, entry: str) -> str:
-    """An ordered scatter's chunk stage with its device walk (the reference's
-    warp walk of 32 broadcasts a batch, hawk/emit/team.py:359-436) replaced by
-    ``hk::linalg::team::scatterWalk``: the same slots in the same order into
-    the same shared bins, so the same bits, with one match a batch."""
-    lines = body.split("\n")
-    start = next((i for i, ln in enumerate(lines) if ln.strip() == "if (hawk_tm.rank < 32) {"), None)
-    if start is None:
-        raise HawkError(f"{entry!r}: the ordered scatter's chunk walk is not where the b200 target expects it")
-    end = next((i for i in range(start + 1, len(lines)) if lines[i].strip() == "hawk_tm.sync();"), None)
-    if end is None or "hawk_bin[hawk_key] += hawk_x;" not in "\n".join(lines[start:end]):
-        raise HawkError(f"{entry!r}: the ordered scatter's chunk walk is not the plain-real form the b200 "
-                        "target replaces")
-    indent = lines[start][:len(lines[start]) - len(lines[start].lstrip())]
-    call = (f"{indent}hk::linalg::team::scatterWalk<Real>(hawk_tm, hawk_lo * {slots}, hawk_hi * {slots}, hawk_k, "
-            "hawk_v, hawk_bin, 1, hawk_m + 1 + hawk_lane, hawk_cells);")
-    lines = lines[:start] + [call] + lines[end:]
-    # the device branch's serial walk of a target above 1024 cells: the same
-    # walk with the chunk's column of partial sums as its bins
-    serial = next((i for i in range(start + 1, len(lines)) if lines[i].strip() == "if (hawk_tm.rank == 0)"), None)
-    host = next((i for i in range(start + 1, len(lines)) if lines[i].strip() == "#else"), None)
-    if serial is None or host is None or serial > host:
-        raise HawkError(f"{entry!r}: the ordered scatter's serial walk is not where the b200 target expects it")
-    stop = next(i for i in range(serial + 1, host) if lines[i].strip() == "hawk_tm.sync();")
-    indent = lines[serial][:len(lines[serial]) - len(lines[serial].lstrip())]
-    wide = (f"{indent}hk::linalg::team::scatterWalk<Real>(hawk_tm, hawk_lo * {slots}, hawk_hi * {slots}, hawk_k, "
-            "hawk_v, hawk_p + static_cast<std::size_t>(hawk_lane), hawk_chunks, hawk_m + 1 + hawk_lane, hawk_cells);")
-    return "\n".join(lines[:serial] + [wide] + lines[stop:])
+#: Warps a lane chunk of an ordered scatter is walked by (each owns the keys
+#: of one residue mod this): the reference fixes the chunks at up to 256, so
+#: one warp a chunk leaves most of the GPU idle.
+SCATTER_WARPS = 8
+
+
+def _scatter_chunk_body(step) -> str:
+    """The ordered scatter's chunk stage (the reference's text,
+    hawk/emit/team.py:340-436, walks a chunk on one warp with 32 broadcasts
+    a batch) as ``hk::linalg::team::scatterChunk``: SCATTER_WARPS warps a
+    chunk, each owning the keys of one residue, one match a batch -- each
+    partial sum the same operations in the same order, so the same bits."""
+    from hawk.emit.spelling import binding_name
+
+    planes = dict(step.planes)
+    k, v, part, status = (binding_name("wide_out", planes[r]) for r in ("k", "v", "part", "status"))
+    return "\n".join([
+        "        const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here();",
+        "        const long long hawk_lane = hawk_i;",
+        f"        {{  // scatter_chunks, n = {int(step.n)}: {SCATTER_WARPS} warps a chunk",
+        f"            hk::linalg::team::scatterChunk<Real, {SCATTER_WARPS}>(hawk_tm, hawk_lane, count, nSamples, "
+        f"{int(step.n)}, {k}.data(), {v}.data(), {part}.data(), const_cast<std::int32_t*>({status}.data()));",
+        "        }"])
 
 
 def _slot_records(walk) -> list:
