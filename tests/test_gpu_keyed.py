@@ -200,3 +200,16 @@ def test_a_target_of_no_cells_reports_any_key_but_the_skip_key():
     with pytest.raises(HawkError, match=r"got a key outside \[0, 0\)"):
         scatter(key, x, np.zeros(0))
     scatter(np.full(n, -1, np.int32), x, np.zeros(0))
+
+
+def test_an_ordered_scatter_of_no_lanes_leaves_the_target_as_it_was():
+    acc = np.linspace(1.0, 2.0, 9)
+    got = scatter(np.zeros(0, np.int32), np.zeros(0), acc)
+    np.testing.assert_array_equal(got, acc)
+    np.testing.assert_array_equal(got, oracle.ordered_scatter(np.zeros(0, np.int32), np.zeros(0), acc)[0])
+
+
+def test_an_ordered_sum_over_no_keys_runs_no_team():
+    out = torch.zeros(0, dtype=torch.float64, device="cuda")
+    runtime.run(runtime.load(BUNDLES, "ordered_total"), x=dev(np.zeros(0)), out=out)
+    assert host(out).shape == (0,)
