@@ -453,6 +453,13 @@ def team_lu_160(A: Matrix[160, 160], b: Vector[160], x: Mutable[Vector[160]], de
     info = status
 
 
+@hawk.kernel
+def warp_eigvals_32(A: Matrix[32, 32], w: Mutable[Vector[32]], info: Mutable[Int32]):
+    vals, _vecs, status = m.eigh(A)
+    w = vals
+    info = status
+
+
 #: The team-form kernels: per sample, Cholesky solves (x, X, the factor L and
 #: its status) and LU solves with partial pivoting (x, X, det(A) -- its own
 #: factor, as hawk.math.det spells it -- and the status), at sizes above the
@@ -462,7 +469,7 @@ def team_lu_160(A: Matrix[160, 160], b: Vector[160], x: Mutable[Vector[160]], de
 #: in its scratch plane.
 TEAM_KERNELS = {k.name: k for k in (team_chol_33, team_lu_33, team_chol_64, team_lu_64, team_chol_128,
                                     team_lu_128, team_chol_from_64, team_chol_512, team_lu_160, team_eigh_40,
-                                    team_lstsq_40)}
+                                    team_lstsq_40, warp_eigvals_32)}
 
 
 #: Every kernel the bundles hold, by name, with the scalar modes each is built in.
@@ -488,7 +495,8 @@ KERNELS = {
     "keyed_sum": (keyed_sum, ("float64",)),
     "histogram": (histogram, ("float64",)),
     "bitmask": (bitmask, ("float64",)),
-    **{name: (k, ("float64",)) for name, k in TEAM_KERNELS.items()},
+    **{name: (k, ("float64", "float32") if name == "warp_eigvals_32" else ("float64",))
+       for name, k in TEAM_KERNELS.items()},
     **{name: (k, ("float64",)) for name, k in READBACK_KERNELS.items()},
     **{name: (k, ("float64",)) for name, k in KEYED_KERNELS.items()},
     **{name: (k, ("float64",)) for name, k in NET_KERNELS.items()},

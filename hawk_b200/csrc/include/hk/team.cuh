@@ -1036,5 +1036,122 @@ HK_FI void scatterChunk(const Team& tm, long long lane, long long count, long lo
 #endif
 
 }  // namespace team
+
+// ---------------------------------------------- the warp-form eigenvalues
+
+namespace warp {
+
+// The warp entry of an eigenvalues-only eigh (hawk/ir/team.py:236, the step
+// `eigh_warp` of hawk/emit/team.py:492-505): one warp a lane, the values and
+// the status of the one-thread form (hk/linalg.cuh eighValues: cyclic Jacobi,
+// ascending values, info bits 1 and 2) with each rotation's row and column
+// updates spread over the warp -- every element gets the one-thread form's
+// operations in its order, so the same bits.  The working matrix lives in the
+// block's shared scratch (one warp a block).
+template <class T> struct EighValuesScratch {
+    T s[32 * 32];
+    T w[32];
+    int info;
+};
+
+template <class T> struct EighValuesLane {
+    T w;            // this lane's eigenvalue (ascending by lane)
+    int info;
+};
+
+#if defined(__CUDA_ARCH__)
+template <int N, class T>
+HK_FI EighValuesLane<T> eighValues(EighValuesScratch<T>& sc, const T* a) {
+    static_assert(N >= 1 && N <= 32, "the warp form holds up to 32 x 32");
+    const T zero = T(0), one = T(1), half = T(0.5);
+    const T eps = linalg::EighEps<T>::value();
+    const int ln = static_cast<int>(threadIdx.x & 31u);
+    T* const s = sc.s;
+    for (int e = ln; e < N * N; e += 32) {
+        const int i = e / N, j = e % N;
+        s[e] = (j >= i) ? (half * a[i * N + j]) + (half * a[j * N + i]) : zero;
+    }
+    __syncwarp();
+    if (N == 1) {
+        if (ln == 0) {
+            sc.w[0] = a[0];
+            sc.info = 0;
+        }
+        __syncwarp();
+        return {ln < N ? sc.w[ln] : zero, sc.info};
+    }
+    // the lower half mirrors the upper and the Frobenius sum, in the fill's order: one lane
+    T fro2 = zero;
+    if (ln == 0) {
+        for (int i = 0; i < N; ++i)
+            for (int j = 0; j < N; ++j) {
+                if (j < i) s[i * N + j] = s[j * N + i];
+                fro2 = fro2 + (s[i * N + j] * s[i * N + j]);
+            }
+    }
+    __syncwarp();
+    for (int sweep = 0; sweep < linalg::eigh_sweeps(N); ++sweep)
+        for (int p = 0; p < N - 1; ++p)
+            for (int q = p + 1; q < N; ++q) {
+                const T app = s[p * N + p], aqq = s[q * N + q], apq = s[p * N + q];
+                __syncwarp();           // every lane has read the pivot block before it changes
+                if (!(math::abs(apq) <= (eps * math::sqrt(math::abs(app * aqq))))) {
+                    const T theta = (aqq - app) / (T(2) * apq);
+                    const T sg = (theta < zero) ? T(-1) : one;
+                    const T tn = sg / (math::abs(theta) + math::sqrt((theta * theta) + one));
+                    const T cs = one / math::sqrt((tn * tn) + one);
+                    const T sn = tn * cs;
+                    if (ln == 0) {
+                        s[p * N + p] = app - (tn * apq);
+                        s[q * N + q] = aqq + (tn * apq);
+                        s[p * N + q] = zero;
+                        s[q * N + p] = zero;
+                    }
+                    for (int k = ln; k < N; k += 32) {
+                        if ((k != p) && (k != q)) {
+                            const T akp = s[k * N + p], akq = s[k * N + q];
+                            const T np = (cs * akp) - (sn * akq);
+                            const T nq = (sn * akp) + (cs * akq);
+                            s[k * N + p] = np;
+                            s[p * N + k] = np;
+                            s[k * N + q] = nq;
+                            s[q * N + k] = nq;
+                        }
+                    }
+                }
+                __syncwarp();
+            }
+    if (ln == 0) {
+        int info = 0;
+        T off2 = zero;
+        for (int i = 0; i < N; ++i) {
+            sc.w[i] = s[i * N + i];
+            for (int j = 0; j < N; ++j)
+                if (j != i) off2 = off2 + (s[i * N + j] * s[i * N + j]);
+        }
+        const T tol = static_cast<T>(N) * eps;
+        if (!(off2 <= ((tol * tol) * fro2))) info = 1;
+        for (int i = 0; i < N - 1; ++i) {
+            int lo = i;
+            for (int j = i + 1; j < N; ++j)
+                if (sc.w[j] < sc.w[lo]) lo = j;
+            if (lo != i) {
+                const T tw = sc.w[i];
+                sc.w[i] = sc.w[lo];
+                sc.w[lo] = tw;
+            }
+        }
+        const T gap = tol * math::sqrt(fro2);
+        bool tight = false;
+        for (int i = 0; i < N - 1; ++i)
+            if (!((sc.w[i + 1] - sc.w[i]) > gap)) tight = true;
+        sc.info = tight ? info + 2 : info;
+    }
+    __syncwarp();
+    return {ln < N ? sc.w[ln] : zero, sc.info};
+}
+#endif
+
+}  // namespace warp
 }  // namespace linalg
 }  // namespace hk

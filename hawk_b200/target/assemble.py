@@ -36,7 +36,6 @@ _UNBUILT = {
     "hk::geometry::": "ray primitives",
     "hk::banded::": "the banded scalar mode",
     "hk::random::": "in-kernel random draws",
-    "hk::linalg::warp::": "the warp-form eigensolver (eighValues of n <= 32 under the team form)",
     "hawk_abi::mix_count": "auto dispatch branch counts",
     "hawk_abi::tiled": "wide (tiled) scratch planes",
     "hawk_abi::warp_sum": "warp-per-lane sums",

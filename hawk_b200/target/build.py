@@ -145,7 +145,7 @@ def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "flo
     from .split import expand
 
     name = name or kernel.name
-    if expand(kernel, name) is not None:
+    if expand(kernel, name, mode) is not None:
         return build_split_kernel(kernel, directory, name=name, mode=mode)
     directory = Path(directory)
     directory.mkdir(parents=True, exist_ok=True)

@@ -73,14 +73,33 @@ def team_geometry(spec, elem: int) -> tuple:
     return 32 * TEAM_WARPS_IN_PLACE, max(inplace) * TEAM_WARPS_IN_PLACE
 
 
-def expand(kernel, name: str):
+def expand(kernel, name: str, mode: str = "float64"):
     """``(members, block)``: the stage kernels and the reference's sidecar block
-    (stages, cells, team_planes), or None for a kernel that runs in one launch."""
+    (stages, cells, team_planes), or None for a kernel that runs in one launch.
+
+    A kernel that runs in one launch under the reference's general split may
+    still have a warp entry on a device-only sm_100 build (an eigenvalues-only
+    32 x 32 eigh, hawk/ir/team.py:236-275): then it is cut the way the
+    reference cuts it there, into a copy, an ``eigh_warp`` and a reader
+    stage."""
     from hawk.artifact.bundle import _expand_split
+    from hawk.emit import policy
+    from hawk.targets.cards import _BUILD_ARCH
+    from hawk.trace.kernel import TeamStage
 
     members, names, _kinds, blocks = _expand_split([kernel], [name], [None], device=True, device_only=False)
     block = blocks.get(name)
-    if block is None or len(members) < 2:
+    if block is not None and len(members) >= 2:
+        return members, block
+    token = _BUILD_ARCH.set("sm_100")
+    try:
+        with policy.using(scalar=mode, device_only=True):
+            members, names, _kinds, blocks = _expand_split([kernel], [name], [None], device=True, device_only=True)
+    finally:
+        _BUILD_ARCH.reset(token)
+    block = blocks.get(name)
+    warp = any(isinstance(mm, TeamStage) and any(st.op == "eigh_warp" for st in mm.team.steps) for mm in members)
+    if block is None or len(members) < 2 or not warp:
         return None
     return members, block
 
@@ -102,7 +121,7 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
 
     if mode not in MODES:
         raise HawkError(f"scalar mode {mode!r} is not built on the b200 target (built: {sorted(MODES)})")
-    found = expand(kernel, name)
+    found = expand(kernel, name, mode)
     if found is None:
         raise HawkError(f"{name!r} runs in one launch; it is not a split kernel")
     members, block = found

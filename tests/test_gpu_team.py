@@ -218,3 +218,42 @@ def test_team_lstsq_by_householder_qr():
         want = np.linalg.lstsq(J[lane], r[lane], rcond=None)[0]
         cond = np.linalg.cond(J[lane])
         assert np.abs(got["x"][:, lane] - want).max() <= 50 * n * EPS * cond * np.abs(want).max()
+
+
+@pytest.mark.parametrize("mode", ["float64", "float32"])
+def test_warp_form_eigenvalues_at_32(mode):
+    """An eigenvalues-only 32 x 32 eigh takes the reference's warp entry on a
+    device-only sm_100 build (hawk/ir/team.py:236-275): a copy stage, an
+    eigh_warp stage (one warp a lane, hk::linalg::warp::eighValues), a reader.
+    In float64 its values and status are the one-thread form's bits (the
+    oracle's); in float32 within the one-thread form's rounding of numpy's
+    float64 eigenvalues, and the repeated eigenvalue of lane 2 reported in bit 2."""
+    n, lanes = 32, 9
+    rng = np.random.default_rng(32)
+    mats = []
+    for lane in range(lanes):
+        g = rng.standard_normal((n, n))
+        a = (g + g.T) / 2
+        if lane == 2:
+            q, _ = np.linalg.qr(rng.standard_normal((n, n)))
+            a = (q * np.r_[np.ones(n // 2), np.linspace(2, 3, n - n // 2)]) @ q.T
+        mats.append(a)
+    dt = np.float64 if mode == "float64" else np.float32
+    A = np.ascontiguousarray(np.moveaxis(np.stack(mats), 0, -1)).astype(dt)
+    k = runtime.load(BUNDLES, "warp_eigvals_32", mode)
+    w = torch.full((n, lanes), float("nan"), dtype=torch.float64 if mode == "float64" else torch.float32,
+                   device="cuda")
+    info = nan(lanes, torch.int32)
+    runtime.run(k, A=dev(A), w=w, info=info)
+    got_w, got_info = host(w), host(info)
+    assert got_info[2] & 2
+    if mode == "float64":
+        want_w, _v, want_info = oracle.sym_eigen(A, vectors=False)
+        np.testing.assert_array_equal(got_info, want_info)
+        _exact(got_w, want_w)
+    else:
+        eps32 = np.finfo(np.float32).eps
+        for lane in range(lanes):
+            ref = np.linalg.eigvalsh(A[..., lane].astype(np.float64))
+            bound = 100 * n * eps32 * np.abs(A[..., lane]).max() * n
+            np.testing.assert_allclose(got_w[:, lane], ref, rtol=0, atol=bound)
