@@ -553,6 +553,8 @@ def run_team(local: int, cpu_threads: int | None = None) -> dict:
             sample = max(1, min(lanes, 256 if n == 64 else 64))
             sub = {key: np.ascontiguousarray(w[key][..., :sample]) for key in ("A", "b", "B")}
             fn = oracle.team_chol if kernel == "team_chol" else oracle.team_lu
+            one = {key: np.ascontiguousarray(w[key][..., :1]) for key in ("A", "b", "B")}
+            fn(one["A"], one["b"], one["B"])            # the oracle library loaded before the clock
             t0 = time.perf_counter()
             fn(sub["A"], sub["b"], sub["B"], threads=threads)
             cpu_s = time.perf_counter() - t0
@@ -564,6 +566,37 @@ def run_team(local: int, cpu_threads: int | None = None) -> dict:
                          "cpu_baseline": {"lanes_per_s": sample / cpu_s, "threads": threads, "sample_lanes": sample,
                                           "kind": "port"}}
             del planes, w
+    # the warp-form eigenvalues of 32 x 32 symmetric matrices, one warp a lane
+    lanes = 1 << 14
+    rng = np.random.default_rng(32)
+    g = rng.standard_normal((32, 32, lanes))
+    a64 = np.ascontiguousarray((g + g.transpose(1, 0, 2)) / 2)
+    for mode, tdt in (("float64", torch.float64), ("float32", torch.float32)):
+        k = runtime.load(BUNDLES, "warp_eigvals_32", mode, local)
+        planes = {"A": torch.as_tensor(a64, device=dev).to(tdt), "w": torch.empty((32, lanes), dtype=tdt, device=dev),
+                  "info": torch.empty(lanes, dtype=torch.int32, device=dev)}
+        for _ in range(2):
+            runtime.run(k, **planes)
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            runtime.run(k, **planes)
+            b.record()
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+        ms = statistics.median(times)
+        rec = {"lanes": lanes, "n": 32, "ms": round(ms, 5), "lanes_per_s": lanes / (ms * 1e-3)}
+        if mode == "float64":
+            sample = 256
+            oracle.sym_eigen(np.ascontiguousarray(a64[..., :1]), vectors=False)      # load the library first
+            t0 = time.perf_counter()
+            oracle.sym_eigen(np.ascontiguousarray(a64[..., :sample]), vectors=False, threads=threads)
+            rec["cpu_baseline"] = {"lanes_per_s": sample / (time.perf_counter() - t0), "threads": threads,
+                                   "sample_lanes": sample, "kind": "port"}
+        out[f"warp_eigvals_32.{mode}"] = rec
+        del planes
     return out
 
 
