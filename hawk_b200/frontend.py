@@ -18,7 +18,8 @@ native build and a third-party package:
   when used.
 
 The front end is found on ``sys.path``, else under the directory named by
-``HAWK_FRONTEND``.  Only the build side imports this module.
+``HAWK_FRONTEND``, else in a checkout named ``reference`` beside this
+repository.  Only the build side imports this module.
 """
 
 from __future__ import annotations
@@ -33,7 +34,9 @@ from pathlib import Path
 
 from .errors import HawkError
 
-_FALLBACK_ROOTS = ("/root/reference",)
+#: Where the front end is looked for last: a checkout named ``reference``
+#: beside this repository.
+_FALLBACK_ROOTS = (str(Path(__file__).resolve().parents[2] / "reference"),)
 
 
 def _root_of(candidate) -> Path | None:
