@@ -24,3 +24,20 @@ def test_a_gradient_plane_smaller_than_its_table_is_named():
     assert "the gradient of the lookup plane 'W' (shape (120,)) needs that many elements, got shape (119,)" in msg
     planes["bar_W"] = SimpleNamespace(size=120, shape=(120,))
     assert adjoint_errors({"bar_W": "W"}, planes) == []
+
+
+def test_the_teams_a_stage_launches():
+    """hawk/_lane_bind.py:123-134: lanes, keys x groups, an ordered scatter's
+    target cells, and its chunks -- times the warps the b200 chunk stage walks
+    each chunk with."""
+    from types import SimpleNamespace
+
+    from hawk_b200.runtime import SplitKernel
+
+    fake = SimpleNamespace(scatter_chunks=SplitKernel.scatter_chunks, keyed_size=lambda keyed, n: n // 8)
+    grid = lambda record, n, count, sizes: SplitKernel.grid(fake, record, n, count, sizes)  # noqa: E731
+    assert grid({"grid": "lanes"}, 100, 37, {}) == 37
+    assert grid({"grid": "keys", "keyed": {"width": 1}, "groups": 64}, 800, 800, {}) == 100 * 64
+    assert grid({"grid": "targets", "of": "acc"}, 20000, 20000, {"acc": 7}) == 7
+    assert grid({"grid": "chunks", "of": "acc", "groups": 8}, 20000, 20000, {"acc": 7}) == 256 * 8
+    assert grid({"grid": "chunks", "of": "acc"}, 50, 50, {"acc": 200}) == 1
