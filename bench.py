@@ -49,7 +49,7 @@ BYTES_F64 = {
     "poly_loss": 24, "poly_loss_vjp": 25.5,
     "gravity": 96, "gravity_jvp": 144, "gravity_vjp": 144,
     "spd_solve": 384, "spd_solve_vjp": 720,
-    "kepler": 28, "kepler_vjp": 40,
+    "kepler": 28, "kepler_vjp": 40, "trig": 24,
     # scattered commits: the streamed per-sample planes (the slot planes stay in L2)
     "segment_sum": 8, "keyed_sum": 12, "histogram": 12, "bitmask": 8, "gather": 20, "gather_vjp": 28,
 }

@@ -14,6 +14,9 @@ c3 gravity         f = G m1 m2 / |d|^3 * d, u = -G m1 m2 / |d|, d = r2 - r1
 c4 spd_solve       x = cho_solve(cholesky(A), b) for a 6x6 SPD A
 c5 kepler          Newton on E - e sin E = M from E = M, at most 32 trips,
                    leaving when |dE| < 1e-14; E and the trip count (int32)
+   trig            s = sin(x), c = cos(x): the device library's sin and cos
+                   as output planes, for the bitwise check against the host
+                   target's libm
 
 Stepping kernels (automatic, ``steps="auto"``: each launch runs up to the
 ``fused_steps`` word of steps per sample, a sample leaving at its own finish;
@@ -88,6 +91,12 @@ def kepler(e: Scalar, M: Scalar, E: Mutable[Scalar], iters: Mutable[Int32]):
             break
     E = Ek
     iters = n
+
+
+@hawk.kernel
+def trig(x: Scalar, s: Mutable[Scalar], c: Mutable[Scalar]):
+    s = m.sin(x)
+    c = m.cos(x)
 
 
 def _rk4_accel(stiff, damp, p, q):
@@ -487,6 +496,7 @@ KERNELS = {
     "spd_solve_vjp": (Kernel("spd_solve_vjp", vjp(spd_solve, wrt=("A", "b"))), ("float64",)),
     "kepler": (kepler, ("float64",)),
     "kepler_vjp": (Kernel("kepler_vjp", vjp(kepler, wrt=("e", "M"))), ("float64",)),
+    "trig": (trig, ("float64",)),
     "oscillator": (oscillator, ("float64",)),
     "orbit": (orbit, ("float64",)),
     "gather": (gather, ("float64",)),

@@ -104,18 +104,36 @@ def finish_subtrees(op: str, mode: str, cols: int, leaf_hi, leaf_comp, leaves: i
                       values.data_ptr(), 0, stream)
 
 
+def shard_counts(total_samples: int, world: int) -> list:
+    """Every rank's leaf count when ``total_samples`` are cut by ``shard_range``."""
+    return [leaves_of(shard_range(total_samples, world, r)[1]) if shard_range(total_samples, world, r)[1] else 0
+            for r in range(world)]
+
+
 def run_cells(kernel, *, group=None, base: int = 0, count: int | None = None, n_samples: int | None = None,
-              stream=None, **arrays) -> None:
+              total_samples: int | None = None, stream=None, **arrays) -> None:
     """``hawk_b200.runtime.run`` of a kernel with cells over this rank's shard,
     its cells summed over the samples of every rank of ``group``.
 
     Each rank binds its own shard's planes (``n_samples`` local samples, a
     multiple of 131072 on every rank but the last); the cells every rank
-    receives are bit-identical to one GPU's over the concatenated shards."""
+    receives are bit-identical to one GPU's over the concatenated shards.
+
+    ``total_samples``: the sample count of the whole job, cut over the ranks by
+    ``shard_range``.  Every rank's leaf count then follows from it, so the call
+    makes one collective (the partials) and no host round trip; this rank's
+    shard must be the one ``shard_range`` gives it (refused otherwise).  Without
+    it the ranks first exchange their leaf counts (a second collective, read
+    back on the host).
+
+    Every launch and every collective is ordered on ``stream`` (the current
+    stream when None): the partials are gathered after the kernels that write
+    them, and the final tree runs after the gather lands."""
     import torch
     import torch.distributed as dist
 
     from . import runtime
+    from .errors import HawkError
 
     with kernel._lock:
         pending = runtime.launch_cells(kernel, base=base, count=count, n_samples=n_samples, stream=stream,
@@ -127,25 +145,34 @@ def run_cells(kernel, *, group=None, base: int = 0, count: int | None = None, n_
         leaves = kernel.cells_leaves(state, lo, hi, stream) if hi > lo else 0
         world = dist.get_world_size(group) if dist.is_initialized() else 1
         if world > 1:
-            counts_t = torch.tensor([leaves], dtype=torch.int64, device=f"cuda:{kernel.device}")
-            every = [torch.zeros_like(counts_t) for _ in range(world)]
-            dist.all_gather(every, counts_t, group=group)
-            counts = [int(c.item()) for c in every]
-            if aligned(counts):
-                op = kernel.sums[0]["op"] if kernel.sums else "sum"
-                finish_subtrees(op, kernel.mode, cols, state["leaf_hi"], state["leaf_comp"], leaves,
-                                state["values"], group, runtime._stream(stream, kernel.device))
-                kernel.write_cells(state["values"], outputs, stream)
-                return
-            width = max(max(counts), 1)
-            flat_hi = state["leaf_hi"].view(-1)
-            flat_comp = state["leaf_comp"].view(-1)
-            pad = torch.zeros((2, cols, width), dtype=flat_hi.dtype, device=flat_hi.device)
-            if leaves:
-                pad[0, :, :leaves] = flat_hi[:cols * leaves].view(cols, leaves)
-                pad[1, :, :leaves] = flat_comp[:cols * leaves].view(cols, leaves)
-            all_hi, all_comp = gather_leaves(pad[0], pad[1], counts, group)
-            total = all_hi.shape[1]
+            with torch.cuda.stream(runtime._torch_stream(stream, kernel.device)):
+                if total_samples is not None:
+                    rank = dist.get_rank(group)
+                    want = shard_range(int(total_samples), world, rank)[1]
+                    if hi - lo != -(-want // ROW):
+                        raise HawkError(f"rank {rank}: its shard holds {hi - lo} rows of 32 samples but "
+                                        f"shard_range({total_samples}, {world}, {rank}) gives it {want} samples")
+                    counts = shard_counts(int(total_samples), world)
+                else:
+                    counts_t = torch.tensor([leaves], dtype=torch.int64, device=f"cuda:{kernel.device}")
+                    every = torch.zeros(world, dtype=torch.int64, device=f"cuda:{kernel.device}")
+                    dist.all_gather_into_tensor(every, counts_t, group=group)
+                    counts = [int(c) for c in every.cpu().tolist()]
+                if aligned(counts):
+                    op = kernel.sums[0]["op"] if kernel.sums else "sum"
+                    finish_subtrees(op, kernel.mode, cols, state["leaf_hi"], state["leaf_comp"], leaves,
+                                    state["values"], group, runtime._stream(stream, kernel.device))
+                    kernel.write_cells(state["values"], outputs, stream)
+                    return
+                width = max(max(counts), 1)
+                flat_hi = state["leaf_hi"].view(-1)
+                flat_comp = state["leaf_comp"].view(-1)
+                pad = torch.zeros((2, cols, width), dtype=flat_hi.dtype, device=flat_hi.device)
+                if leaves:
+                    pad[0, :, :leaves] = flat_hi[:cols * leaves].view(cols, leaves)
+                    pad[1, :, :leaves] = flat_comp[:cols * leaves].view(cols, leaves)
+                all_hi, all_comp = gather_leaves(pad[0], pad[1], counts, group)
+                total = all_hi.shape[1]
         else:
             all_hi, all_comp, total = state["leaf_hi"], state["leaf_comp"], leaves
         if total:

@@ -69,6 +69,12 @@ def kepler(n: int, seed: int = 0) -> dict:
             "bar_E": rng.standard_normal(n)}
 
 
+def trig(n: int, seed: int = 0) -> dict:
+    """Arguments of sin/cos: x ~ U[0, 2 pi) (the range Kepler's Newton trips take)."""
+    rng = np.random.default_rng(seed)
+    return {"x": rng.uniform(0.0, 2.0 * np.pi, n)}
+
+
 def oscillator(n: int, seed: int = 0, stop_max: int = 64, done_every: int = 0) -> dict:
     """Damped oscillators: w in [0.5, 3], z in [0, 0.3], x(0) ~ N(0, 1), v(0) = 0,
     each stopping after its own 1..stop_max steps; every ``done_every``-th sample
@@ -160,4 +166,4 @@ def team(n: int, lanes: int, kind: str, seed: int = 0, bad: int | None = TEAM_BA
 
 
 MAKERS = {"energy": energy, "poly_loss": poly_loss, "gravity": gravity, "spd_solve": spd_solve, "kepler": kepler,
-          "oscillator": oscillator, "orbit": orbit, "scatter": scatter}
+          "trig": trig, "oscillator": oscillator, "orbit": orbit, "scatter": scatter}

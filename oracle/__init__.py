@@ -28,7 +28,6 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-MATH_LIBM, MATH_CR = 0, 1
 OP = {"sum": 0, "max": 1, "min": 2}
 _LOCK = threading.Lock()
 _LIB = None
@@ -56,7 +55,7 @@ def build() -> Path:
         return out
     out.parent.mkdir(parents=True, exist_ok=True)
     cmd = ["gcc", "-O3", "-march=native", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-std=c11",
-           "-shared", str(HERE / "hawk_oracle.c"), "-o", str(out), "-lquadmath", "-lm"]
+           "-shared", str(HERE / "hawk_oracle.c"), "-o", str(out), "-lm"]
     env = dict(os.environ)
     env.pop("CC", None)
     run = subprocess.run(cmd, capture_output=True, text=True, env=env)
@@ -70,8 +69,6 @@ _I = ctypes.c_int64
 _D = ctypes.c_double
 _F = ctypes.c_float
 _SIGS = {
-    "hko_set_math": (None, [ctypes.c_int]),
-    "hko_get_math": (ctypes.c_int, []),
     "hko_energy": (None, [_P, _I, _P, _I, _I]),
     "hko_energy_vjp": (None, [_P, _I, _P, _P, _I, _I, _I]),
     "hko_energy_jvp": (None, [_P, _I, _P, _I, _P, _I, _I]),
@@ -89,6 +86,7 @@ _SIGS = {
     "hko_spd_solve": (None, [_P, _P, _I, _P, _I, _I, _I]),
     "hko_spd_solve_vjp": (None, [_P, _P, _P, _I, _P, _P, _I, _I, _I]),
     "hko_kepler": (None, [_P, _P, _P, _P, _I, _I]),
+    "hko_trig": (None, [_P, _P, _P, _I, _I]),
     "hko_kepler_vjp": (None, [_P, _P, _P, _P, _P, _I, _I]),
     "hko_oscillator": (ctypes.c_uint32, [_P, _P, _P, _P, _P, _P, _P, _D, _I, _I, _I]),
     "hko_orbit": (ctypes.c_uint32, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I]),
@@ -117,24 +115,6 @@ def lib() -> ctypes.CDLL:
 def _p(a: np.ndarray):
     assert a.flags.c_contiguous
     return a.ctypes.data_as(ctypes.c_void_p)
-
-
-def set_math(mode: int) -> None:
-    lib().hko_set_math(int(mode))
-
-
-class math_mode:
-    """``with math_mode(MATH_CR): ...`` -- sin/cos correctly rounded inside."""
-
-    def __init__(self, mode: int) -> None:
-        self.mode = mode
-
-    def __enter__(self):
-        self.prev = lib().hko_get_math()
-        lib().hko_set_math(self.mode)
-
-    def __exit__(self, *exc):
-        lib().hko_set_math(self.prev)
 
 
 def tiles(n: int, threads: int, align: int = 1):
@@ -361,6 +341,15 @@ def kepler(e, M, threads: int = 1):
     it = np.empty(n, dtype=np.int32)
     parallel(lambda b, c: lib().hko_kepler(_p(e), _p(M), _p(E), _p(it), b, c), n, threads)
     return E, it
+
+
+def trig(x, threads: int = 1):
+    """(sin x, cos x) by the host's libm."""
+    x = np.ascontiguousarray(x, dtype=np.float64)
+    n = x.shape[0]
+    s, c = np.empty(n), np.empty(n)
+    parallel(lambda b, cc: lib().hko_trig(_p(x), _p(s), _p(c), b, cc), n, threads)
+    return s, c
 
 
 def kepler_vjp(e, M, bar_E, threads: int = 1):

@@ -2,8 +2,8 @@
  * hawk_oracle.c -- TEST INFRASTRUCTURE ONLY (see hawk_oracle.h): the CPU
  * restatement of the reference's host target for the five benchmark kernels.
  *
- * Built with -O2 -ffp-contract=off (no FMA contraction), the reference's
- * `native` host profile (hawk/compile/toolchain.py:897-900).  Each kernel
+ * Built with -O3 -march=native -ffp-contract=off (no FMA contraction), the
+ * reference's `native` host profile (hawk/compile/toolchain.py:897-900).  Each kernel
  * function below states the body the reference renderer writes for the kernel
  * (hawk/emit/render.py:140; the kernels are the ones in hawk_b200/configs.py),
  * operation for operation, inside the serial host loop of
@@ -14,17 +14,12 @@
 #include "hawk_oracle.h"
 
 #include <math.h>
-#include <quadmath.h>
 #include <stdlib.h>
 #include <string.h>
 
-static int g_math = HKO_MATH_LIBM;
-
-void hko_set_math(int mode) { g_math = mode; }
-int hko_get_math(void) { return g_math; }
-
-static double o_sin(double x) { return g_math == HKO_MATH_CR ? (double)sinq((__float128)x) : sin(x); }
-static double o_cos(double x) { return g_math == HKO_MATH_CR ? (double)cosq((__float128)x) : cos(x); }
+/* glibc's sin and cos: the reference host target's libm */
+static double o_sin(double x) { return sin(x); }
+static double o_cos(double x) { return cos(x); }
 
 /* ------------------------------------------------------------------ c1 energy */
 
@@ -839,6 +834,14 @@ void hko_lstsq_qr(int m, int n, const double* J, const double* r, int64_t pitch,
  *   tb0 = ((E - (e * sin E)) - M) / (1 - (e * cos E));  E' = E - tb0;  n' = n + 1;
  *   leave after the trip when |tb0| < 1e-14.
  */
+/* s = sin(x); c = cos(x) */
+void hko_trig(const double* x, double* s, double* c, int64_t base, int64_t count) {
+    for (int64_t i = base; i < base + count; ++i) {
+        s[i] = o_sin(x[i]);
+        c[i] = o_cos(x[i]);
+    }
+}
+
 void hko_kepler(const double* e, const double* M, double* E, int32_t* iters, int64_t base, int64_t count) {
     for (int64_t i = base; i < base + count; ++i) {
         const double Mi = M[i], ei = e[i];

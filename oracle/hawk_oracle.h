@@ -12,10 +12,8 @@
  * component-major: component k of sample i of a vector plane is v[k * pitch + i].
  *
  * Math: the reference's host build calls glibc's sin/cos (its host profile
- * equals glibc bit for bit, tests/test_math_parity.py:4-14).  HKO_MATH_LIBM
- * restates that; HKO_MATH_CR uses the correctly rounded values (libquadmath's
- * sinq/cosq at 113 bits, rounded once to double), the independent reference
- * for a device that rounds sin/cos correctly.
+ * equals glibc bit for bit, tests/test_math_parity.py:4-14), and so does this
+ * library: the host's own libm, the reference host target's math exactly.
  */
 #ifndef HAWK_ORACLE_H
 #define HAWK_ORACLE_H
@@ -26,15 +24,9 @@
 extern "C" {
 #endif
 
-#define HKO_MATH_LIBM 0
-#define HKO_MATH_CR 1
-
 #define HKO_OP_SUM 0
 #define HKO_OP_MAX 1
 #define HKO_OP_MIN 2
-
-void hko_set_math(int mode);
-int hko_get_math(void);
 
 /* c1: out = 0.5 * dot(v, v) */
 void hko_energy(const double* v, int64_t pitch, double* out, int64_t base, int64_t count);
@@ -81,6 +73,8 @@ void hko_spd_solve_vjp(const double* A, const double* b, const double* bar_x, in
 
 /* c5: Kepler's equation by Newton, and its VJP through the loop */
 void hko_kepler(const double* e, const double* M, double* E, int32_t* iters, int64_t base, int64_t count);
+/* trig: s = sin(x), c = cos(x) (the host target's libm) */
+void hko_trig(const double* x, double* s, double* c, int64_t base, int64_t count);
 void hko_kepler_vjp(const double* e, const double* M, const double* bar_E, double* bar_e, double* bar_M,
                     int64_t base, int64_t count);
 

@@ -14,6 +14,8 @@ sample shows.
 
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import pytest
 
@@ -174,9 +176,8 @@ def test_kepler_fwd_vjp(n):
     e, M = dev(w["e"]), dev(w["M"])
     E, it = nan_like((n,)), torch.full((n,), -1, dtype=torch.int32, device="cuda")
     runtime.run(runtime.load(BUNDLES, "kepler"), e=e, M=M, E=E, iters=it)
-    with oracle.math_mode(oracle.MATH_CR):
-        wE, wit = oracle.kepler(w["e"], w["M"])
-        wbe, wbM = oracle.kepler_vjp(w["e"], w["M"], w["bar_E"])
+    wE, wit = oracle.kepler(w["e"], w["M"])
+    wbe, wbM = oracle.kepler_vjp(w["e"], w["M"], w["bar_E"])
     np.testing.assert_array_equal(host(it), wit)           # int32 plane: bit-exact
     same(host(E), wE)
     be, bM = nan_like((n,)), nan_like((n,))
@@ -185,24 +186,59 @@ def test_kepler_fwd_vjp(n):
     same(host(bM), wbM)
 
 
-def test_kepler_against_the_glibc_oracle():
-    """Against the reference host target's own math (glibc): E within 1e-12 and
-    the iteration counts equal except where glibc's own 1-ulp misrounding of
-    sin/cos moves an exit test (measured: about 1 sample in 4 million)."""
-    n = 1 << 18
-    w = workloads.kepler(n, seed=11)
+def trig_arguments(seed: int) -> np.ndarray:
+    """Arguments over every range of glibc's sin/cos method, with its range
+    boundaries and special values."""
+    rng = np.random.default_rng(seed)
+    x = np.concatenate([rng.uniform(-0.126, 0.126, 1 << 20), rng.uniform(-8.0, 8.0, 1 << 22),
+                        rng.uniform(-105414350.0, 105414350.0, 1 << 20),
+                        np.ldexp(rng.uniform(1, 2, 1 << 18), rng.integers(27, 1024, 1 << 18)),
+                        np.ldexp(rng.uniform(1, 2, 1 << 16), rng.integers(-1074, -20, 1 << 16)),
+                        [0.0, -0.0, 2.0 ** -1074, 2.0 ** -27, 2.0 ** -26, 0.126, 0.85546875, 2.426265,
+                         105414350.0, 1e22, 6381956970095103.0 * 2.0 ** 797, 1.7976931348623157e308,
+                         np.inf, -np.inf, np.nan]])
+    sign = rng.integers(0, 2, x.shape[0]) * 2 - 1
+    return x * sign
+
+
+def test_trig_has_glibcs_bits():
+    """sin and cos on the device against the host's glibc (the reference host
+    target's libm) on 6.4 million arguments over every range of its method,
+    the large-argument reduction and the special values: bit-identical."""
+    x = trig_arguments(17)
+    n = x.shape[0]
+    s, c = nan_like((n,)), nan_like((n,))
+    runtime.run(runtime.load(BUNDLES, "trig"), x=dev(x), s=s, c=c)
+    ws, wc = oracle.trig(x, threads=max(1, min(32, os.cpu_count() or 1)))
+    same(host(s), ws)
+    same(host(c), wc)
+
+
+@pytest.mark.parametrize("seed", [11, 12])
+def test_kepler_full_size_against_the_glibc_oracle(seed):
+    """The configuration's full size, 2^24 samples: the int32 iteration counts
+    equal the reference host target's (glibc's sin/cos) on every sample, and E
+    and the VJP bit-identical to it."""
+    n = workloads.FULL_N["kepler"]
+    w = workloads.kepler(n, seed=seed)
+    e, M = dev(w["e"]), dev(w["M"])
     E, it = nan_like((n,)), torch.full((n,), -1, dtype=torch.int32, device="cuda")
-    runtime.run(runtime.load(BUNDLES, "kepler"), e=dev(w["e"]), M=dev(w["M"]), E=E, iters=it)
-    with oracle.math_mode(oracle.MATH_LIBM):
-        wE, wit = oracle.kepler(w["e"], w["M"], threads=8)
-    np.testing.assert_allclose(host(E), wE, rtol=1e-12)
-    assert int((host(it) != wit).sum()) <= 2
+    runtime.run(runtime.load(BUNDLES, "kepler"), e=e, M=M, E=E, iters=it)
+    threads = max(1, min(32, os.cpu_count() or 1))
+    wE, wit = oracle.kepler(w["e"], w["M"], threads=threads)
+    assert int((host(it) != wit).sum()) == 0
+    same(host(E), wE)
+    be, bM = nan_like((n,)), nan_like((n,))
+    runtime.run(runtime.load(BUNDLES, "kepler_vjp"), e=e, M=M, bar_E=dev(w["bar_E"]), bar_e=be, bar_M=bM)
+    wbe, wbM = oracle.kepler_vjp(w["e"], w["M"], w["bar_E"], threads=threads)
+    same(host(be), wbe)
+    same(host(bM), wbM)
 
 
 def test_kepler_beyond_two_to_the_twenty():
-    """Mean anomalies from 2^20 to 1e300 (sin/cos through the Payne-Hanek
-    reduction), infinities and NaN: bit-identical to the correctly rounded
-    oracle, iteration counts included."""
+    """Mean anomalies from 2^20 to 1e300 (sin/cos through both argument
+    reductions), infinities and NaN: bit-identical to the glibc oracle,
+    iteration counts included."""
     rng = np.random.default_rng(5)
     # below 2^52 or so e*sin(E) still moves E, so the exact sin/cos bits show
     M = np.concatenate([np.ldexp(rng.uniform(1, 2, 4000), rng.integers(20, 52, 4000)),
@@ -212,8 +248,7 @@ def test_kepler_beyond_two_to_the_twenty():
     n = M.shape[0]
     E, it = nan_like((n,)), torch.full((n,), -1, dtype=torch.int32, device="cuda")
     runtime.run(runtime.load(BUNDLES, "kepler"), e=dev(e), M=dev(M), E=E, iters=it)
-    with oracle.math_mode(oracle.MATH_CR):
-        wE, wit = oracle.kepler(e, M)
+    wE, wit = oracle.kepler(e, M)
     np.testing.assert_array_equal(host(it), wit)
     same(host(E), wE)
 

@@ -4,7 +4,10 @@ Each rank binds its contiguous shard (``sharded.shard_range``), writes its
 32-sample rows, folds them into leaf partials, all-gathers the partials and
 runs the same pairwise tree; every rank's Param gradients must be
 bit-identical to the oracle's finish over all samples (hawk/_cells.py:94-119
-over the unsharded rows).  Skipped with fewer GPUs than ranks.
+over the unsharded rows).  Two call forms: the leaf counts exchanged by the
+ranks on the current stream, and the counts derived from the job's sample
+count (``total_samples``) with every launch and collective on a side stream.
+Skipped with fewer GPUs than ranks.
 """
 
 from __future__ import annotations
@@ -32,7 +35,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, n, queue):
+def _rank_main(rank, world, port, n, form, queue):
     import torch.distributed as dist
 
     from hawk_b200 import runtime, sharded, workloads
@@ -53,7 +56,15 @@ def _rank_main(rank, world, port, n, queue):
                  for k in ("bar_a", "bar_b", "bar_c")}
         abc = {k: dev(np.array([w[k]])) for k in ("a", "b", "c")}
         vjp = runtime.load(BUNDLES, "poly_loss_vjp", "float64", rank)
-        sharded.run_cells(vjp, x=dev(w["x"][sl]), t=dev(w["t"][sl]), bar_r=dev(w["bar_r"][sl]), **abc, **cells)
+        planes = dict(x=dev(w["x"][sl]), t=dev(w["t"][sl]), bar_r=dev(w["bar_r"][sl]), **abc, **cells)
+        if form == "side stream":
+            side = torch.cuda.Stream(device=rank)
+            side.wait_stream(torch.cuda.current_stream(rank))
+            for _ in range(2):          # the second call's finish reuses the first's scratch
+                sharded.run_cells(vjp, total_samples=n, stream=side, **planes)
+            side.synchronize()
+        else:
+            sharded.run_cells(vjp, **planes)
         torch.cuda.synchronize(rank)
         queue.put((rank, base, count, [float(cells[k].cpu()[0]) for k in ("bar_a", "bar_b", "bar_c")]))
     finally:
@@ -65,9 +76,10 @@ def _worlds():
     return [w for w in (2, 4, 8) if w <= max(count, 2)]
 
 
+@pytest.mark.parametrize("form", ["counts exchanged", "side stream"])
 @pytest.mark.parametrize("shape", ["ragged", "aligned"])
 @pytest.mark.parametrize("world", _worlds())
-def test_sharded_param_gradients_bit_identical_to_one_device(world, shape):
+def test_sharded_param_gradients_bit_identical_to_one_device(world, shape, form):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs, {torch.cuda.device_count()} visible")
     import torch.multiprocessing as mp
@@ -83,7 +95,7 @@ def test_sharded_param_gradients_bit_identical_to_one_device(world, shape):
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, n, queue)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, n, form, queue)) for r in range(world)]
     for p in procs:
         p.start()
     results = [queue.get(timeout=300) for _ in range(world)]

@@ -118,3 +118,56 @@ def test_unequal_or_odd_leaf_counts_take_the_full_gather():
     assert not sharded.aligned([6, 6])
     assert not sharded.aligned([0, 0])
     assert sharded.aligned([16, 16, 16])
+
+
+def test_shard_counts_follow_the_cut():
+    for n in (1, 131072, 131073, 3 * 131072 + 5, 10 ** 7):
+        for world in (1, 2, 3, 8):
+            counts = sharded.shard_counts(n, world)
+            assert counts == [sharded.leaves_of(sharded.shard_range(n, world, r)[1])
+                              if sharded.shard_range(n, world, r)[1] else 0 for r in range(world)]
+            assert sum(counts) == sharded.leaves_of(n)
+
+
+def _leaving_rank_main(rank, world, port, queue):
+    """Rank 1 takes part in the first step's gather and then leaves (between
+    steps, nothing of its own in flight); rank 0 goes on to the second step's
+    gather, which must end with an error inside the group's timeout."""
+    import datetime
+    import time
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    lh = torch.full((3, 2), float(rank))
+    lc = torch.zeros((3, 2))
+    sharded.gather_leaves(lh, lc, [2] * world)
+    if rank == 1:
+        queue.put((rank, "left", 0.0))
+        queue.close()
+        queue.join_thread()
+        os._exit(0)                      # leaves without another collective
+    t0 = time.monotonic()
+    try:
+        sharded.gather_leaves(lh, lc, [2] * world)
+        queue.put((rank, "no error", time.monotonic() - t0))
+    except Exception as exc:            # noqa: BLE001 -- the error is the result
+        queue.put((rank, f"error: {type(exc).__name__}", time.monotonic() - t0))
+    queue.close()
+    queue.join_thread()
+    os._exit(0)
+
+
+def test_a_rank_that_leaves_between_steps_ends_the_others_next_gather_with_an_error():
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_rank_main, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = sorted(queue.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert results[1][1] == "left"
+    assert results[0][1].startswith("error"), results
+    assert results[0][2] < 60.0, results
