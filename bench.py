@@ -17,11 +17,24 @@ same step through the public API (``hawk_b200.runtime.run`` /
 step and the gradient cells read back.  Scaling is weak: every GPU holds its
 own 2^26 samples of one global problem, and ``value`` counts all of them.
 
+After the timed steps the step's three cells are compared with the CPU
+oracle's finish over the samples of every rank (``parity``).  Then every other
+configuration runs at its full size on every GPU (``configs``, weak scaling as
+the headline): energy c1, gravity c3, the SPD solve c4 and Kepler c5 -- each
+kernel's device time and HBM (c5: FP64-pipe) fraction, the whole job's
+fwd + VJP samples/s, every output compared bit for bit with the oracle on
+every rank, and on one GPU the oracle's samples/s on 1 and all host threads
+and a public-API e2e -- the headline step in float32 (c2f32), and on several
+GPUs the headline's job of 2^26 samples cut over the ranks (c2strong, strong
+scaling).  On one GPU the remaining kernel families (scattered commits,
+stepping, team-form linear algebra, ordered stages) are measured too and
+their detail goes to stderr.
+
 ``--impl reference`` times the reference arm: the CPU restatement of the
 reference's host target (oracle/, the reference itself cannot be built here)
 on all host threads, on a bounded sample of the same workload.
 
-Every line is one JSON object printed by rank 0.
+rank 0 prints one JSON line on stdout.
 """
 
 from __future__ import annotations
@@ -213,6 +226,7 @@ class PolyStep:
         self.leaves = sharded.leaves_of(n)
         counts = [self.leaves] * world
         self.counts = counts
+        self.aligned = sharded.aligned(counts)
         self.leaf_hi = torch.empty((3, self.leaves), dtype=self.tdt, device=self.dev)
         self.leaf_comp = torch.empty((3, self.leaves), dtype=self.tdt, device=self.dev)
         self.cells = torch.empty(3, dtype=self.tdt, device=self.dev)
@@ -250,33 +264,76 @@ class PolyStep:
         self._keep = (hi, comp)
 
 
+def time_steps(s: PolyStep, steps: int, warmup: int, dist, marks: bool = False):
+    """``warmup`` untimed steps, then ``steps`` timed ones between barriers:
+    (ms per step, max over ranks; per-kernel marks or None)."""
+    import torch
+
+    stream = torch.cuda.current_stream(s.device).cuda_stream
+    for _ in range(warmup):
+        s.step(stream)
+    barrier(dist)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)] if marks else None
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(dist)
+    start.record()
+    for k in range(steps):
+        s.step(stream, ev[k] if ev else None)
+    end.record()
+    torch.cuda.synchronize()
+    barrier(dist)
+    return max_over_ranks(start.elapsed_time(end), dist) / steps, ev
+
+
+def headline_parity(s: PolyStep, world: int, dist) -> dict:
+    """The step's cells against the oracle over the samples of every rank:
+    each rank's 32-sample rows and leaf partials by the oracle, the partials
+    gathered in rank order, the same tree (hawk/_cells.py:94-119) -- the
+    oracle's finish over the concatenated samples.  Every rank compares its
+    own cells; the result holds only if all are bit-identical."""
+    import torch
+
+    import oracle
+
+    w = s.host
+    dt = np.float64 if s.mode == "float64" else np.float32
+    threads = max(1, (os.cpu_count() or 1) // world)
+    a, b, c = (dt(w[k]) for k in ("a", "b", "c"))
+    hi, comp = oracle.poly_loss_vjp_rows(w["x"], w["t"], w["bar_r"], a, b, c, threads)
+    got = [float(v) for v in s.cells.cpu().tolist()]
+    if world == 1:
+        want = [float(oracle.cells_finish(hi[k], comp[k])) for k in range(3)]
+    elif s.mode == "float64":
+        parts = [oracle.cells_leaves(hi[k], comp[k]) for k in range(3)]
+        pack = torch.tensor(np.stack([np.stack([p[0] for p in parts]), np.stack([p[1] for p in parts])]),
+                            device=s.dev)
+        gathered = torch.empty((world, *pack.shape), dtype=pack.dtype, device=s.dev)
+        dist.all_gather_into_tensor(gathered, pack)
+        g = gathered.cpu().numpy()
+        all_hi = np.concatenate([g[r, 0] for r in range(world)], axis=1)
+        all_comp = np.concatenate([g[r, 1] for r in range(world)], axis=1)
+        want = [float(oracle.cells_tree(all_hi[k], all_comp[k])) for k in range(3)]
+    else:
+        return {"cells_bitwise": None, "why": "the oracle's leaf stage is float64 only"}
+    ok = got == want
+    if dist is not None:
+        flag = torch.tensor([1.0 if ok else 0.0], dtype=torch.float64, device=s.dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        ok = bool(flag.item() == 1.0)
+    return {"cells_bitwise": ok, "samples": s.n * world, "ranks": world, "cells": got,
+            "oracle": "oracle/hawk_oracle.c rows + leaves per rank, one tree"}
+
+
 def run_headline(args, world, rank, local, dist) -> dict:
     import torch
 
-    from hawk_b200 import abi
-
     torch.cuda.set_device(local)
     s = PolyStep(args.n, args.mode, local, rank, world, dist)
-    stream = torch.cuda.current_stream(local).cuda_stream
-    for _ in range(args.warmup):
-        s.step(stream)
-    barrier(dist)
-    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clocks:
-        barrier(dist)
-        start.record()
-        for k in range(args.steps):
-            s.step(stream, marks[k])
-        end.record()
-        torch.cuda.synchronize()
-        barrier(dist)
-    local_ms = start.elapsed_time(end)
-    total_ms = max_over_ranks(local_ms, dist)
+        per_step, marks = time_steps(s, args.steps, args.warmup, dist, marks=True)
     fwd_ms = statistics.mean(m[0].elapsed_time(m[1]) for m in marks)
     vjp_ms = statistics.mean(m[1].elapsed_time(m[2]) for m in marks)
     leaf_ms = statistics.mean(m[2].elapsed_time(m[3]) for m in marks)
-    per_step = total_ms / args.steps
     samples = args.n * world
     item = 8 if args.mode == "float64" else 4
     vjp_bytes = args.n * (3 * item + 6 * item / 32)
@@ -285,6 +342,9 @@ def run_headline(args, world, rank, local, dist) -> dict:
     dominant = ("poly_loss_vjp", vjp_ms, vjp_bytes) if vjp_ms >= fwd_ms else ("poly_loss", fwd_ms, fwd_bytes)
     achieved = dominant[2] / (dominant[1] * 1e-3) / 1e9
     traffic = profile_traffic(dominant[0], args.mode, args.n)
+    # our kernels a step: fwd, VJP, leaf stage, then the tree -- or, over ranks
+    # holding aligned subtrees, the subtree and the last levels (two launches)
+    per_launch = 5 if (world > 1 and s.aligned) else 4
     result = {
         "value": samples / (per_step * 1e-3),
         "ms_per_step": per_step,
@@ -295,14 +355,32 @@ def run_headline(args, world, rank, local, dist) -> dict:
                      "algorithmic_bytes": dominant[2]},
         "kernels_ms": {"poly_loss": round(fwd_ms, 5), "poly_loss_vjp": round(vjp_ms, 5),
                        "cells_leaves": round(leaf_ms, 5)},
-        "gpu_launches": 4 * args.steps,
-        "check": {"cells": [float(v) for v in s.cells.cpu().tolist()]},
+        "gpu_launches": per_launch * args.steps,
         "fwd_gbs": round(fwd_bytes / (fwd_ms * 1e-3) / 1e9, 1),
         "vjp_gbs": round(vjp_bytes / (vjp_ms * 1e-3) / 1e9, 1),
     }
+    result["parity"] = headline_parity(s, world, dist)
     result["e2e"] = run_e2e(args, s, world, dist)
-    _ = abi
+    del s
+    torch.cuda.empty_cache()
     return result
+
+
+def run_c2_variant(args, world, rank, local, dist, mode: str, total: int | None) -> dict:
+    """The headline step in another form: ``mode`` float32, or (``total``) a
+    fixed job of ``total`` samples cut over the ranks (strong scaling).  Its
+    time per step (slowest rank) and its cells against the oracle."""
+    import torch
+
+    n = args.n if total is None else total // world
+    s = PolyStep(n, mode, local, rank, world, dist)
+    per_step, _ = time_steps(s, max(5, min(args.steps, 20)), 3, dist)
+    par = headline_parity(s, world, dist)
+    out = {"n_per_gpu": n, "samples": n * world, "ms_per_step": round(per_step, 5),
+           "value": _sig(n * world / (per_step * 1e-3)), "bitwise": par["cells_bitwise"]}
+    del s
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_e2e(args, s, world, dist) -> dict:
@@ -323,7 +401,8 @@ def run_e2e(args, s, world, dist) -> dict:
         s.bar_r.copy_(host["bar_r"], non_blocking=True)
         runtime.run(s.fwd, x=s.x, t=s.t, a=w["a"], b=w["b"], c=w["c"], r=s.r)
         if world > 1:
-            sharded.run_cells(s.vjp, x=s.x, t=s.t, bar_r=s.bar_r, **s.abc, **cells)
+            sharded.run_cells(s.vjp, total_samples=args.n * world, x=s.x, t=s.t, bar_r=s.bar_r, **s.abc,
+                              **cells)
         else:
             runtime.run(s.vjp, x=s.x, t=s.t, bar_r=s.bar_r, **s.abc, **cells)
         cells_host[0:1].copy_(cells["bar_a"], non_blocking=True)
@@ -359,10 +438,273 @@ def profile_traffic(kernel: str, mode: str, n: int):
     return round(entry["dram_bytes_per_sample"] * n)
 
 
-# ------------------------------------------------------------ per-config table
-def run_configs(local: int) -> dict:
-    """Every benchmark kernel at its configuration's full size: device time per
-    launch (median of 10 after 3 warm-ups), samples/s and HBM fraction."""
+# ------------------------------------------------------ the configuration suite
+def _sig(x: float, digits: int = 4) -> float:
+    """``x`` to ``digits`` significant digits (short JSON)."""
+    return float(f"{x:.{digits}g}")
+
+
+def fp64_pipe_frac(kernel: str):
+    """The FP64 pipe's busy fraction of ``kernel`` from its committed ncu
+    summary, or None when there is none."""
+    path = REPO / "profiles" / "ncu_summary.json"
+    if not path.exists():
+        return None
+    entry = json.loads(path.read_text()).get(f"{kernel}.float64") or {}
+    return entry.get("fp64_pipe_frac")
+
+
+class Case:
+    """One benchmark configuration on one GPU: its seeded inputs, every
+    kernel bound to device planes, the oracle's outputs for the same inputs
+    and a bounded CPU sample of fwd + VJP."""
+
+    def __init__(self, key: str, n: int, seed: int, device: int) -> None:
+        import torch
+
+        from hawk_b200 import workloads
+
+        self.key, self.n, self.device = key, n, device
+        self.dev = torch.device("cuda", device)
+        maker = {"c1": workloads.energy, "c3": workloads.gravity, "c4": workloads.spd_solve,
+                 "c5": workloads.kepler}[key]
+        self.w = maker(n, seed)
+        w = self.w
+        t, e = self._t, self._e
+        if key == "c1":
+            v = t(w["v"])
+            self.kernels = [("energy", {"v": v, "out": e(n)}, {}),
+                            ("energy_vjp", {"v": v, "bar_out": t(w["bar_out"]), "bar_v": e((3, n))}, {}),
+                            ("energy_jvp", {"v": v, "dot_v": t(w["dot_v"]), "dot_out": e(n)}, {})]
+        elif key == "c3":
+            g = {k: t(w[k]) for k in ("r1", "r2", "m1", "m2")}
+            G = {"G": w["G"]}
+            self.kernels = [("gravity", {**g, "f": e((3, n)), "u": e(n)}, G),
+                            ("gravity_vjp", {**g, "bar_f": t(w["bar_f"]), "bar_u": t(w["bar_u"]),
+                                             "bar_r1": e((3, n)), "bar_r2": e((3, n))}, G),
+                            ("gravity_jvp", {**g, "dot_r1": t(w["dr1"]), "dot_r2": t(w["dr2"]), "dot_f": e((3, n)),
+                                             "dot_u": e(n)}, G)]
+        elif key == "c4":
+            A, b = t(w["A"]), t(w["b"])
+            self.kernels = [("spd_solve", {"A": A, "b": b, "x": e((6, n))}, {}),
+                            ("spd_solve_vjp", {"A": A, "b": b, "bar_x": t(w["bar_x"]), "bar_A": e((6, 6, n)),
+                                               "bar_b": e((6, n))}, {})]
+        else:
+            kp = {"e": t(w["e"]), "M": t(w["M"])}
+            self.kernels = [("kepler", {**kp, "E": e(n), "iters": e(n, torch.int32)}, {}),
+                            ("kepler_vjp", {**kp, "bar_E": t(w["bar_E"]), "bar_e": e(n), "bar_M": e(n)}, {})]
+        # the planes each kernel writes (compared with the oracle)
+        self.outputs = {"energy": ("out",), "energy_vjp": ("bar_v",), "energy_jvp": ("dot_out",),
+                        "gravity": ("f", "u"), "gravity_vjp": ("bar_r1", "bar_r2"), "gravity_jvp": ("dot_f", "dot_u"),
+                        "spd_solve": ("x",), "spd_solve_vjp": ("bar_A", "bar_b"),
+                        "kepler": ("E", "iters"), "kepler_vjp": ("bar_e", "bar_M")}
+
+    def _t(self, a):
+        import torch
+
+        return torch.as_tensor(np.ascontiguousarray(a), device=self.dev)
+
+    def _e(self, shape, dtype=None):
+        import torch
+
+        return torch.full(shape if isinstance(shape, tuple) else (shape,), -1 if dtype == torch.int32 else float("nan"),
+                          dtype=dtype or torch.float64, device=self.dev)
+
+    def time(self, reps: int = 10) -> dict:
+        """Device time per launch of every kernel (median of ``reps`` after 3 warm-ups)."""
+        import torch
+
+        from hawk_b200 import runtime
+        from hawk_b200.planes import from_torch
+
+        out = {}
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        for name, planes, values in self.kernels:
+            k = runtime.load(BUNDLES, name, "float64", self.device)
+            bound = {key: from_torch(v) for key, v in planes.items()}
+            k.check(bound, values, self.n)
+            k.bind_all(bound, values, self.n)
+            for _ in range(3):
+                k.launch(0, self.n, self.n, stream)
+            times = []
+            for _ in range(reps):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                k.launch(0, self.n, self.n, stream)
+                b.record()
+                b.synchronize()
+                times.append(a.elapsed_time(b))
+            info = k.entry.info(self.n)
+            out[name] = {"ms": statistics.median(times), "regs": info["regs"], "block": info["block"],
+                         "grid": info["grid"], "blocks_per_sm": info["blocks_per_sm"]}
+        return out
+
+    def oracle_outputs(self, threads: int) -> dict:
+        import oracle
+
+        w = self.w
+        if self.key == "c1":
+            return {"energy": (oracle.energy(w["v"], threads),),
+                    "energy_vjp": (oracle.energy_vjp(w["v"], w["bar_out"], threads),),
+                    "energy_jvp": (oracle.energy_jvp(w["v"], w["dot_v"], threads),)}
+        if self.key == "c3":
+            g = (w["r1"], w["r2"])
+            return {"gravity": oracle.gravity(*g, w["m1"], w["m2"], w["G"], threads),
+                    "gravity_vjp": oracle.gravity_vjp(*g, w["bar_f"], w["bar_u"], w["m1"], w["m2"], w["G"], threads),
+                    "gravity_jvp": oracle.gravity_jvp(*g, w["dr1"], w["dr2"], w["m1"], w["m2"], w["G"], threads)}
+        if self.key == "c4":
+            return {"spd_solve": (oracle.spd_solve(w["A"], w["b"], threads),),
+                    "spd_solve_vjp": oracle.spd_solve_vjp(w["A"], w["b"], w["bar_x"], threads)}
+        return {"kepler": oracle.kepler(w["e"], w["M"], threads),
+                "kepler_vjp": oracle.kepler_vjp(w["e"], w["M"], w["bar_E"], threads)}
+
+    def parity(self, threads: int) -> dict:
+        """Every output of every kernel (as the last timed launch left it)
+        against the oracle on the same inputs: bit-identical or not, per kernel."""
+        import torch
+
+        torch.cuda.synchronize(self.device)
+        want = self.oracle_outputs(threads)
+        res = {}
+        for name, planes, _values in self.kernels:
+            ok = True
+            for plane, ref in zip(self.outputs[name], want[name]):
+                got = planes[plane].cpu().numpy()
+                ok = ok and bool(np.array_equal(got, np.asarray(ref), equal_nan=True))
+            res[name] = ok
+        return res
+
+    def cpu_fwd_vjp(self, threads: int, sample: int) -> float:
+        """Samples/s of the oracle's fwd + VJP over the first ``sample`` samples."""
+        import oracle
+
+        w = self.w
+        m = min(sample, self.n)
+
+        def cut(a):
+            return np.ascontiguousarray(np.asarray(a)[..., :m])
+
+        if self.key == "c1":
+            v, bo = cut(w["v"]), cut(w["bar_out"])
+            run = (lambda: (oracle.energy(v, threads), oracle.energy_vjp(v, bo, threads)))
+        elif self.key == "c3":
+            r1, r2, m1, m2, bf, bu = (cut(w[k]) for k in ("r1", "r2", "m1", "m2", "bar_f", "bar_u"))
+            run = (lambda: (oracle.gravity(r1, r2, m1, m2, w["G"], threads),
+                            oracle.gravity_vjp(r1, r2, bf, bu, m1, m2, w["G"], threads)))
+        elif self.key == "c4":
+            A, b, bx = cut(w["A"]), cut(w["b"]), cut(w["bar_x"])
+            run = (lambda: (oracle.spd_solve(A, b, threads), oracle.spd_solve_vjp(A, b, bx, threads)))
+        else:
+            e_, M, bE = cut(w["e"]), cut(w["M"]), cut(w["bar_E"])
+            run = (lambda: (oracle.kepler(e_, M, threads), oracle.kepler_vjp(e_, M, bE, threads)))
+        run()                                           # the library loaded, the pages touched
+        best = float("inf")
+        for _ in range(2):
+            t0 = time.perf_counter()
+            run()
+            best = min(best, time.perf_counter() - t0)
+        return m / best
+
+    def e2e(self, steps: int = 3) -> dict:
+        """fwd + VJP through the public API (``runtime.run``) with the inputs
+        copied from pinned host memory every step and the outputs read back."""
+        import torch
+
+        from hawk_b200 import runtime
+
+        fwd_name, fwd_planes, fwd_values = self.kernels[0]
+        vjp_name, vjp_planes, vjp_values = self.kernels[1]
+        outs = set(self.outputs[fwd_name]) | set(self.outputs[vjp_name])
+        inputs = {k: v for k, v in {**fwd_planes, **vjp_planes}.items() if k not in outs}
+        host_in = {k: v.cpu().pin_memory() for k, v in inputs.items()}
+        host_out = {k: torch.empty(v.shape, dtype=v.dtype).pin_memory()
+                    for k, v in {**fwd_planes, **vjp_planes}.items() if k in outs}
+        fwd = runtime.load(BUNDLES, fwd_name, "float64", self.device)
+        vjp = runtime.load(BUNDLES, vjp_name, "float64", self.device)
+        stream = torch.cuda.current_stream(self.device)
+
+        def step():
+            for k, v in inputs.items():
+                v.copy_(host_in[k], non_blocking=True)
+            runtime.run(fwd, **fwd_planes, **fwd_values)
+            runtime.run(vjp, **vjp_planes, **vjp_values)
+            for k, v in host_out.items():
+                v.copy_(fwd_planes.get(k, vjp_planes.get(k)), non_blocking=True)
+
+        step()
+        torch.cuda.synchronize(self.device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            step()
+        b.record(stream)
+        b.synchronize()
+        ms = a.elapsed_time(b) / steps
+        h2d = sum(v.numel() * v.element_size() for v in host_in.values())
+        d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+        return {"value": self.n / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": steps}
+
+
+#: The configurations measured beside the headline: the per-GPU samples of each
+#: and the 1-thread / all-thread CPU samples of its fwd + VJP.
+SUITE = {"c1": (1 << 24, 1 << 22, 1 << 24), "c3": (1 << 23, 1 << 20, 1 << 22),
+         "c4": (1 << 20, 1 << 17, 1 << 19), "c5": (1 << 24, 1 << 17, 1 << 20)}
+SUITE_NAMES = {"c1": "energy", "c3": "gravity", "c4": "spd_solve", "c5": "kepler"}
+
+
+def run_suite(world: int, rank: int, local: int, dist) -> tuple:
+    """Every configuration beside the headline at its full size on every GPU
+    (weak scaling: each rank its own seeded samples): each kernel's device time
+    and HBM fraction, the whole job's fwd + VJP samples/s (slowest rank), every
+    output checked bit for bit against the oracle on every rank; on one GPU
+    also the oracle on 1 and all host threads and the public-API e2e.  Returns
+    (compact summary, detail)."""
+    import torch
+
+    pk = peaks()
+    cores = os.cpu_count() or 1
+    threads = max(1, cores // world)
+    compact, detail = {}, {}
+    for key, (n, cpu1, cpuall) in SUITE.items():
+        case = Case(key, n, seed=2000 + 97 * rank + ord(key[1]), device=local)
+        times = case.time()
+        par = case.parity(threads)
+        names = [k[0] for k in case.kernels]
+        ms = [times[k]["ms"] for k in names]
+        step_ms = max_over_ranks(ms[0] + ms[1], dist)
+        ok = all(par.values())
+        if dist is not None:
+            flag = torch.tensor([1.0 if ok else 0.0], dtype=torch.float64, device=f"cuda:{local}")
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+            ok = bool(flag.item() == 1.0)
+        rec = {"n": n, "sps": _sig(n * world / (step_ms * 1e-3)), "ms": [round(m, 4) for m in ms],
+               "bitwise": ok}
+        if key == "c5":
+            rec["fp64"] = [fp64_pipe_frac(k) for k in names]
+            rec["trips"] = round(float(case.kernels[0][1]["iters"].double().mean().item()), 3)
+        else:
+            rec["hbm"] = [round(BYTES_F64[k] * n / (m * 1e-3) / 1e9 / pk["hbm_gbs"], 3) for k, m in zip(names, ms)]
+        det = {"kernels": {k: {**times[k], "bitwise": par[k]} for k in names}, "n": n, "world": world}
+        if world == 1:
+            one = case.cpu_fwd_vjp(1, cpu1)
+            allc = case.cpu_fwd_vjp(cores, cpuall)
+            rec["cpu"] = [_sig(one), _sig(allc)]
+            det["cpu"] = {"threads": [1, cores], "samples": [cpu1, cpuall], "value": [one, allc], "kind": "port"}
+            e2e = case.e2e()
+            rec["e2e"] = _sig(e2e["value"])
+            det["e2e"] = e2e
+        compact[key] = rec
+        detail[SUITE_NAMES[key]] = det
+        del case
+        torch.cuda.empty_cache()
+    return compact, detail
+
+
+def run_scatter(local: int) -> dict:
+    """The scattered-commit kernels (hk/accum.cuh): 2^24 samples into
+    SCATTER_SLOTS slots, random keys for the atomics, sorted keys for the
+    warp-run commit; device time per launch and the streamed bytes' rate."""
     import torch
 
     from hawk_b200 import runtime, workloads
@@ -378,11 +720,11 @@ def run_configs(local: int) -> dict:
     def e(shape, dtype=torch.float64):
         return torch.empty(shape, dtype=dtype, device=dev)
 
-    def time_kernel(name, planes, values, n, mode="float64", key=None):
-        k = runtime.load(BUNDLES, name, mode, local)
+    def time_kernel(name, planes, n):
+        k = runtime.load(BUNDLES, name, "float64", local)
         bound = {key: from_torch(v) for key, v in planes.items()}
-        k.check(bound, values, n)
-        k.bind_all(bound, values, n)
+        k.check(bound, {}, n)
+        k.bind_all(bound, {}, n)
         stream = torch.cuda.current_stream(local).cuda_stream
         for _ in range(3):
             k.launch(0, n, n, stream)
@@ -395,77 +737,22 @@ def run_configs(local: int) -> dict:
             b.synchronize()
             times.append(a.elapsed_time(b))
         ms = statistics.median(times)
-        per = BYTES_F64[name] * (0.5 if mode == "float32" else 1.0)
-        gbs = per * n / (ms * 1e-3) / 1e9
-        info = k.entry.info(n)
-        out[key or name] = {"n": n, "ms": round(ms, 5), "samples_per_s": n / (ms * 1e-3), "gbs": round(gbs, 1),
-                            "hbm_frac": round(gbs / pk["hbm_gbs"], 4), "bytes_per_sample": per,
-                            "regs": info["regs"], "blocks_per_sm": info["blocks_per_sm"], "grid": info["grid"],
-                            "block": info["block"]}
+        gbs = BYTES_F64[name] * n / (ms * 1e-3) / 1e9
+        out[name] = {"n": n, "ms": round(ms, 5), "samples_per_s": n / (ms * 1e-3), "gbs": round(gbs, 1),
+                     "hbm_frac": round(gbs / pk["hbm_gbs"], 4)}
 
-    n = workloads.FULL_N["energy"]
-    w = workloads.energy(n, 1)
-    v = t(w["v"])
-    time_kernel("energy", {"v": v, "out": e(n)}, {}, n)
-    time_kernel("energy_vjp", {"v": v, "bar_out": t(w["bar_out"]), "bar_v": e((3, n))}, {}, n)
-    time_kernel("energy_jvp", {"v": v, "dot_v": t(w["dot_v"]), "dot_out": e(n)}, {}, n)
-    del v, w
-    # c2 in both scalar modes: the forward and the Param-gradient VJP (rows; the
-    # finish is the headline step's)
-    n = workloads.FULL_N["poly_loss"]
-    for mode, dt in (("float64", np.float64), ("float32", np.float32)):
-        w = workloads.poly_loss(n, 1, dtype=dt)
-        tdt = torch.float64 if mode == "float64" else torch.float32
-        x, tt = t(w["x"]), t(w["t"])
-        time_kernel("poly_loss", {"x": x, "t": tt, "r": e(n, tdt)}, {k: w[k] for k in ("a", "b", "c")}, n, mode,
-                    f"poly_loss.{mode}")
-        rows = -(-n // 32)
-        vp = {"x": x, "t": tt, "bar_r": t(w["bar_r"]),
-              **{k: torch.tensor([w[k]], dtype=tdt, device=dev) for k in ("a", "b", "c")},
-              **{k: e(rows, tdt) for k in ("bar_a", "bar_a_comp", "bar_b", "bar_b_comp", "bar_c", "bar_c_comp")}}
-        time_kernel("poly_loss_vjp", vp, {}, n, mode, f"poly_loss_vjp.{mode}")
-        del x, tt, vp, w
-    n = workloads.FULL_N["gravity"]
-    w = workloads.gravity(n, 1)
-    g = {k: t(w[k]) for k in ("r1", "r2", "m1", "m2")}
-    time_kernel("gravity", {**g, "f": e((3, n)), "u": e(n)}, {"G": 1.0}, n)
-    time_kernel("gravity_jvp", {**g, "dot_r1": t(w["dr1"]), "dot_r2": t(w["dr2"]), "dot_f": e((3, n)),
-                                "dot_u": e(n)}, {"G": 1.0}, n)
-    time_kernel("gravity_vjp", {**g, "bar_f": t(w["bar_f"]), "bar_u": t(w["bar_u"]), "bar_r1": e((3, n)),
-                                "bar_r2": e((3, n))}, {"G": 1.0}, n)
-    del g, w
-    n = workloads.FULL_N["spd_solve"]
-    w = workloads.spd_solve(n, 1)
-    A, b = t(w["A"]), t(w["b"])
-    time_kernel("spd_solve", {"A": A, "b": b, "x": e((6, n))}, {}, n)
-    time_kernel("spd_solve_vjp", {"A": A, "b": b, "bar_x": t(w["bar_x"]), "bar_A": e((6, 6, n)),
-                                  "bar_b": e((6, n))}, {}, n)
-    del A, b, w
-    n = workloads.FULL_N["kepler"]
-    w = workloads.kepler(n, 1)
-    kp = {"e": t(w["e"]), "M": t(w["M"])}
-    iters = e(n, torch.int32)
-    time_kernel("kepler", {**kp, "E": e(n), "iters": iters}, {}, n)
-    mean_trips = float(iters.double().mean().item())
-    time_kernel("kepler_vjp", {**kp, "bar_E": t(w["bar_E"]), "bar_e": e(n), "bar_M": e(n)}, {}, n)
-    out["kepler"]["mean_trips"] = round(mean_trips, 4)
-    out["kepler"]["bound"] = "fp64"
-    out["kepler_vjp"]["bound"] = "fp64"
-    del kp, iters, w
-    # scattered commits (hk/accum.cuh): 2^24 samples into SCATTER_SLOTS slots,
-    # random keys for the atomics, sorted keys for the warp-run commit
     n = 1 << 24
     w = workloads.scatter(n, 1, slots=SCATTER_SLOTS)
     x, key, skey = t(w["x"]), t(w["key"]), t(w["sorted_key"])
     segs = -(-n // workloads.SEGMENT)
-    time_kernel("segment_sum", {"x": x, "acc": e(segs), "acc_c": e(segs)}, {}, n)
-    time_kernel("keyed_sum", {"x": x, "key": skey, "acc": e(SCATTER_SLOTS)}, {}, n)
-    time_kernel("histogram", {"x": x, "key": key, "acc": e(SCATTER_SLOTS), "acc_c": e(SCATTER_SLOTS)}, {}, n)
-    time_kernel("bitmask", {"bits": t(w["bits"]), "key": key, "acc": e(SCATTER_SLOTS, torch.uint32)}, {}, n)
+    time_kernel("segment_sum", {"x": x, "acc": e(segs), "acc_c": e(segs)}, n)
+    time_kernel("keyed_sum", {"x": x, "key": skey, "acc": e(SCATTER_SLOTS)}, n)
+    time_kernel("histogram", {"x": x, "key": key, "acc": e(SCATTER_SLOTS), "acc_c": e(SCATTER_SLOTS)}, n)
+    time_kernel("bitmask", {"bits": t(w["bits"]), "key": key, "acc": e(SCATTER_SLOTS, torch.uint32)}, n)
     idx, wt, table = t(w["idx"]), t(w["w"]), t(w["table"])
-    time_kernel("gather", {"idx": idx, "w": wt, "table": table, "y": e(n)}, {}, n)
+    time_kernel("gather", {"idx": idx, "w": wt, "table": table, "y": e(n)}, n)
     time_kernel("gather_vjp", {"idx": idx, "w": wt, "table": table, "bar_y": t(w["bar_y"]), "bar_w": e(n),
-                               "bar_table": e(SCATTER_SLOTS)}, {}, n)
+                               "bar_table": e(SCATTER_SLOTS)}, n)
     for name in ("segment_sum", "keyed_sum", "histogram", "bitmask", "gather", "gather_vjp"):
         out[name]["slots"] = SCATTER_SLOTS if name != "segment_sum" else segs
         out[name]["bound"] = "atomics" if name in ("histogram", "bitmask", "gather_vjp") else "hbm"
@@ -852,7 +1139,7 @@ def run_only_steps(name: str, n: int, steps: int, warmup: int, local: int, persi
 
 def _only_planes(name: str, n: int, dev):
     """Seeded planes of a scatter or team-form benchmark kernel at ``n``
-    samples (lanes), as ``run_configs`` / ``run_team`` bind them."""
+    samples (lanes), as ``run_scatter`` / ``run_team`` bind them."""
     import torch
 
     from hawk_b200 import workloads
@@ -1051,14 +1338,24 @@ def main() -> int:
     dist = init_dist(world, local)
     torch.cuda.set_device(local)
     res = run_headline(args, world, rank, local, dist)
-    configs = None
-    if world == 1 and not args.no_configs:
-        configs = run_configs(local)
-        configs["stepping"] = run_steps(local)
-        configs["team"] = run_team(local)
-        configs["keyed"] = run_keyed(local)
+    configs, detail = {}, {}
+    if not args.no_configs:
+        configs, detail = run_suite(world, rank, local, dist)
+        configs["c2f32"] = run_c2_variant(args, world, rank, local, dist, "float32", None)
+        if world > 1:
+            # strong scaling: the headline's 2^26-sample job cut over the ranks
+            configs["c2strong"] = run_c2_variant(args, world, rank, local, dist, args.mode, args.n)
+        if world == 1:
+            detail["scatter"] = run_scatter(local)
+            detail["stepping"] = run_steps(local)
+            detail["team"] = run_team(local)
+            detail["keyed"] = run_keyed(local)
     cpu = cpu_baseline(args.mode, args.cpu_sample) if (rank == 0 and world == 1) else None
     if rank == 0:
+        if detail:
+            # the per-kernel detail (stages, registers, grids, CPU samples) on
+            # stderr; stdout holds the one JSON line
+            print(json.dumps({"detail": detail}), file=sys.stderr, flush=True)
         line = {
             "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
@@ -1069,11 +1366,15 @@ def main() -> int:
                        "samples_per_gpu": args.n, "mode": args.mode, "parallelism": f"samples x{world}",
                        "l2": "inputs 1.5 GB/GPU > 126 MB L2, no flush"},
             "roofline": res["roofline"], "e2e": res["e2e"], "gpu_launches": res["gpu_launches"],
-            "clocks": res["clocks"], "cpu_baseline": cpu, "kernels_ms": res["kernels_ms"],
-            "fwd_gbs": res["fwd_gbs"], "vjp_gbs": res["vjp_gbs"], "check": res["check"],
+            "clocks": res["clocks"], "cpu_baseline": cpu, "parity": res["parity"],
+            "kernels_ms": res["kernels_ms"], "fwd_gbs": res["fwd_gbs"], "vjp_gbs": res["vjp_gbs"],
+            # last, so that a record keeping the end of the line keeps it: per
+            # configuration n per GPU, whole-job fwd+VJP samples/s (sps), each
+            # kernel's ms and HBM (FP64-pipe for c5) fraction, outputs bitwise
+            # equal to the oracle on every rank, CPU oracle [1 thread, all
+            # threads] and public-API e2e samples/s (one GPU)
+            "configs": configs,
         }
-        if configs is not None:
-            line["configs"] = configs
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
