@@ -7,7 +7,7 @@ using Int = long long;
 
 HK_SELF_CHECK_EXPORTS
 
-extern "C" __global__ void __launch_bounds__(256) energy_jvp(
+extern "C" __global__ void __launch_bounds__(128, 13) energy_jvp(
     hk::abi::ScalarHandle p_mut_dot_out,
     hk::abi::GRefMirror p_vin_dot_v,
     hk::abi::GRefMirror p_vin_v,

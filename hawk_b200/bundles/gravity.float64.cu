@@ -7,7 +7,7 @@ using Int = long long;
 
 HK_SELF_CHECK_EXPORTS
 
-extern "C" __global__ void __launch_bounds__(256) gravity(
+extern "C" __global__ void __launch_bounds__(128, 11) gravity(
     hk::abi::GRefMirror p_mut_f,
     hk::abi::ScalarHandle p_mut_u,
     hk::abi::GRefMirror p_vin_r1,

@@ -7,7 +7,7 @@ using Int = long long;
 
 HK_SELF_CHECK_EXPORTS
 
-extern "C" __global__ void __launch_bounds__(256) spd_solve(
+extern "C" __global__ void __launch_bounds__(128, 5) spd_solve(
     hk::abi::GRefMirror p_mut_x,
     hk::abi::GRefMirror p_vin_b,
     hk::abi::GRefMirror p_mtx_A,

@@ -7,7 +7,7 @@ using Int = long long;
 
 HK_SELF_CHECK_EXPORTS
 
-extern "C" __global__ void __launch_bounds__(256, 2) spd_solve_vjp(
+extern "C" __global__ void __launch_bounds__(128, 5) spd_solve_vjp(
     hk::abi::GRefMirror p_mut_bar_A,
     hk::abi::GRefMirror p_mut_bar_b,
     hk::abi::GRefMirror p_vin_b,

@@ -326,14 +326,17 @@ int hkb_library_entry(hkb_library* lib, const char* name, hkb_entry** out) {
         cudaGetLastError();
     }
     // Threads per block: the size that keeps the most warps resident per SM (the
-    // register file is the limit of a heavy entry: at 98 registers, 256-thread
-    // blocks leave 16 warps, 32-thread blocks 19), the larger on a tie.  Every
+    // register file is the limit of a heavy entry: each quarter of the SM holds
+    // 16384 registers, so at 98 registers a thread four warps fit a quarter and
+    // at 96 five -- the unit asks for such a cap with __launch_bounds__(128, 5)),
+    // the larger on a tie, never more than the entry was compiled for.  Every
     // frame indexes by blockDim; a staged entry's tiles assume 256 threads.
     const int candidates[] = {256, 128, 96, 64, 32};
     int best_warps = -1;
     for (int b : candidates) {
         if (entry->team != 0) b = entry->team;          // a team is its block
         else if (entry->dynamic_smem != 0 && b != kBlock) continue;
+        else if (b > attr.maxThreadsPerBlock) continue;
         int bps = 0;
         e2 = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, reinterpret_cast<const void*>(kernel), b,
                                                            entry->dynamic_smem);

@@ -117,11 +117,12 @@ def _word_read() -> str:
 
 
 def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: bool = True,
-                min_blocks: int | None = None) -> Unit:
+                min_blocks: int | None = None, threads: int | None = None) -> Unit:
     """The b200 unit of a traced kernel (``hawk.Kernel``) in scalar mode ``mode``;
     ``staged`` streams its inputs through shared-memory stages filled by the
     TMA unit (hk/stage.cuh) where the stage plan fits; ``min_blocks`` caps the
-    entry's registers so that many 256-thread blocks stay resident per SM."""
+    entry's registers so that that many blocks of ``threads`` (256 when None)
+    stay resident per SM."""
     from hawk.ir.nodes import sample_sums
     from hawk.emit.render import render_body
     from hawk.emit.spelling import element_spelling
@@ -196,7 +197,7 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
     parts = [
         *([f'extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__{name} = {smem_entry}u;']
           if smem_entry else []),
-        wrapper.entry_signature(walk, name, min_blocks),
+        wrapper.entry_signature(walk, name, min_blocks, threads),
         "{",
         wrapper.unpack(walk, plan),
         *run_states,
@@ -229,6 +230,7 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
                 digest=hashlib.sha256(text.encode()).hexdigest(),
                 notes={"dynamic_smem": smem, "staged": plan is not None,
                        "stages": plan.stages if plan is not None else 0, "min_blocks": min_blocks or 0,
+                       "block": threads or 256,
                        "persist": f"{name}{PERSIST_SUFFIX}" if persist is not None else None,
                        "range": f"{name}{RANGE_SUFFIX}" if ranged is not None else None,
                        "step_fp64_ops": step_fp64_ops(kernel) if persist is not None else None,
