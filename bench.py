@@ -303,7 +303,7 @@ def headline_parity(s: PolyStep, world: int, dist) -> dict:
     got = [float(v) for v in s.cells.cpu().tolist()]
     if world == 1:
         want = [float(oracle.cells_finish(hi[k], comp[k])) for k in range(3)]
-    elif s.mode == "float64":
+    else:
         parts = [oracle.cells_leaves(hi[k], comp[k]) for k in range(3)]
         pack = torch.tensor(np.stack([np.stack([p[0] for p in parts]), np.stack([p[1] for p in parts])]),
                             device=s.dev)
@@ -313,8 +313,6 @@ def headline_parity(s: PolyStep, world: int, dist) -> dict:
         all_hi = np.concatenate([g[r, 0] for r in range(world)], axis=1)
         all_comp = np.concatenate([g[r, 1] for r in range(world)], axis=1)
         want = [float(oracle.cells_tree(all_hi[k], all_comp[k])) for k in range(3)]
-    else:
-        return {"cells_bitwise": None, "why": "the oracle's leaf stage is float64 only"}
     ok = got == want
     if dist is not None:
         flag = torch.tensor([1.0 if ok else 0.0], dtype=torch.float64, device=s.dev)

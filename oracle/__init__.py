@@ -80,6 +80,8 @@ _SIGS = {
     "hko_cells_finish_f32": (_F, [ctypes.c_int, _P, _P, _I]),
     "hko_cells_leaves_d": (None, [ctypes.c_int, _P, _P, _I, _P, _P]),
     "hko_cells_tree_d": (_D, [ctypes.c_int, _P, _P, _I]),
+    "hko_cells_leaves_f": (None, [ctypes.c_int, _P, _P, _I, _P, _P]),
+    "hko_cells_tree_f": (_F, [ctypes.c_int, _P, _P, _I]),
     "hko_gravity": (None, [_P, _P, _I, _P, _P, _D, _P, _I, _P, _I, _I]),
     "hko_gravity_jvp": (None, [_P, _P, _P, _P, _I, _P, _P, _D, _P, _I, _P, _I, _I]),
     "hko_gravity_vjp": (None, [_P, _P, _P, _I, _P, _P, _P, _D, _P, _P, _I, _I, _I]),
@@ -194,17 +196,23 @@ def cells_finish(hi: np.ndarray, comp: np.ndarray | None, op: str = "sum"):
 
 
 def cells_leaves(hi: np.ndarray, comp: np.ndarray, op: str = "sum"):
-    """The leaf partials ``(leaf_hi, leaf_comp)`` of float64 rows (4096 rows a leaf)."""
+    """The leaf partials ``(leaf_hi, leaf_comp)`` of float64 or float32 rows
+    (4096 rows a leaf), in the rows' type."""
     hi, comp = np.ascontiguousarray(hi), np.ascontiguousarray(comp)
     leaves = -(-hi.shape[0] // 4096)
-    lh, lc = np.empty(leaves), np.empty(leaves)
-    lib().hko_cells_leaves_d(OP[op], _p(hi), _p(comp), hi.shape[0], _p(lh), _p(lc))
+    lh, lc = np.empty(leaves, dtype=hi.dtype), np.empty(leaves, dtype=hi.dtype)
+    fn = lib().hko_cells_leaves_d if hi.dtype == np.float64 else lib().hko_cells_leaves_f
+    fn(OP[op], _p(hi), _p(comp), hi.shape[0], _p(lh), _p(lc))
     return lh, lc
 
 
 def cells_tree(leaf_hi: np.ndarray, leaf_comp: np.ndarray, op: str = "sum") -> float:
-    lh, lc = np.array(leaf_hi, dtype=np.float64), np.array(leaf_comp, dtype=np.float64)
-    return lib().hko_cells_tree_d(OP[op], _p(lh), _p(lc), lh.shape[0])
+    """The pairwise levels over leaf partials (float64 unless both are float32)."""
+    f32 = np.asarray(leaf_hi).dtype == np.float32 and np.asarray(leaf_comp).dtype == np.float32
+    dt = np.float32 if f32 else np.float64
+    lh, lc = np.array(leaf_hi, dtype=dt), np.array(leaf_comp, dtype=dt)
+    fn = lib().hko_cells_tree_f if f32 else lib().hko_cells_tree_d
+    return fn(OP[op], _p(lh), _p(lc), lh.shape[0])
 
 
 def cells_tree_pair(leaf_hi: np.ndarray, leaf_comp: np.ndarray, op: str = "sum") -> tuple:

@@ -171,3 +171,20 @@ def test_a_rank_that_leaves_between_steps_ends_the_others_next_gather_with_an_er
     assert results[1][1] == "left"
     assert results[0][1].startswith("error"), results
     assert results[0][2] < 60.0, results
+
+
+@pytest.mark.parametrize("dtype", [np.float64, np.float32])
+def test_leaf_stage_and_tree_are_the_finish(dtype):
+    """The oracle's finish split where the ranks split it: leaf partials, then
+    the tree over them, equal the one-pass finish bit for bit (both types)."""
+    import oracle
+
+    rng = np.random.default_rng(5)
+    n = 3 * 131072 + 777
+    x = rng.uniform(-2, 2, n).astype(dtype)
+    t = (x + 0.1 * rng.standard_normal(n)).astype(dtype)
+    hi, comp = oracle.poly_loss_vjp_rows(x, t, np.ones(n, dtype=dtype), dtype(0.5), dtype(-1.0), dtype(2.0))
+    for k in range(3):
+        lh, lc = oracle.cells_leaves(hi[k], comp[k])
+        assert lh.dtype == dtype and lh.shape[0] == sharded.leaves_of(n)
+        assert oracle.cells_tree(lh, lc) == oracle.cells_finish(hi[k], comp[k])
