@@ -87,9 +87,10 @@ class DeviceKernel:
         self.directory = Path(directory)
         stem = f"{kernel}.{mode}"
         if sidecar is None:
-            path = self.directory / f"{stem}.json"
-            if not path.exists():
-                raise HawkError(f"no b200 artifact {stem!r} in {self.directory} (no {path.name})")
+            path = sidecar_path(self.directory, kernel, mode)
+            if path is None:
+                raise HawkError(f"no b200 artifact {stem!r} in {self.directory} (no {stem}.json, nor a "
+                                f"{kernel}.json of scalar type {mode})")
             sidecar = json.loads(path.read_text())
         if "b200" not in sidecar:
             raise HawkError(f"{stem}: its sidecar carries no 'b200' block; it was not built for the b200 target")
@@ -718,15 +719,30 @@ _CACHE: dict = {}
 _CACHE_LOCK = threading.Lock()
 
 
+def sidecar_path(directory, kernel: str, mode: str):
+    """The sidecar of ``kernel`` in ``mode``: ``<kernel>.<mode>.json`` (this
+    build's bundles), else the reference's ``<kernel>.json`` when it records
+    that scalar type (a bundle the reference's ``hawk.build`` wrote for the
+    b200 row); None when neither is there."""
+    directory = Path(directory)
+    path = directory / f"{kernel}.{mode}.json"
+    if path.exists():
+        return path
+    path = directory / f"{kernel}.json"
+    if path.exists() and json.loads(path.read_text()).get("scalar_type", "float64") == mode:
+        return path
+    return None
+
+
 def load(directory, kernel: str, mode: str = "float64", device: int | None = None):
-    """Load ``<directory>/<kernel>.<mode>.cubin`` on ``device`` (cached per
-    process): a ``DeviceKernel``, or a ``SplitKernel`` for a kernel built as
-    stages."""
+    """Load ``kernel``'s b200 artifact in scalar mode ``mode`` from ``directory``
+    on ``device`` (cached per process): a ``DeviceKernel``, or a ``SplitKernel``
+    for a kernel built as stages."""
     key = (str(Path(directory).resolve()), kernel, mode, device if device is not None else _current_device())
     with _CACHE_LOCK:
         if key not in _CACHE:
-            path = Path(directory) / f"{kernel}.{mode}.json"
-            split = path.exists() and "split" in json.loads(path.read_text()).get("b200", {})
+            path = sidecar_path(directory, kernel, mode)
+            split = path is not None and "split" in json.loads(path.read_text()).get("b200", {})
             _CACHE[key] = (SplitKernel if split else DeviceKernel)(directory, kernel, mode, key[3])
         return _CACHE[key]
 

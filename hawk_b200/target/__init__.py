@@ -27,14 +27,16 @@ NVRTC_SM100A = "nvrtc-sm100a"
 
 
 def row():
-    """The b200 ``Target`` row."""
-    from hawk.targets import FEATURES, Target
+    """The b200 ``Target`` row: its ``features`` are exactly the entries of the
+    reference's feature table (hawk/targets/features.py:74-152) the b200 build
+    makes (``BUILT_FEATURES``); the render refuses the rest by name."""
+    from hawk.targets import Target
+    from .assemble import BUILT_FEATURES
     from .wrapper import B200
     from .writer import B200_WRITER
 
     return Target("b200", "builds for the B200 (sm_100a) through NVRTC", B200_WRITER, B200,
-                  NVRTC_SM100A, "device", "cubin", ".cubin", ".cu",
-                  frozenset(f for f in FEATURES if f in ("linalg",)) | {"loops"})
+                  NVRTC_SM100A, "device", "cubin", ".cubin", ".cu", BUILT_FEATURES)
 
 
 def install() -> None:

@@ -43,6 +43,31 @@ _UNBUILT = {
 }
 
 
+#: The entries of the reference's feature table (hawk/targets/features.py:74-152)
+#: the b200 row builds; a kernel using any other is refused by the table's own
+#: predicate, with its reason and the alternative it names.
+BUILT_FEATURES = frozenset({"linalg", "sample_reduction", "cross_sample_at", "compensated", "two_path",
+                            "zero_trip_loop"})
+
+
+def refuse_features(name: str, kernel, walk, sinks) -> None:
+    """Refuse the first feature of the reference's table that the kernel uses
+    and the b200 row does not build, by name (the reference's C row refuses
+    the same way, hawk/embedded/verify.py:110-123)."""
+    from hawk.embedded.verify import _every_node, _top
+    from hawk.targets import FEATURES
+
+    kind = getattr(kernel, "kind", None)
+    nodes = list(_every_node(_top(sinks)))
+    for feature, (predicate, (why, fix)) in FEATURES.items():
+        if feature in BUILT_FEATURES:
+            continue
+        hit = predicate(kernel, kind, walk, nodes)
+        if hit is not None:
+            raise HawkError(f"{name!r}: the b200 target does not build the feature {feature!r} "
+                            f"(at {hit[1]} {hit[0]}): {why}; {fix}")
+
+
 #: The team-form calls the device library builds (hk/team.cuh).
 TEAM_BUILT = frozenset({"Team", "TeamCholesky", "TeamLu", "cholesky", "choleskyFrom", "choSolve", "triLower",
                         "triUpperT", "lu", "luSolve", "luSolveT", "luInverse", "luDet", "blockSum",
@@ -132,7 +157,9 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
     name = name or kernel.name
     walk, sinks = kernel.walk, kernel.sinks
     _refuse(name, walk)
-    rendered = render_body(sinks, walk, indent="        ", writer=B200_WRITER)
+    refuse_features(name, kernel, walk, sinks)
+    kind = getattr(kernel, "kind", None)
+    rendered = render_body(sinks, walk, indent="        ", kind=kind, writer=B200_WRITER)
     body = body_text(rendered.text)
     refuse_unbuilt(name, body)
     sums = sample_sums(sinks)
@@ -174,7 +201,7 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
             # branch per launch on the fused_steps word -- 1 runs the single step's
             # body, any other word the fused loop (hawk/emit/wrapper.py:1507-1545)
             plan, smem = None, 0
-            single = render_body(one_step.sinks, one_step.walk, indent="        ", writer=B200_WRITER)
+            single = render_body(one_step.sinks, one_step.walk, indent="        ", kind=kind, writer=B200_WRITER)
             loop = [f"    if ({_word_read()} == 1) {{",
                     wrapper.index_prologue(), body_text(single.text), wrapper.index_epilogue(),
                     "    } else {",

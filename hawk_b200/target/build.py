@@ -163,19 +163,14 @@ def build_split_kernel(kernel, directory, *, name: str | None = None, mode: str 
     return sidecar
 
 
-def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "float64",
-                 staged: bool | None = None, bounds: tuple | None = None) -> dict:
-    """Render, compile and write one kernel's b200 artifact; returns its sidecar.
-    ``staged`` streams the inputs through TMA-filled shared-memory stages;
-    ``None`` decides by the unstaged entry's register count.  A kernel the
-    reference's split cuts into stages is built by ``build_split_kernel``."""
-    from .split import expand
-
-    name = name or kernel.name
-    if expand(kernel, name, mode) is not None:
-        return build_split_kernel(kernel, directory, name=name, mode=mode)
-    directory = Path(directory)
-    directory.mkdir(parents=True, exist_ok=True)
+def choose_unit(kernel, name: str, mode: str = "float64", staged: bool | None = None,
+                bounds: tuple | None = None) -> tuple:
+    """The unit the b200 row builds for a (not split) kernel and its compile:
+    ``(unit, cubin, log, ptxas)``.  The policy, by the entry's registers:
+    above ``REGISTER_BOUND`` a cap to two 256-thread blocks a SM, or staged
+    inputs where that cap spills; then, one warp slot short of the next, the
+    cap ``next_slot_bounds`` gives where it does not spill.  ``staged`` True
+    asks for the staged unit, ``bounds`` for a fixed ``(threads, blocks)``."""
     if bounds is not None:
         unit = render_unit(kernel, name, mode, staged=False, threads=bounds[0], min_blocks=bounds[1])
     else:
@@ -198,16 +193,18 @@ def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "flo
         c_cubin, c_log, c_ptxas = compile_cubin(capped.text, name)
         if not _spills(c_ptxas, name):
             unit, cubin, log, ptxas = capped, c_cubin, c_log, c_ptxas
-    stem = f"{name}.{mode}"
-    (directory / f"{stem}.cu").write_text(unit.text)
-    (directory / f"{stem}.cubin").write_bytes(cubin)
-    sidecar = _reference_sidecar(name, kernel.walk, mode, getattr(kernel, "lane_space", None))
-    sidecar = json.loads(json.dumps(sidecar, default=str))
-    sidecar["b200"] = {
+    return unit, cubin, log, ptxas
+
+
+def b200_block(unit, walk, ptxas: dict, name: str, unit_file: str, cubin_file: str) -> dict:
+    """The sidecar's ``b200`` block: what the b200 runtime binds and launches
+    from (the entry, its frame, sample sums, slot records, register policy,
+    the NVRTC options and the ptxas report)."""
+    return {
         "entry": name,
         "arch": ARCH,
-        "unit": f"{stem}.cu",
-        "cubin": f"{stem}.cubin",
+        "unit": unit_file,
+        "cubin": cubin_file,
         "unit_digest": unit.digest,
         "frame": unit.frame,
         "dynamic_smem": unit.notes.get("dynamic_smem", 0),
@@ -221,10 +218,32 @@ def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "flo
         "folds": unit.notes.get("folds") or {},
         "private_targets": unit.notes.get("private_targets") or [],
         "sample_sums": [{"name": n, "op": op, "companion": comp} for n, op, comp in unit.sums],
-        "slots": _slot_records(kernel.walk),
+        "slots": _slot_records(walk),
         "nvrtc_options": [o for o in options() if not o.startswith("-I")],
         "ptxas": ptxas,
     }
+
+
+def build_kernel(kernel, directory, *, name: str | None = None, mode: str = "float64",
+                 staged: bool | None = None, bounds: tuple | None = None) -> dict:
+    """Render, compile and write one kernel's b200 artifact; returns its sidecar.
+    ``staged`` streams the inputs through TMA-filled shared-memory stages;
+    ``None`` decides by the unstaged entry's register count.  A kernel the
+    reference's split cuts into stages is built by ``build_split_kernel``."""
+    from .split import expand
+
+    name = name or kernel.name
+    if expand(kernel, name, mode) is not None:
+        return build_split_kernel(kernel, directory, name=name, mode=mode)
+    directory = Path(directory)
+    directory.mkdir(parents=True, exist_ok=True)
+    unit, cubin, log, ptxas = choose_unit(kernel, name, mode, staged, bounds)
+    stem = f"{name}.{mode}"
+    (directory / f"{stem}.cu").write_text(unit.text)
+    (directory / f"{stem}.cubin").write_bytes(cubin)
+    sidecar = _reference_sidecar(name, kernel.walk, mode, getattr(kernel, "lane_space", None))
+    sidecar = json.loads(json.dumps(sidecar, default=str))
+    sidecar["b200"] = b200_block(unit, kernel.walk, ptxas, name, f"{stem}.cu", f"{stem}.cubin")
     (directory / f"{stem}.json").write_text(json.dumps(sidecar, indent=1, sort_keys=True))
     return sidecar
 

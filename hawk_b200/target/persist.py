@@ -235,7 +235,8 @@ def range_entry(kernel, name: str, wrapper) -> str | None:
 
     counter = binding_name("lookup", _counter_name(kernel))
     on_entry = f"hawk_abi::finish_count({counter});"
-    single = body_text(render_body(one_step.sinks, one_step.walk, indent="        ", writer=B200_WRITER).text)
+    single = body_text(render_body(one_step.sinks, one_step.walk, indent="        ", kind=getattr(kernel, "kind", None),
+                                   writer=B200_WRITER).text)
     pre, step, post = body_text(split.pre), body_text(split.step), body_text(split.post)
     guard = body_text(split.guard) if split.guard is not None else None
     carries = [(f"hk_c{j}", _carry_type(t), cname, body_text(init), nxt)

@@ -48,7 +48,8 @@ def refill_frame(kernel, walk) -> str | None:
     cut = interchanged_loops(walk)
     if len(cut) != 1:
         return None
-    seg = render_lane_segments(kernel.sinks, walk, cut, indent="            ", writer=B200_WRITER)
+    seg = render_lane_segments(kernel.sinks, walk, cut, indent="            ", kind=getattr(kernel, "kind", None),
+                               writer=B200_WRITER)
     if seg.guard is not None or len(seg.segments) != 2 or len(seg.loops) != 1:
         return None
     loop = seg.loops[0]

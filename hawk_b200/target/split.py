@@ -170,7 +170,8 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
         else:                       # a copy stage: the stage's own sinks, a block per lane
             from hawk.emit.render import render_body
 
-            body = body_text(render_body(member.sinks, walk, indent="        ", writer=B200_WRITER).text)
+            body = body_text(render_body(member.sinks, walk, indent="        ", kind=getattr(member, "kind", None),
+                                         writer=B200_WRITER).text)
             smem = 0
         refuse_unbuilt(member.name, body)
         team_record = dict(record.get("team") or {})
