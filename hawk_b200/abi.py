@@ -73,8 +73,33 @@ def lib() -> ctypes.CDLL:
                 fn = getattr(handle, name)
                 fn.restype = res
                 fn.argtypes = args
+            check_build_digest(handle.hkb_build_digest().decode(), sources_digest())
             _LIB = handle
         return _LIB
+
+
+def sources_digest():
+    """The digest of the library's sources beside the package (the digest its
+    build stamps in, ``hawk_b200.csrc.build.source_digest``), or None where the
+    sources are not shipped."""
+    try:
+        from .csrc import build
+    except ImportError:
+        return None
+    if not all(p.exists() for p in build.SOURCES + build.HEADERS):
+        return None
+    return build.source_digest()
+
+
+def check_build_digest(built: str, sources) -> None:
+    """Refuse a library built from other sources than the ones beside it (the
+    reference refuses a stale extension the same way at import,
+    hawk/__init__.py:128-209): its kernels and ABI would not be the ones the
+    headers and units here declare."""
+    if sources is not None and built != sources:
+        raise HawkError(f"{LIBRARY_PATH.name} is stale: it was built from sources whose digest is "
+                        f"{built[:16]}..., the sources beside it now hash to {sources[:16]}...; "
+                        "rebuild it with `python -m hawk_b200.csrc.build`")
 
 
 def check(status: int, what: str) -> None:

@@ -38,6 +38,9 @@ g2 segment_sum     acc[i / 256] += x, the default (compensated) policy: the key
 g3 keyed_sum       acc[key] += x over a Sorted key (runs found per warp)
 g4 histogram       acc[key] += x over any key, compensated
 g5 bitmask         acc[key] |= bits (32-bit words)
+g6 comp_scatter    acc[key] += x under the compensated sink policy (a Kind):
+                   each add's rounding error committed into the kernel's own
+                   companion plane acc_c
 """
 
 from __future__ import annotations
@@ -49,6 +52,7 @@ hawk = load()
 import hawk.math as m  # noqa: E402
 from hawk import Grid, Index, Int32, Kernel, Matrix, Mutable, Param, Scalar, Sorted, Table, Terminated, UInt32, Vector  # noqa: E402,E501
 from hawk.diff import jvp, param_planes, vjp  # noqa: E402
+from hawk.ext import Kind, sink_policy  # noqa: E402
 
 
 @hawk.kernel
@@ -237,6 +241,17 @@ def histogram(x: Scalar, key: Index, acc: Mutable[Scalar]):
 @hawk.kernel
 def bitmask(bits: UInt32, key: Index, acc: Mutable[UInt32]):
     hawk.scatter(acc, policy="or")[key] |= bits
+
+
+#: The compensated sink policy (hawk/ext): the scatter's plain commit into acc
+#: becomes a compensated one whose residuals go to the declared plane acc_c.
+COMPENSATED_SINK = Kind("compensated", sink=sink_policy("compensated", into="acc_c"))
+
+
+@hawk.kernel(kind=COMPENSATED_SINK)
+def comp_scatter(x: Scalar, key: Index, acc: Mutable[Scalar], acc_c: Mutable[Scalar]):
+    hawk.scatter(acc, policy="plain")[key] += x
+    hawk.scatter(acc_c, policy="plain")[key] += 0.0
 
 
 @hawk.kernel
@@ -505,6 +520,7 @@ KERNELS = {
     "keyed_sum": (keyed_sum, ("float64",)),
     "histogram": (histogram, ("float64",)),
     "bitmask": (bitmask, ("float64",)),
+    "comp_scatter": (comp_scatter, ("float64",)),
     **{name: (k, ("float64", "float32") if name == "warp_eigvals_32" else ("float64",))
        for name, k in TEAM_KERNELS.items()},
     **{name: (k, ("float64",)) for name, k in READBACK_KERNELS.items()},

@@ -29,6 +29,7 @@ serialises its bind+launch under its lock, as the reference's HostKernel does
 from __future__ import annotations
 
 import ctypes
+import hashlib
 import json
 import threading
 from pathlib import Path
@@ -79,6 +80,13 @@ def _box(kind: str, value):
     raise HawkError(f"slot kind {kind!r} is not a by-value slot")
 
 
+#: Bits of a unit's error word (hk/stage.cuh) and what each reports.
+WAIT_FULL, WAIT_EMPTY, WAIT_DRAIN = 1, 2, 4
+WAIT_ERRORS = {WAIT_FULL: "a staged input tile did not arrive within the wait limit",
+               WAIT_EMPTY: "a shared-memory stage was not released within the wait limit",
+               WAIT_DRAIN: "a block gave up with copies into shared memory still in flight"}
+
+
 class DeviceKernel:
     """One b200 artifact's entry on one device, self-checked at load."""
 
@@ -98,6 +106,7 @@ class DeviceKernel:
         self.name = sidecar["kernel"]
         self.mode = sidecar.get("scalar_type", mode)
         b200 = sidecar["b200"]
+        check_unit_digest(self.directory, b200)
         self.frame = b200["frame"]
         self.sums = b200["sample_sums"]
         self.slots = [(s["role"], s["name"], s["dtype"], tuple(s["shape"])) for s in b200["slots"]]
@@ -118,6 +127,7 @@ class DeviceKernel:
         self.folds = {t: self.library.entry(e) for t, e in (b200.get("folds") or {}).items()}
         self.descriptor = descriptor_for_sidecar(sidecar)
         self.block = abi.ArgBlock(self.descriptor)
+        self.poisoned = ""
         self._lock = threading.Lock()
         self._held: list = []
         self._scratch: dict = {}
@@ -292,11 +302,38 @@ class DeviceKernel:
         self._held = held
 
     def launch(self, base: int, count: int, n_samples: int, stream: int | None = None) -> None:
-        """The launch crossing over ``[base, base + count)`` of the bound planes."""
+        """The launch crossing over ``[base, base + count)`` of the bound planes.
+        An entry that stages its inputs through shared memory waits on the
+        copies with bounded waits: after its launch the stream is synchronised
+        and the unit's error word checked (``check_waits``)."""
         if self.frame == "row" and base % ROW:
             raise HawkError(f"kernel {self.name!r} reduces over 32-sample rows, so a partition must "
                             f"start on a row (base % 32 == 0), got base={base}")
-        self.entry.launch(self.block, base, count, n_samples, _stream(stream, self.device))
+        if self.poisoned:
+            raise HawkError(self.poisoned)
+        s = _stream(stream, self.device)
+        self.entry.launch(self.block, base, count, n_samples, s)
+        if self.sidecar["b200"].get("stages"):
+            _torch_stream(s, self.device).synchronize()
+            self.check_waits()
+
+    def check_waits(self) -> None:
+        """Read and clear the unit's error word and refuse what it reports: a
+        stage's copy that did not arrive, or a stage not released, within the
+        wait limit (the launch's outputs are incomplete); a block that gave up
+        with copies into shared memory still in flight (``kErrDrain``), after
+        which this unit is not launched again in this process -- another block
+        may have been given that shared memory while the copy was landing."""
+        flags = self.library.errors(clear=True)
+        if not flags:
+            return
+        what = [text for bit, text in WAIT_ERRORS.items() if flags & bit]
+        message = f"kernel {self.name!r}: {'; '.join(what) or f'error word {flags:#x}'}"
+        if flags & WAIT_DRAIN:
+            self.poisoned = (message + "; the unit is not launched again in this process (reload the "
+                             "library in a new process)")
+            raise HawkError(self.poisoned)
+        raise HawkError(message + "; the launch's outputs are incomplete")
 
     def cells_state(self, n: int):
         """The kernel's own cell scratch at sample count ``n`` (made once per n):
@@ -433,6 +470,7 @@ class SplitKernel:
         self.name = sidecar["kernel"]
         self.mode = sidecar.get("scalar_type", mode)
         b200 = sidecar["b200"]
+        check_unit_digest(self.directory, b200)
         self.device = int(device if device is not None else _current_device())
         self.team_planes = sidecar.get("team_planes") or {}
         self.keyed = sidecar.get("keyed") or {}
@@ -717,6 +755,19 @@ class SplitKernel:
 
 _CACHE: dict = {}
 _CACHE_LOCK = threading.Lock()
+
+
+def check_unit_digest(directory, b200: dict) -> None:
+    """Refuse an artifact whose unit beside it no longer has the digest its
+    sidecar records: the CUBIN and the sidecar's slot records may then be of
+    another unit (a unit edited or re-rendered without its sidecar)."""
+    unit = Path(directory) / b200.get("unit", "")
+    want = b200.get("unit_digest")
+    if want and unit.is_file():
+        got = hashlib.sha256(unit.read_bytes()).hexdigest()
+        if got != want:
+            raise HawkError(f"{unit.name} is stale against its sidecar: the unit hashes to {got[:16]}..., "
+                            f"the sidecar records {want[:16]}...; rebuild the artifact")
 
 
 def sidecar_path(directory, kernel: str, mode: str):

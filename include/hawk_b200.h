@@ -200,7 +200,9 @@ int hkb_cells_finish(int op, int dtype, int ncols, const void* const* hi, const 
  * Limit: ncols * ceil(rows / 4096) <= HKB_NOALLOC_LEAF_CAP, else HKB_ERR_RANGE
  * (8192 leaves: 33.5M rows for one column).  The first call on a device looks
  * up the array's device address (cudaGetSymbolAddress) and caches it; make
- * that first call before capturing any stream.  All calls share the one array:
+ * that first call before capturing any stream.  The cached address belongs to
+ * the device's primary context: after cudaDeviceReset on a device, reload the
+ * library in a new process before calling this again.  All calls share the one array:
  * calls that can overlap on the GPU (different streams, different host threads)
  * race on it and must be ordered by the caller.  Every partial is written
  * before it is read within a call, so no state carries between calls. */

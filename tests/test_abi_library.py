@@ -53,3 +53,69 @@ def test_cells_scratch_size():
     # two partials (hi, comp) per leaf of 4096 rows, per column
     assert abi.cells_scratch_bytes("float64", 3, 4096 * 5 + 1) == 2 * 3 * 6 * 8
     assert abi.cells_scratch_bytes("float32", 1, 1) == 2 * 4
+
+
+def test_a_library_built_from_other_sources_is_refused():
+    """The reference refuses a stale extension at import (hawk/__init__.py:128-209);
+    the loader compares the digest the library was stamped with against its
+    sources beside the package."""
+    import pytest
+    from hawk_b200.errors import HawkError
+
+    assert abi.build_digest() == abi.sources_digest()
+    abi.check_build_digest("a" * 64, None)               # no sources shipped: nothing to compare
+    abi.check_build_digest("a" * 64, "a" * 64)
+    with pytest.raises(HawkError, match="is stale: it was built from sources whose digest is aaaaaaaa"):
+        abi.check_build_digest("a" * 64, "b" * 64)
+
+
+def test_an_artifact_whose_unit_changed_is_refused_before_loading(tmp_path):
+    """A sidecar records its unit's digest; a unit edited (or re-rendered)
+    without its sidecar and CUBIN is refused by name, before the CUBIN is read."""
+    import shutil
+
+    import pytest
+    from hawk_b200 import runtime
+    from hawk_b200.errors import HawkError
+
+    bundles = REPO / "hawk_b200" / "bundles"
+    for suffix in (".cu", ".json"):
+        shutil.copy(bundles / f"energy.float64{suffix}", tmp_path / f"energy.float64{suffix}")
+    unit = tmp_path / "energy.float64.cu"
+    unit.write_text(unit.read_text().replace("0.5", "0.25", 1))
+    with pytest.raises(HawkError, match="energy.float64.cu is stale against its sidecar"):
+        runtime.DeviceKernel(tmp_path, "energy", "float64", device=0)
+
+
+def test_the_static_scratch_cap_is_the_headers():
+    """The Python binding's cap of the allocation-free finish is the header's
+    HKB_NOALLOC_LEAF_CAP (the refusal test sizes its case from it)."""
+    text = (REPO / "include" / "hawk_b200.h").read_text()
+    (cap,) = re.findall(r"#define\s+HKB_NOALLOC_LEAF_CAP\s+(\d+)", text)
+    assert abi.NOALLOC_LEAF_CAP == int(cap)
+    (rows,) = re.findall(r"#define\s+HKB_LEAF_ROWS\s+(\d+)", text)
+    assert abi.LEAF_ROWS == int(rows)
+
+
+def test_wait_errors_name_what_ran_out_and_a_drain_stops_the_unit():
+    """The bits of a unit's error word (hk/stage.cuh kErrFullWait, kErrEmptyWait,
+    kErrDrain) as the runtime reports them; a drain that ran out is fatal to
+    the unit (later launches are refused)."""
+    import pytest
+    from types import SimpleNamespace
+
+    from hawk_b200 import runtime
+    from hawk_b200.errors import HawkError
+
+    stage = (REPO / "hawk_b200" / "csrc" / "include" / "hk" / "stage.cuh").read_text()
+    for name, bit in (("kErrFullWait", runtime.WAIT_FULL), ("kErrEmptyWait", runtime.WAIT_EMPTY),
+                      ("kErrDrain", runtime.WAIT_DRAIN)):
+        assert re.search(rf"{name} = {bit}u;", stage), name
+    words = iter([runtime.WAIT_FULL, 0, runtime.WAIT_DRAIN])
+    fake = SimpleNamespace(name="staged", poisoned="", library=SimpleNamespace(errors=lambda clear=True: next(words)))
+    with pytest.raises(HawkError, match="did not arrive within the wait limit; the launch's outputs are incomplete"):
+        runtime.DeviceKernel.check_waits(fake)
+    runtime.DeviceKernel.check_waits(fake)
+    with pytest.raises(HawkError, match="still in flight; the unit is not launched again"):
+        runtime.DeviceKernel.check_waits(fake)
+    assert fake.poisoned

@@ -172,3 +172,27 @@ def test_bitmask_through_a_private_copy_and_straight_to_the_plane(slots):
     want = np.zeros(slots, dtype=np.uint32)
     np.bitwise_or.at(want, w["key"], w["bits"])
     np.testing.assert_array_equal(host(acc), want)
+
+
+@pytest.mark.parametrize("slots", [300, 3000, 50000])
+@pytest.mark.parametrize("n", [1000, 65536 + 17, 300000])
+def test_compensated_sink_policy_commits_its_residuals_into_the_declared_plane(n, slots):
+    """A kernel built under the compensated sink policy (a Kind,
+    hawk/ext): the scatter's commit into acc is compensated, each add's
+    rounding residual going to the kernel's own plane acc_c (no runtime-owned
+    companion).  acc + acc_c, per slot, is the exact sum of the prior values
+    and the terms within the compensated bound; acc alone carries the plain
+    bound; through shared-memory copies of the targets when they fit a block
+    (300 slots), partly (3000) or not at all (50000)."""
+    w = workloads.scatter(n, seed=n + slots, slots=slots)
+    rng = np.random.default_rng(slots)
+    prior = rng.uniform(0.0, 1.0, slots)
+    x = w["x"] * np.exp(rng.uniform(-20.0, 20.0, n))       # magnitudes that round away bits
+    acc, acc_c = dev(prior.copy()), torch.zeros(slots, dtype=torch.float64, device="cuda")
+    k = runtime.load(BUNDLES, "comp_scatter")
+    runtime.run(k, x=dev(x), key=dev(w["key"]), acc=acc, acc_c=acc_c)
+    want, mag, cnt = exact(w["key"], x, slots, prior)
+    a, c = host(acc), host(acc_c)
+    within(a + c, want, mag, 2)
+    within(a, want, mag, 2 + cnt.max())
+    assert np.any(c != 0.0)                                  # the residuals were committed

@@ -72,3 +72,16 @@ def test_a_size_beyond_the_static_scratch_is_refused():
     out = torch.zeros(3, dtype=torch.float64, device="cuda")
     with pytest.raises(HawkError, match="static scratch"):
         abi.cells_finish_noalloc("sum", "float64", ptrs, ptrs, rows, out.data_ptr())
+
+
+@pytest.mark.parametrize("dtype", ["float64", "float32"])
+def test_a_call_at_exactly_the_cap_equals_the_scratch_finish(dtype):
+    """ncols * leaves == HKB_NOALLOC_LEAF_CAP: every partial slot of the static
+    array is used (for float64 the companions' half ends at its last byte), on
+    two calls in a row."""
+    ncols = 4
+    rows = (abi.NOALLOC_LEAF_CAP // ncols) * abi.LEAF_ROWS
+    for seed in (5, 6):
+        got, want = _finish_both("sum", dtype, rows, ncols, seed)
+        assert np.isfinite(want).all()
+        np.testing.assert_array_equal(got, want)
