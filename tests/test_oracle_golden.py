@@ -79,12 +79,14 @@ def test_gravity_golden(golden):
     f, u = oracle.gravity(g["r1"], g["r2"], g["m1"], g["m2"], float(g["G"]))
     close(f, g["f"])
     close(u, g["u"])
+    # measured worst relative differences from the interpreter: 3.9e-15 (JVP),
+    # 8.3e-16 (VJP) -- its numpy expression order, not the host unit's
     df, du = oracle.gravity_jvp(g["r1"], g["r2"], g["dr1"], g["dr2"], g["m1"], g["m2"], float(g["G"]))
-    close(df, g["dot_f"], rtol=1e-11)
-    close(du, g["dot_u"], rtol=1e-11)
+    close(df, g["dot_f"])
+    close(du, g["dot_u"])
     b1, b2 = oracle.gravity_vjp(g["r1"], g["r2"], g["bar_f"], g["bar_u"], g["m1"], g["m2"], float(g["G"]))
-    close(b1, g["bar_r1"], rtol=1e-11)
-    close(b2, g["bar_r2"], rtol=1e-11)
+    close(b1, g["bar_r1"])
+    close(b2, g["bar_r2"])
 
 
 def test_spd_solve_golden(golden):
@@ -100,9 +102,10 @@ def test_kepler_golden(golden):
     E, it = oracle.kepler(g["e"], g["M"])
     close(E, g["E"])
     np.testing.assert_array_equal(it, g["iters"])
+    # glibc's sin/cos on both sides: measured bit-identical to the interpreter
     be, bM = oracle.kepler_vjp(g["e"], g["M"], g["bar_E"])
-    close(be, g["bar_e"], rtol=1e-10)
-    close(bM, g["bar_M"], rtol=1e-10)
+    close(be, g["bar_e"])
+    close(bM, g["bar_M"])
 
 
 def test_kepler_known_answer(golden):
