@@ -1,0 +1,101 @@
+// hawk_b200 unit 'poly_loss_vjp' (scalar mode banded), sm_100a.
+// Body text: the reference renderer's; entry, views and frame: the b200 wrapper.
+#include "hk/hawk_b200.cuh"
+
+using Real = double;
+using Int = long long;
+
+HK_SELF_CHECK_EXPORTS
+
+extern "C" __global__ void __launch_bounds__(256) poly_loss_vjp(
+    hk::abi::ScalarHandle p_aout_bar_a,
+    hk::abi::ScalarHandle p_aout_bar_a_comp,
+    hk::abi::ScalarHandle p_aout_bar_b,
+    hk::abi::ScalarHandle p_aout_bar_b_comp,
+    hk::abi::ScalarHandle p_aout_bar_c,
+    hk::abi::ScalarHandle p_aout_bar_c_comp,
+    hk::abi::ScalarHandle p_psc_bar_r,
+    hk::abi::ScalarHandle p_psc_t,
+    hk::abi::ScalarHandle p_psc_x,
+    hk::abi::ScalarHandle p_lut_a,
+    hk::abi::ScalarHandle p_lut_b,
+    hk::abi::ScalarHandle p_lut_c,
+    long long base,
+    long long count,
+    long long nSamples)
+{
+    const hk::ScalarOut<Real> aout_bar_a(p_aout_bar_a);
+    (void)aout_bar_a;
+    const hk::ScalarOut<Real> aout_bar_a_comp(p_aout_bar_a_comp);
+    (void)aout_bar_a_comp;
+    const hk::ScalarOut<Real> aout_bar_b(p_aout_bar_b);
+    (void)aout_bar_b;
+    const hk::ScalarOut<Real> aout_bar_b_comp(p_aout_bar_b_comp);
+    (void)aout_bar_b_comp;
+    const hk::ScalarOut<Real> aout_bar_c(p_aout_bar_c);
+    (void)aout_bar_c;
+    const hk::ScalarOut<Real> aout_bar_c_comp(p_aout_bar_c_comp);
+    (void)aout_bar_c_comp;
+    const hk::ScalarIn<Real> psc_bar_r(p_psc_bar_r);
+    (void)psc_bar_r;
+    const hk::ScalarIn<Real> psc_t(p_psc_t);
+    (void)psc_t;
+    const hk::ScalarIn<Real> psc_x(p_psc_x);
+    (void)psc_x;
+    const hk::ScalarIn<Real> lut_a(p_lut_a);
+    (void)lut_a;
+    const auto lut_a_cell = lut_a.cell();
+    (void)lut_a_cell;
+    const hk::ScalarIn<Real> lut_b(p_lut_b);
+    (void)lut_b;
+    const auto lut_b_cell = lut_b.cell();
+    (void)lut_b_cell;
+    const hk::ScalarIn<Real> lut_c(p_lut_c);
+    (void)lut_c;
+    const auto lut_c_cell = lut_c.cell();
+    (void)lut_c_cell;
+    const long long hawk_rows = (count + 31) >> 5;
+    for (long long hawk_r0 = hk::warp_first() * 8; hawk_r0 < hawk_rows; hawk_r0 += hk::warp_step() * 8) {
+        Real hawk_terms[24];
+#pragma unroll
+        for (int hawk_k = 0; hawk_k < 24; ++hawk_k) hawk_terms[hawk_k] = hk::ss::identity<Real>(hk::ss::kSum);
+#pragma unroll
+        for (int hawk_q = 0; hawk_q < 8; ++hawk_q) {
+        Real* const hawk_ss = hawk_terms + hawk_q * 3;
+        const long long hawk_flat = ((hawk_r0 + hawk_q) << 5) + static_cast<long long>(threadIdx.x & 31u);
+        if (hawk_flat < count) {
+        const long long hawk_i = base + hawk_flat;
+        const hk::SampleIndex i{hawk_i};
+        (void)hawk_i;
+        (void)nSamples;
+        const auto psc_x_i = psc_x[i].eval();
+        const auto t17 = (psc_bar_r[i].eval() * ((((((lut_a_cell * psc_x_i) * psc_x_i) * psc_x_i) + (lut_b_cell * psc_x_i)) + lut_c_cell) - psc_t[i].eval()));
+        const auto t18 = (t17 + t17);
+        const auto t19 = (t18 * psc_x_i);
+        hawk_ss[0] = ((t19 * psc_x_i) * psc_x_i);
+        hawk_ss[1] = t19;
+        hawk_ss[2] = t18;
+        }
+        }
+        auto hawk_ss_store = [&](int hawk_col, auto hawk_s, auto hawk_c) {
+            (void)hawk_c;
+            const int hawk_q = hawk_col / 3;
+            if (hawk_r0 + hawk_q >= hawk_rows) return;
+            const long long hawk_row = (base >> 5) + hawk_r0 + hawk_q;
+            hawk_col -= hawk_q * 3;
+            if (hawk_col == 0) {
+                aout_bar_a.data()[hawk_row] = hawk_s + hawk_c;
+                aout_bar_a_comp.data()[hawk_row] = static_cast<decltype(hawk_c)>(0);
+            }
+            else if (hawk_col == 1) {
+                aout_bar_b.data()[hawk_row] = hawk_s + hawk_c;
+                aout_bar_b_comp.data()[hawk_row] = static_cast<decltype(hawk_c)>(0);
+            }
+            else if (hawk_col == 2) {
+                aout_bar_c.data()[hawk_row] = hawk_s + hawk_c;
+                aout_bar_c_comp.data()[hawk_row] = static_cast<decltype(hawk_c)>(0);
+            }
+        };
+        hk::ss::rows_reduce<8, 3, hk::ss::kSum>(hawk_terms, hawk_ss_store);
+    }
+}

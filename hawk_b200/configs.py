@@ -14,6 +14,9 @@ c3 gravity         f = G m1 m2 / |d|^3 * d, u = -G m1 m2 / |d|, d = r2 - r1
 c4 spd_solve       x = cho_solve(cholesky(A), b) for a 6x6 SPD A
 c5 kepler          Newton on E - e sin E = M from E = M, at most 32 trips,
                    leaving when |dE| < 1e-14; E and the trip count (int32)
+   band_rows       s = hawk.sum(x), q = hawk.sum(x * x), in the banded scalar mode
+   band_max/min    hi = hawk.max(x) / lo = hawk.min(x), banded
+   band_chain      out = exp(x x / 2 + y) / (y + 1.5) - sin(x) / 4, banded and float64
    trig            s = sin(x), c = cos(x): the device library's sin and cos
                    as output planes, for the bitwise check against the host
                    target's libm
@@ -95,6 +98,28 @@ def kepler(e: Scalar, M: Scalar, E: Mutable[Scalar], iters: Mutable[Int32]):
             break
     E = Ek
     iters = n
+
+
+@hawk.kernel
+def band_rows(x: Scalar, s: Mutable[Scalar], q: Mutable[Scalar]):
+    s = hawk.sum(x)
+    q = hawk.sum(x * x)
+
+
+@hawk.kernel
+def band_max(x: Scalar, hi: Mutable[Scalar]):
+    hi = hawk.max(x)
+
+
+@hawk.kernel
+def band_min(x: Scalar, lo: Mutable[Scalar]):
+    lo = hawk.min(x)
+
+
+@hawk.kernel
+def band_chain(x: Scalar, y: Scalar, out: Mutable[Scalar]):
+    t = x * x * 0.5 + y
+    out = m.exp(t) / (y + 1.5) - m.sin(x) * 0.25
 
 
 @hawk.kernel
@@ -503,7 +528,7 @@ KERNELS = {
     "energy_jvp": (Kernel("energy_jvp", jvp(energy, wrt=("v",))), ("float64",)),
     "poly_loss": (poly_loss, ("float64", "float32")),
     "poly_loss_vjp": (Kernel("poly_loss_vjp", vjp(param_planes(poly_loss), wrt=("a", "b", "c"))),
-                      ("float64", "float32")),
+                      ("float64", "float32", "banded")),
     "gravity": (gravity, ("float64",)),
     "gravity_jvp": (Kernel("gravity_jvp", jvp(gravity, wrt=("r1", "r2"))), ("float64",)),
     "gravity_vjp": (Kernel("gravity_vjp", vjp(gravity, wrt=("r1", "r2"))), ("float64",)),
@@ -512,6 +537,10 @@ KERNELS = {
     "kepler": (kepler, ("float64",)),
     "kepler_vjp": (Kernel("kepler_vjp", vjp(kepler, wrt=("e", "M"))), ("float64",)),
     "trig": (trig, ("float64",)),
+    "band_rows": (band_rows, ("banded", "float64")),
+    "band_max": (band_max, ("banded",)),
+    "band_min": (band_min, ("banded",)),
+    "band_chain": (band_chain, ("banded", "float64")),
     "oscillator": (oscillator, ("float64",)),
     "orbit": (orbit, ("float64",)),
     "gather": (gather, ("float64",)),

@@ -46,7 +46,9 @@ SINK_ROLES = ("mutable", "out", "accum_out", "terminated")
 FUSED_STEPS = "fused_steps"
 ROW = 32
 
-_WIRE_OF_MODE = {"float64": "float64", "float32": "float32"}
+#: The element type of each scalar mode's planes and cells (a banded value is
+#: an IEEE binary64 in its 8-byte cell on the b200 target).
+_WIRE_OF_MODE = {"float64": "float64", "float32": "float32", "banded": "float64"}
 _INT_DTYPES = ("i32", "i64", "int32", "uint32")
 
 
@@ -105,6 +107,7 @@ class DeviceKernel:
         self.sidecar = sidecar
         self.name = sidecar["kernel"]
         self.mode = sidecar.get("scalar_type", mode)
+        self.element = _WIRE_OF_MODE.get(self.mode, self.mode)
         b200 = sidecar["b200"]
         check_unit_digest(self.directory, b200)
         self.frame = b200["frame"]
@@ -138,7 +141,8 @@ class DeviceKernel:
     def _wire(self, name: str, dtype: str) -> str:
         wire = self.sidecar.get("arg_dtypes", {}).get(name)
         if wire:
-            return wire                     # an index word rides 64 bits (hawk/runtime.py:221-225)
+            # an index word rides 64 bits (hawk/runtime.py:221-225); a banded cell is a binary64 word
+            return _WIRE_OF_MODE.get(wire, wire) if wire == "banded" else wire
         if dtype in _INT_DTYPES:
             return {"i32": "int32", "i64": "int64"}.get(dtype, dtype)
         return _WIRE_OF_MODE[self.mode]
@@ -344,7 +348,7 @@ class DeviceKernel:
         if n not in self._scratch:
             rows = -(-n // ROW)
             leaves = -(-rows // abi.LEAF_ROWS)
-            dt = torch.float64 if self.mode == "float64" else torch.float32
+            dt = torch.float64 if self.element == "float64" else torch.float32
             dev = torch.device("cuda", self.device)
             planes = {}
             for s in self.sums:
@@ -361,7 +365,7 @@ class DeviceKernel:
     def cells_leaves(self, state: dict, lo: int, hi: int, stream=None) -> int:
         """Rows ``[lo, hi)`` of every column folded into one partial per leaf
         (one launch for all columns); returns the leaf count."""
-        itemsize = 8 if self.mode == "float64" else 4
+        itemsize = 8 if self.element == "float64" else 4
         op = self.sums[0]["op"] if self.sums else "sum"
         rows = state["rows"]
         his = [rows[s["name"]].data_ptr() + lo * itemsize for s in self.sums]
@@ -370,14 +374,14 @@ class DeviceKernel:
         leaves = -(-count // abi.LEAF_ROWS)
         leaf_hi, leaf_comp = state["leaf_hi"], state["leaf_comp"]
         # the partials of column k start at k * leaves (a (cols, leaves) view)
-        abi.cells_leaves(op, self.mode, his, comps, count, leaf_hi.data_ptr(), leaf_comp.data_ptr(),
+        abi.cells_leaves(op, self.element, his, comps, count, leaf_hi.data_ptr(), leaf_comp.data_ptr(),
                          _stream(stream, self.device))
         return leaves
 
     def cells_tree(self, leaf_hi, leaf_comp, leaves: int, values, stream=None) -> None:
         """The pairwise levels over ``leaves`` partials per column, into ``values``."""
         op = self.sums[0]["op"] if self.sums else "sum"
-        abi.cells_tree(op, self.mode, len(self.sums), leaf_hi.data_ptr(), leaf_comp.data_ptr(), leaves,
+        abi.cells_tree(op, self.element, len(self.sums), leaf_hi.data_ptr(), leaf_comp.data_ptr(), leaves,
                        values.data_ptr(), _stream(stream, self.device))
 
     def write_cells(self, values, outputs: dict, stream=None) -> None:
@@ -469,6 +473,7 @@ class SplitKernel:
         self.sidecar = sidecar
         self.name = sidecar["kernel"]
         self.mode = sidecar.get("scalar_type", mode)
+        self.element = _WIRE_OF_MODE.get(self.mode, self.mode)
         b200 = sidecar["b200"]
         check_unit_digest(self.directory, b200)
         self.device = int(device if device is not None else _current_device())
@@ -543,7 +548,7 @@ class SplitKernel:
         key = (n, tuple(sorted(sizes.items())))
         if key not in self._scratch:
             dev = torch.device("cuda", self.device)
-            real = torch.float64 if self.mode == "float64" else torch.float32
+            real = torch.float64 if self.element == "float64" else torch.float32
             self._scratch[key] = {
                 name: torch.full((int(spec.get("per_lane", 1)) * self.team_units(spec, n, sizes),),
                                  spec.get("fill", 0),
@@ -579,7 +584,7 @@ class SplitKernel:
 
         key = ("keyed", n)
         if key not in self._scratch:
-            real = torch.float64 if self.mode == "float64" else torch.float32
+            real = torch.float64 if self.element == "float64" else torch.float32
             dev = torch.device("cuda", self.device)
             planes = {}
             for name, spec in self.keyed.items():
@@ -635,7 +640,7 @@ class SplitKernel:
         import torch
 
         if not self._values:
-            real = torch.float64 if self.mode == "float64" else torch.float32
+            real = torch.float64 if self.element == "float64" else torch.float32
             self._values = {c: torch.empty(int(spec.get("columns", 1)), dtype=real,
                                            device=torch.device("cuda", self.device))
                             for c, spec in self.cell_specs.items()}
@@ -667,8 +672,8 @@ class SplitKernel:
             raise HawkError(f"kernel {self.name!r}: " + "; ".join(errors))
         for c, spec in self.cells.items():
             p = planes[c]
-            if p.dtype != self.mode or p.device != self.device or p.size < int(spec.get("columns", 1)):
-                raise HawkError(f"kernel {self.name!r}: cell {c!r} must be a {self.mode} plane of "
+            if p.dtype != self.element or p.device != self.device or p.size < int(spec.get("columns", 1)):
+                raise HawkError(f"kernel {self.name!r}: cell {c!r} must be a {self.element} plane of "
                                 f"{spec.get('columns', 1)} value(s) on device {self.device}, got {p.dtype} "
                                 f"{p.shape} on {p.device}")
         count = n_samples - base if count is None else count
@@ -839,8 +844,8 @@ def launch_cells(kernel: DeviceKernel, *, base: int = 0, count: int | None = Non
     if cells:
         for c in cells:
             p = planes[c]
-            if p.dtype != kernel.mode or p.device != kernel.device:
-                raise HawkError(f"kernel {kernel.name!r}: cell {c!r} must be a {kernel.mode} plane on device "
+            if p.dtype != kernel.element or p.device != kernel.device:
+                raise HawkError(f"kernel {kernel.name!r}: cell {c!r} must be a {kernel.element} plane on device "
                                 f"{kernel.device}, got {p.dtype} on {p.device}")
             outputs[c] = p
         state = kernel.cells_state(n_samples)

@@ -160,7 +160,7 @@ def run_cells(kernel, *, group=None, base: int = 0, count: int | None = None, n_
                     counts = [int(c) for c in every.cpu().tolist()]
                 if aligned(counts):
                     op = kernel.sums[0]["op"] if kernel.sums else "sum"
-                    finish_subtrees(op, kernel.mode, cols, state["leaf_hi"], state["leaf_comp"], leaves,
+                    finish_subtrees(op, kernel.element, cols, state["leaf_hi"], state["leaf_comp"], leaves,
                                     state["values"], group, runtime._stream(stream, kernel.device))
                     kernel.write_cells(state["values"], outputs, stream)
                     return

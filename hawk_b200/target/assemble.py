@@ -25,9 +25,14 @@ from .refill import refill_frame
 from .wrapper import B200, StagePlan, lane_frame_staged, sample_sum_store
 from .writer import B200_WRITER, body_text
 
-#: Scalar modes the b200 target builds: the reference's float64 and float32
-#: (hawk/emit/wrapper.py:136-143).  The banded mode is a host/cells form.
-MODES = {"float64": "double", "float32": "float"}
+#: Scalar modes the b200 target builds, each with its C++ element type: the
+#: reference's float64, float32 and banded (hawk/emit/wrapper.py:136-143).  A
+#: banded value on the b200 target is an IEEE binary64 in its 8-byte cell (this
+#: build's own cell format; the reference's packed BandedReal is defined only by
+#: the absent aether-dsc): every operation is correctly rounded, within the
+#: 0.5 ULP53 a banded op is certified to, and a sum over samples keeps the
+#: banded row contract (each row's compensated pair rounded once).
+MODES = {"float64": "double", "float32": "float", "banded": "double"}
 
 #: Library namespaces the device library does not provide: a body naming one is
 #: refused with the construct it stands for.
@@ -66,6 +71,27 @@ def refuse_features(name: str, kernel, walk, sinks) -> None:
         if hit is not None:
             raise HawkError(f"{name!r}: the b200 target does not build the feature {feature!r} "
                             f"(at {hit[1]} {hit[0]}): {why}; {fix}")
+
+
+def refuse_banded(name: str, kernel, walk, sinks) -> None:
+    """What the banded mode does not build: the ops the reference refuses in
+    it (hawk/emit/wrapper.py:179-213: an atomic scattered add, the
+    uncertified math functions), any scattered commit (the reference routes a
+    banded build's compensated scatter to ordered stages, which this mode does
+    not build), and kernels its split cuts into stages."""
+    from hawk.emit.wrapper import BANDED, refuse_uncertified
+
+    if walk.companions or any(str(k).startswith("accum") for k in walk.kinds):
+        raise HawkError(f"{name!r}: a scattered commit is not built in scalar mode 'banded' on the b200 target "
+                        "(a cell has no atomic add, and the ordered stages the reference routes a banded "
+                        "scatter to are not built banded here); build this kernel in float64 or float32")
+    try:
+        refuse_uncertified(sinks, walk, BANDED)
+    except Exception as exc:                     # the reference's HawkError, re-raised as this path's
+        raise HawkError(f"{name!r}: {exc}") from None
+    if getattr(kernel, "team", None) is not None:
+        raise HawkError(f"{name!r}: a kernel split into stages is not built in scalar mode 'banded' on the b200 "
+                        "target; build it in float64 or float32")
 
 
 #: The team-form calls the device library builds (hk/team.cuh).
@@ -158,6 +184,8 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
     walk, sinks = kernel.walk, kernel.sinks
     _refuse(name, walk)
     refuse_features(name, kernel, walk, sinks)
+    if mode == "banded":
+        refuse_banded(name, kernel, walk, sinks)
     kind = getattr(kernel, "kind", None)
     rendered = render_body(sinks, walk, indent="        ", kind=kind, writer=B200_WRITER)
     body = body_text(rendered.text)
@@ -176,12 +204,12 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
         elem = element_spelling(sums[0].ttype.dtype)
         plan = StagePlan(walk, elem_bytes, 256 * wrapper.fold_rows(len(sums))) if staged else None
         if plan is not None and plan.enabled:
-            opened, closed = wrapper.sample_sum_frame_staged(plan, len(sums), elem, sample_sum_store(sums),
+            opened, closed = wrapper.sample_sum_frame_staged(plan, len(sums), elem, sample_sum_store(sums, banded=mode == "banded"),
                                                              sums[0].op)
             smem = plan.smem_bytes
         else:
             plan = None
-            opened, closed = wrapper.sample_sum_frame(len(sums), elem, sample_sum_store(sums), sums[0].op)
+            opened, closed = wrapper.sample_sum_frame(len(sums), elem, sample_sum_store(sums, banded=mode == "banded"), sums[0].op)
         loop = [opened, body, closed]
         frame = "row"
     else:

@@ -398,11 +398,14 @@ def lane_frame_staged(plan: StagePlan) -> tuple:
     return opened, closed
 
 
-def sample_sum_store(sums) -> str:
+def sample_sum_store(sums, banded: bool = False) -> str:
     """``hawk_ss_store``: butterfly column ``q * W + k`` is sink ``k``'s term of
     the trip's row ``q``; it goes to that sink's row plane (and its companion
     for a sum) at ``hawk_row``.  A row past the last is not stored.  ``__K__``
-    and ``__W__`` are filled by the frame."""
+    and ``__W__`` are filled by the frame.  In the banded mode a sum's row is
+    its compensated pair rounded once (``hawk_s + hawk_c``) and its companion
+    row zero -- the reference's banded row is its accumulator's value and a
+    zero companion (``ssOut_`` / ``ssComp_``, hawk/emit/wrapper.py:699-705)."""
     sp = _spelling()
     lines = ["        auto hawk_ss_store = [&](int hawk_col, auto hawk_s, auto hawk_c) {",
              "            (void)hawk_c;",
@@ -413,10 +416,15 @@ def sample_sum_store(sums) -> str:
     for k, sink in enumerate(sums):
         hi = sp.binding_name(sink.role, sink.name)
         lines.append(f"            {'else ' if k else ''}if (hawk_col == {k}) {{")
-        lines.append(f"                {hi}.data()[hawk_row] = hawk_s;")
-        if sink.op == "sum":
+        if banded and sink.op == "sum":
             comp = sp.binding_name(sink.role, sink.companion.name)
-            lines.append(f"                {comp}.data()[hawk_row] = hawk_c;")
+            lines.append(f"                {hi}.data()[hawk_row] = hawk_s + hawk_c;")
+            lines.append(f"                {comp}.data()[hawk_row] = static_cast<decltype(hawk_c)>(0);")
+        else:
+            lines.append(f"                {hi}.data()[hawk_row] = hawk_s;")
+            if sink.op == "sum":
+                comp = sp.binding_name(sink.role, sink.companion.name)
+                lines.append(f"                {comp}.data()[hawk_row] = hawk_c;")
         lines.append("            }")
     return "\n".join(lines + ["        };"])
 

@@ -276,6 +276,26 @@ def spd_solve_vjp(A, b, bar_x, threads: int = 1):
 OPS = {"sum": 0, "max": 1, "min": 2}
 
 
+def rows(terms, op: str = "sum"):
+    """``(hi, comp)``: the 32-sample rows of one column of terms, as the host
+    frame makes them (float64)."""
+    terms = np.ascontiguousarray(terms, dtype=np.float64)
+    n = terms.shape[0]
+    nrows = -(-n // 32)
+    hi, comp = np.empty(max(nrows, 1)), np.empty(max(nrows, 1))
+    lib().hko_rows_f64(OPS[op], _p(terms), n, _p(hi), _p(comp))
+    return hi[:nrows], comp[:nrows]
+
+
+def banded_rows(terms, op: str = "sum"):
+    """The banded mode's rows of one column: each row's compensated pair
+    rounded once (hi + comp) and a zero companion; max/min rows as they are."""
+    hi, comp = rows(terms, op)
+    if op != "sum":
+        return hi, np.zeros_like(hi)
+    return hi + comp, np.zeros_like(hi)
+
+
 def sample_sum(terms, op: str = "sum") -> float:
     """A reduction over samples as a kernel makes it: the 32-sample rows of
     the terms, then the ordered finish of the rows into the cell."""

@@ -239,3 +239,29 @@ def test_every_committed_unit_re_renders_byte_for_byte(name, mode, staged):
         got = (Path(d) / f"{name}.{mode}.cu").read_text()
     committed = (BUNDLES / ("staged" if staged else "") / f"{name}.{mode}.cu").read_text()
     assert got == committed
+
+
+@hawk.kernel
+def banded_scatter(x: Scalar, lane: Index, acc: Mutable[Scalar]):
+    hawk.scatter(acc)[lane] += x
+
+
+@hawk.kernel
+def banded_erf(x: Scalar, y: Mutable[Scalar]):
+    y = hm.erf(x)
+
+
+@pytest.mark.parametrize("kernel,what", [(banded_scatter, "scattered commit"), (banded_erf, "hawk.math.erf")],
+                         ids=["scatter", "erf"])
+def test_the_banded_mode_refuses_what_it_does_not_build(kernel, what):
+    with pytest.raises(HawkError, match=what):
+        choose_unit(kernel, kernel.name, "banded")
+    choose_unit(kernel, kernel.name, "float64")
+
+
+def test_a_banded_row_is_its_compensated_pair_rounded_once():
+    unit, _cubin, _log, _ptxas = choose_unit(configs.band_rows, "band_rows", "banded")
+    assert "aout_s.data()[hawk_row] = hawk_s + hawk_c;" in unit.text
+    assert "aout_s_comp.data()[hawk_row] = static_cast<decltype(hawk_c)>(0);" in unit.text
+    f64, _cubin, _log, _ptxas = choose_unit(configs.band_rows, "band_rows", "float64")
+    assert "aout_s.data()[hawk_row] = hawk_s;" in f64.text
