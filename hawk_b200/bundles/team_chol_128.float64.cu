@@ -1,5 +1,6 @@
 // hawk_b200 unit 'team_chol_128' (scalar mode float64), sm_100a.
 // Body text: the reference renderer's; entry, views and frame: the b200 wrapper.
+#define HK_TEAM_LOWER_STAGED 0
 #include "hk/hawk_b200.cuh"
 
 using Real = double;

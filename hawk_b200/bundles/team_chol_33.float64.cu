@@ -1,5 +1,6 @@
 // hawk_b200 unit 'team_chol_33' (scalar mode float64), sm_100a.
 // Body text: the reference renderer's; entry, views and frame: the b200 wrapper.
+#define HK_TEAM_LOWER_STAGED 1
 #include "hk/hawk_b200.cuh"
 
 using Real = double;
@@ -52,7 +53,7 @@ extern "C" __global__ void __launch_bounds__(256) team_chol_33(
 }
 
 extern "C" __device__ const unsigned int hk_team_threads__team_chol_33_2 = 32u;
-extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_chol_33_2 = 9904u;
+extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_chol_33_2 = 5424u;
 extern "C" __global__ void __launch_bounds__(32) team_chol_33_2(
     hk::abi::ScalarHandle p_wout_tm0_a,
     hk::abi::ScalarHandle p_wout_tm0_info,

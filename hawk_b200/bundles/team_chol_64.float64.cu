@@ -1,5 +1,6 @@
 // hawk_b200 unit 'team_chol_64' (scalar mode float64), sm_100a.
 // Body text: the reference renderer's; entry, views and frame: the b200 wrapper.
+#define HK_TEAM_LOWER_STAGED 1
 #include "hk/hawk_b200.cuh"
 
 using Real = double;
@@ -52,7 +53,7 @@ extern "C" __global__ void __launch_bounds__(256) team_chol_64(
 }
 
 extern "C" __device__ const unsigned int hk_team_threads__team_chol_64_2 = 32u;
-extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_chol_64_2 = 34944u;
+extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_chol_64_2 = 18304u;
 extern "C" __global__ void __launch_bounds__(32) team_chol_64_2(
     hk::abi::ScalarHandle p_wout_tm0_a,
     hk::abi::ScalarHandle p_wout_tm0_info,

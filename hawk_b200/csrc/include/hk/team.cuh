@@ -51,6 +51,14 @@ namespace team {
 
 #if defined(__CUDACC__) || defined(__CUDACC_RTC__)
 
+}  // namespace team
+}  // namespace linalg
+}  // namespace hk
+extern "C" __device__ unsigned int hk_error_flags;     // the unit's error word (HK_SELF_CHECK_EXPORTS defines it)
+namespace hk {
+namespace linalg {
+namespace team {
+
 // The head of a team entry's dynamic shared memory: the staged-factor tag
 // (below) in its last 16 bytes; the staged matrix and right-hand sides follow.
 constexpr unsigned kScratchBytes = 128u;
@@ -76,6 +84,12 @@ HK_HD constexpr unsigned round16(unsigned long long b) { return static_cast<unsi
 template <class T> HK_HD constexpr unsigned inplace_bytes(int n) { return kScratchBytes + round16(sizeof(T) * n); }
 template <class T> HK_HD constexpr unsigned staged_bytes(int n, int k) {
     return inplace_bytes<T>(n) + round16(sizeof(T) * n * (n + 1)) + round16(sizeof(T) * n * k);
+}
+// The Cholesky family reads and writes only the lower triangle: staged, it is
+// packed by rows (n (n + 1) / 2 entries), half the full copy, so twice as many
+// teams fit an SM.
+template <class T> HK_HD constexpr unsigned staged_lower_bytes(int n, int k) {
+    return inplace_bytes<T>(n) + round16(sizeof(T) * n * (n + 1) / 2) + round16(sizeof(T) * n * k);
 }
 
 // The team of a lane: one warp.  A team entry's block holds several warps,
@@ -130,21 +144,96 @@ template <class T> struct Mat {
     HK_FI T& operator()(int i, int j) const { return p[static_cast<long long>(i) * ld + j]; }
 };
 
+// A lower triangle packed by rows in shared memory has entry (i, j), j <= i,
+// at i (i + 1) / 2 + j.  The rows' offsets are the triangular numbers, which
+// are distinct modulo 32 over any 32 consecutive rows, so a column walk across
+// the lanes is free of bank conflicts.  EitherMat is a row-major matrix
+// (ld > 0) or, with ld == 0, such a triangle: one accessor for a call that may
+// run staged or in place keeps one code path (and one register budget).
+template <class T> struct EitherMat {
+    T* p;
+    int ld;
+    HK_FI T& operator()(int i, int j) const {
+        const long long row = ld ? static_cast<long long>(i) * ld : static_cast<long long>((i * (i + 1)) >> 1);
+        return p[row + j];
+    }
+};
+
+// The packed lower triangle's select-free accessor, for a unit whose team
+// stage always stages it (HK_TEAM_LOWER_STAGED == 1).
+template <class T> struct Tri {
+    T* p;
+    int ld;                     // unused: the layout is the triangle's
+    HK_FI T& operator()(int i, int j) const { return p[((i * (i + 1)) >> 1) + j]; }
+};
+
 // The working copy of a call: the matrix (staged or the scratch plane itself)
-// and the right-hand sides (staged or in place).
-template <class T, int N> struct Work {
-    Mat<T> m;
+// and the right-hand sides (staged or in place); `lower` when the staged copy
+// is a packed lower triangle.
+template <class T, int N, class M = Mat<T>> struct Work {
+    M m;
     T* x;
     bool staged;
+    bool lower;
 };
+
+// How a unit's Cholesky-family calls (which read and write only the lower
+// triangle) hold their matrix, set by the build before the library is
+// included: 1, the team stage's shared memory holds every call's packed
+// triangle (the accessor is Tri); 0, no call stages (the plane, in place);
+// undefined, decided per call by the team's shared memory (EitherMat).
+#if defined(HK_TEAM_LOWER_STAGED) && HK_TEAM_LOWER_STAGED == 1
+template <class T> using LowerMat = Tri<T>;
+#elif defined(HK_TEAM_LOWER_STAGED) && HK_TEAM_LOWER_STAGED == 0
+template <class T> using LowerMat = Mat<T>;
+#else
+template <class T> using LowerMat = EitherMat<T>;
+#endif
+
+// Error bit of the unit's hk_error_flags word (hk/stage.cuh holds the others):
+// a team's shared memory did not hold the packed triangle its unit was built
+// to stage; the call did nothing.
+constexpr unsigned kErrTeamSmem = 8u;
+
+// The working copy of a Cholesky-family call: the packed triangle and the
+// right-hand sides staged, or the plane itself and the right-hand sides in
+// place, as the unit was built (above).  `ok` is false when a unit built to
+// stage finds too little shared memory (never, by the build's sizing).
+template <class T, int N> HK_FI Work<T, N, LowerMat<T>> work_lower(const Team& tm, T* a, T* x, int k, bool* ok) {
+    *ok = true;
+    const bool fits = tm.bytes >= staged_lower_bytes<T>(N, k);
+    unsigned char* base = tm.smem + inplace_bytes<T>(N);
+    T* tri = reinterpret_cast<T*>(base);
+    T* xs = reinterpret_cast<T*>(base + round16(sizeof(T) * N * (N + 1) / 2));
+#if defined(HK_TEAM_LOWER_STAGED) && HK_TEAM_LOWER_STAGED == 1
+    if (!fits) {
+        *ok = false;
+        if (tm.rank == 0) atomicOr(&hk_error_flags, kErrTeamSmem);
+    }
+    return Work<T, N, LowerMat<T>>{LowerMat<T>{tri, 0}, xs, true, true};
+#elif defined(HK_TEAM_LOWER_STAGED) && HK_TEAM_LOWER_STAGED == 0
+    (void)fits, (void)tri, (void)xs;
+    return Work<T, N, LowerMat<T>>{LowerMat<T>{a, N}, x, false, false};
+#else
+    if (!fits) return Work<T, N, LowerMat<T>>{LowerMat<T>{a, N}, x, false, false};
+    return Work<T, N, LowerMat<T>>{LowerMat<T>{tri, 0}, xs, true, true};
+#endif
+}
+
+// The staged-factor tag of plane address a for a working copy: a packed copy
+// is tagged one byte past it, so a full copy never takes a packed one for its
+// own.
+template <class T, int N, class M> HK_FI const void* tag_of(const Work<T, N, M>& w, const T* a) {
+    return static_cast<const void*>(reinterpret_cast<const unsigned char*>(a) + (w.lower ? 1 : 0));
+}
 
 template <class T, int N> HK_FI Work<T, N> work(const Team& tm, T* a, T* x, int k) {
     const bool staged = tm.bytes >= staged_bytes<T>(N, k);
-    if (!staged) return Work<T, N>{Mat<T>{a, N}, x, false};
+    if (!staged) return Work<T, N>{Mat<T>{a, N}, x, false, false};
     unsigned char* base = tm.smem + inplace_bytes<T>(N);
     T* m = reinterpret_cast<T*>(base);
     T* xs = reinterpret_cast<T*>(base + round16(sizeof(T) * N * (N + 1)));
-    return Work<T, N>{Mat<T>{m, N + 1}, xs, true};
+    return Work<T, N>{Mat<T>{m, N + 1}, xs, true, false};
 }
 
 // An elementwise pass over e in [0, count) by the team, U entries of a thread
@@ -165,27 +254,30 @@ template <int U, class V, class S> HK_FI void batched(const Team& tm, int count,
 
 // matrix: plane (stride N) -> working copy, then a barrier; a copy the
 // staged area already holds (the factor the previous call made) is kept
-template <class T, int N> HK_FI void load_matrix(const Team& tm, const Work<T, N>& w, const T* a) {
-    if (w.staged && *tag_slot(tm) != static_cast<const void*>(a)) {
+template <class T, int N, class M> HK_FI void load_matrix(const Team& tm, const Work<T, N, M>& w, const T* a) {
+    if (w.staged && *tag_slot(tm) != tag_of(w, a)) {
         tm.sync();              // every thread has read the tag before it changes
-        batched<8>(tm, N * N, [&](int e) { return a[e]; }, [&](int e, T v) { w.m(e / N, e % N) = v; });
-        if (tm.rank == 0) *tag_slot(tm) = a;
+        batched<8>(tm, N * N, [&](int e) { return (!w.lower || e % N <= e / N) ? a[e] : T(0); },
+                   [&](int e, T v) {
+                       if (!w.lower || e % N <= e / N) w.m(e / N, e % N) = v;
+                   });
+        if (tm.rank == 0) *tag_slot(tm) = tag_of(w, a);
     }
     tm.sync();
 }
 
 // the staged area now holds the final matrix of plane address a (or nothing)
 template <class T> HK_FI void set_tag(const Team& tm, const T* a) {
-    if (tm.rank == 0) *tag_slot(tm) = a;
+    if (tm.rank == 0) *tag_slot(tm) = static_cast<const void*>(a);
 }
 
-template <class T, int N> HK_FI void load_rhs(const Team& tm, const Work<T, N>& w, const T* x, int k) {
+template <class T, int N, class M> HK_FI void load_rhs(const Team& tm, const Work<T, N, M>& w, const T* x, int k) {
     if (w.staged)
         for (int e = tm.rank; e < N * k; e += tm.size) w.x[e] = x[e];
     tm.sync();
 }
 
-template <class T, int N> HK_FI void store_rhs(const Team& tm, const Work<T, N>& w, T* x, int k) {
+template <class T, int N, class M> HK_FI void store_rhs(const Team& tm, const Work<T, N, M>& w, T* x, int k) {
     if (w.staged)
         for (int e = tm.rank; e < N * k; e += tm.size) x[e] = w.x[e];
     tm.sync();
@@ -282,7 +374,9 @@ template <class T, int N> HK_FI void swaps(const Team& tm, T* x, int k, const st
 // zeros (what the one-thread form's factor reads as).
 template <int N, class T>
 HK_FI void cholesky(const Team& tm, const TeamCholesky<T, N>& f, T* a) {
-    const detail::Work<T, N> w = detail::work<T, N>(tm, a, nullptr, 0);
+    bool ok = true;
+    const auto w = detail::work_lower<T, N>(tm, a, nullptr, 0, &ok);
+    if (!ok) return;
     if (w.staged) {
         tm.sync();              // every thread has read the tag before it changes
         detail::set_tag(tm, static_cast<const T*>(nullptr));
@@ -370,7 +464,7 @@ HK_FI void cholesky(const Team& tm, const TeamCholesky<T, N>& f, T* a) {
                        },
                        [&](int e, T v) { a[e] = v; });
     if (tm.rank == 0) *f.info = info;
-    if (w.staged && info == 0) detail::set_tag(tm, static_cast<const T*>(a));
+    if (w.staged && info == 0) detail::set_tag(tm, detail::tag_of(w, a));
     tm.sync();
 }
 
@@ -409,10 +503,12 @@ HK_FI void choSolve(const Team& tm, const TeamCholesky<T, N>& f, const T* b, T* 
         for (int e = tm.rank; e < N * k; e += tm.size) x[e] = b[e];
         tm.sync();
     }
-    const detail::Work<T, N> w = detail::work<T, N>(tm, f.a, x, k);
+    bool ok = true;
+    const auto w = detail::work_lower<T, N>(tm, f.a, x, k, &ok);
+    if (!ok) return;
     detail::load_matrix<T, N>(tm, w, f.a);
     detail::load_rhs<T, N>(tm, w, x, k);
-    const detail::Mat<T> l = w.m;
+    const auto l = w.m;
     detail::forward<T, N, true>(tm, w.x, k, [&](int i, int j) { return l(i, j); }, [&](int i) { return l(i, i); });
     detail::backward<T, N, true>(tm, w.x, k, [&](int i, int j) { return l(j, i); }, [&](int i) { return l(i, i); });
     detail::store_rhs<T, N>(tm, w, x, k);
@@ -425,10 +521,12 @@ HK_FI void triLower(const Team& tm, const TeamCholesky<T, N>& f, const T* b, T* 
         for (int e = tm.rank; e < N * k; e += tm.size) x[e] = b[e];
         tm.sync();
     }
-    const detail::Work<T, N> w = detail::work<T, N>(tm, f.a, x, k);
+    bool ok = true;
+    const auto w = detail::work_lower<T, N>(tm, f.a, x, k, &ok);
+    if (!ok) return;
     detail::load_matrix<T, N>(tm, w, f.a);
     detail::load_rhs<T, N>(tm, w, x, k);
-    const detail::Mat<T> l = w.m;
+    const auto l = w.m;
     detail::forward<T, N, true>(tm, w.x, k, [&](int i, int j) { return l(i, j); }, [&](int i) { return l(i, i); });
     detail::store_rhs<T, N>(tm, w, x, k);
 }
@@ -439,10 +537,12 @@ HK_FI void triUpperT(const Team& tm, const TeamCholesky<T, N>& f, const T* b, T*
         for (int e = tm.rank; e < N * k; e += tm.size) x[e] = b[e];
         tm.sync();
     }
-    const detail::Work<T, N> w = detail::work<T, N>(tm, f.a, x, k);
+    bool ok = true;
+    const auto w = detail::work_lower<T, N>(tm, f.a, x, k, &ok);
+    if (!ok) return;
     detail::load_matrix<T, N>(tm, w, f.a);
     detail::load_rhs<T, N>(tm, w, x, k);
-    const detail::Mat<T> l = w.m;
+    const auto l = w.m;
     detail::backward<T, N, true>(tm, w.x, k, [&](int i, int j) { return l(j, i); }, [&](int i) { return l(i, i); });
     detail::store_rhs<T, N>(tm, w, x, k);
 }

@@ -132,12 +132,14 @@ class Unit:
     entries: str = ""               # the text after the prelude: the entry (and its fold / persist entries)
 
 
-def prelude_lines(name: str, mode: str) -> list:
-    """The head of a unit: the device library, the scalar-mode aliases and the
-    self-check exports (hawk/artifact/layout.py:35-61)."""
+def prelude_lines(name: str, mode: str, defines=()) -> list:
+    """The head of a unit: the build's settings for the device library
+    (``defines``), the library, the scalar-mode aliases and the self-check
+    exports (hawk/artifact/layout.py:35-61)."""
     return [
         f"// hawk_b200 unit {name!r} (scalar mode {mode}), sm_100a.",
         "// Body text: the reference renderer's; entry, views and frame: the b200 wrapper.",
+        *(f"#define {d}" for d in defines),
         '#include "hk/hawk_b200.cuh"',
         "",
         f"using Real = {MODES[mode]};",

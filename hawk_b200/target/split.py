@@ -56,6 +56,17 @@ def _staged_bytes(n: int, k: int, elem: int) -> int:
     return _inplace_bytes(n, elem) + _round16(elem * n * (n + 1)) + _round16(elem * n * k)
 
 
+#: Team calls that read and write only a factor's lower triangle; staged, it
+#: is packed (hk::linalg::team::staged_lower_bytes).
+LOWER_OPS = frozenset({"chol", "chol_from", "cho_solve", "tri_lower", "tri_upper_t"})
+
+
+def _staged_lower_bytes(n: int, k: int, elem: int) -> int:
+    """hk::linalg::team::staged_lower_bytes: the in-place part, the packed
+    lower triangle, the right-hand sides."""
+    return _inplace_bytes(n, elem) + _round16(elem * n * (n + 1) // 2) + _round16(elem * n * k)
+
+
 def team_geometry(spec, elem: int) -> tuple:
     """``(threads, smem)`` of a team stage's block.  A team is one warp
     (hk/team.cuh).  When the largest staged need of the stage's calls leaves
@@ -66,11 +77,20 @@ def team_geometry(spec, elem: int) -> tuple:
     for step in spec.steps:
         n = int(step.n)
         k = n if step.op == "lu_inverse" else int(step.k or 0)
-        needs.append(_staged_bytes(n, k, elem))
+        needs.append(_staged_lower_bytes(n, k, elem) if step.op in LOWER_OPS else _staged_bytes(n, k, elem))
         inplace.append(_inplace_bytes(n, elem))
     if needs and max(needs) * TEAM_STAGED_WARPS <= TEAM_SMEM_LIMIT:
         return 32, max(needs)
     return 32 * TEAM_WARPS_IN_PLACE, max(inplace) * TEAM_WARPS_IN_PLACE
+
+
+def lower_staged(spec, smem: int, threads: int) -> bool | None:
+    """Whether the Cholesky-family calls of a team stage stage their packed
+    triangle (True), work in place (False), or the stage makes none (None)."""
+    lower = [st for st in spec.steps if st.op in LOWER_OPS]
+    if not lower:
+        return None
+    return threads == 32 and smem > 0
 
 
 def expand(kernel, name: str, mode: str = "float64"):
@@ -127,6 +147,7 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
     members, block = found
     elem = 8 if mode == "float64" else 4
     parts, stages = [], []
+    lower_modes: set = set()
     for member, record in zip(members, block["stages"]):
         if getattr(member, "one_step", None) is not None:
             raise HawkError(f"{name!r}: an automatic stepping kernel's stages are not built on the b200 target")
@@ -155,6 +176,9 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
             if "__shared__" in body:
                 # the body keeps arrays of its own in shared memory: one team a block
                 threads, smem = 32, (smem // max(threads // 32, 1) if smem else 0)
+            staged_lower = lower_staged(member.team, smem, threads)
+            if staged_lower is not None:
+                lower_modes.add(staged_lower)
             if "hawk_map" in body:
                 raise HawkError(f"{name!r}: a block sum over an index map (an active-set build) is not built "
                                 "on the b200 target")
@@ -197,7 +221,10 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
                        "groups": team_record.get("groups"), "of": team_record.get("of"),
                        "status": team_record.get("status"),
                        "ops": [st.op for st in member.team.steps] if isinstance(member, TeamStage) else []})
-    text = "\n".join([*prelude_lines(name, mode), "", *parts])
+    # every Cholesky-family call of the unit stages its packed triangle, or
+    # none does: the library compiles that one accessor (hk/team.cuh)
+    defines = [f"HK_TEAM_LOWER_STAGED {int(lower_modes.pop())}"] if len(lower_modes) == 1 else []
+    text = "\n".join([*prelude_lines(name, mode, defines), "", *parts])
     unit = Unit(name=name, mode=mode, text=text, body="", frame="split",
                 digest=hashlib.sha256(text.encode()).hexdigest(), entries="\n".join(parts),
                 notes={"dynamic_smem": 0, "staged": False, "stages": 0, "min_blocks": 0, "persist": None,

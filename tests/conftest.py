@@ -24,6 +24,20 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (a B200); run with -m gpu")
 
 
+def pytest_sessionstart(session):
+    """Bring the in-tree builds up to date before any test loads them: the
+    C-ABI library (nvcc) when a source or header is newer than it -- the loader
+    refuses a library stale against its sources -- and each bundle's CUBIN
+    (NVRTC) when its unit or a header is newer.  Each is a no-op when current;
+    without a compiler the tests run on what is built."""
+    try:
+        from hawk_b200.csrc import build
+        build.build_library()
+        build.build_cubins()
+    except Exception as exc:                     # noqa: BLE001 -- reported by the tests that need them
+        print(f"conftest: the in-tree builds were not refreshed ({exc})")
+
+
 @pytest.fixture(scope="session")
 def golden():
     cache = {}
