@@ -91,10 +91,10 @@ extern "C" __global__ void __launch_bounds__(256) poly_loss_vjp(
 #pragma unroll
         for (int hawk_q = 0; hawk_q < 8; ++hawk_q) {
         Real* const hawk_ss = hawk_terms + hawk_q * 3;
-        const long long hawk_flat = ((hawk_r0 + hawk_q) << 5) + static_cast<long long>(threadIdx.x & 31u);
+        const long long hawk_flat = ((hawk_r0 + static_cast<long long>((threadIdx.x & 31u) >> 2)) << 5) + static_cast<long long>(threadIdx.x & 3u) + 4 * hawk_q;
         if (hawk_flat < count) {
         const long long hawk_i = base + hawk_flat;
-        const hk::SampleIndex i{hawk_i, hk_st, static_cast<int>((((threadIdx.x >> 5) * 8 + hawk_q) << 5) + (threadIdx.x & 31u))};
+        const hk::SampleIndex i{hawk_i, hk_st, static_cast<int>(hawk_flat - hk_t * 2048)};
         (void)hawk_i;
         (void)nSamples;
         const auto psc_x_i = psc_x[i].eval();
@@ -126,7 +126,7 @@ extern "C" __global__ void __launch_bounds__(256) poly_loss_vjp(
                 aout_bar_c_comp.data()[hawk_row] = hawk_c;
             }
         };
-        hk::ss::rows_reduce<8, 3, hk::ss::kSum>(hawk_terms, hawk_ss_store);
+        hk::ss::rows_reduce_lanes<8, 3, hk::ss::kSum>(hawk_terms, hawk_ss_store);
         }
         if (hk_use) {
             hk_pipe.release(hk_j);

@@ -196,6 +196,83 @@ __device__ __forceinline__ void rows_reduce(T (&h)[K * W], Store&& store) {
         if (j < held) store(first + j, h[j], root_comp<OP>(h[j], c[j]));
 }
 
+// The halving rounds across lane bits OFF, OFF / 2, ..., 1, starting from M
+// columns a lane; FIRST as in halve (for the round that opens a row's tree).
+template <int M, int OFF, int OP, bool FIRST, class T>
+__device__ __forceinline__ void lane_rounds(T* h, T* c, unsigned lane) {
+    if constexpr (OFF >= 1) {
+        halve<M, OP, FIRST>(h, c, OFF, (lane & static_cast<unsigned>(OFF)) != 0u);
+        lane_rounds<M - M / 2, OFF / 2, OP, false>(h, c, lane);
+    }
+}
+template <int M, int OFF> constexpr int held_after() {
+    if constexpr (OFF >= 1) return held_after<M - M / 2, OFF / 2>();
+    else return M;
+}
+
+// The rows of K consecutive 32-sample rows with each row spread over P = 32 / K
+// lanes: lane l holds, in slot q, sample (l % P) + P q of row l / P
+// (h[q * W + k] for column k, identity past the last sample).  A row's tree
+// pairs samples 16 apart first, then 8, ..., 1 (the row tree above); the
+// levels whose pairs lie in one lane (16, ..., P apart: slots q and q + K/2,
+// then q + K/4, ...) are joined in registers, the rest (P/2, ..., 1 apart) by
+// the halving butterfly across lanes, starting from the W columns of the
+// lane's row.  Every node joins the same two operands, lower sample first, as
+// in rows_reduce, and after the in-register levels each lane holds exactly
+// the columns rows_reduce's lane holds after as many rounds, so the rows are
+// the same bits; the in-register levels take no shuffle and no select.
+// store(col, sum, comp), col = row * W + k, as in rows_reduce.  All 32 lanes
+// of the warp must call it.
+template <int K, int W, int OP, class T, class Store>
+__device__ __forceinline__ void rows_reduce_lanes(T (&h)[K * W], Store&& store) {
+    constexpr int P = 32 / K;
+    static_assert(K * P == 32, "K must be a power of two dividing 32");
+    T c[K * W];
+#pragma unroll
+    for (int k = 0; k < K * W; ++k) c[k] = T(0);
+    if constexpr (K >= 2) {
+#pragma unroll
+        for (int q = 0; q < K / 2; ++q)
+#pragma unroll
+            for (int k = 0; k < W; ++k) {
+                T& s = h[q * W + k];
+                const T s2 = h[(q + K / 2) * W + k];
+                if constexpr (OP == kSum) {
+                    const T t = s + s2;
+                    c[q * W + k] = two_sum_err(s, s2, t);
+                    s = t;
+                } else {
+                    s = extreme(OP, s, s2);
+                }
+            }
+#pragma unroll
+        for (int span = K / 4; span >= 1; span /= 2)
+#pragma unroll
+            for (int q = 0; q < span; ++q)
+#pragma unroll
+                for (int k = 0; k < W; ++k)
+                    pair_combine_unchecked<OP>(h[q * W + k], c[q * W + k], h[(q + span) * W + k],
+                                               c[(q + span) * W + k]);
+    }
+    const unsigned lane = threadIdx.x & 31u;
+    lane_rounds<W, P / 2, OP, K == 1>(h, c, lane);
+    int first = static_cast<int>(lane / P) * W, held = W, m = W;
+#pragma unroll
+    for (int off = P / 2; off >= 1; off /= 2) {
+        if (lane & static_cast<unsigned>(off)) {
+            first += m / 2;
+            held -= m / 2;
+        } else if (held > m / 2) {
+            held = m / 2;
+        }
+        m -= m / 2;
+    }
+    constexpr int MF = held_after<W, P / 2>();
+#pragma unroll
+    for (int j = 0; j < MF; ++j)
+        if (j < held) store(first + j, h[j], root_comp<OP>(h[j], c[j]));
+}
+
 #endif
 
 }  // namespace ss

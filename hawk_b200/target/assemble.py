@@ -201,17 +201,18 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
     wrapper = B200
     smem = 0
     frame_note = None
-    elem_bytes = 8 if mode == "float64" else 4
+    elem_bytes = 4 if mode == "float32" else 8
     if sums:
         elem = element_spelling(sums[0].ttype.dtype)
         plan = StagePlan(walk, elem_bytes, 256 * wrapper.fold_rows(len(sums))) if staged else None
         if plan is not None and plan.enabled:
             opened, closed = wrapper.sample_sum_frame_staged(plan, len(sums), elem, sample_sum_store(sums, banded=mode == "banded"),
-                                                             sums[0].op)
+                                                             sums[0].op, elem_bytes=elem_bytes)
             smem = plan.smem_bytes
         else:
             plan = None
-            opened, closed = wrapper.sample_sum_frame(len(sums), elem, sample_sum_store(sums, banded=mode == "banded"), sums[0].op)
+            opened, closed = wrapper.sample_sum_frame(len(sums), elem, sample_sum_store(sums, banded=mode == "banded"),
+                                                      sums[0].op, elem_bytes=elem_bytes)
         loop = [opened, body, closed]
         frame = "row"
     else:

@@ -184,19 +184,50 @@ class B200Wrapper:
             k *= 2
         return k
 
+    @staticmethod
+    def row_lanes(k: int, elem_bytes: int) -> int:
+        """Lanes over which each row of a K-row trip is spread (``P`` = 32 / K),
+        or 0 for the plain mapping.  Spread, lane l holds samples (l % P) + P q
+        of row l / P and the row tree's levels 16 ... P apart are joined in
+        registers (hk::ss::rows_reduce_lanes); P lanes read P consecutive
+        samples of a row, so the spread is taken only where that is a whole
+        32-byte sector (P * element size >= 32)."""
+        p = 32 // k
+        return p if p * elem_bytes >= 32 and p < 32 else 0
+
+    @staticmethod
+    def _flat(lanes: int) -> str:
+        """The sample of the trip's slot ``hawk_q`` on this lane, counted from
+        the partition's start."""
+        if not lanes:
+            return "((hawk_r0 + hawk_q) << 5) + static_cast<long long>(threadIdx.x & 31u)"
+        shift = lanes.bit_length() - 1
+        return (f"((hawk_r0 + static_cast<long long>((threadIdx.x & 31u) >> {shift})) << 5) + "
+                f"static_cast<long long>(threadIdx.x & {lanes - 1}u) + {lanes} * hawk_q")
+
+    @staticmethod
+    def _reduce(k: int, width: int, code: str, lanes: int) -> str:
+        fn = "rows_reduce_lanes" if lanes else "rows_reduce"
+        return f"hk::ss::{fn}<{k}, {width}, {code}>(hawk_terms, hawk_ss_store);"
+
     def sample_sum_frame(self, width: int, elem: str, store: str,
-                         op: str = "sum", live: str | None = None) -> tuple:
+                         op: str = "sum", live: str | None = None, elem_bytes: int = 8) -> tuple:
         """The row frame around a body writing ``width`` terms into ``hawk_ss``.
 
-        A warp takes K consecutive rows per trip (lane l on sample 32 * row + l
-        of each, loads of all K rows in flight together); the K rows' columns
-        are reduced in one halving butterfly (hk::ss::rows_reduce).  ``store``
-        is the body of ``hawk_ss_store(hawk_col, hawk_s, hawk_c)`` at row
-        ``hawk_row``; a lane past ``count`` adds the identity."""
+        A warp takes K consecutive rows per trip, loads of all K rows in flight
+        together.  Where a row spreads over P = 32 / K lanes (``row_lanes``),
+        lane l takes samples (l % P) + P q of row l / P and joins its own
+        samples' tree levels in registers before the butterfly
+        (hk::ss::rows_reduce_lanes); otherwise lane l takes sample 32 * row + l
+        of each row and the K rows' columns are reduced in one halving
+        butterfly (hk::ss::rows_reduce).  ``store`` is the body of
+        ``hawk_ss_store(hawk_col, hawk_s, hawk_c)`` at row ``hawk_row``; a lane
+        past ``count`` adds the identity."""
         if live is not None:
             raise HawkError("a sample sum over an active-set prefix is not built on the b200 target")
         code = _OP_CODE[op]
         k = self.fold_rows(width)
+        lanes = self.row_lanes(k, elem_bytes)
         opened = (
             "    const long long hawk_rows = (count + 31) >> 5;\n"
             f"    for (long long hawk_r0 = hk::warp_first() * {k}; hawk_r0 < hawk_rows; "
@@ -208,7 +239,7 @@ class B200Wrapper:
             "#pragma unroll\n"
             f"        for (int hawk_q = 0; hawk_q < {k}; ++hawk_q) {{\n"
             f"        {elem}* const hawk_ss = hawk_terms + hawk_q * {width};\n"
-            "        const long long hawk_flat = ((hawk_r0 + hawk_q) << 5) + static_cast<long long>(threadIdx.x & 31u);\n"
+            f"        const long long hawk_flat = {self._flat(lanes)};\n"
             "        if (hawk_flat < count) {\n"
             "        const long long hawk_i = base + hawk_flat;\n"
             "        const hk::SampleIndex i{hawk_i};\n"
@@ -218,16 +249,18 @@ class B200Wrapper:
             "        }\n"
             "        }\n"
             f"{store.replace('__K__', str(k)).replace('__W__', str(width))}\n"
-            f"        hk::ss::rows_reduce<{k}, {width}, {code}>(hawk_terms, hawk_ss_store);\n"
+            f"        {self._reduce(k, width, code, lanes)}\n"
             "    }")
         return opened, closed
 
     def sample_sum_frame_staged(self, plan: StagePlan, width: int, elem: str, store: str,
-                                op: str = "sum") -> tuple:
+                                op: str = "sum", elem_bytes: int = 8) -> tuple:
         """The row frame over tiles of 8 warps x K rows staged through shared
-        memory: warp w of the CTA takes rows [w K, (w + 1) K) of each tile."""
+        memory: warp w of the CTA takes rows [w K, (w + 1) K) of each tile,
+        its lanes mapped onto them as in ``sample_sum_frame``."""
         code = _OP_CODE[op]
         k = self.fold_rows(width)
+        lanes = self.row_lanes(k, elem_bytes)
         span = 256 * k
         opened = "\n".join([
             "    const long long hawk_rows = (count + 31) >> 5;",
@@ -242,11 +275,10 @@ class B200Wrapper:
             "#pragma unroll",
             f"        for (int hawk_q = 0; hawk_q < {k}; ++hawk_q) {{",
             f"        {elem}* const hawk_ss = hawk_terms + hawk_q * {width};",
-            "        const long long hawk_flat = ((hawk_r0 + hawk_q) << 5) + static_cast<long long>(threadIdx.x & 31u);",
+            f"        const long long hawk_flat = {self._flat(lanes)};",
             "        if (hawk_flat < count) {",
             "        const long long hawk_i = base + hawk_flat;",
-            f"        const hk::SampleIndex i{{hawk_i, hk_st, static_cast<int>((((threadIdx.x >> 5) * {k} + hawk_q) << 5) "
-            "+ (threadIdx.x & 31u))};",
+            f"        const hk::SampleIndex i{{hawk_i, hk_st, static_cast<int>(hawk_flat - hk_t * {256 * k})}};",
             "        (void)hawk_i;",
             "        (void)nSamples;",
         ])
@@ -255,7 +287,7 @@ class B200Wrapper:
             "        }",
             "        if (hawk_r0 < hawk_rows) {",
             store.replace("__K__", str(k)).replace("__W__", str(width)),
-            f"        hk::ss::rows_reduce<{k}, {width}, {code}>(hawk_terms, hawk_ss_store);",
+            f"        {self._reduce(k, width, code, lanes)}",
             "        }",
             plan.loop_tail(),
         ])
