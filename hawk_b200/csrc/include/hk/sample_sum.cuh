@@ -34,10 +34,13 @@ template <class T> HK_HD bool finite(T x) { return (x - x) == (x - x); }
 // (Knuth, TAOCP vol. 2, 4.2.2 Theorem B; no intermediate of 2Sum overflows
 // unless s does: Boldo, Graillat and Muller, ACM TOMS 44(1), 2017).  Where s
 // is not finite the residual is discarded by every caller (the node's
-// compensation becomes 0).
+// compensation becomes 0).  A zero residual is never -0: a round-to-nearest
+// sum is -0 only when both operands are -0, here a - (s - bb) and b - bb,
+// which needs a = b = -0 and s - bb = +0 -- but then s = -0, bb = +0 and
+// s - bb = -0.  (The reference's Fast2Sum residual carries an explicit + 0.)
 template <class T> HK_HD T two_sum_err(T a, T b, T s) {
     const T bb = s - a;
-    return ((a - (s - bb)) + (b - bb)) + T(0);
+    return (a - (s - bb)) + (b - bb);
 }
 
 template <class T> HK_HD T extreme(int op, T a, T b) {
