@@ -6,6 +6,7 @@ using Real = double;
 using Int = long long;
 
 HK_SELF_CHECK_EXPORTS
+HK_DYNAMIC_SMEM(49280)
 
 extern "C" __global__ void __launch_bounds__(256) poly_loss_vjp(
     hk::abi::ScalarHandle p_aout_bar_a,
@@ -36,11 +37,11 @@ extern "C" __global__ void __launch_bounds__(256) poly_loss_vjp(
     (void)aout_bar_c;
     const hk::ScalarOut<Real> aout_bar_c_comp(p_aout_bar_c_comp);
     (void)aout_bar_c_comp;
-    const hk::ScalarIn<Real> psc_bar_r(p_psc_bar_r);
+    const hk::ScalarIn<Real> psc_bar_r(p_psc_bar_r, 0u);
     (void)psc_bar_r;
-    const hk::ScalarIn<Real> psc_t(p_psc_t);
+    const hk::ScalarIn<Real> psc_t(p_psc_t, 2048u);
     (void)psc_t;
-    const hk::ScalarIn<Real> psc_x(p_psc_x);
+    const hk::ScalarIn<Real> psc_x(p_psc_x, 4096u);
     (void)psc_x;
     const hk::ScalarIn<Real> lut_a(p_lut_a);
     (void)lut_a;
@@ -55,7 +56,23 @@ extern "C" __global__ void __launch_bounds__(256) poly_loss_vjp(
     const auto lut_c_cell = lut_c.cell();
     (void)lut_c_cell;
     const long long hawk_rows = (count + 31) >> 5;
-    for (long long hawk_r0 = hk::warp_first() * 8; hawk_r0 < hawk_rows; hawk_r0 += hk::warp_step() * 8) {
+    extern __shared__ __align__(128) unsigned char hk_smem[];
+    hk::stage::WarpTile hk_tile(hk_smem, 6144u, 6144u);
+    const bool hk_aligned = hk::stage::aligned(psc_bar_r.data(), 0ull, base * static_cast<long long>(sizeof(*psc_bar_r.data()))) && hk::stage::aligned(psc_t.data(), 0ull, base * static_cast<long long>(sizeof(*psc_t.data()))) && hk::stage::aligned(psc_x.data(), 0ull, base * static_cast<long long>(sizeof(*psc_x.data())));
+    auto hk_fill = [&](long long hk_r) {      // warp-uniform: the trip starting at row hk_r
+        if (!hk_aligned || ((hk_r + 8) << 5) > count) return;
+        hk_tile.fill([&](unsigned char* hk_to, unsigned long long* hk_bar) {
+            const long long hk_first = hk_r << 5;
+            hk::stage::copy(hk_to + 0u, psc_bar_r.data() + base + hk_first, 2048u, hk_bar);
+            hk::stage::copy(hk_to + 2048u, psc_t.data() + base + hk_first, 2048u, hk_bar);
+            hk::stage::copy(hk_to + 4096u, psc_x.data() + base + hk_first, 2048u, hk_bar);
+        });
+    };
+    const long long hk_step = hk::warp_step() * 8;
+    long long hawk_r0 = hk::warp_first() * 8;
+    if (hawk_r0 < hawk_rows) hk_fill(hawk_r0);
+    for (; hawk_r0 < hawk_rows; hawk_r0 += hk_step) {
+        const unsigned char* const hk_st = hk_tile.acquire();
         Real hawk_terms[24];
 #pragma unroll
         for (int hawk_k = 0; hawk_k < 24; ++hawk_k) hawk_terms[hawk_k] = hk::ss::identity<Real>(hk::ss::kSum);
@@ -65,7 +82,7 @@ extern "C" __global__ void __launch_bounds__(256) poly_loss_vjp(
         const long long hawk_flat = ((hawk_r0 + static_cast<long long>((threadIdx.x & 31u) >> 2)) << 5) + static_cast<long long>(threadIdx.x & 3u) + 4 * hawk_q;
         if (hawk_flat < count) {
         const long long hawk_i = base + hawk_flat;
-        const hk::SampleIndex i{hawk_i};
+        const hk::SampleIndex i{hawk_i, hk_st, static_cast<int>(hawk_flat - (hawk_r0 << 5))};
         (void)hawk_i;
         (void)nSamples;
         const auto psc_x_i = psc_x[i].eval();
@@ -77,6 +94,7 @@ extern "C" __global__ void __launch_bounds__(256) poly_loss_vjp(
         hawk_ss[2] = t18;
         }
         }
+        if (hawk_r0 + hk_step < hawk_rows) hk_fill(hawk_r0 + hk_step);
         auto hawk_ss_store = [&](int hawk_col, auto hawk_s, auto hawk_c) {
             (void)hawk_c;
             const int hawk_q = hawk_col / 3;
@@ -98,4 +116,5 @@ extern "C" __global__ void __launch_bounds__(256) poly_loss_vjp(
         };
         hk::ss::rows_reduce_lanes<8, 3, hk::ss::kSum>(hawk_terms, hawk_ss_store);
     }
+    hk_tile.finish();
 }

@@ -28,6 +28,7 @@ namespace stage {
 constexpr unsigned kErrFullWait = 1u;    // a stage's data did not arrive in time
 constexpr unsigned kErrEmptyWait = 2u;   // a stage was not released in time
 constexpr unsigned kErrDrain = 4u;       // copies still in flight when the CTA gave up
+constexpr unsigned kErrWarpWait = 16u;   // a warp's tile did not arrive in time; it read global memory
 
 // Bound of one wait: two seconds.
 constexpr unsigned long long kWaitNs = 2000000000ull;
@@ -88,6 +89,10 @@ HK_FI void copy(void* dst, const void* src, unsigned bytes, unsigned long long* 
 }
 
 HK_FI void fail(unsigned bit) { atomicOr(&hk_error_flags, bit); }
+
+// Orders this thread's earlier generic-proxy accesses to shared memory before
+// later async-proxy (bulk copy) writes to it.
+HK_FI void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 #endif
 
 // Whether a plane component can be copied in tiles: 16-byte aligned start and
@@ -174,6 +179,75 @@ struct Pipe {
 #pragma unroll
         for (int s = 0; s < S; ++s)
             if (((issued >> s) & 1u) && !wait(full + s, (parity >> s) & 1u)) hk::stage::fail(kErrDrain);
+    }
+};
+
+// One warp's own tile of inputs, fetched one trip ahead: the warp's lane 0
+// issues the next trip's bulk copies on the warp's mbarrier before the warp
+// reduces the current trip, so the copies overlap the reduction and need no
+// registers; no other warp takes part, so nothing waits across warps.  The
+// block's dynamic shared memory holds the warps' barriers in its first 128
+// bytes, then one `stage_bytes` tile per warp.
+//
+// A tile that does not arrive within kWaitNs is not waited for again: the warp
+// sets kErrWarpWait, reads that trip's inputs and every later trip's from
+// global memory (the same values, so the outputs are complete), issues no more
+// copies, and before it returns waits once more (bounded) for the copy still
+// landing, setting kErrDrain if it never does.
+struct WarpTile {
+    unsigned long long* bar;
+    unsigned char* buf;
+    unsigned tx_bytes;
+    unsigned parity = 0u;
+    bool pending = false;    // a fill has been issued and not yet taken
+    bool broken = false;     // a wait ran out: no more fills
+
+    // Every lane of the warp calls it.
+    HK_FI WarpTile(unsigned char* shared, unsigned stage_bytes, unsigned tx) {
+        const unsigned w = threadIdx.x >> 5;
+        bar = reinterpret_cast<unsigned long long*>(shared) + w;
+        buf = shared + 128 + static_cast<unsigned long long>(w) * stage_bytes;
+        tx_bytes = tx;
+        if ((threadIdx.x & 31u) == 0u) {
+            init(bar, 1u);
+            fence_init();
+        }
+        __syncwarp();
+    }
+
+    // Every lane: fill the tile through `issue(tile, barrier)`, run by lane 0
+    // (the tile's bulk copies on the barrier).  The warp's earlier reads of the
+    // tile are ordered before the copies' writes.
+    template <class Issue>
+    HK_FI void fill(Issue&& issue) {
+        if (broken) return;
+        __syncwarp();
+        fence_proxy_async();
+        if ((threadIdx.x & 31u) == 0u) {
+            arrive_expect_tx(bar, tx_bytes);
+            issue(buf, bar);
+        }
+        pending = true;
+    }
+
+    // Every lane: the filled tile, or nullptr (none pending, or its wait ran
+    // out) -- the caller then reads global memory.
+    HK_FI const unsigned char* acquire() {
+        if (!pending || broken) return nullptr;
+        if (__all_sync(0xffffffffu, wait(bar, parity))) {
+            parity ^= 1u;
+            pending = false;
+            return buf;
+        }
+        broken = true;
+        if ((threadIdx.x & 31u) == 0u) fail(kErrWarpWait);
+        return nullptr;
+    }
+
+    // Every lane, before the warp returns: a copy still landing is waited for.
+    HK_FI void finish() {
+        if (pending && (threadIdx.x & 31u) == 0u && !wait(bar, parity)) fail(kErrDrain);
+        __syncwarp();
     }
 };
 #endif

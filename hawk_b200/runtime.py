@@ -32,6 +32,7 @@ import ctypes
 import hashlib
 import json
 import threading
+import warnings
 from pathlib import Path
 
 from . import abi
@@ -83,10 +84,12 @@ def _box(kind: str, value):
 
 
 #: Bits of a unit's error word (hk/stage.cuh) and what each reports.
-WAIT_FULL, WAIT_EMPTY, WAIT_DRAIN = 1, 2, 4
+WAIT_FULL, WAIT_EMPTY, WAIT_DRAIN, WAIT_WARP = 1, 2, 4, 16
 WAIT_ERRORS = {WAIT_FULL: "a staged input tile did not arrive within the wait limit",
                WAIT_EMPTY: "a shared-memory stage was not released within the wait limit",
-               WAIT_DRAIN: "a block gave up with copies into shared memory still in flight"}
+               WAIT_DRAIN: "a block gave up with copies into shared memory still in flight",
+               WAIT_WARP: "a warp's fetched-ahead input tile did not arrive within the wait limit "
+                          "(the warp read those inputs from global memory instead)"}
 
 
 class DeviceKernel:
@@ -327,7 +330,12 @@ class DeviceKernel:
         wait limit (the launch's outputs are incomplete); a block that gave up
         with copies into shared memory still in flight (``kErrDrain``), after
         which this unit is not launched again in this process -- another block
-        may have been given that shared memory while the copy was landing."""
+        may have been given that shared memory while the copy was landing.  A
+        warp-tiled entry's wait that ran out alone (``kErrWarpWait``) left the
+        outputs complete -- the warp read global memory instead -- and is
+        reported as a warning.  A staged entry is checked after every launch;
+        a warp-tiled one, whose launches do not synchronise, when the caller
+        calls this (a synchronising read of the word)."""
         flags = self.library.errors(clear=True)
         if not flags:
             return
@@ -337,6 +345,9 @@ class DeviceKernel:
             self.poisoned = (message + "; the unit is not launched again in this process (reload the "
                              "library in a new process)")
             raise HawkError(self.poisoned)
+        if flags == WAIT_WARP:
+            warnings.warn(message + "; the outputs are complete", RuntimeWarning, stacklevel=2)
+            return
         raise HawkError(message + "; the launch's outputs are incomplete")
 
     def cells_state(self, n: int):

@@ -170,12 +170,13 @@ def _word_read() -> str:
 
 
 def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: bool = True,
-                min_blocks: int | None = None, threads: int | None = None) -> Unit:
+                min_blocks: int | None = None, threads: int | None = None, warp_tiled: bool = True) -> Unit:
     """The b200 unit of a traced kernel (``hawk.Kernel``) in scalar mode ``mode``;
     ``staged`` streams its inputs through shared-memory stages filled by the
     TMA unit (hk/stage.cuh) where the stage plan fits; ``min_blocks`` caps the
     entry's registers so that that many blocks of ``threads`` (256 when None)
-    stay resident per SM."""
+    stay resident per SM; ``warp_tiled`` lets a row frame fetch each warp's
+    next trip ahead where the wrapper takes it (``B200.warp_tiled``)."""
     from hawk.ir.nodes import sample_sums
     from hawk.emit.render import render_body
     from hawk.emit.spelling import element_spelling
@@ -201,18 +202,25 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
     wrapper = B200
     smem = 0
     frame_note = None
+    tiled = False
     elem_bytes = 4 if mode == "float32" else 8
     if sums:
         elem = element_spelling(sums[0].ttype.dtype)
+        store = sample_sum_store(sums, banded=mode == "banded")
         plan = StagePlan(walk, elem_bytes, 256 * wrapper.fold_rows(len(sums))) if staged else None
+        tile = StagePlan(walk, elem_bytes, 32 * wrapper.fold_rows(len(sums))) if warp_tiled else None
         if plan is not None and plan.enabled:
-            opened, closed = wrapper.sample_sum_frame_staged(plan, len(sums), elem, sample_sum_store(sums, banded=mode == "banded"),
-                                                             sums[0].op, elem_bytes=elem_bytes)
+            opened, closed = wrapper.sample_sum_frame_staged(plan, len(sums), elem, store, sums[0].op,
+                                                             elem_bytes=elem_bytes)
             smem = plan.smem_bytes
+        elif tile is not None and tile.enabled and wrapper.warp_tiled(tile, len(sums), elem_bytes):
+            opened, closed = wrapper.sample_sum_frame_warp_tiled(tile, len(sums), elem, store, sums[0].op,
+                                                                 elem_bytes=elem_bytes)
+            plan, tiled = tile, True
+            smem = 128 + 8 * tile.stage_bytes
         else:
             plan = None
-            opened, closed = wrapper.sample_sum_frame(len(sums), elem, sample_sum_store(sums, banded=mode == "banded"),
-                                                      sums[0].op, elem_bytes=elem_bytes)
+            opened, closed = wrapper.sample_sum_frame(len(sums), elem, store, sums[0].op, elem_bytes=elem_bytes)
         loop = [opened, body, closed]
         frame = "row"
     else:
@@ -286,8 +294,9 @@ def render_unit(kernel, name: str | None = None, mode: str = "float64", staged: 
     records = tuple((s.name, s.op, s.companion.name if s.op == "sum" else None) for s in sums)
     return Unit(name=name, mode=mode, text=text, body=body, frame=frame, sums=records, entries=entries,
                 digest=hashlib.sha256(text.encode()).hexdigest(),
-                notes={"dynamic_smem": smem, "staged": plan is not None,
-                       "stages": plan.stages if plan is not None else 0, "min_blocks": min_blocks or 0,
+                notes={"dynamic_smem": smem, "staged": plan is not None and not tiled,
+                       "stages": plan.stages if plan is not None and not tiled else 0, "warp_tiled": tiled,
+                       "min_blocks": min_blocks or 0,
                        "block": threads or 256,
                        "persist": f"{name}{PERSIST_SUFFIX}" if persist is not None else None,
                        "range": f"{name}{RANGE_SUFFIX}" if ranged is not None else None,

@@ -172,7 +172,8 @@ def choose_unit(kernel, name: str, mode: str = "float64", staged: bool | None = 
     cap ``next_slot_bounds`` gives where it does not spill.  ``staged`` True
     asks for the staged unit, ``bounds`` for a fixed ``(threads, blocks)``."""
     if bounds is not None:
-        unit = render_unit(kernel, name, mode, staged=False, threads=bounds[0], min_blocks=bounds[1])
+        unit = render_unit(kernel, name, mode, staged=False, threads=bounds[0], min_blocks=bounds[1],
+                           warp_tiled=False)
     else:
         unit = render_unit(kernel, name, mode, staged=bool(staged))
     cubin, log, ptxas = compile_cubin(unit.text, name)
@@ -189,7 +190,8 @@ def choose_unit(kernel, name: str, mode: str = "float64", staged: bool | None = 
     slot = next_slot_bounds(ptxas.get(name, {}).get("regs", 0))
     if (bounds is None and slot is not None and not unit.notes.get("staged") and not unit.notes.get("dynamic_smem")
             and not unit.notes.get("private_smem") and getattr(kernel, "one_step", None) is None):
-        capped = render_unit(kernel, name, mode, staged=False, threads=slot[0], min_blocks=slot[1])
+        capped = render_unit(kernel, name, mode, staged=False, threads=slot[0], min_blocks=slot[1],
+                             warp_tiled=False)
         c_cubin, c_log, c_ptxas = compile_cubin(capped.text, name)
         if not _spills(c_ptxas, name):
             unit, cubin, log, ptxas = capped, c_cubin, c_log, c_ptxas
@@ -209,6 +211,7 @@ def b200_block(unit, walk, ptxas: dict, name: str, unit_file: str, cubin_file: s
         "frame": unit.frame,
         "dynamic_smem": unit.notes.get("dynamic_smem", 0),
         "stages": unit.notes.get("stages", 0),
+        "warp_tiled": unit.notes.get("warp_tiled", False),
         "min_blocks": unit.notes.get("min_blocks", 0),
         "block": unit.notes.get("block", 256),
         "persist": unit.notes.get("persist"),

@@ -145,7 +145,7 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
     if found is None:
         raise HawkError(f"{name!r} runs in one launch; it is not a split kernel")
     members, block = found
-    elem = 8 if mode == "float64" else 4
+    elem = 4 if mode == "float32" else 8
     parts, stages = [], []
     lower_modes: set = set()
     for member, record in zip(members, block["stages"]):
@@ -156,7 +156,7 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
         if threads is None:
             # a per-lane stage: the lane frame, or the row frame of the sample
             # sums it reduces into cells a later stage reads
-            unit = render_unit(member, member.name, mode, staged=False)
+            unit = render_unit(member, member.name, mode, staged=False, warp_tiled=False)
             if unit.notes.get("persist") or unit.notes.get("folds"):
                 raise HawkError(f"{name!r}: stage {member.name!r} commits into a compensated scatter target, "
                                 "which a split kernel's stage does not build yet")

@@ -121,6 +121,50 @@ def test_poly_loss_rows_through_the_entry():
         same(host(out[name + "_comp"]), comp[j])
 
 
+@pytest.mark.parametrize("shift,n,base", [(0, 256 * 37, 0), (0, 256 * 37 + 1, 0), (0, 256 * 37 - 1, 0),
+                                          (1, 5000, 0), (0, 40000, 4096), (1, 40000, 4096)],
+                         ids=["whole-tiles", "one-past", "one-short", "unaligned", "partition", "unaligned-partition"])
+def test_warp_tiled_rows_match_the_oracle(shift, n, base):
+    """The VJP's row frame fetches each warp's next trip into its shared-memory
+    tile (``warp_tiled`` in the sidecar): whole trips come from the tile, a
+    partial last trip and planes off the 16-byte boundary (``shift`` of one
+    element: every trip) from global memory.  Every row of the partition
+    equals the oracle's, rows outside it are untouched, and no bounded wait
+    ran out."""
+    import warnings
+
+    from hawk_b200.planes import as_plane
+
+    k = runtime.load(BUNDLES, "poly_loss_vjp")
+    assert k.sidecar["b200"]["warp_tiled"]
+    w = workloads.poly_loss(n, seed=n + shift)
+
+    def shifted(a):
+        t = torch.empty(len(a) + shift, dtype=torch.float64, device="cuda")
+        t[shift:] = dev(a)
+        return t[shift:]
+
+    rows = -(-n // 32)
+    planes = {name: shifted(w[name]) for name in ("x", "t", "bar_r")}
+    planes.update({name: dev(np.array([w[name]])) for name in ("a", "b", "c")})
+    out = {name: nan_like((rows,)) for name in ("bar_a", "bar_a_comp", "bar_b", "bar_b_comp", "bar_c", "bar_c_comp")}
+    bound = {name: as_plane(name, obj) for name, obj in {**planes, **out}.items()}
+    k.check(bound, {}, n)
+    k.bind_all(bound, {}, n)
+    k.launch(base, n - base, n)
+    torch.cuda.synchronize()
+    with warnings.catch_warnings():
+        warnings.simplefilter("error")
+        k.check_waits()
+    hi, comp = oracle.poly_loss_vjp_rows(w["x"], w["t"], w["bar_r"], w["a"], w["b"], w["c"])
+    lo = base // 32
+    for j, name in enumerate(("bar_a", "bar_b", "bar_c")):
+        got_hi, got_comp = host(out[name]), host(out[name + "_comp"])
+        assert np.isnan(got_hi[:lo]).all() and np.isnan(got_comp[:lo]).all()
+        same(got_hi[lo:], hi[j, lo:])
+        same(got_comp[lo:], comp[j, lo:])
+
+
 @pytest.mark.parametrize("n", SIZES)
 def test_gravity_fwd_jvp_vjp(n):
     w = workloads.gravity(n, seed=n)
