@@ -191,7 +191,7 @@ def barrier(dist):
 class PolyStep:
     """The headline step on one GPU, bound once (device-resident planes)."""
 
-    def __init__(self, n: int, mode: str, device: int, rank: int, world: int, dist) -> None:
+    def __init__(self, n: int, mode: str, device: int, rank: int, world: int, dist, finish: str = "peer") -> None:
         import torch
 
         from hawk_b200 import runtime, sharded, workloads
@@ -234,6 +234,17 @@ class PolyStep:
         self.gathered = torch.empty((max(world, 1), 2, 3), dtype=self.tdt, device=self.dev)
         self.hi_ptrs = [self.row_planes[k].data_ptr() for k in ("bar_a", "bar_b", "bar_c")]
         self.comp_ptrs = [self.row_planes[k + "_comp"].data_ptr() for k in ("bar_a", "bar_b", "bar_c")]
+        # ranks holding aligned subtrees finish over NVLink peer memory (one
+        # launch), or with an NCCL all-gather between two tree launches
+        self.peer = (sharded.PeerFinish(mode, 3, device) if world > 1 and self.aligned and finish == "peer"
+                     else None)
+
+    def close(self) -> None:
+        """Free the peer exchange (collective: every rank calls it)."""
+        if self.peer is not None:
+            self.peer.check()
+            self.peer.close()
+            self.peer = None
 
     def step(self, stream: int, marks=None) -> None:
         from hawk_b200 import abi, sharded
@@ -253,7 +264,7 @@ class PolyStep:
             marks[3].record()
         if self.world > 1 and sharded.aligned(self.counts):
             sharded.finish_subtrees("sum", self.mode, 3, self.leaf_hi, self.leaf_comp, self.leaves, self.cells,
-                                    stream=stream, pack=self.pack, gathered=self.gathered)
+                                    stream=stream, pack=self.pack, gathered=self.gathered, peer=self.peer)
             return
         if self.world > 1:
             hi, comp = sharded.gather_leaves(self.leaf_hi, self.leaf_comp, self.counts)
@@ -326,10 +337,12 @@ def run_headline(args, world, rank, local, dist) -> dict:
     import torch
 
     torch.cuda.set_device(local)
-    s = PolyStep(args.n, args.mode, local, rank, world, dist)
+    s = PolyStep(args.n, args.mode, local, rank, world, dist, args.finish)
     with Clocks(local) as clocks:
         per_step, marks = time_steps(s, args.steps, args.warmup, dist, marks=True)
     s.vjp.check_waits()      # a warp-tiled entry's bounded waits, read once the steps are done
+    if s.peer is not None:
+        s.peer.check()       # the peer finish's bounded waits
     fwd_ms = statistics.mean(m[0].elapsed_time(m[1]) for m in marks)
     vjp_ms = statistics.mean(m[1].elapsed_time(m[2]) for m in marks)
     leaf_ms = statistics.mean(m[2].elapsed_time(m[3]) for m in marks)
@@ -358,8 +371,13 @@ def run_headline(args, world, rank, local, dist) -> dict:
         "fwd_gbs": round(fwd_bytes / (fwd_ms * 1e-3) / 1e9, 1),
         "vjp_gbs": round(vjp_bytes / (vjp_ms * 1e-3) / 1e9, 1),
     }
+    if s.peer is not None:
+        result["finish"] = "peer memory (one launch: subtree, NVLink stores, flags, last levels)"
+    elif world > 1:
+        result["finish"] = "NCCL all-gather of the subtree roots"
     result["parity"] = headline_parity(s, world, dist)
     result["e2e"] = run_e2e(args, s, world, dist)
+    s.close()
     del s
     torch.cuda.empty_cache()
     return result
@@ -372,11 +390,12 @@ def run_c2_variant(args, world, rank, local, dist, mode: str, total: int | None)
     import torch
 
     n = args.n if total is None else total // world
-    s = PolyStep(n, mode, local, rank, world, dist)
+    s = PolyStep(n, mode, local, rank, world, dist, args.finish)
     per_step, _ = time_steps(s, max(5, min(args.steps, 20)), 3, dist)
     par = headline_parity(s, world, dist)
     out = {"n_per_gpu": n, "samples": n * world, "ms_per_step": round(per_step, 5),
            "value": _sig(n * world / (per_step * 1e-3)), "bitwise": par["cells_bitwise"]}
+    s.close()
     del s
     torch.cuda.empty_cache()
     return out
@@ -401,7 +420,7 @@ def run_e2e(args, s, world, dist) -> dict:
         runtime.run(s.fwd, x=s.x, t=s.t, a=w["a"], b=w["b"], c=w["c"], r=s.r)
         if world > 1:
             sharded.run_cells(s.vjp, total_samples=args.n * world, x=s.x, t=s.t, bar_r=s.bar_r, **s.abc,
-                              **cells)
+                              peer=s.peer, **cells)
         else:
             runtime.run(s.vjp, x=s.x, t=s.t, bar_r=s.bar_r, **s.abc, **cells)
         cells_host[0:1].copy_(cells["bar_a"], non_blocking=True)
@@ -1310,6 +1329,8 @@ def main() -> int:
     ap.add_argument("--n", type=int, default=1 << 26, help="samples per GPU")
     ap.add_argument("--mode", default="float64", choices=("float64", "float32"))
     ap.add_argument("--no-configs", action="store_true", help="skip the per-config table")
+    ap.add_argument("--finish", default="nccl", choices=("peer", "nccl"),
+                    help="the cells' last step across GPUs: one launch over NVLink peer memory, or NCCL")
     ap.add_argument("--cpu-sample", type=int, default=1 << 23)
     ap.add_argument("--only", default=None, help="time one benchmark kernel at --n samples (profiling runs); "
                     "'keyed': the ordered stages and the net axis")

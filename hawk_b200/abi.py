@@ -54,7 +54,16 @@ SIGNATURES = {
                                     _c.c_int64, _P, _P, _P]),
     "hkb_cells_finish_noalloc": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _c.POINTER(_P), _c.POINTER(_P),
                                             _c.c_int64, _P, _P]),
+    "hkb_peer_create": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.POINTER(_P), _P]),
+    "hkb_peer_connect": (_c.c_int, [_P, _P]),
+    "hkb_peer_finish": (_c.c_int, [_P, _c.c_int, _P, _P, _c.c_int64, _P, _c.c_uint64, _c.c_uint64, _P]),
+    "hkb_peer_status": (_c.c_int, [_P, _c.POINTER(_c.c_uint)]),
+    "hkb_peer_free": (None, [_P]),
 }
+
+PEER_HANDLE_BYTES = 64
+PEER_MAX_RANKS = 8
+PEER_TIMEOUT = 1
 
 _LOCK = threading.Lock()
 _LIB = None
@@ -270,3 +279,41 @@ def cells_tree_ex(op: str, dtype: str, ncols: int, hi: int, comp: int, count: in
     check(lib().hkb_cells_tree_ex(OP[op], DTYPE[dtype], int(ncols), vp(hi), vp(comp), int(count),
                                   int(elem_stride), int(col_stride), vp(out), vp(out_comp), vp(stream)),
           "hkb_cells_tree_ex")
+
+
+class PeerArea:
+    """This rank's exchange area for the peer-memory finish (``hkb_peer_*``):
+    made on ``device``, its CUDA IPC handle in ``handle`` (bytes) until
+    ``connect`` opens the other ranks' handles."""
+
+    def __init__(self, device: int, rank: int, world: int, dtype: str, ncols: int) -> None:
+        self._h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(PEER_HANDLE_BYTES)
+        check(lib().hkb_peer_create(int(device), int(rank), int(world), DTYPE[dtype], int(ncols),
+                                    ctypes.byref(self._h), buf), "hkb_peer_create")
+        self.handle = buf.raw
+        self.world = world
+
+    def connect(self, handles: list) -> None:
+        joined = b"".join(bytes(h) for h in handles)
+        if len(joined) != self.world * PEER_HANDLE_BYTES:
+            raise HawkError(f"hkb_peer_connect: {len(handles)} handles for a world of {self.world}")
+        buf = ctypes.create_string_buffer(joined, len(joined))
+        check(lib().hkb_peer_connect(self._h, buf), "hkb_peer_connect")
+
+    def finish(self, op: str, leaf_hi: int, leaf_comp: int, leaves: int, out: int, seq: int,
+               timeout_ns: int = 0, stream: int = 0) -> None:
+        vp = lambda v: ctypes.c_void_p(int(v) or None)   # noqa: E731
+        check(lib().hkb_peer_finish(self._h, OP[op], vp(leaf_hi), vp(leaf_comp), int(leaves), vp(out), int(seq),
+                                    int(timeout_ns), vp(stream)), "hkb_peer_finish")
+
+    def status(self) -> int:
+        flags = ctypes.c_uint(0)
+        check(lib().hkb_peer_status(self._h, ctypes.byref(flags)), "hkb_peer_status")
+        return int(flags.value)
+
+    def free(self) -> None:
+        h = getattr(self, "_h", None)
+        if h and h.value and _LIB is not None:
+            _LIB.hkb_peer_free(h)
+            self._h = None

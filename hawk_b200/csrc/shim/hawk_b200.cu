@@ -887,3 +887,240 @@ extern "C" int hkb_cells_finish_noalloc(int op, int dtype, int ncols, const void
     if (status != HKB_OK) return status;
     return hkb_cells_tree(op, dtype, ncols, lh, lc, leaves, out, stream);
 }
+
+// ------------------------------------------- cells across GPUs, peer memory
+//
+// The last step of a sharded finish without a collective library: every rank
+// folds its leaves to one (hi, comp) root per column, stores the root into
+// every rank's exchange area over NVLink (plain peer stores through CUDA IPC
+// mappings), raises a round flag beside it (release at system scope), waits
+// (bounded) until every rank's flag of the round is up in its own area
+// (acquire at system scope), and folds the ranks' roots in rank order.  The
+// area keeps two round parities, so a rank one round ahead writes the other
+// parity's slots and never overwrites a root its peer is still to read: a rank
+// can only start round s + 2 after every rank has published round s + 1, which
+// each does only after its round s finished.
+
+namespace {
+
+constexpr int kPeerRanks = HKB_PEER_MAX_RANKS;
+constexpr size_t kPeerFlagsAt = 256;                                             // after the status word
+constexpr size_t kPeerSlotsAt = kPeerFlagsAt + 2 * kPeerRanks * kMaxCols * 8;   // after the flags
+constexpr size_t kPeerAreaBytes = kPeerSlotsAt + 2 * kPeerRanks * kMaxCols * 2 * 8 + 256;
+constexpr unsigned long long kPeerWaitNs = 2000000000ull;
+
+struct PeerAreas {
+    unsigned char* area[kPeerRanks];
+};
+
+__device__ __forceinline__ unsigned long long peer_now() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void peer_release(unsigned long long* flag, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long peer_acquire(const unsigned long long* flag) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long* peer_flag(unsigned char* area, int parity, int rank, int col) {
+    return reinterpret_cast<unsigned long long*>(area + kPeerFlagsAt) + (parity * kPeerRanks + rank) * kMaxCols + col;
+}
+
+template <class T>
+__device__ __forceinline__ T* peer_slot(unsigned char* area, int parity, int rank, int col) {
+    return reinterpret_cast<T*>(area + kPeerSlotsAt) + ((parity * kPeerRanks + rank) * kMaxCols + col) * 2;
+}
+
+// One block per column: this rank's pairwise levels over its leaves (in place,
+// as tree_kernel), the root published to every rank, then the ranks' roots
+// folded in rank order -- the levels tree_kernel runs over world * leaves
+// leaves once each rank's own leaves are joined.
+template <class T, int OP>
+__global__ void __launch_bounds__(1024) peer_finish_kernel(T* leaf_hi, T* leaf_comp, long long leaves, PeerAreas peers,
+                                                          int rank, int world, unsigned long long seq,
+                                                          unsigned long long limit_ns, T* out) {
+    const int col = blockIdx.x;
+    T* h = leaf_hi + col * leaves;
+    T* c = leaf_comp + col * leaves;
+    for (long long st = 1; st < leaves; st <<= 1) {
+        for (long long idx = static_cast<long long>(threadIdx.x) * 2 * st; idx < leaves;
+             idx += static_cast<long long>(blockDim.x) * 2 * st) {
+            if (idx + st < leaves) {
+                T a = h[idx], ac = c[idx];
+                hk::ss::tree_join<OP>(a, ac, h[idx + st], c[idx + st]);
+                h[idx] = a;
+                c[idx] = ac;
+            }
+        }
+        __syncthreads();
+    }
+    const int parity = static_cast<int>(seq & 1ull);
+    unsigned char* const mine = peers.area[rank];
+    __shared__ int missing;
+    if (threadIdx.x == 0) missing = 0;
+    __syncthreads();
+    const int j = static_cast<int>(threadIdx.x);
+    if (j < world) {
+        // publish this rank's root into rank j's area, then its flag
+        volatile T* slot = peer_slot<T>(peers.area[j], parity, rank, col);
+        slot[0] = h[0];
+        slot[1] = c[0];
+        peer_release(peer_flag(peers.area[j], parity, rank, col), seq);
+        // wait for rank j's root of this round in this rank's area
+        const unsigned long long* flag = peer_flag(mine, parity, j, col);
+        bool up = peer_acquire(flag) == seq;
+        if (!up) {
+            const unsigned long long t0 = peer_now();
+            while (!(up = peer_acquire(flag) == seq))
+                if (peer_now() - t0 > limit_ns) break;
+        }
+        if (!up) {
+            atomicAdd(&missing, 1);
+            atomicOr(reinterpret_cast<unsigned*>(mine), HKB_PEER_TIMEOUT);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && missing == 0) {
+        T v[kPeerRanks], vc[kPeerRanks];
+        for (int r = 0; r < world; ++r) {
+            const volatile T* slot = peer_slot<T>(mine, parity, r, col);
+            v[r] = slot[0];
+            vc[r] = slot[1];
+        }
+        for (int st = 1; st < world; st <<= 1)
+            for (int idx = 0; idx + st < world; idx += 2 * st) hk::ss::tree_join<OP>(v[idx], vc[idx], v[idx + st], vc[idx + st]);
+        out[col] = (OP == hk::ss::kSum) ? (hk::ss::finite(v[0]) ? v[0] + vc[0] : v[0]) : v[0];
+    }
+}
+
+}  // namespace
+
+struct hkb_peer {
+    int device = 0, rank = 0, world = 1, dtype = HKB_F64, ncols = 1;
+    unsigned char* mine = nullptr;
+    PeerAreas areas{};
+    bool opened[kPeerRanks] = {};
+};
+
+extern "C" {
+
+int hkb_peer_create(int device, int rank, int world, int dtype, int ncols, hkb_peer** out, void* handle_out) {
+    if (out == nullptr || handle_out == nullptr) return fail(HKB_ERR_ARGUMENT, "hkb_peer_create: null output");
+    *out = nullptr;
+    if (world < 1 || world > kPeerRanks || rank < 0 || rank >= world)
+        return fail(HKB_ERR_RANGE, "rank %d of world %d: the peer finish takes 1..%d ranks", rank, world, kPeerRanks);
+    if (dtype != HKB_F64 && dtype != HKB_F32) return fail(HKB_ERR_ARGUMENT, "unknown dtype %d", dtype);
+    if (ncols < 1 || ncols > kMaxCols) return fail(HKB_ERR_RANGE, "ncols %d is outside 1..%d", ncols, kMaxCols);
+    DeviceScope scope(device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "selecting the device");
+    hkb_peer* p = new (std::nothrow) hkb_peer();
+    if (p == nullptr) return fail(HKB_ERR_ARGUMENT, "out of host memory");
+    p->device = device;
+    p->rank = rank;
+    p->world = world;
+    p->dtype = dtype;
+    p->ncols = ncols;
+    cudaError_t err = cudaMalloc(reinterpret_cast<void**>(&p->mine), kPeerAreaBytes);
+    if (err == cudaSuccess) err = cudaMemset(p->mine, 0, kPeerAreaBytes);
+    if (err == cudaSuccess) err = cudaDeviceSynchronize();
+    cudaIpcMemHandle_t handle;
+    if (err == cudaSuccess) err = cudaIpcGetMemHandle(&handle, p->mine);
+    if (err != cudaSuccess) {
+        if (p->mine != nullptr) cudaFree(p->mine);
+        delete p;
+        return cuda_fail(err, "making the exchange area");
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == HKB_PEER_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle_out, &handle, sizeof handle);
+    p->areas.area[rank] = p->mine;
+    *out = p;
+    return HKB_OK;
+}
+
+int hkb_peer_connect(hkb_peer* peer, const void* handles) {
+    if (peer == nullptr || handles == nullptr) return fail(HKB_ERR_ARGUMENT, "hkb_peer_connect: null argument");
+    DeviceScope scope(peer->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "selecting the device");
+    for (int r = 0; r < peer->world; ++r) {
+        if (r == peer->rank || peer->opened[r]) continue;
+        cudaIpcMemHandle_t handle;
+        std::memcpy(&handle, static_cast<const char*>(handles) + static_cast<size_t>(r) * HKB_PEER_HANDLE_BYTES,
+                    sizeof handle);
+        void* ptr = nullptr;
+        const cudaError_t err = cudaIpcOpenMemHandle(&ptr, handle, cudaIpcMemLazyEnablePeerAccess);
+        if (err != cudaSuccess) return fail(HKB_ERR_CUDA, "opening rank %d's exchange area: %s (%s)", r,
+                                            cudaGetErrorString(err), cudaGetErrorName(err));
+        peer->areas.area[r] = static_cast<unsigned char*>(ptr);
+        peer->opened[r] = true;
+    }
+    return HKB_OK;
+}
+
+int hkb_peer_finish(hkb_peer* peer, int op, void* leaf_hi, void* leaf_comp, int64_t leaves, void* out,
+                    uint64_t seq, uint64_t timeout_ns, void* stream) {
+    if (peer == nullptr || leaf_hi == nullptr || leaf_comp == nullptr || out == nullptr)
+        return fail(HKB_ERR_ARGUMENT, "hkb_peer_finish: null argument");
+    int status = check_cells(op, peer->dtype, peer->ncols);
+    if (status != HKB_OK) return status;
+    if (leaves < 1) return fail(HKB_ERR_RANGE, "a tree needs at least one leaf");
+    if (seq == 0) return fail(HKB_ERR_ARGUMENT, "hkb_peer_finish: rounds are numbered from 1");
+    for (int r = 0; r < peer->world; ++r)
+        if (peer->areas.area[r] == nullptr)
+            return fail(HKB_ERR_ARGUMENT, "rank %d's exchange area is not connected (hkb_peer_connect)", r);
+    DeviceScope scope(peer->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "selecting the device");
+    const unsigned long long limit = timeout_ns ? timeout_ns : kPeerWaitNs;
+    auto s = static_cast<cudaStream_t>(stream);
+    const dim3 grid(static_cast<unsigned>(peer->ncols));
+    const long long n = leaves;
+    const int rk = peer->rank, w = peer->world;
+    if (peer->dtype == HKB_F64) {
+        double* h = static_cast<double*>(leaf_hi);
+        double* c = static_cast<double*>(leaf_comp);
+        double* o = static_cast<double*>(out);
+        switch (op) {
+            case HKB_OP_SUM: peer_finish_kernel<double, hk::ss::kSum><<<grid, 1024, 0, s>>>(h, c, n, peer->areas, rk, w, seq, limit, o); break;
+            case HKB_OP_MAX: peer_finish_kernel<double, hk::ss::kMax><<<grid, 1024, 0, s>>>(h, c, n, peer->areas, rk, w, seq, limit, o); break;
+            default: peer_finish_kernel<double, hk::ss::kMin><<<grid, 1024, 0, s>>>(h, c, n, peer->areas, rk, w, seq, limit, o); break;
+        }
+    } else {
+        float* h = static_cast<float*>(leaf_hi);
+        float* c = static_cast<float*>(leaf_comp);
+        float* o = static_cast<float*>(out);
+        switch (op) {
+            case HKB_OP_SUM: peer_finish_kernel<float, hk::ss::kSum><<<grid, 1024, 0, s>>>(h, c, n, peer->areas, rk, w, seq, limit, o); break;
+            case HKB_OP_MAX: peer_finish_kernel<float, hk::ss::kMax><<<grid, 1024, 0, s>>>(h, c, n, peer->areas, rk, w, seq, limit, o); break;
+            default: peer_finish_kernel<float, hk::ss::kMin><<<grid, 1024, 0, s>>>(h, c, n, peer->areas, rk, w, seq, limit, o); break;
+        }
+    }
+    HKB_CUDA(cudaGetLastError(), "launching the peer finish");
+    return HKB_OK;
+}
+
+int hkb_peer_status(hkb_peer* peer, unsigned* flags) {
+    if (peer == nullptr || flags == nullptr) return fail(HKB_ERR_ARGUMENT, "hkb_peer_status: null argument");
+    *flags = 0;
+    DeviceScope scope(peer->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "selecting the device");
+    HKB_CUDA(cudaMemcpy(flags, peer->mine, sizeof(unsigned), cudaMemcpyDeviceToHost), "reading the exchange status");
+    HKB_CUDA(cudaMemset(peer->mine, 0, sizeof(unsigned)), "clearing the exchange status");
+    return HKB_OK;
+}
+
+void hkb_peer_free(hkb_peer* peer) {
+    if (peer == nullptr) return;
+    DeviceScope scope(peer->device);
+    for (int r = 0; r < kPeerRanks; ++r)
+        if (peer->opened[r]) cudaIpcCloseMemHandle(peer->areas.area[r]);
+    if (peer->mine != nullptr) cudaFree(peer->mine);
+    delete peer;
+}
+
+}  // extern "C"

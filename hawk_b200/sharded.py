@@ -11,8 +11,9 @@ exchange is for cells (sample sums such as Param gradients):
 2. when every rank holds the same power-of-two number of leaves, each folds
    its own leaves to one (hi, comp) pair per column (an aligned subtree of the
    one-device tree), the ranks all-gather the pairs and every rank runs the
-   last levels over them; otherwise the ranks all-gather their leaf partials
-   (NCCL over NVLink on B200s)
+   last levels over them -- with a ``PeerFinish``, all of it in one launch that
+   stores each rank's pairs into every rank's memory over NVLink; otherwise
+   the ranks all-gather their leaf partials (NCCL over NVLink on B200s)
 3. and every rank folds all leaves in rank order with the same pairwise tree
    (``hkb_cells_tree``).
 
@@ -75,8 +76,71 @@ def aligned(counts) -> bool:
     return first > 0 and (first & (first - 1)) == 0 and all(c == first for c in counts)
 
 
+class PeerFinish:
+    """The last step of ``finish_subtrees`` over NVLink peer memory in one
+    launch per call (``hkb_peer_finish``), in place of the NCCL all-gather
+    between two tree launches: each rank folds its leaves to one root per
+    column, stores the root into every rank's exchange area (plain peer stores
+    through CUDA IPC mappings) with a round flag, waits (bounded, two seconds)
+    for every rank's flag of the round, and folds the roots in rank order --
+    the same tree, bit for bit.
+
+    Made collectively (every rank of ``group``, once): each rank allocates its
+    area on ``device`` and the ranks exchange the areas' IPC handles
+    (``all_gather_object``).  Every call after that is collective too, in the
+    same order on every rank (rounds are numbered by the call).  A wait that
+    ran out leaves the cells unwritten and is reported by ``check``;
+    ``close`` (collective: a barrier first, so no rank still stores into an
+    area) frees the area."""
+
+    def __init__(self, mode: str, cols: int, device: int, group=None) -> None:
+        import torch.distributed as dist
+
+        from . import abi
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.mode, self.cols = mode, cols
+        self.area = abi.PeerArea(device, self.rank, self.world, mode, cols)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, self.area.handle, group=group)
+        self.area.connect(handles)
+        self.seq = 0
+
+    def finish(self, op: str, leaf_hi, leaf_comp, leaves: int, values, stream: int = 0,
+               timeout_ns: int = 0) -> None:
+        """The cells of every column over every rank's ``leaves`` partials of
+        ``leaf_hi`` / ``leaf_comp`` (``(cols, leaves)``, folded in place) into
+        ``values``, on ``stream``."""
+        from .errors import HawkError
+
+        if leaf_hi.shape[0] < self.cols or values.numel() < self.cols:
+            raise HawkError(f"the peer finish was made for {self.cols} columns")
+        self.seq += 1
+        self.area.finish(op, leaf_hi.data_ptr(), leaf_comp.data_ptr(), leaves, values.data_ptr(), self.seq,
+                         timeout_ns, stream)
+
+    def check(self) -> None:
+        """Read (synchronising) and clear the area's status word; a wait that
+        ran out raises ``HawkError``."""
+        from . import abi
+        from .errors import HawkError
+
+        flags = self.area.status()
+        if flags & abi.PEER_TIMEOUT:
+            raise HawkError(f"rank {self.rank}: a peer finish waited past its limit for another rank's root "
+                            "(the cells of that call were not written)")
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        dist.barrier(self.group)
+        self.area.free()
+
+
 def finish_subtrees(op: str, mode: str, cols: int, leaf_hi, leaf_comp, leaves: int, values, group=None,
-                    stream: int = 0, pack=None, gathered=None) -> None:
+                    stream: int = 0, pack=None, gathered=None, peer: PeerFinish | None = None) -> None:
     """The cells of ``cols`` columns from every rank's ``leaves`` partials
     (``(cols, leaves)`` tensors; ``leaves`` a power of two, the same on every
     rank), into ``values``: this rank's tree over its own leaves to one (hi,
@@ -85,12 +149,16 @@ def finish_subtrees(op: str, mode: str, cols: int, leaf_hi, leaf_comp, leaves: i
     The pairwise levels of the one-device tree over ``world * leaves`` leaves
     join each rank's leaves among themselves first, so this is the same tree,
     bit for bit (hawk/_cells.py:108-119).  ``pack`` ``(2, cols)`` and
-    ``gathered`` ``(world, 2, cols)`` may be passed preallocated."""
+    ``gathered`` ``(world, 2, cols)`` may be passed preallocated.  With
+    ``peer`` the three steps are one ``PeerFinish`` launch over peer memory."""
     import torch
     import torch.distributed as dist
 
     from . import abi
 
+    if peer is not None:
+        peer.finish(op, leaf_hi, leaf_comp, leaves, values, stream)
+        return
     world = dist.get_world_size(group)
     if pack is None:
         pack = torch.empty((2, cols), dtype=leaf_hi.dtype, device=leaf_hi.device)
@@ -111,7 +179,7 @@ def shard_counts(total_samples: int, world: int) -> list:
 
 
 def run_cells(kernel, *, group=None, base: int = 0, count: int | None = None, n_samples: int | None = None,
-              total_samples: int | None = None, stream=None, **arrays) -> None:
+              total_samples: int | None = None, stream=None, peer: PeerFinish | None = None, **arrays) -> None:
     """``hawk_b200.runtime.run`` of a kernel with cells over this rank's shard,
     its cells summed over the samples of every rank of ``group``.
 
@@ -128,7 +196,9 @@ def run_cells(kernel, *, group=None, base: int = 0, count: int | None = None, n_
 
     Every launch and every collective is ordered on ``stream`` (the current
     stream when None): the partials are gathered after the kernels that write
-    them, and the final tree runs after the gather lands."""
+    them, and the final tree runs after the gather lands.  ``peer``: a
+    ``PeerFinish`` of this group for the kernel's columns, used where every
+    rank holds the same power-of-two leaf count (else the gather runs)."""
     import torch
     import torch.distributed as dist
 
@@ -161,7 +231,7 @@ def run_cells(kernel, *, group=None, base: int = 0, count: int | None = None, n_
                 if aligned(counts):
                     op = kernel.sums[0]["op"] if kernel.sums else "sum"
                     finish_subtrees(op, kernel.element, cols, state["leaf_hi"], state["leaf_comp"], leaves,
-                                    state["values"], group, runtime._stream(stream, kernel.device))
+                                    state["values"], group, runtime._stream(stream, kernel.device), peer=peer)
                     kernel.write_cells(state["values"], outputs, stream)
                     return
                 width = max(max(counts), 1)

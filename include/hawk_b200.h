@@ -210,6 +210,43 @@ int hkb_cells_finish(int op, int dtype, int ncols, const void* const* hi, const 
 int hkb_cells_finish_noalloc(int op, int dtype, int ncols, const void* const* hi, const void* const* comp,
                              int64_t rows, void* out, void* stream);
 
+/* ------------------------------------- cells across GPUs over peer memory */
+
+/* The last step of a sharded finish in one launch over NVLink, replacing an
+ * NCCL all-gather of the ranks' subtree roots (no counterpart in the
+ * reference: its ranks finish on the host, tests/mpi/test_hawk_rank_oracle.py:
+ * 94-168).  Each rank holds the same power-of-two number of leaves of every
+ * column (an aligned subtree of the one-device tree, as for
+ * hkb_cells_tree_ex).  One rank's exchange area lives in its own device
+ * memory: for each of two round parities, every rank's (hi, comp) root of
+ * every column and a round flag.  hkb_peer_finish folds this rank's leaves to
+ * its root (the pairwise levels of hkb_cells_tree), stores the root into every
+ * rank's area with plain peer stores, raises its flag there, waits until every
+ * rank's flag of this round is up in its own area, and runs the last pairwise
+ * levels over the ranks' roots in rank order: the same tree, bit for bit, as
+ * one hkb_cells_tree over all ranks' leaves.
+ *
+ * hkb_peer_create allocates this rank's area on `device` (zeroed) and writes
+ * its CUDA IPC handle (HKB_PEER_HANDLE_BYTES bytes) to handle_out;
+ * hkb_peer_connect opens the other ranks' handles (`handles`: world handles in
+ * rank order; this rank's own entry is not read).  `seq` numbers the rounds:
+ * 1, 2, 3, ... the same on every rank.  Every wait is bounded by timeout_ns of
+ * the GPU's global timer (0: two seconds); a wait that runs out leaves `out`
+ * untouched and sets HKB_PEER_TIMEOUT in the area's status word, which
+ * hkb_peer_status reads and clears (a synchronising read).  Before
+ * hkb_peer_free, every rank must be past its last hkb_peer_finish (a host
+ * barrier): a peer still storing into a freed area would write freed memory. */
+#define HKB_PEER_HANDLE_BYTES 64
+#define HKB_PEER_MAX_RANKS 8
+#define HKB_PEER_TIMEOUT 1u
+typedef struct hkb_peer hkb_peer;
+int hkb_peer_create(int device, int rank, int world, int dtype, int ncols, hkb_peer** out, void* handle_out);
+int hkb_peer_connect(hkb_peer* peer, const void* handles);
+int hkb_peer_finish(hkb_peer* peer, int op, void* leaf_hi, void* leaf_comp, int64_t leaves, void* out,
+                    uint64_t seq, uint64_t timeout_ns, void* stream);
+int hkb_peer_status(hkb_peer* peer, unsigned* flags);
+void hkb_peer_free(hkb_peer* peer);
+
 #ifdef __cplusplus
 }
 #endif

@@ -97,6 +97,26 @@ def test_the_static_scratch_cap_is_the_headers():
     assert abi.LEAF_ROWS == int(rows)
 
 
+def test_the_peer_finish_constants_are_the_headers_and_bad_shapes_are_refused():
+    """The binding's handle size, rank limit and timeout bit are the header's;
+    hkb_peer_create refuses a world or column count outside its area before it
+    touches a device, and hkb_peer_finish a null area."""
+    text = (REPO / "include" / "hawk_b200.h").read_text()
+    for name, value in (("HKB_PEER_HANDLE_BYTES", abi.PEER_HANDLE_BYTES), ("HKB_PEER_MAX_RANKS", abi.PEER_MAX_RANKS),
+                        ("HKB_PEER_TIMEOUT", abi.PEER_TIMEOUT)):
+        (got,) = re.findall(rf"#define\s+{name}\s+(\d+)u?", text)
+        assert value == int(got), name
+    lib = abi.lib()
+    out = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(abi.PEER_HANDLE_BYTES)
+    assert lib.hkb_peer_create(0, 0, abi.PEER_MAX_RANKS + 1, 0, 3, ctypes.byref(out), handle) == 5
+    assert "1..8 ranks" in lib.hkb_last_error().decode()
+    assert lib.hkb_peer_create(0, 2, 2, 0, 3, ctypes.byref(out), handle) == 5
+    assert lib.hkb_peer_create(0, 0, 2, 0, 9, ctypes.byref(out), handle) == 5
+    assert out.value is None
+    assert lib.hkb_peer_finish(None, 0, None, None, 1, None, 1, 0, None) == 1
+
+
 def test_wait_errors_name_what_ran_out_and_a_drain_stops_the_unit():
     """The bits of a unit's error word (hk/stage.cuh kErrFullWait, kErrEmptyWait,
     kErrDrain) as the runtime reports them; a drain that ran out is fatal to
