@@ -88,6 +88,8 @@ extern "C" __global__ void __launch_bounds__(128) team_chol_512_2(
     }
 }
 
+extern "C" __device__ const unsigned int hk_team_threads__team_chol_512_3 = 256u;
+extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_chol_512_3 = 0u;
 extern "C" __global__ void __launch_bounds__(256) team_chol_512_3(
     hk::abi::ScalarHandle p_mut_info,
     hk::abi::GRefMirror p_mut_x,
@@ -105,14 +107,13 @@ extern "C" __global__ void __launch_bounds__(256) team_chol_512_3(
     (void)lut_tm0_info;
     const hk::ScalarIn<Real> lut_tm0_x0(p_lut_tm0_x0);
     (void)lut_tm0_x0;
-    for (long long hawk_flat = hk::lane_first(); hawk_flat < count; hawk_flat += hk::lane_step()) {
-        const long long hawk_i = base + hawk_flat;
-        const hk::SampleIndex i{hawk_i};
-        (void)hawk_i;
-        (void)nSamples;
-        const hk::Slice<Real, 512> hawk_la0{lut_tm0_x0.data() + static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 512};
-        const auto t2 = hawk_la0;
-        mut_x[i] = t2;
-        mut_info[i] = lut_tm0_info[hk::SampleIndex::make(static_cast<std::size_t>(static_cast<Int>(hawk_i)))].eval();
+    __shared__ __align__(16) unsigned char hk_tile[32 * 33 * 8];
+    const long long hk_lane_tiles = (count + 31) / 32;
+    const long long hk_end0 = hk_lane_tiles * 16;
+    const long long hk_end1 = hk_end0 + hk_lane_tiles * 1;
+    for (long long hk_t = blockIdx.x; hk_t < hk_end1; hk_t += gridDim.x) {
+        if (hk_t < hk_end0) hk::linalg::team::copyOutTile(lut_tm0_x0.data(), mut_x.data(), mut_x.pitch, 512LL, base, count, hk_t, hk_tile);
+        else hk::linalg::team::copyOutTile(lut_tm0_info.data(), mut_info.data(), 0ull, 1LL, base, count, hk_t - hk_end0, hk_tile);
     }
+    (void)nSamples;
 }

@@ -142,6 +142,8 @@ extern "C" __global__ void __launch_bounds__(128) team_lu_128_2(
     }
 }
 
+extern "C" __device__ const unsigned int hk_team_threads__team_lu_128_3 = 256u;
+extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__team_lu_128_3 = 0u;
 extern "C" __global__ void __launch_bounds__(256) team_lu_128_3(
     hk::abi::GRefMirror p_mut_X,
     hk::abi::ScalarHandle p_mut_det,
@@ -171,18 +173,17 @@ extern "C" __global__ void __launch_bounds__(256) team_lu_128_3(
     (void)lut_tm0_x1;
     const hk::ScalarIn<Real> lut_tm1_d0(p_lut_tm1_d0);
     (void)lut_tm1_d0;
-    for (long long hawk_flat = hk::lane_first(); hawk_flat < count; hawk_flat += hk::lane_step()) {
-        const long long hawk_i = base + hawk_flat;
-        const hk::SampleIndex i{hawk_i};
-        (void)hawk_i;
-        (void)nSamples;
-        const hk::Slice<Real, 128> hawk_la0{lut_tm0_x0.data() + static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 128};
-        const auto t2 = hawk_la0;
-        mut_x[i] = t2;
-        const hk::Slice<Real, 128, 2> hawk_la1{lut_tm0_x1.data() + static_cast<std::size_t>(static_cast<Int>(hawk_i)) * 256};
-        const auto t5 = hawk_la1;
-        mut_X[i] = t5;
-        mut_det[i] = lut_tm1_d0[hk::SampleIndex::make(static_cast<std::size_t>(static_cast<Int>(hawk_i)))].eval();
-        mut_info[i] = lut_tm0_info[hk::SampleIndex::make(static_cast<std::size_t>(static_cast<Int>(hawk_i)))].eval();
+    __shared__ __align__(16) unsigned char hk_tile[32 * 33 * 8];
+    const long long hk_lane_tiles = (count + 31) / 32;
+    const long long hk_end0 = hk_lane_tiles * 4;
+    const long long hk_end1 = hk_end0 + hk_lane_tiles * 8;
+    const long long hk_end2 = hk_end1 + hk_lane_tiles * 1;
+    const long long hk_end3 = hk_end2 + hk_lane_tiles * 1;
+    for (long long hk_t = blockIdx.x; hk_t < hk_end3; hk_t += gridDim.x) {
+        if (hk_t < hk_end0) hk::linalg::team::copyOutTile(lut_tm0_x0.data(), mut_x.data(), mut_x.pitch, 128LL, base, count, hk_t, hk_tile);
+        else if (hk_t < hk_end1) hk::linalg::team::copyOutTile(lut_tm0_x1.data(), mut_X.data(), mut_X.pitch, 256LL, base, count, hk_t - hk_end0, hk_tile);
+        else if (hk_t < hk_end2) hk::linalg::team::copyOutTile(lut_tm1_d0.data(), mut_det.data(), 0ull, 1LL, base, count, hk_t - hk_end1, hk_tile);
+        else hk::linalg::team::copyOutTile(lut_tm0_info.data(), mut_info.data(), 0ull, 1LL, base, count, hk_t - hk_end2, hk_tile);
     }
+    (void)nSamples;
 }

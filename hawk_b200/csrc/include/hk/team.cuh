@@ -1133,6 +1133,33 @@ HK_FI void scatterChunk(const Team& tm, long long lane, long long count, long lo
     }
     tm.sync();
 }
+
+// A reader stage's copy of a lane-major scratch plane (lane l's `comps`
+// components contiguous at src[l * comps]) into a component-major output
+// plane (component k of sample l at dst[k * pitch + l]), for the lanes
+// [base, base + count): tile `tile` of the (lane tiles x component tiles)
+// grid, 32 x 32 elements staged through `smem` (32 x 33 elements of T), so
+// both the reads (one lane's 32 components) and the writes (one component of
+// 32 lanes) are 32 consecutive elements a warp instruction.  Every thread of
+// the block calls it for the same tile.
+template <class T>
+__device__ __forceinline__ void copyOutTile(const T* src, T* dst, unsigned long long pitch, long long comps,
+                                            long long base, long long count, long long tile, unsigned char* smem) {
+    T (*t)[33] = reinterpret_cast<T (*)[33]>(smem);
+    const long long ktiles = (comps + 31) / 32;
+    const long long lt = tile / ktiles, kt = tile - lt * ktiles;
+    const int tx = static_cast<int>(threadIdx.x & 31u), rows = static_cast<int>(blockDim.x >> 5);
+    for (int r = static_cast<int>(threadIdx.x >> 5); r < 32; r += rows) {
+        const long long lane = lt * 32 + r, k = kt * 32 + tx;
+        if (lane < count && k < comps) t[r][tx] = src[static_cast<std::size_t>(base + lane) * comps + k];
+    }
+    __syncthreads();
+    for (int r = static_cast<int>(threadIdx.x >> 5); r < 32; r += rows) {
+        const long long k = kt * 32 + r, lane = lt * 32 + tx;
+        if (lane < count && k < comps) dst[static_cast<std::size_t>(k) * pitch + base + lane] = t[tx][r];
+    }
+    __syncthreads();
+}
 #endif
 
 }  // namespace team

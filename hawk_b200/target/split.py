@@ -23,6 +23,7 @@ planes (``team_planes``) for the runtime's split runner.
 from __future__ import annotations
 
 import hashlib
+import re
 
 from ..errors import HawkError
 from .assemble import MODES, Unit, prelude_lines, refuse_unbuilt, render_unit
@@ -160,6 +161,14 @@ def render_split_unit(kernel, name: str, mode: str = "float64"):
             if unit.notes.get("persist") or unit.notes.get("folds"):
                 raise HawkError(f"{name!r}: stage {member.name!r} commits into a compensated scatter target, "
                                 "which a split kernel's stage does not build yet")
+            copies = _reader_copies(unit, walk) if not unit.sums else None
+            if copies is not None:
+                parts += _reader_entry(member.name, walk, copies)
+                stages.append({"entry": member.name, "kind": "team", "threads": READER_THREADS, "dynamic_smem": 0,
+                               "slots": _slot_records(walk), "sample_sums": [],
+                               "cells_in": list(record.get("cells_in") or ()), "cells_out": [], "grid": "lanes",
+                               "keyed": None, "groups": None, "of": None, "status": None, "ops": ["copy_out"]})
+                continue
             parts.append(unit.entries)
             stages.append({"entry": member.name, "kind": unit.frame, "threads": None, "dynamic_smem": 0,
                            "slots": _slot_records(walk), "lane_refill": unit.notes.get("lane_refill", False),
@@ -280,6 +289,99 @@ def _scatter_chunk_body(step) -> str:
         f"            hk::linalg::team::scatterChunk<Real, {SCATTER_WARPS}>(hawk_tm, hawk_lane, count, nSamples, "
         f"{int(step.n)}, {k}.data(), {v}.data(), {part}.data(), const_cast<std::int32_t*>({status}.data()));",
         "        }"])
+
+
+#: Threads a block of a reader stage copies its tiles with.
+READER_THREADS = 256
+
+_SLICE = re.compile(r"^const hk::Slice<Real, (\d+)(?:, (\d+))?> (hawk_la\d+)\{(\w+)\.data\(\) \+ "
+                    r"static_cast<std::size_t>\(static_cast<Int>\(hawk_i\)\) \* (\d+)\};$")
+_ALIAS = re.compile(r"^const auto (t\d+) = (hawk_la\d+);$")
+_STORE = re.compile(r"^(\w+)\[i\] = (t\d+);$")
+_SCALAR = re.compile(r"^(\w+)\[i\] = (\w+)\[hk::SampleIndex::make\(static_cast<std::size_t>\("
+                     r"static_cast<Int>\(hawk_i\)\)\)\]\.eval\(\);$")
+
+
+def _reader_copies(unit, walk) -> list | None:
+    """A per-lane stage that only copies team scratch into the kernel's outputs
+    (each output the lane's slice of a lane-major scratch plane, or one
+    element of it): ``[(output binding, scratch binding, components), ...]``,
+    else None.  The reference emits such a stage after a team stage (its
+    readers, hawk/emit/team.py): one thread a lane, each copying its lane's
+    whole slice -- for a 128 x 128 factor 16384 elements a thread, and only as
+    many threads as lanes."""
+    from hawk.emit.spelling import binding_name
+
+    comps = {}
+    for role, name in walk.arg_spec:
+        n = 1
+        for e in walk.slot_types[(role, name)].shape:
+            n *= int(e)
+        comps[binding_name(role, name)] = (role, n)
+    slices, temps, out = {}, {}, []
+    for raw in unit.body.split("\n"):
+        line = raw.strip()
+        if not line:
+            continue
+        m = _SLICE.match(line)
+        if m:
+            rows, cols, la, src, size = m.groups()
+            if int(rows) * int(cols or 1) != int(size):
+                return None
+            slices[la] = (src, int(size))
+            continue
+        m = _ALIAS.match(line)
+        if m and m.group(2) in slices:
+            temps[m.group(1)] = slices[m.group(2)]
+            continue
+        m = _STORE.match(line)
+        if m and m.group(2) in temps:
+            src, size = temps[m.group(2)]
+            if comps.get(m.group(1), (None, 0))[1] != size:
+                return None
+            out.append((m.group(1), src, size))
+            continue
+        m = _SCALAR.match(line)
+        if m and comps.get(m.group(1), (None, 0))[1] == 1 and m.group(2) in comps:
+            out.append((m.group(1), m.group(2), 1))
+            continue
+        return None
+    return out or None
+
+
+def _reader_entry(name: str, walk, copies: list) -> list:
+    """The reader stage as a team-geometry entry: every block copies 32 x 32
+    tiles (``hk::linalg::team::copyOutTile``) of every (output, scratch) pair,
+    grid-striding over all pairs' tiles, so the copy runs with 8 warps a 256
+    lanes' worth of blocks and reads and writes 32 consecutive elements a warp
+    instruction.  Each element is copied unchanged, so the outputs are those
+    of the reference's per-lane copy."""
+    bounds = []
+    lines = ["    __shared__ __align__(16) unsigned char hk_tile[32 * 33 * 8];",
+             "    const long long hk_lane_tiles = (count + 31) / 32;"]
+    for j, (_dst, _src, size) in enumerate(copies):
+        prev = f"hk_end{j - 1} + " if j else ""
+        lines.append(f"    const long long hk_end{j} = {prev}hk_lane_tiles * {-(-size // 32)};")
+        bounds.append(f"hk_end{j}")
+    lines.append(f"    for (long long hk_t = blockIdx.x; hk_t < {bounds[-1]}; hk_t += gridDim.x) {{")
+    for j, (dst, src, size) in enumerate(copies):
+        pitch = f"{dst}.pitch" if size > 1 else "0ull"
+        start = f"hk_t - hk_end{j - 1}" if j else "hk_t"
+        cond = f"if (hk_t < hk_end{j})" if j == 0 else (f"else if (hk_t < hk_end{j})" if j < len(copies) - 1
+                                                          else "else")
+        lines.append(f"        {cond} hk::linalg::team::copyOutTile({src}.data(), {dst}.data(), {pitch}, {size}LL, "
+                     f"base, count, {start}, hk_tile);")
+    lines += ["    }", "    (void)nSamples;"]
+    return [
+        f'extern "C" __device__ const unsigned int hk_team_threads__{name} = {READER_THREADS}u;',
+        f'extern "C" __device__ const unsigned int hk_dynamic_smem_bytes__{name} = 0u;',
+        B200.entry_signature(walk, name, threads=READER_THREADS),
+        "{",
+        B200.unpack(walk),
+        *lines,
+        "}",
+        "",
+    ]
 
 
 def _slot_records(walk) -> list:
