@@ -1384,7 +1384,8 @@ def main() -> int:
             "config": {"workload": "poly_loss fwd + Param-gradient VJP (c2: r=(a x^3+b x+c-t)^2, "
                                    "grads of a,b,c summed over all samples)",
                        "samples_per_gpu": args.n, "mode": args.mode, "parallelism": f"samples x{world}",
-                       "l2": "inputs 1.5 GB/GPU > 126 MB L2, no flush"},
+                       "l2": "inputs 1.5 GB/GPU > 126 MB L2, no flush",
+                       **({"cells_finish": res["finish"]} if "finish" in res else {})},
             "roofline": res["roofline"], "e2e": res["e2e"], "gpu_launches": res["gpu_launches"],
             "clocks": res["clocks"], "cpu_baseline": cpu, "parity": res["parity"],
             "kernels_ms": res["kernels_ms"], "fwd_gbs": res["fwd_gbs"], "vjp_gbs": res["vjp_gbs"],
