@@ -891,22 +891,25 @@ extern "C" int hkb_cells_finish_noalloc(int op, int dtype, int ncols, const void
 // ------------------------------------------- cells across GPUs, peer memory
 //
 // The last step of a sharded finish without a collective library: every rank
-// folds its leaves to one (hi, comp) root per column, stores the root into
+// folds its leaves to one (hi, comp) root per column and stores the root into
 // every rank's exchange area over NVLink (plain peer stores through CUDA IPC
-// mappings), raises a round flag beside it (release at system scope), waits
-// (bounded) until every rank's flag of the round is up in its own area
-// (acquire at system scope), and folds the ranks' roots in rank order.  The
-// area keeps two round parities, so a rank one round ahead writes the other
-// parity's slots and never overwrites a root its peer is still to read: a rank
-// can only start round s + 2 after every rank has published round s + 1, which
-// each does only after its round s finished.
+// mappings), each 32-bit half of a value in its own 8-byte word beside the
+// round's tag -- a word is written and read whole, so a reader that sees the
+// round's tag in a word has that word's half, and no fence or flag is needed
+// (the low-latency form collective libraries use for small messages).  Each
+// rank waits (bounded) until every rank's words of the round carry the tag in
+// its own area, and folds the roots in rank order.  The area keeps two round
+// parities, so a rank one round ahead writes the other parity's words and never
+// overwrites a root its peer is still to read: a rank can only start round
+// s + 2 after every rank has published round s + 1, which each does only after
+// its round s finished.
 
 namespace {
 
 constexpr int kPeerRanks = HKB_PEER_MAX_RANKS;
-constexpr size_t kPeerFlagsAt = 256;                                             // after the status word
-constexpr size_t kPeerSlotsAt = kPeerFlagsAt + 2 * kPeerRanks * kMaxCols * 8;   // after the flags
-constexpr size_t kPeerAreaBytes = kPeerSlotsAt + 2 * kPeerRanks * kMaxCols * 2 * 8 + 256;
+constexpr int kPeerWords = 4;                                   // hi's two halves, then comp's
+constexpr size_t kPeerWordsAt = 256;                            // after the status word
+constexpr size_t kPeerAreaBytes = kPeerWordsAt + 2 * kPeerRanks * kMaxCols * kPeerWords * 8 + 256;
 constexpr unsigned long long kPeerWaitNs = 2000000000ull;
 
 struct PeerAreas {
@@ -919,24 +922,33 @@ __device__ __forceinline__ unsigned long long peer_now() {
     return t;
 }
 
-__device__ __forceinline__ void peer_release(unsigned long long* flag, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(v) : "memory");
+__device__ __forceinline__ unsigned long long* peer_words(unsigned char* area, int parity, int rank, int col) {
+    return reinterpret_cast<unsigned long long*>(area + kPeerWordsAt) +
+           ((parity * kPeerRanks + rank) * kMaxCols + col) * kPeerWords;
 }
 
-__device__ __forceinline__ unsigned long long peer_acquire(const unsigned long long* flag) {
+__device__ __forceinline__ void peer_put(unsigned long long* word, unsigned half, unsigned tag) {
+    const unsigned long long v = (static_cast<unsigned long long>(tag) << 32) | half;
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(word), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long peer_get(const unsigned long long* word) {
     unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(word) : "memory");
     return v;
 }
 
-__device__ __forceinline__ unsigned long long* peer_flag(unsigned char* area, int parity, int rank, int col) {
-    return reinterpret_cast<unsigned long long*>(area + kPeerFlagsAt) + (parity * kPeerRanks + rank) * kMaxCols + col;
+// A value as its 32-bit halves (one for a float) and back.
+__device__ __forceinline__ void peer_halves(double x, unsigned* h) {
+    const unsigned long long b = static_cast<unsigned long long>(__double_as_longlong(x));
+    h[0] = static_cast<unsigned>(b);
+    h[1] = static_cast<unsigned>(b >> 32);
 }
-
-template <class T>
-__device__ __forceinline__ T* peer_slot(unsigned char* area, int parity, int rank, int col) {
-    return reinterpret_cast<T*>(area + kPeerSlotsAt) + ((parity * kPeerRanks + rank) * kMaxCols + col) * 2;
+__device__ __forceinline__ void peer_halves(float x, unsigned* h) { h[0] = __float_as_uint(x); }
+__device__ __forceinline__ void peer_join(const unsigned* h, double& x) {
+    x = __longlong_as_double(static_cast<long long>((static_cast<unsigned long long>(h[1]) << 32) | h[0]));
 }
+__device__ __forceinline__ void peer_join(const unsigned* h, float& x) { x = __uint_as_float(h[0]); }
 
 // One block per column: this rank's pairwise levels over its leaves (in place,
 // as tree_kernel), the root published to every rank, then the ranks' roots
@@ -946,6 +958,7 @@ template <class T, int OP>
 __global__ void __launch_bounds__(1024) peer_finish_kernel(T* leaf_hi, T* leaf_comp, long long leaves, PeerAreas peers,
                                                           int rank, int world, unsigned long long seq,
                                                           unsigned long long limit_ns, T* out) {
+    constexpr int H = sizeof(T) / 4;           // halves a value
     const int col = blockIdx.x;
     T* h = leaf_hi + col * leaves;
     T* c = leaf_comp + col * leaves;
@@ -962,26 +975,44 @@ __global__ void __launch_bounds__(1024) peer_finish_kernel(T* leaf_hi, T* leaf_c
         __syncthreads();
     }
     const int parity = static_cast<int>(seq & 1ull);
+    const unsigned tag = static_cast<unsigned>(seq);
     unsigned char* const mine = peers.area[rank];
     __shared__ int missing;
+    __shared__ T roots[kPeerRanks], comps[kPeerRanks];
     if (threadIdx.x == 0) missing = 0;
     __syncthreads();
     const int j = static_cast<int>(threadIdx.x);
     if (j < world) {
-        // publish this rank's root into rank j's area, then its flag
-        volatile T* slot = peer_slot<T>(peers.area[j], parity, rank, col);
-        slot[0] = h[0];
-        slot[1] = c[0];
-        peer_release(peer_flag(peers.area[j], parity, rank, col), seq);
-        // wait for rank j's root of this round in this rank's area
-        const unsigned long long* flag = peer_flag(mine, parity, j, col);
-        bool up = peer_acquire(flag) == seq;
-        if (!up) {
-            const unsigned long long t0 = peer_now();
-            while (!(up = peer_acquire(flag) == seq))
-                if (peer_now() - t0 > limit_ns) break;
+        // publish this rank's root into rank j's area: every half with the tag
+        unsigned mh[2] = {0u, 0u}, mc[2] = {0u, 0u};
+        peer_halves(h[0], mh);
+        peer_halves(c[0], mc);
+        unsigned long long* w = peer_words(peers.area[j], parity, rank, col);
+        for (int k = 0; k < H; ++k) {
+            peer_put(w + k, mh[k], tag);
+            peer_put(w + 2 + k, mc[k], tag);
         }
-        if (!up) {
+        // rank j's root of this round from this rank's area
+        const unsigned long long* r = peer_words(mine, parity, j, col);
+        unsigned rh[2] = {0u, 0u}, rc[2] = {0u, 0u};
+        bool up = false;
+        unsigned long long t0 = 0;
+        for (bool first = true;; first = false) {
+            up = true;
+            for (int k = 0; k < H; ++k) {
+                const unsigned long long a = peer_get(r + k), b = peer_get(r + 2 + k);
+                up = up && static_cast<unsigned>(a >> 32) == tag && static_cast<unsigned>(b >> 32) == tag;
+                rh[k] = static_cast<unsigned>(a);
+                rc[k] = static_cast<unsigned>(b);
+            }
+            if (up) break;
+            if (first) t0 = peer_now();
+            else if (peer_now() - t0 > limit_ns) break;
+        }
+        if (up) {
+            peer_join(rh, roots[j]);
+            peer_join(rc, comps[j]);
+        } else {
             atomicAdd(&missing, 1);
             atomicOr(reinterpret_cast<unsigned*>(mine), HKB_PEER_TIMEOUT);
         }
@@ -990,9 +1021,8 @@ __global__ void __launch_bounds__(1024) peer_finish_kernel(T* leaf_hi, T* leaf_c
     if (threadIdx.x == 0 && missing == 0) {
         T v[kPeerRanks], vc[kPeerRanks];
         for (int r = 0; r < world; ++r) {
-            const volatile T* slot = peer_slot<T>(mine, parity, r, col);
-            v[r] = slot[0];
-            vc[r] = slot[1];
+            v[r] = roots[r];
+            vc[r] = comps[r];
         }
         for (int st = 1; st < world; st <<= 1)
             for (int idx = 0; idx + st < world; idx += 2 * st) hk::ss::tree_join<OP>(v[idx], vc[idx], v[idx + st], vc[idx + st]);
@@ -1070,7 +1100,9 @@ int hkb_peer_finish(hkb_peer* peer, int op, void* leaf_hi, void* leaf_comp, int6
     int status = check_cells(op, peer->dtype, peer->ncols);
     if (status != HKB_OK) return status;
     if (leaves < 1) return fail(HKB_ERR_RANGE, "a tree needs at least one leaf");
-    if (seq == 0) return fail(HKB_ERR_ARGUMENT, "hkb_peer_finish: rounds are numbered from 1");
+    if ((seq & 0xffffffffull) == 0)
+        return fail(HKB_ERR_ARGUMENT, "hkb_peer_finish: round %llu has a zero tag (rounds are numbered from 1 and "
+                    "skip multiples of 2^32)", (unsigned long long)seq);
     for (int r = 0; r < peer->world; ++r)
         if (peer->areas.area[r] == nullptr)
             return fail(HKB_ERR_ARGUMENT, "rank %d's exchange area is not connected (hkb_peer_connect)", r);

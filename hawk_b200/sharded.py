@@ -81,9 +81,10 @@ class PeerFinish:
     launch per call (``hkb_peer_finish``), in place of the NCCL all-gather
     between two tree launches: each rank folds its leaves to one root per
     column, stores the root into every rank's exchange area (plain peer stores
-    through CUDA IPC mappings) with a round flag, waits (bounded, two seconds)
-    for every rank's flag of the round, and folds the roots in rank order --
-    the same tree, bit for bit.
+    through CUDA IPC mappings, each 32-bit half in a word beside the round's
+    tag), waits (bounded, two seconds) until every rank's words of the round
+    carry the tag, and folds the roots in rank order -- the same tree, bit for
+    bit.
 
     Made collectively (every rank of ``group``, once): each rank allocates its
     area on ``device`` and the ranks exchange the areas' IPC handles
@@ -118,6 +119,8 @@ class PeerFinish:
         if leaf_hi.shape[0] < self.cols or values.numel() < self.cols:
             raise HawkError(f"the peer finish was made for {self.cols} columns")
         self.seq += 1
+        if self.seq & 0xFFFFFFFF == 0:      # a round's tag is its low 32 bits; tag 0 is a fresh area's
+            self.seq += 1
         self.area.finish(op, leaf_hi.data_ptr(), leaf_comp.data_ptr(), leaves, values.data_ptr(), self.seq,
                          timeout_ns, stream)
 

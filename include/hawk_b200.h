@@ -219,18 +219,20 @@ int hkb_cells_finish_noalloc(int op, int dtype, int ncols, const void* const* hi
  * column (an aligned subtree of the one-device tree, as for
  * hkb_cells_tree_ex).  One rank's exchange area lives in its own device
  * memory: for each of two round parities, every rank's (hi, comp) root of
- * every column and a round flag.  hkb_peer_finish folds this rank's leaves to
- * its root (the pairwise levels of hkb_cells_tree), stores the root into every
- * rank's area with plain peer stores, raises its flag there, waits until every
- * rank's flag of this round is up in its own area, and runs the last pairwise
- * levels over the ranks' roots in rank order: the same tree, bit for bit, as
- * one hkb_cells_tree over all ranks' leaves.
+ * every column, each 32-bit half of a value in an 8-byte word beside the
+ * round's tag.  hkb_peer_finish folds this rank's leaves to its root (the
+ * pairwise levels of hkb_cells_tree), stores the root's tagged words into
+ * every rank's area with plain peer stores, waits until every rank's words of
+ * this round carry the tag in its own area, and runs the last pairwise levels
+ * over the ranks' roots in rank order: the same tree, bit for bit, as one
+ * hkb_cells_tree over all ranks' leaves.
  *
  * hkb_peer_create allocates this rank's area on `device` (zeroed) and writes
  * its CUDA IPC handle (HKB_PEER_HANDLE_BYTES bytes) to handle_out;
  * hkb_peer_connect opens the other ranks' handles (`handles`: world handles in
  * rank order; this rank's own entry is not read).  `seq` numbers the rounds:
- * 1, 2, 3, ... the same on every rank.  Every wait is bounded by timeout_ns of
+ * 1, 2, 3, ... the same on every rank, skipping multiples of 2^32 (a round's
+ * tag is its low 32 bits, and a fresh area holds tag 0).  Every wait is bounded by timeout_ns of
  * the GPU's global timer (0: two seconds); a wait that runs out leaves `out`
  * untouched and sets HKB_PEER_TIMEOUT in the area's status word, which
  * hkb_peer_status reads and clears (a synchronising read).  Before
