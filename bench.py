@@ -1329,7 +1329,7 @@ def main() -> int:
     ap.add_argument("--n", type=int, default=1 << 26, help="samples per GPU")
     ap.add_argument("--mode", default="float64", choices=("float64", "float32"))
     ap.add_argument("--no-configs", action="store_true", help="skip the per-config table")
-    ap.add_argument("--finish", default="nccl", choices=("peer", "nccl"),
+    ap.add_argument("--finish", default="peer", choices=("peer", "nccl"),
                     help="the cells' last step across GPUs: one launch over NVLink peer memory, or NCCL")
     ap.add_argument("--cpu-sample", type=int, default=1 << 23)
     ap.add_argument("--only", default=None, help="time one benchmark kernel at --n samples (profiling runs); "
