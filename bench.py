@@ -372,7 +372,7 @@ def run_headline(args, world, rank, local, dist) -> dict:
         "vjp_gbs": round(vjp_bytes / (vjp_ms * 1e-3) / 1e9, 1),
     }
     if s.peer is not None:
-        result["finish"] = "peer memory (one launch: subtree, NVLink stores, flags, last levels)"
+        result["finish"] = "peer memory (one launch: subtree, tagged NVLink stores, last levels)"
     elif world > 1:
         result["finish"] = "NCCL all-gather of the subtree roots"
     result["parity"] = headline_parity(s, world, dist)
