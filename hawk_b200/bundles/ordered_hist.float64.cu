@@ -107,8 +107,8 @@ extern "C" __global__ void __launch_bounds__(32) ordered_hist_3(
         (void)nSamples;
         const hk::linalg::team::Team hawk_tm = hk::linalg::team::Team::here();
         const long long hawk_lane = hawk_i;
-        {  // scatter_chunks, n = 1: 8 warps a chunk
-            hk::linalg::team::scatterChunk<Real, 8>(hawk_tm, hawk_lane, count, nSamples, 1, wout_tms_acc_k.data(), wout_tms_acc_v.data(), wout_tms_acc_p.data(), const_cast<std::int32_t*>(wout_tms_acc_m.data()));
+        {  // scatter_chunks, n = 1: 16 warps a chunk
+            hk::linalg::team::scatterChunk<Real, 16>(hawk_tm, hawk_lane, count, nSamples, 1, wout_tms_acc_k.data(), wout_tms_acc_v.data(), wout_tms_acc_p.data(), const_cast<std::int32_t*>(wout_tms_acc_m.data()));
         }
         __syncwarp();
     }
