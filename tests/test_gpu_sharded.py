@@ -126,7 +126,7 @@ def test_sharded_param_gradients_bit_identical_to_one_device(world, shape, form)
 
 
 def _skip_main(rank, world, port, queue):
-    """Two ranks on the exchange area directly: round 2 is rank 0's alone."""
+    """Two ranks on the exchange area directly: the second exchange is rank 0's alone."""
     import torch.distributed as dist
 
     from hawk_b200 import abi
@@ -143,7 +143,7 @@ def _skip_main(rank, world, port, queue):
         out = {}
         for seq in (1, 2, 3):
             if seq == 2 and rank == 1:
-                continue                                    # rank 1 leaves round 2
+                continue                                    # rank 1 leaves the second exchange
             hi = torch.tensor([[1.0 + rank + seq]], dtype=torch.float64, device=f"cuda:{rank}")
             comp = torch.zeros_like(hi)
             cell = torch.full((1,), float("nan"), dtype=torch.float64, device=f"cuda:{rank}")
