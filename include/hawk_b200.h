@@ -227,6 +227,10 @@ int hkb_cells_finish_noalloc(int op, int dtype, int ncols, const void* const* hi
  * over the ranks' roots in rank order: the same tree, bit for bit, as one
  * hkb_cells_tree over all ranks' leaves.
  *
+ * leaf_hi / leaf_comp hold this rank's `leaves` partials of each of the area's
+ * ncols columns, column by column (ncols x leaves), and are folded in place;
+ * out receives ncols values.
+ *
  * hkb_peer_create allocates this rank's area on `device` (zeroed) and writes
  * its CUDA IPC handle (HKB_PEER_HANDLE_BYTES bytes) to handle_out;
  * hkb_peer_connect opens the other ranks' handles (`handles`: world handles in
